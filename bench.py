@@ -1,0 +1,330 @@
+#!/usr/bin/env python
+"""Benchmark of the LNS16 mul_mat hot path (G-LNSadd/s), one JSON line.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--mode base]
+                    [--workload configs1|configs0]
+
+Workload (default configs1): BASELINE configs[1]'s mul_mat -- weights
+1536 x 576 (ggml src0 ne=(576,1536)), activations 576 x 512 (src1 ne=(576,512)),
+xlns16 codes converted from numpy default_rng(1) N(0,0.02) / N(0,1) values;
+dst 512 x 1536 xlns16 codes.  One step = one lnsb_mul_mat_lns call (the whole
+op, every chain in element order).  configs0 is the reference's own CPU case
+(576 x 1536 by 1536 x 8, K = 1536).
+
+N > 1 (torchrun): weak scaling by output-row sharding -- each rank owns 1536
+different weight rows of a (1536 * N)-row matrix, computes its shard and the
+step ends with an NCCL all-gather of the output shards (the exchange step).
+
+--impl reference: the reference's CPU algorithm (the oracle restatement under
+oracle/, the reference itself cannot be built: its arithmetic library is
+absent) timed on this host's cores on a bounded sample of the same workload.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "xlns-ggml-backend_b200"))
+
+METRIC = "LNS16 mul_mat G-LNSadd/s"
+UNIT = "G-LNSadd/s"
+WORKLOADS = {
+    "configs1": dict(desc="BASELINE configs[1] LNS16 mul_mat: W 1536x576 (k-major codes) x X 576x512 -> 512x1536 codes",
+                     K=576, M=1536, N=512, seed=1),
+    "configs0": dict(desc="BASELINE configs[0] LNS16 mul_mat: W 576x1536 x X 1536x8 -> 8x576 codes",
+                     K=1536, M=576, N=8, seed=0),
+}
+# Primitive integer operations of one LNS addition (including the operand
+# product and the table load) in this build's restated algorithm, fixed per
+# mode before tuning: the c_mode of the integer-issue roofline.
+C_MODE = {"base": 18, "monte": 23, "monte_bylpvip": 34, "lpvip": 30, "sum32": 32}
+SMS = 148
+LANES_PER_SM = 128
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--mode", default="base")
+    p.add_argument("--workload", default="configs1", choices=sorted(WORKLOADS))
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), d.get("sm_max_mhz", 1965.0), "measured"
+    except OSError:
+        return 6650.0, 1965.0, "fallback"
+
+
+def adds_of(K, M, N):
+    return M * N * max(K - 1, 0)
+
+
+def algorithmic_bytes(K, M, N):
+    return 2 * (K * M + K * N + M * N)
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (read-only queries)."""
+    FIELDS = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id):
+        self.bus = (bus_id or "").lower()
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and (not self.bus or self.bus.endswith(parts[0].lower()[-12:]) or parts[0].lower().endswith(self.bus[-12:])):
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------ CPU baseline (the checker's port)
+
+def cpu_leg(wl, mode, seconds, nthreads):
+    """Times the oracle's mul_mat (the reference algorithm restated in C) on a
+    bounded sample of the workload: the first R weight rows against all tokens."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle
+    K, M, N = wl["K"], wl["M"], wl["N"]
+    rng = np.random.default_rng(wl["seed"])
+    w = oracle.from_f32_16(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    x = oracle.from_f32_16(rng.normal(0, 1, (N, K)).astype(np.float32))
+    rows = max(1, min(M, 8))
+    t0 = time.perf_counter()
+    oracle.mul_mat16(mode, w[:rows], x, nthreads=nthreads)
+    dt = time.perf_counter() - t0
+    rows = int(max(1, min(M, rows * seconds / max(dt, 1e-6))))
+    t0 = time.perf_counter()
+    oracle.mul_mat16(mode, w[:rows], x, nthreads=nthreads)
+    dt = time.perf_counter() - t0
+    adds = adds_of(K, rows, N)
+    return {"value": adds / dt / 1e9, "unit": UNIT, "cores": nthreads, "kind": "port",
+            "sample": "first %d of %d weight rows x all %d tokens x K=%d (%d LNS adds, %.1f s)" % (rows, M, N, K, adds, dt)}
+
+
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    nthreads = os.cpu_count() or 1
+    vals = []
+    for _ in range(args.warmup):
+        cpu_leg(wl, args.mode, 0.5, nthreads)
+    t0 = time.perf_counter()
+    leg = None
+    for _ in range(args.steps):
+        leg = cpu_leg(wl, args.mode, 3.0, nthreads)
+        vals.append(leg["value"])
+    wall = time.perf_counter() - t0
+    v = statistics.median(vals)
+    leg["value"] = v
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": wall * 1000 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u16 (xlns16 codes)", "data": "synthetic",
+        "config": {"workload": wl["desc"] + " [bounded sample per step on host cores]", "mode": args.mode},
+        "cpu_baseline": leg, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU
+
+def run_ours(args, wl):
+    import numpy as np
+    import torch
+    import lnsb200
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    K, M, N = wl["K"], wl["M"], wl["N"]
+    ks = lnsb200.KernelSet(16, args.mode)
+    ks.upload_tables()
+    rng = np.random.default_rng(wl["seed"] + 1000 * rank)
+    w_f32 = torch.from_numpy(rng.normal(0, 0.02, (M, K)).astype(np.float32)).cuda()    # ggml src0 rows
+    x_f32 = torch.from_numpy(rng.normal(0, 1, (N, K)).astype(np.float32)).cuda()
+    w = torch.empty(K * M, dtype=torch.int16, device="cuda")                          # k-major codes
+    x = torch.empty(N * K, dtype=torch.int16, device="cuda")
+    ks.to_lns_transposed(w_f32, w, M, K, M)
+    ks.to_lns(x_f32, x)
+    out = torch.empty(N * M, dtype=torch.int16, device="cuda")
+    gathered = torch.empty(world * N * M, dtype=torch.int16, device="cuda") if world > 1 else None
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device="cuda")          # 256 MB > L2 (126 MB)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        ks.mul_mat_lns(w, x, out, K, M, N, monte_seed=7)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+
+    bus = None
+    try:
+        p = torch.cuda.get_device_properties(local)
+        bus = "%02x:%02x.0" % (p.pci_bus_id, p.pci_device_id)
+    except Exception:
+        pass
+    sampler = ClockSampler(bus)
+    sampler.start()
+    time.sleep(0.4)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()                      # untimed: L2 flushed before every step
+        ev[i][0].record(stream)
+        ks.mul_mat_lns(w, x, out, K, M, N, monte_seed=7)
+        ev[i][1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+        ev[i][2].record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop()
+    step_ms = sum(a.elapsed_time(c) for a, b, c in ev)
+    kern_ms = sum(a.elapsed_time(b) for a, b, c in ev)
+    if dist:
+        t = torch.tensor([step_ms, kern_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms, kern_ms = t.tolist()
+
+    # e2e through the C ABI with host buffers: H2D of F32 activations, to_lns,
+    # mul_mat with F32 out, D2H of the F32 result (weights stay resident, as
+    # the reference's weight cache keeps them)
+    xh = torch.from_numpy(rng.normal(0, 1, (N, K)).astype(np.float32)).pin_memory()
+    yh = torch.empty(N * M, dtype=torch.float32).pin_memory()
+    xd = torch.empty(N * K, dtype=torch.float32, device="cuda")
+    yd = torch.empty(N * M, dtype=torch.float32, device="cuda")
+
+    def e2e_step():
+        xd.copy_(xh.view(-1), non_blocking=True)
+        ks.to_lns(xd, x)
+        ks.mul_mat(w, x, yd, K, M, N, monte_seed=7)
+        yh.copy_(yd, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+        dist.barrier()
+
+    adds = adds_of(K, M, N)
+    value = adds * world * args.steps / (step_ms / 1000) / 1e9
+    e2e_val = adds * world * args.steps / (e2e_ms / 1000) / 1e9
+    kern_s = kern_ms / 1000 / args.steps
+    hbm, smmax, src = peaks()
+    f_mhz = clocks.get("sm_mhz") or smmax
+    c = C_MODE.get(args.mode, 18)
+    int_peak = SMS * LANES_PER_SM * f_mhz * 1e6 / c / 1e9
+    achieved = adds / kern_s / 1e9
+    bytes_alg = algorithmic_bytes(K, M, N)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u16 (xlns16 codes; integer LNS arithmetic)", "data": "synthetic",
+        "config": {"workload": wl["desc"] + (" per rank, output rows sharded + NCCL all_gather" if world > 1 else ""),
+                   "K": K, "M": M, "N": N, "mode": args.mode, "parallelism": "rowshard%d" % world,
+                   "l2": "flushed (256 MB write) before every timed step"},
+        "roofline": {"bound": "int", "achieved": achieved, "peak": int_peak, "unit": UNIT, "frac": achieved / int_peak,
+                     "traffic": None, "c_mode": c, "sm_mhz_used": f_mhz,
+                     "note": "integer-issue bound: %d SMs x %d lanes x f_sm / c_mode (%s SM clock)" % (SMS, LANES_PER_SM, "sampled" if clocks.get("sm_mhz") else src),
+                     "hbm": {"achieved_gbs": bytes_alg / kern_s / 1e9, "peak_gbs": hbm, "frac": bytes_alg / kern_s / 1e9 / hbm,
+                             "algorithmic_bytes": bytes_alg}},
+        "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": N * K * 4, "d2h_bytes_per_step": N * M * 4},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_leg(wl, args.mode, 10.0, os.cpu_count() or 1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference(args, wl)
+    return run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

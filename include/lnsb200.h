@@ -1,0 +1,151 @@
+/*
+ * lnsb200.h -- C ABI of the B200-native LNSCUDA16 / LNSCUDA32 hot path.
+ *
+ * The reference (xlnsresearch/xlns-ggml-backend) puts its GPU work behind one
+ * C++ interface, lns_cuda::kernel_set (lns-backend/cuda/lns-cuda-kernels.h:85-139).
+ * This header is that interface as a plain C ABI: one function per method,
+ * the format as an argument (16 = xlns16 / LNSCUDA16, 32 = xlns32 / LNSCUDA32),
+ * device pointers and sizes in, a status code out, every launch asynchronous
+ * on the caller's stream.  A ctypes / cgo / JNI binding needs nothing else.
+ *
+ * Build mode.  Like the reference, the xlns16 summation mode is fixed when
+ * the library is built (GGML_LNS16_SUM = base | monte | lpvip | sum32, plus
+ * GGML_LNS16_MONTE_BYLPVIP): liblnsb200_<mode>.so.  lnsb_sum_mode() reports it.
+ *
+ * Conventions (lns-cuda-kernels.h:12-26):
+ *   - tensors are contiguous arrays in ggml element order (ne[0] fastest);
+ *   - reductions run in element order, one sequential chain per output;
+ *   - Monte reductions start from monte_seed; reduction i starts i * draws
+ *     LFSR steps later (CPU loop order);
+ *   - xlns16 values are uint16 codes, xlns32 values uint32 codes.
+ *
+ * Status codes: 0 = success; > 0 = the cudaError_t of a failed CUDA call;
+ * < 0 = LNSB_E_* below.  lnsb_error_string() names either kind.
+ */
+#ifndef LNSB200_H
+#define LNSB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LNSB_XLNS16 16
+#define LNSB_XLNS32 32
+
+#define LNSB_OK             0
+#define LNSB_E_INVALID    (-1)   /* bad format, null pointer, negative size, bad broadcast */
+#define LNSB_E_NO_TABLES  (-2)   /* lnsb_upload_tables was not run on this device */
+#define LNSB_E_UNSUPPORTED (-3)  /* argument combination this build does not implement */
+#define LNSB_E_TOO_LARGE  (-4)   /* size beyond a documented limit */
+#define LNSB_E_NO_DEVICE  (-5)   /* no usable CUDA device */
+
+/* a cudaStream_t; NULL is the legacy default stream */
+typedef void * lnsb_stream_t;
+
+typedef struct { int64_t ne[4]; } lnsb_shape4;   /* lns-cuda-kernels.h:39-43 */
+
+/*
+ * dst = W^T x per activation slice, sequential over k
+ * (mul_mat_args, lns-cuda-kernels.h:45-58):
+ *   w   LNS, K x M per weight slice, k-major (element (k, m) at k*M + m),
+ *       ne02 * ne03 slices
+ *   x   LNS, N x K per activation slice, ne12 * ne13 slices
+ *   dst F32, N x M per activation slice
+ * Activation slice (i12, i13) uses weight slice (i12 / (ne12/ne02), i13 / (ne13/ne03)).
+ */
+typedef struct {
+    const void * w;
+    const void * x;
+    float *      dst;
+    int64_t      K, M, N;
+    int64_t      ne02, ne03, ne12, ne13;
+    uint16_t     monte_seed;
+} lnsb_mul_mat_args;
+
+/*
+ * dst = softmax(src * scale + mask) over rows of src.ne[0]; mask (optional)
+ * broadcasts over dims 2 and 3; work holds src.nelements() LNS values
+ * (soft_max_args, lns-cuda-kernels.h:60-71).
+ */
+typedef struct {
+    const float * src;
+    lnsb_shape4   src_shape;
+    const float * mask;
+    lnsb_shape4   mask_shape;
+    float         scale;
+    float *       dst;
+    void *        work;
+    uint16_t      monte_seed;
+} lnsb_soft_max_args;
+
+/* ---- identity: kernel_set::format_name / value_size / sum_mode / monte_impl
+ *      (lns-cuda-kernels.h:89-95) ---- */
+const char * lnsb_format_name(int fmt);        /* "xlns16" | "xlns32" | NULL */
+size_t       lnsb_value_size(int fmt);         /* 2 | 4 | 0 */
+const char * lnsb_sum_mode(int fmt);           /* "base"|"monte"|"lpvip"|"sum32" for 16, NULL for 32 */
+const char * lnsb_monte_impl(int fmt);         /* "pure16"|"bylpvip" in a monte build, else NULL */
+/* device description with "sum=<mode>[, monte=<impl>]" (ggml-lns-cuda.cpp:21-31,61-74) */
+const char * lnsb_description(int fmt);
+
+/* ---- draw accounting: kernel_set::*_draws (lns-cuda-kernels.h:97-100) ---- */
+uint64_t lnsb_mul_mat_draws(int fmt, const lnsb_mul_mat_args * args);
+uint64_t lnsb_soft_max_draws(int fmt, int64_t ncols, int64_t nrows);
+uint64_t lnsb_rms_norm_draws(int fmt, int64_t ncols, int64_t nrows);
+
+/* ---- kernel_set::upload_tables (lns-cuda-kernels.h:102-104): builds the
+ *      arithmetic tables once per process and uploads them to the current
+ *      device once per device.  Must run before any other call on a device. ---- */
+int lnsb_upload_tables(int fmt);
+
+/* ---- conversions: kernel_set::to_lns / to_lns_transposed (lns-cuda-kernels.h:106-112) ---- */
+int lnsb_to_lns(int fmt, const float * src, void * dst, int64_t n, lnsb_stream_t stream);
+/* dst[c * dst_ld + r] = lns(src[r * cols + c]) */
+int lnsb_to_lns_transposed(int fmt, const float * src, void * dst, int64_t rows, int64_t cols,
+                           int64_t dst_ld, lnsb_stream_t stream);
+/* dst[i] = float(src[i]) -- the op-boundary decode the reference fuses into
+ * every kernel's store (lns-cuda-kernels.cuh:155,249,324) */
+int lnsb_to_f32(int fmt, const void * src, float * dst, int64_t n, lnsb_stream_t stream);
+
+/* ---- the hot path ---- */
+
+/* kernel_set::mul_mat (lns-cuda-kernels.h:114) */
+int lnsb_mul_mat(int fmt, const lnsb_mul_mat_args * args, lnsb_stream_t stream);
+/* same product with LNS codes out: dst_lns is N x M per activation slice
+ * (args->dst is ignored).  The reference's LNS16-typed dst path,
+ * lns-ops.cpp:374-379. */
+int lnsb_mul_mat_lns(int fmt, const lnsb_mul_mat_args * args, void * dst_lns, lnsb_stream_t stream);
+
+/* kernel_set::soft_max (lns-cuda-kernels.h:136) */
+int lnsb_soft_max(int fmt, const lnsb_soft_max_args * args, lnsb_stream_t stream);
+/* codes in, codes out: src [ne3][ne2][ne1][ne0], mask (may be NULL) codes
+ * [mne3][mne2][mne1][ne0] with ne0 == src ne0, mne1 >= ne1, dims 2/3
+ * broadcast; scale is an LNS code; work holds nelements(src) LNS values.
+ * The reference's LNS16-typed path, lns-ops.cpp:643-695. */
+int lnsb_soft_max_lns(int fmt, const void * src, const int64_t ne[4], const void * mask,
+                      const int64_t mne[4], uint32_t scale, void * dst, void * work,
+                      uint16_t monte_seed, lnsb_stream_t stream);
+
+/* kernel_set::rms_norm (lns-cuda-kernels.h:132-134) */
+int lnsb_rms_norm(int fmt, const float * src, float * dst, int64_t ncols, int64_t nrows, float eps,
+                  uint16_t monte_seed, lnsb_stream_t stream);
+/* codes in, codes out (lns-ops.cpp:701-736 with LNS16 tensors) */
+int lnsb_rms_norm_lns(int fmt, const void * src, void * dst, int64_t ncols, int64_t nrows, float eps,
+                      uint16_t monte_seed, lnsb_stream_t stream);
+
+/* ---- Monte state: one LFSR per process, seed 7 (ggml-lns.h:13-24).  All
+ *      return 0 on success, LNSB_E_UNSUPPORTED outside a monte build;
+ *      set_state rejects 0 (absorbing). ---- */
+int lnsb_monte_get_state(uint16_t * state);
+int lnsb_monte_set_state(uint16_t state);
+/* *start = current state, then advance it by `draws` steps (lns-ops.cpp:178-195) */
+int lnsb_monte_reserve(uint64_t draws, uint16_t * start);
+
+const char * lnsb_error_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

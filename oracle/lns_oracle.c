@@ -1,0 +1,793 @@
+/*
+ * lns_oracle.c -- CPU restatement of the LNS16/LNS32 reduction hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY (the checker, never the product).  Written in
+ * plain C from the published LNS mathematics and the reference's call sites;
+ * no reference source is copied (the reference's arithmetic library xlnscpp
+ * is not in its checkout at all).  Each function names the reference code
+ * whose behaviour it restates.
+ *
+ * Number formats (format facts: lns-backend/tests/test-lns16-sum32.cpp:37-51,
+ * lns-backend/src/lns16-sum32.h:54-81):
+ *   xlns16: bit 15 sign, bits 14..0 = round(log2|x| * 128) + 0x4000.
+ *           0x0000 / 0x8000 are zero, 0x7FFF / 0xFFFF saturate; -inf = 0xFFFF.
+ *   xlns32: bit 31 sign, bits 30..0 = log2|x| * 2^23 + 0x40000000.
+ */
+#include "lns_oracle.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ===================================================================== */
+/* xlns16                                                                 */
+/* ===================================================================== */
+
+#define X16_LOGMASK  0x7FFFu
+#define X16_SIGNMASK 0x8000u
+#define X16_OFFSET   0x4000u
+#define X16_ZERO     0x0000u
+#define X16_NEG_INF  0xFFFFu
+#define X16_ESSZER   1280      /* sb/db are zero for |z| > 1280 (0x500) */
+
+static int      g_ready;
+static uint16_t g_sb16[X16_ESSZER + 1];      /* sb(-n), n = 0..1280            */
+static int16_t  g_db16[X16_ESSZER + 1];      /* db(-n) adjustment, n = 1..1280 */
+static uint16_t g_conv16[65536];             /* bf16 pattern -> xlns16         */
+static float    g_dec16[65536];              /* xlns16 -> float                */
+static uint16_t g_exp16[65536];              /* xlns16 exp                     */
+
+/*
+ * Gaussian logarithms at F=7.  The reference adds through a table of the
+ * ideal sb/db functions (docs/CUDA.md:138-143, "1280-entry sb/db table";
+ * essential zero 0x500).  The table values are the ideal functions rounded
+ * with the C idiom (int)(v + 0.5); for the db branch the value rounded is
+ * log2(2^n - 1), which is negative for n < 128, where that idiom rounds one
+ * step high.  This is what reproduces the reference's printed two-term
+ * statistics (results/sum32-evidence/standalone-sum32-invariants.txt:4:
+ * "base max 1 ULP (mean 0.025)"; the exactly rounded table gives 0 / 0.000).
+ */
+static void build16(void) {
+    for (int n = 0; n <= X16_ESSZER; n++) {
+        double sb = log(1.0 + pow(2.0, -(double)n / 128.0)) / log(2.0) * 128.0;
+        g_sb16[n] = (uint16_t)(sb + .5);
+        if (n == 0) {
+            g_db16[n] = 0;
+        } else {
+            double dbneg = log(pow(2.0, (double)n / 128.0) - 1.0) / log(2.0) * 128.0;
+            g_db16[n] = (int16_t)(-n + (int16_t)(dbneg + .5));
+        }
+    }
+    /*
+     * float -> xlns16: a 65536-entry table indexed by the float's upper 16
+     * bits (README.md:75-76 "65536-entry lookup table"), each entry the
+     * truncating conversion (int)(log2|b| * 128) of that bfloat16 value b.
+     * Out-of-range logs saturate (|x| >= 2^128 -> 0x7FFF, below 2^-128 -> 0).
+     */
+    for (uint32_t i = 0; i < 65536; i++) {
+        uint32_t bits = i << 16;
+        float f;
+        memcpy(&f, &bits, 4);
+        uint16_t sign = (i & 0x8000u) ? X16_SIGNMASK : 0;
+        float a = fabsf(f);
+        uint16_t code;
+        if (a == 0.0f || a != a) {
+            code = X16_ZERO;
+        } else if (isinf(a)) {
+            code = (uint16_t)(sign | X16_LOGMASK);
+        } else {
+            double l = log((double)a) / log(2.0) * 128.0;
+            long t = (long)l;                     /* truncation toward zero */
+            long c = t + (long)X16_OFFSET;
+            if (c < 0) c = 0;
+            if (c > (long)X16_LOGMASK) c = X16_LOGMASK;
+            code = (uint16_t)(sign | (uint16_t)c);
+        }
+        g_conv16[i] = code;
+    }
+    /*
+     * xlns16 -> float: 2^(l/128) held to 7 significant decimal digits, then
+     * rounded to float; zero log field -> 0.0f.  The reference's printed
+     * decodes carry that precision, not the correctly rounded float:
+     * 2^(491/128) prints as 14.280130 (results/sum32-evidence/
+     * unit-tests-lns16-base.txt:23, correctly rounded: 14.280133) and
+     * 2^(1355/128) as 1537.0380 (standalone-sum32-invariants.txt:9).
+     */
+    for (uint32_t c = 0; c < 65536; c++) {
+        if ((c & X16_LOGMASK) == 0) {
+            g_dec16[c] = 0.0f;
+        } else {
+            double v = pow(2.0, (double)((int)(c & X16_LOGMASK) - (int)X16_OFFSET) / 128.0);
+            char buf[32];
+            snprintf(buf, sizeof buf, "%.7g", v);    /* 7 significant digits */
+            v = strtod(buf, NULL);
+            g_dec16[c] = (float)((c & X16_SIGNMASK) ? -v : v);
+        }
+    }
+    /* exp through float, as a 65536-entry table (docs/CUDA.md:138-140) */
+    for (uint32_t c = 0; c < 65536; c++) {
+        float e = expf(g_dec16[c]);
+        uint32_t bits;
+        memcpy(&bits, &e, 4);
+        g_exp16[c] = g_conv16[bits >> 16];
+    }
+}
+
+uint16_t orc16_from_f32(float x) {
+    uint32_t bits;
+    memcpy(&bits, &x, 4);
+    return g_conv16[bits >> 16];
+}
+
+float orc16_to_f32(uint16_t v) { return g_dec16[v]; }
+
+/* xlns16_mul: add the log fields; underflow -> signed zero, overflow -> saturate */
+uint16_t orc16_mul(uint16_t a, uint16_t b) {
+    int p = (int)(a & X16_LOGMASK) + (int)(b & X16_LOGMASK) - (int)X16_OFFSET;
+    if (p < 0) p = 0;
+    if (p > (int)X16_LOGMASK) p = X16_LOGMASK;
+    return (uint16_t)(((a ^ b) & X16_SIGNMASK) | (uint16_t)p);
+}
+
+uint16_t orc16_div(uint16_t a, uint16_t b) {
+    int p = (int)(a & X16_LOGMASK) - (int)(b & X16_LOGMASK) + (int)X16_OFFSET;
+    if (p < 0) p = 0;
+    if (p > (int)X16_LOGMASK) p = X16_LOGMASK;
+    return (uint16_t)(((a ^ b) & X16_SIGNMASK) | (uint16_t)p);
+}
+
+/*
+ * xlns16_add in its "alt" form: the result is the larger operand scaled by
+ * 2^(adjust/128), adjust = sb or db of z = min - max; z == 0 with opposite
+ * signs is exact cancellation (xlns16 zero); |z| > 1280 adds nothing.
+ * Ties in magnitude keep the second operand's sign.
+ */
+uint16_t orc16_add(uint16_t a, uint16_t b) {
+    int al = a & X16_LOGMASK, bl = b & X16_LOGMASK;
+    uint16_t mx = (al > bl) ? a : b;
+    int n = al > bl ? al - bl : bl - al;
+    int usedb = (a ^ b) & X16_SIGNMASK;
+    if (n == 0 && usedb) return X16_ZERO;
+    int adj = 0;
+    if (n <= X16_ESSZER) adj = usedb ? g_db16[n] : g_sb16[n];
+    int p = (int)(mx & X16_LOGMASK) + adj;
+    if (p < 0) p = 0;
+    if (p > (int)X16_LOGMASK) p = X16_LOGMASK;
+    return (uint16_t)((mx & X16_SIGNMASK) | (uint16_t)p);
+}
+
+uint16_t orc16_sub(uint16_t a, uint16_t b) { return orc16_add(a, (uint16_t)(b ^ X16_SIGNMASK)); }
+uint16_t orc16_exp(uint16_t a) { return g_exp16[a]; }
+
+/* xlns16_sqrt: halve the signed log (rounding odd logs away from zero) */
+uint16_t orc16_sqrt(uint16_t a) {
+    int16_t s = (int16_t)(uint16_t)(a << 1);
+    int q = s / 4;                                   /* C division truncates */
+    return (uint16_t)(((uint16_t)q & X16_LOGMASK) ^ 0x2000u);
+}
+
+/* xlns16_recip: negate the log, keep the sign */
+uint16_t orc16_recip(uint16_t a) {
+    return (uint16_t)((a & X16_SIGNMASK) | ((uint16_t)(~a + 1u) & X16_LOGMASK));
+}
+
+static inline uint32_t canon16(uint16_t v) {
+    return (v & X16_SIGNMASK) ? (uint32_t)(~v & 0xFFFFu) : (uint32_t)(v | 0x10000u);
+}
+int orc16_gt(uint16_t a, uint16_t b) { return canon16(a) > canon16(b); }
+static inline int is_zero16(uint16_t v) { return (v & X16_LOGMASK) == 0; }
+
+uint16_t orc16_mask_from_f32(float m) { return m <= -3.0e38f ? X16_NEG_INF : orc16_from_f32(m); }
+
+/* ===================================================================== */
+/* xlns32                                                                 */
+/* ===================================================================== */
+
+#define X32_LOGMASK  0x7FFFFFFFu
+#define X32_SIGNMASK 0x80000000u
+#define X32_OFFSET   0x40000000u
+#define X32_NEG_INF  0xFFFFFFFFu
+#define X32_ONE_OCT  (1u << 23)
+#define X32_ESS      (26u << 23)
+
+/*
+ * Addition tables for xlns32 (the reference's LNS32 configuration,
+ * "xlns32_alt": table sb with linear interpolation, cotransformed db;
+ * docs/CUDA.md:141-143, lns-backend/src/lns16-sum32.h:22-24).  This is a
+ * restatement of that scheme, not the library's table layout:
+ *   sb: knots every 2^-10 octave on [0,8), every 2^-7 on [8,26)
+ *   db: knots every 2^-11 / 2^-10 / 2^-9 / 2^-7 octave on [1,2) / [2,4) /
+ *       [4,8) / [8,26); on (0,1) the cotransformation
+ *       db(z) = log2(A + B),  A = 1 - 2^z2,  B = 2^z2 (1 - 2^z1)
+ *       with z1 = z rounded to 2^-11 octave and z2 = z - z1 (exact tables).
+ * Knot values are rounded to nearest; interpolation floors.
+ */
+typedef struct { uint32_t lo, hi; int shift; int base; } seg_t;
+static const seg_t k_sb_seg[2] = { {0u, 8u << 23, 13, 0}, {8u << 23, 26u << 23, 16, 0} };
+static const seg_t k_db_seg[4] = { {1u << 23, 2u << 23, 12, 0}, {2u << 23, 4u << 23, 13, 0},
+                                   {4u << 23, 8u << 23, 14, 0}, {8u << 23, 26u << 23, 16, 0} };
+static int32_t * g_sb32;   /* concatenated knots of both sb segments */
+static int32_t * g_db32;   /* concatenated knots of the 4 db segments */
+static int       g_sb_base[2], g_db_base[4];
+static int32_t   g_db32_hi[2048];    /* db at z1 = -j * 2^-11 octave, j = 1..2047 */
+static int32_t   g_db32_lo[4096];    /* db at z2 = -k * 2^-23 octave, k = 1..4095 */
+static uint32_t * g_logm32;          /* floor(log2(1 + j/2^23) * 2^23), j < 2^23 */
+static float    * g_expm32;          /* float nearest 2^(f/2^23), f < 2^23     */
+static int32_t  * g_lpvip_db;        /* exact db on the LPVIP singular branch  */
+static int16_t    g_sbf[2304], g_dbf[2304];  /* Monte: sb/db at 8 extra bits  */
+
+static int KNOT_MODE = 1;
+static int32_t knot_round(long double v) {
+    v *= (long double)X32_ONE_OCT;
+    if (KNOT_MODE == 0) return (int32_t)llroundl(v);
+    if (KNOT_MODE == 1) return (int32_t)v;            /* truncation toward zero */
+    return (int32_t)floorl(v);
+}
+static int32_t knot_sb(uint32_t d) {
+    long double x = (long double)d / (long double)X32_ONE_OCT;
+    return knot_round(log1pl(exp2l(-x)) / 0.693147180559945309417232121458176568L);
+}
+static int32_t knot_db(uint32_t d) {
+    long double x = (long double)d / (long double)X32_ONE_OCT;
+    return knot_round(log1pl(-exp2l(-x)) / 0.693147180559945309417232121458176568L);
+}
+void orc_set_knot_mode(int m) { KNOT_MODE = m; }
+
+static int build32(void) {
+    int tot = 0;
+    for (int s = 0; s < 2; s++) { g_sb_base[s] = tot; tot += (int)((k_sb_seg[s].hi - k_sb_seg[s].lo) >> k_sb_seg[s].shift) + 1; }
+    g_sb32 = (int32_t *)malloc(sizeof(int32_t) * (size_t)tot);
+    for (int s = 0; s < 2; s++) {
+        int n = (int)((k_sb_seg[s].hi - k_sb_seg[s].lo) >> k_sb_seg[s].shift);
+        for (int i = 0; i <= n; i++) g_sb32[g_sb_base[s] + i] = knot_sb(k_sb_seg[s].lo + ((uint32_t)i << k_sb_seg[s].shift));
+    }
+    tot = 0;
+    for (int s = 0; s < 4; s++) { g_db_base[s] = tot; tot += (int)((k_db_seg[s].hi - k_db_seg[s].lo) >> k_db_seg[s].shift) + 1; }
+    g_db32 = (int32_t *)malloc(sizeof(int32_t) * (size_t)tot);
+    for (int s = 0; s < 4; s++) {
+        int n = (int)((k_db_seg[s].hi - k_db_seg[s].lo) >> k_db_seg[s].shift);
+        for (int i = 0; i <= n; i++) g_db32[g_db_base[s] + i] = knot_db(k_db_seg[s].lo + ((uint32_t)i << k_db_seg[s].shift));
+    }
+    g_db32_hi[0] = 0;
+    for (int j = 1; j < 2048; j++) g_db32_hi[j] = knot_db((uint32_t)j << 12);
+    g_db32_lo[0] = 0;
+    for (int k = 1; k < 4096; k++) g_db32_lo[k] = knot_db((uint32_t)k);
+
+    /* LNS32 conversions, exact by construction */
+    g_logm32 = (uint32_t *)malloc(sizeof(uint32_t) << 23);
+    g_expm32 = (float *)malloc(sizeof(float) << 23);
+    g_lpvip_db = (int32_t *)malloc(sizeof(int32_t) << 23);
+    if (!g_logm32 || !g_expm32 || !g_lpvip_db) return -1;
+    for (uint32_t j = 0; j < (1u << 23); j++) {
+        long double m = 1.0L + (long double)j / (long double)X32_ONE_OCT;
+        long double v = log2l(m) * (long double)X32_ONE_OCT;
+        g_logm32[j] = (uint32_t)floorl(v);
+        g_expm32[j] = (float)exp2l((long double)j / (long double)X32_ONE_OCT);
+        g_lpvip_db[j] = j == 0 ? 0 : knot_db(j);
+    }
+    /* Monte fine tables: 256 sub-steps per xlns16 ULP */
+    for (int n = 0; n < 2304; n++) {
+        long double x = (long double)n / 128.0L;
+        long double sb = log1pl(exp2l(-x)) / 0.693147180559945309417232121458176568L;
+        g_sbf[n] = (int16_t)llroundl(sb * 32768.0L);
+        if (n == 0) {
+            g_dbf[n] = 0;
+        } else {
+            long double db = log1pl(-exp2l(-x)) / 0.693147180559945309417232121458176568L;
+            long double r = roundl(db * 32768.0L);
+            g_dbf[n] = (int16_t)(r < -32768.0L ? -32768 : r);
+        }
+    }
+    return 0;
+}
+
+static inline int32_t interp(const int32_t * t, const seg_t * sg, int base, uint32_t d) {
+    uint32_t off = d - sg->lo;
+    uint32_t i = off >> sg->shift;
+    uint32_t f = off & ((1u << sg->shift) - 1u);
+    int32_t a = t[base + (int)i], b = t[base + (int)i + 1];
+    return a + (int32_t)(((int64_t)(b - a) * (int64_t)f) >> sg->shift);
+}
+
+static inline int32_t sb32(uint32_t d) {
+    if (d >= X32_ESS) return 0;
+    int s = d >= k_sb_seg[1].lo;
+    return interp(g_sb32, &k_sb_seg[s], g_sb_base[s], d);
+}
+
+static inline int32_t db32(uint32_t d) {   /* d > 0 */
+    if (d >= X32_ESS) return 0;
+    if (d >= X32_ONE_OCT) {
+        int s = d >= (8u << 23) ? 3 : d >= (4u << 23) ? 2 : d >= (2u << 23) ? 1 : 0;
+        return interp(g_db32, &k_db_seg[s], g_db_base[s], d);
+    }
+    uint32_t d1 = d >> 12, d2 = d & 4095u;
+    if (d1 == 0) return g_db32_lo[d2];
+    if (d2 == 0) return g_db32_hi[d1];
+    int32_t la = g_db32_lo[d2];
+    int32_t lb = -(int32_t)d2 + g_db32_hi[d1];
+    int32_t hi = la > lb ? la : lb;
+    uint32_t gap = (uint32_t)(la > lb ? la - lb : lb - la);
+    return hi + sb32(gap);
+}
+
+static inline uint32_t mul32(uint32_t a, uint32_t b) {
+    int64_t p = (int64_t)(a & X32_LOGMASK) + (int64_t)(b & X32_LOGMASK) - (int64_t)X32_OFFSET;
+    if (p < 0) p = 0;
+    if (p > (int64_t)X32_LOGMASK) p = X32_LOGMASK;
+    return ((a ^ b) & X32_SIGNMASK) | (uint32_t)p;
+}
+uint32_t orc32_mul(uint32_t a, uint32_t b) { return mul32(a, b); }
+
+static inline uint32_t div32(uint32_t a, uint32_t b) {
+    int64_t p = (int64_t)(a & X32_LOGMASK) - (int64_t)(b & X32_LOGMASK) + (int64_t)X32_OFFSET;
+    if (p < 0) p = 0;
+    if (p > (int64_t)X32_LOGMASK) p = X32_LOGMASK;
+    return ((a ^ b) & X32_SIGNMASK) | (uint32_t)p;
+}
+
+/* xlns32_add ("alt" form, same structure as xlns16's) */
+static inline uint32_t add32(uint32_t a, uint32_t b) {
+    uint32_t al = a & X32_LOGMASK, bl = b & X32_LOGMASK;
+    uint32_t mx = al > bl ? a : b;
+    uint32_t d = al > bl ? al - bl : bl - al;
+    int usedb = ((a ^ b) & X32_SIGNMASK) != 0;
+    if (d == 0 && usedb) return 0;
+    int32_t adj = usedb ? db32(d) : sb32(d);
+    int64_t p = (int64_t)(mx & X32_LOGMASK) + adj;
+    if (p < 0) p = 0;
+    if (p > (int64_t)X32_LOGMASK) p = X32_LOGMASK;
+    return (mx & X32_SIGNMASK) | (uint32_t)p;
+}
+uint32_t orc32_add(uint32_t a, uint32_t b) { return add32(a, b); }
+static inline uint32_t sub32(uint32_t a, uint32_t b) { return add32(a, b ^ X32_SIGNMASK); }
+
+static inline uint32_t sqrt32(uint32_t a) {
+    int32_t s = (int32_t)(a << 1);
+    int32_t q = s / 4;
+    return ((uint32_t)q & X32_LOGMASK) ^ 0x20000000u;
+}
+static inline uint32_t recip32(uint32_t a) { return (a & X32_SIGNMASK) | ((~a + 1u) & X32_LOGMASK); }
+static inline uint64_t canon32(uint32_t v) {
+    return (v & X32_SIGNMASK) ? (uint64_t)(~v) : ((uint64_t)v | 0x100000000ull);
+}
+static inline int gt32(uint32_t a, uint32_t b) { return canon32(a) > canon32(b); }
+static inline int is_zero32(uint32_t v) { return (v & X32_LOGMASK) == 0; }
+
+/*
+ * float -> xlns32: (int)(log2|x| * 2^23), truncation toward zero
+ * (lns-backend/src32/lns32-ops.cpp:58-62 uses libm log per element).  Here
+ * the truncation is exact: log2 of the 24-bit mantissa comes from a table
+ * built in long double, the exponent is added as an integer.
+ */
+uint32_t orc32_from_f32(float x) {
+    uint32_t b;
+    memcpy(&b, &x, 4);
+    uint32_t sign = b & 0x80000000u;
+    uint32_t ex = (b >> 23) & 0xFFu, man = b & 0x7FFFFFu;
+    if (ex == 0xFFu) return man ? 0u : (sign | X32_LOGMASK);
+    if (ex == 0 && man == 0) return 0u;
+    int e;
+    if (ex == 0) {                         /* subnormal: normalise */
+        e = -126;
+        while (!(man & 0x800000u)) { man <<= 1; e--; }
+        man &= 0x7FFFFFu;
+    } else {
+        e = (int)ex - 127;
+    }
+    int64_t l = (int64_t)e * (int64_t)X32_ONE_OCT + (int64_t)g_logm32[man];
+    if (e < 0 && man != 0) l += 1;         /* ceil for |x| < 1 */
+    return sign | (uint32_t)((l + (int64_t)X32_OFFSET) & (int64_t)X32_LOGMASK);
+}
+
+/* scale a float in [1,2) by 2^e, rounding to nearest even into subnormals */
+static float scale_pow2(float m, int e) {
+    uint32_t mb;
+    memcpy(&mb, &m, 4);
+    uint32_t mant = (mb & 0x7FFFFFu) | 0x800000u;     /* 24-bit significand */
+    uint32_t out;
+    if (e > 127) {
+        out = 0x7F800000u;
+    } else if (e >= -126) {
+        out = ((uint32_t)(e + 127) << 23) | (mant & 0x7FFFFFu);
+    } else {
+        int sh = -126 - e;                             /* >= 1 */
+        if (sh > 25) {
+            out = 0;
+        } else {
+            uint32_t q = mant >> sh, rem = mant & ((1u << sh) - 1u), half = 1u << (sh - 1);
+            if (rem > half || (rem == half && (q & 1u))) q++;
+            out = q;                                   /* may carry into the normal range */
+        }
+    }
+    float r;
+    memcpy(&r, &out, 4);
+    return r;
+}
+
+float orc32_to_f32(uint32_t v) {
+    if ((v & X32_LOGMASK) == 0) return 0.0f;
+    int32_t l = (int32_t)(v & X32_LOGMASK) - (int32_t)X32_OFFSET;
+    int e = l >> 23;                                   /* floor */
+    uint32_t f = (uint32_t)l & 0x7FFFFFu;
+    float r = scale_pow2(g_expm32[f], e);
+    return (v & X32_SIGNMASK) ? -r : r;
+}
+
+uint32_t orc32_mask_from_f32(float m) { return m <= -3.0e38f ? X32_NEG_INF : orc32_from_f32(m); }
+
+/*
+ * Float exp used by xlns32's exp (the reference evaluates it with float
+ * libm, docs/CUDA.md:159-161).  Own definition so host and device agree bit
+ * for bit: range reduction by 2^n, Taylor series of e^r (|r| <= ln2/2) to
+ * degree 14 in double with explicit fused multiply-adds, one rounding to
+ * float at the end.
+ */
+float orc_expf(float x) {
+    if (x != x) return x;
+    double xd = (double)x;
+    if (xd > 200.0) xd = 200.0;
+    if (xd < -200.0) xd = -200.0;
+    double t = xd * 1.4426950408889634074;
+    double n = nearbyint(t);
+    double r = (t - n) * 0.69314718055994530942;
+    static const double c[15] = {
+        1.0, 1.0, 1.0 / 2, 1.0 / 6, 1.0 / 24, 1.0 / 120, 1.0 / 720, 1.0 / 5040, 1.0 / 40320,
+        1.0 / 362880, 1.0 / 3628800, 1.0 / 39916800, 1.0 / 479001600, 1.0 / 6227020800.0,
+        1.0 / 87178291200.0 };
+    double p = c[14];
+    for (int i = 13; i >= 0; i--) p = fma(p, r, c[i]);
+    return (float)ldexp(p, (int)n);
+}
+
+static inline uint32_t exp32(uint32_t v) { return orc32_from_f32(orc_expf(orc32_to_f32(v))); }
+
+/* ===================================================================== */
+/* LPVIP: 32-bit accumulator with Mitchell-approximated sb/db            */
+/* ===================================================================== */
+
+/*
+ * Restatement of the LPVIP accumulator the reference takes from xlnscpp's
+ * xlns32lpvip.cpp (README.md:113 "32-bit LPVIP accumulator", test-lns-backend.cpp:48-55
+ * "Mitchell-approximated adds"; docs/CUDA.md:176-180: the singular branch of
+ * the subtraction is evaluated exactly).  Mitchell: 2^z ~ 2^floor(z)(1 + frac z),
+ * log2(m 2^k) ~ k + (m - 1).  Opposite signs closer than one octave use the
+ * exact db (tabulated for all 2^23 inputs).
+ */
+static inline uint32_t mitchell_exp2_neg(uint32_t d) {      /* ~2^(-d) at F=23, d >= 0 */
+    uint32_t q = (d + X32_ONE_OCT - 1u) >> 23;               /* ceil(d) in octaves */
+    uint32_t frac = (q << 23) - d;                           /* z - floor(z) */
+    if (q >= 32) return 0;
+    return (X32_ONE_OCT + frac) >> q;
+}
+static inline int32_t mitchell_log2(uint32_t v) {             /* ~log2(v / 2^23), v > 0 */
+    int k = 31 - __builtin_clz(v);                             /* msb position */
+    int e = k - 23;
+    uint32_t m = e >= 0 ? (v >> e) : (v << -e);                /* [2^23, 2^24) */
+    return (int32_t)(e * (int32_t)X32_ONE_OCT) + (int32_t)(m - X32_ONE_OCT);
+}
+uint32_t orc32_add_lpvip(uint32_t a, uint32_t b) {
+    uint32_t al = a & X32_LOGMASK, bl = b & X32_LOGMASK;
+    uint32_t mx = al > bl ? a : b;
+    uint32_t d = al > bl ? al - bl : bl - al;
+    int usedb = ((a ^ b) & X32_SIGNMASK) != 0;
+    if (d == 0 && usedb) return 0;
+    int32_t adj;
+    uint32_t u = mitchell_exp2_neg(d);
+    if (!usedb) {
+        adj = mitchell_log2(X32_ONE_OCT + u);
+    } else if (d < X32_ONE_OCT) {
+        adj = g_lpvip_db[d];
+    } else {
+        adj = (X32_ONE_OCT - u) ? mitchell_log2(X32_ONE_OCT - u) : 0;
+    }
+    int64_t p = (int64_t)(mx & X32_LOGMASK) + adj;
+    if (p < 0) p = 0;
+    if (p > (int64_t)X32_LOGMASK) p = X32_LOGMASK;
+    return (mx & X32_SIGNMASK) | (uint32_t)p;
+}
+
+/* ===================================================================== */
+/* Monte LFSR (lns-backend/src/lns-ops.cpp:178-195)                      */
+/* ===================================================================== */
+
+static uint16_t g_lfsr_log[65536], g_lfsr_alog[65535];
+
+uint16_t orc_lfsr_step(uint16_t s) {
+    uint16_t bit = s & 1u;
+    s >>= 1;
+    if (bit) s ^= 0xB400u;
+    return s;
+}
+
+static void build_lfsr(void) {
+    uint16_t s = 1;
+    for (uint32_t i = 0; i < 65535; i++) {
+        g_lfsr_alog[i] = s;
+        g_lfsr_log[s] = (uint16_t)i;
+        s = orc_lfsr_step(s);
+    }
+}
+
+/* state after n steps: the step is multiplication by a field generator */
+uint16_t orc_lfsr_jump(uint16_t s, uint64_t n) {
+    if (s == 0) return 0;
+    return g_lfsr_alog[((uint64_t)g_lfsr_log[s] + n % 65535u) % 65535u];
+}
+
+/*
+ * Monte add (restatement of Monte-Carlo LNS, xlnscpp's xlns16monte.cpp;
+ * README.md:112 "unbiased in expectation"): the Gaussian-log adjustment at
+ * 8 extra fraction bits is rounded stochastically with the low byte of the
+ * next LFSR state (one draw per addition, lns-ops.cpp:89-92).
+ */
+static inline uint16_t add16_monte(uint16_t a, uint16_t b, uint16_t * st) {
+    *st = orc_lfsr_step(*st);
+    int al = a & X16_LOGMASK, bl = b & X16_LOGMASK;
+    uint16_t mx = (al > bl) ? a : b;
+    int n = al > bl ? al - bl : bl - al;
+    int usedb = (a ^ b) & X16_SIGNMASK;
+    if (n == 0 && usedb) return X16_ZERO;
+    int fine = n < 2304 ? (usedb ? g_dbf[n] : g_sbf[n]) : 0;
+    int adj = (fine + (int)(*st & 0xFFu)) >> 8;
+    int p = (int)(mx & X16_LOGMASK) + adj;
+    if (p < 0) p = 0;
+    if (p > (int)X16_LOGMASK) p = X16_LOGMASK;
+    return (uint16_t)((mx & X16_SIGNMASK) | (uint16_t)p);
+}
+
+/* Monte by LPVIP: the term's 16 dither bits ride below the xlns16 LSB */
+static inline uint16_t add16_monte_bylpvip(uint16_t a, uint16_t b, uint16_t * st) {
+    *st = orc_lfsr_step(*st);
+    uint32_t r = orc32_add_lpvip((uint32_t)a << 16, ((uint32_t)b << 16) | *st);
+    return (uint16_t)(r >> 16);
+}
+
+/* ===================================================================== */
+/* Reductions (the GGML_LNS16_SUM policies, lns-cuda-xlns16.cu:67-130)   */
+/* ===================================================================== */
+
+static inline uint16_t narrow_sum32(uint32_t s) {          /* lns16-sum32.h:76-81 */
+    if ((s & X32_LOGMASK) >= 0x7FFF8000u) return (uint16_t)((s >> 16) | X16_LOGMASK);
+    return (uint16_t)((s + 0x8000u) >> 16);
+}
+
+typedef struct { uint32_t acc; uint16_t st; } red_t;
+
+static inline void red_from(int mode, red_t * r, uint16_t v) {
+    r->acc = (mode == ORC_LPVIP || mode == ORC_SUM32) ? ((uint32_t)v << 16) : v;
+}
+static inline void red_add(int mode, red_t * r, uint16_t t) {
+    switch (mode) {
+        case ORC_MONTE:         r->acc = add16_monte((uint16_t)r->acc, t, &r->st); break;
+        case ORC_MONTE_BYLPVIP: r->acc = add16_monte_bylpvip((uint16_t)r->acc, t, &r->st); break;
+        case ORC_LPVIP:         r->acc = orc32_add_lpvip(r->acc, (uint32_t)t << 16); break;
+        case ORC_SUM32:         r->acc = add32(r->acc, (uint32_t)t << 16); break;
+        default:                r->acc = orc16_add((uint16_t)r->acc, t); break;
+    }
+}
+static inline uint16_t red_finish(int mode, const red_t * r) {
+    if (mode == ORC_SUM32) return narrow_sum32(r->acc);
+    if (mode == ORC_LPVIP) return (uint16_t)(r->acc >> 16);
+    return (uint16_t)r->acc;
+}
+static inline int stochastic(int mode) { return mode == ORC_MONTE || mode == ORC_MONTE_BYLPVIP; }
+
+uint16_t orc16_sum(int mode, const uint16_t * a, int64_t n, uint16_t * lfsr) {
+    if (n == 0) return X16_ZERO;
+    red_t r;
+    r.st = lfsr ? *lfsr : 7;
+    red_from(mode, &r, a[0]);
+    for (int64_t i = 1; i < n; i++) red_add(mode, &r, a[i]);
+    if (lfsr) *lfsr = r.st;
+    return red_finish(mode, &r);
+}
+
+uint16_t orc16_vec_dot(int mode, const uint16_t * a, const uint16_t * b, int64_t n, uint16_t * lfsr) {
+    if (n == 0) return X16_ZERO;
+    red_t r;
+    r.st = lfsr ? *lfsr : 7;
+    red_from(mode, &r, orc16_mul(a[0], b[0]));
+    for (int64_t i = 1; i < n; i++) red_add(mode, &r, orc16_mul(a[i], b[i]));
+    if (lfsr) *lfsr = r.st;
+    return red_finish(mode, &r);
+}
+
+uint64_t orc_mul_mat_draws(int mode, int64_t K, int64_t M, int64_t N, int64_t ne12, int64_t ne13) {
+    if (!stochastic(mode) || K == 0) return 0;
+    return (uint64_t)ne12 * (uint64_t)ne13 * (uint64_t)M * (uint64_t)N * (uint64_t)(K - 1);
+}
+uint64_t orc_soft_max_draws(int mode, int64_t ncols, int64_t nrows) {
+    return stochastic(mode) && ncols > 0 ? (uint64_t)nrows * (uint64_t)(ncols - 1) : 0;
+}
+uint64_t orc_rms_norm_draws(int mode, int64_t ncols, int64_t nrows) {
+    return stochastic(mode) ? (uint64_t)nrows * (uint64_t)ncols : 0;
+}
+
+/* ===================================================================== */
+/* Ops                                                                    */
+/* ===================================================================== */
+
+/* lns_mul_mat (lns-ops.cpp:293-384): one sequential dot per output; outputs
+ * are independent, so threads split them without changing any bit. */
+void orc16_mul_mat(int mode, const uint16_t * w, const uint16_t * x, uint16_t * dst,
+                   int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne03, int64_t ne12, int64_t ne13,
+                   uint16_t monte_seed, int nthreads) {
+    const int64_t r2 = ne12 / ne02, r3 = ne13 / ne03;
+    const int64_t total = ne12 * ne13 * M * N;
+    (void)nthreads;
+#ifdef _OPENMP
+    #pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+#endif
+    for (int64_t o = 0; o < total; o++) {
+        /* o = ((z * M + m) * N + n), the CPU loop order (i13, i12, i0, i1) */
+        const int64_t n = o % N, m = (o / N) % M, z = o / (N * M);
+        const int64_t i12 = z % ne12, i13 = z / ne12;
+        const uint16_t * wr = w + (((i13 / r3) * ne02 + i12 / r2) * M + m) * K;
+        const uint16_t * xr = x + (z * N + n) * K;
+        uint16_t out;
+        if (K == 0) {
+            out = X16_ZERO;
+        } else {
+            red_t r;
+            r.st = stochastic(mode) ? orc_lfsr_jump(monte_seed, (uint64_t)o * (uint64_t)(K - 1)) : 0;
+            red_from(mode, &r, orc16_mul(wr[0], xr[0]));
+            for (int64_t k = 1; k < K; k++) red_add(mode, &r, orc16_mul(wr[k], xr[k]));
+            out = red_finish(mode, &r);
+        }
+        dst[(z * N + n) * M + m] = out;
+    }
+}
+
+void orc32_mul_mat(const uint32_t * w, const uint32_t * x, uint32_t * dst,
+                   int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne03, int64_t ne12, int64_t ne13,
+                   int nthreads) {
+    const int64_t r2 = ne12 / ne02, r3 = ne13 / ne03;
+    const int64_t total = ne12 * ne13 * M * N;
+    (void)nthreads;
+#ifdef _OPENMP
+    #pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+#endif
+    for (int64_t o = 0; o < total; o++) {
+        const int64_t n = o % N, m = (o / N) % M, z = o / (N * M);
+        const int64_t i12 = z % ne12, i13 = z / ne12;
+        const uint32_t * wr = w + (((i13 / r3) * ne02 + i12 / r2) * M + m) * K;
+        const uint32_t * xr = x + (z * N + n) * K;
+        uint32_t acc = 0;
+        if (K > 0) {
+            acc = mul32(wr[0], xr[0]);
+            for (int64_t k = 1; k < K; k++) acc = add32(acc, mul32(wr[k], xr[k]));
+        }
+        dst[(z * N + n) * M + m] = acc;
+    }
+}
+
+/* k_soft_max (lns-cuda-kernels.cuh:255-325) = xlns16_softmax[_masked]
+ * (lns16-sum32.h:158-198 shows the control flow) */
+void orc16_soft_max(int mode, const uint16_t * src, const int64_t ne[4], const uint16_t * mask,
+                    const int64_t mne[4], uint16_t scale, uint16_t * dst, uint16_t monte_seed, int nthreads) {
+    const int64_t n = ne[0], nrows = ne[1] * ne[2] * ne[3];
+    (void)nthreads;
+    if (n == 0) return;
+#ifdef _OPENMP
+    #pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+#endif
+    for (int64_t row = 0; row < nrows; row++) {
+        const int64_t i1 = row % ne[1], i2 = (row / ne[1]) % ne[2], i3 = row / (ne[1] * ne[2]);
+        const uint16_t * xs = src + row * n;
+        const uint16_t * ms = mask ? mask + (((i3 % mne[3]) * mne[2] + i2 % mne[2]) * mne[1] + i1) * n : NULL;
+        uint16_t * c = dst + row * n;
+        uint16_t mx = X16_NEG_INF;
+        for (int64_t i = 0; i < n; i++) {
+            uint16_t v = xs[i];
+            if (v != X16_NEG_INF) {
+                v = orc16_mul(v, scale);
+                if (ms) {
+                    if (ms[i] == X16_NEG_INF) v = X16_NEG_INF;
+                    else if (!is_zero16(ms[i])) v = orc16_add(v, ms[i]);
+                }
+            }
+            c[i] = v;
+            if (orc16_gt(v, mx)) mx = v;
+        }
+        for (int64_t i = 0; i < n; i++) c[i] = orc16_exp(orc16_sub(c[i], mx));
+        red_t r;
+        r.st = stochastic(mode) ? orc_lfsr_jump(monte_seed, (uint64_t)row * (uint64_t)(n - 1)) : 0;
+        red_from(mode, &r, c[0]);
+        for (int64_t i = 1; i < n; i++) red_add(mode, &r, c[i]);
+        const uint16_t total = red_finish(mode, &r);
+        for (int64_t i = 0; i < n; i++) c[i] = orc16_div(c[i], total);
+    }
+}
+
+void orc32_soft_max(const uint32_t * src, const int64_t ne[4], const uint32_t * mask,
+                    const int64_t mne[4], uint32_t scale, uint32_t * dst, int nthreads) {
+    const int64_t n = ne[0], nrows = ne[1] * ne[2] * ne[3];
+    (void)nthreads;
+    if (n == 0) return;
+#ifdef _OPENMP
+    #pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+#endif
+    for (int64_t row = 0; row < nrows; row++) {
+        const int64_t i1 = row % ne[1], i2 = (row / ne[1]) % ne[2], i3 = row / (ne[1] * ne[2]);
+        const uint32_t * xs = src + row * n;
+        const uint32_t * ms = mask ? mask + (((i3 % mne[3]) * mne[2] + i2 % mne[2]) * mne[1] + i1) * n : NULL;
+        uint32_t * c = dst + row * n;
+        uint32_t mx = X32_NEG_INF;
+        for (int64_t i = 0; i < n; i++) {
+            uint32_t v = xs[i];
+            if (v != X32_NEG_INF) {
+                v = mul32(v, scale);
+                if (ms) {
+                    if (ms[i] == X32_NEG_INF) v = X32_NEG_INF;
+                    else if (!is_zero32(ms[i])) v = add32(v, ms[i]);
+                }
+            }
+            c[i] = v;
+            if (gt32(v, mx)) mx = v;
+        }
+        for (int64_t i = 0; i < n; i++) c[i] = exp32(sub32(c[i], mx));
+        uint32_t total = c[0];
+        for (int64_t i = 1; i < n; i++) total = add32(total, c[i]);
+        for (int64_t i = 0; i < n; i++) c[i] = div32(c[i], total);
+    }
+}
+
+/* k_rms_norm (lns-cuda-kernels.cuh:225-250) = xlns16_rms_norm[_sum32]
+ * (lns16-sum32.h:142-151): sum of squares from zero, n additions */
+void orc16_rms_norm(int mode, const uint16_t * src, uint16_t * dst, int64_t ncols, int64_t nrows,
+                    float eps, uint16_t monte_seed, int nthreads) {
+    (void)nthreads;
+    if (ncols == 0) return;
+    const uint16_t eps_l = orc16_from_f32(eps);
+    const uint16_t inv_n = orc16_from_f32(1.0f / (float)ncols);
+#ifdef _OPENMP
+    #pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+#endif
+    for (int64_t row = 0; row < nrows; row++) {
+        const uint16_t * xs = src + row * ncols;
+        red_t r;
+        r.st = stochastic(mode) ? orc_lfsr_jump(monte_seed, (uint64_t)row * (uint64_t)ncols) : 0;
+        red_from(mode, &r, X16_ZERO);
+        for (int64_t i = 0; i < ncols; i++) red_add(mode, &r, orc16_mul(xs[i], xs[i]));
+        const uint16_t mean = orc16_mul(red_finish(mode, &r), inv_n);
+        const uint16_t inv = orc16_recip(orc16_sqrt(orc16_add(mean, eps_l)));
+        for (int64_t i = 0; i < ncols; i++) dst[row * ncols + i] = orc16_mul(xs[i], inv);
+    }
+}
+
+void orc32_rms_norm(const uint32_t * src, uint32_t * dst, int64_t ncols, int64_t nrows, float eps, int nthreads) {
+    (void)nthreads;
+    if (ncols == 0) return;
+    const uint32_t eps_l = orc32_from_f32(eps);
+    const uint32_t inv_n = orc32_from_f32(1.0f / (float)ncols);
+#ifdef _OPENMP
+    #pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+#endif
+    for (int64_t row = 0; row < nrows; row++) {
+        const uint32_t * xs = src + row * ncols;
+        uint32_t acc = 0;
+        for (int64_t i = 0; i < ncols; i++) acc = add32(acc, mul32(xs[i], xs[i]));
+        const uint32_t mean = mul32(acc, inv_n);
+        const uint32_t inv = recip32(sqrt32(add32(mean, eps_l)));
+        for (int64_t i = 0; i < ncols; i++) dst[row * ncols + i] = mul32(xs[i], inv);
+    }
+}
+
+void orc16_from_f32_n(const float * src, uint16_t * dst, int64_t n) { for (int64_t i = 0; i < n; i++) dst[i] = orc16_from_f32(src[i]); }
+void orc16_to_f32_n(const uint16_t * src, float * dst, int64_t n) { for (int64_t i = 0; i < n; i++) dst[i] = g_dec16[src[i]]; }
+void orc32_from_f32_n(const float * src, uint32_t * dst, int64_t n) { for (int64_t i = 0; i < n; i++) dst[i] = orc32_from_f32(src[i]); }
+void orc32_to_f32_n(const uint32_t * src, float * dst, int64_t n) { for (int64_t i = 0; i < n; i++) dst[i] = orc32_to_f32(src[i]); }
+
+int orc_init(void) {
+    if (g_ready) return 0;
+    build16();
+    if (build32() != 0) return -1;
+    build_lfsr();
+    g_ready = 1;
+    return 0;
+}

@@ -1,0 +1,114 @@
+/*
+ * lns_oracle.h -- CPU restatement of the reference's LNS16/LNS32 reduction
+ * hot path.  TEST INFRASTRUCTURE ONLY: tests/, __graft_entry__.smoke() and
+ * bench.py's CPU-baseline leg may call this library, as the checker; the
+ * product (the CUDA library under xlns-ggml-backend_b200/) never links it.
+ *
+ * What it restates (reference = xlnsresearch/xlns-ggml-backend):
+ *   - xlns16 / xlns32 arithmetic of the external library xlnscpp
+ *     @ 41843b034689d5ca91e32a0043cc37265fb2ef5c (absent from the reference
+ *     checkout; patches/xlnscpp-base-commit.txt).  The published algorithm
+ *     (Gaussian-logarithm addition via sb/db tables, F=7 / F=23 fixed point)
+ *     is restated from the mathematics; every choice the reference's own
+ *     committed outputs could decide was checked against them (see
+ *     tests/golden/reference_pins.json and tests/test_oracle_pins.py).
+ *   - the four GGML_LNS16_SUM reductions (lns-backend/src/lns-ops.cpp:110-134,
+ *     lns-backend/cuda/lns-cuda-xlns16.cu:67-130, lns-backend/src/lns16-sum32.h).
+ *   - the op loops of lns_mul_mat / lns_soft_max / lns_rms_norm
+ *     (lns-backend/src/lns-ops.cpp:293-384, 643-736) and their xlns32 twins
+ *     (lns-backend/src32/lns32-ops.cpp:98-144, 384-478), in the per-output
+ *     form of lns-backend/cuda/lns-cuda-kernels.cuh:80-325.
+ *   - the Monte LFSR (lns-backend/src/lns-ops.cpp:155-195).
+ *
+ * Parity status: the xlns16 base adder and the operand products are pinned by
+ * the reference's printed known answers; the float->xlns16 conversion table,
+ * the xlns32 adder, the Monte dither rule and the LPVIP adder are restated
+ * algorithms whose bit patterns the reference checkout cannot confirm
+ * ("parity unpinned" for those parts -- see DESIGN.md).
+ */
+#ifndef LNS_ORACLE_H
+#define LNS_ORACLE_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* summation modes (GGML_LNS16_SUM, plus GGML_LNS16_MONTE_BYLPVIP) */
+enum { ORC_BASE = 0, ORC_MONTE = 1, ORC_MONTE_BYLPVIP = 2, ORC_LPVIP = 3, ORC_SUM32 = 4 };
+
+int      orc_init(void);            /* builds every table; idempotent; 0 = ok */
+void     orc_set_knot_mode(int m);  /* probe hook: xlns32 knot rounding (before init) */
+
+/* ---- xlns16 scalar arithmetic ---- */
+uint16_t orc16_from_f32(float x);
+float    orc16_to_f32(uint16_t v);
+uint16_t orc16_mul(uint16_t a, uint16_t b);
+uint16_t orc16_div(uint16_t a, uint16_t b);
+uint16_t orc16_add(uint16_t a, uint16_t b);
+uint16_t orc16_sub(uint16_t a, uint16_t b);
+uint16_t orc16_exp(uint16_t a);
+uint16_t orc16_sqrt(uint16_t a);
+uint16_t orc16_recip(uint16_t a);
+int      orc16_gt(uint16_t a, uint16_t b);
+
+/* ---- xlns32 scalar arithmetic ---- */
+uint32_t orc32_from_f32(float x);
+float    orc32_to_f32(uint32_t v);
+uint32_t orc32_mul(uint32_t a, uint32_t b);
+uint32_t orc32_add(uint32_t a, uint32_t b);
+uint32_t orc32_add_lpvip(uint32_t a, uint32_t b);
+float    orc_expf(float x);
+
+/* ---- Monte LFSR ---- */
+uint16_t orc_lfsr_step(uint16_t s);
+uint16_t orc_lfsr_jump(uint16_t s, uint64_t n);
+
+/* ---- reductions over xlns16 terms (mode = ORC_*) ---- */
+uint16_t orc16_sum(int mode, const uint16_t * a, int64_t n, uint16_t * lfsr);
+uint16_t orc16_vec_dot(int mode, const uint16_t * a, const uint16_t * b, int64_t n, uint16_t * lfsr);
+
+/* ---- draw accounting (lns-cuda-kernels.cuh:371-382) ---- */
+uint64_t orc_mul_mat_draws(int mode, int64_t K, int64_t M, int64_t N, int64_t ne12, int64_t ne13);
+uint64_t orc_soft_max_draws(int mode, int64_t ncols, int64_t nrows);
+uint64_t orc_rms_norm_draws(int mode, int64_t ncols, int64_t nrows);
+
+/*
+ * Ops on codes.  Layouts are ggml element order:
+ *   w   [ne03][ne02][M][K]   (weight row m = ggml src0 row)
+ *   x   [ne13][ne12][N][K]
+ *   dst [ne13][ne12][N][M]
+ * monte_seed is the LFSR state where the op's first reduction starts.
+ * nthreads > 1 parallelises over independent outputs (bitwise identical).
+ */
+void orc16_mul_mat(int mode, const uint16_t * w, const uint16_t * x, uint16_t * dst,
+                   int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne03, int64_t ne12, int64_t ne13,
+                   uint16_t monte_seed, int nthreads);
+void orc32_mul_mat(const uint32_t * w, const uint32_t * x, uint32_t * dst,
+                   int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne03, int64_t ne12, int64_t ne13,
+                   int nthreads);
+/* src [ne3][ne2][ne1][ne0]; mask (may be NULL) [mne3][mne2][mne1][ne0] codes */
+void orc16_soft_max(int mode, const uint16_t * src, const int64_t ne[4], const uint16_t * mask,
+                    const int64_t mne[4], uint16_t scale, uint16_t * dst, uint16_t monte_seed, int nthreads);
+void orc32_soft_max(const uint32_t * src, const int64_t ne[4], const uint32_t * mask,
+                    const int64_t mne[4], uint32_t scale, uint32_t * dst, int nthreads);
+void orc16_rms_norm(int mode, const uint16_t * src, uint16_t * dst, int64_t ncols, int64_t nrows,
+                    float eps, uint16_t monte_seed, int nthreads);
+void orc32_rms_norm(const uint32_t * src, uint32_t * dst, int64_t ncols, int64_t nrows, float eps, int nthreads);
+
+/* mask conversion of ggml's F32 mask (lns-ops.cpp:634-637, lns32-ops.cpp:376) */
+uint16_t orc16_mask_from_f32(float m);
+uint32_t orc32_mask_from_f32(float m);
+
+/* batch conversions */
+void orc16_from_f32_n(const float * src, uint16_t * dst, int64_t n);
+void orc16_to_f32_n(const uint16_t * src, float * dst, int64_t n);
+void orc32_from_f32_n(const float * src, uint32_t * dst, int64_t n);
+void orc32_to_f32_n(const uint32_t * src, float * dst, int64_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,184 @@
+"""ctypes access to the CPU oracle (oracle/_build/liblns_oracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg, as the checker.  The product never imports it.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+BUILD = os.path.join(HERE, "_build")
+SO = os.path.join(BUILD, "liblns_oracle.so")
+PINCHECK = os.path.join(BUILD, "pincheck")
+
+MODE = {"base": 0, "monte": 1, "monte_bylpvip": 2, "lpvip": 3, "sum32": 4}
+
+_lib = None
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(SO):
+            build()
+        L = ctypes.CDLL(SO)
+        u16p = np.ctypeslib.ndpointer(np.uint16, flags="C")
+        u32p = np.ctypeslib.ndpointer(np.uint32, flags="C")
+        f32p = np.ctypeslib.ndpointer(np.float32, flags="C")
+        i64 = ctypes.c_int64
+        i64a = ctypes.POINTER(ctypes.c_int64)
+        sig = {
+            "orc_init": (ctypes.c_int, []),
+            "orc16_from_f32": (ctypes.c_uint16, [ctypes.c_float]),
+            "orc16_to_f32": (ctypes.c_float, [ctypes.c_uint16]),
+            "orc16_add": (ctypes.c_uint16, [ctypes.c_uint16, ctypes.c_uint16]),
+            "orc16_mul": (ctypes.c_uint16, [ctypes.c_uint16, ctypes.c_uint16]),
+            "orc32_add": (ctypes.c_uint32, [ctypes.c_uint32, ctypes.c_uint32]),
+            "orc32_from_f32": (ctypes.c_uint32, [ctypes.c_float]),
+            "orc_lfsr_step": (ctypes.c_uint16, [ctypes.c_uint16]),
+            "orc_lfsr_jump": (ctypes.c_uint16, [ctypes.c_uint16, ctypes.c_uint64]),
+            "orc_mul_mat_draws": (ctypes.c_uint64, [ctypes.c_int, i64, i64, i64, i64, i64]),
+            "orc_soft_max_draws": (ctypes.c_uint64, [ctypes.c_int, i64, i64]),
+            "orc_rms_norm_draws": (ctypes.c_uint64, [ctypes.c_int, i64, i64]),
+            "orc16_mul_mat": (None, [ctypes.c_int, u16p, u16p, u16p, i64, i64, i64, i64, i64, i64, i64,
+                                     ctypes.c_uint16, ctypes.c_int]),
+            "orc32_mul_mat": (None, [u32p, u32p, u32p, i64, i64, i64, i64, i64, i64, i64, ctypes.c_int]),
+            "orc16_soft_max": (None, [ctypes.c_int, u16p, i64a, ctypes.c_void_p, i64a, ctypes.c_uint16, u16p,
+                                      ctypes.c_uint16, ctypes.c_int]),
+            "orc32_soft_max": (None, [u32p, i64a, ctypes.c_void_p, i64a, ctypes.c_uint32, u32p, ctypes.c_int]),
+            "orc16_rms_norm": (None, [ctypes.c_int, u16p, u16p, i64, i64, ctypes.c_float, ctypes.c_uint16, ctypes.c_int]),
+            "orc32_rms_norm": (None, [u32p, u32p, i64, i64, ctypes.c_float, ctypes.c_int]),
+            "orc16_mask_from_f32": (ctypes.c_uint16, [ctypes.c_float]),
+            "orc32_mask_from_f32": (ctypes.c_uint32, [ctypes.c_float]),
+            "orc16_from_f32_n": (None, [f32p, u16p, i64]),
+            "orc16_to_f32_n": (None, [u16p, f32p, i64]),
+            "orc32_from_f32_n": (None, [f32p, u32p, i64]),
+            "orc32_to_f32_n": (None, [u32p, f32p, i64]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        if L.orc_init() != 0:
+            raise RuntimeError("oracle table construction failed")
+        _lib = L
+    return _lib
+
+
+def _ne(shape):
+    return (ctypes.c_int64 * 4)(*(list(shape) + [1] * (4 - len(shape))))
+
+
+def from_f32_16(a):
+    a = np.ascontiguousarray(a, np.float32)
+    out = np.empty(a.shape, np.uint16)
+    lib().orc16_from_f32_n(a.ravel(), out.ravel(), a.size)
+    return out
+
+
+def to_f32_16(c):
+    c = np.ascontiguousarray(c, np.uint16)
+    out = np.empty(c.shape, np.float32)
+    lib().orc16_to_f32_n(c.ravel(), out.ravel(), c.size)
+    return out
+
+
+def from_f32_32(a):
+    a = np.ascontiguousarray(a, np.float32)
+    out = np.empty(a.shape, np.uint32)
+    lib().orc32_from_f32_n(a.ravel(), out.ravel(), a.size)
+    return out
+
+
+def to_f32_32(c):
+    c = np.ascontiguousarray(c, np.uint32)
+    out = np.empty(c.shape, np.float32)
+    lib().orc32_to_f32_n(c.ravel(), out.ravel(), c.size)
+    return out
+
+
+def mul_mat16(mode, w_rows, x, slices=(1, 1, 1, 1), seed=7, nthreads=1):
+    """w_rows: codes [ne03][ne02][M][K] (weight rows), x: codes [ne13][ne12][N][K];
+    returns codes [ne13][ne12][N][M]."""
+    ne02, ne03, ne12, ne13 = slices
+    M, K = w_rows.shape[-2], w_rows.shape[-1]
+    N = x.shape[-2]
+    w = np.ascontiguousarray(w_rows, np.uint16).reshape(-1)
+    xx = np.ascontiguousarray(x, np.uint16).reshape(-1)
+    out = np.empty(ne12 * ne13 * N * M, np.uint16)
+    lib().orc16_mul_mat(MODE[mode], w, xx, out, K, M, N, ne02, ne03, ne12, ne13, seed, nthreads)
+    return out.reshape(ne13, ne12, N, M) if (ne12 * ne13) > 1 else out.reshape(N, M)
+
+
+def mul_mat32(w_rows, x, slices=(1, 1, 1, 1), nthreads=1):
+    ne02, ne03, ne12, ne13 = slices
+    M, K = w_rows.shape[-2], w_rows.shape[-1]
+    N = x.shape[-2]
+    w = np.ascontiguousarray(w_rows, np.uint32).reshape(-1)
+    xx = np.ascontiguousarray(x, np.uint32).reshape(-1)
+    out = np.empty(ne12 * ne13 * N * M, np.uint32)
+    lib().orc32_mul_mat(w, xx, out, K, M, N, ne02, ne03, ne12, ne13, nthreads)
+    return out.reshape(ne13, ne12, N, M) if (ne12 * ne13) > 1 else out.reshape(N, M)
+
+
+def soft_max16(mode, src, shape, mask=None, mask_shape=None, scale_code=0x4000, seed=7, nthreads=1):
+    s = np.ascontiguousarray(src, np.uint16).reshape(-1)
+    out = np.empty_like(s)
+    m = None if mask is None else np.ascontiguousarray(mask, np.uint16).reshape(-1)
+    lib().orc16_soft_max(MODE[mode], s, _ne(shape), None if m is None else m.ctypes.data_as(ctypes.c_void_p),
+                         _ne(mask_shape or (1, 1, 1, 1)), scale_code, out, seed, nthreads)
+    return out
+
+
+def soft_max32(src, shape, mask=None, mask_shape=None, scale_code=0x40000000, nthreads=1):
+    s = np.ascontiguousarray(src, np.uint32).reshape(-1)
+    out = np.empty_like(s)
+    m = None if mask is None else np.ascontiguousarray(mask, np.uint32).reshape(-1)
+    lib().orc32_soft_max(s, _ne(shape), None if m is None else m.ctypes.data_as(ctypes.c_void_p),
+                         _ne(mask_shape or (1, 1, 1, 1)), scale_code, out, nthreads)
+    return out
+
+
+def rms_norm16(mode, src, ncols, nrows, eps, seed=7, nthreads=1):
+    s = np.ascontiguousarray(src, np.uint16).reshape(-1)
+    out = np.empty_like(s)
+    lib().orc16_rms_norm(MODE[mode], s, out, ncols, nrows, eps, seed, nthreads)
+    return out
+
+
+def rms_norm32(src, ncols, nrows, eps, nthreads=1):
+    s = np.ascontiguousarray(src, np.uint32).reshape(-1)
+    out = np.empty_like(s)
+    lib().orc32_rms_norm(s, out, ncols, nrows, eps, nthreads)
+    return out
+
+
+def mask16(m):
+    m = np.ascontiguousarray(m, np.float32)
+    return np.array([lib().orc16_mask_from_f32(float(v)) for v in m.ravel()], np.uint16).reshape(m.shape)
+
+
+def mask32(m):
+    m = np.ascontiguousarray(m, np.float32)
+    return np.array([lib().orc32_mask_from_f32(float(v)) for v in m.ravel()], np.uint32).reshape(m.shape)
+
+
+def lfsr_jump(s, n):
+    return lib().orc_lfsr_jump(s, n)
+
+
+def pincheck():
+    import json
+    if not os.path.exists(PINCHECK):
+        build()
+    out = json.loads(subprocess.run([PINCHECK], capture_output=True, text=True, check=True).stdout)
+    standalone = {k: out.pop(k) for k in ("two_term", "ones", "long_dot", "rms_standalone")}
+    out["standalone"] = standalone
+    return out

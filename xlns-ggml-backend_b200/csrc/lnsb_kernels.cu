@@ -1,0 +1,892 @@
+// B200 (sm_100a) kernels of the LNSCUDA16 / LNSCUDA32 hot path and the C ABI
+// of include/lnsb200.h.
+//
+// The hot path is the reduction inside three ops (lns-backend/cuda/
+// lns-cuda-kernels.cuh:80-157, 225-250, 255-325): every output is one
+// sequential chain of LNS additions, in element order, because LNS addition
+// is not associative.  Parallelism therefore comes only from independent
+// outputs; each kernel below is organised around keeping as many chains in
+// flight as possible per SM, with operands staged in shared memory and the
+// Gaussian-log table resident there.
+#include <cuda_runtime.h>
+
+#include <array>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "lnsb200.h"
+#include "lnsb_arith.cuh"
+#include "lnsb_tables.h"
+
+namespace lnsb {
+
+uint32_t host_from_f32_32(float x);   // defined below; the host twin of from_f32_32
+
+namespace {
+
+constexpr int k_max_devices = 64;
+
+// ============================ table registry ===============================
+
+struct device_slot {
+    bool       ready16 = false, ready32 = false;
+    dev_tables t{};
+};
+std::mutex                                 g_mu;
+std::array<device_slot, k_max_devices>     g_slots;
+
+template <class T>
+cudaError_t upload(const std::vector<T> & v, const T ** out) {
+    if (v.empty()) { *out = nullptr; return cudaSuccess; }
+    void * p = nullptr;
+    cudaError_t e = cudaMalloc(&p, v.size() * sizeof(T));
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpy(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { cudaFree(p); return e; }
+    *out = static_cast<const T *>(p);
+    return cudaSuccess;
+}
+
+int current_device(int * dev) {
+    const cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return (int) e;
+    if (*dev < 0 || *dev >= k_max_devices) return LNSB_E_NO_DEVICE;
+    return 0;
+}
+
+// the current device's tables, or an error if lnsb_upload_tables did not run
+int tables_for(int fmt, const dev_tables ** out) {
+    int dev = 0;
+    const int st = current_device(&dev);
+    if (st != 0) return st;
+    std::lock_guard<std::mutex> lock(g_mu);
+    const device_slot & s = g_slots[dev];
+    if (fmt == LNSB_XLNS16 ? !s.ready16 : !s.ready32) return LNSB_E_NO_TABLES;
+    *out = &s.t;
+    return 0;
+}
+
+__host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+int status_of(cudaError_t e) { return e == cudaSuccess ? 0 : (int) e; }
+int launch_status() { return status_of(cudaGetLastError()); }
+
+bool valid_fmt(int fmt) { return fmt == LNSB_XLNS16 || fmt == LNSB_XLNS32; }
+
+unsigned grid_for(int64_t n, int block) {
+    int64_t b = (n + block - 1) / block;
+    if (b < 1) b = 1;
+    if (b > 148 * 64) b = 148 * 64;     // grid-stride beyond 64 blocks per SM
+    return (unsigned) b;
+}
+
+// ============================ conversions ==================================
+
+template <int FMT>
+__global__ void k_to_lns(dev_tables T, const float * __restrict__ src, void * __restrict__ dst, int64_t n) {
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t) blockDim.x * gridDim.x) {
+        if constexpr (FMT == 16) static_cast<uint16_t *>(dst)[i] = (uint16_t) from_f32_16(T, src[i]);
+        else                     static_cast<uint32_t *>(dst)[i] = from_f32_32(T, src[i]);
+    }
+}
+
+// dst[c * dst_ld + r] = lns(src[r * cols + c]), through a 32x32 shared tile so
+// both the F32 reads and the LNS writes are coalesced
+template <int FMT>
+__global__ void k_to_lns_transposed(dev_tables T, const float * __restrict__ src, void * __restrict__ dst,
+                                    int64_t rows, int64_t cols, int64_t dst_ld) {
+    using V = typename std::conditional<FMT == 16, uint16_t, uint32_t>::type;
+    __shared__ V tile[32][33];
+    const int64_t r0 = (int64_t) blockIdx.y * 32, c0 = (int64_t) blockIdx.x * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int64_t r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) {
+            const float f = src[r * cols + c];
+            tile[i][threadIdx.x] = FMT == 16 ? (V) from_f32_16(T, f) : (V) from_f32_32(T, f);
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int64_t c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) static_cast<V *>(dst)[c * dst_ld + r] = tile[threadIdx.x][i];
+    }
+}
+
+template <int FMT>
+__global__ void k_to_f32(dev_tables T, const void * __restrict__ src, float * __restrict__ dst, int64_t n) {
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t) blockDim.x * gridDim.x) {
+        if constexpr (FMT == 16) dst[i] = to_f32_16(T, static_cast<const uint16_t *>(src)[i]);
+        else                     dst[i] = to_f32_32(T, static_cast<const uint32_t *>(src)[i]);
+    }
+}
+
+// ============================ MUL_MAT (xlns16) =============================
+//
+// CTA tile: BM = 32 weight rows x BN = 64 tokens, 256 threads; each thread
+// owns TM = 2 rows x TN = 4 tokens = 8 independent chains and interleaves
+// their additions, so eight dependent table lookups are in flight per thread.
+// K advances in chunks of KC = 64: the k-major weight tile [KC][BM] and the
+// activation tile [BN][KC] are staged in shared memory with cp.async (double
+// buffered); the Gaussian-log table (6.7 KB) is resident in shared memory for
+// the whole kernel.  A thread reads 2 weights per k with one 32-bit load and
+// 8 k-steps of a token with one 128-bit load.
+constexpr int MM_BM = 32, MM_BN = 64, MM_KC = 64, MM_TM = 2, MM_TN = 4;
+constexpr int MM_THREADS = (MM_BM / MM_TM) * (MM_BN / MM_TN);   // 256
+constexpr int MM_XPITCH  = MM_KC + 8;                           // halfwords, breaks bank aliasing
+constexpr int MM_WTILE   = MM_KC * MM_BM;                       // halfwords
+constexpr int MM_XTILE   = MM_BN * MM_XPITCH;                   // halfwords
+constexpr int MM_TABPAD  = (k16_tab_bytes + 15) / 16 * 16;       // keeps the tiles 16-byte aligned
+constexpr int MM_FINE    = k_mode == M_MONTE ? 2 * k16_monte_n * 2 : 0;
+constexpr int MM_SMEM    = MM_TABPAD + MM_FINE + 2 * (MM_WTILE + MM_XTILE) * 2;
+
+__device__ __forceinline__ void cp_async16(void * smem, const void * gmem) {
+    const unsigned s = (unsigned) __cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// Stage one K chunk.  vec: 16-byte aligned rows and full tiles (fast path).
+__device__ __forceinline__ void mm16_stage(uint16_t * ws, uint16_t * xs, const uint16_t * __restrict__ W,
+                                           const uint16_t * __restrict__ X, int64_t K, int64_t M, int64_t N,
+                                           int64_t m0, int64_t n0, int64_t k0, bool vec) {
+    const int tid = threadIdx.x;
+    if (vec) {
+        {   // weights: KC rows of BM halfwords = 4 x 16 B each -> 256 copies
+            const int r = tid >> 2, q = tid & 3;
+            const int64_t k = k0 + r;
+            if (k < K) cp_async16(ws + r * MM_BM + q * 8, W + k * M + m0 + q * 8);
+        }
+#pragma unroll
+        for (int it = 0; it < 2; it++) {   // tokens: BN rows of KC halfwords = 8 x 16 B -> 512 copies
+            const int c = tid + it * MM_THREADS;
+            const int r = c >> 3, q = c & 7;
+            const int64_t n = n0 + r;
+            if (n < N && k0 + q * 8 < K) cp_async16(xs + r * MM_XPITCH + q * 8, X + n * K + k0 + q * 8);
+        }
+    } else {
+        for (int i = tid; i < MM_WTILE; i += MM_THREADS) {
+            const int r = i / MM_BM, c = i % MM_BM;
+            const int64_t k = k0 + r, m = m0 + c;
+            ws[r * MM_BM + c] = (k < K && m < M) ? W[k * M + m] : (uint16_t) 0;
+        }
+        for (int i = tid; i < MM_BN * MM_KC; i += MM_THREADS) {
+            const int r = i / MM_KC, c = i % MM_KC;
+            const int64_t n = n0 + r, k = k0 + c;
+            xs[r * MM_XPITCH + c] = (n < N && k < K) ? X[n * K + k] : (uint16_t) 0;
+        }
+    }
+}
+
+template <bool OUT_F32>
+__global__ void __launch_bounds__(MM_THREADS)
+k_mul_mat16(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X, void * __restrict__ dst,
+            int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3,
+            uint32_t monte_seed, int vec) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    int16_t *  tab  = reinterpret_cast<int16_t *>(smem);
+    int16_t *  fine = reinterpret_cast<int16_t *>(smem + MM_TABPAD);
+    uint16_t * tiles = reinterpret_cast<uint16_t *>(smem + MM_TABPAD + MM_FINE);
+    uint16_t * wsb[2] = { tiles, tiles + MM_WTILE + MM_XTILE };
+    uint16_t * xsb[2] = { tiles + MM_WTILE, tiles + 2 * MM_WTILE + MM_XTILE };
+
+    for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += MM_THREADS) tab[i] = T.sbdb16[i];
+    if constexpr (k_mode == M_MONTE) {
+        for (int i = threadIdx.x; i < 2 * k16_monte_n; i += MM_THREADS) fine[i] = T.monte16[i];
+    }
+
+    const int64_t z   = blockIdx.z;
+    const int64_t i12 = z % ne12, i13 = z / ne12;
+    const int64_t m0  = (int64_t) blockIdx.x * MM_BM, n0 = (int64_t) blockIdx.y * MM_BN;
+    const uint16_t * Wz = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
+    const uint16_t * Xz = X + z * N * K;
+
+    const int ty = threadIdx.x / (MM_BN / MM_TN), tx = threadIdx.x % (MM_BN / MM_TN);
+    const int mloc = ty * MM_TM;                           // rows mloc, mloc + 1
+    // tokens tx, tx + 16, tx + 32, tx + 48 (strided so a warp's 128-bit loads
+    // walk consecutive tile rows)
+
+    red16 R{ &T, tab, fine };
+    uint32_t acc[MM_TM][MM_TN];
+    uint32_t st[MM_TM][MM_TN];
+
+    const int nchunks = (int) ((K + MM_KC - 1) / MM_KC);
+    if (nchunks > 0) {
+        mm16_stage(wsb[0], xsb[0], Wz, Xz, K, M, N, m0, n0, 0, vec != 0);
+        cp_async_commit();
+    }
+    for (int c = 0; c < nchunks; c++) {
+        if (c + 1 < nchunks) {
+            mm16_stage(wsb[(c + 1) & 1], xsb[(c + 1) & 1], Wz, Xz, K, M, N, m0, n0, (int64_t) (c + 1) * MM_KC, vec != 0);
+            cp_async_commit();
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const uint16_t * ws = wsb[c & 1];
+        const uint16_t * xs = xsb[c & 1];
+        const int kvalid = (int) imin64(MM_KC, K - (int64_t) c * MM_KC);
+        int kk = 0;
+        if (c == 0) {
+            // first term of every chain: the product at k = 0
+            const uint32_t w2 = *reinterpret_cast<const uint32_t *>(ws + mloc);
+#pragma unroll
+            for (int i = 0; i < MM_TM; i++) {
+                const uint32_t w = (w2 >> (16 * i)) & 0xFFFFu;
+#pragma unroll
+                for (int j = 0; j < MM_TN; j++) {
+                    const uint32_t x = xs[(tx + 16 * j) * MM_XPITCH];
+                    acc[i][j] = R.from(mul16(w, x));
+                    if constexpr (k_stochastic) {
+                        const int64_t m = m0 + mloc + i, n = n0 + tx + 16 * j;
+                        const unsigned long long out = ((unsigned long long) z * (unsigned long long) M +
+                                                        (unsigned long long) m) * (unsigned long long) N +
+                                                       (unsigned long long) n;
+                        st[i][j] = lfsr_jump(T, monte_seed, out * (unsigned long long) (K - 1));
+                    } else {
+                        st[i][j] = 0;
+                    }
+                }
+            }
+            kk = 1;
+        }
+        if (kvalid == MM_KC) {
+            // full chunk: 8-step blocks; the first block of chunk 0 starts at k = 1
+            if (kk == 1) {
+#pragma unroll
+                for (int k = 1; k < 8; k++) {
+                    const uint32_t w2 = *reinterpret_cast<const uint32_t *>(ws + k * MM_BM + mloc);
+#pragma unroll
+                    for (int i = 0; i < MM_TM; i++) {
+                        const uint32_t w = (w2 >> (16 * i)) & 0xFFFFu;
+#pragma unroll
+                        for (int j = 0; j < MM_TN; j++) {
+                            acc[i][j] = R.add(acc[i][j], mul16(w, xs[(tx + 16 * j) * MM_XPITCH + k]), st[i][j]);
+                        }
+                    }
+                }
+                kk = 8;
+            }
+            for (; kk < MM_KC; kk += 8) {
+                uint4 xv[MM_TN];
+#pragma unroll
+                for (int j = 0; j < MM_TN; j++) xv[j] = *reinterpret_cast<const uint4 *>(xs + (tx + 16 * j) * MM_XPITCH + kk);
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const uint32_t w2 = *reinterpret_cast<const uint32_t *>(ws + (kk + u) * MM_BM + mloc);
+#pragma unroll
+                    for (int i = 0; i < MM_TM; i++) {
+                        const uint32_t w = (w2 >> (16 * i)) & 0xFFFFu;
+#pragma unroll
+                        for (int j = 0; j < MM_TN; j++) {
+                            const uint32_t word = u < 2 ? xv[j].x : u < 4 ? xv[j].y : u < 6 ? xv[j].z : xv[j].w;
+                            const uint32_t x = (word >> (16 * (u & 1))) & 0xFFFFu;
+                            acc[i][j] = R.add(acc[i][j], mul16(w, x), st[i][j]);
+                        }
+                    }
+                }
+            }
+        } else {
+            for (; kk < kvalid; kk++) {
+                const uint32_t w2 = *reinterpret_cast<const uint32_t *>(ws + kk * MM_BM + mloc);
+#pragma unroll
+                for (int i = 0; i < MM_TM; i++) {
+                    const uint32_t w = (w2 >> (16 * i)) & 0xFFFFu;
+#pragma unroll
+                    for (int j = 0; j < MM_TN; j++) {
+                        acc[i][j] = R.add(acc[i][j], mul16(w, xs[(tx + 16 * j) * MM_XPITCH + kk]), st[i][j]);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+#pragma unroll
+    for (int i = 0; i < MM_TM; i++) {
+        const int64_t m = m0 + mloc + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < MM_TN; j++) {
+            const int64_t n = n0 + tx + 16 * j;
+            if (n >= N) continue;
+            const uint32_t v = K == 0 ? 0u : R.finish(acc[i][j]);
+            const int64_t o = (z * N + n) * M + m;
+            if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
+            else                   static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
+        }
+    }
+}
+
+// ============================ MUL_MAT (xlns32) =============================
+// One chain per thread: block = 64 weight rows (threads) x 1 token group of 4.
+template <bool OUT_F32>
+__global__ void __launch_bounds__(128)
+k_mul_mat32(dev_tables T, const uint32_t * __restrict__ W, const uint32_t * __restrict__ X, void * __restrict__ dst,
+            int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3) {
+    constexpr int NB = 4;
+    const int64_t m = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t n0 = (int64_t) blockIdx.y * NB;
+    const int64_t z = blockIdx.z, i12 = z % ne12, i13 = z / ne12;
+    if (m >= M) return;
+    const uint32_t * ws = W + ((i13 / r3) * ne02 + i12 / r2) * K * M + m;
+    const uint32_t * xs = X + z * N * K + n0 * K;
+    const int nb = (int) imin64(NB, N - n0);
+    uint32_t acc[NB] = { 0, 0, 0, 0 };
+    if (K > 0) {
+        const uint32_t w0 = ws[0];
+#pragma unroll
+        for (int j = 0; j < NB; j++) if (j < nb) acc[j] = mul32(w0, __ldg(xs + j * K));
+        for (int64_t k = 1; k < K; k++) {
+            const uint32_t w = ws[k * M];
+#pragma unroll
+            for (int j = 0; j < NB; j++) if (j < nb) acc[j] = add32(T, acc[j], mul32(w, __ldg(xs + j * K + k)));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < NB; j++) {
+        if (j >= nb) continue;
+        const int64_t o = (z * N + n0 + j) * M + m;
+        if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_32(T, acc[j]);
+        else                   static_cast<uint32_t *>(dst)[o] = acc[j];
+    }
+}
+
+// ============================ RMS_NORM =====================================
+// Block = 32 rows.  Each lane runs its row's sum-of-squares chain (n additions
+// from zero); the scaling pass is done by the whole block, coalesced.
+template <int FMT, bool IO_F32>
+__global__ void __launch_bounds__(128)
+k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst, int64_t ncols, int64_t nrows,
+           uint32_t eps_l, uint32_t inv_n, uint32_t monte_seed) {
+    __shared__ int16_t  tab[k16_tab_bytes / 2];
+    __shared__ int16_t  fine[k_mode == M_MONTE ? 2 * k16_monte_n : 2];
+    __shared__ uint32_t s_inv[32];
+    if constexpr (FMT == 16) {
+        for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += blockDim.x) tab[i] = T.sbdb16[i];
+        if constexpr (k_mode == M_MONTE) for (int i = threadIdx.x; i < 2 * k16_monte_n; i += blockDim.x) fine[i] = T.monte16[i];
+    }
+    __syncthreads();
+    const int64_t row0 = (int64_t) blockIdx.x * 32;
+    auto load = [&](int64_t idx) -> uint32_t {
+        if constexpr (IO_F32) {
+            const float f = static_cast<const float *>(src)[idx];
+            return FMT == 16 ? from_f32_16(T, f) : from_f32_32(T, f);
+        } else {
+            return FMT == 16 ? (uint32_t) static_cast<const uint16_t *>(src)[idx] : static_cast<const uint32_t *>(src)[idx];
+        }
+    };
+    if (threadIdx.x < 32) {
+        const int64_t row = row0 + threadIdx.x;
+        if (row < nrows) {
+            if constexpr (FMT == 16) {
+                red16 R{ &T, tab, fine };
+                uint32_t st = k_stochastic ? lfsr_jump(T, monte_seed, (unsigned long long) row * (unsigned long long) ncols) : 0u;
+                uint32_t acc = R.from(0u);
+                for (int64_t i = 0; i < ncols; i++) {
+                    const uint32_t v = load(row * ncols + i);
+                    acc = R.add(acc, mul16(v, v), st);
+                }
+                const uint32_t mean = mul16(R.finish(acc), inv_n);
+                s_inv[threadIdx.x] = recip16(sqrt16(add16(mean, eps_l, tab)));
+            } else {
+                uint32_t acc = 0u;
+                for (int64_t i = 0; i < ncols; i++) {
+                    const uint32_t v = load(row * ncols + i);
+                    acc = add32(T, acc, mul32(v, v));
+                }
+                const uint32_t mean = mul32(acc, inv_n);
+                s_inv[threadIdx.x] = recip32(sqrt32(add32(T, mean, eps_l)));
+            }
+        }
+    }
+    __syncthreads();
+    const int64_t nr = imin64(32, nrows - row0);
+    for (int64_t e = threadIdx.x; e < nr * ncols; e += blockDim.x) {
+        const int64_t r = e / ncols;
+        const int64_t idx = (row0 + r) * ncols + (e - r * ncols);
+        const uint32_t inv = s_inv[r];
+        const uint32_t v = load(idx);
+        if constexpr (FMT == 16) {
+            const uint32_t y = mul16(v, inv);
+            if constexpr (IO_F32) static_cast<float *>(dst)[idx] = to_f32_16(T, y);
+            else                  static_cast<uint16_t *>(dst)[idx] = (uint16_t) y;
+        } else {
+            const uint32_t y = mul32(v, inv);
+            if constexpr (IO_F32) static_cast<float *>(dst)[idx] = to_f32_32(T, y);
+            else                  static_cast<uint32_t *>(dst)[idx] = y;
+        }
+    }
+}
+
+// ============================ SOFT_MAX =====================================
+// Block = 32 rows, 128 threads.  Pass 1 (whole block): scale, mask, row max;
+// pass 2 (whole block): c = exp(v - max) into the work buffer; pass 3 (one
+// lane per row): the normaliser chain over c in element order; pass 4 (whole
+// block): dst = c / total.
+template <int FMT, bool IO_F32>
+__global__ void __launch_bounds__(128)
+k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const void * __restrict__ mask,
+           lnsb_shape4 ms, uint32_t scale_l, void * __restrict__ dst, void * __restrict__ work,
+           uint32_t monte_seed) {
+    __shared__ int16_t  tab[k16_tab_bytes / 2];
+    __shared__ int16_t  fine[k_mode == M_MONTE ? 2 * k16_monte_n : 2];
+    __shared__ uint32_t s_max[32][4];
+    __shared__ uint32_t s_tot[32];
+    constexpr uint32_t NEG_INF = FMT == 16 ? 0xFFFFu : 0xFFFFFFFFu;
+    if constexpr (FMT == 16) {
+        for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += blockDim.x) tab[i] = T.sbdb16[i];
+        if constexpr (k_mode == M_MONTE) for (int i = threadIdx.x; i < 2 * k16_monte_n; i += blockDim.x) fine[i] = T.monte16[i];
+    }
+    __syncthreads();
+    const int64_t n = s.ne[0];
+    const int64_t nrows = s.ne[1] * s.ne[2] * s.ne[3];
+    const int64_t row0 = (int64_t) blockIdx.x * 32;
+    const int64_t nr = imin64(32, nrows - row0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    auto ld = [&](const void * p, int64_t idx) -> uint32_t {
+        return FMT == 16 ? (uint32_t) static_cast<const uint16_t *>(p)[idx] : static_cast<const uint32_t *>(p)[idx];
+    };
+    auto value = [&](int64_t row, int64_t i) -> uint32_t {   // scaled, masked logit
+        uint32_t v;
+        if constexpr (IO_F32) {
+            const float f = static_cast<const float *>(src)[row * n + i];
+            v = FMT == 16 ? from_f32_16(T, f) : from_f32_32(T, f);
+        } else {
+            v = ld(src, row * n + i);
+        }
+        if (v != NEG_INF) {
+            v = FMT == 16 ? mul16(v, scale_l) : mul32(v, scale_l);
+            if (mask != nullptr) {
+                const int64_t i1 = row % s.ne[1], i2 = (row / s.ne[1]) % s.ne[2], i3 = row / (s.ne[1] * s.ne[2]);
+                const int64_t mrow = ((i3 % ms.ne[3]) * ms.ne[2] + i2 % ms.ne[2]) * ms.ne[1] + i1;
+                uint32_t mk;
+                if constexpr (IO_F32) {
+                    const float mf = static_cast<const float *>(mask)[mrow * n + i];
+                    mk = mf <= -3.0e38f ? NEG_INF : (FMT == 16 ? from_f32_16(T, mf) : from_f32_32(T, mf));
+                } else {
+                    mk = ld(mask, mrow * n + i);
+                }
+                if (mk == NEG_INF) v = NEG_INF;
+                else if (FMT == 16 ? !is_zero16(mk) : !is_zero32(mk)) v = FMT == 16 ? add16(v, mk, tab) : add32(T, v, mk);
+            }
+        }
+        return v;
+    };
+
+    // pass 1: row max (each warp takes rows warp, warp + 4, ...)
+    for (int r = warp; r < nr; r += 4) {
+        const int64_t row = row0 + r;
+        uint32_t mx = NEG_INF;
+        for (int64_t i = lane; i < n; i += 32) {
+            const uint32_t v = value(row, i);
+            if (FMT == 16 ? gt16(v, mx) : gt32(v, mx)) mx = v;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const uint32_t o = __shfl_xor_sync(0xFFFFFFFFu, mx, off);
+            if (FMT == 16 ? gt16(o, mx) : gt32(o, mx)) mx = o;
+        }
+        if (lane == 0) s_max[r][0] = mx;
+    }
+    __syncthreads();
+    // pass 2: c = exp(v - max) into work
+    for (int r = warp; r < nr; r += 4) {
+        const int64_t row = row0 + r;
+        const uint32_t mx = s_max[r][0];
+        for (int64_t i = lane; i < n; i += 32) {
+            const uint32_t v = value(row, i);
+            if constexpr (FMT == 16) static_cast<uint16_t *>(work)[row * n + i] = __ldg(T.exp16 + sub16(v, mx, tab));
+            else                     static_cast<uint32_t *>(work)[row * n + i] = exp32(T, sub32(T, v, mx));
+        }
+    }
+    __syncthreads();
+    // pass 3: the normaliser, one sequential chain per row (xlns16_sum order)
+    if (threadIdx.x < nr) {
+        const int64_t row = row0 + threadIdx.x;
+        const void * c = work;
+        if constexpr (FMT == 16) {
+            red16 R{ &T, tab, fine };
+            uint32_t st = k_stochastic ? lfsr_jump(T, monte_seed, (unsigned long long) row * (unsigned long long) (n - 1)) : 0u;
+            uint32_t acc = R.from(ld(c, row * n));
+            for (int64_t i = 1; i < n; i++) acc = R.add(acc, ld(c, row * n + i), st);
+            s_tot[threadIdx.x] = R.finish(acc);
+        } else {
+            uint32_t acc = ld(c, row * n);
+            for (int64_t i = 1; i < n; i++) acc = add32(T, acc, ld(c, row * n + i));
+            s_tot[threadIdx.x] = acc;
+        }
+    }
+    __syncthreads();
+    // pass 4: dst = c / total
+    for (int r = warp; r < nr; r += 4) {
+        const int64_t row = row0 + r;
+        const uint32_t tot = s_tot[r];
+        for (int64_t i = lane; i < n; i += 32) {
+            const uint32_t cv = ld(work, row * n + i);
+            if constexpr (FMT == 16) {
+                const uint32_t y = div16(cv, tot);
+                if constexpr (IO_F32) static_cast<float *>(dst)[row * n + i] = to_f32_16(T, y);
+                else                  static_cast<uint16_t *>(dst)[row * n + i] = (uint16_t) y;
+            } else {
+                const uint32_t y = div32(cv, tot);
+                if constexpr (IO_F32) static_cast<float *>(dst)[row * n + i] = to_f32_32(T, y);
+                else                  static_cast<uint32_t *>(dst)[row * n + i] = y;
+            }
+        }
+    }
+}
+
+// ============================ launch helpers ===============================
+
+int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32, cudaStream_t stream) {
+    if (!valid_fmt(fmt) || a == nullptr) return LNSB_E_INVALID;
+    if (a->K < 0 || a->M < 0 || a->N < 0 || a->ne02 <= 0 || a->ne03 <= 0 || a->ne12 <= 0 || a->ne13 <= 0) return LNSB_E_INVALID;
+    if (a->ne12 % a->ne02 != 0 || a->ne13 % a->ne03 != 0) return LNSB_E_INVALID;
+    if (a->M == 0 || a->N == 0) return 0;
+    if (dst == nullptr || (a->K > 0 && (a->w == nullptr || a->x == nullptr))) return LNSB_E_INVALID;
+    if (a->ne12 * a->ne13 > 65535) return LNSB_E_TOO_LARGE;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const int64_t r2 = a->ne12 / a->ne02, r3 = a->ne13 / a->ne03;
+    if (fmt == LNSB_XLNS16) {
+        const int64_t gx = (a->M + MM_BM - 1) / MM_BM, gy = (a->N + MM_BN - 1) / MM_BN;
+        if (gx > 0x7FFFFFFF || gy > 65535) return LNSB_E_TOO_LARGE;
+        const dim3 grid((unsigned) gx, (unsigned) gy, (unsigned) (a->ne12 * a->ne13));
+        const bool vec = a->M % 8 == 0 && a->K % 8 == 0 && ((uintptr_t) a->w % 16) == 0 && ((uintptr_t) a->x % 16) == 0 &&
+                         a->M % MM_BM == 0;
+        static bool attr_set[k_max_devices][2] = {};
+        auto kern = out_f32 ? k_mul_mat16<true> : k_mul_mat16<false>;
+        int dev = 0;
+        const int ds = current_device(&dev);
+        if (ds != 0) return ds;
+        if (!attr_set[dev][out_f32]) {
+            const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MM_SMEM);
+            if (e != cudaSuccess) return (int) e;
+            attr_set[dev][out_f32] = true;
+        }
+        kern<<<grid, MM_THREADS, MM_SMEM, stream>>>(*T, static_cast<const uint16_t *>(a->w),
+                                                    static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
+                                                    a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0);
+    } else {
+        const int64_t gx = (a->M + 127) / 128, gy = (a->N + 3) / 4;
+        if (gy > 65535) return LNSB_E_TOO_LARGE;
+        const dim3 grid((unsigned) gx, (unsigned) gy, (unsigned) (a->ne12 * a->ne13));
+        auto kern = out_f32 ? k_mul_mat32<true> : k_mul_mat32<false>;
+        kern<<<grid, 128, 0, stream>>>(*T, static_cast<const uint32_t *>(a->w), static_cast<const uint32_t *>(a->x), dst,
+                                       a->K, a->M, a->N, a->ne02, a->ne12, r2, r3);
+    }
+    return launch_status();
+}
+
+int rms_norm_impl(int fmt, const void * src, void * dst, int64_t ncols, int64_t nrows, float eps, uint16_t seed,
+                  bool io_f32, cudaStream_t stream) {
+    if (!valid_fmt(fmt) || ncols < 0 || nrows < 0) return LNSB_E_INVALID;
+    if (nrows == 0 || ncols == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const host_tables & H = get_host_tables(false, false);
+    uint32_t eps_l, inv_n;
+    const float invf = 1.0f / (float) ncols;
+    if (fmt == LNSB_XLNS16) {
+        uint32_t b;
+        std::memcpy(&b, &eps, 4);  eps_l = H.conv16[b >> 16];
+        std::memcpy(&b, &invf, 4); inv_n = H.conv16[b >> 16];
+    } else {
+        eps_l = host_from_f32_32(eps);
+        inv_n = host_from_f32_32(invf);
+    }
+    const unsigned blocks = (unsigned) ((nrows + 31) / 32);
+    if (fmt == LNSB_XLNS16) {
+        if (io_f32) k_rms_norm<16, true><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed);
+        else        k_rms_norm<16, false><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed);
+    } else {
+        if (io_f32) k_rms_norm<32, true><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed);
+        else        k_rms_norm<32, false><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed);
+    }
+    return launch_status();
+}
+
+int soft_max_impl(int fmt, const void * src, lnsb_shape4 s, const void * mask, lnsb_shape4 ms, uint32_t scale_l,
+                  void * dst, void * work, uint16_t seed, bool io_f32, cudaStream_t stream) {
+    if (!valid_fmt(fmt)) return LNSB_E_INVALID;
+    for (int i = 0; i < 4; i++) if (s.ne[i] < 0) return LNSB_E_INVALID;
+    const int64_t nrows = s.ne[1] * s.ne[2] * s.ne[3];
+    if (nrows == 0 || s.ne[0] == 0) return 0;
+    if (src == nullptr || dst == nullptr || work == nullptr) return LNSB_E_INVALID;
+    if (mask != nullptr) {
+        if (ms.ne[0] != s.ne[0] || ms.ne[1] < s.ne[1] || ms.ne[2] <= 0 || ms.ne[3] <= 0) return LNSB_E_INVALID;
+    } else {
+        ms = lnsb_shape4{ { 1, 1, 1, 1 } };
+    }
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const unsigned blocks = (unsigned) ((nrows + 31) / 32);
+    if (fmt == LNSB_XLNS16) {
+        if (io_f32) k_soft_max<16, true><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed);
+        else        k_soft_max<16, false><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed);
+    } else {
+        if (io_f32) k_soft_max<32, true><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed);
+        else        k_soft_max<32, false><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed);
+    }
+    return launch_status();
+}
+
+// ============================ Monte state ==================================
+std::mutex g_monte_mu;
+uint16_t   g_monte_state = 7;
+
+const char * mode_name() {
+    switch (k_mode) {
+        case M_MONTE:
+        case M_MONTE_BYLPVIP: return "monte";
+        case M_LPVIP:         return "lpvip";
+        case M_SUM32:         return "sum32";
+        default:              return "base";
+    }
+}
+
+}  // namespace
+
+// float -> xlns32 on the host, identical to the device conversion
+uint32_t host_from_f32_32(float x) {
+    const host_tables & H = get_host_tables(true, false);
+    uint32_t b;
+    std::memcpy(&b, &x, 4);
+    const uint32_t sign = b & 0x80000000u;
+    uint32_t ex = (b >> 23) & 0xFFu, man = b & 0x7FFFFFu;
+    if (ex == 0xFFu) return man ? 0u : (sign | 0x7FFFFFFFu);
+    if (ex == 0 && man == 0) return 0u;
+    int e;
+    if (ex == 0) {
+        e = -126;
+        while (!(man & 0x800000u)) { man <<= 1; e--; }
+        man &= 0x7FFFFFu;
+    } else {
+        e = (int) ex - 127;
+    }
+    long long l = (long long) e * (long long) k32_one + (long long) H.logm32[man];
+    if (e < 0 && man != 0) l += 1;
+    return sign | (uint32_t) ((l + 0x40000000LL) & 0x7FFFFFFFLL);
+}
+
+}  // namespace lnsb
+
+using namespace lnsb;
+
+// ================================ C ABI =====================================
+
+extern "C" {
+
+const char * lnsb_format_name(int fmt) {
+    return fmt == LNSB_XLNS16 ? "xlns16" : fmt == LNSB_XLNS32 ? "xlns32" : nullptr;
+}
+
+size_t lnsb_value_size(int fmt) { return fmt == LNSB_XLNS16 ? 2 : fmt == LNSB_XLNS32 ? 4 : 0; }
+
+const char * lnsb_sum_mode(int fmt) { return fmt == LNSB_XLNS16 ? mode_name() : nullptr; }
+
+const char * lnsb_monte_impl(int fmt) {
+    if (fmt != LNSB_XLNS16) return nullptr;
+    if (k_mode == M_MONTE) return "pure16";
+    if (k_mode == M_MONTE_BYLPVIP) return "bylpvip";
+    return nullptr;
+}
+
+const char * lnsb_description(int fmt) {
+    if (fmt == LNSB_XLNS32) return "Logarithmic Number System on B200 (xlns32)";
+    if (fmt != LNSB_XLNS16) return nullptr;
+    switch (k_mode) {
+        case M_MONTE:         return "Logarithmic Number System on B200 (xlns16, sum=monte, monte=pure16)";
+        case M_MONTE_BYLPVIP: return "Logarithmic Number System on B200 (xlns16, sum=monte, monte=bylpvip)";
+        case M_LPVIP:         return "Logarithmic Number System on B200 (xlns16, sum=lpvip)";
+        case M_SUM32:         return "Logarithmic Number System on B200 (xlns16, sum=sum32)";
+        default:              return "Logarithmic Number System on B200 (xlns16, sum=base)";
+    }
+}
+
+uint64_t lnsb_mul_mat_draws(int fmt, const lnsb_mul_mat_args * a) {
+    if (fmt != LNSB_XLNS16 || !k_stochastic || a == nullptr || a->K <= 0) return 0;
+    return (uint64_t) a->ne12 * (uint64_t) a->ne13 * (uint64_t) a->M * (uint64_t) a->N * (uint64_t) (a->K - 1);
+}
+
+uint64_t lnsb_soft_max_draws(int fmt, int64_t ncols, int64_t nrows) {
+    return fmt == LNSB_XLNS16 && k_stochastic && ncols > 0 ? (uint64_t) nrows * (uint64_t) (ncols - 1) : 0;
+}
+
+uint64_t lnsb_rms_norm_draws(int fmt, int64_t ncols, int64_t nrows) {
+    return fmt == LNSB_XLNS16 && k_stochastic ? (uint64_t) nrows * (uint64_t) ncols : 0;
+}
+
+int lnsb_upload_tables(int fmt) {
+    if (!valid_fmt(fmt)) return LNSB_E_INVALID;
+    int dev = 0;
+    int st = current_device(&dev);
+    if (st != 0) return st;
+    const bool need32 = fmt == LNSB_XLNS32;
+    const bool need_lpvip = k_mode == M_LPVIP || k_mode == M_MONTE_BYLPVIP;
+    std::lock_guard<std::mutex> lock(g_mu);
+    device_slot & s = g_slots[dev];
+    if ((fmt == LNSB_XLNS16 && s.ready16) || (fmt == LNSB_XLNS32 && s.ready32)) return 0;
+    const host_tables & H = get_host_tables(need32, need_lpvip);
+    dev_tables & t = s.t;
+    cudaError_t e = cudaSuccess;
+    if (t.sbdb16 == nullptr) {
+        if (e == cudaSuccess) e = upload(H.sbdb16, &t.sbdb16);
+        if (e == cudaSuccess) e = upload(H.conv16, &t.conv16);
+        if (e == cudaSuccess) e = upload(H.dec16, &t.dec16);
+        if (e == cudaSuccess) e = upload(H.exp16, &t.exp16);
+        if (e == cudaSuccess) e = upload(H.monte16, &t.monte16);
+        if (e == cudaSuccess) e = upload(H.sb32, &t.sb32);
+        if (e == cudaSuccess) e = upload(H.db32, &t.db32);
+        if (e == cudaSuccess) e = upload(H.db32_hi, &t.db32_hi);
+        if (e == cudaSuccess) e = upload(H.db32_lo, &t.db32_lo);
+        if (e == cudaSuccess) e = upload(H.lfsr_log, &t.lfsr_log);
+        if (e == cudaSuccess) e = upload(H.lfsr_alog, &t.lfsr_alog);
+        t.sb_base1 = H.sb_seg[1].base;
+        for (int i = 0; i < 4; i++) t.db_base[i] = H.db_seg[i].base;
+    }
+    if (e == cudaSuccess && need_lpvip && t.lpvip_db == nullptr) e = upload(H.lpvip_db, &t.lpvip_db);
+    if (e == cudaSuccess && need32 && t.logm32 == nullptr) {
+        e = upload(H.logm32, &t.logm32);
+        if (e == cudaSuccess) e = upload(H.expm32, &t.expm32);
+    }
+    if (e != cudaSuccess) return (int) e;
+    if (fmt == LNSB_XLNS16) s.ready16 = true;
+    else s.ready32 = true;
+    return 0;
+}
+
+int lnsb_to_lns(int fmt, const float * src, void * dst, int64_t n, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || n < 0) return LNSB_E_INVALID;
+    if (n == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (fmt == LNSB_XLNS16) k_to_lns<16><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
+    else                    k_to_lns<32><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
+    return launch_status();
+}
+
+int lnsb_to_lns_transposed(int fmt, const float * src, void * dst, int64_t rows, int64_t cols, int64_t dst_ld,
+                           lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || rows < 0 || cols < 0 || dst_ld < rows) return LNSB_E_INVALID;
+    if (rows == 0 || cols == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    if ((cols + 31) / 32 > 0x7FFFFFFF || (rows + 31) / 32 > 65535) return LNSB_E_TOO_LARGE;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const dim3 grid((unsigned) ((cols + 31) / 32), (unsigned) ((rows + 31) / 32));
+    const dim3 block(32, 8);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (fmt == LNSB_XLNS16) k_to_lns_transposed<16><<<grid, block, 0, s>>>(*T, src, dst, rows, cols, dst_ld);
+    else                    k_to_lns_transposed<32><<<grid, block, 0, s>>>(*T, src, dst, rows, cols, dst_ld);
+    return launch_status();
+}
+
+int lnsb_to_f32(int fmt, const void * src, float * dst, int64_t n, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || n < 0) return LNSB_E_INVALID;
+    if (n == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (fmt == LNSB_XLNS16) k_to_f32<16><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
+    else                    k_to_f32<32><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
+    return launch_status();
+}
+
+int lnsb_mul_mat(int fmt, const lnsb_mul_mat_args * args, lnsb_stream_t stream) {
+    return mul_mat_impl(fmt, args, args ? args->dst : nullptr, true, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_mul_mat_lns(int fmt, const lnsb_mul_mat_args * args, void * dst_lns, lnsb_stream_t stream) {
+    return mul_mat_impl(fmt, args, dst_lns, false, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_soft_max(int fmt, const lnsb_soft_max_args * a, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || a == nullptr) return LNSB_E_INVALID;
+    uint32_t scale_l;
+    if (fmt == LNSB_XLNS16) {
+        const host_tables & H = get_host_tables(false, false);
+        uint32_t b;
+        std::memcpy(&b, &a->scale, 4);
+        scale_l = H.conv16[b >> 16];
+    } else {
+        scale_l = host_from_f32_32(a->scale);
+    }
+    return soft_max_impl(fmt, a->src, a->src_shape, a->mask, a->mask_shape, scale_l, a->dst, a->work, a->monte_seed,
+                         true, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_soft_max_lns(int fmt, const void * src, const int64_t ne[4], const void * mask, const int64_t mne[4],
+                      uint32_t scale, void * dst, void * work, uint16_t monte_seed, lnsb_stream_t stream) {
+    if (ne == nullptr || (mask != nullptr && mne == nullptr)) return LNSB_E_INVALID;
+    lnsb_shape4 s{ { ne[0], ne[1], ne[2], ne[3] } };
+    lnsb_shape4 ms{ { 1, 1, 1, 1 } };
+    if (mask != nullptr) ms = lnsb_shape4{ { mne[0], mne[1], mne[2], mne[3] } };
+    return soft_max_impl(fmt, src, s, mask, ms, scale, dst, work, monte_seed, false, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_rms_norm(int fmt, const float * src, float * dst, int64_t ncols, int64_t nrows, float eps, uint16_t monte_seed,
+                  lnsb_stream_t stream) {
+    return rms_norm_impl(fmt, src, dst, ncols, nrows, eps, monte_seed, true, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_rms_norm_lns(int fmt, const void * src, void * dst, int64_t ncols, int64_t nrows, float eps,
+                      uint16_t monte_seed, lnsb_stream_t stream) {
+    return rms_norm_impl(fmt, src, dst, ncols, nrows, eps, monte_seed, false, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_monte_get_state(uint16_t * state) {
+    if (!k_stochastic) return LNSB_E_UNSUPPORTED;
+    if (state == nullptr) return LNSB_E_INVALID;
+    std::lock_guard<std::mutex> lock(g_monte_mu);
+    *state = g_monte_state;
+    return 0;
+}
+
+int lnsb_monte_set_state(uint16_t state) {
+    if (!k_stochastic) return LNSB_E_UNSUPPORTED;
+    if (state == 0) return LNSB_E_INVALID;
+    std::lock_guard<std::mutex> lock(g_monte_mu);
+    g_monte_state = state;
+    return 0;
+}
+
+int lnsb_monte_reserve(uint64_t draws, uint16_t * start) {
+    if (!k_stochastic) return LNSB_E_UNSUPPORTED;
+    if (start == nullptr) return LNSB_E_INVALID;
+    const host_tables & H = get_host_tables(false, false);
+    std::lock_guard<std::mutex> lock(g_monte_mu);
+    *start = g_monte_state;
+    const uint64_t k = ((uint64_t) H.lfsr_log[g_monte_state] + draws % 65535u) % 65535u;
+    g_monte_state = H.lfsr_alog[k];
+    return 0;
+}
+
+const char * lnsb_error_string(int status) {
+    switch (status) {
+        case LNSB_OK:            return "success";
+        case LNSB_E_INVALID:     return "invalid argument";
+        case LNSB_E_NO_TABLES:   return "lnsb_upload_tables has not run on this device";
+        case LNSB_E_UNSUPPORTED: return "not supported by this build";
+        case LNSB_E_TOO_LARGE:   return "size beyond a documented limit";
+        case LNSB_E_NO_DEVICE:   return "no usable CUDA device";
+        default:                 return status > 0 ? cudaGetErrorString((cudaError_t) status) : "unknown error";
+    }
+}
+
+}  // extern "C"

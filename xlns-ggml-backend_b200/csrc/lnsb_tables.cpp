@@ -1,0 +1,165 @@
+// Host table builder of the product library (see lnsb_tables.h).
+#include "lnsb_tables.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+namespace lnsb {
+namespace {
+
+constexpr long double k_ln2 = 0.693147180559945309417232121458176568L;
+
+void build16(host_tables & t) {
+    t.sbdb16.assign(k16_tab_bytes / 2, 0);
+    for (int n = 0; n <= k16_ess; n++) {
+        const double sb = std::log(1.0 + std::pow(2.0, -(double) n / 128.0)) / std::log(2.0) * 128.0;
+        const int sbv = (int) (uint16_t) (sb + .5);
+        int dbv = 0;
+        if (n > 0) {
+            const double dbneg = std::log(std::pow(2.0, (double) n / 128.0) - 1.0) / std::log(2.0) * 128.0;
+            dbv = -n + (int) (int16_t) (dbneg + .5);
+        }
+        t.sbdb16[n]                      = (int16_t) (2 * sbv);
+        t.sbdb16[k16_sign_off / 2 + n]   = (int16_t) (2 * dbv);
+    }
+    // entries n = 1281 of both halves stay 0 (essential zero)
+
+    t.conv16.resize(65536);
+    for (uint32_t i = 0; i < 65536; i++) {
+        const uint32_t bits = i << 16;
+        float f;
+        std::memcpy(&f, &bits, 4);
+        const uint16_t sign = (i & 0x8000u) ? 0x8000u : 0;
+        const float a = std::fabs(f);
+        uint16_t code;
+        if (a == 0.0f || a != a) {
+            code = 0;
+        } else if (std::isinf(a)) {
+            code = (uint16_t) (sign | 0x7FFFu);
+        } else {
+            const double l = std::log((double) a) / std::log(2.0) * 128.0;
+            long c = (long) l + 0x4000L;          // truncation toward zero, then offset
+            if (c < 0) c = 0;
+            if (c > 0x7FFF) c = 0x7FFF;
+            code = (uint16_t) (sign | (uint16_t) c);
+        }
+        t.conv16[i] = code;
+    }
+
+    t.dec16.resize(65536);
+    for (uint32_t c = 0; c < 65536; c++) {
+        if ((c & 0x7FFFu) == 0) {
+            t.dec16[c] = 0.0f;
+            continue;
+        }
+        double v = std::pow(2.0, (double) ((int) (c & 0x7FFFu) - 0x4000) / 128.0);
+        char buf[32];
+        std::snprintf(buf, sizeof buf, "%.7g", v);
+        v = std::strtod(buf, nullptr);
+        t.dec16[c] = (float) ((c & 0x8000u) ? -v : v);
+    }
+
+    t.exp16.resize(65536);
+    for (uint32_t c = 0; c < 65536; c++) {
+        const float e = std::exp(t.dec16[c]);    // float overload: expf
+        uint32_t bits;
+        std::memcpy(&bits, &e, 4);
+        t.exp16[c] = t.conv16[bits >> 16];
+    }
+
+    t.monte16.assign(2 * k16_monte_n, 0);
+    for (int n = 0; n < k16_monte_n; n++) {
+        const long double x  = (long double) n / 128.0L;
+        const long double sb = log1pl(exp2l(-x)) / k_ln2;
+        t.monte16[n] = (int16_t) llroundl(sb * 32768.0L);
+        if (n > 0) {
+            const long double db = log1pl(-exp2l(-x)) / k_ln2;
+            long double r = roundl(db * 32768.0L);
+            if (r < -32768.0L) r = -32768.0L;
+            t.monte16[k16_monte_n + n] = (int16_t) r;
+        }
+    }
+
+    t.lfsr_log.assign(65536, 0);
+    t.lfsr_alog.assign(65535, 0);
+    uint16_t s = 1;
+    for (uint32_t i = 0; i < 65535; i++) {
+        t.lfsr_alog[i] = s;
+        t.lfsr_log[s]  = (uint16_t) i;
+        const uint16_t bit = s & 1u;
+        s >>= 1;
+        if (bit) s ^= 0xB400u;
+    }
+}
+
+// xlns32 knots are the exact functions truncated toward zero at F=23
+int32_t knot(long double v) { return (int32_t) (v * (long double) k32_one); }
+int32_t knot_sb(uint32_t d) { return knot(log1pl(exp2l(-(long double) d / (long double) k32_one)) / k_ln2); }
+int32_t knot_db(uint32_t d) { return knot(log1pl(-exp2l(-(long double) d / (long double) k32_one)) / k_ln2); }
+
+void build32(host_tables & t, bool need32, bool need_lpvip) {
+    t.sb_seg[0] = { 0u, 8u << 23, 13, 0 };
+    t.sb_seg[1] = { 8u << 23, 26u << 23, 16, 0 };
+    t.db_seg[0] = { 1u << 23, 2u << 23, 12, 0 };
+    t.db_seg[1] = { 2u << 23, 4u << 23, 13, 0 };
+    t.db_seg[2] = { 4u << 23, 8u << 23, 14, 0 };
+    t.db_seg[3] = { 8u << 23, 26u << 23, 16, 0 };
+    int tot = 0;
+    for (auto & sg : t.sb_seg) { sg.base = tot; tot += (int) ((sg.hi - sg.lo) >> sg.shift) + 1; }
+    t.sb32.resize(tot);
+    for (const auto & sg : t.sb_seg) {
+        const int n = (int) ((sg.hi - sg.lo) >> sg.shift);
+        for (int i = 0; i <= n; i++) t.sb32[sg.base + i] = knot_sb(sg.lo + ((uint32_t) i << sg.shift));
+    }
+    tot = 0;
+    for (auto & sg : t.db_seg) { sg.base = tot; tot += (int) ((sg.hi - sg.lo) >> sg.shift) + 1; }
+    t.db32.resize(tot);
+    for (const auto & sg : t.db_seg) {
+        const int n = (int) ((sg.hi - sg.lo) >> sg.shift);
+        for (int i = 0; i <= n; i++) t.db32[sg.base + i] = knot_db(sg.lo + ((uint32_t) i << sg.shift));
+    }
+    t.db32_hi.assign(2048, 0);
+    for (int j = 1; j < 2048; j++) t.db32_hi[j] = knot_db((uint32_t) j << 12);
+    t.db32_lo.assign(4096, 0);
+    for (int k = 1; k < 4096; k++) t.db32_lo[k] = knot_db((uint32_t) k);
+
+    if (need32) {
+        t.logm32.resize((size_t) 1 << 23);
+        t.expm32.resize((size_t) 1 << 23);
+        for (uint32_t j = 0; j < (1u << 23); j++) {
+            const long double m = 1.0L + (long double) j / (long double) k32_one;
+            t.logm32[j] = (uint32_t) floorl(log2l(m) * (long double) k32_one);
+            t.expm32[j] = (float) exp2l((long double) j / (long double) k32_one);
+        }
+    }
+    if (need_lpvip) {
+        t.lpvip_db.resize((size_t) 1 << 23);
+        t.lpvip_db[0] = 0;
+        for (uint32_t j = 1; j < (1u << 23); j++) t.lpvip_db[j] = knot_db(j);
+    }
+}
+
+}  // namespace
+
+const host_tables & get_host_tables(bool need32, bool need_lpvip) {
+    static std::mutex mu;
+    static host_tables t;
+    static bool built16 = false, built32 = false, have32 = false, have_lpvip = false;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!built16) {
+        build16(t);
+        built16 = true;
+    }
+    if (!built32 || (need32 && !have32) || (need_lpvip && !have_lpvip)) {
+        build32(t, need32 || have32, need_lpvip || have_lpvip);
+        built32    = true;
+        have32     = have32 || need32;
+        have_lpvip = have_lpvip || need_lpvip;
+    }
+    return t;
+}
+
+}  // namespace lnsb

@@ -1,0 +1,147 @@
+"""Host-side mirror of the reference's lns_cuda::kernel_set
+(lns-backend/cuda/lns-cuda-kernels.h:85-139) over the C ABI of
+include/lnsb200.h.
+
+One KernelSet per (summation-mode build, format), like the reference's
+xlns16_kernels() / xlns32_kernels().  Tensors are torch CUDA tensors used
+purely as device memory: uint16 (xlns16 codes), int32 (xlns32 codes, same
+bits as uint32) or float32.  Every call launches asynchronously on the
+current torch stream (or the given one) and raises LnsbError on failure --
+there is no CPU fallback.
+"""
+import ctypes
+
+from . import _lib
+from ._lib import MODES, XLNS16, XLNS32, LnsbError, MulMatArgs, Shape4, SoftMaxArgs  # noqa: F401
+
+__all__ = ["KernelSet", "MODES", "XLNS16", "XLNS32", "LnsbError", "MulMatArgs", "SoftMaxArgs", "Shape4",
+           "kernels", "monte_get_state", "monte_set_state", "monte_reserve"]
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _shape4(shape):
+    ne = list(shape) + [1] * (4 - len(shape))
+    return Shape4((ctypes.c_int64 * 4)(*ne))
+
+
+class KernelSet:
+    """kernel_set for one format of one summation-mode build."""
+
+    def __init__(self, fmt=XLNS16, mode="base"):
+        if fmt not in (XLNS16, XLNS32):
+            raise ValueError("format must be 16 or 32")
+        self.fmt = fmt
+        self.mode = mode
+        self.lib = _lib.load(mode)
+
+    # ---- identity (kernel_set::format_name ... monte_impl) ----
+    def format_name(self):
+        return self.lib.lnsb_format_name(self.fmt).decode()
+
+    def value_size(self):
+        return self.lib.lnsb_value_size(self.fmt)
+
+    def sum_mode(self):
+        r = self.lib.lnsb_sum_mode(self.fmt)
+        return r.decode() if r else None
+
+    def monte_impl(self):
+        r = self.lib.lnsb_monte_impl(self.fmt)
+        return r.decode() if r else None
+
+    def description(self):
+        return self.lib.lnsb_description(self.fmt).decode()
+
+    # ---- draw accounting ----
+    def mul_mat_draws(self, K, M, N, ne02=1, ne03=1, ne12=1, ne13=1):
+        a = MulMatArgs(None, None, None, K, M, N, ne02, ne03, ne12, ne13, 0)
+        return self.lib.lnsb_mul_mat_draws(self.fmt, ctypes.byref(a))
+
+    def soft_max_draws(self, ncols, nrows):
+        return self.lib.lnsb_soft_max_draws(self.fmt, ncols, nrows)
+
+    def rms_norm_draws(self, ncols, nrows):
+        return self.lib.lnsb_rms_norm_draws(self.fmt, ncols, nrows)
+
+    # ---- tables / conversions ----
+    def upload_tables(self):
+        _lib.check(self.lib, "lnsb_upload_tables", self.lib.lnsb_upload_tables(self.fmt))
+
+    def to_lns(self, src, dst, stream=None):
+        _lib.check(self.lib, "lnsb_to_lns", self.lib.lnsb_to_lns(self.fmt, _ptr(src), _ptr(dst), src.numel(), _stream(stream)))
+
+    def to_lns_transposed(self, src, dst, rows, cols, dst_ld, stream=None):
+        _lib.check(self.lib, "lnsb_to_lns_transposed",
+                   self.lib.lnsb_to_lns_transposed(self.fmt, _ptr(src), _ptr(dst), rows, cols, dst_ld, _stream(stream)))
+
+    def to_f32(self, src, dst, stream=None):
+        _lib.check(self.lib, "lnsb_to_f32", self.lib.lnsb_to_f32(self.fmt, _ptr(src), _ptr(dst), src.numel(), _stream(stream)))
+
+    # ---- the hot path ----
+    def _mm_args(self, w, x, dst, K, M, N, slices, monte_seed):
+        ne02, ne03, ne12, ne13 = slices
+        return MulMatArgs(w.data_ptr(), x.data_ptr(), dst.data_ptr() if dst is not None else None,
+                          K, M, N, ne02, ne03, ne12, ne13, monte_seed)
+
+    def mul_mat(self, w, x, dst, K, M, N, slices=(1, 1, 1, 1), monte_seed=7, stream=None):
+        """dst (F32, [slices][N][M]) = W^T x; w k-major [K][M] per weight slice, x [N][K]."""
+        a = self._mm_args(w, x, dst, K, M, N, slices, monte_seed)
+        _lib.check(self.lib, "lnsb_mul_mat", self.lib.lnsb_mul_mat(self.fmt, ctypes.byref(a), _stream(stream)))
+
+    def mul_mat_lns(self, w, x, dst, K, M, N, slices=(1, 1, 1, 1), monte_seed=7, stream=None):
+        """as mul_mat with LNS codes out"""
+        a = self._mm_args(w, x, None, K, M, N, slices, monte_seed)
+        _lib.check(self.lib, "lnsb_mul_mat_lns", self.lib.lnsb_mul_mat_lns(self.fmt, ctypes.byref(a), _ptr(dst), _stream(stream)))
+
+    def soft_max(self, src, shape, dst, work, mask=None, mask_shape=None, scale=1.0, monte_seed=7, stream=None):
+        a = SoftMaxArgs(src.data_ptr(), _shape4(shape), mask.data_ptr() if mask is not None else None,
+                        _shape4(mask_shape or (1, 1, 1, 1)), scale, dst.data_ptr(), work.data_ptr(), monte_seed)
+        _lib.check(self.lib, "lnsb_soft_max", self.lib.lnsb_soft_max(self.fmt, ctypes.byref(a), _stream(stream)))
+
+    def soft_max_lns(self, src, shape, dst, work, mask=None, mask_shape=None, scale_code=0x4000, monte_seed=7, stream=None):
+        ne = (ctypes.c_int64 * 4)(*(list(shape) + [1] * (4 - len(shape))))
+        mne = (ctypes.c_int64 * 4)(*(list(mask_shape) + [1] * (4 - len(mask_shape)))) if mask is not None else None
+        _lib.check(self.lib, "lnsb_soft_max_lns",
+                   self.lib.lnsb_soft_max_lns(self.fmt, _ptr(src), ne, _ptr(mask), mne, scale_code, _ptr(dst),
+                                              _ptr(work), monte_seed, _stream(stream)))
+
+    def rms_norm(self, src, dst, ncols, nrows, eps, monte_seed=7, stream=None):
+        _lib.check(self.lib, "lnsb_rms_norm",
+                   self.lib.lnsb_rms_norm(self.fmt, _ptr(src), _ptr(dst), ncols, nrows, eps, monte_seed, _stream(stream)))
+
+    def rms_norm_lns(self, src, dst, ncols, nrows, eps, monte_seed=7, stream=None):
+        _lib.check(self.lib, "lnsb_rms_norm_lns",
+                   self.lib.lnsb_rms_norm_lns(self.fmt, _ptr(src), _ptr(dst), ncols, nrows, eps, monte_seed, _stream(stream)))
+
+
+def kernels(fmt=XLNS16, mode="base"):
+    return KernelSet(fmt, mode)
+
+
+# ---- Monte state (ggml-lns.h:13-24): process-wide, per monte build ----
+def monte_get_state(mode="monte"):
+    lib = _lib.load(mode)
+    s = ctypes.c_uint16()
+    _lib.check(lib, "lnsb_monte_get_state", lib.lnsb_monte_get_state(ctypes.byref(s)))
+    return s.value
+
+
+def monte_set_state(state, mode="monte"):
+    lib = _lib.load(mode)
+    _lib.check(lib, "lnsb_monte_set_state", lib.lnsb_monte_set_state(state))
+
+
+def monte_reserve(draws, mode="monte"):
+    lib = _lib.load(mode)
+    s = ctypes.c_uint16()
+    _lib.check(lib, "lnsb_monte_reserve", lib.lnsb_monte_reserve(draws, ctypes.byref(s)))
+    return s.value
