@@ -128,6 +128,26 @@ int lnsb_soft_max_lns(int fmt, const void * src, const int64_t ne[4], const void
                       const int64_t mne[4], uint32_t scale, void * dst, void * work,
                       uint16_t monte_seed, lnsb_stream_t stream);
 
+/* Allocation-free variant of lnsb_soft_max_lns.  No counterpart in the
+ * reference: it is for callers that must not call cudaMalloc (code running
+ * inside a CUDA-graph capture, a host allocator that owns all device memory,
+ * a latency-critical loop that may not hit the driver's allocator).  The
+ * per-element scratch the normaliser needs lives in one static device array
+ * of LNSB_NOALLOC_SCRATCH_BYTES built into this library, so
+ * nelements(src) * value_size must not exceed that (else LNSB_E_TOO_LARGE).
+ * The array belongs to the loaded library, so every GPU that uses it holds
+ * those bytes until the process exits.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) -- make that first call
+ * before any stream capture.  The arithmetic tables still come from
+ * lnsb_upload_tables, a one-time set-up call that does allocate.  All calls
+ * share the one array: calls that can overlap on the GPU (different streams,
+ * or different host threads, without ordering between them) race on it and
+ * must be serialised by the caller. */
+#define LNSB_NOALLOC_SCRATCH_BYTES ((size_t) 8 << 20)
+int lnsb_soft_max_lns_noalloc(int fmt, const void * src, const int64_t ne[4], const void * mask,
+                              const int64_t mne[4], uint32_t scale, void * dst, uint16_t monte_seed,
+                              lnsb_stream_t stream);
+
 /* kernel_set::rms_norm (lns-cuda-kernels.h:132-134) */
 int lnsb_rms_norm(int fmt, const float * src, float * dst, int64_t ncols, int64_t nrows, float eps,
                   uint16_t monte_seed, lnsb_stream_t stream);

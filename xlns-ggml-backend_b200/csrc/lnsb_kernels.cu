@@ -19,6 +19,12 @@
 #include "lnsb_arith.cuh"
 #include "lnsb_tables.h"
 
+// Scratch of lnsb_soft_max_lns_noalloc: a file-scope device array, so that
+// entry point never allocates.  Host code must not use this name as a device
+// address (in host code it is only a stand-in); the device address is looked
+// up per device with cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LNSB_NOALLOC_SCRATCH_BYTES];
+
 namespace lnsb {
 
 uint32_t host_from_f32_32(float x);   // defined below; the host twin of from_f32_32
@@ -838,6 +844,35 @@ int lnsb_soft_max_lns(int fmt, const void * src, const int64_t ne[4], const void
     lnsb_shape4 ms{ { 1, 1, 1, 1 } };
     if (mask != nullptr) ms = lnsb_shape4{ { mne[0], mne[1], mne[2], mne[3] } };
     return soft_max_impl(fmt, src, s, mask, ms, scale, dst, work, monte_seed, false, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_soft_max_lns_noalloc(int fmt, const void * src, const int64_t ne[4], const void * mask,
+                              const int64_t mne[4], uint32_t scale, void * dst, uint16_t monte_seed,
+                              lnsb_stream_t stream) {
+    static void * scratch_of[k_max_devices] = {};   // device address of g_noalloc_scratch, per device
+    static std::mutex scratch_mu;
+    if (!valid_fmt(fmt) || ne == nullptr || (mask != nullptr && mne == nullptr)) return LNSB_E_INVALID;
+    for (int i = 0; i < 4; i++) if (ne[i] < 0) return LNSB_E_INVALID;
+    const int64_t nel = ne[0] * ne[1] * ne[2] * ne[3];
+    if (nel == 0) return 0;
+    if ((uint64_t) nel > LNSB_NOALLOC_SCRATCH_BYTES / lnsb_value_size(fmt)) return LNSB_E_TOO_LARGE;
+    int dev = 0;
+    const int st = current_device(&dev);
+    if (st != 0) return st;
+    void * scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(scratch_mu);
+        if (scratch_of[dev] == nullptr) {
+            void * p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess) return (int) e;
+            scratch_of[dev] = p;
+        }
+        scratch = scratch_of[dev];
+    }
+    // every element of the scratch is written (exp pass) before it is read
+    // (normaliser and division passes), so nothing needs clearing between calls
+    return lnsb_soft_max_lns(fmt, src, ne, mask, mne, scale, dst, scratch, monte_seed, stream);
 }
 
 int lnsb_rms_norm(int fmt, const float * src, float * dst, int64_t ncols, int64_t nrows, float eps, uint16_t monte_seed,

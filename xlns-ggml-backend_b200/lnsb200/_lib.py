@@ -54,6 +54,8 @@ SIGNATURES = [
     ("lnsb_soft_max", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(SoftMaxArgs), _VP]),
     ("lnsb_soft_max_lns", ctypes.c_int, [ctypes.c_int, _VP, ctypes.POINTER(_I64), _VP, ctypes.POINTER(_I64),
                                          ctypes.c_uint32, _VP, _VP, ctypes.c_uint16, _VP]),
+    ("lnsb_soft_max_lns_noalloc", ctypes.c_int, [ctypes.c_int, _VP, ctypes.POINTER(_I64), _VP, ctypes.POINTER(_I64),
+                                                 ctypes.c_uint32, _VP, ctypes.c_uint16, _VP]),
     ("lnsb_rms_norm", ctypes.c_int, [ctypes.c_int, _VP, _VP, _I64, _I64, ctypes.c_float, ctypes.c_uint16, _VP]),
     ("lnsb_rms_norm_lns", ctypes.c_int, [ctypes.c_int, _VP, _VP, _I64, _I64, ctypes.c_float, ctypes.c_uint16, _VP]),
     ("lnsb_monte_get_state", ctypes.c_int, [ctypes.POINTER(ctypes.c_uint16)]),
