@@ -133,6 +133,25 @@ def test_mul_mat16_special_codes(orc, ks16):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("where", ["early", "late", "none"])
+def test_mul_mat16_range_fallback(orc, ks16, where):
+    """A zero operand (or a huge one) part-way along K: the base kernel's
+    key-form fast path must hand the chains over to packed codes at that
+    chunk and still match bit for bit."""
+    rng = np.random.default_rng(17)
+    M, K, N = 128, 300, 40
+    w = codes16(orc, rng, (M, K), 0.02)
+    x = codes16(orc, rng, (N, K), 1.0)
+    if where == "early":
+        x[3, 5] = 0x0000            # exact zero in the first chunk
+    elif where == "late":
+        w[7, 250] = 0x0000          # zero in a later chunk
+        x[11, 251] = 0x7FF0         # and a huge activation
+    want = orc.mul_mat16(ks16.mode, w, x, seed=3, nthreads=NT).ravel()
+    got = run_mm16(ks16, w, x, seed=3)
+    assert np.array_equal(got, want)
+
+
 def test_draw_accounting(ks16, orc):
     for args in [(1536, 576, 8, 1, 1), (1, 4, 4, 1, 1), (0, 4, 4, 1, 1), (10, 3, 5, 4, 2)]:
         K, M, N, ne12, ne13 = args

@@ -327,6 +327,259 @@ k_mul_mat16(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __re
     }
 }
 
+// ===================== MUL_MAT (xlns16, base mode, key form) ================
+//
+// The base-mode hot kernel.  Every chain carries its accumulator as a key
+// (lnsb_tables.h): key = 16 * log + 4 * [value >= 0].  One LNS addition of a
+// product p is then
+//     d   = |a - p|                 one signed difference gives n and the sign case
+//     adj = T[min(d, KEYMAX)]       sb or db (or the cancellation sentinel), * 16
+//     a   = max(max(a, p) + adj, 4) max() picks the larger magnitude and, on a tie,
+//                                   the positive one; the clamp maps x + (-x) to +0
+// and the product key is wkey + xkey with one mask fixing the sign flag, so an
+// addition costs 8 integer instructions instead of ~30 on packed codes.
+// This form drops the saturation of the product and of the sum, so it is
+// used for a K chunk only when that chunk's operands prove neither can
+// happen: every product >= 2^-120 (log >= 964, beyond the largest db step, so
+// no sum underflows either) and every product small enough that K additions
+// cannot reach 2^127.  Otherwise the chain continues on packed codes with the
+// full xlns16 semantics -- the bits are the same either way.
+//
+// Tile: 64 weight rows x 32 tokens, 128 threads, 4 x 4 chains per thread;
+// K chunks of 32 staged with cp.async (double buffered) and converted to key
+// form once per chunk in shared memory; the 20 KB key table sits at shared
+// offset 0, so its byte index needs no address arithmetic.
+constexpr int FB_BM = 64, FB_BN = 32, FB_KC = 32, FB_TM = 4, FB_TN = 4;
+constexpr int FB_THREADS = (FB_BM / FB_TM) * (FB_BN / FB_TN);      // 128
+constexpr int FB_XP  = FB_KC + 8;                                  // x code pitch, halfwords
+constexpr int FB_XKP = FB_KC + 4;                                  // x key pitch, words
+constexpr int FB_WCODES = FB_KC * FB_BM;                           // halfwords
+constexpr int FB_XCODES = FB_BN * FB_XP;                           // halfwords
+constexpr int FB_OFF_WKEY = k16_key_bytes;
+constexpr int FB_OFF_XKEY = FB_OFF_WKEY + FB_KC * FB_BM * 4;
+constexpr int FB_OFF_TAB2 = FB_OFF_XKEY + FB_BN * FB_XKP * 4;      // packed-code table (slow path)
+constexpr int FB_OFF_RED  = FB_OFF_TAB2 + MM_TABPAD;
+constexpr int FB_OFF_CODE = FB_OFF_RED + 64;
+constexpr int FB_SMEM     = FB_OFF_CODE + 2 * (FB_WCODES + FB_XCODES) * 2;
+
+__device__ __forceinline__ void fb_stage(uint16_t * wc, uint16_t * xc, const uint16_t * __restrict__ W,
+                                         const uint16_t * __restrict__ X, int64_t K, int64_t M, int64_t N,
+                                         int64_t m0, int64_t n0, int64_t k0, bool vec) {
+    const int tid = threadIdx.x;
+    if (vec) {
+#pragma unroll
+        for (int it = 0; it < 2; it++) {           // weights: 32 k-rows x 128 B = 256 x 16 B
+            const int c = tid + it * FB_THREADS;
+            const int r = c >> 3, q = c & 7;
+            if (k0 + r < K) cp_async16(wc + r * FB_BM + q * 8, W + (k0 + r) * M + m0 + q * 8);
+        }
+        {                                          // tokens: 32 rows x 64 B = 128 x 16 B
+            const int r = tid >> 2, q = tid & 3;
+            if (n0 + r < N && k0 + q * 8 < K) cp_async16(xc + r * FB_XP + q * 8, X + (n0 + r) * K + k0 + q * 8);
+        }
+    } else {
+        for (int i = tid; i < FB_WCODES; i += FB_THREADS) {
+            const int r = i / FB_BM, c = i % FB_BM;
+            const int64_t k = k0 + r, m = m0 + c;
+            wc[r * FB_BM + c] = (k < K && m < M) ? W[k * M + m] : (uint16_t) 0x4000;
+        }
+        for (int i = tid; i < FB_BN * FB_KC; i += FB_THREADS) {
+            const int r = i / FB_KC, c = i % FB_KC;
+            const int64_t n = n0 + r, k = k0 + c;
+            xc[r * FB_XP + c] = (n < N && k < K) ? X[n * K + k] : (uint16_t) 0x4000;
+        }
+    }
+}
+
+// one addition in key form (see above)
+__device__ __forceinline__ int key_step(int a, int p, const unsigned char * tab) {
+    const int d   = min(abs(a - p), k16_key_max);
+    const int adj = *reinterpret_cast<const int *>(tab + d);
+    return __viaddmax_s32(max(a, p), adj, 4);
+}
+__device__ __forceinline__ int key_of_code_w(uint32_t c) {      // weight operand: log biased by -0x4000
+    return (int) (((c & 0x7FFFu) - 0x4000u) << 4) | (int) ((~c >> 13) & 4u);
+}
+__device__ __forceinline__ int key_of_code_x(uint32_t c) {      // activation operand: +4 folds the sign flag
+    return (int) ((c & 0x7FFFu) << 4) + (int) ((~c >> 13) & 4u) + 4;
+}
+__device__ __forceinline__ int key_of_product(int wkey, int xkey) { return (wkey + xkey) & ~8; }
+__device__ __forceinline__ uint32_t code_of_key(int key) {
+    return ((uint32_t) (key >> 4) & 0x7FFFu) | ((key & 4) ? 0u : 0x8000u);
+}
+
+template <bool OUT_F32>
+__global__ void __launch_bounds__(FB_THREADS, 4)
+k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
+                 void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
+                 int64_t r2, int64_t r3, int pmax, int vec) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    int *      wkeys = reinterpret_cast<int *>(smem + FB_OFF_WKEY);
+    int *      xkeys = reinterpret_cast<int *>(smem + FB_OFF_XKEY);
+    int16_t *  tab2  = reinterpret_cast<int16_t *>(smem + FB_OFF_TAB2);
+    int *      red   = reinterpret_cast<int *>(smem + FB_OFF_RED);
+    uint16_t * codes = reinterpret_cast<uint16_t *>(smem + FB_OFF_CODE);
+
+    for (int i = threadIdx.x; i < k16_key_bytes / 4; i += FB_THREADS) reinterpret_cast<int *>(smem)[i] = T.key16[i];
+    for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += FB_THREADS) tab2[i] = T.sbdb16[i];
+
+    const int64_t z = blockIdx.z, i12 = z % ne12, i13 = z / ne12;
+    const int64_t m0 = (int64_t) blockIdx.x * FB_BM, n0 = (int64_t) blockIdx.y * FB_BN;
+    const uint16_t * Wz = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
+    const uint16_t * Xz = X + z * N * K;
+    const int tm = threadIdx.x % (FB_BM / FB_TM), tn = threadIdx.x / (FB_BM / FB_TM);
+    const int mloc = tm * FB_TM;                        // rows mloc .. mloc+3
+    const int warp = threadIdx.x >> 5;
+    // tokens tn, tn + 8, tn + 16, tn + 24
+
+    int      akey[FB_TM][FB_TN];
+    uint32_t acc[FB_TM][FB_TN];
+    bool fast = true;                                   // uniform across the block
+    const int nchunks = (int) ((K + FB_KC - 1) / FB_KC);
+    const int64_t nvalid = imin64(FB_BN, N - n0);
+    red16 R{ &T, tab2, nullptr };
+
+    if (nchunks > 0) {
+        fb_stage(codes, codes + FB_WCODES, Wz, Xz, K, M, N, m0, n0, 0, vec != 0);
+        cp_async_commit();
+    }
+    for (int c = 0; c < nchunks; c++) {
+        uint16_t * wc = codes + (c & 1) * (FB_WCODES + FB_XCODES);
+        uint16_t * xc = wc + FB_WCODES;
+        if (c + 1 < nchunks) {
+            uint16_t * wn = codes + ((c + 1) & 1) * (FB_WCODES + FB_XCODES);
+            fb_stage(wn, wn + FB_WCODES, Wz, Xz, K, M, N, m0, n0, (int64_t) (c + 1) * FB_KC, vec != 0);
+            cp_async_commit();
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const int kvalid = (int) imin64(FB_KC, K - (int64_t) c * FB_KC);
+        if (fast) {
+            // convert this chunk to key form; operand log ranges for the range check
+            int wmin = 0x7FFF, wmax = 0, xmin = 0x7FFF, xmax = 0;
+            for (int i = threadIdx.x; i < FB_KC * FB_BM; i += FB_THREADS) {
+                const int r = i / FB_BM;
+                const uint32_t cw = wc[i];
+                wkeys[i] = key_of_code_w(cw);
+                if (r < kvalid) { const int l = (int) (cw & 0x7FFFu); wmin = min(wmin, l); wmax = max(wmax, l); }
+            }
+            for (int i = threadIdx.x; i < FB_BN * FB_KC; i += FB_THREADS) {
+                const int r = i / FB_KC, col = i % FB_KC;
+                const uint32_t cx = xc[r * FB_XP + col];
+                xkeys[r * FB_XKP + col] = key_of_code_x(cx);
+                if (r < nvalid && col < kvalid) { const int l = (int) (cx & 0x7FFFu); xmin = min(xmin, l); xmax = max(xmax, l); }
+            }
+            wmin = __reduce_min_sync(0xFFFFFFFFu, wmin);
+            wmax = __reduce_max_sync(0xFFFFFFFFu, wmax);
+            xmin = __reduce_min_sync(0xFFFFFFFFu, xmin);
+            xmax = __reduce_max_sync(0xFFFFFFFFu, xmax);
+            if ((threadIdx.x & 31) == 0) {
+                red[warp * 4 + 0] = wmin; red[warp * 4 + 1] = wmax; red[warp * 4 + 2] = xmin; red[warp * 4 + 3] = xmax;
+            }
+            __syncthreads();
+            int a0 = 0x7FFF, a1 = 0, b0 = 0x7FFF, b1 = 0;
+#pragma unroll
+            for (int w = 0; w < FB_THREADS / 32; w++) {
+                a0 = min(a0, red[w * 4 + 0]); a1 = max(a1, red[w * 4 + 1]);
+                b0 = min(b0, red[w * 4 + 2]); b1 = max(b1, red[w * 4 + 3]);
+            }
+            const bool ok = a0 + b0 - 0x4000 >= 964 && a1 + b1 - 0x4000 <= pmax;
+            if (!ok) {
+                fast = false;
+                if (c > 0) {
+#pragma unroll
+                    for (int i = 0; i < FB_TM; i++)
+#pragma unroll
+                        for (int j = 0; j < FB_TN; j++) acc[i][j] = code_of_key(akey[i][j]);
+                }
+            }
+        }
+        int k = 0;
+        if (fast) {
+            if (c == 0) {
+                const int4 w4 = *reinterpret_cast<const int4 *>(wkeys + mloc);
+                const int wv[4] = { w4.x, w4.y, w4.z, w4.w };
+#pragma unroll
+                for (int i = 0; i < FB_TM; i++)
+#pragma unroll
+                    for (int j = 0; j < FB_TN; j++) akey[i][j] = key_of_product(wv[i], xkeys[(tn + 8 * j) * FB_XKP]);
+                k = 1;
+                for (; k < 4 && k < kvalid; k++) {
+                    const int4 wk = *reinterpret_cast<const int4 *>(wkeys + k * FB_BM + mloc);
+                    const int w2[4] = { wk.x, wk.y, wk.z, wk.w };
+#pragma unroll
+                    for (int i = 0; i < FB_TM; i++)
+#pragma unroll
+                        for (int j = 0; j < FB_TN; j++)
+                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem);
+                }
+            }
+            for (; k + 4 <= kvalid; k += 4) {
+                int4 xv[FB_TN];
+#pragma unroll
+                for (int j = 0; j < FB_TN; j++) xv[j] = *reinterpret_cast<const int4 *>(xkeys + (tn + 8 * j) * FB_XKP + k);
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int4 wk = *reinterpret_cast<const int4 *>(wkeys + (k + u) * FB_BM + mloc);
+                    const int w2[4] = { wk.x, wk.y, wk.z, wk.w };
+#pragma unroll
+                    for (int i = 0; i < FB_TM; i++)
+#pragma unroll
+                        for (int j = 0; j < FB_TN; j++) {
+                            const int xk = u == 0 ? xv[j].x : u == 1 ? xv[j].y : u == 2 ? xv[j].z : xv[j].w;
+                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xk), smem);
+                        }
+                }
+            }
+            for (; k < kvalid; k++) {
+                const int4 wk = *reinterpret_cast<const int4 *>(wkeys + k * FB_BM + mloc);
+                const int w2[4] = { wk.x, wk.y, wk.z, wk.w };
+#pragma unroll
+                for (int i = 0; i < FB_TM; i++)
+#pragma unroll
+                    for (int j = 0; j < FB_TN; j++)
+                        akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem);
+            }
+        } else {
+            // packed codes, full xlns16 semantics
+            if (c == 0) {
+#pragma unroll
+                for (int i = 0; i < FB_TM; i++)
+#pragma unroll
+                    for (int j = 0; j < FB_TN; j++) acc[i][j] = mul16(wc[mloc + i], xc[(tn + 8 * j) * FB_XP]);
+                k = 1;
+            }
+            uint32_t st = 0;
+            for (; k < kvalid; k++) {
+#pragma unroll
+                for (int i = 0; i < FB_TM; i++) {
+                    const uint32_t w = wc[k * FB_BM + mloc + i];
+#pragma unroll
+                    for (int j = 0; j < FB_TN; j++) acc[i][j] = R.add(acc[i][j], mul16(w, xc[(tn + 8 * j) * FB_XP + k]), st);
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+#pragma unroll
+    for (int i = 0; i < FB_TM; i++) {
+        const int64_t m = m0 + mloc + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < FB_TN; j++) {
+            const int64_t n = n0 + tn + 8 * j;
+            if (n >= N) continue;
+            const uint32_t v = K == 0 ? 0u : (fast ? code_of_key(akey[i][j]) : acc[i][j]);
+            const int64_t o = (z * N + n) * M + m;
+            if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
+            else                   static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
+        }
+    }
+}
+
 // ============================ MUL_MAT (xlns32) =============================
 // One chain per thread: block = 64 weight rows (threads) x 1 token group of 4.
 template <bool OUT_F32>
@@ -560,7 +813,31 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
     const int64_t r2 = a->ne12 / a->ne02, r3 = a->ne13 / a->ne03;
-    if (fmt == LNSB_XLNS16) {
+    if (fmt == LNSB_XLNS16 && k_mode == M_BASE) {
+        const int64_t gx = (a->M + FB_BM - 1) / FB_BM, gy = (a->N + FB_BN - 1) / FB_BN;
+        if (gx > 0x7FFFFFFF || gy > 65535) return LNSB_E_TOO_LARGE;
+        const dim3 grid((unsigned) gx, (unsigned) gy, (unsigned) (a->ne12 * a->ne13));
+        const bool vec = a->M % FB_BM == 0 && a->K % 8 == 0 && ((uintptr_t) a->w % 16) == 0 && ((uintptr_t) a->x % 16) == 0;
+        // product log bound that keeps K additions below 2^127: each addition
+        // rounds by at most 2^(1/128), so |sum| <= K * max|p| * 2^(K/128)
+        int lg = 0;
+        while ((int64_t) 1 << lg < a->K) lg++;
+        const int64_t pmax64 = 0x7FFF - 128 - 128 * (int64_t) lg - a->K;
+        const int pmax = (int) (pmax64 < 0 ? -1 : pmax64);
+        static bool fattr[k_max_devices][2] = {};
+        auto kern = out_f32 ? k_mul_mat16_fast<true> : k_mul_mat16_fast<false>;
+        int dev = 0;
+        const int ds = current_device(&dev);
+        if (ds != 0) return ds;
+        if (!fattr[dev][out_f32]) {
+            const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FB_SMEM);
+            if (e != cudaSuccess) return (int) e;
+            fattr[dev][out_f32] = true;
+        }
+        kern<<<grid, FB_THREADS, FB_SMEM, stream>>>(*T, static_cast<const uint16_t *>(a->w),
+                                                    static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
+                                                    a->ne12, r2, r3, pmax, vec ? 1 : 0);
+    } else if (fmt == LNSB_XLNS16) {
         const int64_t gx = (a->M + MM_BM - 1) / MM_BM, gy = (a->N + MM_BN - 1) / MM_BN;
         if (gx > 0x7FFFFFFF || gy > 65535) return LNSB_E_TOO_LARGE;
         const dim3 grid((unsigned) gx, (unsigned) gy, (unsigned) (a->ne12 * a->ne13));
@@ -751,6 +1028,7 @@ int lnsb_upload_tables(int fmt) {
         if (e == cudaSuccess) e = upload(H.dec16, &t.dec16);
         if (e == cudaSuccess) e = upload(H.exp16, &t.exp16);
         if (e == cudaSuccess) e = upload(H.monte16, &t.monte16);
+        if (e == cudaSuccess) e = upload(H.key16, &t.key16);
         if (e == cudaSuccess) e = upload(H.sb32, &t.sb32);
         if (e == cudaSuccess) e = upload(H.db32, &t.db32);
         if (e == cudaSuccess) e = upload(H.db32_hi, &t.db32_hi);

@@ -27,6 +27,17 @@ void build16(host_tables & t) {
     }
     // entries n = 1281 of both halves stay 0 (essential zero)
 
+    t.key16.assign(k16_key_bytes / 4, 0);
+    for (int n = 0; n <= k16_ess; n++) {
+        t.key16[(16 * n) / 4] = 8 * t.sbdb16[n];                                 // 16 * sb(n)
+        if (n == 0) {
+            t.key16[1] = k16_key_cancel;                                          // byte 4: x + (-x)
+        } else {
+            t.key16[(16 * n - 4) / 4] = 8 * t.sbdb16[k16_sign_off / 2 + n];      // 16 * db(n)
+            t.key16[(16 * n + 4) / 4] = 8 * t.sbdb16[k16_sign_off / 2 + n];
+        }
+    }
+
     t.conv16.resize(65536);
     for (uint32_t i = 0; i < 65536; i++) {
         const uint32_t bits = i << 16;

@@ -34,6 +34,17 @@ constexpr int k16_ess_clamp2 = 2 * (k16_ess + 1);   // 2562: clamp of 2n, entry 
 // Monte fine tables: sb/db at 8 extra fraction bits, n = 0..2303
 constexpr int k16_monte_n = 2304;
 
+// "Key" form of the xlns16 Gaussian-log table, for the base-mode mul_mat fast
+// path.  A value is carried as key = 16 * log + 4 * (value >= 0 ? 1 : 0); for
+// two keys a (accumulator) and p (term), |a - p| is 16n (same signs) or
+// 16n +- 4 (opposite signs), n = |log a - log p|.  The table is indexed by
+// that difference as a byte offset: 32-bit entry at byte 16n holds 16 * sb(n),
+// at bytes 16n - 4 and 16n + 4 16 * db(n) (n >= 1), at byte 4 the exact-
+// cancellation sentinel, and 0 from n = 1281 on (essential zero).
+constexpr int k16_key_max   = 16 * (k16_ess + 1) + 4;          // largest index used
+constexpr int k16_key_bytes = (k16_key_max + 4 + 15) / 16 * 16;  // 20512
+constexpr int k16_key_cancel = -(1 << 30);
+
 // xlns32 interpolation geometry (units: 2^-23 octave)
 struct seg32 { uint32_t lo, hi; int shift; int base; };
 constexpr uint32_t k32_one = 1u << 23;
@@ -46,6 +57,7 @@ struct host_tables {
     std::vector<float>    dec16;       // 65536
     std::vector<uint16_t> exp16;       // 65536
     std::vector<int16_t>  monte16;     // [2 * k16_monte_n]: sb fine, then db fine
+    std::vector<int32_t>  key16;       // k16_key_bytes / 4 entries, see k16_key_max
     // xlns32
     seg32 sb_seg[2], db_seg[4];
     std::vector<int32_t>  sb32, db32;  // concatenated knots
