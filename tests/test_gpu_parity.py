@@ -79,6 +79,8 @@ def run_mm16(ks, w_rows, x, slices=(1, 1, 1, 1), seed=7, f32=False):
 @pytest.mark.parametrize("K,M,N", [
     (1536, 576, 8),      # BASELINE configs[0] shape
     (576, 1536, 64),     # configs[1] shape, 64 of its 512 tokens
+    (576, 1536, 512),    # configs[1] in full (the tiled throughput kernel)
+    (96, 1024, 640),     # tiled kernel, K tail in the last chunk
     (1, 64, 8),          # K=1: no addition at all
     (2, 32, 3),
     (7, 40, 5),          # K not a multiple of 8, M not a multiple of 32
@@ -134,19 +136,20 @@ def test_mul_mat16_special_codes(orc, ks16):
 
 
 @pytest.mark.parametrize("where", ["early", "late", "none"])
-def test_mul_mat16_range_fallback(orc, ks16, where):
-    """A zero operand (or a huge one) part-way along K: the base kernel's
+@pytest.mark.parametrize("M,K,N", [(128, 300, 40), (1024, 100, 640)])
+def test_mul_mat16_range_fallback(orc, ks16, where, M, K, N):
+    """A zero operand (or a huge one) part-way along K: the base kernels'
     key-form fast path must hand the chains over to packed codes at that
-    chunk and still match bit for bit."""
+    point and still match bit for bit (small shape: latency kernel; large:
+    tiled kernel)."""
     rng = np.random.default_rng(17)
-    M, K, N = 128, 300, 40
     w = codes16(orc, rng, (M, K), 0.02)
     x = codes16(orc, rng, (N, K), 1.0)
     if where == "early":
         x[3, 5] = 0x0000            # exact zero in the first chunk
     elif where == "late":
-        w[7, 250] = 0x0000          # zero in a later chunk
-        x[11, 251] = 0x7FF0         # and a huge activation
+        w[7, K - 50] = 0x0000       # zero in a later chunk
+        x[11, K - 49] = 0x7FF0      # and a huge activation
     want = orc.mul_mat16(ks16.mode, w, x, seed=3, nthreads=NT).ravel()
     got = run_mm16(ks16, w, x, seed=3)
     assert np.array_equal(got, want)

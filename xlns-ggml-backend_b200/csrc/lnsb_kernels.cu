@@ -330,12 +330,14 @@ k_mul_mat16(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __re
 // ===================== MUL_MAT (xlns16, base mode, key form) ================
 //
 // The base-mode hot kernel.  Every chain carries its accumulator as a key
-// (lnsb_tables.h): key = 16 * log + 4 * [value >= 0].  One LNS addition of a
+// (lnsb_tables.h): key = 16 * log + 4 * sign.  One LNS addition of a
 // product p is then
 //     d   = |a - p|                 one signed difference gives n and the sign case
 //     adj = T[min(d, KEYMAX)]       sb or db (or the cancellation sentinel), * 16
-//     a   = max(max(a, p) + adj, 4) max() picks the larger magnitude and, on a tie,
-//                                   the positive one; the clamp maps x + (-x) to +0
+//     a   = max(max(a, p) + adj, 0) max() picks the larger magnitude (a tie of
+//                                   equal signs is harmless); for x + (-x) the
+//                                   sentinel drives the sum below 0 and the clamp
+//                                   gives key 0 = +0, as xlns16_add does
 // and the product key is wkey + xkey with one mask fixing the sign flag, so an
 // addition costs 8 integer instructions instead of ~30 on packed codes.
 // This form drops the saturation of the product and of the sum, so it is
@@ -355,11 +357,11 @@ constexpr int FB_XP  = FB_KC + 8;                                  // x code pit
 constexpr int FB_XKP = FB_KC + 4;                                  // x key pitch, words
 constexpr int FB_WCODES = FB_KC * FB_BM;                           // halfwords
 constexpr int FB_XCODES = FB_BN * FB_XP;                           // halfwords
-constexpr int FB_OFF_WKEY = k16_key_bytes;
+constexpr int FB_REPL     = k16_key_bytes + 36;                   // replica stride: shifts banks by 9 words
+constexpr int FB_OFF_WKEY = (2 * FB_REPL + 15) / 16 * 16;
 constexpr int FB_OFF_XKEY = FB_OFF_WKEY + FB_KC * FB_BM * 4;
-constexpr int FB_OFF_TAB2 = FB_OFF_XKEY + FB_BN * FB_XKP * 4;      // packed-code table (slow path)
-constexpr int FB_OFF_RED  = FB_OFF_TAB2 + MM_TABPAD;
-constexpr int FB_OFF_CODE = FB_OFF_RED + 64;
+constexpr int FB_OFF_RED  = FB_OFF_XKEY + FB_BN * FB_XKP * 4;
+constexpr int FB_OFF_CODE = FB_OFF_RED + 128;
 constexpr int FB_SMEM     = FB_OFF_CODE + 2 * (FB_WCODES + FB_XCODES) * 2;
 
 __device__ __forceinline__ void fb_stage(uint16_t * wc, uint16_t * xc, const uint16_t * __restrict__ W,
@@ -391,37 +393,55 @@ __device__ __forceinline__ void fb_stage(uint16_t * wc, uint16_t * xc, const uin
     }
 }
 
-// one addition in key form (see above)
-__device__ __forceinline__ int key_step(int a, int p, const unsigned char * tab) {
-    const int d   = min(abs(a - p), k16_key_max);
+// one addition in key form (see above); rbase: byte offset of this thread's
+// table replica, folded into the clamp
+__device__ __forceinline__ int key_step(int a, int p, const unsigned char * tab, int rbase) {
+    const int d   = __viaddmin_s32(abs(a - p), rbase, k16_key_max + rbase);
     const int adj = *reinterpret_cast<const int *>(tab + d);
-    return __viaddmax_s32(max(a, p), adj, 4);
+    return __viaddmax_s32(max(a, p), adj, 0);
 }
-__device__ __forceinline__ int key_of_code_w(uint32_t c) {      // weight operand: log biased by -0x4000
-    return (int) (((c & 0x7FFFu) - 0x4000u) << 4) | (int) ((~c >> 13) & 4u);
+// Largest growth of a sum's log (units of 2^-7 octave) over n additions whose
+// terms are no larger than max(|sum|, |term|): each xlns16 addition returns the
+// exact sum times at most 2^(1/128), so |sum_n| <= 2^(n/128) (n+1) max, i.e.
+// growth <= 128 ceil(log2(n+1)) + n.  One more 128 covers the last addition.
+__host__ __device__ constexpr int growth_bound(int n) {
+    int lg = 0;
+    while ((1 << lg) < n + 1) lg++;
+    return 128 * lg + n + 128;
 }
-__device__ __forceinline__ int key_of_code_x(uint32_t c) {      // activation operand: +4 folds the sign flag
-    return (int) ((c & 0x7FFFu) << 4) + (int) ((~c >> 13) & 4u) + 4;
+
+__device__ __forceinline__ int key_of_code_w(uint32_t c) {      // weight operand: 16 * log + 4 * sign
+    return (int) (((c << 4) & 0x7FFF0u) | ((c >> 13) & 4u));
 }
+__device__ __forceinline__ int key_of_code_x(uint32_t c) {      // activation operand carries the -0x4000 bias
+    return (int) (((c << 4) & 0x7FFF0u) | ((c >> 13) & 4u)) - 16 * 0x4000;
+}
+// sign flags add to 4 * (ws + xs); bit 3 is set only for two negatives
 __device__ __forceinline__ int key_of_product(int wkey, int xkey) { return (wkey + xkey) & ~8; }
 __device__ __forceinline__ uint32_t code_of_key(int key) {
-    return ((uint32_t) (key >> 4) & 0x7FFFu) | ((key & 4) ? 0u : 0x8000u);
+    return ((uint32_t) (key >> 4) & 0x7FFFu) | (((uint32_t) key & 4u) << 13);
 }
+__device__ __forceinline__ int key_of_code(uint32_t c) { return key_of_code_w(c); }
 
 template <bool OUT_F32>
 __global__ void __launch_bounds__(FB_THREADS, 4)
 k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
                  void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
-                 int64_t r2, int64_t r3, int pmax, int vec) {
+                 int64_t r2, int64_t r3, int vec) {
     extern __shared__ __align__(16) unsigned char smem[];
     int *      wkeys = reinterpret_cast<int *>(smem + FB_OFF_WKEY);
     int *      xkeys = reinterpret_cast<int *>(smem + FB_OFF_XKEY);
-    int16_t *  tab2  = reinterpret_cast<int16_t *>(smem + FB_OFF_TAB2);
     int *      red   = reinterpret_cast<int *>(smem + FB_OFF_RED);
     uint16_t * codes = reinterpret_cast<uint16_t *>(smem + FB_OFF_CODE);
 
-    for (int i = threadIdx.x; i < k16_key_bytes / 4; i += FB_THREADS) reinterpret_cast<int *>(smem)[i] = T.key16[i];
-    for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += FB_THREADS) tab2[i] = T.sbdb16[i];
+    // two replicas of the key table, one per lane parity: same-sign lookups
+    // of one replica fall in banks 4j, the other's in 4j + 1
+    for (int i = threadIdx.x; i < k16_key_bytes / 4; i += FB_THREADS) {
+        const int v = T.key16[i];
+        reinterpret_cast<int *>(smem)[i] = v;
+        reinterpret_cast<int *>(smem + FB_REPL)[i] = v;
+    }
+    const int rbase = (threadIdx.x & 1) * FB_REPL;
 
     const int64_t z = blockIdx.z, i12 = z % ne12, i13 = z / ne12;
     const int64_t m0 = (int64_t) blockIdx.x * FB_BM, n0 = (int64_t) blockIdx.y * FB_BN;
@@ -437,7 +457,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
     bool fast = true;                                   // uniform across the block
     const int nchunks = (int) ((K + FB_KC - 1) / FB_KC);
     const int64_t nvalid = imin64(FB_BN, N - n0);
-    red16 R{ &T, tab2, nullptr };
+    red16 R{ &T, T.sbdb16, nullptr };                   // slow path reads the packed table from L1/L2
 
     if (nchunks > 0) {
         fb_stage(codes, codes + FB_WCODES, Wz, Xz, K, M, N, m0, n0, 0, vec != 0);
@@ -471,21 +491,34 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
                 xkeys[r * FB_XKP + col] = key_of_code_x(cx);
                 if (r < nvalid && col < kvalid) { const int l = (int) (cx & 0x7FFFu); xmin = min(xmin, l); xmax = max(xmax, l); }
             }
+            // the largest accumulator log entering this chunk
+            int amax = 0;
+            if (c > 0) {
+#pragma unroll
+                for (int i = 0; i < FB_TM; i++)
+#pragma unroll
+                    for (int j = 0; j < FB_TN; j++) amax = max(amax, akey[i][j] >> 4);
+            }
             wmin = __reduce_min_sync(0xFFFFFFFFu, wmin);
             wmax = __reduce_max_sync(0xFFFFFFFFu, wmax);
             xmin = __reduce_min_sync(0xFFFFFFFFu, xmin);
             xmax = __reduce_max_sync(0xFFFFFFFFu, xmax);
+            amax = __reduce_max_sync(0xFFFFFFFFu, amax);
             if ((threadIdx.x & 31) == 0) {
-                red[warp * 4 + 0] = wmin; red[warp * 4 + 1] = wmax; red[warp * 4 + 2] = xmin; red[warp * 4 + 3] = xmax;
+                red[warp * 8 + 0] = wmin; red[warp * 8 + 1] = wmax; red[warp * 8 + 2] = xmin; red[warp * 8 + 3] = xmax;
+                red[warp * 8 + 4] = amax;
             }
             __syncthreads();
-            int a0 = 0x7FFF, a1 = 0, b0 = 0x7FFF, b1 = 0;
+            int a0 = 0x7FFF, a1 = 0, b0 = 0x7FFF, b1 = 0, am = 0;
 #pragma unroll
             for (int w = 0; w < FB_THREADS / 32; w++) {
-                a0 = min(a0, red[w * 4 + 0]); a1 = max(a1, red[w * 4 + 1]);
-                b0 = min(b0, red[w * 4 + 2]); b1 = max(b1, red[w * 4 + 3]);
+                a0 = min(a0, red[w * 8 + 0]); a1 = max(a1, red[w * 8 + 1]);
+                b0 = min(b0, red[w * 8 + 2]); b1 = max(b1, red[w * 8 + 3]);
+                am = max(am, red[w * 8 + 4]);
             }
-            const bool ok = a0 + b0 - 0x4000 >= 964 && a1 + b1 - 0x4000 <= pmax;
+            // exact in key form: every product >= 2^-120 (no sum can underflow)
+            // and no sum can reach 2^127 within this chunk (growth_bound)
+            const bool ok = a0 + b0 - 0x4000 >= 964 && max(am, a1 + b1 - 0x4000) + growth_bound(FB_KC) <= 0x7FFF;
             if (!ok) {
                 fast = false;
                 if (c > 0) {
@@ -513,7 +546,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
                     for (int i = 0; i < FB_TM; i++)
 #pragma unroll
                         for (int j = 0; j < FB_TN; j++)
-                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem);
+                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem, rbase);
                 }
             }
             for (; k + 4 <= kvalid; k += 4) {
@@ -529,7 +562,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 #pragma unroll
                         for (int j = 0; j < FB_TN; j++) {
                             const int xk = u == 0 ? xv[j].x : u == 1 ? xv[j].y : u == 2 ? xv[j].z : xv[j].w;
-                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xk), smem);
+                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xk), smem, rbase);
                         }
                 }
             }
@@ -540,7 +573,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
                 for (int i = 0; i < FB_TM; i++)
 #pragma unroll
                     for (int j = 0; j < FB_TN; j++)
-                        akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem);
+                        akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem, rbase);
             }
         } else {
             // packed codes, full xlns16 semantics
@@ -577,6 +610,165 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
             if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
             else                   static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
         }
+    }
+}
+
+// ============== MUL_MAT (xlns16, base mode, few outputs: latency form) ========
+//
+// When M*N is too small to fill the GPU with the tiled kernel (decode, the
+// reference's K=1536 x N=8 case), time is one chain's latency: K dependent
+// additions.  This kernel minimises that latency: one chain per thread (128
+// consecutive weight rows of one token per CTA), the token's row resident in
+// shared memory, W streamed through cp.async in 64-step chunks, and the key
+// form with a signed 41 KB table, so the dependent path of one addition is
+//     t = min(a - p, KM)  (DPX add-min)  ->  max(t, -KM)  ->  table load
+//       ->  a = max(max(a, p) + adj, 4)  (DPX add-max)
+// Range safety is decided per K chunk for the whole block (as in
+// k_mul_mat16_fast), so the chunk's steps carry no branch and consecutive
+// steps overlap; a chunk that fails the check runs on packed codes.
+constexpr int LT_ROWS = 128, LT_KC = 128;
+constexpr int LT_KM   = k16_key_max;                              // 20500
+constexpr int LT_TABS = (2 * LT_KM + 4 + 15) / 16 * 16;           // signed table bytes
+constexpr int LT_OFF_TAB2 = LT_TABS;
+constexpr int LT_OFF_W    = LT_OFF_TAB2 + MM_TABPAD;              // 2 stages of W codes
+constexpr int LT_WSTAGE   = LT_KC * LT_ROWS;                      // halfwords
+constexpr int LT_OFF_X    = LT_OFF_W + 2 * LT_WSTAGE * 2;         // x keys (K words) then x codes (K halfwords)
+constexpr int LT_MAX_K    = 16384;
+inline int lt_smem(int64_t K) { return LT_OFF_X + (int) K * 6 + 16; }
+
+__device__ __forceinline__ void lt_stage(uint16_t * ws, const uint16_t * __restrict__ W, int64_t K, int64_t M,
+                                         int64_t m0, int64_t k0, bool vec) {
+    if (vec) {
+#pragma unroll
+        for (int it = 0; it < (LT_KC * LT_ROWS / 8) / LT_ROWS; it++) {   // 1024 copies of 16 B
+            const int c = threadIdx.x + it * LT_ROWS;
+            const int r = c >> 4, q = c & 15;
+            if (k0 + r < K) {
+                if (m0 + q * 8 < M) cp_async16(ws + r * LT_ROWS + q * 8, W + (k0 + r) * M + m0 + q * 8);
+                else *reinterpret_cast<uint4 *>(ws + r * LT_ROWS + q * 8) = make_uint4(0x40004000u, 0x40004000u, 0x40004000u, 0x40004000u);
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < LT_WSTAGE; i += LT_ROWS) {
+            const int r = i / LT_ROWS, c = i % LT_ROWS;
+            const int64_t k = k0 + r, m = m0 + c;
+            ws[i] = (k < K && m < M) ? W[k * M + m] : (uint16_t) 0x4000;
+        }
+    }
+}
+
+template <bool OUT_F32>
+__global__ void __launch_bounds__(LT_ROWS)
+k_mul_mat16_lat(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
+                void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
+                int64_t r2, int64_t r3, int vec) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    int16_t *  tab2  = reinterpret_cast<int16_t *>(smem + LT_OFF_TAB2);
+    uint16_t * wst   = reinterpret_cast<uint16_t *>(smem + LT_OFF_W);
+    int *      xkeys = reinterpret_cast<int *>(smem + LT_OFF_X);
+    uint16_t * xcod  = reinterpret_cast<uint16_t *>(smem + LT_OFF_X + K * 4);
+    __shared__ int red[LT_ROWS / 32][4];
+
+    // signed table: entry for difference D (a multiple of 4) at byte LT_KM + D
+    for (int i = threadIdx.x; i < LT_TABS / 4; i += LT_ROWS) {
+        const int d = i * 4 - LT_KM;
+        const int ad = d < 0 ? -d : d;
+        reinterpret_cast<int *>(smem)[i] = ad <= k16_key_max ? T.key16[ad / 4] : 0;
+    }
+    for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += LT_ROWS) tab2[i] = T.sbdb16[i];
+
+    const int64_t z = blockIdx.z, i12 = z % ne12, i13 = z / ne12;
+    const int64_t n = blockIdx.y;
+    const int64_t m0 = (int64_t) blockIdx.x * LT_ROWS;
+    const int64_t m = m0 + threadIdx.x;
+    const int warp = threadIdx.x >> 5;
+    const uint16_t * Wz = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
+    const uint16_t * xr = X + (z * N + n) * K;
+    int xmin = 0x7FFF, xmax = 0;
+    for (int64_t k = threadIdx.x; k < K; k += LT_ROWS) {
+        const uint32_t c = xr[k];
+        xcod[k]  = (uint16_t) c;
+        xkeys[k] = key_of_code_x(c);
+        xmin = min(xmin, (int) (c & 0x7FFFu));
+        xmax = max(xmax, (int) (c & 0x7FFFu));
+    }
+    xmin = __reduce_min_sync(0xFFFFFFFFu, xmin);
+    xmax = __reduce_max_sync(0xFFFFFFFFu, xmax);
+    if ((threadIdx.x & 31) == 0) { red[warp][0] = xmin; red[warp][1] = xmax; }
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < LT_ROWS / 32; w++) { xmin = min(xmin, red[w][0]); xmax = max(xmax, red[w][1]); }
+
+    const int nchunks = (int) ((K + LT_KC - 1) / LT_KC);
+    if (nchunks > 0) {
+        lt_stage(wst, Wz, K, M, m0, 0, vec != 0);
+        cp_async_commit();
+    }
+    int a = 0;                                          // accumulator key
+    for (int c = 0; c < nchunks; c++) {
+        const uint16_t * ws = wst + (c & 1) * LT_WSTAGE;
+        if (c + 1 < nchunks) {
+            lt_stage(wst + ((c + 1) & 1) * LT_WSTAGE, Wz, K, M, m0, (int64_t) (c + 1) * LT_KC, vec != 0);
+            cp_async_commit();
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const int64_t kb = (int64_t) c * LT_KC;
+        const int kvalid = (int) imin64(LT_KC, K - kb);
+        // block-wide range check of this chunk (see k_mul_mat16_fast): 16x2
+        // SIMD min/max over the staged codes (columns past M hold 1.0)
+        unsigned vmin = 0x7FFF7FFFu, vmax = 0u;
+#pragma unroll
+        for (int it = 0; it < LT_WSTAGE / 8 / LT_ROWS; it++) {
+            const int v = threadIdx.x + it * LT_ROWS;           // 16-byte vector index
+            if ((v >> 4) < kvalid) {
+                const uint4 q = *reinterpret_cast<const uint4 *>(ws + v * 8);
+                const unsigned w0 = q.x & 0x7FFF7FFFu, w1 = q.y & 0x7FFF7FFFu, w2 = q.z & 0x7FFF7FFFu, w3 = q.w & 0x7FFF7FFFu;
+                vmin = __vminu2(vmin, __vminu2(__vminu2(w0, w1), __vminu2(w2, w3)));
+                vmax = __vmaxu2(vmax, __vmaxu2(__vmaxu2(w0, w1), __vmaxu2(w2, w3)));
+            }
+        }
+        int wmin = (int) min(vmin & 0xFFFFu, vmin >> 16), wmax = (int) max(vmax & 0xFFFFu, vmax >> 16);
+        int amax = c > 0 ? (a >> 4) : 0;
+        wmin = __reduce_min_sync(0xFFFFFFFFu, wmin);
+        wmax = __reduce_max_sync(0xFFFFFFFFu, wmax);
+        amax = __reduce_max_sync(0xFFFFFFFFu, m < M ? amax : 0);
+        __syncthreads();                                // red[] reuse
+        if ((threadIdx.x & 31) == 0) { red[warp][0] = wmin; red[warp][1] = wmax; red[warp][2] = amax; }
+        __syncthreads();
+        int w0 = 0x7FFF, w1 = 0, am = 0;
+#pragma unroll
+        for (int w = 0; w < LT_ROWS / 32; w++) { w0 = min(w0, red[w][0]); w1 = max(w1, red[w][1]); am = max(am, red[w][2]); }
+        const bool fast = w0 + xmin - 0x4000 >= 964 && max(am, w1 + xmax - 0x4000) + growth_bound(LT_KC) <= 0x7FFF;
+
+        int k = 0;
+        if (fast) {
+            if (c == 0) {
+                a = key_of_product(key_of_code_w(ws[threadIdx.x]), xkeys[0]);
+                k = 1;
+            }
+#pragma unroll 8
+            for (; k < kvalid; k++) {
+                const int p   = key_of_product(key_of_code_w(ws[k * LT_ROWS + threadIdx.x]), xkeys[kb + k]);
+                const int t   = max(__viaddmin_s32(a, -p, LT_KM), -LT_KM);
+                const int adj = *reinterpret_cast<const int *>(smem + LT_KM + t);
+                a = __viaddmax_s32(max(a, p), adj, 0);
+            }
+        } else {
+            uint32_t ac = c == 0 ? mul16(ws[threadIdx.x], xcod[0]) : code_of_key(a);
+            if (c == 0) k = 1;
+            for (; k < kvalid; k++) ac = add16(ac, mul16(ws[k * LT_ROWS + threadIdx.x], xcod[kb + k]), tab2);
+            a = key_of_code(ac);
+        }
+        __syncthreads();
+    }
+    if (m < M) {
+        const uint32_t v = K == 0 ? 0u : code_of_key(a);
+        const int64_t o = (z * N + n) * M + m;
+        if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
+        else                   static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
     }
 }
 
@@ -813,17 +1005,29 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
     const int64_t r2 = a->ne12 / a->ne02, r3 = a->ne13 / a->ne03;
-    if (fmt == LNSB_XLNS16 && k_mode == M_BASE) {
+    const int64_t tiles = ((a->M + FB_BM - 1) / FB_BM) * ((a->N + FB_BN - 1) / FB_BN) * a->ne12 * a->ne13;
+    if (fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && a->K <= LT_MAX_K && a->N <= 65535) {
+        // few outputs: one chain per thread, latency form
+        const dim3 grid((unsigned) ((a->M + LT_ROWS - 1) / LT_ROWS), (unsigned) a->N, (unsigned) (a->ne12 * a->ne13));
+        const bool vec = a->M % 8 == 0 && ((uintptr_t) a->w % 16) == 0;
+        const int smem = lt_smem(a->K);
+        auto kern = out_f32 ? k_mul_mat16_lat<true> : k_mul_mat16_lat<false>;
+        static int lattr[k_max_devices][2] = {};
+        int dev = 0;
+        const int ds = current_device(&dev);
+        if (ds != 0) return ds;
+        if (lattr[dev][out_f32] < smem) {
+            const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return (int) e;
+            lattr[dev][out_f32] = smem;
+        }
+        kern<<<grid, LT_ROWS, smem, stream>>>(*T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
+                                              dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, vec ? 1 : 0);
+    } else if (fmt == LNSB_XLNS16 && k_mode == M_BASE) {
         const int64_t gx = (a->M + FB_BM - 1) / FB_BM, gy = (a->N + FB_BN - 1) / FB_BN;
         if (gx > 0x7FFFFFFF || gy > 65535) return LNSB_E_TOO_LARGE;
         const dim3 grid((unsigned) gx, (unsigned) gy, (unsigned) (a->ne12 * a->ne13));
         const bool vec = a->M % FB_BM == 0 && a->K % 8 == 0 && ((uintptr_t) a->w % 16) == 0 && ((uintptr_t) a->x % 16) == 0;
-        // product log bound that keeps K additions below 2^127: each addition
-        // rounds by at most 2^(1/128), so |sum| <= K * max|p| * 2^(K/128)
-        int lg = 0;
-        while ((int64_t) 1 << lg < a->K) lg++;
-        const int64_t pmax64 = 0x7FFF - 128 - 128 * (int64_t) lg - a->K;
-        const int pmax = (int) (pmax64 < 0 ? -1 : pmax64);
         static bool fattr[k_max_devices][2] = {};
         auto kern = out_f32 ? k_mul_mat16_fast<true> : k_mul_mat16_fast<false>;
         int dev = 0;
@@ -836,7 +1040,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         }
         kern<<<grid, FB_THREADS, FB_SMEM, stream>>>(*T, static_cast<const uint16_t *>(a->w),
                                                     static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
-                                                    a->ne12, r2, r3, pmax, vec ? 1 : 0);
+                                                    a->ne12, r2, r3, vec ? 1 : 0);
     } else if (fmt == LNSB_XLNS16) {
         const int64_t gx = (a->M + MM_BM - 1) / MM_BM, gy = (a->N + MM_BN - 1) / MM_BN;
         if (gx > 0x7FFFFFFF || gy > 65535) return LNSB_E_TOO_LARGE;

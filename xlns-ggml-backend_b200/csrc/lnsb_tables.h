@@ -35,7 +35,7 @@ constexpr int k16_ess_clamp2 = 2 * (k16_ess + 1);   // 2562: clamp of 2n, entry 
 constexpr int k16_monte_n = 2304;
 
 // "Key" form of the xlns16 Gaussian-log table, for the base-mode mul_mat fast
-// path.  A value is carried as key = 16 * log + 4 * (value >= 0 ? 1 : 0); for
+// path.  A value is carried as key = 16 * log + 4 * (value < 0 ? 1 : 0); for
 // two keys a (accumulator) and p (term), |a - p| is 16n (same signs) or
 // 16n +- 4 (opposite signs), n = |log a - log p|.  The table is indexed by
 // that difference as a byte offset: 32-bit entry at byte 16n holds 16 * sb(n),
