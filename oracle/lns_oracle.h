@@ -23,8 +23,8 @@
  * Parity status: the xlns16 base adder and the operand products are pinned by
  * the reference's printed known answers; the float->xlns16 conversion table,
  * the xlns32 adder, the Monte dither rule and the LPVIP adder are restated
- * algorithms whose bit patterns the reference checkout cannot confirm
- * ("parity unpinned" for those parts -- see DESIGN.md).
+ * algorithms whose bit patterns the reference checkout cannot confirm: parity
+ * is unpinned for those parts beyond the printed figures they reproduce.
  */
 #ifndef LNS_ORACLE_H
 #define LNS_ORACLE_H

@@ -6,8 +6,9 @@ oracle; tests/golden/reference_pins.json holds what the reference printed
 (tests/golden/make_pins.py).  PINNED lists every figure the restatement
 reproduces digit for digit -- each is asserted exactly.  The remaining
 figures depend on parts of the absent xlnscpp library that the evidence does
-not determine ("Parity status"); they are reported, and
-bounded where the reference states a gate.
+not determine (the conversion table's bias, the Monte dither rule, the LPVIP
+adder); they are printed beside the reference's by test_report, and bounded
+where the reference states a gate.
 """
 import json
 import os
@@ -107,5 +108,7 @@ def test_report(computed, pins, capsys):
     walk({"standalone": computed["standalone"], "suite": computed["suite"]},
          {"standalone": pins["standalone"], "suite": pins["suite"]}, ())
     with capsys.disabled():
-        pass
+        print("\n%-40s %-45s %s" % ("figure", "this oracle", "reference printed"))
+        for name, c, p in rows:
+            print("%-40s %-45s %s" % (name, c, p))
     assert rows
