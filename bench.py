@@ -69,6 +69,21 @@ def peaks():
         return 6650.0, 1965.0, "fallback"
 
 
+# ncu capture summary of the kernel each workload runs (DRAM bytes of one launch)
+PROFILE = {"configs1": "profiles/k_mul_mat16_fast_configs1.md", "configs0": "profiles/k_mul_mat16_lat_configs0.md"}
+
+
+def traffic_of(workload):
+    try:
+        with open(os.path.join(ROOT, PROFILE[workload])) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":")[1])
+    except (OSError, KeyError, ValueError):
+        pass
+    return None
+
+
 def adds_of(K, M, N):
     return M * N * max(K - 1, 0)
 
@@ -318,7 +333,9 @@ def run_ours(args, wl):
                    "K": K, "M": M, "N": N, "mode": args.mode, "parallelism": "rowshard%d" % world,
                    "l2": "flushed (256 MB write) before every timed step"},
         "roofline": {"bound": "int", "achieved": achieved, "peak": int_peak, "unit": UNIT, "frac": achieved / int_peak,
-                     "traffic": None, "c_mode": c, "sm_mhz_used": f_mhz,
+                     "traffic": traffic_of(args.workload) if args.mode == "base" else None,
+                     "traffic_source": PROFILE.get(args.workload) if args.mode == "base" else None,
+                     "c_mode": c, "sm_mhz_used": f_mhz,
                      "note": "integer-issue bound: %d SMs x %d lanes x f_sm / c_mode (%s SM clock)" % (SMS, LANES_PER_SM, "sampled" if clocks.get("sm_mhz") else src),
                      "hbm": {"achieved_gbs": bytes_alg / kern_s / 1e9, "peak_gbs": hbm, "frac": bytes_alg / kern_s / 1e9 / hbm,
                              "algorithmic_bytes": bytes_alg}},
