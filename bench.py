@@ -55,7 +55,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--mode", default="base")
-    p.add_argument("--workload", default="configs1", choices=sorted(WORKLOADS))
+    p.add_argument("--workload", default="configs1", choices=sorted(WORKLOADS) + ["configs4"])
+    p.add_argument("--sweep-k", type=int, default=4096, help="configs4: K in {2048, 4096, 8192, 14336}")
+    p.add_argument("--sweep-n", type=int, default=16, help="configs4: tokens in {1, 16, 128}")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -209,6 +211,12 @@ def run_ours(args, wl):
                                 device_id=torch.device("cuda", local))
 
     K, M, N = wl["K"], wl["M"], wl["N"]
+    strong = wl.get("strong", False)
+    if strong:
+        from lnsb200 import shard
+        if M % world:
+            raise SystemExit("configs4 needs the 8192 rows to divide by the GPU count")
+        M = M // world                       # this rank's rows
     ks = lnsb200.KernelSet(16, args.mode)
     ks.upload_tables()
     rng = np.random.default_rng(wl["seed"] + 1000 * rank)
@@ -219,7 +227,7 @@ def run_ours(args, wl):
     ks.to_lns_transposed(w_f32, w, M, K, M)
     ks.to_lns(x_f32, x)
     out = torch.empty(N * M, dtype=torch.int16, device="cuda")
-    gathered = torch.empty(world * N * M, dtype=torch.int16, device="cuda") if world > 1 else None
+    from lnsb200 import shard
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device="cuda")          # 256 MB > L2 (126 MB)
     stream = torch.cuda.current_stream()
 
@@ -241,7 +249,7 @@ def run_ours(args, wl):
     def step():
         launch()
         if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
+            shard.all_gather_rows(out.view(N, M), world).contiguous()
 
     for _ in range(args.warmup):
         flush.zero_()
@@ -268,7 +276,7 @@ def run_ours(args, wl):
         launch()
         ev[i][1].record(stream)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
+            shard.all_gather_rows(out.view(N, M), world).contiguous()    # ggml [N][M*world] order
         ev[i][2].record(stream)
     torch.cuda.synchronize()
     if dist:
@@ -318,6 +326,7 @@ def run_ours(args, wl):
     adds = adds_of(K, M, N)
     value = adds * world * args.steps / (step_ms / 1000) / 1e9
     e2e_val = adds * world * args.steps / (e2e_ms / 1000) / 1e9
+    scaling = "strong" if strong else "weak"
     kern_s = kern_ms / 1000 / args.steps
     hbm, smmax, src = peaks()
     f_mhz = clocks.get("sm_mhz") or smmax
@@ -327,9 +336,9 @@ def run_ours(args, wl):
     bytes_alg = algorithmic_bytes(K, M, N)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": step_ms / args.steps, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
         "dtype": "u16 (xlns16 codes; integer LNS arithmetic)", "data": "synthetic",
-        "config": {"workload": wl["desc"] + (" per rank, output rows sharded + NCCL all_gather" if world > 1 else ""),
+        "config": {"workload": wl["desc"] + ((" per rank" if not strong else "") + ", output rows sharded + NCCL all_gather" if world > 1 else ""),
                    "K": K, "M": M, "N": N, "mode": args.mode, "parallelism": "rowshard%d" % world,
                    "l2": "flushed (256 MB write) before every timed step"},
         "roofline": {"bound": "int", "achieved": achieved, "peak": int_peak, "unit": UNIT, "frac": achieved / int_peak,
@@ -343,7 +352,7 @@ def run_ours(args, wl):
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not strong:
         line["cpu_baseline"] = cpu_leg(wl, args.mode, 10.0, os.cpu_count() or 1)
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -354,7 +363,14 @@ def run_ours(args, wl):
 
 def main():
     args = parse()
-    wl = WORKLOADS[args.workload]
+    if args.workload == "configs4":
+        # 8192 x K weights, K x N activations, seed 3; output rows
+        # sharded across the ranks (strong scaling), gathered with NCCL
+        wl = dict(desc="BASELINE configs[4] LNS16 mul_mat sweep: W 8192x%d x X %dx%d, rows sharded"
+                       % (args.sweep_k, args.sweep_k, args.sweep_n),
+                  K=args.sweep_k, M=8192, N=args.sweep_n, seed=3, strong=True)
+    else:
+        wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, wl)
     return run_ours(args, wl)

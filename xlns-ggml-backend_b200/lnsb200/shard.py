@@ -1,0 +1,64 @@
+"""Output-row sharding of mul_mat across ranks (one process per GPU).
+
+Every output of mul_mat is an independent chain of LNS additions, so
+splitting the M output rows into contiguous blocks changes no bit: rank r
+keeps the k-major weight columns [m0, m1) of every slice (its own [K][M_r]
+matrix), computes dst[:, m0:m1] and the ranks exchange their blocks with one
+all-gather.  Monte chains start from their global output index, so the Monte
+result is shard-invariant too (the C ABI takes the global row offset through
+the weight pointer only; callers that shard Monte mul_mats pass each rank's
+start state, see monte_seed_for_shard).
+
+The all-gather yields [world][N][M_r]; dst in ggml order is [N][M], i.e. the
+gathered blocks permuted (gather_layout).
+"""
+
+
+def row_range(M, world, rank):
+    """[m0, m1) of rank's rows: contiguous blocks, the first M % world ranks one row longer."""
+    base, extra = divmod(M, world)
+    m0 = rank * base + min(rank, extra)
+    return m0, m0 + base + (1 if rank < extra else 0)
+
+
+def equal_shards(M, world):
+    return M % world == 0
+
+
+def shard_weights_kmajor(w_kmajor, M, world, rank):
+    """The rank's columns of a k-major [K][M] weight (a torch tensor or numpy array)."""
+    m0, m1 = row_range(M, world, rank)
+    return w_kmajor.reshape(-1, M)[:, m0:m1]
+
+
+def gather_layout(gathered, world, N, Mr):
+    """[world][N][Mr] -> [N][world*Mr] (ggml dst order) for equal shards."""
+    return gathered.reshape(world, N, Mr).permute(1, 0, 2).reshape(N, world * Mr)
+
+
+def all_gather_rows(dst_shard, world, group=None):
+    """All-gathers equal [N][Mr] row blocks into the full [N][world*Mr] output
+    (NCCL: one all_gather_into_tensor; gloo, for CPU tests: all_gather).  The
+    codes travel as raw bytes: neither backend has a 16-bit integer type, and
+    a gather does no arithmetic."""
+    import torch
+    import torch.distributed as dist
+    N, Mr = dst_shard.shape
+    src = dst_shard.contiguous().view(-1).view(torch.uint8)
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty(world * src.numel(), dtype=torch.uint8, device=dst_shard.device)
+        dist.all_gather_into_tensor(out, src, group=group)
+    else:
+        parts = [torch.empty_like(src) for _ in range(world)]
+        dist.all_gather(parts, src, group=group)
+        out = torch.cat(parts)
+    return gather_layout(out.view(dst_shard.dtype), world, N, Mr)
+
+
+def monte_seed_for_shard(seed, jump, M, N, K, rank, world):
+    """LFSR state where rank's first chain starts, given the op's seed, for a
+    single-slice mul_mat: the chain of global output o = m * N + n starts
+    o * (K-1) draws after the op's seed, so the rank's outputs are the global
+    ones shifted by m0 * N.  jump(s, n) is the LFSR jump-ahead."""
+    m0, _ = row_range(M, world, rank)
+    return jump(seed, m0 * N * max(K - 1, 0))
