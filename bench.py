@@ -54,7 +54,7 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--mode", default="base")
+    p.add_argument("--mode", default=None, help="sum mode library (default: base; sum32 for configs4)")
     p.add_argument("--workload", default="configs1", choices=sorted(WORKLOADS) + ["configs4"])
     p.add_argument("--sweep-k", type=int, default=4096, help="configs4: K in {2048, 4096, 8192, 14336}")
     p.add_argument("--sweep-n", type=int, default=16, help="configs4: tokens in {1, 16, 128}")
@@ -371,6 +371,8 @@ def main():
                   K=args.sweep_k, M=8192, N=args.sweep_n, seed=3, strong=True)
     else:
         wl = WORKLOADS[args.workload]
+    if args.mode is None:
+        args.mode = "sum32" if args.workload == "configs4" else "base"
     if args.impl == "reference":
         return run_reference(args, wl)
     return run_ours(args, wl)

@@ -87,6 +87,7 @@ def run_mm16(ks, w_rows, x, slices=(1, 1, 1, 1), seed=7, f32=False):
     (65, 96, 65),        # one full K chunk + 1; ragged token tile
     (200, 37, 1),        # N=1 (decode), odd M
     (4096, 64, 2),       # long K
+    (40, 2048, 640),     # enough units for two tokens per lane (sum32 flat-add kernel)
 ])
 def test_mul_mat16(orc, ks16, K, M, N):
     rng = np.random.default_rng(K * 7919 + M * 31 + N)
@@ -270,7 +271,8 @@ def codes32(orc, rng, shape, sigma):
     return orc.from_f32_32(rng.normal(0.0, sigma, shape).astype(np.float32))
 
 
-@pytest.mark.parametrize("K,M,N", [(576, 96, 9), (1, 8, 2), (129, 33, 4)])
+@pytest.mark.parametrize("K,M,N", [(576, 96, 9), (1, 8, 2), (129, 33, 4), (7, 40, 5), (200, 37, 1),
+                                   (40, 2048, 640), (1536, 576, 8)])
 def test_mul_mat32(orc, ks32, K, M, N):
     rng = np.random.default_rng(K + M + N)
     w = codes32(orc, rng, (M, K), 0.02)
@@ -279,6 +281,28 @@ def test_mul_mat32(orc, ks32, K, M, N):
     out = torch.empty(N * M, dtype=torch.int32, device="cuda")
     ks32.mul_mat_lns(dev32(np.ascontiguousarray(w.T)), dev32(x), out, K, M, N)
     assert np.array_equal(host32(out), want)
+
+
+def test_mul_mat32_slices_specials_f32(orc, ks32):
+    """broadcast slices, special codes (zeros, saturation, cancelling tokens) and F32 output"""
+    rng = np.random.default_rng(17)
+    ne02, ne03, ne12, ne13 = 1, 2, 3, 2
+    M, K, N = 48, 70, 6
+    w = codes32(orc, rng, (ne03, ne02, M, K), 0.5)
+    x = codes32(orc, rng, (ne13, ne12, N, K), 1.0)
+    specials = np.array([0, 0x80000000, 0x7FFFFFFF, 0xFFFFFFFF, 0x40000000, 0xC0000000, 1], np.uint32)
+    w.ravel()[rng.integers(0, w.size, 300)] = rng.choice(specials, 300)
+    x.ravel()[rng.integers(0, x.size, 100)] = rng.choice(specials, 100)
+    x[0, 0, 1] = x[0, 0, 0] ^ 0x80000000
+    want = orc.mul_mat32(w, x, slices=(ne02, ne03, ne12, ne13), nthreads=NT).ravel()
+    wk = np.ascontiguousarray(np.swapaxes(w, -1, -2))
+    out = torch.empty(want.size, dtype=torch.int32, device="cuda")
+    ks32.mul_mat_lns(dev32(wk), dev32(x), out, K, M, N, (ne02, ne03, ne12, ne13))
+    assert np.array_equal(host32(out), want)
+    outf = torch.empty(want.size, dtype=torch.float32, device="cuda")
+    ks32.mul_mat(dev32(wk), dev32(x), outf, K, M, N, (ne02, ne03, ne12, ne13))
+    torch.cuda.synchronize()
+    assert np.array_equal(outf.cpu().numpy().view(np.uint32), orc.to_f32_32(want).view(np.uint32))
 
 
 def test_soft_max32_rms_norm32(orc, ks32):

@@ -33,6 +33,7 @@ struct dev_tables {
     const int32_t *  db32;
     const int32_t *  db32_hi;    // 2048
     const int32_t *  db32_lo;    // 4096
+    const int32_t *  flat32;     // k32f_words (flat xlns32 addition image)
     const uint32_t * logm32;     // 2^23 or null
     const float *    expm32;     // 2^23 or null
     const int32_t *  lpvip_db;   // 2^23 or null
@@ -153,6 +154,99 @@ __device__ __forceinline__ uint32_t add32(const dev_tables & T, uint32_t a, uint
     long long p = (long long) (mx & 0x7FFFFFFFu) + adj;
     p = p < 0 ? 0 : (p > 0x7FFFFFFFLL ? 0x7FFFFFFFLL : p);
     return (mx & 0x80000000u) | (uint32_t) p;
+}
+
+// add32 over the flat image F (k32f_sb; shared memory in the kernels), without
+// branches: every lane makes the cotransformation lookups and the result is
+// selected afterwards, so the chains of a warp and of one thread interleave
+// instead of diverging.  Same bits as add32:
+//   cot (opposite signs, d < 1): db(d) = max(la, lb) + sb(|la - lb|) with
+//     la = db(d & 4095), lb = db(d & ~4095) - (d & 4095); the k32f_none
+//     entries reproduce the cases d < 4096 and d % 4096 == 0 (|la - lb| >= ess)
+//   otherwise sb(d) or db(d) by interpolation; z >= ess lands on the last
+//     knot (value 0) with fraction 0
+// The interpolation product fits in 32 bits (checked when the image is built).
+__host__ __device__ __forceinline__ uint32_t add32f(const int32_t * F, uint32_t a, uint32_t b) {
+    const uint32_t al = a & 0x7FFFFFFFu, bl = b & 0x7FFFFFFFu;
+    const bool     agt   = al > bl;
+    const uint32_t d     = agt ? al - bl : bl - al;
+    const uint32_t mx    = agt ? a : b;
+    const bool     usedb = (int32_t) (a ^ b) < 0;
+    const bool     cot   = usedb && d < k32_one;
+    const int32_t  d2 = (int32_t) (d & 4095u);
+    const int32_t  la = F[k32f_lo + d2];
+    const int32_t  lb = F[k32f_hi + (int32_t) ((d >> 12) & 2047u)] - d2;
+    const int32_t  hi = la > lb ? la : lb;
+    const uint32_t gap = (uint32_t) (la > lb ? la - lb : lb - la);
+    uint32_t z = cot ? gap : d;
+    z = z < k32_ess ? z : k32_ess;
+    const int32_t  desc = F[k32f_desc + (int32_t) (z >> 23) + (usedb && !cot ? k32f_desc_db : 0)];
+    const int      sh   = desc & 31;
+    const int32_t  i    = (int32_t) (z >> sh) + (desc >> 5);
+    const int32_t  f    = (int32_t) (z & ((1u << sh) - 1u));
+    const int32_t  v0 = F[i], v1 = F[i + 1];
+    const int32_t  adj = v0 + (((v1 - v0) * f) >> sh) + (cot ? hi : 0);
+    const uint32_t u = (mx & 0x7FFFFFFFu) + (uint32_t) adj;      // adj > -2^28: wrap means negative
+    uint32_t p = u < 0x7FFFFFFFu ? u : 0x7FFFFFFFu;
+    if (u >= 0xC0000000u) p = 0;
+    const uint32_t r = (mx & 0x80000000u) | p;
+    return (usedb && d == 0) ? 0u : r;
+}
+
+// sb(z) or db(z) (db: z >= 1) by interpolation in multiply form: entry e of
+// k32f_dsc2 / k32f_dms gives the left knot's word and 2^(32 - shift), so the
+// shifts run as multiplications on the multiply-add pipe, not the integer ALU.
+__device__ __forceinline__ int32_t interp32f(const int32_t * F, uint32_t z, int e) {
+    const int2     ds = reinterpret_cast<const int2 *>(F + k32f_dsc2)[e];
+    const uint32_t ir = __umulhi(z, (uint32_t) ds.y);                    // z >> shift
+    const int32_t  f  = (int32_t) ir * F[k32f_dms + e] + (int32_t) z;     // z mod 2^shift
+    const int32_t * kp = F + ds.x + (int32_t) ir;
+    const int32_t  v0 = kp[0], v1 = kp[1];
+    return v0 + __mulhi((v1 - v0) * f, ds.y);                           // floor(.. / 2^shift)
+}
+
+// the cotransformed db of add32f_lean's rare branch: opposite signs, d < 1
+__device__ __forceinline__ uint32_t add32f_cot(const int32_t * F, uint32_t mx, uint32_t d) {
+    const int32_t  d2 = (int32_t) (d & 4095u);
+    const int32_t  la = F[k32f_lo + d2];
+    const int32_t  lb = F[k32f_hi + (int32_t) (d >> 12)] - d2;
+    const int32_t  hi = la > lb ? la : lb;
+    uint32_t       z  = (uint32_t) (la > lb ? la - lb : lb - la);
+    z = z < k32_ess ? z : k32_ess;
+    const int32_t  p = (int32_t) (mx & 0x7FFFFFFFu) + hi + interp32f(F, z, (int) (z >> 23));   // hi + sb < 0
+    const uint32_t r = (mx & 0x80000000u) | (uint32_t) (p > 0 ? p : 0);
+    return d == 0 ? 0u : r;
+}
+
+// add32 over the flat image for throughput kernels, in two parts so a thread
+// can interleave several chains: add32f_main for every chain, then a branch
+// per chain for the lanes that need add32f_cot.  The main part is sb(d), or
+// db(d) for d >= 1, and needs no clamp from below: 0 <= sb <= 2^23, and
+// d + db(d) >= 0 for every d >= 1 (checked exhaustively over the table), so
+// |mx| + adj >= 0.  Above, |mx| + adj > 0x7FFFFFFF carries into the sign bit
+// (mx + adj then differs from mx in bit 31) and saturates to 0x7FFFFFFF.  The
+// cotransformed db (opposite signs, d < 1, exact cancellation included) is
+// the cot part.  Same bits as add32.
+struct add32f_part {
+    uint32_t r, mx, d;
+    bool     cot;
+};
+__device__ __forceinline__ add32f_part add32f_main(const int32_t * F, uint32_t a, uint32_t b) {
+    add32f_part o;
+    const uint32_t al = a & 0x7FFFFFFFu, bl = b & 0x7FFFFFFFu;
+    const bool     agt   = al > bl;
+    o.d  = agt ? al - bl : bl - al;
+    o.mx = agt ? a : b;
+    const bool     usedb = (int32_t) (a ^ b) < 0;
+    const uint32_t z     = o.d < k32_ess ? o.d : k32_ess;
+    const uint32_t r     = o.mx + (uint32_t) interp32f(F, z, (int) (z >> 23) + (usedb ? k32f_dsc2_db : 0));
+    o.r   = (int32_t) (r ^ o.mx) < 0 ? (o.mx | 0x7FFFFFFFu) : r;
+    o.cot = usedb && o.d < k32_one;
+    return o;
+}
+__device__ __forceinline__ uint32_t add32f_lean(const int32_t * F, uint32_t a, uint32_t b) {
+    const add32f_part o = add32f_main(F, a, b);
+    return o.cot ? add32f_cot(F, o.mx, o.d) : o.r;
 }
 
 __device__ __forceinline__ uint32_t sub32(const dev_tables & T, uint32_t a, uint32_t b) {

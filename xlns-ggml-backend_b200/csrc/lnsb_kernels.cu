@@ -150,6 +150,11 @@ __device__ __forceinline__ void cp_async16(void * smem, const void * gmem) {
     const unsigned s = (unsigned) __cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
 }
+// zero-fills the 16 bytes beyond src_bytes (0 or 16 here)
+__device__ __forceinline__ void cp_async16_zfill(void * smem, const void * gmem, int src_bytes) {
+    const unsigned s = (unsigned) __cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
@@ -772,37 +777,284 @@ k_mul_mat16_lat(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * 
     }
 }
 
-// ============================ MUL_MAT (xlns32) =============================
-// One chain per thread: block = 64 weight rows (threads) x 1 token group of 4.
-template <bool OUT_F32>
-__global__ void __launch_bounds__(128)
-k_mul_mat32(dev_tables T, const uint32_t * __restrict__ W, const uint32_t * __restrict__ X, void * __restrict__ dst,
-            int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3) {
-    constexpr int NB = 4;
-    const int64_t m = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t n0 = (int64_t) blockIdx.y * NB;
-    const int64_t z = blockIdx.z, i12 = z % ne12, i13 = z / ne12;
-    if (m >= M) return;
-    const uint32_t * ws = W + ((i13 / r3) * ne02 + i12 / r2) * K * M + m;
-    const uint32_t * xs = X + z * N * K + n0 * K;
-    const int nb = (int) imin64(NB, N - n0);
-    uint32_t acc[NB] = { 0, 0, 0, 0 };
-    if (K > 0) {
-        const uint32_t w0 = ws[0];
+// ================= MUL_MAT over the flat xlns32 addition ====================
+//
+// xlns16 in sum32 mode (acc32 = add32(acc32, t << 16), narrowed once at the
+// end; lns-backend/cuda/lns-cuda-xlns16.cu:75-130, lns16-sum32.h:59-107) and
+// the xlns32 format (lns-backend/cuda/lns-cuda-xlns32.cu:30-67) share this
+// kernel.  The flat addition image (k32f_words, ~100 KB) is resident in shared
+// memory, one CTA per SM (32 warps for xlns16, 16 for xlns32).  A warp runs
+// 32 x TN chains side by side: 32 consecutive weight rows (one per lane)
+// against TN tokens (two once there are enough units of work, so a lane has
+// two independent chains to interleave).  Units of work (slice, 32-row block,
+// token group) are dealt to warps round-robin with the CTA index fastest, so a
+// small problem spreads over every SM; all units cost the same K steps, so the
+// static deal is balanced.  Operands stream through a per-warp cp.async ring
+// of 8-step chunks (the warp's 32 consecutive rows of the k-major weights, and
+// each token's 8 values), A32_STAGES - 1 chunks ahead; unaligned operands take
+// a register-prefetch path instead.  Each step is add32f_main for every chain
+// (ALU work moved to the multiply pipe where the interpolation allows) and a
+// branch per chain for the rare cotransformed case (add32f_cot).
+constexpr int A32_THREADS = 512;
+// threads per CTA: 32 warps per SM where the per-warp rings fit beside the
+// table (xlns16), else 16
+__host__ __device__ constexpr int a32_threads(int fmt, bool ring) { return fmt == 16 && ring ? 1024 : A32_THREADS; }
+constexpr int A32_SMEM    = k32f_words * 4;
+#ifndef LNSB_A32_TN2_MIN_UNITS
+#define LNSB_A32_TN2_MIN_UNITS 2     // two tokens per lane once each warp gets this many units
+#endif
+
+template <int FMT> struct a32_fmt;
+template <> struct a32_fmt<16> {
+    using elem = uint16_t;
+    static constexpr int xvec = 1;    // uint4 per 8 values
+    __device__ static __forceinline__ uint32_t term(uint32_t w, uint32_t x) { return mul16(w, x) << 16; }
+    __device__ static __forceinline__ uint32_t finish(uint32_t acc) {
+        if ((acc & 0x7FFFFFFFu) >= 0x7FFF8000u) return ((acc >> 16) | 0x7FFFu) & 0xFFFFu;
+        return (acc + 0x8000u) >> 16;
+    }
+    __device__ static __forceinline__ void store(const dev_tables & T, void * dst, int64_t o, uint32_t v, bool f32) {
+        if (f32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
+        else     static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
+    }
+};
+template <> struct a32_fmt<32> {
+    using elem = uint32_t;
+    static constexpr int xvec = 2;
+    __device__ static __forceinline__ uint32_t term(uint32_t w, uint32_t x) { return mul32(w, x); }
+    __device__ static __forceinline__ uint32_t finish(uint32_t acc) { return acc; }
+    __device__ static __forceinline__ void store(const dev_tables & T, void * dst, int64_t o, uint32_t v, bool f32) {
+        if (f32) static_cast<float *>(dst)[o] = to_f32_32(T, v);
+        else     static_cast<uint32_t *>(dst)[o] = v;
+    }
+};
+
+template <int FMT, int TN>
+struct a32_chunk {
+    uint32_t w[8];
+    uint4    x[TN][a32_fmt<FMT>::xvec];
+    __device__ __forceinline__ uint32_t xv(int t, int j) const {
+        const uint32_t * p = reinterpret_cast<const uint32_t *>(&x[t][0]);
+        if constexpr (FMT == 16) return (p[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
+        else                     return p[j];
+    }
+};
+
+template <int FMT, int TN>
+__device__ __forceinline__ void a32_load(a32_chunk<FMT, TN> & c, const typename a32_fmt<FMT>::elem * __restrict__ wl,
+                                         const typename a32_fmt<FMT>::elem * const (&xt)[TN], int64_t k0, int64_t K,
+                                         int64_t M, bool vecx) {
+    using E = typename a32_fmt<FMT>::elem;
+    if (k0 + 8 <= K) {
 #pragma unroll
-        for (int j = 0; j < NB; j++) if (j < nb) acc[j] = mul32(w0, __ldg(xs + j * K));
-        for (int64_t k = 1; k < K; k++) {
-            const uint32_t w = ws[k * M];
+        for (int j = 0; j < 8; j++) c.w[j] = __ldg(wl + (k0 + j) * M);
+    } else {
 #pragma unroll
-            for (int j = 0; j < NB; j++) if (j < nb) acc[j] = add32(T, acc[j], mul32(w, __ldg(xs + j * K + k)));
-        }
+        for (int j = 0; j < 8; j++) c.w[j] = k0 + j < K ? (uint32_t) __ldg(wl + (k0 + j) * M) : 0u;
     }
 #pragma unroll
-    for (int j = 0; j < NB; j++) {
-        if (j >= nb) continue;
-        const int64_t o = (z * N + n0 + j) * M + m;
-        if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_32(T, acc[j]);
-        else                   static_cast<uint32_t *>(dst)[o] = acc[j];
+    for (int t = 0; t < TN; t++) {
+        if (vecx && k0 + 8 <= K) {
+#pragma unroll
+            for (int v = 0; v < a32_fmt<FMT>::xvec; v++) c.x[t][v] = __ldg(reinterpret_cast<const uint4 *>(xt[t] + k0) + v);
+        } else {
+            __align__(16) E tmp[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) tmp[j] = k0 + j < K ? __ldg(xt[t] + k0 + j) : (E) 0;
+#pragma unroll
+            for (int v = 0; v < a32_fmt<FMT>::xvec; v++) c.x[t][v] = reinterpret_cast<const uint4 *>(tmp)[v];
+        }
+    }
+}
+
+// One step of every chain of a lane: the main parts first (independent, so
+// they interleave), then a single branch for the chains that need the fix.
+template <int FMT, int TN>
+__device__ __forceinline__ void a32_step_x(const int32_t * F, uint32_t (&acc)[TN], uint32_t w, const uint32_t (&x)[TN]) {
+    using OP = a32_fmt<FMT>;
+    uint32_t    b[TN];
+    add32f_part o[TN];
+#pragma unroll
+    for (int t = 0; t < TN; t++) {
+        b[t] = OP::term(w, x[t]);
+        o[t] = add32f_main(F, acc[t], b[t]);
+    }
+#pragma unroll
+    for (int t = 0; t < TN; t++) acc[t] = o[t].cot ? add32f_cot(F, o[t].mx, o[t].d) : o[t].r;
+}
+template <int FMT, int TN>
+__device__ __forceinline__ void a32_step(const int32_t * F, uint32_t (&acc)[TN], uint32_t w, const a32_chunk<FMT, TN> & c,
+                                         int j) {
+    uint32_t x[TN];
+#pragma unroll
+    for (int t = 0; t < TN; t++) x[t] = c.xv(t, j);
+    a32_step_x<FMT, TN>(F, acc, w, x);
+}
+
+// The steps of one 8-step chunk: j in [j0, kv) (kv < 8 only in the last chunk).
+template <int FMT, int TN>
+__device__ __forceinline__ void a32_steps(const int32_t * F, const a32_chunk<FMT, TN> & c, uint32_t (&acc)[TN],
+                                          bool first, int64_t kv) {
+    using OP = a32_fmt<FMT>;
+    if (first) {
+#pragma unroll
+        for (int t = 0; t < TN; t++) acc[t] = OP::term(c.w[0], c.xv(t, 0));
+#pragma unroll
+        for (int j = 1; j < 8; j++) {
+            if (j < kv) a32_step<FMT, TN>(F, acc, c.w[j], c, j);
+        }
+    } else if (kv >= 8) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) a32_step<FMT, TN>(F, acc, c.w[j], c, j);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (j < kv) a32_step<FMT, TN>(F, acc, c.w[j], c, j);
+        }
+    }
+}
+
+// Per-warp ring of A32_STAGES chunks in shared memory, filled with cp.async:
+// chunk c + A32_STAGES - 1 is in flight while chunk c is consumed.  A stage is
+// the 8 x 32 weights of the warp's row block ([k][row], as in global memory)
+// and the 8 values of each of its TN tokens.  Needs 16-byte aligned weight
+// rows (M * size % 16 == 0) and token rows (K * size % 16 == 0).
+constexpr int A32_STAGES = 4;
+template <int FMT, int TN>
+struct a32_ring {
+    using E = typename a32_fmt<FMT>::elem;
+    static constexpr int es     = (int) sizeof(E);
+    static constexpr int wbytes = 8 * 32 * es;
+    static constexpr int stage  = wbytes + TN * 8 * es;
+    static constexpr int warp_bytes = A32_STAGES * stage;
+    static constexpr int smem   = k32f_words * 4 + (a32_threads(FMT, true) / 32) * warp_bytes;
+
+    // issue chunk k0 of the row block starting at row m0 (wb: the slice's k-major weights)
+    __device__ static __forceinline__ void issue(unsigned char * st, const E * __restrict__ wb, const E * const (&xt)[TN],
+                                                 int64_t m0, int64_t k0, int64_t K, int64_t M, int lane) {
+        constexpr int per_k = 32 * es / 16;              // 16-byte pieces per weight row of the block
+#pragma unroll
+        for (int p = lane; p < 8 * per_k; p += 32) {
+            const int     k = p / per_k, q = p % per_k;
+            const int64_t kk = k0 + k, mm = m0 + q * (16 / es);
+            const bool    ok = kk < K && mm < M;          // M % (16 / es) == 0: pieces are whole
+            cp_async16_zfill(st + k * 32 * es + q * 16, ok ? (const void *) (wb + kk * M + mm) : (const void *) wb,
+                             ok ? 16 : 0);
+        }
+        constexpr int per_t = 8 * es / 16;
+        if (lane < TN * per_t) {
+            const int     t = lane / per_t, q = lane % per_t;
+            const int64_t kk = k0 + q * (16 / es);
+            const bool    ok = kk < K;
+            cp_async16_zfill(st + wbytes + t * 8 * es + q * 16, ok ? (const void *) (xt[t] + kk) : (const void *) xt[t],
+                             ok ? 16 : 0);
+        }
+    }
+    __device__ static __forceinline__ void read(a32_chunk<FMT, TN> & c, const unsigned char * st, int lane) {
+        const E * ws = reinterpret_cast<const E *>(st);
+#pragma unroll
+        for (int j = 0; j < 8; j++) c.w[j] = ws[j * 32 + lane];
+#pragma unroll
+        for (int t = 0; t < TN; t++) {
+#pragma unroll
+            for (int v = 0; v < a32_fmt<FMT>::xvec; v++)
+                c.x[t][v] = reinterpret_cast<const uint4 *>(st + wbytes + t * 8 * es)[v];
+        }
+    }
+};
+
+template <int FMT, int TN, bool OUT_F32, bool RING>
+__global__ void __launch_bounds__(a32_threads(FMT, RING), 1)
+k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
+              const typename a32_fmt<FMT>::elem * __restrict__ X, void * __restrict__ dst, int64_t K, int64_t M,
+              int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3, int64_t nz, int vecx) {
+    using E  = typename a32_fmt<FMT>::elem;
+    using OP = a32_fmt<FMT>;
+    using RG = a32_ring<FMT, TN>;
+    extern __shared__ __align__(16) int32_t F[];
+    constexpr int NT = a32_threads(FMT, RING);
+    for (int i = threadIdx.x; i < k32f_words / 4; i += NT)
+        reinterpret_cast<int4 *>(F)[i] = __ldg(reinterpret_cast<const int4 *>(T.flat32) + i);
+    __syncthreads();
+
+    const int     lane = threadIdx.x & 31;
+    unsigned char * ring = reinterpret_cast<unsigned char *>(F) + k32f_words * 4 + (threadIdx.x >> 5) * RG::warp_bytes;
+    const int64_t RB = (M + 31) / 32, TG = (N + TN - 1) / TN;
+    const int64_t units  = nz * RB * TG;
+    const int64_t nwarps = (int64_t) gridDim.x * (NT / 32);
+    const int64_t nchunks = (K + 7) / 8;
+    const bool    lat = units <= nwarps;                 // one round: chain latency bounds the time
+    for (int64_t u = (int64_t) (threadIdx.x >> 5) * gridDim.x + blockIdx.x; u < units; u += nwarps) {
+        const int64_t tg = u % TG, rest = u / TG, rb = rest % RB, z = rest / RB;
+        const int64_t i12 = z % ne12, i13 = z / ne12;
+        const int64_t m0 = rb * 32, m = m0 + lane;
+        const E * wb = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
+        const E * xt[TN];
+#pragma unroll
+        for (int t = 0; t < TN; t++) {
+            const int64_t n = tg * TN + t;
+            xt[t] = X + (z * N + (n < N ? n : N - 1)) * K;
+        }
+        uint32_t acc[TN];
+#pragma unroll
+        for (int t = 0; t < TN; t++) acc[t] = 0;
+        if (K > 0) {
+            a32_chunk<FMT, TN> cur;
+            if constexpr (RING) {
+#pragma unroll
+                for (int s = 0; s < A32_STAGES - 1; s++) {
+                    if (s < nchunks) RG::issue(ring + s * RG::stage, wb, xt, m0, s * 8, K, M, lane);
+                    cp_async_commit();
+                }
+                for (int64_t c = 0; c < nchunks; c++) {
+                    cp_async_wait<A32_STAGES - 2>();
+                    __syncwarp();                       // every lane's copies of chunk c landed
+                    const int64_t nx = c + A32_STAGES - 1;   // refills the stage chunk c - 1 used
+                    if (nx < nchunks) RG::issue(ring + (int) (nx % A32_STAGES) * RG::stage, wb, xt, m0, nx * 8, K, M, lane);
+                    cp_async_commit();
+                    const unsigned char * st = ring + (int) (c % A32_STAGES) * RG::stage;
+                    if (lat) {                           // few units: all 8 steps unrolled, operands in registers
+                        RG::read(cur, st, lane);
+                        a32_steps<FMT, TN>(F, cur, acc, c == 0, K - c * 8);
+                        continue;
+                    }
+                    const E * ws = reinterpret_cast<const E *>(st) + lane;
+                    const E * xs = reinterpret_cast<const E *>(st + RG::wbytes);
+                    int j = 0;
+                    if (c == 0) {
+#pragma unroll
+                        for (int t = 0; t < TN; t++) acc[t] = OP::term(ws[0], xs[t * 8]);
+                        j = 1;
+                    }
+                    const int kv = (int) imin64(8, K - c * 8);
+#pragma unroll 2
+                    for (; j < kv; j++) {
+                        uint32_t x[TN];
+#pragma unroll
+                        for (int t = 0; t < TN; t++) x[t] = xs[t * 8 + j];
+                        a32_step_x<FMT, TN>(F, acc, ws[j * 32], x);
+                    }
+                }
+                cp_async_wait<0>();
+                __syncwarp();                           // the ring is free for the next unit
+            } else {
+                const E * wl = wb + (m < M ? m : M - 1);
+                a32_chunk<FMT, TN> nxt;
+                a32_load<FMT, TN>(cur, wl, xt, 0, K, M, vecx != 0);
+                for (int64_t c = 0; c < nchunks; c++) {
+                    if (c + 1 < nchunks) a32_load<FMT, TN>(nxt, wl, xt, (c + 1) * 8, K, M, vecx != 0);
+                    a32_steps<FMT, TN>(F, cur, acc, c == 0, K - c * 8);
+                    cur = nxt;
+                }
+            }
+        }
+        if (m < M) {
+#pragma unroll
+            for (int t = 0; t < TN; t++) {
+                const int64_t n = tg * TN + t;
+                if (n < N) OP::store(T, dst, (z * N + n) * M + m, K == 0 ? 0u : OP::finish(acc[t]), OUT_F32);
+            }
+        }
     }
 }
 
@@ -994,6 +1246,68 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
 
 // ============================ launch helpers ===============================
 
+int sm_count(int dev) {
+    static int sms[k_max_devices] = {};
+    if (sms[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        sms[dev] = v;
+    }
+    return sms[dev];
+}
+
+template <int FMT, int TN, bool OUT_F32, bool RING>
+int launch_a32(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, int64_t r2, int64_t r3, int64_t units,
+               int dev, bool vecx, cudaStream_t stream) {
+    static bool attr[k_max_devices] = {};
+    auto kern = k_mul_mat_a32<FMT, TN, OUT_F32, RING>;
+    constexpr int smem = RING ? a32_ring<FMT, TN>::smem : A32_SMEM;
+    if (!attr[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return (int) e;
+        attr[dev] = true;
+    }
+    using E = typename a32_fmt<FMT>::elem;
+    const int64_t grid = units < sm_count(dev) ? units : sm_count(dev);
+    kern<<<(unsigned) grid, a32_threads(FMT, RING), smem, stream>>>(T, static_cast<const E *>(a->w), static_cast<const E *>(a->x),
+                                                       dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3,
+                                                       a->ne12 * a->ne13, vecx ? 1 : 0);
+    return launch_status();
+}
+
+template <int FMT, int TN>
+int launch_a32_by(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, bool out_f32, bool ring, int64_t r2,
+                  int64_t r3, int64_t units, int dev, bool vecx, cudaStream_t stream) {
+    if (ring) return out_f32 ? launch_a32<FMT, TN, true, true>(T, a, dst, r2, r3, units, dev, vecx, stream)
+                             : launch_a32<FMT, TN, false, true>(T, a, dst, r2, r3, units, dev, vecx, stream);
+    return out_f32 ? launch_a32<FMT, TN, true, false>(T, a, dst, r2, r3, units, dev, vecx, stream)
+                   : launch_a32<FMT, TN, false, false>(T, a, dst, r2, r3, units, dev, vecx, stream);
+}
+
+// sum32-mode xlns16 and xlns32 mul_mat: one or two tokens per lane
+int mul_mat_a32(int fmt, const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, bool out_f32, int64_t r2,
+                int64_t r3, cudaStream_t stream) {
+    int dev = 0;
+    const int ds = current_device(&dev);
+    if (ds != 0) return ds;
+    const int64_t nz = a->ne12 * a->ne13, RB = (a->M + 31) / 32;
+    const int64_t es0 = fmt == LNSB_XLNS16 ? 2 : 4;
+    const bool ring0 = (a->K * es0) % 16 == 0 && ((uintptr_t) a->x % 16) == 0 && (a->M * es0) % 16 == 0 &&
+                       ((uintptr_t) a->w % 16) == 0;
+    const int64_t warps = (int64_t) sm_count(dev) * (a32_threads(fmt == LNSB_XLNS16 ? 16 : 32, ring0) / 32);
+    const bool tn2 = a->N >= 2 && nz * RB * ((a->N + 1) / 2) >= LNSB_A32_TN2_MIN_UNITS * warps;
+    const int64_t units = nz * RB * (tn2 ? (a->N + 1) / 2 : a->N);
+    const int64_t es = fmt == LNSB_XLNS16 ? 2 : 4;
+    const bool vecx = (a->K * es) % 16 == 0 && ((uintptr_t) a->x % 16) == 0;
+    const bool ring = vecx && (a->M * es) % 16 == 0 && ((uintptr_t) a->w % 16) == 0;
+    if (fmt == LNSB_XLNS16) {
+        if (tn2) return launch_a32_by<16, 2>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream);
+        return launch_a32_by<16, 1>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream);
+    }
+    if (tn2) return launch_a32_by<32, 2>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream);
+    return launch_a32_by<32, 1>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream);
+}
+
 int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32, cudaStream_t stream) {
     if (!valid_fmt(fmt) || a == nullptr) return LNSB_E_INVALID;
     if (a->K < 0 || a->M < 0 || a->N < 0 || a->ne02 <= 0 || a->ne03 <= 0 || a->ne12 <= 0 || a->ne13 <= 0) return LNSB_E_INVALID;
@@ -1041,7 +1355,9 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         kern<<<grid, FB_THREADS, FB_SMEM, stream>>>(*T, static_cast<const uint16_t *>(a->w),
                                                     static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
                                                     a->ne12, r2, r3, vec ? 1 : 0);
-    } else if (fmt == LNSB_XLNS16) {
+    } else if (fmt == LNSB_XLNS32 || k_mode == M_SUM32) {
+        return mul_mat_a32(fmt, *T, a, dst, out_f32, r2, r3, stream);
+    } else {
         const int64_t gx = (a->M + MM_BM - 1) / MM_BM, gy = (a->N + MM_BN - 1) / MM_BN;
         if (gx > 0x7FFFFFFF || gy > 65535) return LNSB_E_TOO_LARGE;
         const dim3 grid((unsigned) gx, (unsigned) gy, (unsigned) (a->ne12 * a->ne13));
@@ -1060,13 +1376,6 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         kern<<<grid, MM_THREADS, MM_SMEM, stream>>>(*T, static_cast<const uint16_t *>(a->w),
                                                     static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
                                                     a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0);
-    } else {
-        const int64_t gx = (a->M + 127) / 128, gy = (a->N + 3) / 4;
-        if (gy > 65535) return LNSB_E_TOO_LARGE;
-        const dim3 grid((unsigned) gx, (unsigned) gy, (unsigned) (a->ne12 * a->ne13));
-        auto kern = out_f32 ? k_mul_mat32<true> : k_mul_mat32<false>;
-        kern<<<grid, 128, 0, stream>>>(*T, static_cast<const uint32_t *>(a->w), static_cast<const uint32_t *>(a->x), dst,
-                                       a->K, a->M, a->N, a->ne02, a->ne12, r2, r3);
     }
     return launch_status();
 }
@@ -1224,6 +1533,7 @@ int lnsb_upload_tables(int fmt) {
     device_slot & s = g_slots[dev];
     if ((fmt == LNSB_XLNS16 && s.ready16) || (fmt == LNSB_XLNS32 && s.ready32)) return 0;
     const host_tables & H = get_host_tables(need32, need_lpvip);
+    if (H.flat32.size() != (size_t) k32f_words) return LNSB_E_NO_TABLES;
     dev_tables & t = s.t;
     cudaError_t e = cudaSuccess;
     if (t.sbdb16 == nullptr) {
@@ -1237,6 +1547,7 @@ int lnsb_upload_tables(int fmt) {
         if (e == cudaSuccess) e = upload(H.db32, &t.db32);
         if (e == cudaSuccess) e = upload(H.db32_hi, &t.db32_hi);
         if (e == cudaSuccess) e = upload(H.db32_lo, &t.db32_lo);
+        if (e == cudaSuccess) e = upload(H.flat32, &t.flat32);
         if (e == cudaSuccess) e = upload(H.lfsr_log, &t.lfsr_log);
         if (e == cudaSuccess) e = upload(H.lfsr_alog, &t.lfsr_alog);
         t.sb_base1 = H.sb_seg[1].base;

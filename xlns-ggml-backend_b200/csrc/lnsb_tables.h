@@ -50,6 +50,35 @@ struct seg32 { uint32_t lo, hi; int shift; int base; };
 constexpr uint32_t k32_one = 1u << 23;
 constexpr uint32_t k32_ess = 26u << 23;
 
+// Flat xlns32 addition image (int32 words): everything one xlns32 addition
+// reads, in one block that a kernel keeps in shared memory.
+//   [k32f_sb,   +10498)  sb knots: [0,8) step 2^13, [8,26] step 2^16
+//   [k32f_db,   +8452)   db knots: [1,2) step 2^12, [2,4) 2^13, [4,8) 2^14, [8,26] 2^16
+//   [k32f_lo,   +4096)   db(d) for d = 0..4095 (cotransformation, low part)
+//   [k32f_hi,   +2048)   db(j << 12) for j = 0..2047 (cotransformation, high part)
+//                        index 0 of both holds k32f_none, which makes the
+//                        cotransformation's special cases (d < 4096 or d a
+//                        multiple of 4096) fall out of the general formula
+//   [k32f_desc, +96)     interpolation descriptor per octave s = min(z, ess) >> 23:
+//                        sb at +s, db at +k32f_desc_db + s, (base << 5) | shift,
+//                        the left knot of z being word (z >> shift) + base
+//   [k32f_dsc2, +134)    the same descriptors in multiply form, entry e = s (sb) or
+//                        k32f_dsc2_db + s (db): int2 {base, 2^(32 - shift)}, so
+//                        z >> shift = umulhi(z, 2^(32 - shift)) and t >> shift =
+//                        mulhi(t, 2^(32 - shift))
+//   [k32f_dms,  +67)     -2^shift per entry e: z mod 2^shift = (z >> shift) * -2^shift + z
+constexpr int     k32f_sb      = 0;
+constexpr int     k32f_db      = 10498;
+constexpr int     k32f_lo      = 18950;
+constexpr int     k32f_hi      = 23046;
+constexpr int     k32f_desc    = 25094;
+constexpr int     k32f_desc_db = 48;
+constexpr int     k32f_dsc2    = 25190;         // 8-byte aligned
+constexpr int     k32f_dsc2_db = 40;            // db entries on other banks than sb's
+constexpr int     k32f_dms     = 25324;
+constexpr int     k32f_words   = 25392;         // multiple of 4 (16-byte copies)
+constexpr int32_t k32f_none    = -(1 << 30);
+
 struct host_tables {
     // xlns16
     std::vector<int16_t>  sbdb16;      // k16_tab_bytes / 2 entries, smem image
@@ -63,6 +92,7 @@ struct host_tables {
     std::vector<int32_t>  sb32, db32;  // concatenated knots
     std::vector<int32_t>  db32_hi;     // 2048
     std::vector<int32_t>  db32_lo;     // 4096
+    std::vector<int32_t>  flat32;      // k32f_words, see k32f_sb
     std::vector<uint32_t> logm32;      // 2^23 (LNS32 conversion), may be empty
     std::vector<float>    expm32;      // 2^23 (LNS32 decode), may be empty
     std::vector<int32_t>  lpvip_db;    // 2^23 (LPVIP singular branch), may be empty
