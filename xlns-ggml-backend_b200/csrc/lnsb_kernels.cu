@@ -362,7 +362,15 @@ constexpr int FB_XP  = FB_KC + 8;                                  // x code pit
 constexpr int FB_XKP = FB_KC + 4;                                  // x key pitch, words
 constexpr int FB_WCODES = FB_KC * FB_BM;                           // halfwords
 constexpr int FB_XCODES = FB_BN * FB_XP;                           // halfwords
-constexpr int FB_REPL     = k16_key_bytes + 36;                   // replica stride: shifts banks by 9 words
+// Monte (GGML_LNS16_SUM=monte) runs the same kernel over the fine tables in
+// key form (k16m_key_max): adj = 16 * floor((fine + low byte of the chain's
+// next LFSR state) / 256), one LFSR step per addition and chain.  A dithered
+// step exceeds the exact sum by at most one ulp and falls short by at most one,
+// so the chunk range check below holds for it unchanged.
+constexpr bool FB_MONTE   = k_mode == M_MONTE;
+constexpr int  FB_KEYB    = FB_MONTE ? k16m_key_bytes : k16_key_bytes;
+constexpr int  FB_KEYMAX  = FB_MONTE ? k16m_key_max : k16_key_max;
+constexpr int FB_REPL     = FB_KEYB + 36;                         // replica stride: word offset = 1 mod 4
 constexpr int FB_OFF_WKEY = (2 * FB_REPL + 15) / 16 * 16;
 constexpr int FB_OFF_XKEY = FB_OFF_WKEY + FB_KC * FB_BM * 4;
 constexpr int FB_OFF_RED  = FB_OFF_XKEY + FB_BN * FB_XKP * 4;
@@ -399,10 +407,14 @@ __device__ __forceinline__ void fb_stage(uint16_t * wc, uint16_t * xc, const uin
 }
 
 // one addition in key form (see above); rbase: byte offset of this thread's
-// table replica, folded into the clamp
-__device__ __forceinline__ int key_step(int a, int p, const unsigned char * tab, int rbase) {
-    const int d   = __viaddmin_s32(abs(a - p), rbase, k16_key_max + rbase);
-    const int adj = *reinterpret_cast<const int *>(tab + d);
+// table replica, folded into the clamp; st: the chain's LFSR state (Monte)
+__device__ __forceinline__ int key_step(int a, int p, const unsigned char * tab, int rbase, uint32_t & st) {
+    const int d   = __viaddmin_s32(abs(a - p), rbase, FB_KEYMAX + rbase);
+    int adj = *reinterpret_cast<const int *>(tab + d);
+    if constexpr (FB_MONTE) {
+        st  = lfsr_step(st);
+        adj = ((adj + (int) (st & 0xFFu)) >> 4) & ~15;
+    }
     return __viaddmax_s32(max(a, p), adj, 0);
 }
 // Largest growth of a sum's log (units of 2^-7 octave) over n additions whose
@@ -429,10 +441,10 @@ __device__ __forceinline__ uint32_t code_of_key(int key) {
 __device__ __forceinline__ int key_of_code(uint32_t c) { return key_of_code_w(c); }
 
 template <bool OUT_F32>
-__global__ void __launch_bounds__(FB_THREADS, 4)
+__global__ void __launch_bounds__(FB_THREADS, FB_MONTE ? 2 : 4)
 k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
                  void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
-                 int64_t r2, int64_t r3, int vec) {
+                 int64_t r2, int64_t r3, uint32_t monte_seed, int vec) {
     extern __shared__ __align__(16) unsigned char smem[];
     int *      wkeys = reinterpret_cast<int *>(smem + FB_OFF_WKEY);
     int *      xkeys = reinterpret_cast<int *>(smem + FB_OFF_XKEY);
@@ -441,8 +453,9 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 
     // two replicas of the key table, one per lane parity: same-sign lookups
     // of one replica fall in banks 4j, the other's in 4j + 1
-    for (int i = threadIdx.x; i < k16_key_bytes / 4; i += FB_THREADS) {
-        const int v = T.key16[i];
+    const int32_t * keytab = FB_MONTE ? T.mkey16 : T.key16;
+    for (int i = threadIdx.x; i < FB_KEYB / 4; i += FB_THREADS) {
+        const int v = keytab[i];
         reinterpret_cast<int *>(smem)[i] = v;
         reinterpret_cast<int *>(smem + FB_REPL)[i] = v;
     }
@@ -459,10 +472,25 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 
     int      akey[FB_TM][FB_TN];
     uint32_t acc[FB_TM][FB_TN];
+    uint32_t st[FB_TM][FB_TN];                          // Monte: each chain's LFSR state
     bool fast = true;                                   // uniform across the block
     const int nchunks = (int) ((K + FB_KC - 1) / FB_KC);
     const int64_t nvalid = imin64(FB_BN, N - n0);
-    red16 R{ &T, T.sbdb16, nullptr };                   // slow path reads the packed table from L1/L2
+    red16 R{ &T, T.sbdb16, T.monte16 };                 // slow path reads the packed tables from L1/L2
+#pragma unroll
+    for (int i = 0; i < FB_TM; i++)
+#pragma unroll
+        for (int j = 0; j < FB_TN; j++) {
+            st[i][j] = 0;
+            if constexpr (FB_MONTE) {
+                // the chain of output (z, m, n) starts (its index in the CPU's loop
+                // order z, m, n) * (K - 1) draws after the seed
+                const int64_t m = imin64(m0 + mloc + i, M - 1), n = imin64(n0 + tn + 8 * j, N - 1);
+                const unsigned long long out = ((unsigned long long) z * (unsigned long long) M + (unsigned long long) m) *
+                                               (unsigned long long) N + (unsigned long long) n;
+                if (K > 1) st[i][j] = lfsr_jump(T, monte_seed, out * (unsigned long long) (K - 1));
+            }
+        }
 
     if (nchunks > 0) {
         fb_stage(codes, codes + FB_WCODES, Wz, Xz, K, M, N, m0, n0, 0, vec != 0);
@@ -551,7 +579,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
                     for (int i = 0; i < FB_TM; i++)
 #pragma unroll
                         for (int j = 0; j < FB_TN; j++)
-                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem, rbase);
+                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem, rbase, st[i][j]);
                 }
             }
             for (; k + 4 <= kvalid; k += 4) {
@@ -567,7 +595,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 #pragma unroll
                         for (int j = 0; j < FB_TN; j++) {
                             const int xk = u == 0 ? xv[j].x : u == 1 ? xv[j].y : u == 2 ? xv[j].z : xv[j].w;
-                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xk), smem, rbase);
+                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xk), smem, rbase, st[i][j]);
                         }
                 }
             }
@@ -578,7 +606,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
                 for (int i = 0; i < FB_TM; i++)
 #pragma unroll
                     for (int j = 0; j < FB_TN; j++)
-                        akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem, rbase);
+                        akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem, rbase, st[i][j]);
             }
         } else {
             // packed codes, full xlns16 semantics
@@ -589,13 +617,12 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
                     for (int j = 0; j < FB_TN; j++) acc[i][j] = mul16(wc[mloc + i], xc[(tn + 8 * j) * FB_XP]);
                 k = 1;
             }
-            uint32_t st = 0;
             for (; k < kvalid; k++) {
 #pragma unroll
                 for (int i = 0; i < FB_TM; i++) {
                     const uint32_t w = wc[k * FB_BM + mloc + i];
 #pragma unroll
-                    for (int j = 0; j < FB_TN; j++) acc[i][j] = R.add(acc[i][j], mul16(w, xc[(tn + 8 * j) * FB_XP + k]), st);
+                    for (int j = 0; j < FB_TN; j++) acc[i][j] = R.add(acc[i][j], mul16(w, xc[(tn + 8 * j) * FB_XP + k]), st[i][j]);
                 }
             }
         }
@@ -1337,7 +1364,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         }
         kern<<<grid, LT_ROWS, smem, stream>>>(*T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
                                               dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, vec ? 1 : 0);
-    } else if (fmt == LNSB_XLNS16 && k_mode == M_BASE) {
+    } else if (fmt == LNSB_XLNS16 && (k_mode == M_BASE || k_mode == M_MONTE)) {
         const int64_t gx = (a->M + FB_BM - 1) / FB_BM, gy = (a->N + FB_BN - 1) / FB_BN;
         if (gx > 0x7FFFFFFF || gy > 65535) return LNSB_E_TOO_LARGE;
         const dim3 grid((unsigned) gx, (unsigned) gy, (unsigned) (a->ne12 * a->ne13));
@@ -1354,7 +1381,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         }
         kern<<<grid, FB_THREADS, FB_SMEM, stream>>>(*T, static_cast<const uint16_t *>(a->w),
                                                     static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
-                                                    a->ne12, r2, r3, vec ? 1 : 0);
+                                                    a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0);
     } else if (fmt == LNSB_XLNS32 || k_mode == M_SUM32) {
         return mul_mat_a32(fmt, *T, a, dst, out_f32, r2, r3, stream);
     } else {
@@ -1543,6 +1570,7 @@ int lnsb_upload_tables(int fmt) {
         if (e == cudaSuccess) e = upload(H.exp16, &t.exp16);
         if (e == cudaSuccess) e = upload(H.monte16, &t.monte16);
         if (e == cudaSuccess) e = upload(H.key16, &t.key16);
+        if (e == cudaSuccess) e = upload(H.mkey16, &t.mkey16);
         if (e == cudaSuccess) e = upload(H.sb32, &t.sb32);
         if (e == cudaSuccess) e = upload(H.db32, &t.db32);
         if (e == cudaSuccess) e = upload(H.db32_hi, &t.db32_hi);

@@ -96,6 +96,17 @@ void build16(host_tables & t) {
         }
     }
 
+    t.mkey16.assign(k16m_key_bytes / 4, 0);
+    for (int n = 0; n < k16_monte_n; n++) {
+        t.mkey16[(16 * n) / 4] = t.monte16[n];
+        if (n == 0) {
+            t.mkey16[1] = k16_key_cancel;
+        } else {
+            t.mkey16[(16 * n - 4) / 4] = t.monte16[k16_monte_n + n];
+            t.mkey16[(16 * n + 4) / 4] = t.monte16[k16_monte_n + n];
+        }
+    }
+
     t.lfsr_log.assign(65536, 0);
     t.lfsr_alog.assign(65535, 0);
     uint16_t s = 1;

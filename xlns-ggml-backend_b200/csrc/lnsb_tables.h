@@ -45,6 +45,13 @@ constexpr int k16_key_max   = 16 * (k16_ess + 1) + 4;          // largest index 
 constexpr int k16_key_bytes = (k16_key_max + 4 + 15) / 16 * 16;  // 20512
 constexpr int k16_key_cancel = -(1 << 30);
 
+// The same key indexing over the Monte fine tables, for the Monte mul_mat fast
+// path: 32-bit entry at byte 16n holds the fine sb(n) (x 256), at bytes 16n -
+// 4 and 16n + 4 the fine db(n) (n >= 1), at byte 4 the cancellation sentinel,
+// and 0 from n = k16_monte_n on (the fine tables' end).
+constexpr int k16m_key_max   = 16 * k16_monte_n + 4;
+constexpr int k16m_key_bytes = (k16m_key_max + 4 + 15) / 16 * 16;   // 36880
+
 // xlns32 interpolation geometry (units: 2^-23 octave)
 struct seg32 { uint32_t lo, hi; int shift; int base; };
 constexpr uint32_t k32_one = 1u << 23;
@@ -87,6 +94,7 @@ struct host_tables {
     std::vector<uint16_t> exp16;       // 65536
     std::vector<int16_t>  monte16;     // [2 * k16_monte_n]: sb fine, then db fine
     std::vector<int32_t>  key16;       // k16_key_bytes / 4 entries, see k16_key_max
+    std::vector<int32_t>  mkey16;      // k16m_key_bytes / 4 entries, see k16m_key_max
     // xlns32
     seg32 sb_seg[2], db_seg[4];
     std::vector<int32_t>  sb32, db32;  // concatenated knots
