@@ -373,6 +373,45 @@ __device__ __forceinline__ uint32_t add32_lpvip(const dev_tables & T, uint32_t a
     return (mx & 0x80000000u) | (uint32_t) p;
 }
 
+// add32_lpvip in two parts for the throughput kernels.  Mitchell's
+// approximations collapse on the main path: 1 + u lies in [1, 2], so its
+// Mitchell log2 is u itself, and for d >= 1 (u <= 1/2) 1 - u lies in
+// [1/2, 1), whose Mitchell log2 is -2u exactly.  So sb = u, db = -2u with
+// u = mitchell_exp2_neg(d).  On that path db never goes below zero
+// (|mx| >= d >= 1 >= 2u) and sb can only carry into the sign bit, which then
+// saturates.  The singular case (opposite signs, d < 1) reads the exact db
+// table (lpvip_sing).  Same bits as add32_lpvip.
+struct lpvip_part {
+    uint32_t r, mx, d;
+    bool     sing;
+};
+__host__ __device__ __forceinline__ lpvip_part lpvip_main(uint32_t a, uint32_t b) {
+    lpvip_part o;
+    const uint32_t al = a & 0x7FFFFFFFu, bl = b & 0x7FFFFFFFu;
+    const bool     agt   = al > bl;
+    o.d  = agt ? al - bl : bl - al;
+    o.mx = agt ? a : b;
+    const bool     usedb = (int32_t) (a ^ b) < 0;
+    const uint32_t q  = (o.d >> 23) + ((o.d & (k32_one - 1u)) != 0u ? 1u : 0u);   // ceil(d / 2^23)
+    const uint32_t qs = q < 31u ? q : 31u;
+    uint32_t       u  = (k32_one + ((qs << 23) - o.d)) >> qs;
+    if (q >= 32u) u = 0u;
+    const uint32_t r = o.mx + (usedb ? 0u - 2u * u : u);
+    o.r    = (int32_t) (r ^ o.mx) < 0 ? (o.mx | 0x7FFFFFFFu) : r;
+    o.sing = usedb && o.d < k32_one;
+    return o;
+}
+__host__ __device__ __forceinline__ uint32_t lpvip_sing(const int32_t * lpvip_db, uint32_t mx, uint32_t d) {
+    if (d == 0) return 0u;
+#ifdef __CUDA_ARCH__
+    const int32_t adj = __ldg(lpvip_db + d);
+#else
+    const int32_t adj = lpvip_db[d];
+#endif
+    const int32_t p = (int32_t) (mx & 0x7FFFFFFFu) + adj;
+    return (mx & 0x80000000u) | (uint32_t) (p > 0 ? p : 0);
+}
+
 // ============================== Monte ======================================
 
 __device__ __forceinline__ uint32_t lfsr_step(uint32_t s) { return (s >> 1) ^ ((s & 1u) ? 0xB400u : 0u); }

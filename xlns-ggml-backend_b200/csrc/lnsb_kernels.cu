@@ -129,22 +129,10 @@ __global__ void k_to_f32(dev_tables T, const void * __restrict__ src, float * __
 
 // ============================ MUL_MAT (xlns16) =============================
 //
-// CTA tile: BM = 32 weight rows x BN = 64 tokens, 256 threads; each thread
-// owns TM = 2 rows x TN = 4 tokens = 8 independent chains and interleaves
-// their additions, so eight dependent table lookups are in flight per thread.
-// K advances in chunks of KC = 64: the k-major weight tile [KC][BM] and the
-// activation tile [BN][KC] are staged in shared memory with cp.async (double
-// buffered); the Gaussian-log table (6.7 KB) is resident in shared memory for
-// the whole kernel.  A thread reads 2 weights per k with one 32-bit load and
-// 8 k-steps of a token with one 128-bit load.
-constexpr int MM_BM = 32, MM_BN = 64, MM_KC = 64, MM_TM = 2, MM_TN = 4;
-constexpr int MM_THREADS = (MM_BM / MM_TM) * (MM_BN / MM_TN);   // 256
-constexpr int MM_XPITCH  = MM_KC + 8;                           // halfwords, breaks bank aliasing
-constexpr int MM_WTILE   = MM_KC * MM_BM;                       // halfwords
-constexpr int MM_XTILE   = MM_BN * MM_XPITCH;                   // halfwords
-constexpr int MM_TABPAD  = (k16_tab_bytes + 15) / 16 * 16;       // keeps the tiles 16-byte aligned
-constexpr int MM_FINE    = k_mode == M_MONTE ? 2 * k16_monte_n * 2 : 0;
-constexpr int MM_SMEM    = MM_TABPAD + MM_FINE + 2 * (MM_WTILE + MM_XTILE) * 2;
+// Three kernels cover the xlns16 modes: base and Monte run on packed keys
+// (k_mul_mat16_fast, k_mul_mat16_lat), sum32 / lpvip / Monte-by-LPVIP on the
+// 32-bit accumulator kernel k_mul_mat_a32 further down.
+constexpr int MM_TABPAD  = (k16_tab_bytes + 15) / 16 * 16;       // the packed table, 16-byte padded
 
 __device__ __forceinline__ void cp_async16(void * smem, const void * gmem) {
     const unsigned s = (unsigned) __cvta_generic_to_shared(smem);
@@ -158,179 +146,6 @@ __device__ __forceinline__ void cp_async16_zfill(void * smem, const void * gmem,
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
-
-// Stage one K chunk.  vec: 16-byte aligned rows and full tiles (fast path).
-__device__ __forceinline__ void mm16_stage(uint16_t * ws, uint16_t * xs, const uint16_t * __restrict__ W,
-                                           const uint16_t * __restrict__ X, int64_t K, int64_t M, int64_t N,
-                                           int64_t m0, int64_t n0, int64_t k0, bool vec) {
-    const int tid = threadIdx.x;
-    if (vec) {
-        {   // weights: KC rows of BM halfwords = 4 x 16 B each -> 256 copies
-            const int r = tid >> 2, q = tid & 3;
-            const int64_t k = k0 + r;
-            if (k < K) cp_async16(ws + r * MM_BM + q * 8, W + k * M + m0 + q * 8);
-        }
-#pragma unroll
-        for (int it = 0; it < 2; it++) {   // tokens: BN rows of KC halfwords = 8 x 16 B -> 512 copies
-            const int c = tid + it * MM_THREADS;
-            const int r = c >> 3, q = c & 7;
-            const int64_t n = n0 + r;
-            if (n < N && k0 + q * 8 < K) cp_async16(xs + r * MM_XPITCH + q * 8, X + n * K + k0 + q * 8);
-        }
-    } else {
-        for (int i = tid; i < MM_WTILE; i += MM_THREADS) {
-            const int r = i / MM_BM, c = i % MM_BM;
-            const int64_t k = k0 + r, m = m0 + c;
-            ws[r * MM_BM + c] = (k < K && m < M) ? W[k * M + m] : (uint16_t) 0;
-        }
-        for (int i = tid; i < MM_BN * MM_KC; i += MM_THREADS) {
-            const int r = i / MM_KC, c = i % MM_KC;
-            const int64_t n = n0 + r, k = k0 + c;
-            xs[r * MM_XPITCH + c] = (n < N && k < K) ? X[n * K + k] : (uint16_t) 0;
-        }
-    }
-}
-
-template <bool OUT_F32>
-__global__ void __launch_bounds__(MM_THREADS)
-k_mul_mat16(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X, void * __restrict__ dst,
-            int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3,
-            uint32_t monte_seed, int vec) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    int16_t *  tab  = reinterpret_cast<int16_t *>(smem);
-    int16_t *  fine = reinterpret_cast<int16_t *>(smem + MM_TABPAD);
-    uint16_t * tiles = reinterpret_cast<uint16_t *>(smem + MM_TABPAD + MM_FINE);
-    uint16_t * wsb[2] = { tiles, tiles + MM_WTILE + MM_XTILE };
-    uint16_t * xsb[2] = { tiles + MM_WTILE, tiles + 2 * MM_WTILE + MM_XTILE };
-
-    for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += MM_THREADS) tab[i] = T.sbdb16[i];
-    if constexpr (k_mode == M_MONTE) {
-        for (int i = threadIdx.x; i < 2 * k16_monte_n; i += MM_THREADS) fine[i] = T.monte16[i];
-    }
-
-    const int64_t z   = blockIdx.z;
-    const int64_t i12 = z % ne12, i13 = z / ne12;
-    const int64_t m0  = (int64_t) blockIdx.x * MM_BM, n0 = (int64_t) blockIdx.y * MM_BN;
-    const uint16_t * Wz = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
-    const uint16_t * Xz = X + z * N * K;
-
-    const int ty = threadIdx.x / (MM_BN / MM_TN), tx = threadIdx.x % (MM_BN / MM_TN);
-    const int mloc = ty * MM_TM;                           // rows mloc, mloc + 1
-    // tokens tx, tx + 16, tx + 32, tx + 48 (strided so a warp's 128-bit loads
-    // walk consecutive tile rows)
-
-    red16 R{ &T, tab, fine };
-    uint32_t acc[MM_TM][MM_TN];
-    uint32_t st[MM_TM][MM_TN];
-
-    const int nchunks = (int) ((K + MM_KC - 1) / MM_KC);
-    if (nchunks > 0) {
-        mm16_stage(wsb[0], xsb[0], Wz, Xz, K, M, N, m0, n0, 0, vec != 0);
-        cp_async_commit();
-    }
-    for (int c = 0; c < nchunks; c++) {
-        if (c + 1 < nchunks) {
-            mm16_stage(wsb[(c + 1) & 1], xsb[(c + 1) & 1], Wz, Xz, K, M, N, m0, n0, (int64_t) (c + 1) * MM_KC, vec != 0);
-            cp_async_commit();
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
-        const uint16_t * ws = wsb[c & 1];
-        const uint16_t * xs = xsb[c & 1];
-        const int kvalid = (int) imin64(MM_KC, K - (int64_t) c * MM_KC);
-        int kk = 0;
-        if (c == 0) {
-            // first term of every chain: the product at k = 0
-            const uint32_t w2 = *reinterpret_cast<const uint32_t *>(ws + mloc);
-#pragma unroll
-            for (int i = 0; i < MM_TM; i++) {
-                const uint32_t w = (w2 >> (16 * i)) & 0xFFFFu;
-#pragma unroll
-                for (int j = 0; j < MM_TN; j++) {
-                    const uint32_t x = xs[(tx + 16 * j) * MM_XPITCH];
-                    acc[i][j] = R.from(mul16(w, x));
-                    if constexpr (k_stochastic) {
-                        const int64_t m = m0 + mloc + i, n = n0 + tx + 16 * j;
-                        const unsigned long long out = ((unsigned long long) z * (unsigned long long) M +
-                                                        (unsigned long long) m) * (unsigned long long) N +
-                                                       (unsigned long long) n;
-                        st[i][j] = lfsr_jump(T, monte_seed, out * (unsigned long long) (K - 1));
-                    } else {
-                        st[i][j] = 0;
-                    }
-                }
-            }
-            kk = 1;
-        }
-        if (kvalid == MM_KC) {
-            // full chunk: 8-step blocks; the first block of chunk 0 starts at k = 1
-            if (kk == 1) {
-#pragma unroll
-                for (int k = 1; k < 8; k++) {
-                    const uint32_t w2 = *reinterpret_cast<const uint32_t *>(ws + k * MM_BM + mloc);
-#pragma unroll
-                    for (int i = 0; i < MM_TM; i++) {
-                        const uint32_t w = (w2 >> (16 * i)) & 0xFFFFu;
-#pragma unroll
-                        for (int j = 0; j < MM_TN; j++) {
-                            acc[i][j] = R.add(acc[i][j], mul16(w, xs[(tx + 16 * j) * MM_XPITCH + k]), st[i][j]);
-                        }
-                    }
-                }
-                kk = 8;
-            }
-            for (; kk < MM_KC; kk += 8) {
-                uint4 xv[MM_TN];
-#pragma unroll
-                for (int j = 0; j < MM_TN; j++) xv[j] = *reinterpret_cast<const uint4 *>(xs + (tx + 16 * j) * MM_XPITCH + kk);
-#pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    const uint32_t w2 = *reinterpret_cast<const uint32_t *>(ws + (kk + u) * MM_BM + mloc);
-#pragma unroll
-                    for (int i = 0; i < MM_TM; i++) {
-                        const uint32_t w = (w2 >> (16 * i)) & 0xFFFFu;
-#pragma unroll
-                        for (int j = 0; j < MM_TN; j++) {
-                            const uint32_t word = u < 2 ? xv[j].x : u < 4 ? xv[j].y : u < 6 ? xv[j].z : xv[j].w;
-                            const uint32_t x = (word >> (16 * (u & 1))) & 0xFFFFu;
-                            acc[i][j] = R.add(acc[i][j], mul16(w, x), st[i][j]);
-                        }
-                    }
-                }
-            }
-        } else {
-            for (; kk < kvalid; kk++) {
-                const uint32_t w2 = *reinterpret_cast<const uint32_t *>(ws + kk * MM_BM + mloc);
-#pragma unroll
-                for (int i = 0; i < MM_TM; i++) {
-                    const uint32_t w = (w2 >> (16 * i)) & 0xFFFFu;
-#pragma unroll
-                    for (int j = 0; j < MM_TN; j++) {
-                        acc[i][j] = R.add(acc[i][j], mul16(w, xs[(tx + 16 * j) * MM_XPITCH + kk]), st[i][j]);
-                    }
-                }
-            }
-        }
-        __syncthreads();
-    }
-
-#pragma unroll
-    for (int i = 0; i < MM_TM; i++) {
-        const int64_t m = m0 + mloc + i;
-        if (m >= M) continue;
-#pragma unroll
-        for (int j = 0; j < MM_TN; j++) {
-            const int64_t n = n0 + tx + 16 * j;
-            if (n >= N) continue;
-            const uint32_t v = K == 0 ? 0u : R.finish(acc[i][j]);
-            const int64_t o = (z * N + n) * M + m;
-            if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
-            else                   static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
-        }
-    }
-}
 
 // ===================== MUL_MAT (xlns16, base mode, key form) ================
 //
@@ -826,19 +641,35 @@ constexpr int A32_THREADS = 512;
 // threads per CTA: 32 warps per SM where the per-warp rings fit beside the
 // table (xlns16), else 16
 __host__ __device__ constexpr int a32_threads(int fmt, bool ring) { return fmt == 16 && ring ? 1024 : A32_THREADS; }
-constexpr int A32_SMEM    = k32f_words * 4;
 #ifndef LNSB_A32_TN2_MIN_UNITS
 #define LNSB_A32_TN2_MIN_UNITS 2     // two tokens per lane once each warp gets this many units
 #endif
+
+// Accumulation policy of the kernel: the flat xlns32 addition (xlns32, and
+// xlns16 in sum32 mode), LPVIP (xlns16 lpvip: acc32 = add32_lpvip(acc32,
+// t << 16), truncated to 16 bits at the end) or Monte-by-LPVIP (xlns16 monte
+// with GGML_LNS16_MONTE_BYLPVIP: a 16-bit accumulator, each addition
+// add32_lpvip(acc << 16, (t << 16) | next LFSR state) >> 16;
+// lns-backend/src/lns-ops.cpp:93-97).
+enum : int { A32_FLAT = 0, A32_LPVIP = 1, A32_MBL = 2 };
+template <int FMT> __host__ __device__ constexpr int a32_kind() {
+    return FMT == 32 || k_mode == M_SUM32 ? A32_FLAT : (k_mode == M_LPVIP ? A32_LPVIP : A32_MBL);
+}
 
 template <int FMT> struct a32_fmt;
 template <> struct a32_fmt<16> {
     using elem = uint16_t;
     static constexpr int xvec = 1;    // uint4 per 8 values
-    __device__ static __forceinline__ uint32_t term(uint32_t w, uint32_t x) { return mul16(w, x) << 16; }
+    __device__ static __forceinline__ uint32_t term(uint32_t w, uint32_t x) {
+        return a32_kind<16>() == A32_MBL ? mul16(w, x) : mul16(w, x) << 16;
+    }
     __device__ static __forceinline__ uint32_t finish(uint32_t acc) {
-        if ((acc & 0x7FFFFFFFu) >= 0x7FFF8000u) return ((acc >> 16) | 0x7FFFu) & 0xFFFFu;
-        return (acc + 0x8000u) >> 16;
+        if constexpr (a32_kind<16>() == A32_FLAT) {
+            if ((acc & 0x7FFFFFFFu) >= 0x7FFF8000u) return ((acc >> 16) | 0x7FFFu) & 0xFFFFu;
+            return (acc + 0x8000u) >> 16;
+        }
+        if constexpr (a32_kind<16>() == A32_LPVIP) return acc >> 16;
+        return acc;
     }
     __device__ static __forceinline__ void store(const dev_tables & T, void * dst, int64_t o, uint32_t v, bool f32) {
         if (f32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
@@ -895,48 +726,69 @@ __device__ __forceinline__ void a32_load(a32_chunk<FMT, TN> & c, const typename 
 }
 
 // One step of every chain of a lane: the main parts first (independent, so
-// they interleave), then a single branch for the chains that need the fix.
+// they interleave), then a branch per chain for the lanes on the rare path.
+// F: the flat image (A32_FLAT); LP: the LPVIP singular-branch table; st: the
+// chains' LFSR states (A32_MBL).
 template <int FMT, int TN>
-__device__ __forceinline__ void a32_step_x(const int32_t * F, uint32_t (&acc)[TN], uint32_t w, const uint32_t (&x)[TN]) {
+__device__ __forceinline__ void a32_step_x(const int32_t * F, const int32_t * LP, uint32_t (&acc)[TN],
+                                           uint32_t (&st)[TN], uint32_t w, const uint32_t (&x)[TN]) {
     using OP = a32_fmt<FMT>;
-    uint32_t    b[TN];
-    add32f_part o[TN];
+    if constexpr (a32_kind<FMT>() == A32_FLAT) {
+        uint32_t    b[TN];
+        add32f_part o[TN];
 #pragma unroll
-    for (int t = 0; t < TN; t++) {
-        b[t] = OP::term(w, x[t]);
-        o[t] = add32f_main(F, acc[t], b[t]);
+        for (int t = 0; t < TN; t++) {
+            b[t] = OP::term(w, x[t]);
+            o[t] = add32f_main(F, acc[t], b[t]);
+        }
+#pragma unroll
+        for (int t = 0; t < TN; t++) acc[t] = o[t].cot ? add32f_cot(F, o[t].mx, o[t].d) : o[t].r;
+    } else {
+        lpvip_part o[TN];
+#pragma unroll
+        for (int t = 0; t < TN; t++) {
+            if constexpr (a32_kind<FMT>() == A32_MBL) {
+                st[t] = lfsr_step(st[t]);
+                o[t]  = lpvip_main(acc[t] << 16, (OP::term(w, x[t]) << 16) | st[t]);
+            } else {
+                o[t] = lpvip_main(acc[t], OP::term(w, x[t]));
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < TN; t++) {
+            const uint32_t r = o[t].sing ? lpvip_sing(LP, o[t].mx, o[t].d) : o[t].r;
+            acc[t] = a32_kind<FMT>() == A32_MBL ? r >> 16 : r;
+        }
     }
-#pragma unroll
-    for (int t = 0; t < TN; t++) acc[t] = o[t].cot ? add32f_cot(F, o[t].mx, o[t].d) : o[t].r;
 }
 template <int FMT, int TN>
-__device__ __forceinline__ void a32_step(const int32_t * F, uint32_t (&acc)[TN], uint32_t w, const a32_chunk<FMT, TN> & c,
-                                         int j) {
+__device__ __forceinline__ void a32_step(const int32_t * F, const int32_t * LP, uint32_t (&acc)[TN], uint32_t (&st)[TN],
+                                         uint32_t w, const a32_chunk<FMT, TN> & c, int j) {
     uint32_t x[TN];
 #pragma unroll
     for (int t = 0; t < TN; t++) x[t] = c.xv(t, j);
-    a32_step_x<FMT, TN>(F, acc, w, x);
+    a32_step_x<FMT, TN>(F, LP, acc, st, w, x);
 }
 
 // The steps of one 8-step chunk: j in [j0, kv) (kv < 8 only in the last chunk).
 template <int FMT, int TN>
-__device__ __forceinline__ void a32_steps(const int32_t * F, const a32_chunk<FMT, TN> & c, uint32_t (&acc)[TN],
-                                          bool first, int64_t kv) {
+__device__ __forceinline__ void a32_steps(const int32_t * F, const int32_t * LP, const a32_chunk<FMT, TN> & c,
+                                          uint32_t (&acc)[TN], uint32_t (&st)[TN], bool first, int64_t kv) {
     using OP = a32_fmt<FMT>;
     if (first) {
 #pragma unroll
         for (int t = 0; t < TN; t++) acc[t] = OP::term(c.w[0], c.xv(t, 0));
 #pragma unroll
         for (int j = 1; j < 8; j++) {
-            if (j < kv) a32_step<FMT, TN>(F, acc, c.w[j], c, j);
+            if (j < kv) a32_step<FMT, TN>(F, LP, acc, st, c.w[j], c, j);
         }
     } else if (kv >= 8) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) a32_step<FMT, TN>(F, acc, c.w[j], c, j);
+        for (int j = 0; j < 8; j++) a32_step<FMT, TN>(F, LP, acc, st, c.w[j], c, j);
     } else {
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            if (j < kv) a32_step<FMT, TN>(F, acc, c.w[j], c, j);
+            if (j < kv) a32_step<FMT, TN>(F, LP, acc, st, c.w[j], c, j);
         }
     }
 }
@@ -954,7 +806,8 @@ struct a32_ring {
     static constexpr int wbytes = 8 * 32 * es;
     static constexpr int stage  = wbytes + TN * 8 * es;
     static constexpr int warp_bytes = A32_STAGES * stage;
-    static constexpr int smem   = k32f_words * 4 + (a32_threads(FMT, true) / 32) * warp_bytes;
+    static constexpr int table  = a32_kind<FMT>() == A32_FLAT ? k32f_words * 4 : 0;   // flat image bytes
+    static constexpr int smem   = table + (a32_threads(FMT, true) / 32) * warp_bytes;
 
     // issue chunk k0 of the row block starting at row m0 (wb: the slice's k-major weights)
     __device__ static __forceinline__ void issue(unsigned char * st, const E * __restrict__ wb, const E * const (&xt)[TN],
@@ -994,18 +847,23 @@ template <int FMT, int TN, bool OUT_F32, bool RING>
 __global__ void __launch_bounds__(a32_threads(FMT, RING), 1)
 k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
               const typename a32_fmt<FMT>::elem * __restrict__ X, void * __restrict__ dst, int64_t K, int64_t M,
-              int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3, int64_t nz, int vecx) {
+              int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3, int64_t nz, uint32_t monte_seed,
+              int vecx) {
     using E  = typename a32_fmt<FMT>::elem;
     using OP = a32_fmt<FMT>;
     using RG = a32_ring<FMT, TN>;
+    constexpr int KIND = a32_kind<FMT>();
     extern __shared__ __align__(16) int32_t F[];
     constexpr int NT = a32_threads(FMT, RING);
-    for (int i = threadIdx.x; i < k32f_words / 4; i += NT)
-        reinterpret_cast<int4 *>(F)[i] = __ldg(reinterpret_cast<const int4 *>(T.flat32) + i);
-    __syncthreads();
+    if constexpr (KIND == A32_FLAT) {
+        for (int i = threadIdx.x; i < k32f_words / 4; i += NT)
+            reinterpret_cast<int4 *>(F)[i] = __ldg(reinterpret_cast<const int4 *>(T.flat32) + i);
+        __syncthreads();
+    }
+    const int32_t * LP = T.lpvip_db;
 
     const int     lane = threadIdx.x & 31;
-    unsigned char * ring = reinterpret_cast<unsigned char *>(F) + k32f_words * 4 + (threadIdx.x >> 5) * RG::warp_bytes;
+    unsigned char * ring = reinterpret_cast<unsigned char *>(F) + RG::table + (threadIdx.x >> 5) * RG::warp_bytes;
     const int64_t RB = (M + 31) / 32, TG = (N + TN - 1) / TN;
     const int64_t units  = nz * RB * TG;
     const int64_t nwarps = (int64_t) gridDim.x * (NT / 32);
@@ -1022,9 +880,20 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
             const int64_t n = tg * TN + t;
             xt[t] = X + (z * N + (n < N ? n : N - 1)) * K;
         }
-        uint32_t acc[TN];
+        uint32_t acc[TN], st[TN];
 #pragma unroll
-        for (int t = 0; t < TN; t++) acc[t] = 0;
+        for (int t = 0; t < TN; t++) {
+            acc[t] = 0;
+            st[t]  = 0;
+            if constexpr (KIND == A32_MBL) {
+                // the chain of output (z, m, n) starts (its index in the CPU's loop
+                // order z, m, n) * (K - 1) draws after the seed
+                const int64_t mm = m < M ? m : M - 1, nn = imin64(tg * TN + t, N - 1);
+                const unsigned long long out = ((unsigned long long) z * (unsigned long long) M + (unsigned long long) mm) *
+                                               (unsigned long long) N + (unsigned long long) nn;
+                if (K > 1) st[t] = lfsr_jump(T, monte_seed, out * (unsigned long long) (K - 1));
+            }
+        }
         if (K > 0) {
             a32_chunk<FMT, TN> cur;
             if constexpr (RING) {
@@ -1039,14 +908,14 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
                     const int64_t nx = c + A32_STAGES - 1;   // refills the stage chunk c - 1 used
                     if (nx < nchunks) RG::issue(ring + (int) (nx % A32_STAGES) * RG::stage, wb, xt, m0, nx * 8, K, M, lane);
                     cp_async_commit();
-                    const unsigned char * st = ring + (int) (c % A32_STAGES) * RG::stage;
+                    const unsigned char * sg = ring + (int) (c % A32_STAGES) * RG::stage;
                     if (lat) {                           // few units: all 8 steps unrolled, operands in registers
-                        RG::read(cur, st, lane);
-                        a32_steps<FMT, TN>(F, cur, acc, c == 0, K - c * 8);
+                        RG::read(cur, sg, lane);
+                        a32_steps<FMT, TN>(F, LP, cur, acc, st, c == 0, K - c * 8);
                         continue;
                     }
-                    const E * ws = reinterpret_cast<const E *>(st) + lane;
-                    const E * xs = reinterpret_cast<const E *>(st + RG::wbytes);
+                    const E * ws = reinterpret_cast<const E *>(sg) + lane;
+                    const E * xs = reinterpret_cast<const E *>(sg + RG::wbytes);
                     int j = 0;
                     if (c == 0) {
 #pragma unroll
@@ -1059,7 +928,7 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
                         uint32_t x[TN];
 #pragma unroll
                         for (int t = 0; t < TN; t++) x[t] = xs[t * 8 + j];
-                        a32_step_x<FMT, TN>(F, acc, ws[j * 32], x);
+                        a32_step_x<FMT, TN>(F, LP, acc, st, ws[j * 32], x);
                     }
                 }
                 cp_async_wait<0>();
@@ -1070,7 +939,7 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
                 a32_load<FMT, TN>(cur, wl, xt, 0, K, M, vecx != 0);
                 for (int64_t c = 0; c < nchunks; c++) {
                     if (c + 1 < nchunks) a32_load<FMT, TN>(nxt, wl, xt, (c + 1) * 8, K, M, vecx != 0);
-                    a32_steps<FMT, TN>(F, cur, acc, c == 0, K - c * 8);
+                    a32_steps<FMT, TN>(F, LP, cur, acc, st, c == 0, K - c * 8);
                     cur = nxt;
                 }
             }
@@ -1288,7 +1157,7 @@ int launch_a32(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, in
                int dev, bool vecx, cudaStream_t stream) {
     static bool attr[k_max_devices] = {};
     auto kern = k_mul_mat_a32<FMT, TN, OUT_F32, RING>;
-    constexpr int smem = RING ? a32_ring<FMT, TN>::smem : A32_SMEM;
+    constexpr int smem = RING ? a32_ring<FMT, TN>::smem : a32_ring<FMT, TN>::table;
     if (!attr[dev]) {
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return (int) e;
@@ -1298,7 +1167,7 @@ int launch_a32(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, in
     const int64_t grid = units < sm_count(dev) ? units : sm_count(dev);
     kern<<<(unsigned) grid, a32_threads(FMT, RING), smem, stream>>>(T, static_cast<const E *>(a->w), static_cast<const E *>(a->x),
                                                        dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3,
-                                                       a->ne12 * a->ne13, vecx ? 1 : 0);
+                                                       a->ne12 * a->ne13, a->monte_seed, vecx ? 1 : 0);
     return launch_status();
 }
 
@@ -1382,27 +1251,10 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         kern<<<grid, FB_THREADS, FB_SMEM, stream>>>(*T, static_cast<const uint16_t *>(a->w),
                                                     static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
                                                     a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0);
-    } else if (fmt == LNSB_XLNS32 || k_mode == M_SUM32) {
+    } else if (fmt == LNSB_XLNS32 || k_mode == M_SUM32 || k_mode == M_LPVIP || k_mode == M_MONTE_BYLPVIP) {
         return mul_mat_a32(fmt, *T, a, dst, out_f32, r2, r3, stream);
     } else {
-        const int64_t gx = (a->M + MM_BM - 1) / MM_BM, gy = (a->N + MM_BN - 1) / MM_BN;
-        if (gx > 0x7FFFFFFF || gy > 65535) return LNSB_E_TOO_LARGE;
-        const dim3 grid((unsigned) gx, (unsigned) gy, (unsigned) (a->ne12 * a->ne13));
-        const bool vec = a->M % 8 == 0 && a->K % 8 == 0 && ((uintptr_t) a->w % 16) == 0 && ((uintptr_t) a->x % 16) == 0 &&
-                         a->M % MM_BM == 0;
-        static bool attr_set[k_max_devices][2] = {};
-        auto kern = out_f32 ? k_mul_mat16<true> : k_mul_mat16<false>;
-        int dev = 0;
-        const int ds = current_device(&dev);
-        if (ds != 0) return ds;
-        if (!attr_set[dev][out_f32]) {
-            const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MM_SMEM);
-            if (e != cudaSuccess) return (int) e;
-            attr_set[dev][out_f32] = true;
-        }
-        kern<<<grid, MM_THREADS, MM_SMEM, stream>>>(*T, static_cast<const uint16_t *>(a->w),
-                                                    static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
-                                                    a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0);
+        return LNSB_E_UNSUPPORTED;
     }
     return launch_status();
 }
