@@ -71,13 +71,21 @@ def peaks():
         return 6650.0, 1965.0, "fallback"
 
 
-# ncu capture summary of the kernel each workload runs (DRAM bytes of one launch)
-PROFILE = {"configs1": "profiles/k_mul_mat16_fast_configs1.md", "configs0": "profiles/k_mul_mat16_lat_configs0.md"}
+# ncu capture summary of the kernel each (workload, mode) runs (DRAM bytes of one launch)
+PROFILE = {
+    ("configs1", "base"): "profiles/k_mul_mat16_fast_configs1.md",
+    ("configs0", "base"): "profiles/k_mul_mat16_lat_configs0.md",
+    ("configs1", "monte"): "profiles/k_mul_mat16_fast_monte_configs1.md",
+    ("configs1", "sum32"): "profiles/k_mul_mat_a32_sum32_configs1.md",
+    ("configs1", "lpvip"): "profiles/k_mul_mat_a32_lpvip_configs1.md",
+    ("configs1", "monte_bylpvip"): "profiles/k_mul_mat_a32_monte_bylpvip_configs1.md",
+    ("configs4:4096:16", "sum32"): "profiles/k_mul_mat_a32_sum32_configs4_K4096_N16.md",
+}
 
 
-def traffic_of(workload):
+def traffic_of(key):
     try:
-        with open(os.path.join(ROOT, PROFILE[workload])) as f:
+        with open(os.path.join(ROOT, PROFILE[key])) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_launch:"):
                     return int(line.split(":")[1])
@@ -324,6 +332,8 @@ def run_ours(args, wl):
         dist.barrier()
 
     adds = adds_of(K, M, N)
+    wkey = "configs4:%d:%d" % (K, N) if strong else args.workload
+    pkey = (wkey, args.mode) if world == 1 or not strong else None   # the captured launch is this rank's launch
     value = adds * world * args.steps / (step_ms / 1000) / 1e9
     e2e_val = adds * world * args.steps / (e2e_ms / 1000) / 1e9
     scaling = "strong" if strong else "weak"
@@ -342,8 +352,7 @@ def run_ours(args, wl):
                    "K": K, "M": M, "N": N, "mode": args.mode, "parallelism": "rowshard%d" % world,
                    "l2": "flushed (256 MB write) before every timed step"},
         "roofline": {"bound": "int", "achieved": achieved, "peak": int_peak, "unit": UNIT, "frac": achieved / int_peak,
-                     "traffic": traffic_of(args.workload) if args.mode == "base" else None,
-                     "traffic_source": PROFILE.get(args.workload) if args.mode == "base" else None,
+                     "traffic": traffic_of(pkey), "traffic_source": PROFILE.get(pkey),
                      "c_mode": c, "sm_mhz_used": f_mhz,
                      "note": "integer-issue bound: %d SMs x %d lanes x f_sm / c_mode (%s SM clock)" % (SMS, LANES_PER_SM, "sampled" if clocks.get("sm_mhz") else src),
                      "hbm": {"achieved_gbs": bytes_alg / kern_s / 1e9, "peak_gbs": hbm, "frac": bytes_alg / kern_s / 1e9 / hbm,
