@@ -156,6 +156,25 @@ def test_mul_mat16_range_fallback(orc, ks16, where, M, K, N):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("K,M,N", [(1536, 96, 8), (700, 64, 3)])
+def test_mul_mat16_zeros_scattered(orc, ks16, K, M, N):
+    """Zero weights and activations scattered along K (pruned weights, padded
+    activations): chains drop to packed codes around each zero and return to
+    the key form where the operands allow, several times per chain."""
+    rng = np.random.default_rng(K + N)
+    w = codes16(orc, rng, (M, K), 0.02)
+    x = codes16(orc, rng, (N, K), 1.0)
+    for k in (3, 300, 555, 1000, 1290):
+        if k < K:
+            w[rng.integers(0, M, 4), k] = 0x0000
+    for k in (40, 520, 1400):
+        if k < K:
+            x[rng.integers(0, N), k] = rng.choice(np.array([0x0000, 0x8000], np.uint16))
+    want = orc.mul_mat16(ks16.mode, w, x, seed=11, nthreads=NT).ravel()
+    got = run_mm16(ks16, w, x, seed=11)
+    assert np.array_equal(got, want)
+
+
 def test_draw_accounting(ks16, orc):
     for args in [(1536, 576, 8, 1, 1), (1, 4, 4, 1, 1), (0, 4, 4, 1, 1), (10, 3, 5, 4, 2)]:
         K, M, N, ne12, ne13 = args

@@ -30,6 +30,7 @@ struct dev_tables {
     const int16_t *  monte16;    // 2 * k16_monte_n
     const int32_t *  key16;      // k16_key_bytes / 4
     const int32_t *  mkey16;     // k16m_key_bytes / 4
+    const int32_t *  key16s;     // k16s_bytes / 4
     const int32_t *  sb32;
     const int32_t *  db32;
     const int32_t *  db32_hi;    // 2048

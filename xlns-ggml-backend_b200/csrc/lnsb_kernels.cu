@@ -475,13 +475,14 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 // steps overlap; a chunk that fails the check runs on packed codes.
 constexpr int LT_ROWS = 128, LT_KC = 128;
 constexpr int LT_KM   = k16_key_max;                              // 20500
-constexpr int LT_TABS = (2 * LT_KM + 4 + 15) / 16 * 16;           // signed table bytes
+constexpr int LT_TABS = k16s_bytes;                               // signed table bytes
 constexpr int LT_OFF_TAB2 = LT_TABS;
 constexpr int LT_OFF_W    = LT_OFF_TAB2 + MM_TABPAD;              // 2 stages of W codes
 constexpr int LT_WSTAGE   = LT_KC * LT_ROWS;                      // halfwords
 constexpr int LT_OFF_X    = LT_OFF_W + 2 * LT_WSTAGE * 2;         // x keys (K words) then x codes (K halfwords)
-constexpr int LT_MAX_K    = 16384;
-inline int lt_smem(int64_t K) { return LT_OFF_X + (int) K * 6 + 16; }
+constexpr int LT_MAX_K    = 16384;                               // one token per thread
+constexpr int LT_MAX_K2   = 8192;                                // two tokens per thread
+inline int lt_smem(int64_t K, int tn) { return LT_OFF_X + (int) ((K + 3) & ~3) * 6 * tn + 16; }
 
 __device__ __forceinline__ void lt_stage(uint16_t * ws, const uint16_t * __restrict__ W, int64_t K, int64_t M,
                                          int64_t m0, int64_t k0, bool vec) {
@@ -504,7 +505,19 @@ __device__ __forceinline__ void lt_stage(uint16_t * ws, const uint16_t * __restr
     }
 }
 
-template <bool OUT_F32>
+// the signed key table at shared offset 0 and the packed table at LT_OFF_TAB2,
+// as 16-byte asynchronous copies (the caller commits and waits)
+__device__ __forceinline__ void lt_tables_async(const dev_tables & T, unsigned char * smem) {
+    for (int i = threadIdx.x; i < LT_TABS / 16; i += blockDim.x)
+        cp_async16(smem + i * 16, reinterpret_cast<const unsigned char *>(T.key16s) + i * 16);
+    for (int i = threadIdx.x; i < MM_TABPAD / 16; i += blockDim.x)
+        cp_async16(smem + LT_OFF_TAB2 + i * 16, reinterpret_cast<const unsigned char *>(T.sbdb16) + i * 16);
+}
+
+// TN tokens per thread (1 or 2): a thread runs the chains of its weight row
+// against TN tokens, sharing the weight load and key conversion, and the TN
+// independent chains interleave, hiding the dependent path of each.
+template <bool OUT_F32, int TN>
 __global__ void __launch_bounds__(LT_ROWS)
 k_mul_mat16_lat(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
                 void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
@@ -512,32 +525,32 @@ k_mul_mat16_lat(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * 
     extern __shared__ __align__(16) unsigned char smem[];
     int16_t *  tab2  = reinterpret_cast<int16_t *>(smem + LT_OFF_TAB2);
     uint16_t * wst   = reinterpret_cast<uint16_t *>(smem + LT_OFF_W);
-    int *      xkeys = reinterpret_cast<int *>(smem + LT_OFF_X);
-    uint16_t * xcod  = reinterpret_cast<uint16_t *>(smem + LT_OFF_X + K * 4);
+    const int KP = (int) ((K + 3) & ~3);                // token row pitch: 16-byte aligned rows (K <= LT_MAX_K)
+    int *      xkeys = reinterpret_cast<int *>(smem + LT_OFF_X);                  // [TN][KP]
+    uint16_t * xcod  = reinterpret_cast<uint16_t *>(smem + LT_OFF_X + TN * KP * 4); // [TN][KP]
     __shared__ int red[LT_ROWS / 32][4];
 
-    // signed table: entry for difference D (a multiple of 4) at byte LT_KM + D
-    for (int i = threadIdx.x; i < LT_TABS / 4; i += LT_ROWS) {
-        const int d = i * 4 - LT_KM;
-        const int ad = d < 0 ? -d : d;
-        reinterpret_cast<int *>(smem)[i] = ad <= k16_key_max ? T.key16[ad / 4] : 0;
-    }
-    for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += LT_ROWS) tab2[i] = T.sbdb16[i];
+    lt_tables_async(T, smem);                           // signed key table, packed table
+    cp_async_commit();
 
     const int64_t z = blockIdx.z, i12 = z % ne12, i13 = z / ne12;
-    const int64_t n = blockIdx.y;
+    const int64_t n0 = (int64_t) blockIdx.y * TN;
     const int64_t m0 = (int64_t) blockIdx.x * LT_ROWS;
     const int64_t m = m0 + threadIdx.x;
     const int warp = threadIdx.x >> 5;
     const uint16_t * Wz = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
-    const uint16_t * xr = X + (z * N + n) * K;
     int xmin = 0x7FFF, xmax = 0;
-    for (int64_t k = threadIdx.x; k < K; k += LT_ROWS) {
-        const uint32_t c = xr[k];
-        xcod[k]  = (uint16_t) c;
-        xkeys[k] = key_of_code_x(c);
-        xmin = min(xmin, (int) (c & 0x7FFFu));
-        xmax = max(xmax, (int) (c & 0x7FFFu));
+#pragma unroll
+    for (int t = 0; t < TN; t++) {
+        const bool tok = n0 + t < N;                    // a missing token runs on 1.0 and is not stored
+        const uint16_t * xr = X + (z * N + (tok ? n0 + t : N - 1)) * K;
+        for (int64_t k = threadIdx.x; k < K; k += LT_ROWS) {
+            const uint32_t c = tok ? xr[k] : 0x4000u;
+            xcod[t * KP + k]  = (uint16_t) c;
+            xkeys[t * KP + k] = key_of_code_x(c);
+            xmin = min(xmin, (int) (c & 0x7FFFu));
+            xmax = max(xmax, (int) (c & 0x7FFFu));
+        }
     }
     xmin = __reduce_min_sync(0xFFFFFFFFu, xmin);
     xmax = __reduce_max_sync(0xFFFFFFFFu, xmax);
@@ -551,7 +564,9 @@ k_mul_mat16_lat(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * 
         lt_stage(wst, Wz, K, M, m0, 0, vec != 0);
         cp_async_commit();
     }
-    int a = 0;                                          // accumulator key
+    int a[TN];                                          // accumulator keys
+#pragma unroll
+    for (int t = 0; t < TN; t++) a[t] = 0;
     for (int c = 0; c < nchunks; c++) {
         const uint16_t * ws = wst + (c & 1) * LT_WSTAGE;
         if (c + 1 < nchunks) {
@@ -562,8 +577,11 @@ k_mul_mat16_lat(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * 
             cp_async_wait<0>();
         }
         __syncthreads();
-        const int64_t kb = (int64_t) c * LT_KC;
+        const int kb = c * LT_KC;
         const int kvalid = (int) imin64(LT_KC, K - kb);
+        const int * xkc[TN];                            // this chunk's token keys
+#pragma unroll
+        for (int t = 0; t < TN; t++) xkc[t] = xkeys + t * KP + kb;
         // block-wide range check of this chunk (see k_mul_mat16_fast): 16x2
         // SIMD min/max over the staged codes (columns past M hold 1.0)
         unsigned vmin = 0x7FFF7FFFu, vmax = 0u;
@@ -578,7 +596,11 @@ k_mul_mat16_lat(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * 
             }
         }
         int wmin = (int) min(vmin & 0xFFFFu, vmin >> 16), wmax = (int) max(vmax & 0xFFFFu, vmax >> 16);
-        int amax = c > 0 ? (a >> 4) : 0;
+        int amax = 0;
+        if (c > 0) {
+#pragma unroll
+            for (int t = 0; t < TN; t++) amax = max(amax, a[t] >> 4);
+        }
         wmin = __reduce_min_sync(0xFFFFFFFFu, wmin);
         wmax = __reduce_max_sync(0xFFFFFFFFu, wmax);
         amax = __reduce_max_sync(0xFFFFFFFFu, m < M ? amax : 0);
@@ -592,28 +614,228 @@ k_mul_mat16_lat(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * 
 
         int k = 0;
         if (fast) {
+            // one dependent step of chain t with product key p
+            auto step = [&](int t, int p) {
+                const int d   = max(__viaddmin_s32(a[t], -p, LT_KM), -LT_KM);
+                const int adj = *reinterpret_cast<const int *>(smem + LT_KM + d);
+                a[t] = __viaddmax_s32(max(a[t], p), adj, 0);
+            };
             if (c == 0) {
-                a = key_of_product(key_of_code_w(ws[threadIdx.x]), xkeys[0]);
-                k = 1;
+                const int wk = key_of_code_w(ws[threadIdx.x]);
+#pragma unroll
+                for (int t = 0; t < TN; t++) a[t] = key_of_product(wk, xkc[t][0]);
+                for (k = 1; k < 8 && k < kvalid; k++) {
+                    const int wk2 = key_of_code_w(ws[k * LT_ROWS + threadIdx.x]);
+#pragma unroll
+                    for (int t = 0; t < TN; t++) step(t, key_of_product(wk2, xkc[t][k]));
+                }
             }
-#pragma unroll 8
+            // blocks of 8 steps with constant trip counts: the 8 products are
+            // formed first, so the dependent chain runs without operand waits
+            for (; k + 8 <= kvalid; k += 8) {
+                int wk8[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) wk8[u] = key_of_code_w(ws[(k + u) * LT_ROWS + threadIdx.x]);
+#pragma unroll
+                for (int t = 0; t < TN; t++) {
+                    const int4 x0 = *reinterpret_cast<const int4 *>(xkc[t] + k);
+                    const int4 x1 = *reinterpret_cast<const int4 *>(xkc[t] + k + 4);
+                    const int xk8[8] = { x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w };
+                    int p8[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) p8[u] = key_of_product(wk8[u], xk8[u]);
+#pragma unroll
+                    for (int u = 0; u < 8; u++) step(t, p8[u]);
+                }
+            }
             for (; k < kvalid; k++) {
-                const int p   = key_of_product(key_of_code_w(ws[k * LT_ROWS + threadIdx.x]), xkeys[kb + k]);
-                const int t   = max(__viaddmin_s32(a, -p, LT_KM), -LT_KM);
-                const int adj = *reinterpret_cast<const int *>(smem + LT_KM + t);
-                a = __viaddmax_s32(max(a, p), adj, 0);
+                const int wk = key_of_code_w(ws[k * LT_ROWS + threadIdx.x]);
+#pragma unroll
+                for (int t = 0; t < TN; t++) step(t, key_of_product(wk, xkc[t][k]));
             }
         } else {
-            uint32_t ac = c == 0 ? mul16(ws[threadIdx.x], xcod[0]) : code_of_key(a);
-            if (c == 0) k = 1;
-            for (; k < kvalid; k++) ac = add16(ac, mul16(ws[k * LT_ROWS + threadIdx.x], xcod[kb + k]), tab2);
-            a = key_of_code(ac);
+#pragma unroll
+            for (int t = 0; t < TN; t++) {
+                uint32_t ac = c == 0 ? mul16(ws[threadIdx.x], xcod[t * KP]) : code_of_key(a[t]);
+                for (int kk = c == 0 ? 1 : 0; kk < kvalid; kk++)
+                    ac = add16(ac, mul16(ws[kk * LT_ROWS + threadIdx.x], xcod[t * KP + kb + kk]), tab2);
+                a[t] = key_of_code(ac);
+            }
         }
         __syncthreads();
     }
     if (m < M) {
-        const uint32_t v = K == 0 ? 0u : code_of_key(a);
-        const int64_t o = (z * N + n) * M + m;
+#pragma unroll
+        for (int t = 0; t < TN; t++) {
+            if (n0 + t >= N) continue;
+            const uint32_t v = K == 0 ? 0u : code_of_key(a[t]);
+            const int64_t o = (z * N + n0 + t) * M + m;
+            if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
+            else                   static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
+        }
+    }
+}
+
+// ======= MUL_MAT (xlns16, base mode, few outputs, weights resident) ==========
+//
+// For K up to a few thousand the whole weight slice of a CTA -- 32 rows x K
+// codes -- fits in shared memory and is staged once, so the chain loop has no
+// block-wide barrier and no chunk staging (which cost k_mul_mat16_lat about a
+// third of its time).  A CTA is 32 rows x TNC tokens: warp w runs the 32
+// chains of token n0 + w, one per lane, in blocks of 8 steps whose products are
+// formed first.  The key form's range check is made per segment of LR_SEG
+// steps from ranges the prologue records (weights per CTA, tokens per warp),
+// each warp deciding for itself: a segment that fails (a zero weight, say)
+// runs on packed codes, and the chain returns to the key form at the next
+// segment that passes -- the bits are the same either way.
+constexpr int LR_OFF_W  = LT_OFF_TAB2 + MM_TABPAD;                // [K][32] codes, then x keys, x codes
+constexpr int LR_SEG    = 256;
+constexpr int LR_MAXSEG = 16;                                     // K <= LR_SEG * LR_MAXSEG
+inline int lr_smem(int64_t K, int tnc) {
+    const int64_t kp = (K + 3) & ~3;
+    return (int) (LR_OFF_W + kp * 64 + kp * 6 * tnc + 16);
+}
+constexpr int LR_SMEM_MAX = 226 * 1024;                          // leaves room for the static shared memory
+
+template <bool OUT_F32>
+__global__ void __launch_bounds__(128)
+k_mul_mat16_res(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
+                void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
+                int64_t r2, int64_t r3, int vec) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int  Ki    = (int) K;
+    const int  KP    = (Ki + 3) & ~3;
+    const int  tnc   = blockDim.x >> 5;
+    const int  nseg  = (Ki + LR_SEG - 1) / LR_SEG;
+    int16_t *  tab2  = reinterpret_cast<int16_t *>(smem + LT_OFF_TAB2);
+    uint16_t * ws    = reinterpret_cast<uint16_t *>(smem + LR_OFF_W);                        // [K][32]
+    int *      xkeys = reinterpret_cast<int *>(smem + LR_OFF_W + KP * 64);                   // [tnc][KP]
+    uint16_t * xcod  = reinterpret_cast<uint16_t *>(smem + LR_OFF_W + KP * 64 + tnc * KP * 4);
+    __shared__ int wseg[LR_MAXSEG][2];                  // weight log range per segment
+    __shared__ int xseg[4][LR_MAXSEG][2];               // token log range per warp and segment
+
+    const int64_t z = blockIdx.z, i12 = z % ne12, i13 = z / ne12;
+    const int64_t m0 = (int64_t) blockIdx.x * 32, n0 = (int64_t) blockIdx.y * tnc;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint16_t * Wz = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
+    // weight slice: row k of the k-major matrix gives 32 consecutive codes (64 bytes)
+    for (int i = threadIdx.x; i < Ki * 4; i += blockDim.x) {
+        const int r = i >> 2, q = i & 3;
+        const int64_t mm = m0 + q * 8;
+        if (vec && mm < M) {
+            cp_async16(ws + r * 32 + q * 8, Wz + (int64_t) r * M + mm);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) ws[r * 32 + q * 8 + e] = mm + e < M ? Wz[(int64_t) r * M + mm + e] : (uint16_t) 0x4000;
+        }
+    }
+    cp_async_commit();
+    lt_tables_async(T, smem);                           // signed key table, packed table
+    cp_async_commit();
+    for (int i = threadIdx.x; i < nseg; i += blockDim.x) { wseg[i][0] = 0x7FFF; wseg[i][1] = 0; }
+    // this warp's token (8 codes per 16-byte load where the row allows), with
+    // its log range per segment
+    const int64_t n = n0 + warp;
+    const bool    tok = n < N;
+    {
+        const uint16_t * xr = X + (z * N + (tok ? n : N - 1)) * K;
+        const bool xv = ((uintptr_t) xr % 16) == 0;
+        for (int sg = 0; sg < nseg; sg++) {
+            int xmin = 0x7FFF, xmax = 0;
+            auto put = [&](int k, uint32_t c) {
+                xcod[warp * KP + k]  = (uint16_t) c;
+                xkeys[warp * KP + k] = key_of_code_x(c);
+                xmin = min(xmin, (int) (c & 0x7FFFu));
+                xmax = max(xmax, (int) (c & 0x7FFFu));
+            };
+            const int k0 = sg * LR_SEG + lane * 8;      // each lane: 8 consecutive codes of the segment
+            if (xv && k0 + 8 <= Ki) {
+                const uint4 q = __ldg(reinterpret_cast<const uint4 *>(xr + k0));
+                const uint32_t wd[4] = { q.x, q.y, q.z, q.w };
+#pragma unroll
+                for (int e = 0; e < 4; e++) { put(k0 + 2 * e, wd[e] & 0xFFFFu); put(k0 + 2 * e + 1, wd[e] >> 16); }
+            } else {
+                for (int k = k0; k < k0 + 8 && k < Ki; k++) put(k, xr[k]);
+            }
+            xmin = __reduce_min_sync(0xFFFFFFFFu, xmin);
+            xmax = __reduce_max_sync(0xFFFFFFFFu, xmax);
+            if (lane == 0) { xseg[warp][sg][0] = xmin; xseg[warp][sg][1] = xmax; }
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    // weight log range per segment (SIMD over pairs of codes; padding rows hold 1.0)
+    for (int sg = 0; sg < nseg; sg++) {
+        unsigned vmin = 0x7FFF7FFFu, vmax = 0u;
+        const int v1 = min(Ki, (sg + 1) * LR_SEG) * 4;
+#pragma unroll 4
+        for (int v = sg * LR_SEG * 4 + threadIdx.x; v < v1; v += blockDim.x) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(ws + v * 8);
+            const unsigned w0 = q.x & 0x7FFF7FFFu, w1 = q.y & 0x7FFF7FFFu, w2 = q.z & 0x7FFF7FFFu, w3 = q.w & 0x7FFF7FFFu;
+            vmin = __vminu2(vmin, __vminu2(__vminu2(w0, w1), __vminu2(w2, w3)));
+            vmax = __vmaxu2(vmax, __vmaxu2(__vmaxu2(w0, w1), __vmaxu2(w2, w3)));
+        }
+        int wmin = (int) min(vmin & 0xFFFFu, vmin >> 16), wmax = (int) max(vmax & 0xFFFFu, vmax >> 16);
+        wmin = __reduce_min_sync(0xFFFFFFFFu, wmin);
+        wmax = __reduce_max_sync(0xFFFFFFFFu, wmax);
+        if (lane == 0) { atomicMin(&wseg[sg][0], wmin); atomicMax(&wseg[sg][1], wmax); }
+    }
+    __syncthreads();                                    // the last block-wide barrier
+    if (!tok) return;
+    uint32_t v = 0;
+    if (Ki > 0) {
+        const int *      xk = xkeys + warp * KP;
+        const uint16_t * xc = xcod + warp * KP;
+        int      a  = 0;                                // key (fast)
+        uint32_t ac = 0;                                // code (slow)
+        bool     fast = true;                           // uniform across the warp
+        auto step = [&](int p) {
+            const int d   = max(__viaddmin_s32(a, -p, LT_KM), -LT_KM);
+            const int adj = *reinterpret_cast<const int *>(smem + LT_KM + d);
+            a = __viaddmax_s32(max(a, p), adj, 0);
+        };
+        for (int sg = 0; sg < nseg; sg++) {
+            const int s0 = sg * LR_SEG, s1 = min(Ki, s0 + LR_SEG);
+            {
+                // exact in key form over this segment: every product >= 2^-120 (so
+                // no sum, whatever the accumulator, falls below 2^-128), and no sum
+                // can reach 2^127 within it (growth_bound).  The switch goes both
+                // ways, so only the segments that fail run on packed codes.
+                const int am = __reduce_max_sync(0xFFFFFFFFu, sg == 0 ? 0 : fast ? (a >> 4) : (int) (ac & 0x7FFFu));
+                const bool ok = wseg[sg][0] + xseg[warp][sg][0] - 0x4000 >= 964 &&
+                                max(am, wseg[sg][1] + xseg[warp][sg][1] - 0x4000) + growth_bound(LR_SEG) <= 0x7FFF;
+                if (sg > 0 && ok != fast) {
+                    if (ok) a = key_of_code(ac);
+                    else    ac = code_of_key(a);
+                }
+                fast = ok;
+            }
+            int k = s0;
+            if (fast) {
+                if (sg == 0) {
+                    a = key_of_product(key_of_code_w(ws[lane]), xk[0]);
+                    for (k = 1; k < 8 && k < s1; k++) step(key_of_product(key_of_code_w(ws[k * 32 + lane]), xk[k]));
+                }
+                for (; k + 8 <= s1; k += 8) {
+                    const int4 x0 = *reinterpret_cast<const int4 *>(xk + k);
+                    const int4 x1 = *reinterpret_cast<const int4 *>(xk + k + 4);
+                    const int xk8[8] = { x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w };
+                    int p8[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) p8[u] = key_of_product(key_of_code_w(ws[(k + u) * 32 + lane]), xk8[u]);
+#pragma unroll
+                    for (int u = 0; u < 8; u++) step(p8[u]);
+                }
+                for (; k < s1; k++) step(key_of_product(key_of_code_w(ws[k * 32 + lane]), xk[k]));
+            } else {
+                if (sg == 0) { ac = mul16(ws[lane], xc[0]); k = 1; }
+                for (; k < s1; k++) ac = add16(ac, mul16(ws[k * 32 + lane], xc[k]), tab2);
+            }
+        }
+        v = fast ? code_of_key(a) : ac;
+    }
+    if (m0 + lane < M) {
+        const int64_t o = (z * N + n) * M + m0 + lane;
         if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
         else                   static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
     }
@@ -1216,20 +1438,50 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
     if (st != 0) return st;
     const int64_t r2 = a->ne12 / a->ne02, r3 = a->ne13 / a->ne03;
     const int64_t tiles = ((a->M + FB_BM - 1) / FB_BM) * ((a->N + FB_BN - 1) / FB_BN) * a->ne12 * a->ne13;
-    if (fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && a->K <= LT_MAX_K && a->N <= 65535) {
-        // few outputs: one chain per thread, latency form
-        const dim3 grid((unsigned) ((a->M + LT_ROWS - 1) / LT_ROWS), (unsigned) a->N, (unsigned) (a->ne12 * a->ne13));
+    int lr_tnc = (int) (a->N < 4 ? a->N : 4);
+    while (lr_tnc > 1 && lr_smem(a->K, lr_tnc) > LR_SMEM_MAX) lr_tnc--;
+    if (fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && lr_smem(a->K, lr_tnc) <= LR_SMEM_MAX &&
+        a->K <= (int64_t) LR_SEG * LR_MAXSEG && (a->N + lr_tnc - 1) / lr_tnc <= 65535) {
+        // few outputs, weight slices resident in shared memory
+        const dim3 grid((unsigned) ((a->M + 31) / 32), (unsigned) ((a->N + lr_tnc - 1) / lr_tnc), (unsigned) (a->ne12 * a->ne13));
         const bool vec = a->M % 8 == 0 && ((uintptr_t) a->w % 16) == 0;
-        const int smem = lt_smem(a->K);
-        auto kern = out_f32 ? k_mul_mat16_lat<true> : k_mul_mat16_lat<false>;
-        static int lattr[k_max_devices][2] = {};
+        const int smem = lr_smem(a->K, lr_tnc);
+        auto kern = out_f32 ? k_mul_mat16_res<true> : k_mul_mat16_res<false>;
+        static int rattr[k_max_devices][2] = {};
         int dev = 0;
         const int ds = current_device(&dev);
         if (ds != 0) return ds;
-        if (lattr[dev][out_f32] < smem) {
+        if (rattr[dev][out_f32] < smem) {
+            const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LR_SMEM_MAX);
+            if (e != cudaSuccess) return (int) e;
+            rattr[dev][out_f32] = LR_SMEM_MAX;
+        }
+        kern<<<grid, 32 * lr_tnc, smem, stream>>>(*T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
+                                                  dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, vec ? 1 : 0);
+    } else if (fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && a->K <= LT_MAX_K && a->N <= 65535) {
+        // few outputs: latency form, two tokens per thread where they fit
+#ifndef LNSB_LT_TN2
+#define LNSB_LT_TN2 1
+#endif
+        // two tokens per thread share the weight work once there are enough CTAs to fill the
+        // GPU (throughput); with few CTAs the single chain's latency is the time, and one
+        // token per thread keeps it shortest
+        const int64_t ctas1 = ((a->M + LT_ROWS - 1) / LT_ROWS) * a->N * a->ne12 * a->ne13;
+        const int tn = LNSB_LT_TN2 && a->N >= 2 && a->K <= LT_MAX_K2 && ctas1 > 2 * 148 ? 2 : 1;
+        const dim3 grid((unsigned) ((a->M + LT_ROWS - 1) / LT_ROWS), (unsigned) ((a->N + tn - 1) / tn),
+                        (unsigned) (a->ne12 * a->ne13));
+        const bool vec = a->M % 8 == 0 && ((uintptr_t) a->w % 16) == 0;
+        const int smem = lt_smem(a->K, tn);
+        auto kern = tn == 2 ? (out_f32 ? k_mul_mat16_lat<true, 2> : k_mul_mat16_lat<false, 2>)
+                            : (out_f32 ? k_mul_mat16_lat<true, 1> : k_mul_mat16_lat<false, 1>);
+        static int lattr[k_max_devices][2][2] = {};
+        int dev = 0;
+        const int ds = current_device(&dev);
+        if (ds != 0) return ds;
+        if (lattr[dev][out_f32][tn - 1] < smem) {
             const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) return (int) e;
-            lattr[dev][out_f32] = smem;
+            lattr[dev][out_f32][tn - 1] = smem;
         }
         kern<<<grid, LT_ROWS, smem, stream>>>(*T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
                                               dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, vec ? 1 : 0);
@@ -1423,6 +1675,7 @@ int lnsb_upload_tables(int fmt) {
         if (e == cudaSuccess) e = upload(H.monte16, &t.monte16);
         if (e == cudaSuccess) e = upload(H.key16, &t.key16);
         if (e == cudaSuccess) e = upload(H.mkey16, &t.mkey16);
+        if (e == cudaSuccess) e = upload(H.key16s, &t.key16s);
         if (e == cudaSuccess) e = upload(H.sb32, &t.sb32);
         if (e == cudaSuccess) e = upload(H.db32, &t.db32);
         if (e == cudaSuccess) e = upload(H.db32_hi, &t.db32_hi);

@@ -40,6 +40,13 @@ void build16(host_tables & t) {
         }
     }
 
+    t.key16s.assign(k16s_bytes / 4, 0);
+    for (int i = 0; i < k16s_bytes / 4; i++) {
+        const int d = i * 4 - k16_key_max, ad = d < 0 ? -d : d;
+        if (ad <= k16_key_max) t.key16s[i] = t.key16[ad / 4];
+    }
+    t.sbdb16.resize((k16_tab_bytes + 15) / 16 * 8, 0);     // padded to 16 bytes for cp.async copies
+
     t.conv16.resize(65536);
     for (uint32_t i = 0; i < 65536; i++) {
         const uint32_t bits = i << 16;

@@ -45,6 +45,11 @@ constexpr int k16_key_max   = 16 * (k16_ess + 1) + 4;          // largest index 
 constexpr int k16_key_bytes = (k16_key_max + 4 + 15) / 16 * 16;  // 20512
 constexpr int k16_key_cancel = -(1 << 30);
 
+// Signed image of key16 for the latency kernels: the 32-bit entry for a key
+// difference D (a multiple of 4, |D| <= k16_key_max) sits at byte
+// k16_key_max + D, so a clamped signed difference indexes it directly.
+constexpr int k16s_bytes = (2 * k16_key_max + 4 + 15) / 16 * 16;   // 41008
+
 // The same key indexing over the Monte fine tables, for the Monte mul_mat fast
 // path: 32-bit entry at byte 16n holds the fine sb(n) (x 256), at bytes 16n -
 // 4 and 16n + 4 the fine db(n) (n >= 1), at byte 4 the cancellation sentinel,
@@ -95,6 +100,7 @@ struct host_tables {
     std::vector<int16_t>  monte16;     // [2 * k16_monte_n]: sb fine, then db fine
     std::vector<int32_t>  key16;       // k16_key_bytes / 4 entries, see k16_key_max
     std::vector<int32_t>  mkey16;      // k16m_key_bytes / 4 entries, see k16m_key_max
+    std::vector<int32_t>  key16s;      // k16s_bytes / 4 entries, see k16s_bytes
     // xlns32
     seg32 sb_seg[2], db_seg[4];
     std::vector<int32_t>  sb32, db32;  // concatenated knots
