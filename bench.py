@@ -74,7 +74,7 @@ def peaks():
 # ncu capture summary of the kernel each (workload, mode) runs (DRAM bytes of one launch)
 PROFILE = {
     ("configs1", "base"): "profiles/k_mul_mat16_fast_configs1.md",
-    ("configs0", "base"): "profiles/k_mul_mat16_lat_configs0.md",
+    ("configs0", "base"): "profiles/k_mul_mat16_res_configs0.md",
     ("configs1", "monte"): "profiles/k_mul_mat16_fast_monte_configs1.md",
     ("configs1", "sum32"): "profiles/k_mul_mat_a32_sum32_configs1.md",
     ("configs1", "lpvip"): "profiles/k_mul_mat_a32_lpvip_configs1.md",
@@ -361,6 +361,9 @@ def run_ours(args, wl):
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
+    if world == 1 and args.workload == "configs1":
+        # BASELINE's metric is quoted at K=1536: configs[0], timed the same way, beside the main line
+        line["k1536"] = time_secondary(lib, lnsb200, torch, np, WORKLOADS["configs0"], args, flush, stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not strong:
         line["cpu_baseline"] = cpu_leg(wl, args.mode, 10.0, os.cpu_count() or 1)
     if rank == 0:
@@ -368,6 +371,42 @@ def run_ours(args, wl):
     if dist:
         dist.destroy_process_group()
     return 0
+
+
+def time_secondary(lib, lnsb200, torch, np, wl, args, flush, stream):
+    """Device-timed steps of another workload through the same C ABI call (inputs
+    resident, L2 flushed before every step), for a sub-object of the JSON line."""
+    K, M, N = wl["K"], wl["M"], wl["N"]
+    ks = lnsb200.KernelSet(16, args.mode)
+    rng = np.random.default_rng(wl["seed"])
+    w_f32 = torch.from_numpy(rng.normal(0, 0.02, (M, K)).astype(np.float32)).cuda()
+    x_f32 = torch.from_numpy(rng.normal(0, 1, (N, K)).astype(np.float32)).cuda()
+    w = torch.empty(K * M, dtype=torch.int16, device="cuda")
+    x = torch.empty(N * K, dtype=torch.int16, device="cuda")
+    ks.to_lns_transposed(w_f32, w, M, K, M)
+    ks.to_lns(x_f32, x)
+    out = torch.empty(N * M, dtype=torch.int16, device="cuda")
+    a = lnsb200.MulMatArgs(w.data_ptr(), x.data_ptr(), None, K, M, N, 1, 1, 1, 1, 7)
+    ap, op, sp = ctypes.byref(a), ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream.cuda_stream)
+    for _ in range(args.warmup):
+        flush.zero_()
+        if lib.lnsb_mul_mat_lns(16, ap, op, sp) != 0:
+            raise RuntimeError("lnsb_mul_mat_lns failed on the K=1536 workload")
+    torch.cuda.synchronize()
+    steps = max(args.steps, 20)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        lib.lnsb_mul_mat_lns(16, ap, op, sp)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(b.elapsed_time(e) for b, e in ev) / steps
+    adds = adds_of(K, M, N)
+    return {"workload": wl["desc"], "mode": args.mode, "steps": steps, "ms_per_step": ms,
+            "value": adds / (ms / 1000) / 1e9, "unit": UNIT,
+            "bound": "chain latency: %d dependent additions per output" % (K - 1),
+            "l2": "flushed (256 MB write) before every timed step"}
 
 
 def main():
