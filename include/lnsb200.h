@@ -158,6 +158,52 @@ int lnsb_rms_norm_lns(int fmt, const void * src, void * dst, int64_t ncols, int6
 /* ---- Monte state: one LFSR per process, seed 7 (ggml-lns.h:13-24).  All
  *      return 0 on success, LNSB_E_UNSUPPORTED outside a monte build;
  *      set_state rejects 0 (absorbing). ---- */
+/* ---- Elementwise ops of the model graph (kernel_set::binary / scale /
+ * unary / glu / rope, lns-cuda-kernels.h:116-138; lns-backend/src/lns-ops.cpp:
+ * 468-599, 786-868, 1199-1281).  F32 in and out, as at every ggml op
+ * boundary: each operand is converted to LNS (lnsb_to_lns's table), the op
+ * runs in LNS, the result is written back as F32.  Contiguous tensors.
+ * Unsupported combinations return LNSB_E_UNSUPPORTED: gelu and tanh (their
+ * xlnscpp definitions are not pinned), and unary/glu in xlns32. */
+#define LNSB_BINARY_ADD 0
+#define LNSB_BINARY_MUL 1
+#define LNSB_BINARY_DIV 2
+#define LNSB_UNARY_SILU 0
+#define LNSB_UNARY_GELU 1
+#define LNSB_UNARY_RELU 2
+#define LNSB_UNARY_TANH 3
+#define LNSB_GLU_SWIGLU 0
+#define LNSB_GLU_GEGLU  1
+
+/* dst = a op b, b repeated to a's shape (ggml_can_repeat(b, a)); ne[0] innermost */
+int lnsb_binary(int fmt, int op, const float * a, const int64_t ane[4], const float * b, const int64_t bne[4],
+                float * dst, lnsb_stream_t stream);
+/* dst = src * s, plus b when b != 0 (ggml_scale_bias) */
+int lnsb_scale(int fmt, const float * src, float * dst, int64_t n, float s, float b, lnsb_stream_t stream);
+/* silu(x) = x / (1 + exp(-x)) in xlns16 arithmetic; relu */
+int lnsb_unary(int fmt, int op, const float * src, float * dst, int64_t n, lnsb_stream_t stream);
+/* dst[r][c] = act(gate[r * gate_stride + c]) * up[r * up_stride + c] */
+int lnsb_glu(int fmt, int op, const float * gate, const float * up, int64_t gate_stride, int64_t up_stride,
+             float * dst, int64_t ncols, int64_t nrows, lnsb_stream_t stream);
+
+/* rope_args, lns-cuda-kernels.h:73-80: rows of shape.ne[0]; row (i1, i2, i3)
+ * has position index i2 and cos_sin[(i2 * n_dims/2 + j) * 2 + {0, 1}] =
+ * (cos, sin) of its pair j, computed by the caller on the host */
+typedef struct {
+    const float * src;
+    lnsb_shape4   shape;
+    const float * cos_sin;
+    int           n_dims;
+    int           neox;        /* pairs (j, j + n_dims/2) instead of (2j, 2j+1) */
+    float *       dst;
+} lnsb_rope_args;
+int lnsb_rope(int fmt, const lnsb_rope_args * args, lnsb_stream_t stream);
+
+/* F16 storage of F32 values (KV caches): IEEE binary16, round to nearest
+ * even, and back (exact).  No LNS involved; not part of kernel_set. */
+int lnsb_f32_to_f16(const float * src, uint16_t * dst, int64_t n, lnsb_stream_t stream);
+int lnsb_f16_to_f32(const uint16_t * src, float * dst, int64_t n, lnsb_stream_t stream);
+
 int lnsb_monte_get_state(uint16_t * state);
 int lnsb_monte_set_state(uint16_t state);
 /* *start = current state, then advance it by `draws` steps (lns-ops.cpp:178-195) */

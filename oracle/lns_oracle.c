@@ -108,12 +108,17 @@ static void build16(void) {
             g_dec16[c] = (float)((c & X16_SIGNMASK) ? -v : v);
         }
     }
-    /* exp through float, as a 65536-entry table (docs/CUDA.md:138-140) */
+    /* exp as a 65536-entry table (docs/CUDA.md:138-140): the log of e^x is
+     * x log2(e), taken to F=7 by floor from the value's float, x =
+     * xlns162fp(c).  Pinned by the reference's swiglu printout
+     * (results/sum32-evidence/unit-tests-lns16-base.txt:44-63), which silu =
+     * x / (1 + exp(-x)) in xlns16 arithmetic reproduces to every digit with
+     * this rule and not with a float expf converted through fp2xlns16. */
     for (uint32_t c = 0; c < 65536; c++) {
-        float e = expf(g_dec16[c]);
-        uint32_t bits;
-        memcpy(&bits, &e, 4);
-        g_exp16[c] = g_conv16[bits >> 16];
+        long q = (long) floor((double) g_dec16[c] * 1.4426950408889634 * 128.0) + (long) X16_OFFSET;
+        if (q < 0) q = 0;
+        if (q > (long) X16_LOGMASK) q = (long) X16_LOGMASK;
+        g_exp16[c] = (uint16_t) q;
     }
 }
 
@@ -790,4 +795,81 @@ int orc_init(void) {
     build_lfsr();
     g_ready = 1;
     return 0;
+}
+
+/* ===================================================================== */
+/* Elementwise ops at the F32 op boundary (lns-backend/src/lns-ops.cpp:   */
+/* 468-599, 786-868, 1199-1281): each operand is converted with fp2xlns16, */
+/* the op runs in xlns16 and the result is written back with xlns162fp.   */
+/* ===================================================================== */
+
+/* silu(x) = x / (1 + exp(-x)) in xlns16 arithmetic (see the exp table) */
+uint16_t orc16_silu(uint16_t x) {
+    return orc16_div(x, orc16_add((uint16_t) X16_OFFSET, orc16_exp((uint16_t) (x ^ X16_SIGNMASK))));
+}
+/* relu(x): x where x > 0, else the zero code */
+uint16_t orc16_relu(uint16_t x) {
+    return ((x & X16_SIGNMASK) || (x & X16_LOGMASK) == 0) ? (uint16_t) X16_ZERO : x;
+}
+
+static inline uint16_t f2c(float f) { return orc16_from_f32(f); }
+static inline float c2f(uint16_t c) { return orc16_to_f32(c); }
+
+/* dst = a op b, b repeated to a's shape (lns_add / lns_mul / lns_div) */
+void orc16_binary_f32(int op, const float * a, const int64_t ane[4], const float * b, const int64_t bne[4], float * dst) {
+    for (int64_t i3 = 0; i3 < ane[3]; i3++)
+        for (int64_t i2 = 0; i2 < ane[2]; i2++)
+            for (int64_t i1 = 0; i1 < ane[1]; i1++) {
+                const int64_t ra = ((i3 * ane[2] + i2) * ane[1] + i1) * ane[0];
+                const int64_t rb = (((i3 % bne[3]) * bne[2] + (i2 % bne[2])) * bne[1] + (i1 % bne[1])) * bne[0];
+                for (int64_t i0 = 0; i0 < ane[0]; i0++) {
+                    const uint16_t x = f2c(a[ra + i0]), y = f2c(b[rb + i0 % bne[0]]);
+                    const uint16_t r = op == ORC_ADD ? orc16_add(x, y) : op == ORC_MUL ? orc16_mul(x, y) : orc16_div(x, y);
+                    dst[ra + i0] = c2f(r);
+                }
+            }
+}
+
+/* dst = src * s (+ b when b != 0) (lns_scale) */
+void orc16_scale_f32(const float * src, float * dst, int64_t n, float s, float b) {
+    const uint16_t sl = f2c(s), bl = f2c(b);
+    for (int64_t i = 0; i < n; i++) {
+        uint16_t v = orc16_mul(f2c(src[i]), sl);
+        if (b != 0.0f) v = orc16_add(v, bl);
+        dst[i] = c2f(v);
+    }
+}
+
+void orc16_unary_f32(int op, const float * src, float * dst, int64_t n) {
+    for (int64_t i = 0; i < n; i++) {
+        const uint16_t v = f2c(src[i]);
+        dst[i] = c2f(op == ORC_SILU ? orc16_silu(v) : orc16_relu(v));
+    }
+}
+
+/* dst[r][c] = silu(gate[r*gs + c]) * up[r*us + c] (lns_swiglu) */
+void orc16_swiglu_f32(const float * gate, const float * up, int64_t gs, int64_t us, float * dst, int64_t nc, int64_t nr) {
+    for (int64_t r = 0; r < nr; r++)
+        for (int64_t c = 0; c < nc; c++)
+            dst[r * nc + c] = c2f(orc16_mul(orc16_silu(f2c(gate[r * gs + c])), f2c(up[r * us + c])));
+}
+
+/* rotary embedding of rows of ne[0] (lns_rope): pairs (2j, 2j+1), or (j, j +
+ * n_dims/2) for neox, rotated by cos_sin[(i2 * n_dims/2 + j) * 2 + {0,1}] of
+ * the row's position i2; dimensions past n_dims pass through xlns16. */
+void orc16_rope_f32(const float * src, const int64_t ne[4], const float * cos_sin, int n_dims, int neox, float * dst) {
+    const int64_t half = n_dims / 2;
+    for (int64_t i3 = 0; i3 < ne[3]; i3++)
+        for (int64_t i2 = 0; i2 < ne[2]; i2++)
+            for (int64_t i1 = 0; i1 < ne[1]; i1++) {
+                const int64_t row = ((i3 * ne[2] + i2) * ne[1] + i1) * ne[0];
+                for (int64_t j = 0; j < half; j++) {
+                    const uint16_t c = f2c(cos_sin[(i2 * half + j) * 2]), sn = f2c(cos_sin[(i2 * half + j) * 2 + 1]);
+                    const int64_t i0 = neox ? j : 2 * j, i1b = neox ? j + half : 2 * j + 1;
+                    const uint16_t x0 = f2c(src[row + i0]), x1 = f2c(src[row + i1b]);
+                    dst[row + i0]  = c2f(orc16_sub(orc16_mul(x0, c), orc16_mul(x1, sn)));
+                    dst[row + i1b] = c2f(orc16_add(orc16_mul(x0, sn), orc16_mul(x1, c)));
+                }
+                for (int64_t j = n_dims; j < ne[0]; j++) dst[row + j] = c2f(f2c(src[row + j]));
+            }
 }

@@ -61,6 +61,12 @@ def lib():
             "orc16_to_f32_n": (None, [u16p, f32p, i64]),
             "orc32_from_f32_n": (None, [f32p, u32p, i64]),
             "orc32_to_f32_n": (None, [u32p, f32p, i64]),
+            "orc16_silu": (ctypes.c_uint16, [ctypes.c_uint16]),
+            "orc16_binary_f32": (None, [ctypes.c_int, f32p, i64a, f32p, i64a, f32p]),
+            "orc16_scale_f32": (None, [f32p, f32p, i64, ctypes.c_float, ctypes.c_float]),
+            "orc16_unary_f32": (None, [ctypes.c_int, f32p, f32p, i64]),
+            "orc16_swiglu_f32": (None, [f32p, f32p, i64, i64, f32p, i64, i64]),
+            "orc16_rope_f32": (None, [f32p, i64a, f32p, ctypes.c_int, ctypes.c_int, f32p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -70,6 +76,75 @@ def lib():
             raise RuntimeError("oracle table construction failed")
         _lib = L
     return _lib
+
+
+BINARY = {"add": 0, "mul": 1, "div": 2}
+UNARY = {"silu": 0, "relu": 2}
+
+
+def binary16(op, a, b):
+    """a op b at the F32 op boundary, b repeated to a's shape (numpy, innermost last)."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    out = np.empty_like(a)
+    lib().orc16_binary_f32(BINARY[op], a.ravel(), _ne(a.shape[::-1]), b.ravel(), _ne(b.shape[::-1]), out.ravel())
+    return out
+
+
+def scale16(src, s, b=0.0):
+    src = np.ascontiguousarray(src, np.float32)
+    out = np.empty_like(src)
+    lib().orc16_scale_f32(src.ravel(), out.ravel(), src.size, s, b)
+    return out
+
+
+def unary16(op, src):
+    src = np.ascontiguousarray(src, np.float32)
+    out = np.empty_like(src)
+    lib().orc16_unary_f32(UNARY[op], src.ravel(), out.ravel(), src.size)
+    return out
+
+
+def swiglu16(gate, up):
+    """silu(gate) * up, rows of gate.shape[-1]"""
+    gate = np.ascontiguousarray(gate, np.float32)
+    up = np.ascontiguousarray(up, np.float32)
+    nc = gate.shape[-1]
+    out = np.empty_like(gate)
+    lib().orc16_swiglu_f32(gate.ravel(), up.ravel(), nc, nc, out.ravel(), nc, gate.size // nc)
+    return out
+
+
+def rope16(src, cos_sin, n_dims, neox=False):
+    """src [ne3][ne2][ne1][ne0] (numpy order), cos_sin [ne2][n_dims/2][2]"""
+    src = np.ascontiguousarray(src, np.float32)
+    cs = np.ascontiguousarray(cos_sin, np.float32)
+    out = np.empty_like(src)
+    lib().orc16_rope_f32(src.ravel(), _ne(src.shape[::-1]), cs.ravel(), n_dims, 1 if neox else 0, out.ravel())
+    return out
+
+
+def rope_cos_sin(pos, n_dims, freq_base):
+    """(cos, sin) per position and rotated pair in the float recurrence of
+    lns_rope (lns-backend/src/lns-ops.cpp:1231-1262), with the C library's
+    float functions: theta_scale = powf(base, -2/n_dims), t = pos,
+    cos_sin = (cosf(t), sinf(t)), t *= theta_scale per pair."""
+    libm = ctypes.CDLL("libm.so.6")
+    for fn in ("cosf", "sinf"):
+        getattr(libm, fn).restype = ctypes.c_float
+        getattr(libm, fn).argtypes = [ctypes.c_float]
+    libm.powf.restype = ctypes.c_float
+    libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+    half = n_dims // 2
+    ts = np.float32(libm.powf(float(np.float32(freq_base)), float(np.float32(-2.0) / np.float32(n_dims))))
+    out = np.empty((len(pos), half, 2), np.float32)
+    for i, p in enumerate(pos):
+        t = np.float32(p)
+        for j in range(half):
+            out[i, j, 0] = libm.cosf(float(t))
+            out[i, j, 1] = libm.sinf(float(t))
+            t = np.float32(t * ts)
+    return out
 
 
 def _ne(shape):

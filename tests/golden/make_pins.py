@@ -50,6 +50,17 @@ def parse_suite(text):
     return out
 
 
+def parse_swiglu(text, test_src):
+    """The swiglu case of test-lns-backend.cpp (run_swiglu_test): its gate/up
+    inputs from the test source, its printed 2 x 4 output from the log."""
+    def arr(name):
+        m = re.search(r"const float %s\[rows \* cols\] = \{([^}]*)\}" % name, test_src)
+        return [float(v.rstrip("f")) for v in re.findall(r"-?\d+\.\d+f?", m.group(1))]
+    m = re.search(r"LNS swiglu split \(4 x 2\):\s*\[([^\]]*)\]", text)
+    return {"gate": arr("gate"), "up": arr("up"), "out": floats(m.group(1)),
+            "source": "lns-backend/tests/test-lns-backend.cpp run_swiglu_test; unit-tests-lns16-base.txt"}
+
+
 def main(ref):
     ev = os.path.join(ref, "results", "sum32-evidence")
     with open(os.path.join(ev, "standalone-sum32-invariants.txt")) as f:
@@ -60,7 +71,11 @@ def main(ref):
                      ("lns32", "unit-tests-lns32.txt")):
         with open(os.path.join(ev, fn)) as f:
             suite[name] = parse_suite(f.read())
+    with open(os.path.join(ev, "unit-tests-lns16-base.txt")) as f, \
+            open(os.path.join(ref, "lns-backend", "tests", "test-lns-backend.cpp")) as g:
+        swiglu = parse_swiglu(f.read(), g.read())
     pins = {
+        "swiglu": swiglu,
         "source": "xlnsresearch/xlns-ggml-backend results/sum32-evidence/*.txt (outputs of "
                   "lns-backend/tests/test-lns16-sum32.cpp and test-lns-backend.cpp)",
         "standalone": standalone,

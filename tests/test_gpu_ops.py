@@ -1,0 +1,130 @@
+"""GPU parity of the model graph's elementwise ops (lnsb_binary / scale /
+unary / glu / rope and the F16 conversions) against the CPU oracle, bit for
+bit, at the F32 op boundary (lns-backend/src/lns-ops.cpp:468-599, 786-868,
+1199-1281)."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ks():
+    import lnsb200
+    k = lnsb200.KernelSet(16, "base")
+    k.upload_tables()
+    return k
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def f32(rng, shape, sigma=1.0):
+    a = rng.normal(0.0, sigma, shape).astype(np.float32)
+    flat = a.ravel()
+    flat[:: max(1, flat.size // 7)] = 0.0          # zeros among the values
+    return a
+
+
+def same(got, want):
+    return np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("op", ["add", "mul", "div"])
+@pytest.mark.parametrize("bshape", [(1, 1, 1, 576), (1, 1, 5, 576), (2, 1, 5, 576), (1, 1, 1, 1)])
+def test_binary(orc, ks, op, bshape):
+    rng = np.random.default_rng(len(bshape) + bshape[-1] + bshape[-2])
+    a = f32(rng, (2, 3, 5, 576))
+    b = f32(rng, bshape, 0.5)
+    want = orc.binary16(op, a, b)
+    out = torch.empty(a.size, dtype=torch.float32, device="cuda")
+    ks.binary(op, dev(a), a.shape[::-1], dev(b), b.shape[::-1], out)
+    assert same(host(out).reshape(a.shape), want)
+
+
+@pytest.mark.parametrize("s,b", [(0.125, 0.0), (-3.0, 0.5)])
+def test_scale(orc, ks, s, b):
+    rng = np.random.default_rng(3)
+    x = f32(rng, (4096,), 2.0)
+    out = torch.empty_like(dev(x))
+    ks.scale(dev(x), out, x.size, s, b)
+    assert same(host(out), orc.scale16(x, s, b))
+
+
+@pytest.mark.parametrize("op", ["silu", "relu"])
+def test_unary(orc, ks, op):
+    rng = np.random.default_rng(5)
+    x = np.concatenate([f32(rng, (8192,), 3.0), np.array([0.0, -0.0, 1e-30, -1e-30, 60.0, -60.0, 1e30, -1e30], np.float32)])
+    out = torch.empty_like(dev(x))
+    ks.unary(op, dev(x), out, x.size)
+    assert same(host(out), orc.unary16(op, x))
+
+
+def test_swiglu_split_and_fused(orc, ks):
+    rng = np.random.default_rng(7)
+    nc, nr = 1536, 6
+    gate = f32(rng, (nr, nc), 2.0)
+    up = f32(rng, (nr, nc), 1.0)
+    want = orc.swiglu16(gate, up)
+    out = torch.empty((nr, nc), dtype=torch.float32, device="cuda")
+    ks.glu(dev(gate), dev(up), nc, nc, out, nc, nr)
+    assert same(host(out), want)
+    fused = np.concatenate([gate, up], axis=1)          # [gate | up] per row, stride 2 * nc
+    fd = dev(fused)
+    ks.glu(fd, fd[:, nc:], 2 * nc, 2 * nc, out, nc, nr)
+    assert same(host(out), want)
+
+
+def test_swiglu_reference_pin(ks):
+    """the reference's printed swiglu (test-lns-backend.cpp run_swiglu_test) through the GPU"""
+    import json
+    import os
+    from conftest import ROOT
+    p = json.load(open(os.path.join(ROOT, "tests", "golden", "reference_pins.json")))["swiglu"]
+    gate = np.array(p["gate"], np.float32).reshape(2, 4)
+    up = np.array(p["up"], np.float32).reshape(2, 4)
+    out = torch.empty((2, 4), dtype=torch.float32, device="cuda")
+    ks.glu(dev(gate), dev(up), 4, 4, out, 4, 2)
+    assert ["%.6f" % v for v in host(out).ravel()] == ["%.6f" % v for v in p["out"]]
+
+
+@pytest.mark.parametrize("n_dims,neox", [(64, False), (64, True), (32, False)])
+def test_rope(orc, ks, n_dims, neox):
+    rng = np.random.default_rng(n_dims + neox)
+    hd, nh, nt = 64, 9, 7
+    x = f32(rng, (1, nt, nh, hd), 1.0)
+    pos = [0, 1, 2, 5, 17, 100, 255]
+    cs = orc.rope_cos_sin(pos, n_dims, 100000.0)
+    want = orc.rope16(x, cs, n_dims, neox)
+    out = torch.empty(x.size, dtype=torch.float32, device="cuda")
+    ks.rope(dev(x), (hd, nh, nt, 1), dev(cs), n_dims, out, neox=neox)
+    assert same(host(out).reshape(x.shape), want)
+
+
+def test_f16_conversions(ks):
+    rng = np.random.default_rng(9)
+    x = np.concatenate([rng.normal(0, 3.0, 100000).astype(np.float32),
+                        np.array([0.0, -0.0, 65504.0, 7e4, 6e-8, 1e-9, np.inf, -np.inf], np.float32)])
+    h = torch.empty(x.size, dtype=torch.int16, device="cuda")
+    ks.f32_to_f16(dev(x), h, x.size)
+    assert np.array_equal(host(h).view(np.uint16), x.astype(np.float16).view(np.uint16))
+    back = torch.empty_like(dev(x))
+    ks.f16_to_f32(h, back, x.size)
+    assert same(host(back), x.astype(np.float16).astype(np.float32))
+
+
+def test_unsupported_and_invalid(ks):
+    import lnsb200
+    x = torch.zeros(16, dtype=torch.float32, device="cuda")
+    with pytest.raises(lnsb200.LnsbError):
+        ks.unary("gelu", x, x, 16)                      # gelu not pinned: LNSB_E_UNSUPPORTED
+    with pytest.raises(lnsb200.LnsbError):
+        ks.binary("add", x, (16, 1, 1, 1), x, (3, 1, 1, 1), x)   # b does not repeat to a

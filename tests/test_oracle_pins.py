@@ -94,6 +94,17 @@ def test_reference_gates(computed):
         assert s < b and s < 2.0
 
 
+def test_swiglu_pin(pins):
+    """silu in xlns16 arithmetic with the floor-rule exp reproduces the
+    reference's printed swiglu (test-lns-backend.cpp run_swiglu_test) to
+    every digit"""
+    import numpy as np
+    import oracle
+    p = pins["swiglu"]
+    out = oracle.swiglu16(np.array(p["gate"], np.float32).reshape(2, 4), np.array(p["up"], np.float32).reshape(2, 4))
+    assert ["%.6f" % v for v in out.ravel()] == ["%.6f" % v for v in p["out"]]
+
+
 def test_report(computed, pins, capsys):
     """Prints every figure next to the reference's (informational)."""
     rows = []

@@ -8,6 +8,7 @@
 // outputs; each kernel below is organised around keeping as many chains in
 // flight as possible per SM, with operands staged in shared memory and the
 // Gaussian-log table resident there.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <array>
@@ -1362,6 +1363,117 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     }
 }
 
+// ===================== elementwise ops of the model graph ===================
+//
+// F32 in and out, as at every ggml op boundary of the reference's backends
+// (lns-backend/cuda/lns-cuda-kernels.cuh:162-355, lns-backend/src/lns-ops.cpp):
+// convert with the F32 -> LNS table, compute in LNS, write back through the
+// decode table.  Grid-stride loops over elements; the tables are read through
+// the read-only cache (conv16 128 KB, dec16 256 KB, sbdb16 6.7 KB).
+template <int FMT> struct ew;
+template <> struct ew<16> {
+    __device__ static __forceinline__ uint32_t from(const dev_tables & T, float x) { return from_f32_16(T, x); }
+    __device__ static __forceinline__ float    to(const dev_tables & T, uint32_t v) { return to_f32_16(T, v); }
+    __device__ static __forceinline__ uint32_t add(const dev_tables & T, uint32_t a, uint32_t b) { return add16(a, b, T.sbdb16); }
+    __device__ static __forceinline__ uint32_t sub(const dev_tables & T, uint32_t a, uint32_t b) { return add16(a, b ^ 0x8000u, T.sbdb16); }
+    __device__ static __forceinline__ uint32_t mul(uint32_t a, uint32_t b) { return mul16(a, b); }
+    __device__ static __forceinline__ uint32_t div(uint32_t a, uint32_t b) { return div16(a, b); }
+};
+template <> struct ew<32> {
+    __device__ static __forceinline__ uint32_t from(const dev_tables & T, float x) { return from_f32_32(T, x); }
+    __device__ static __forceinline__ float    to(const dev_tables & T, uint32_t v) { return to_f32_32(T, v); }
+    __device__ static __forceinline__ uint32_t add(const dev_tables & T, uint32_t a, uint32_t b) { return add32(T, a, b); }
+    __device__ static __forceinline__ uint32_t sub(const dev_tables & T, uint32_t a, uint32_t b) { return add32(T, a, b ^ 0x80000000u); }
+    __device__ static __forceinline__ uint32_t mul(uint32_t a, uint32_t b) { return mul32(a, b); }
+    __device__ static __forceinline__ uint32_t div(uint32_t a, uint32_t b) { return div32(a, b); }
+};
+
+// silu(x) = x / (1 + exp(-x)) in xlns16 arithmetic over the exp table
+__device__ __forceinline__ uint32_t silu16(const dev_tables & T, uint32_t x) {
+    const uint32_t e = __ldg(T.exp16 + (x ^ 0x8000u));
+    return div16(x, add16(0x4000u, e, T.sbdb16));
+}
+__device__ __forceinline__ uint32_t relu16(uint32_t x) { return ((x & 0x8000u) || (x & 0x7FFFu) == 0) ? 0u : x; }
+
+#define LNSB_GRID_STRIDE(i, n) \
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < (n); i += (int64_t) blockDim.x * gridDim.x)
+
+template <int FMT, int OP>
+__global__ void k_binary(dev_tables T, const float * __restrict__ a, lnsb_shape4 as, const float * __restrict__ b,
+                         lnsb_shape4 bs, float * __restrict__ dst) {
+    using A = ew<FMT>;
+    const int64_t n = as.ne[0] * as.ne[1] * as.ne[2] * as.ne[3];
+    LNSB_GRID_STRIDE(i, n) {
+        const int64_t i0 = i % as.ne[0], r = i / as.ne[0];
+        const int64_t i1 = r % as.ne[1], r2 = r / as.ne[1];
+        const int64_t i2 = r2 % as.ne[2], i3 = r2 / as.ne[2];
+        const int64_t j = (((i3 % bs.ne[3]) * bs.ne[2] + i2 % bs.ne[2]) * bs.ne[1] + i1 % bs.ne[1]) * bs.ne[0] + i0 % bs.ne[0];
+        const uint32_t x = A::from(T, a[i]), y = A::from(T, b[j]);
+        const uint32_t v = OP == LNSB_BINARY_ADD ? A::add(T, x, y) : OP == LNSB_BINARY_MUL ? A::mul(x, y) : A::div(x, y);
+        dst[i] = A::to(T, v);
+    }
+}
+
+template <int FMT>
+__global__ void k_scale(dev_tables T, const float * __restrict__ src, float * __restrict__ dst, int64_t n, uint32_t sl,
+                        uint32_t bl, int has_b) {
+    using A = ew<FMT>;
+    LNSB_GRID_STRIDE(i, n) {
+        uint32_t v = A::mul(A::from(T, src[i]), sl);
+        if (has_b) v = A::add(T, v, bl);
+        dst[i] = A::to(T, v);
+    }
+}
+
+template <int OP>
+__global__ void k_unary16(dev_tables T, const float * __restrict__ src, float * __restrict__ dst, int64_t n) {
+    LNSB_GRID_STRIDE(i, n) {
+        const uint32_t v = from_f32_16(T, src[i]);
+        dst[i] = to_f32_16(T, OP == LNSB_UNARY_SILU ? silu16(T, v) : relu16(v));
+    }
+}
+
+__global__ void k_swiglu16(dev_tables T, const float * __restrict__ gate, const float * __restrict__ up, int64_t gs,
+                           int64_t us, float * __restrict__ dst, int64_t nc, int64_t nr) {
+    LNSB_GRID_STRIDE(i, nc * nr) {
+        const int64_t r = i / nc, c = i - r * nc;
+        const uint32_t g = from_f32_16(T, gate[r * gs + c]), u = from_f32_16(T, up[r * us + c]);
+        dst[i] = to_f32_16(T, mul16(silu16(T, g), u));
+    }
+}
+
+// one thread per rotated pair or passed-through dimension (lns-cuda-kernels.cuh:330-355)
+template <int FMT>
+__global__ void k_rope(dev_tables T, const float * __restrict__ src, lnsb_shape4 s, const float * __restrict__ cos_sin,
+                       int n_dims, int neox, float * __restrict__ dst) {
+    using A = ew<FMT>;
+    const int64_t half = n_dims / 2, per = half + (s.ne[0] - n_dims);
+    const int64_t nrows = s.ne[1] * s.ne[2] * s.ne[3];
+    LNSB_GRID_STRIDE(i, nrows * per) {
+        const int64_t row = i / per, j = i - row * per;
+        const int64_t i2 = (row / s.ne[1]) % s.ne[2];
+        const float * x = src + row * s.ne[0];
+        float *       y = dst + row * s.ne[0];
+        if (j < half) {
+            const int64_t a0 = neox ? j : 2 * j, a1 = neox ? j + half : 2 * j + 1;
+            const uint32_t c = A::from(T, cos_sin[(i2 * half + j) * 2]), sn = A::from(T, cos_sin[(i2 * half + j) * 2 + 1]);
+            const uint32_t x0 = A::from(T, x[a0]), x1 = A::from(T, x[a1]);
+            y[a0] = A::to(T, A::sub(T, A::mul(x0, c), A::mul(x1, sn)));
+            y[a1] = A::to(T, A::add(T, A::mul(x0, sn), A::mul(x1, c)));
+        } else {
+            const int64_t a0 = n_dims + (j - half);
+            y[a0] = A::to(T, A::from(T, x[a0]));
+        }
+    }
+}
+
+__global__ void k_f32_to_f16(const float * __restrict__ src, __half * __restrict__ dst, int64_t n) {
+    LNSB_GRID_STRIDE(i, n) dst[i] = __float2half_rn(src[i]);
+}
+__global__ void k_f16_to_f32(const __half * __restrict__ src, float * __restrict__ dst, int64_t n) {
+    LNSB_GRID_STRIDE(i, n) dst[i] = __half2float(src[i]);
+}
+
 // ============================ launch helpers ===============================
 
 int sm_count(int dev) {
@@ -1809,6 +1921,122 @@ int lnsb_rms_norm(int fmt, const float * src, float * dst, int64_t ncols, int64_
 int lnsb_rms_norm_lns(int fmt, const void * src, void * dst, int64_t ncols, int64_t nrows, float eps,
                       uint16_t monte_seed, lnsb_stream_t stream) {
     return rms_norm_impl(fmt, src, dst, ncols, nrows, eps, monte_seed, false, static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+bool shape_ok(const int64_t ne[4]) {
+    if (ne == nullptr) return false;
+    for (int i = 0; i < 4; i++) if (ne[i] < 0) return false;
+    return true;
+}
+int64_t nel(const int64_t ne[4]) { return ne[0] * ne[1] * ne[2] * ne[3]; }
+lnsb_shape4 shape_of(const int64_t ne[4]) { lnsb_shape4 s; for (int i = 0; i < 4; i++) s.ne[i] = ne[i]; return s; }
+}  // namespace
+
+int lnsb_binary(int fmt, int op, const float * a, const int64_t ane[4], const float * b, const int64_t bne[4],
+                float * dst, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || op < LNSB_BINARY_ADD || op > LNSB_BINARY_DIV || !shape_ok(ane) || !shape_ok(bne)) return LNSB_E_INVALID;
+    const int64_t n = nel(ane);
+    if (n == 0) return 0;
+    for (int i = 0; i < 4; i++) if (bne[i] <= 0 || ane[i] % bne[i] != 0) return LNSB_E_INVALID;   // b repeats to a
+    if (a == nullptr || b == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned g = grid_for(n, 256);
+    const lnsb_shape4 as = shape_of(ane), bs = shape_of(bne);
+#define LNSB_BIN(F, O) k_binary<F, O><<<g, 256, 0, s>>>(*T, a, as, b, bs, dst)
+    if (fmt == LNSB_XLNS16) {
+        if (op == LNSB_BINARY_ADD) LNSB_BIN(16, LNSB_BINARY_ADD); else if (op == LNSB_BINARY_MUL) LNSB_BIN(16, LNSB_BINARY_MUL); else LNSB_BIN(16, LNSB_BINARY_DIV);
+    } else {
+        if (op == LNSB_BINARY_ADD) LNSB_BIN(32, LNSB_BINARY_ADD); else if (op == LNSB_BINARY_MUL) LNSB_BIN(32, LNSB_BINARY_MUL); else LNSB_BIN(32, LNSB_BINARY_DIV);
+    }
+#undef LNSB_BIN
+    return launch_status();
+}
+
+int lnsb_scale(int fmt, const float * src, float * dst, int64_t n, float sv, float bv, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || n < 0) return LNSB_E_INVALID;
+    if (n == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint32_t sl, bl;
+    if (fmt == LNSB_XLNS16) {
+        const host_tables & H = get_host_tables(false, false);
+        uint32_t u;
+        std::memcpy(&u, &sv, 4); sl = H.conv16[u >> 16];
+        std::memcpy(&u, &bv, 4); bl = H.conv16[u >> 16];
+        k_scale<16><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n, sl, bl, bv != 0.0f ? 1 : 0);
+    } else {
+        sl = host_from_f32_32(sv);
+        bl = host_from_f32_32(bv);
+        k_scale<32><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n, sl, bl, bv != 0.0f ? 1 : 0);
+    }
+    return launch_status();
+}
+
+int lnsb_unary(int fmt, int op, const float * src, float * dst, int64_t n, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || op < LNSB_UNARY_SILU || op > LNSB_UNARY_TANH || n < 0) return LNSB_E_INVALID;
+    if (fmt != LNSB_XLNS16 || (op != LNSB_UNARY_SILU && op != LNSB_UNARY_RELU)) return LNSB_E_UNSUPPORTED;
+    if (n == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (op == LNSB_UNARY_SILU) k_unary16<LNSB_UNARY_SILU><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
+    else                       k_unary16<LNSB_UNARY_RELU><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
+    return launch_status();
+}
+
+int lnsb_glu(int fmt, int op, const float * gate, const float * up, int64_t gate_stride, int64_t up_stride, float * dst,
+             int64_t ncols, int64_t nrows, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || (op != LNSB_GLU_SWIGLU && op != LNSB_GLU_GEGLU) || ncols < 0 || nrows < 0) return LNSB_E_INVALID;
+    if (fmt != LNSB_XLNS16 || op != LNSB_GLU_SWIGLU) return LNSB_E_UNSUPPORTED;
+    if (ncols == 0 || nrows == 0) return 0;
+    if (gate == nullptr || up == nullptr || dst == nullptr || gate_stride < ncols || up_stride < ncols) return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    k_swiglu16<<<grid_for(ncols * nrows, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(*T, gate, up, gate_stride,
+                                                                                            up_stride, dst, ncols, nrows);
+    return launch_status();
+}
+
+int lnsb_rope(int fmt, const lnsb_rope_args * a, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || a == nullptr || !shape_ok(a->shape.ne)) return LNSB_E_INVALID;
+    if (a->n_dims <= 0 || a->n_dims % 2 != 0 || a->n_dims > a->shape.ne[0]) return LNSB_E_INVALID;
+    const int64_t nrows = a->shape.ne[1] * a->shape.ne[2] * a->shape.ne[3];
+    if (nrows == 0) return 0;
+    if (a->src == nullptr || a->dst == nullptr || a->cos_sin == nullptr) return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const int64_t per = a->n_dims / 2 + (a->shape.ne[0] - a->n_dims);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (fmt == LNSB_XLNS16) k_rope<16><<<grid_for(nrows * per, 256), 256, 0, s>>>(*T, a->src, a->shape, a->cos_sin, a->n_dims, a->neox, a->dst);
+    else                    k_rope<32><<<grid_for(nrows * per, 256), 256, 0, s>>>(*T, a->src, a->shape, a->cos_sin, a->n_dims, a->neox, a->dst);
+    return launch_status();
+}
+
+int lnsb_f32_to_f16(const float * src, uint16_t * dst, int64_t n, lnsb_stream_t stream) {
+    if (n < 0) return LNSB_E_INVALID;
+    if (n == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    k_f32_to_f16<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, reinterpret_cast<__half *>(dst), n);
+    return launch_status();
+}
+
+int lnsb_f16_to_f32(const uint16_t * src, float * dst, int64_t n, lnsb_stream_t stream) {
+    if (n < 0) return LNSB_E_INVALID;
+    if (n == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    k_f16_to_f32<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(reinterpret_cast<const __half *>(src), dst, n);
+    return launch_status();
 }
 
 int lnsb_monte_get_state(uint16_t * state) {

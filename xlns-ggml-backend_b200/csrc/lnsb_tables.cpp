@@ -82,12 +82,14 @@ void build16(host_tables & t) {
         t.dec16[c] = (float) ((c & 0x8000u) ? -v : v);
     }
 
+    // exp: the log of e^x is x log2(e), taken to F=7 by floor from the value's
+    // float x = xlns162fp(c) (the rule the reference's printed swiglu pins)
     t.exp16.resize(65536);
     for (uint32_t c = 0; c < 65536; c++) {
-        const float e = std::exp(t.dec16[c]);    // float overload: expf
-        uint32_t bits;
-        std::memcpy(&bits, &e, 4);
-        t.exp16[c] = t.conv16[bits >> 16];
+        long q = (long) std::floor((double) t.dec16[c] * 1.4426950408889634 * 128.0) + 0x4000L;
+        if (q < 0) q = 0;
+        if (q > 0x7FFF) q = 0x7FFF;
+        t.exp16[c] = (uint16_t) q;
     }
 
     t.monte16.assign(2 * k16_monte_n, 0);

@@ -123,6 +123,38 @@ class KernelSet:
                    self.lib.lnsb_rms_norm_lns(self.fmt, _ptr(src), _ptr(dst), ncols, nrows, eps, monte_seed, _stream(stream)))
 
 
+    # ---- elementwise ops of the model graph (F32 in and out) ----
+    BINARY = {"add": 0, "mul": 1, "div": 2}
+    UNARY = {"silu": 0, "gelu": 1, "relu": 2, "tanh": 3}
+
+    def binary(self, op, a, a_shape, b, b_shape, dst, stream=None):
+        """dst = a op b, b repeated to a's shape; shapes ggml order (ne0 innermost)"""
+        ane, bne = _shape4(a_shape).ne, _shape4(b_shape).ne
+        _lib.check(self.lib, "lnsb_binary", self.lib.lnsb_binary(self.fmt, self.BINARY[op], _ptr(a), ane, _ptr(b), bne,
+                                                                 _ptr(dst), _stream(stream)))
+
+    def scale(self, src, dst, n, s, b=0.0, stream=None):
+        _lib.check(self.lib, "lnsb_scale", self.lib.lnsb_scale(self.fmt, _ptr(src), _ptr(dst), n, s, b, _stream(stream)))
+
+    def unary(self, op, src, dst, n, stream=None):
+        _lib.check(self.lib, "lnsb_unary", self.lib.lnsb_unary(self.fmt, self.UNARY[op], _ptr(src), _ptr(dst), n,
+                                                               _stream(stream)))
+
+    def glu(self, gate, up, gate_stride, up_stride, dst, ncols, nrows, op="swiglu", stream=None):
+        _lib.check(self.lib, "lnsb_glu", self.lib.lnsb_glu(self.fmt, 0 if op == "swiglu" else 1, _ptr(gate), _ptr(up),
+                                                           gate_stride, up_stride, _ptr(dst), ncols, nrows, _stream(stream)))
+
+    def rope(self, src, shape, cos_sin, n_dims, dst, neox=False, stream=None):
+        a = _lib.RopeArgs(_ptr(src), _shape4(shape), _ptr(cos_sin), n_dims, 1 if neox else 0, _ptr(dst))
+        _lib.check(self.lib, "lnsb_rope", self.lib.lnsb_rope(self.fmt, ctypes.byref(a), _stream(stream)))
+
+    def f32_to_f16(self, src, dst, n, stream=None):
+        _lib.check(self.lib, "lnsb_f32_to_f16", self.lib.lnsb_f32_to_f16(_ptr(src), _ptr(dst), n, _stream(stream)))
+
+    def f16_to_f32(self, src, dst, n, stream=None):
+        _lib.check(self.lib, "lnsb_f16_to_f32", self.lib.lnsb_f16_to_f32(_ptr(src), _ptr(dst), n, _stream(stream)))
+
+
 def kernels(fmt=XLNS16, mode="base"):
     return KernelSet(fmt, mode)
 

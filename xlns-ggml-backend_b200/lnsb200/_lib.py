@@ -33,6 +33,11 @@ class SoftMaxArgs(ctypes.Structure):
                 ("monte_seed", ctypes.c_uint16)]
 
 
+class RopeArgs(ctypes.Structure):
+    _fields_ = [("src", ctypes.c_void_p), ("shape", Shape4), ("cos_sin", ctypes.c_void_p), ("n_dims", ctypes.c_int),
+                ("neox", ctypes.c_int), ("dst", ctypes.c_void_p)]
+
+
 # (name, restype, argtypes) for every function of include/lnsb200.h
 _I64 = ctypes.c_int64
 _VP = ctypes.c_void_p
@@ -58,6 +63,14 @@ SIGNATURES = [
                                                  ctypes.c_uint32, _VP, ctypes.c_uint16, _VP]),
     ("lnsb_rms_norm", ctypes.c_int, [ctypes.c_int, _VP, _VP, _I64, _I64, ctypes.c_float, ctypes.c_uint16, _VP]),
     ("lnsb_rms_norm_lns", ctypes.c_int, [ctypes.c_int, _VP, _VP, _I64, _I64, ctypes.c_float, ctypes.c_uint16, _VP]),
+    ("lnsb_binary", ctypes.c_int, [ctypes.c_int, ctypes.c_int, _VP, ctypes.POINTER(_I64), _VP, ctypes.POINTER(_I64),
+                                   _VP, _VP]),
+    ("lnsb_scale", ctypes.c_int, [ctypes.c_int, _VP, _VP, _I64, ctypes.c_float, ctypes.c_float, _VP]),
+    ("lnsb_unary", ctypes.c_int, [ctypes.c_int, ctypes.c_int, _VP, _VP, _I64, _VP]),
+    ("lnsb_glu", ctypes.c_int, [ctypes.c_int, ctypes.c_int, _VP, _VP, _I64, _I64, _VP, _I64, _I64, _VP]),
+    ("lnsb_rope", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(RopeArgs), _VP]),
+    ("lnsb_f32_to_f16", ctypes.c_int, [_VP, _VP, _I64, _VP]),
+    ("lnsb_f16_to_f32", ctypes.c_int, [_VP, _VP, _I64, _VP]),
     ("lnsb_monte_get_state", ctypes.c_int, [ctypes.POINTER(ctypes.c_uint16)]),
     ("lnsb_monte_set_state", ctypes.c_int, [ctypes.c_uint16]),
     ("lnsb_monte_reserve", ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint16)]),
