@@ -1,0 +1,57 @@
+"""The Llama-architecture decode (lnsb200.model: LNS16
+sum32) on the GPU against the same graph on the CPU oracle: final-token
+logits bit for bit after prefill and after each decode step, and the greedy
+token stream."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(n_layer=2, n_embd=128, n_head=4, n_head_kv=2, head_dim=32, n_ff=256, vocab=1000,
+             rope_base=100000.0, eps=1e-5)
+
+
+def run_both(cfg, mode, n_prompt, n_steps, n_ctx=64):
+    from lnsb200 import model
+    w = model.init_weights(cfg, seed=2)
+    prompt = model.prompt_ids(cfg, n_prompt, seed=2)
+    g = model.GpuOps(cfg, w, mode=mode, n_ctx=n_ctx)
+    o = model.OracleOps(cfg, w, mode=mode, n_ctx=n_ctx)
+    lg = model.forward(g, cfg, prompt, 0)
+    lo = model.forward(o, cfg, prompt, 0)
+    steps = [(lg.cpu().numpy().ravel(), lo.ravel())]
+    pos = n_prompt
+    for _ in range(n_steps):
+        tg, to = g.argmax(lg), o.argmax(lo)
+        assert tg == to
+        lg = model.forward(g, cfg, [tg], pos)
+        lo = model.forward(o, cfg, [to], pos)
+        steps.append((lg.cpu().numpy().ravel(), lo.ravel()))
+        pos += 1
+    return steps
+
+
+@pytest.mark.parametrize("mode", ["sum32", "base"])
+def test_small_model_decode_bit_exact(mode):
+    for i, (a, b) in enumerate(run_both(SMALL, mode, 7, 4)):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), "logits differ at step %d" % i
+
+
+def test_smollm2_shape_decode_bit_exact():
+    """the full configs[2] shape (30 layers, d 576, 9/3 heads, ffn 1536, vocab
+    49152), a short prompt and three decode steps"""
+    from lnsb200 import model
+    for i, (a, b) in enumerate(run_both(model.SMOLLM2_135M, "sum32", 6, 3, n_ctx=16)):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), "logits differ at step %d" % i
+
+
+def test_generate_matches_forward_loop():
+    from lnsb200 import model
+    w = model.init_weights(SMALL, seed=2)
+    prompt = model.prompt_ids(SMALL, 5, seed=2)
+    g = model.GpuOps(SMALL, w, mode="sum32", n_ctx=32)
+    toks = model.generate(g, SMALL, prompt, 6)
+    o = model.OracleOps(SMALL, w, mode="sum32", n_ctx=32)
+    assert toks == model.generate(o, SMALL, prompt, 6)

@@ -1,0 +1,336 @@
+"""Llama-architecture decoder run op by op the way the reference's LNS backends
+run a llama.cpp graph (SmolLM2-135M shape, random
+weights): every ggml op reads F32, converts to LNS, computes and writes F32
+(the op-boundary requantisation), the KV cache is F16, and the ops come in
+llama.cpp's order for the LLaMA graph:
+
+    x = get_rows(tok_embd, ids)                               (F32 copy)
+    per layer:
+      h = rms_norm(x) * attn_norm
+      q, k, v = Wq h, Wk h, Wv h                              (mul_mat)
+      q, k = rope(q), rope(k)                                 (mode NORM, base 1e5)
+      K, V cache <- k, v                                      (F32 -> F16)
+      kq = K^T q per head (GQA: q head i uses kv head i / 3)  (mul_mat, F16 K)
+      p = soft_max_ext(kq, causal mask, 1/sqrt(64))
+      o = Wo (V p)                                            (mul_mat, F16 V)
+      x = x + o
+      h = rms_norm(x) * ffn_norm
+      x = x + W_down swiglu(W_gate h, W_up h)
+    logits = tok_embd (rms_norm(x_last) * output_norm)        (tied output)
+
+`forward` is written once over an ops object: GpuOps runs it through this
+package's kernels (liblnsb200_<mode>.so), OracleOps through the CPU oracle
+(test infrastructure), so both run the same graph.  Greedy decoding takes the
+first largest logit (llama.cpp's greedy sampler).
+
+Weights are drawn in a fixed order from numpy default_rng(seed) N(0, 0.02),
+F32; the norm weights are 1.0.  The prompt is `prompt_len` ids from a separate
+default_rng(seed).integers(0, vocab).
+"""
+import math
+
+import numpy as np
+
+SMOLLM2_135M = dict(n_layer=30, n_embd=576, n_head=9, n_head_kv=3, head_dim=64, n_ff=1536, vocab=49152,
+                    rope_base=100000.0, eps=1e-5)
+
+
+def init_weights(cfg, seed=2):
+    """F32 weights as ggml holds them: a matrix of ne = (K, M) is M rows of K."""
+    rng = np.random.default_rng(seed)
+    E, F, V = cfg["n_embd"], cfg["n_ff"], cfg["vocab"]
+    kv = cfg["n_head_kv"] * cfg["head_dim"]
+    nrm = lambda *s: rng.normal(0.0, 0.02, s).astype(np.float32)
+    w = {"tok_embd": nrm(V, E), "layers": []}
+    for _ in range(cfg["n_layer"]):
+        w["layers"].append({
+            "attn_norm": np.ones(E, np.float32), "wq": nrm(E, E), "wk": nrm(kv, E), "wv": nrm(kv, E), "wo": nrm(E, E),
+            "ffn_norm": np.ones(E, np.float32), "w_gate": nrm(F, E), "w_up": nrm(F, E), "w_down": nrm(E, F)})
+    w["output_norm"] = np.ones(E, np.float32)
+    return w
+
+
+def prompt_ids(cfg, n, seed=2):
+    return [int(v) for v in np.random.default_rng(seed).integers(0, cfg["vocab"], n)]
+
+
+def rope_table(n_ctx, n_dims, base):
+    """(cos, sin) per position and pair for positions 0 .. n_ctx-1, computed
+    on the host in lns_rope's float recurrence (lns-backend/src/lns-ops.cpp:
+    1231-1262) with the C library's cosf / sinf / powf; [n_ctx][n_dims/2][2]"""
+    import ctypes
+    libm = ctypes.CDLL("libm.so.6")
+    for fn in ("cosf", "sinf"):
+        getattr(libm, fn).restype = ctypes.c_float
+        getattr(libm, fn).argtypes = [ctypes.c_float]
+    libm.powf.restype = ctypes.c_float
+    libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+    half = n_dims // 2
+    ts = np.float32(libm.powf(float(np.float32(base)), float(np.float32(-2.0) / np.float32(n_dims))))
+    out = np.empty((n_ctx, half, 2), np.float32)
+    for p in range(n_ctx):
+        t = np.float32(p)
+        for j in range(half):
+            out[p, j, 0] = libm.cosf(float(t))
+            out[p, j, 1] = libm.sinf(float(t))
+            t = np.float32(t * ts)
+    return out
+
+
+def forward(ops, cfg, ids, pos0):
+    """logits (F32, [vocab]) of the last of `ids`, which sit at positions
+    pos0 .. pos0 + len(ids) - 1; the KV cache holds positions < pos0."""
+    T, E = len(ids), cfg["n_embd"]
+    H, HKV, D = cfg["n_head"], cfg["n_head_kv"], cfg["head_dim"]
+    x = ops.embed(ids)                                              # [T][E]
+    for il in range(cfg["n_layer"]):
+        h = ops.mul(ops.rms_norm(x, cfg["eps"]), ops.w(il, "attn_norm"))
+        q = ops.linear(ops.w(il, "wq"), h)                          # [T][H*D]
+        k = ops.linear(ops.w(il, "wk"), h)                          # [T][HKV*D]
+        v = ops.linear(ops.w(il, "wv"), h)
+        q = ops.rope(q, T, H, D, pos0)
+        k = ops.rope(k, T, HKV, D, pos0)
+        ops.kv_store(il, k, v, pos0, T)
+        a = ops.attention(il, q, T, H, HKV, D, pos0)                # [T][H*D]
+        x = ops.add(ops.linear(ops.w(il, "wo"), a), x)
+        h = ops.mul(ops.rms_norm(x, cfg["eps"]), ops.w(il, "ffn_norm"))
+        up = ops.linear(ops.w(il, "w_up"), h)
+        gate = ops.linear(ops.w(il, "w_gate"), h)
+        x = ops.add(ops.linear(ops.w(il, "w_down"), ops.swiglu(gate, up)), x)
+    h = ops.mul(ops.rms_norm(ops.last_row(x), cfg["eps"]), ops.w(None, "output_norm"))
+    return ops.linear(ops.w(None, "output"), h)                    # [1][vocab]
+
+
+def generate(ops, cfg, prompt, n_gen):
+    """prefill the prompt in one batch, then greedy-decode n_gen tokens"""
+    logits = forward(ops, cfg, prompt, 0)
+    out = []
+    pos = len(prompt)
+    for _ in range(n_gen):
+        tok = ops.argmax(logits)
+        out.append(tok)
+        if len(out) == n_gen:
+            break
+        logits = forward(ops, cfg, [tok], pos)
+        pos += 1
+    return out
+
+
+class GpuOps:
+    """The graph's ops through liblnsb200_<mode>.so on one CUDA device (torch
+    for memory and the non-arithmetic reshapes)."""
+
+    def __init__(self, cfg, weights, mode="sum32", n_ctx=256, stream=None):
+        import torch
+        import lnsb200
+        self.torch, self.cfg, self.n_ctx = torch, cfg, n_ctx
+        self.ks = lnsb200.KernelSet(16, mode)
+        self.ks.upload_tables()
+        self.stream = stream
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        E = cfg["n_embd"]
+        kvd = cfg["n_head_kv"] * cfg["head_dim"]
+        self.tok_embd = torch.from_numpy(weights["tok_embd"]).to(self.dev)
+        self.lw = []
+        for L in weights["layers"]:
+            d = {}
+            for name in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"):
+                d[name] = self._weight(L[name])
+            for name in ("attn_norm", "ffn_norm"):
+                d[name] = torch.from_numpy(L[name]).to(self.dev)
+            self.lw.append(d)
+        self.gw = {"output_norm": torch.from_numpy(weights["output_norm"]).to(self.dev),
+                   "output": self._weight(weights["tok_embd"])}
+        self.kc = [torch.empty((n_ctx, kvd), dtype=torch.int16, device=self.dev) for _ in weights["layers"]]
+        self.vc = [torch.empty((n_ctx, kvd), dtype=torch.int16, device=self.dev) for _ in weights["layers"]]
+        self.rope_cs = torch.from_numpy(rope_table(n_ctx, cfg["head_dim"], cfg["rope_base"])).to(self.dev)
+        neg = np.full((n_ctx, n_ctx), -np.inf, np.float32)
+        self.mask_full = torch.from_numpy(np.triu(neg, 1)).to(self.dev)     # row q: 0 for k <= q
+        self.launches = 0
+
+    # weights: F32 rows [M][K] -> xlns16 codes k-major [K][M], once (the weight cache)
+    def _weight(self, rows):
+        torch = self.torch
+        M, K = rows.shape
+        src = torch.from_numpy(np.ascontiguousarray(rows)).to(self.dev)
+        dst = torch.empty(K * M, dtype=torch.int16, device=self.dev)
+        self.ks.to_lns_transposed(src, dst, M, K, M)
+        torch.cuda.synchronize()
+        return (dst, K, M)
+
+    def w(self, il, name):
+        return self.gw[name] if il is None else self.lw[il][name]
+
+    def _f32(self, *shape):
+        return self.torch.empty(shape, dtype=self.torch.float32, device=self.dev)
+
+    def embed(self, ids):
+        return self.tok_embd[self.torch.tensor(ids, device=self.dev)].contiguous()
+
+    def rms_norm(self, x, eps):
+        out = self._f32(*x.shape)
+        self.ks.rms_norm(x, out, x.shape[-1], x.numel() // x.shape[-1], eps, stream=self.stream)
+        self.launches += 1
+        return out
+
+    def mul(self, x, wv):
+        out = self._f32(*x.shape)
+        self.ks.binary("mul", x, (x.shape[-1], x.numel() // x.shape[-1]), wv, (wv.numel(),), out, stream=self.stream)
+        self.launches += 1
+        return out
+
+    def add(self, a, b):
+        out = self._f32(*a.shape)
+        self.ks.binary("add", a, (a.shape[-1], a.numel() // a.shape[-1]), b, (b.shape[-1], b.numel() // b.shape[-1]),
+                       out, stream=self.stream)
+        self.launches += 1
+        return out
+
+    def linear(self, wt, x):
+        codes, K, M = wt
+        N = x.numel() // K
+        xl = self.torch.empty(N * K, dtype=self.torch.int16, device=self.dev)
+        self.ks.to_lns(x, xl, stream=self.stream)
+        out = self._f32(N, M)
+        self.ks.mul_mat(codes, xl, out, K, M, N, stream=self.stream)
+        self.launches += 2
+        return out
+
+    def rope(self, x, T, nh, hd, pos0):
+        out = self._f32(T, nh * hd)
+        self.ks.rope(x, (hd, nh, T, 1), self.rope_cs[pos0:pos0 + T], hd, out, stream=self.stream)
+        self.launches += 1
+        return out
+
+    def kv_store(self, il, k, v, pos0, T):
+        n = k.numel()
+        self.ks.f32_to_f16(k, self.kc[il][pos0:pos0 + T], n, stream=self.stream)
+        self.ks.f32_to_f16(v, self.vc[il][pos0:pos0 + T], n, stream=self.stream)
+        self.launches += 2
+
+    def attention(self, il, q, T, H, HKV, D, pos0):
+        torch, ks = self.torch, self.ks
+        nkv = pos0 + T
+        # K and V of the cache, F16 -> F32 -> xlns16 codes, laid out as mul_mat weights per kv head:
+        # K: [h][dim][token] (reduce over dim), V: [h][token][dim] (reduce over tokens)
+        kf = self._f32(nkv, HKV * D)
+        vf = self._f32(nkv, HKV * D)
+        ks.f16_to_f32(self.kc[il][:nkv], kf, kf.numel(), stream=self.stream)
+        ks.f16_to_f32(self.vc[il][:nkv], vf, vf.numel(), stream=self.stream)
+        kh = kf.view(nkv, HKV, D).permute(1, 0, 2).contiguous()          # [h][token][dim] F32
+        vh = vf.view(nkv, HKV, D).permute(1, 0, 2).contiguous()
+        kl = torch.empty(HKV * D * nkv, dtype=torch.int16, device=self.dev)
+        vl = torch.empty(HKV * nkv * D, dtype=torch.int16, device=self.dev)
+        for h in range(HKV):
+            ks.to_lns_transposed(kh[h], kl[h * D * nkv:(h + 1) * D * nkv], nkv, D, nkv, stream=self.stream)
+        ks.to_lns(vh, vl, stream=self.stream)
+        # kq[h][t][k] = sum_d K[k][d] q[t][d], q head h on kv head h / (H / HKV)
+        qh = q.view(T, H, D).permute(1, 0, 2).contiguous()                # [h][t][dim]
+        ql = torch.empty(qh.numel(), dtype=torch.int16, device=self.dev)
+        ks.to_lns(qh, ql, stream=self.stream)
+        kq = self._f32(H, T, nkv)
+        ks.mul_mat(kl, ql, kq, D, nkv, T, (HKV, 1, H, 1), stream=self.stream)
+        # causal mask rows pos0 .. pos0+T-1, scale 1/sqrt(head_dim)
+        mask = self.mask_full[pos0:pos0 + T, :nkv].contiguous()
+        p = self._f32(H, T, nkv)
+        work = torch.empty(p.numel(), dtype=torch.int16, device=self.dev)
+        ks.soft_max(kq, (nkv, T, H, 1), p, work, mask, (nkv, T, 1, 1), 1.0 / math.sqrt(D), stream=self.stream)
+        # o[h][t][d] = sum_k V[k][d] p[h][t][k]
+        pl = torch.empty(p.numel(), dtype=torch.int16, device=self.dev)
+        ks.to_lns(p, pl, stream=self.stream)
+        o = self._f32(H, T, D)
+        ks.mul_mat(vl, pl, o, nkv, D, T, (HKV, 1, H, 1), stream=self.stream)
+        self.launches += 9 + HKV
+        return o.permute(1, 0, 2).contiguous().view(T, H * D)
+
+    def swiglu(self, gate, up):
+        out = self._f32(*gate.shape)
+        nc = gate.shape[-1]
+        self.ks.glu(gate, up, nc, nc, out, nc, gate.numel() // nc, stream=self.stream)
+        self.launches += 1
+        return out
+
+    def last_row(self, x):
+        return x[-1:].contiguous()
+
+    def argmax(self, logits):
+        return int(self.torch.argmax(logits.view(-1)).item())
+
+
+class OracleOps:
+    """The same ops on the CPU through the oracle (test infrastructure only:
+    the checker of GpuOps)."""
+
+    def __init__(self, cfg, weights, mode="sum32", n_ctx=256, nthreads=8):
+        import oracle
+        self.o, self.cfg, self.mode, self.nt = oracle, cfg, mode, nthreads
+        self.weights = weights
+        self.wc = {}
+        kvd = cfg["n_head_kv"] * cfg["head_dim"]
+        self.kc = [np.zeros((n_ctx, kvd), np.float16) for _ in weights["layers"]]
+        self.vc = [np.zeros((n_ctx, kvd), np.float16) for _ in weights["layers"]]
+        self.rope_cs = rope_table(n_ctx, cfg["head_dim"], cfg["rope_base"])
+
+    def w(self, il, name):
+        key = (il, name)
+        if key not in self.wc:
+            if il is None:
+                v = self.weights["tok_embd"] if name == "output" else self.weights[name]
+            else:
+                v = self.weights["layers"][il][name]
+            if v.ndim == 2:
+                v = self.o.from_f32_16(v)                      # weight codes, rows [M][K]
+            self.wc[key] = v
+        return self.wc[key]
+
+    def embed(self, ids):
+        return self.weights["tok_embd"][ids].copy()
+
+    def rms_norm(self, x, eps):
+        c = self.o.from_f32_16(x)
+        r = self.o.rms_norm16(self.mode, c.ravel(), x.shape[-1], x.size // x.shape[-1], eps, nthreads=self.nt)
+        return self.o.to_f32_16(r).reshape(x.shape)
+
+    def mul(self, x, wv):
+        return self.o.binary16("mul", x, wv.reshape(1, -1))
+
+    def add(self, a, b):
+        return self.o.binary16("add", a, b)
+
+    def linear(self, w, x):
+        xc = self.o.from_f32_16(x.reshape(-1, w.shape[1]))
+        return self.o.to_f32_16(self.o.mul_mat16(self.mode, w, xc, nthreads=self.nt)).reshape(-1, w.shape[0])
+
+    def rope(self, x, T, nh, hd, pos0):
+        return self.o.rope16(x.reshape(1, T, nh, hd), self.rope_cs[pos0:pos0 + T], hd).reshape(T, nh * hd)
+
+    def kv_store(self, il, k, v, pos0, T):
+        self.kc[il][pos0:pos0 + T] = k.astype(np.float16)
+        self.vc[il][pos0:pos0 + T] = v.astype(np.float16)
+
+    def attention(self, il, q, T, H, HKV, D, pos0):
+        o = self.o
+        nkv = pos0 + T
+        kf = self.kc[il][:nkv].astype(np.float32).reshape(nkv, HKV, D)
+        vf = self.vc[il][:nkv].astype(np.float32).reshape(nkv, HKV, D)
+        kw = o.from_f32_16(np.ascontiguousarray(kf.transpose(1, 0, 2)))          # [h][token][dim]: rows M=token, K=dim
+        vw = o.from_f32_16(np.ascontiguousarray(vf.transpose(1, 2, 0)))          # [h][dim][token]: rows M=dim, K=token
+        qc = o.from_f32_16(np.ascontiguousarray(q.reshape(T, H, D).transpose(1, 0, 2)))
+        kq = o.to_f32_16(o.mul_mat16(self.mode, kw.reshape(1, HKV, nkv, D), qc.reshape(1, H, T, D),
+                                     slices=(HKV, 1, H, 1), nthreads=self.nt)).reshape(H, T, nkv)
+        m = np.triu(np.full((T + pos0, T + pos0), -np.inf, np.float32), 1)[pos0:pos0 + T, :nkv]
+        sc = int(o.from_f32_16(np.array([1.0 / math.sqrt(D)], np.float32))[0])
+        p = o.to_f32_16(o.soft_max16(self.mode, o.from_f32_16(kq).ravel(), (nkv, T, H, 1), o.mask16(m).ravel(),
+                                     (nkv, T, 1, 1), sc, nthreads=self.nt)).reshape(H, T, nkv)
+        out = o.to_f32_16(o.mul_mat16(self.mode, vw.reshape(1, HKV, D, nkv), o.from_f32_16(p).reshape(1, H, T, nkv),
+                                      slices=(HKV, 1, H, 1), nthreads=self.nt)).reshape(H, T, D)
+        return np.ascontiguousarray(out.transpose(1, 0, 2)).reshape(T, H * D)
+
+    def swiglu(self, gate, up):
+        return self.o.swiglu16(gate, up)
+
+    def last_row(self, x):
+        return x[-1:].copy()
+
+    def argmax(self, logits):
+        return int(np.argmax(logits.ravel()))
