@@ -59,6 +59,8 @@ def parse():
     p.add_argument("--sweep-k", type=int, default=4096, help="configs4: K in {2048, 4096, 8192, 14336}")
     p.add_argument("--sweep-n", type=int, default=16, help="configs4: tokens in {1, 16, 128}")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-decode", action="store_true", help="skip the model decode measurement")
+    p.add_argument("--decode-mode", default="sum32", help="sum mode of the decode (BASELINE configs[2]: sum32)")
     return p.parse_args()
 
 
@@ -364,6 +366,9 @@ def run_ours(args, wl):
     if world == 1 and args.workload == "configs1":
         # BASELINE's metric is quoted at K=1536: configs[0], timed the same way, beside the main line
         line["k1536"] = time_secondary(lib, lnsb200, torch, np, WORKLOADS["configs0"], args, flush, stream)
+    if args.workload == "configs1" and not args.no_decode:
+        # the metric's second half: model decode tok/s, one sequence per GPU
+        line["decode"] = run_decode(torch, dist, rank, world, args, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not strong:
         line["cpu_baseline"] = cpu_leg(wl, args.mode, 10.0, os.cpu_count() or 1)
     if rank == 0:
@@ -407,6 +412,63 @@ def time_secondary(lib, lnsb200, torch, np, wl, args, flush, stream):
             "value": adds / (ms / 1000) / 1e9, "unit": UNIT,
             "bound": "chain latency: %d dependent additions per output" % (K - 1),
             "l2": "flushed (256 MB write) before every timed step"}
+
+
+def run_decode(torch, dist, rank, world, args, cpu=False):
+    """SmolLM2-135M-shaped random-init Llama, LNS16 in the
+    decode sum mode, 128-token prompt prefill then 128-token greedy decode, one
+    independent sequence per GPU (prompt seed 2 + rank).  Device-timed with
+    events; each step's token goes back to the host (greedy argmax) and the
+    next token id comes from it, so the decode is end to end.  The time is the
+    max over ranks; tok/s counts every rank's tokens."""
+    import lnsb200.model as model
+    cfg = model.SMOLLM2_135M
+    w = model.init_weights(cfg, seed=2)
+    g = model.GpuOps(cfg, w, mode=args.decode_mode, n_ctx=256)
+    prompt = model.prompt_ids(cfg, 128, seed=2 + rank)
+    stream = torch.cuda.current_stream()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    model.forward(g, cfg, prompt[:8], 0)                 # warm-up (also fills the allocator)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e[0].record(stream)
+    logits = model.forward(g, cfg, prompt, 0)
+    toks = [g.argmax(logits)]
+    e[1].record(stream)
+    pos = len(prompt)
+    for _ in range(127):
+        logits = model.forward(g, cfg, [toks[-1]], pos)
+        toks.append(g.argmax(logits))
+        pos += 1
+    e[2].record(stream)
+    torch.cuda.synchronize()
+    pre_ms, dec_ms = e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])
+    if dist:
+        t = torch.tensor([pre_ms, dec_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pre_ms, dec_ms = t.tolist()
+    out = {"model": "SmolLM2-135M shape (30 layers, d 576, 9/3 heads, ffn 1536, vocab 49152), random N(0,0.02) weights seed 2",
+           "mode": args.decode_mode, "prompt": 128, "generated": 128, "sequences": world,
+           "prefill_tok_per_s": world * 128 / (pre_ms / 1000), "decode_tok_per_s": world * 127 / (dec_ms / 1000),
+           "ms_per_token": dec_ms / 127, "prefill_ms": pre_ms,
+           "timing": "device events; one greedy token per step read back to the host",
+           "first_tokens": toks[:8]}
+    if cpu:
+        # the CPU oracle (the reference's algorithm, host cores) on a bounded sample:
+        # prefill of 8 tokens, then 2 decode steps
+        import time
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        o = model.OracleOps(cfg, w, mode=args.decode_mode, n_ctx=16, nthreads=os.cpu_count() or 1)
+        lo = model.forward(o, cfg, prompt[:8], 0)
+        t0 = time.perf_counter()
+        tk = o.argmax(lo)
+        for p in range(8, 10):
+            tk = o.argmax(model.forward(o, cfg, [tk], p))
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"decode_tok_per_s": 2 / dt, "cores": os.cpu_count() or 1, "kind": "port",
+                               "sample": "oracle model: 8-token prefill, then 2 decode steps timed (%.1f s)" % dt}
+    return out
 
 
 def main():

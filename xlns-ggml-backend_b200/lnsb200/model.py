@@ -85,17 +85,14 @@ def forward(ops, cfg, ids, pos0):
     x = ops.embed(ids)                                              # [T][E]
     for il in range(cfg["n_layer"]):
         h = ops.mul(ops.rms_norm(x, cfg["eps"]), ops.w(il, "attn_norm"))
-        q = ops.linear(ops.w(il, "wq"), h)                          # [T][H*D]
-        k = ops.linear(ops.w(il, "wk"), h)                          # [T][HKV*D]
-        v = ops.linear(ops.w(il, "wv"), h)
+        q, k, v = ops.linears(il, ("wq", "wk", "wv"), h)            # [T][H*D], [T][HKV*D] x 2
         q = ops.rope(q, T, H, D, pos0)
         k = ops.rope(k, T, HKV, D, pos0)
         ops.kv_store(il, k, v, pos0, T)
         a = ops.attention(il, q, T, H, HKV, D, pos0)                # [T][H*D]
         x = ops.add(ops.linear(ops.w(il, "wo"), a), x)
         h = ops.mul(ops.rms_norm(x, cfg["eps"]), ops.w(il, "ffn_norm"))
-        up = ops.linear(ops.w(il, "w_up"), h)
-        gate = ops.linear(ops.w(il, "w_gate"), h)
+        up, gate = ops.linears(il, ("w_up", "w_gate"), h)
         x = ops.add(ops.linear(ops.w(il, "w_down"), ops.swiglu(gate, up)), x)
     h = ops.mul(ops.rms_norm(ops.last_row(x), cfg["eps"]), ops.w(None, "output_norm"))
     return ops.linear(ops.w(None, "output"), h)                    # [1][vocab]
@@ -133,8 +130,13 @@ class GpuOps:
         self.tok_embd = torch.from_numpy(weights["tok_embd"]).to(self.dev)
         self.lw = []
         for L in weights["layers"]:
-            d = {}
-            for name in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"):
+            # q/k/v and up/gate share their input: one mul_mat over the stacked
+            # rows computes the same chains (each output is its own reduction)
+            d = {"qkv": self._weight(np.concatenate([L["wq"], L["wk"], L["wv"]])),
+                 "upgate": self._weight(np.concatenate([L["w_up"], L["w_gate"]])),
+                 "split": {("wq", "wk", "wv"): [L["wq"].shape[0], L["wk"].shape[0], L["wv"].shape[0]],
+                           ("w_up", "w_gate"): [L["w_up"].shape[0], L["w_gate"].shape[0]]}}
+            for name in ("wo", "w_down"):
                 d[name] = self._weight(L[name])
             for name in ("attn_norm", "ffn_norm"):
                 d[name] = torch.from_numpy(L[name]).to(self.dev)
@@ -195,6 +197,15 @@ class GpuOps:
         self.ks.mul_mat(codes, xl, out, K, M, N, stream=self.stream)
         self.launches += 2
         return out
+
+    def linears(self, il, names, x):
+        key = "qkv" if names[0] == "wq" else "upgate"
+        y = self.linear(self.lw[il][key], x)
+        outs, c = [], 0
+        for m in self.lw[il]["split"][tuple(names)]:
+            outs.append(y[:, c:c + m].contiguous())
+            c += m
+        return outs
 
     def rope(self, x, T, nh, hd, pos0):
         out = self._f32(T, nh * hd)
@@ -300,6 +311,9 @@ class OracleOps:
     def linear(self, w, x):
         xc = self.o.from_f32_16(x.reshape(-1, w.shape[1]))
         return self.o.to_f32_16(self.o.mul_mat16(self.mode, w, xc, nthreads=self.nt)).reshape(-1, w.shape[0])
+
+    def linears(self, il, names, x):
+        return [self.linear(self.w(il, n), x) for n in names]
 
     def rope(self, x, T, nh, hd, pos0):
         return self.o.rope16(x.reshape(1, T, nh, hd), self.rope_cs[pos0:pos0 + T], hd).reshape(T, nh * hd)
