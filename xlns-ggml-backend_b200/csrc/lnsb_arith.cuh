@@ -413,6 +413,25 @@ __host__ __device__ __forceinline__ uint32_t lpvip_sing(const int32_t * lpvip_db
     return (mx & 0x80000000u) | (uint32_t) (p > 0 ? p : 0);
 }
 
+// ===================== additions of non-negative terms =====================
+// The normalisers sum non-negative terms only (squares in rms_norm, exp values
+// in soft_max), so their chains never take db, the cotransformation or the
+// exact cancellation: for a, b >= 0 these are add16 and add32 exactly.
+// tab: the sbdb16 image; F: a flat xlns32 image whose sb knots and
+// descriptors are filled (the rest is never read here).
+__device__ __forceinline__ uint32_t padd16(uint32_t a, uint32_t b, const int16_t * tab) {
+    const int d = abs((int) a - (int) b);
+    const int adj = tab[min(d, k16_ess + 1)] >> 1;
+    return (uint32_t) min(max((int) a, (int) b) + adj, 0x7FFF);
+}
+__device__ __forceinline__ uint32_t padd32f(const int32_t * F, uint32_t a, uint32_t b) {
+    const uint32_t d  = a > b ? a - b : b - a;
+    const uint32_t mx = a > b ? a : b;
+    const uint32_t z  = d < k32_ess ? d : k32_ess;
+    const uint32_t r  = mx + (uint32_t) interp32f(F, z, (int) (z >> 23));
+    return (int32_t) r < 0 ? 0x7FFFFFFFu : r;                      // saturation: the carry into bit 31
+}
+
 // ============================== Monte ======================================
 
 __device__ __forceinline__ uint32_t lfsr_step(uint32_t s) { return (s >> 1) ^ ((s & 1u) ? 0xB400u : 0u); }

@@ -1178,21 +1178,45 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
 }
 
 // ============================ RMS_NORM =====================================
-// Block = 32 rows.  Each lane runs its row's sum-of-squares chain (n additions
-// from zero); the scaling pass is done by the whole block, coalesced.
+// Block = up to 32 rows (rpb).  Each lane runs its row's sum-of-squares chain
+// (n additions from zero); the scaling pass is done by the whole block,
+// coalesced.  In base and sum32 modes (NNCHAIN) the squares are first formed
+// by the whole block into shared memory and the chain is the non-negative
+// addition over a shared-memory table (padd16 / padd32f); the other modes
+// run the general reduction policy.
+constexpr bool NNCHAIN = k_mode == M_BASE || k_mode == M_SUM32;
+constexpr int  NN_TAB  = k_mode == M_SUM32 ? k32f_words * 4 : 0;   // flat image bytes in dynamic smem
+
+// the sb knots and the descriptors of the flat xlns32 image (all a
+// non-negative chain reads) into shared memory at their flat-image offsets
+__device__ __forceinline__ void nn_tables(const dev_tables & T, int32_t * F) {
+    if constexpr (k_mode == M_SUM32) {
+        for (int i = threadIdx.x; i < k32f_db; i += blockDim.x) F[i] = __ldg(T.flat32 + i);
+        for (int i = k32f_dsc2 + threadIdx.x; i < k32f_words; i += blockDim.x) F[i] = __ldg(T.flat32 + i);
+    }
+}
+// one non-negative addition of the mode: accumulator form (sum32: acc32) and term code
+__device__ __forceinline__ uint32_t nn_add(const int32_t * F, const int16_t * tab, uint32_t acc, uint32_t t) {
+    if constexpr (k_mode == M_SUM32) return padd32f(F, acc, t << 16);
+    else                             return padd16(acc, t, tab);
+}
+
 template <int FMT, bool IO_F32>
 __global__ void __launch_bounds__(128)
 k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst, int64_t ncols, int64_t nrows,
-           uint32_t eps_l, uint32_t inv_n, uint32_t monte_seed) {
+           uint32_t eps_l, uint32_t inv_n, uint32_t monte_seed, int rpb, int nn_ok) {
     __shared__ int16_t  tab[k16_tab_bytes / 2];
     __shared__ int16_t  fine[k_mode == M_MONTE ? 2 * k16_monte_n : 2];
     __shared__ uint32_t s_inv[32];
+    extern __shared__ __align__(16) int32_t dyn[];          // NNCHAIN: [flat image (sum32)][squares: rpb x ncols]
+    constexpr bool NNC = FMT == 16 && NNCHAIN;
+    const bool     NN  = NNC && nn_ok != 0;                 // the squares fit in shared memory
     if constexpr (FMT == 16) {
         for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += blockDim.x) tab[i] = T.sbdb16[i];
         if constexpr (k_mode == M_MONTE) for (int i = threadIdx.x; i < 2 * k16_monte_n; i += blockDim.x) fine[i] = T.monte16[i];
     }
-    __syncthreads();
-    const int64_t row0 = (int64_t) blockIdx.x * 32;
+    const int64_t row0 = (int64_t) blockIdx.x * rpb;
+    const int64_t nr = imin64(rpb, nrows - row0);
     auto load = [&](int64_t idx) -> uint32_t {
         if constexpr (IO_F32) {
             const float f = static_cast<const float *>(src)[idx];
@@ -1201,32 +1225,45 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
             return FMT == 16 ? (uint32_t) static_cast<const uint16_t *>(src)[idx] : static_cast<const uint32_t *>(src)[idx];
         }
     };
-    if (threadIdx.x < 32) {
-        const int64_t row = row0 + threadIdx.x;
-        if (row < nrows) {
-            if constexpr (FMT == 16) {
-                red16 R{ &T, tab, fine };
-                uint32_t st = k_stochastic ? lfsr_jump(T, monte_seed, (unsigned long long) row * (unsigned long long) ncols) : 0u;
-                uint32_t acc = R.from(0u);
-                for (int64_t i = 0; i < ncols; i++) {
-                    const uint32_t v = load(row * ncols + i);
-                    acc = R.add(acc, mul16(v, v), st);
-                }
-                const uint32_t mean = mul16(R.finish(acc), inv_n);
-                s_inv[threadIdx.x] = recip16(sqrt16(add16(mean, eps_l, tab)));
-            } else {
-                uint32_t acc = 0u;
-                for (int64_t i = 0; i < ncols; i++) {
-                    const uint32_t v = load(row * ncols + i);
-                    acc = add32(T, acc, mul32(v, v));
-                }
-                const uint32_t mean = mul32(acc, inv_n);
-                s_inv[threadIdx.x] = recip32(sqrt32(add32(T, mean, eps_l)));
-            }
+    uint16_t * sq = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + NN_TAB);
+    if (NN) {
+        nn_tables(T, dyn);
+        for (int64_t e = threadIdx.x; e < nr * ncols; e += blockDim.x) {
+            const uint32_t v = load(row0 * ncols + e);
+            sq[e] = (uint16_t) mul16(v, v);
         }
     }
     __syncthreads();
-    const int64_t nr = imin64(32, nrows - row0);
+    if (threadIdx.x < nr) {
+        const int64_t row = row0 + threadIdx.x;
+        if (NN) {
+            const uint16_t * q = sq + threadIdx.x * ncols;
+            uint32_t acc = 0u;                              // the zero code (acc32 0 in sum32)
+            for (int64_t i = 0; i < ncols; i++) acc = nn_add(dyn, tab, acc, q[i]);
+            red16 R{ &T, tab, fine };
+            const uint32_t mean = mul16(R.finish(acc), inv_n);
+            s_inv[threadIdx.x] = recip16(sqrt16(add16(mean, eps_l, tab)));
+        } else if constexpr (FMT == 16) {
+            red16 R{ &T, tab, fine };
+            uint32_t st = k_stochastic ? lfsr_jump(T, monte_seed, (unsigned long long) row * (unsigned long long) ncols) : 0u;
+            uint32_t acc = R.from(0u);
+            for (int64_t i = 0; i < ncols; i++) {
+                const uint32_t v = load(row * ncols + i);
+                acc = R.add(acc, mul16(v, v), st);
+            }
+            const uint32_t mean = mul16(R.finish(acc), inv_n);
+            s_inv[threadIdx.x] = recip16(sqrt16(add16(mean, eps_l, tab)));
+        } else {
+            uint32_t acc = 0u;
+            for (int64_t i = 0; i < ncols; i++) {
+                const uint32_t v = load(row * ncols + i);
+                acc = add32(T, acc, mul32(v, v));
+            }
+            const uint32_t mean = mul32(acc, inv_n);
+            s_inv[threadIdx.x] = recip32(sqrt32(add32(T, mean, eps_l)));
+        }
+    }
+    __syncthreads();
     for (int64_t e = threadIdx.x; e < nr * ncols; e += blockDim.x) {
         const int64_t r = e / ncols;
         const int64_t idx = (row0 + r) * ncols + (e - r * ncols);
@@ -1253,7 +1290,8 @@ template <int FMT, bool IO_F32>
 __global__ void __launch_bounds__(128)
 k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const void * __restrict__ mask,
            lnsb_shape4 ms, uint32_t scale_l, void * __restrict__ dst, void * __restrict__ work,
-           uint32_t monte_seed) {
+           uint32_t monte_seed, int rpb, int nn_ok) {
+    extern __shared__ __align__(16) int32_t dyn[];          // NNCHAIN: [flat image (sum32)][exp terms: rpb x n]
     __shared__ int16_t  tab[k16_tab_bytes / 2];
     __shared__ int16_t  fine[k_mode == M_MONTE ? 2 * k16_monte_n : 2];
     __shared__ uint32_t s_max[32][4];
@@ -1266,8 +1304,8 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     __syncthreads();
     const int64_t n = s.ne[0];
     const int64_t nrows = s.ne[1] * s.ne[2] * s.ne[3];
-    const int64_t row0 = (int64_t) blockIdx.x * 32;
-    const int64_t nr = imin64(32, nrows - row0);
+    const int64_t row0 = (int64_t) blockIdx.x * rpb;
+    const int64_t nr = imin64(rpb, nrows - row0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     auto ld = [&](const void * p, int64_t idx) -> uint32_t {
@@ -1316,14 +1354,22 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         if (lane == 0) s_max[r][0] = mx;
     }
     __syncthreads();
-    // pass 2: c = exp(v - max) into work
+    // pass 2: c = exp(v - max) into work (and, for the non-negative chain, shared memory)
+    const bool NN = FMT == 16 && NNCHAIN && nn_ok != 0;
+    uint16_t * cs = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + NN_TAB);
+    if (NN) nn_tables(T, dyn);
     for (int r = warp; r < nr; r += 4) {
         const int64_t row = row0 + r;
         const uint32_t mx = s_max[r][0];
         for (int64_t i = lane; i < n; i += 32) {
             const uint32_t v = value(row, i);
-            if constexpr (FMT == 16) static_cast<uint16_t *>(work)[row * n + i] = __ldg(T.exp16 + sub16(v, mx, tab));
-            else                     static_cast<uint32_t *>(work)[row * n + i] = exp32(T, sub32(T, v, mx));
+            if constexpr (FMT == 16) {
+                const uint16_t e = __ldg(T.exp16 + sub16(v, mx, tab));
+                static_cast<uint16_t *>(work)[row * n + i] = e;
+                if (NN) cs[r * n + i] = e;
+            } else {
+                static_cast<uint32_t *>(work)[row * n + i] = exp32(T, sub32(T, v, mx));
+            }
         }
     }
     __syncthreads();
@@ -1331,7 +1377,13 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     if (threadIdx.x < nr) {
         const int64_t row = row0 + threadIdx.x;
         const void * c = work;
-        if constexpr (FMT == 16) {
+        if (NN) {
+            const uint16_t * q = cs + threadIdx.x * n;
+            red16 R{ &T, tab, fine };
+            uint32_t acc = R.from(q[0]);
+            for (int64_t i = 1; i < n; i++) acc = nn_add(dyn, tab, acc, q[i]);
+            s_tot[threadIdx.x] = R.finish(acc);
+        } else if constexpr (FMT == 16) {
             red16 R{ &T, tab, fine };
             uint32_t st = k_stochastic ? lfsr_jump(T, monte_seed, (unsigned long long) row * (unsigned long long) (n - 1)) : 0u;
             uint32_t acc = R.from(ld(c, row * n));
@@ -1623,6 +1675,24 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
     return launch_status();
 }
 
+constexpr int NN_SMEM_MAX = 200 * 1024;      // dynamic shared memory of a normaliser block, at most
+
+// raises a kernel's dynamic shared memory limit once per device and kernel
+int nn_smem_attr(const void * kern, int bytes) {
+    if (bytes <= 48 * 1024) return 0;
+    int dev = 0;
+    const int ds = current_device(&dev);
+    if (ds != 0) return ds;
+    static std::mutex mu;
+    static std::array<std::vector<std::pair<const void *, int>>, k_max_devices> done;
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto & e : done[dev]) if (e.first == kern && e.second >= bytes) return 0;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, NN_SMEM_MAX);
+    if (e != cudaSuccess) return (int) e;
+    done[dev].push_back({ kern, NN_SMEM_MAX });
+    return 0;
+}
+
 int rms_norm_impl(int fmt, const void * src, void * dst, int64_t ncols, int64_t nrows, float eps, uint16_t seed,
                   bool io_f32, cudaStream_t stream) {
     if (!valid_fmt(fmt) || ncols < 0 || nrows < 0) return LNSB_E_INVALID;
@@ -1642,13 +1712,25 @@ int rms_norm_impl(int fmt, const void * src, void * dst, int64_t ncols, int64_t 
         eps_l = host_from_f32_32(eps);
         inv_n = host_from_f32_32(invf);
     }
-    const unsigned blocks = (unsigned) ((nrows + 31) / 32);
+    // non-negative chains over shared memory (base, sum32): the block's squares must fit
+    int rpb = 32, nn_ok = 0, dsmem = 0;
+    if (fmt == LNSB_XLNS16 && NNCHAIN) {
+        const int64_t fit = (NN_SMEM_MAX - NN_TAB) / (ncols * 2);
+        if (fit >= 1) {
+            rpb = (int) imin64(32, fit);
+            nn_ok = 1;
+            dsmem = NN_TAB + (int) (((int64_t) rpb * ncols * 2 + 15) / 16 * 16);
+        }
+    }
+    const unsigned blocks = (unsigned) ((nrows + rpb - 1) / rpb);
     if (fmt == LNSB_XLNS16) {
-        if (io_f32) k_rms_norm<16, true><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed);
-        else        k_rms_norm<16, false><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed);
+        auto kern = io_f32 ? k_rms_norm<16, true> : k_rms_norm<16, false>;
+        const int st2 = nn_smem_attr((const void *) kern, dsmem);
+        if (st2 != 0) return st2;
+        kern<<<blocks, 128, dsmem, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, nn_ok);
     } else {
-        if (io_f32) k_rms_norm<32, true><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed);
-        else        k_rms_norm<32, false><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed);
+        if (io_f32) k_rms_norm<32, true><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, 0);
+        else        k_rms_norm<32, false><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, 0);
     }
     return launch_status();
 }
@@ -1668,13 +1750,24 @@ int soft_max_impl(int fmt, const void * src, lnsb_shape4 s, const void * mask, l
     const dev_tables * T = nullptr;
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
-    const unsigned blocks = (unsigned) ((nrows + 31) / 32);
+    int rpb = 32, nn_ok = 0, dsmem = 0;
+    if (fmt == LNSB_XLNS16 && NNCHAIN) {
+        const int64_t fit = (NN_SMEM_MAX - NN_TAB) / (s.ne[0] * 2);
+        if (fit >= 1) {
+            rpb = (int) imin64(32, fit);
+            nn_ok = 1;
+            dsmem = NN_TAB + (int) (((int64_t) rpb * s.ne[0] * 2 + 15) / 16 * 16);
+        }
+    }
+    const unsigned blocks = (unsigned) ((nrows + rpb - 1) / rpb);
     if (fmt == LNSB_XLNS16) {
-        if (io_f32) k_soft_max<16, true><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed);
-        else        k_soft_max<16, false><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed);
+        auto kern = io_f32 ? k_soft_max<16, true> : k_soft_max<16, false>;
+        const int st2 = nn_smem_attr((const void *) kern, dsmem);
+        if (st2 != 0) return st2;
+        kern<<<blocks, 128, dsmem, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed, rpb, nn_ok);
     } else {
-        if (io_f32) k_soft_max<32, true><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed);
-        else        k_soft_max<32, false><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed);
+        if (io_f32) k_soft_max<32, true><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed, rpb, 0);
+        else        k_soft_max<32, false><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed, rpb, 0);
     }
     return launch_status();
 }
