@@ -429,6 +429,8 @@ def run_decode(torch, dist, rank, world, args, cpu=False):
     stream = torch.cuda.current_stream()
     e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     model.forward(g, cfg, prompt[:8], 0)                 # warm-up (also fills the allocator)
+    dec = model.GraphDecoder(g, cfg)                     # one CUDA graph per decode position,
+    dec.prepare(len(prompt), len(prompt) + 127)          # captured once before the timed region
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -436,11 +438,7 @@ def run_decode(torch, dist, rank, world, args, cpu=False):
     logits = model.forward(g, cfg, prompt, 0)
     toks = [g.argmax(logits)]
     e[1].record(stream)
-    pos = len(prompt)
-    for _ in range(127):
-        logits = model.forward(g, cfg, [toks[-1]], pos)
-        toks.append(g.argmax(logits))
-        pos += 1
+    toks += dec.decode(toks[0], len(prompt), 127)       # each step's token copied to pinned host memory
     e[2].record(stream)
     torch.cuda.synchronize()
     pre_ms, dec_ms = e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])
@@ -452,7 +450,7 @@ def run_decode(torch, dist, rank, world, args, cpu=False):
            "mode": args.decode_mode, "prompt": 128, "generated": 128, "sequences": world,
            "prefill_tok_per_s": world * 128 / (pre_ms / 1000), "decode_tok_per_s": world * 127 / (dec_ms / 1000),
            "ms_per_token": dec_ms / 127, "prefill_ms": pre_ms,
-           "timing": "device events; one greedy token per step read back to the host",
+           "timing": "device events; prefill eager, decode as one CUDA graph per position (captured before the timed region); each step's greedy token is copied to pinned host memory",
            "first_tokens": toks[:8]}
     if cpu:
         # the CPU oracle (the reference's algorithm, host cores) on a bounded sample:

@@ -55,3 +55,19 @@ def test_generate_matches_forward_loop():
     toks = model.generate(g, SMALL, prompt, 6)
     o = model.OracleOps(SMALL, w, mode="sum32", n_ctx=32)
     assert toks == model.generate(o, SMALL, prompt, 6)
+
+
+def test_graph_decode_matches_eager():
+    """CUDA-graph decode (one graph per position) gives the eager path's tokens"""
+    from lnsb200 import model
+    w = model.init_weights(SMALL, seed=2)
+    prompt = model.prompt_ids(SMALL, 5, seed=2)
+    g = model.GpuOps(SMALL, w, mode="sum32", n_ctx=32)
+    eager = model.generate(g, SMALL, prompt, 7)
+    g2 = model.GpuOps(SMALL, w, mode="sum32", n_ctx=32)
+    first = g2.argmax(model.forward(g2, SMALL, prompt, 0))
+    dec = model.GraphDecoder(g2, SMALL)
+    dec.prepare(len(prompt), len(prompt) + 6)
+    # capturing does not run the graphs; the cache still holds only the prompt
+    toks = dec.decode(first, len(prompt), 6)
+    assert [first] + toks == eager

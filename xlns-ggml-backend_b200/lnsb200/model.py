@@ -80,7 +80,7 @@ def rope_table(n_ctx, n_dims, base):
 def forward(ops, cfg, ids, pos0):
     """logits (F32, [vocab]) of the last of `ids`, which sit at positions
     pos0 .. pos0 + len(ids) - 1; the KV cache holds positions < pos0."""
-    T, E = len(ids), cfg["n_embd"]
+    T, E = (ids.numel() if hasattr(ids, "numel") else len(ids)), cfg["n_embd"]
     H, HKV, D = cfg["n_head"], cfg["n_head_kv"], cfg["head_dim"]
     x = ops.embed(ids)                                              # [T][E]
     for il in range(cfg["n_layer"]):
@@ -167,6 +167,8 @@ class GpuOps:
         return self.torch.empty(shape, dtype=self.torch.float32, device=self.dev)
 
     def embed(self, ids):
+        if isinstance(ids, self.torch.Tensor):                          # token ids already on the device
+            return self.tok_embd.index_select(0, ids.view(-1)).contiguous()
         return self.tok_embd[self.torch.tensor(ids, device=self.dev)].contiguous()
 
     def rms_norm(self, x, eps):
@@ -266,6 +268,50 @@ class GpuOps:
 
     def argmax(self, logits):
         return int(self.torch.argmax(logits.view(-1)).item())
+
+
+class GraphDecoder:
+    """Greedy decode with one CUDA graph per position: the step at position
+    pos (embedding of the current token, the 30 layers, the output matmul,
+    argmax into the device token, and the token's copy to pinned host memory)
+    is captured once and replayed, so a decode step costs no host work.  The
+    kernels and their order are those of the eager path."""
+
+    def __init__(self, ops, cfg):
+        import torch
+        self.torch, self.ops, self.cfg = torch, ops, cfg
+        self.tok = torch.zeros(1, dtype=torch.int64, device=ops.dev)
+        self.host = torch.zeros(ops.n_ctx, dtype=torch.int64).pin_memory()
+        self.graphs = {}
+
+    def capture(self, pos):
+        torch = self.torch
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            logits = forward(self.ops, self.cfg, self.tok, pos)
+            self.tok.copy_(torch.argmax(logits.view(-1)).view(1))
+            self.host[pos:pos + 1].copy_(self.tok, non_blocking=True)
+        self.graphs[pos] = g
+
+    def prepare(self, pos_from, pos_to):
+        """capture the steps at positions pos_from .. pos_to - 1 (after one eager
+        step has set every kernel's launch attributes)"""
+        # one eager step first, at the last position (its cache slot is written
+        # again by that position's own step before anything reads it), so no
+        # kernel's first-use setup falls inside a capture
+        forward(self.ops, self.cfg, self.tok, pos_to - 1)
+        self.torch.cuda.synchronize()
+        for p in range(pos_from, pos_to):
+            if p not in self.graphs:
+                self.capture(p)
+
+    def decode(self, first_token, pos_from, n):
+        """n tokens: first_token is the one the prefill produced (at pos_from)"""
+        self.tok.fill_(first_token)
+        for p in range(pos_from, pos_from + n):
+            self.graphs[p].replay()
+        self.torch.cuda.current_stream().synchronize()
+        return [int(v) for v in self.host[pos_from:pos_from + n]]
 
 
 class OracleOps:
