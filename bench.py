@@ -369,6 +369,10 @@ def run_ours(args, wl):
     if args.workload == "configs1" and not args.no_decode:
         # the metric's second half: model decode tok/s, one sequence per GPU
         line["decode"] = run_decode(torch, dist, rank, world, args, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
+        if world == 1:
+            # the same model and prompt in LNS32, on 1 GPU
+            line["decode_lns32"] = run_decode(torch, dist, rank, world, args,
+                                              cpu=(rank == 0 and not args.no_cpu_baseline), fmt=32)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not strong:
         line["cpu_baseline"] = cpu_leg(wl, args.mode, 10.0, os.cpu_count() or 1)
     if rank == 0:
@@ -414,17 +418,18 @@ def time_secondary(lib, lnsb200, torch, np, wl, args, flush, stream):
             "l2": "flushed (256 MB write) before every timed step"}
 
 
-def run_decode(torch, dist, rank, world, args, cpu=False):
-    """SmolLM2-135M-shaped random-init Llama, LNS16 in the
-    decode sum mode, 128-token prompt prefill then 128-token greedy decode, one
-    independent sequence per GPU (prompt seed 2 + rank).  Device-timed with
-    events; each step's token goes back to the host (greedy argmax) and the
-    next token id comes from it, so the decode is end to end.  The time is the
-    max over ranks; tok/s counts every rank's tokens."""
+def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16):
+    """BASELINE configs[2] (fmt 16) and configs[3] (fmt 32): SmolLM2-135M-shaped
+    random-init Llama, LNS16 in the decode sum mode or LNS32, 128-token prompt
+    prefill then 128-token greedy decode, one independent sequence per GPU
+    (prompt seed 2 + rank).  Device-timed with events; each step's token goes
+    back to the host (greedy argmax) and the next token id comes from it, so
+    the decode is end to end.  The time is the max over ranks; tok/s counts
+    every rank's tokens."""
     import lnsb200.model as model
     cfg = model.SMOLLM2_135M
     w = model.init_weights(cfg, seed=2)
-    g = model.GpuOps(cfg, w, mode=args.decode_mode, n_ctx=256)
+    g = model.GpuOps(cfg, w, mode=args.decode_mode, n_ctx=256, fmt=fmt)
     prompt = model.prompt_ids(cfg, 128, seed=2 + rank)
     stream = torch.cuda.current_stream()
     e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
@@ -447,7 +452,7 @@ def run_decode(torch, dist, rank, world, args, cpu=False):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         pre_ms, dec_ms = t.tolist()
     out = {"model": "SmolLM2-135M shape (30 layers, d 576, 9/3 heads, ffn 1536, vocab 49152), random N(0,0.02) weights seed 2",
-           "mode": args.decode_mode, "prompt": 128, "generated": 128, "sequences": world,
+           "format": "xlns%d" % fmt, "mode": args.decode_mode if fmt == 16 else None, "prompt": 128, "generated": 128, "sequences": world,
            "prefill_tok_per_s": world * 128 / (pre_ms / 1000), "decode_tok_per_s": world * 127 / (dec_ms / 1000),
            "ms_per_token": dec_ms / 127, "prefill_ms": pre_ms,
            "timing": "device events; prefill eager, decode as one CUDA graph per position (captured before the timed region); each step's greedy token is copied to pinned host memory",
@@ -457,7 +462,7 @@ def run_decode(torch, dist, rank, world, args, cpu=False):
         # prefill of 8 tokens, then 2 decode steps
         import time
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        o = model.OracleOps(cfg, w, mode=args.decode_mode, n_ctx=16, nthreads=os.cpu_count() or 1)
+        o = model.OracleOps(cfg, w, mode=args.decode_mode, n_ctx=16, nthreads=os.cpu_count() or 1, fmt=fmt)
         lo = model.forward(o, cfg, prompt[:8], 0)
         t0 = time.perf_counter()
         tk = o.argmax(lo)

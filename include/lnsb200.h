@@ -163,8 +163,8 @@ int lnsb_rms_norm_lns(int fmt, const void * src, void * dst, int64_t ncols, int6
  * 468-599, 786-868, 1199-1281).  F32 in and out, as at every ggml op
  * boundary: each operand is converted to LNS (lnsb_to_lns's table), the op
  * runs in LNS, the result is written back as F32.  Contiguous tensors.
- * Unsupported combinations return LNSB_E_UNSUPPORTED: gelu and tanh (their
- * xlnscpp definitions are not pinned), and unary/glu in xlns32. */
+ * Unsupported combinations return LNSB_E_UNSUPPORTED: gelu, tanh and geglu
+ * (their xlnscpp definitions are not pinned). */
 #define LNSB_BINARY_ADD 0
 #define LNSB_BINARY_MUL 1
 #define LNSB_BINARY_DIV 2
@@ -180,7 +180,7 @@ int lnsb_binary(int fmt, int op, const float * a, const int64_t ane[4], const fl
                 float * dst, lnsb_stream_t stream);
 /* dst = src * s, plus b when b != 0 (ggml_scale_bias) */
 int lnsb_scale(int fmt, const float * src, float * dst, int64_t n, float s, float b, lnsb_stream_t stream);
-/* silu(x) = x / (1 + exp(-x)) in xlns16 arithmetic; relu */
+/* silu(x) = x / (1 + exp(-x)) in LNS arithmetic (xlns32: exp through float, as in its softmax); relu */
 int lnsb_unary(int fmt, int op, const float * src, float * dst, int64_t n, lnsb_stream_t stream);
 /* dst[r][c] = act(gate[r * gate_stride + c]) * up[r * up_stride + c] */
 int lnsb_glu(int fmt, int op, const float * gate, const float * up, int64_t gate_stride, int64_t up_stride,

@@ -873,3 +873,71 @@ void orc16_rope_f32(const float * src, const int64_t ne[4], const float * cos_si
                 for (int64_t j = n_dims; j < ne[0]; j++) dst[row + j] = c2f(f2c(src[row + j]));
             }
 }
+
+/* ---- the same ops in xlns32 (lns-backend/src32/lns32-ops.cpp) ---- */
+
+/* silu(x) = x / (1 + exp(-x)) in xlns32 arithmetic, exp through float as in
+ * the xlns32 softmax (exp32) */
+uint32_t orc32_silu(uint32_t x) {
+    return div32(x, add32(0x40000000u, exp32(x ^ X32_SIGNMASK)));
+}
+
+static inline uint32_t f2c32(float f) { return orc32_from_f32(f); }
+static inline float c2f32(uint32_t c) { return orc32_to_f32(c); }
+
+uint32_t orc32_relu(uint32_t x) {
+    return ((x & X32_SIGNMASK) || (x & ~X32_SIGNMASK) == 0) ? 0u : x;
+}
+
+void orc32_unary_f32(int op, const float * src, float * dst, int64_t n) {
+    for (int64_t i = 0; i < n; i++) {
+        const uint32_t v = f2c32(src[i]);
+        dst[i] = c2f32(op == ORC_SILU ? orc32_silu(v) : orc32_relu(v));
+    }
+}
+
+void orc32_binary_f32(int op, const float * a, const int64_t ane[4], const float * b, const int64_t bne[4], float * dst) {
+    for (int64_t i3 = 0; i3 < ane[3]; i3++)
+        for (int64_t i2 = 0; i2 < ane[2]; i2++)
+            for (int64_t i1 = 0; i1 < ane[1]; i1++) {
+                const int64_t ra = ((i3 * ane[2] + i2) * ane[1] + i1) * ane[0];
+                const int64_t rb = (((i3 % bne[3]) * bne[2] + (i2 % bne[2])) * bne[1] + (i1 % bne[1])) * bne[0];
+                for (int64_t i0 = 0; i0 < ane[0]; i0++) {
+                    const uint32_t x = f2c32(a[ra + i0]), y = f2c32(b[rb + i0 % bne[0]]);
+                    const uint32_t r = op == ORC_ADD ? add32(x, y) : op == ORC_MUL ? mul32(x, y) : div32(x, y);
+                    dst[ra + i0] = c2f32(r);
+                }
+            }
+}
+
+void orc32_scale_f32(const float * src, float * dst, int64_t n, float s, float b) {
+    const uint32_t sl = f2c32(s), bl = f2c32(b);
+    for (int64_t i = 0; i < n; i++) {
+        uint32_t v = mul32(f2c32(src[i]), sl);
+        if (b != 0.0f) v = add32(v, bl);
+        dst[i] = c2f32(v);
+    }
+}
+
+void orc32_swiglu_f32(const float * gate, const float * up, int64_t gs, int64_t us, float * dst, int64_t nc, int64_t nr) {
+    for (int64_t r = 0; r < nr; r++)
+        for (int64_t c = 0; c < nc; c++)
+            dst[r * nc + c] = c2f32(mul32(orc32_silu(f2c32(gate[r * gs + c])), f2c32(up[r * us + c])));
+}
+
+void orc32_rope_f32(const float * src, const int64_t ne[4], const float * cos_sin, int n_dims, int neox, float * dst) {
+    const int64_t half = n_dims / 2;
+    for (int64_t i3 = 0; i3 < ne[3]; i3++)
+        for (int64_t i2 = 0; i2 < ne[2]; i2++)
+            for (int64_t i1 = 0; i1 < ne[1]; i1++) {
+                const int64_t row = ((i3 * ne[2] + i2) * ne[1] + i1) * ne[0];
+                for (int64_t j = 0; j < half; j++) {
+                    const uint32_t c = f2c32(cos_sin[(i2 * half + j) * 2]), sn = f2c32(cos_sin[(i2 * half + j) * 2 + 1]);
+                    const int64_t i0 = neox ? j : 2 * j, i1b = neox ? j + half : 2 * j + 1;
+                    const uint32_t x0 = f2c32(src[row + i0]), x1 = f2c32(src[row + i1b]);
+                    dst[row + i0]  = c2f32(add32(mul32(x0, c), mul32(x1, sn) ^ X32_SIGNMASK));
+                    dst[row + i1b] = c2f32(add32(mul32(x0, sn), mul32(x1, c)));
+                }
+                for (int64_t j = n_dims; j < ne[0]; j++) dst[row + j] = c2f32(f2c32(src[row + j]));
+            }
+}

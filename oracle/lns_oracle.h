@@ -113,6 +113,14 @@ void orc16_unary_f32(int op, const float * src, float * dst, int64_t n);
 void orc16_swiglu_f32(const float * gate, const float * up, int64_t gs, int64_t us, float * dst, int64_t nc, int64_t nr);
 void orc16_rope_f32(const float * src, const int64_t ne[4], const float * cos_sin, int n_dims, int neox, float * dst);
 
+uint32_t orc32_silu(uint32_t x);
+uint32_t orc32_relu(uint32_t x);
+void orc32_unary_f32(int op, const float * src, float * dst, int64_t n);
+void orc32_binary_f32(int op, const float * a, const int64_t ane[4], const float * b, const int64_t bne[4], float * dst);
+void orc32_scale_f32(const float * src, float * dst, int64_t n, float s, float b);
+void orc32_swiglu_f32(const float * gate, const float * up, int64_t gs, int64_t us, float * dst, int64_t nc, int64_t nr);
+void orc32_rope_f32(const float * src, const int64_t ne[4], const float * cos_sin, int n_dims, int neox, float * dst);
+
 /* batch conversions */
 void orc16_from_f32_n(const float * src, uint16_t * dst, int64_t n);
 void orc16_to_f32_n(const uint16_t * src, float * dst, int64_t n);

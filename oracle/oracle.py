@@ -65,8 +65,13 @@ def lib():
             "orc16_binary_f32": (None, [ctypes.c_int, f32p, i64a, f32p, i64a, f32p]),
             "orc16_scale_f32": (None, [f32p, f32p, i64, ctypes.c_float, ctypes.c_float]),
             "orc16_unary_f32": (None, [ctypes.c_int, f32p, f32p, i64]),
+            "orc32_unary_f32": (None, [ctypes.c_int, f32p, f32p, i64]),
             "orc16_swiglu_f32": (None, [f32p, f32p, i64, i64, f32p, i64, i64]),
             "orc16_rope_f32": (None, [f32p, i64a, f32p, ctypes.c_int, ctypes.c_int, f32p]),
+            "orc32_binary_f32": (None, [ctypes.c_int, f32p, i64a, f32p, i64a, f32p]),
+            "orc32_scale_f32": (None, [f32p, f32p, i64, ctypes.c_float, ctypes.c_float]),
+            "orc32_swiglu_f32": (None, [f32p, f32p, i64, i64, f32p, i64, i64]),
+            "orc32_rope_f32": (None, [f32p, i64a, f32p, ctypes.c_int, ctypes.c_int, f32p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -82,45 +87,48 @@ BINARY = {"add": 0, "mul": 1, "div": 2}
 UNARY = {"silu": 0, "relu": 2}
 
 
-def binary16(op, a, b):
+def binary16(op, a, b, fmt=16):
     """a op b at the F32 op boundary, b repeated to a's shape (numpy, innermost last)."""
     a = np.ascontiguousarray(a, np.float32)
     b = np.ascontiguousarray(b, np.float32)
     out = np.empty_like(a)
-    lib().orc16_binary_f32(BINARY[op], a.ravel(), _ne(a.shape[::-1]), b.ravel(), _ne(b.shape[::-1]), out.ravel())
+    fn = lib().orc16_binary_f32 if fmt == 16 else lib().orc32_binary_f32
+    fn(BINARY[op], a.ravel(), _ne(a.shape[::-1]), b.ravel(), _ne(b.shape[::-1]), out.ravel())
     return out
 
 
-def scale16(src, s, b=0.0):
+def scale16(src, s, b=0.0, fmt=16):
     src = np.ascontiguousarray(src, np.float32)
     out = np.empty_like(src)
-    lib().orc16_scale_f32(src.ravel(), out.ravel(), src.size, s, b)
+    (lib().orc16_scale_f32 if fmt == 16 else lib().orc32_scale_f32)(src.ravel(), out.ravel(), src.size, s, b)
     return out
 
 
-def unary16(op, src):
+def unary16(op, src, fmt=16):
     src = np.ascontiguousarray(src, np.float32)
     out = np.empty_like(src)
-    lib().orc16_unary_f32(UNARY[op], src.ravel(), out.ravel(), src.size)
+    (lib().orc16_unary_f32 if fmt == 16 else lib().orc32_unary_f32)(UNARY[op], src.ravel(), out.ravel(), src.size)
     return out
 
 
-def swiglu16(gate, up):
+def swiglu16(gate, up, fmt=16):
     """silu(gate) * up, rows of gate.shape[-1]"""
     gate = np.ascontiguousarray(gate, np.float32)
     up = np.ascontiguousarray(up, np.float32)
     nc = gate.shape[-1]
     out = np.empty_like(gate)
-    lib().orc16_swiglu_f32(gate.ravel(), up.ravel(), nc, nc, out.ravel(), nc, gate.size // nc)
+    (lib().orc16_swiglu_f32 if fmt == 16 else lib().orc32_swiglu_f32)(gate.ravel(), up.ravel(), nc, nc, out.ravel(),
+                                                                       nc, gate.size // nc)
     return out
 
 
-def rope16(src, cos_sin, n_dims, neox=False):
+def rope16(src, cos_sin, n_dims, neox=False, fmt=16):
     """src [ne3][ne2][ne1][ne0] (numpy order), cos_sin [ne2][n_dims/2][2]"""
     src = np.ascontiguousarray(src, np.float32)
     cs = np.ascontiguousarray(cos_sin, np.float32)
     out = np.empty_like(src)
-    lib().orc16_rope_f32(src.ravel(), _ne(src.shape[::-1]), cs.ravel(), n_dims, 1 if neox else 0, out.ravel())
+    (lib().orc16_rope_f32 if fmt == 16 else lib().orc32_rope_f32)(src.ravel(), _ne(src.shape[::-1]), cs.ravel(), n_dims,
+                                                                   1 if neox else 0, out.ravel())
     return out
 
 

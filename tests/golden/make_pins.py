@@ -71,9 +71,12 @@ def main(ref):
                      ("lns32", "unit-tests-lns32.txt")):
         with open(os.path.join(ev, fn)) as f:
             suite[name] = parse_suite(f.read())
-    with open(os.path.join(ev, "unit-tests-lns16-base.txt")) as f, \
-            open(os.path.join(ref, "lns-backend", "tests", "test-lns-backend.cpp")) as g:
-        swiglu = parse_swiglu(f.read(), g.read())
+    with open(os.path.join(ref, "lns-backend", "tests", "test-lns-backend.cpp")) as g:
+        test_src = g.read()
+    with open(os.path.join(ev, "unit-tests-lns16-base.txt")) as f:
+        swiglu = parse_swiglu(f.read(), test_src)
+    with open(os.path.join(ev, "unit-tests-lns32.txt")) as f:
+        swiglu["out_lns32"] = parse_swiglu(f.read(), test_src)["out"]
     pins = {
         "swiglu": swiglu,
         "source": "xlnsresearch/xlns-ggml-backend results/sum32-evidence/*.txt (outputs of "

@@ -1,7 +1,7 @@
-"""The Llama-architecture decode (lnsb200.model: LNS16
-sum32) on the GPU against the same graph on the CPU oracle: final-token
-logits bit for bit after prefill and after each decode step, and the greedy
-token stream."""
+"""The Llama-architecture decode (lnsb200.model: the LNS16 sum32 model and
+the LNS32 model) on the GPU against the same graph on the CPU oracle:
+final-token logits bit for bit after prefill and after each decode step, and
+the greedy token stream."""
 import numpy as np
 import pytest
 
@@ -13,12 +13,12 @@ SMALL = dict(n_layer=2, n_embd=128, n_head=4, n_head_kv=2, head_dim=32, n_ff=256
              rope_base=100000.0, eps=1e-5)
 
 
-def run_both(cfg, mode, n_prompt, n_steps, n_ctx=64):
+def run_both(cfg, mode, n_prompt, n_steps, n_ctx=64, fmt=16):
     from lnsb200 import model
     w = model.init_weights(cfg, seed=2)
     prompt = model.prompt_ids(cfg, n_prompt, seed=2)
-    g = model.GpuOps(cfg, w, mode=mode, n_ctx=n_ctx)
-    o = model.OracleOps(cfg, w, mode=mode, n_ctx=n_ctx)
+    g = model.GpuOps(cfg, w, mode=mode, n_ctx=n_ctx, fmt=fmt)
+    o = model.OracleOps(cfg, w, mode=mode, n_ctx=n_ctx, fmt=fmt)
     lg = model.forward(g, cfg, prompt, 0)
     lo = model.forward(o, cfg, prompt, 0)
     steps = [(lg.cpu().numpy().ravel(), lo.ravel())]
@@ -47,6 +47,18 @@ def test_smollm2_shape_decode_bit_exact():
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), "logits differ at step %d" % i
 
 
+def test_small_model_decode_bit_exact_xlns32():
+    for i, (a, b) in enumerate(run_both(SMALL, "sum32", 7, 4, fmt=32)):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), "logits differ at step %d" % i
+
+
+def test_smollm2_shape_decode_bit_exact_xlns32():
+    """the LNS32 model (every op in xlns32) at the full SmolLM2-135M shape"""
+    from lnsb200 import model
+    for i, (a, b) in enumerate(run_both(model.SMOLLM2_135M, "sum32", 6, 3, n_ctx=16, fmt=32)):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), "logits differ at step %d" % i
+
+
 def test_generate_matches_forward_loop():
     from lnsb200 import model
     w = model.init_weights(SMALL, seed=2)
@@ -71,3 +83,15 @@ def test_graph_decode_matches_eager():
     # capturing does not run the graphs; the cache still holds only the prompt
     toks = dec.decode(first, len(prompt), 6)
     assert [first] + toks == eager
+
+
+def test_graph_decode_matches_eager_xlns32():
+    from lnsb200 import model
+    w = model.init_weights(SMALL, seed=2)
+    prompt = model.prompt_ids(SMALL, 5, seed=2)
+    eager = model.generate(model.GpuOps(SMALL, w, mode="sum32", n_ctx=32, fmt=32), SMALL, prompt, 5)
+    g2 = model.GpuOps(SMALL, w, mode="sum32", n_ctx=32, fmt=32)
+    first = g2.argmax(model.forward(g2, SMALL, prompt, 0))
+    dec = model.GraphDecoder(g2, SMALL)
+    dec.prepare(len(prompt), len(prompt) + 4)
+    assert [first] + dec.decode(first, len(prompt), 4) == eager

@@ -1,7 +1,7 @@
 """GPU parity of the model graph's elementwise ops (lnsb_binary / scale /
 unary / glu / rope and the F16 conversions) against the CPU oracle, bit for
-bit, at the F32 op boundary (lns-backend/src/lns-ops.cpp:468-599, 786-868,
-1199-1281)."""
+bit, at the F32 op boundary, in xlns16 (lns-backend/src/lns-ops.cpp:468-599,
+786-868, 1199-1281) and xlns32 (lns-backend/src32/lns32-ops.cpp)."""
 import numpy as np
 import pytest
 
@@ -11,11 +11,18 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture(scope="module")
-def ks():
+def kss():
     import lnsb200
-    k = lnsb200.KernelSet(16, "base")
-    k.upload_tables()
-    return k
+    out = {}
+    for fmt in (16, 32):
+        out[fmt] = lnsb200.KernelSet(fmt, "base")
+        out[fmt].upload_tables()
+    return out
+
+
+@pytest.fixture(scope="module")
+def ks(kss):
+    return kss[16]
 
 
 def dev(a):
@@ -38,42 +45,50 @@ def same(got, want):
     return np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+FMTS = pytest.mark.parametrize("fmt", [16, 32])
+
+
+@FMTS
 @pytest.mark.parametrize("op", ["add", "mul", "div"])
 @pytest.mark.parametrize("bshape", [(1, 1, 1, 576), (1, 1, 5, 576), (2, 1, 5, 576), (1, 1, 1, 1)])
-def test_binary(orc, ks, op, bshape):
+def test_binary(orc, kss, fmt, op, bshape):
     rng = np.random.default_rng(len(bshape) + bshape[-1] + bshape[-2])
     a = f32(rng, (2, 3, 5, 576))
     b = f32(rng, bshape, 0.5)
-    want = orc.binary16(op, a, b)
+    want = orc.binary16(op, a, b, fmt=fmt)
     out = torch.empty(a.size, dtype=torch.float32, device="cuda")
-    ks.binary(op, dev(a), a.shape[::-1], dev(b), b.shape[::-1], out)
+    kss[fmt].binary(op, dev(a), a.shape[::-1], dev(b), b.shape[::-1], out)
     assert same(host(out).reshape(a.shape), want)
 
 
+@FMTS
 @pytest.mark.parametrize("s,b", [(0.125, 0.0), (-3.0, 0.5)])
-def test_scale(orc, ks, s, b):
+def test_scale(orc, kss, fmt, s, b):
     rng = np.random.default_rng(3)
     x = f32(rng, (4096,), 2.0)
     out = torch.empty_like(dev(x))
-    ks.scale(dev(x), out, x.size, s, b)
-    assert same(host(out), orc.scale16(x, s, b))
+    kss[fmt].scale(dev(x), out, x.size, s, b)
+    assert same(host(out), orc.scale16(x, s, b, fmt=fmt))
 
 
+@FMTS
 @pytest.mark.parametrize("op", ["silu", "relu"])
-def test_unary(orc, ks, op):
+def test_unary(orc, kss, fmt, op):
     rng = np.random.default_rng(5)
     x = np.concatenate([f32(rng, (8192,), 3.0), np.array([0.0, -0.0, 1e-30, -1e-30, 60.0, -60.0, 1e30, -1e30], np.float32)])
     out = torch.empty_like(dev(x))
-    ks.unary(op, dev(x), out, x.size)
-    assert same(host(out), orc.unary16(op, x))
+    kss[fmt].unary(op, dev(x), out, x.size)
+    assert same(host(out), orc.unary16(op, x, fmt=fmt))
 
 
-def test_swiglu_split_and_fused(orc, ks):
+@FMTS
+def test_swiglu_split_and_fused(orc, kss, fmt):
+    ks = kss[fmt]
     rng = np.random.default_rng(7)
     nc, nr = 1536, 6
     gate = f32(rng, (nr, nc), 2.0)
     up = f32(rng, (nr, nc), 1.0)
-    want = orc.swiglu16(gate, up)
+    want = orc.swiglu16(gate, up, fmt=fmt)
     out = torch.empty((nr, nc), dtype=torch.float32, device="cuda")
     ks.glu(dev(gate), dev(up), nc, nc, out, nc, nr)
     assert same(host(out), want)
@@ -83,8 +98,10 @@ def test_swiglu_split_and_fused(orc, ks):
     assert same(host(out), want)
 
 
-def test_swiglu_reference_pin(ks):
-    """the reference's printed swiglu (test-lns-backend.cpp run_swiglu_test) through the GPU"""
+@FMTS
+def test_swiglu_reference_pin(kss, fmt):
+    """the reference's printed swiglu (test-lns-backend.cpp run_swiglu_test, the
+    LNS16 and LNS32 runs) through the GPU"""
     import json
     import os
     from conftest import ROOT
@@ -92,18 +109,21 @@ def test_swiglu_reference_pin(ks):
     gate = np.array(p["gate"], np.float32).reshape(2, 4)
     up = np.array(p["up"], np.float32).reshape(2, 4)
     out = torch.empty((2, 4), dtype=torch.float32, device="cuda")
-    ks.glu(dev(gate), dev(up), 4, 4, out, 4, 2)
-    assert ["%.6f" % v for v in host(out).ravel()] == ["%.6f" % v for v in p["out"]]
+    kss[fmt].glu(dev(gate), dev(up), 4, 4, out, 4, 2)
+    want = p["out"] if fmt == 16 else p["out_lns32"]
+    assert ["%.6f" % v for v in host(out).ravel()] == ["%.6f" % v for v in want]
 
 
+@FMTS
 @pytest.mark.parametrize("n_dims,neox", [(64, False), (64, True), (32, False)])
-def test_rope(orc, ks, n_dims, neox):
+def test_rope(orc, kss, fmt, n_dims, neox):
+    ks = kss[fmt]
     rng = np.random.default_rng(n_dims + neox)
     hd, nh, nt = 64, 9, 7
     x = f32(rng, (1, nt, nh, hd), 1.0)
     pos = [0, 1, 2, 5, 17, 100, 255]
     cs = orc.rope_cos_sin(pos, n_dims, 100000.0)
-    want = orc.rope16(x, cs, n_dims, neox)
+    want = orc.rope16(x, cs, n_dims, neox, fmt=fmt)
     out = torch.empty(x.size, dtype=torch.float32, device="cuda")
     ks.rope(dev(x), (hd, nh, nt, 1), dev(cs), n_dims, out, neox=neox)
     assert same(host(out).reshape(x.shape), want)
@@ -128,3 +148,12 @@ def test_unsupported_and_invalid(ks):
         ks.unary("gelu", x, x, 16)                      # gelu not pinned: LNSB_E_UNSUPPORTED
     with pytest.raises(lnsb200.LnsbError):
         ks.binary("add", x, (16, 1, 1, 1), x, (3, 1, 1, 1), x)   # b does not repeat to a
+
+
+def test_unsupported_xlns32(kss):
+    import lnsb200
+    x = torch.zeros(16, dtype=torch.float32, device="cuda")
+    with pytest.raises(lnsb200.LnsbError):
+        kss[32].unary("tanh", x, x, 16)
+    with pytest.raises(lnsb200.LnsbError):
+        kss[32].glu(x, x, 4, 4, x, 4, 4, op="geglu")

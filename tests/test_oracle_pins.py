@@ -103,6 +103,10 @@ def test_swiglu_pin(pins):
     p = pins["swiglu"]
     out = oracle.swiglu16(np.array(p["gate"], np.float32).reshape(2, 4), np.array(p["up"], np.float32).reshape(2, 4))
     assert ["%.6f" % v for v in out.ravel()] == ["%.6f" % v for v in p["out"]]
+    # xlns32: the same form, exp through float as in the xlns32 softmax (unit-tests-lns32.txt:41-43)
+    out32 = oracle.swiglu16(np.array(p["gate"], np.float32).reshape(2, 4), np.array(p["up"], np.float32).reshape(2, 4),
+                            fmt=32)
+    assert ["%.6f" % v for v in out32.ravel()] == ["%.6f" % v for v in p["out_lns32"]]
 
 
 def test_report(computed, pins, capsys):

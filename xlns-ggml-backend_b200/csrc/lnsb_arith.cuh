@@ -424,11 +424,19 @@ __device__ __forceinline__ uint32_t padd16(uint32_t a, uint32_t b, const int16_t
     const int adj = tab[min(d, k16_ess + 1)] >> 1;
     return (uint32_t) min(max((int) a, (int) b) + adj, 0x7FFF);
 }
+// padd32f: sb by interpolation with the segment chosen by a compare (no
+// descriptor load on the chain's dependent path), shifts in place of the
+// multiply form
 __device__ __forceinline__ uint32_t padd32f(const int32_t * F, uint32_t a, uint32_t b) {
     const uint32_t d  = a > b ? a - b : b - a;
     const uint32_t mx = a > b ? a : b;
     const uint32_t z  = d < k32_ess ? d : k32_ess;
-    const uint32_t r  = mx + (uint32_t) interp32f(F, z, (int) (z >> 23));
+    const bool     hi = z >= ((uint32_t) k32f_sb_split << 23);
+    const int      sh = hi ? k32f_sb_sh1 : k32f_sb_sh0;
+    const int32_t  i  = (int32_t) (z >> sh) + (hi ? k32f_sb_base1 : k32f_sb);
+    const int32_t  f  = (int32_t) (z & ((1u << sh) - 1u));
+    const int32_t  v0 = F[i], v1 = F[i + 1];
+    const uint32_t r  = mx + (uint32_t) (v0 + (((v1 - v0) * f) >> sh));
     return (int32_t) r < 0 ? 0x7FFFFFFFu : r;                      // saturation: the carry into bit 31
 }
 

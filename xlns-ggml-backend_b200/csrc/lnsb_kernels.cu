@@ -145,8 +145,16 @@ __device__ __forceinline__ void cp_async16_zfill(void * smem, const void * gmem,
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+// `bytes` (a multiple of 16; both addresses 16-byte aligned) from global to
+// shared memory by the whole block, every piece in flight at once; the caller
+// commits, waits and synchronises
+__device__ __forceinline__ void stage_async(void * smem, const void * gmem, int bytes);
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+__device__ __forceinline__ void stage_async(void * smem, const void * gmem, int bytes) {
+    for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x)
+        cp_async16(static_cast<unsigned char *>(smem) + 16 * i, static_cast<const unsigned char *>(gmem) + 16 * i);
+}
 
 // ===================== MUL_MAT (xlns16, base mode, key form) ================
 //
@@ -864,6 +872,9 @@ constexpr int A32_THREADS = 512;
 // threads per CTA: 32 warps per SM where the per-warp rings fit beside the
 // table (xlns16), else 16
 __host__ __device__ constexpr int a32_threads(int fmt, bool ring) { return fmt == 16 && ring ? 1024 : A32_THREADS; }
+#ifndef LNSB_A32_LAT_BF
+#define LNSB_A32_LAT_BF 1            // one round of units (chain latency bound): branch-free adder
+#endif
 #ifndef LNSB_A32_TN2_MIN_UNITS
 #define LNSB_A32_TN2_MIN_UNITS 2     // two tokens per lane once each warp gets this many units
 #endif
@@ -948,15 +959,29 @@ __device__ __forceinline__ void a32_load(a32_chunk<FMT, TN> & c, const typename 
     }
 }
 
+// L2 prefetch of the weights of the chunk at k0 (one lane's column)
+constexpr int A32_L2PF = 6;        // chunks ahead
+template <int FMT>
+__device__ __forceinline__ void a32_prefetch_l2(const typename a32_fmt<FMT>::elem * wl, int64_t k0, int64_t K, int64_t M) {
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        if (k0 + j < K) asm volatile("prefetch.global.L2 [%0];\n" ::"l"(__cvta_generic_to_global(wl + (k0 + j) * M)));
+}
+
 // One step of every chain of a lane: the main parts first (independent, so
 // they interleave), then a branch per chain for the lanes on the rare path.
 // F: the flat image (A32_FLAT); LP: the LPVIP singular-branch table; st: the
 // chains' LFSR states (A32_MBL).
-template <int FMT, int TN>
+template <int FMT, int TN, bool BF = false>
 __device__ __forceinline__ void a32_step_x(const int32_t * F, const int32_t * LP, uint32_t (&acc)[TN],
                                            uint32_t (&st)[TN], uint32_t w, const uint32_t (&x)[TN]) {
     using OP = a32_fmt<FMT>;
-    if constexpr (a32_kind<FMT>() == A32_FLAT) {
+    if constexpr (a32_kind<FMT>() == A32_FLAT && BF) {
+        // latency regime: the branch-free adder (every lane makes the
+        // cotransformation lookups), no divergence on the dependent path
+#pragma unroll
+        for (int t = 0; t < TN; t++) acc[t] = add32f(F, acc[t], OP::term(w, x[t]));
+    } else if constexpr (a32_kind<FMT>() == A32_FLAT) {
         uint32_t    b[TN];
         add32f_part o[TN];
 #pragma unroll
@@ -984,17 +1009,17 @@ __device__ __forceinline__ void a32_step_x(const int32_t * F, const int32_t * LP
         }
     }
 }
-template <int FMT, int TN>
+template <int FMT, int TN, bool BF = false>
 __device__ __forceinline__ void a32_step(const int32_t * F, const int32_t * LP, uint32_t (&acc)[TN], uint32_t (&st)[TN],
                                          uint32_t w, const a32_chunk<FMT, TN> & c, int j) {
     uint32_t x[TN];
 #pragma unroll
     for (int t = 0; t < TN; t++) x[t] = c.xv(t, j);
-    a32_step_x<FMT, TN>(F, LP, acc, st, w, x);
+    a32_step_x<FMT, TN, BF>(F, LP, acc, st, w, x);
 }
 
 // The steps of one 8-step chunk: j in [j0, kv) (kv < 8 only in the last chunk).
-template <int FMT, int TN>
+template <int FMT, int TN, bool BF = false>
 __device__ __forceinline__ void a32_steps(const int32_t * F, const int32_t * LP, const a32_chunk<FMT, TN> & c,
                                           uint32_t (&acc)[TN], uint32_t (&st)[TN], bool first, int64_t kv) {
     using OP = a32_fmt<FMT>;
@@ -1003,15 +1028,15 @@ __device__ __forceinline__ void a32_steps(const int32_t * F, const int32_t * LP,
         for (int t = 0; t < TN; t++) acc[t] = OP::term(c.w[0], c.xv(t, 0));
 #pragma unroll
         for (int j = 1; j < 8; j++) {
-            if (j < kv) a32_step<FMT, TN>(F, LP, acc, st, c.w[j], c, j);
+            if (j < kv) a32_step<FMT, TN, BF>(F, LP, acc, st, c.w[j], c, j);
         }
     } else if (kv >= 8) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) a32_step<FMT, TN>(F, LP, acc, st, c.w[j], c, j);
+        for (int j = 0; j < 8; j++) a32_step<FMT, TN, BF>(F, LP, acc, st, c.w[j], c, j);
     } else {
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            if (j < kv) a32_step<FMT, TN>(F, LP, acc, st, c.w[j], c, j);
+            if (j < kv) a32_step<FMT, TN, BF>(F, LP, acc, st, c.w[j], c, j);
         }
     }
 }
@@ -1079,8 +1104,9 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
     extern __shared__ __align__(16) int32_t F[];
     constexpr int NT = a32_threads(FMT, RING);
     if constexpr (KIND == A32_FLAT) {
-        for (int i = threadIdx.x; i < k32f_words / 4; i += NT)
-            reinterpret_cast<int4 *>(F)[i] = __ldg(reinterpret_cast<const int4 *>(T.flat32) + i);
+        stage_async(F, T.flat32, k32f_words * 4);
+        cp_async_commit();
+        cp_async_wait<0>();
         __syncthreads();
     }
     const int32_t * LP = T.lpvip_db;
@@ -1134,7 +1160,7 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
                     const unsigned char * sg = ring + (int) (c % A32_STAGES) * RG::stage;
                     if (lat) {                           // few units: all 8 steps unrolled, operands in registers
                         RG::read(cur, sg, lane);
-                        a32_steps<FMT, TN>(F, LP, cur, acc, st, c == 0, K - c * 8);
+                        a32_steps<FMT, TN, LNSB_A32_LAT_BF != 0>(F, LP, cur, acc, st, c == 0, K - c * 8);
                         continue;
                     }
                     const E * ws = reinterpret_cast<const E *>(sg) + lane;
@@ -1157,10 +1183,15 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
                 cp_async_wait<0>();
                 __syncwarp();                           // the ring is free for the next unit
             } else {
+                // registers hold chunk c + 1 while chunk c runs; the weights of chunk
+                // c + A32_L2PF are prefetched into L2 so that those loads hit there
+                // (a lane's 8 steps are shorter than a DRAM miss in the latency regime)
                 const E * wl = wb + (m < M ? m : M - 1);
                 a32_chunk<FMT, TN> nxt;
+                for (int64_t c = 1; c < A32_L2PF && c < nchunks; c++) a32_prefetch_l2<FMT>(wl, c * 8, K, M);
                 a32_load<FMT, TN>(cur, wl, xt, 0, K, M, vecx != 0);
                 for (int64_t c = 0; c < nchunks; c++) {
+                    if (c + A32_L2PF < nchunks) a32_prefetch_l2<FMT>(wl, (c + A32_L2PF) * 8, K, M);
                     if (c + 1 < nchunks) a32_load<FMT, TN>(nxt, wl, xt, (c + 1) * 8, K, M, vecx != 0);
                     a32_steps<FMT, TN>(F, LP, cur, acc, st, c == 0, K - c * 8);
                     cur = nxt;
@@ -1185,15 +1216,18 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
 // addition over a shared-memory table (padd16 / padd32f); the other modes
 // run the general reduction policy.
 constexpr bool NNCHAIN = k_mode == M_BASE || k_mode == M_SUM32;
-constexpr int  NN_TAB  = k_mode == M_SUM32 ? k32f_words * 4 : 0;   // flat image bytes in dynamic smem
+constexpr int  NN_TAB  = k_mode == M_SUM32 ? k32f_sb_bytes16 : 0;   // sb knot bytes in dynamic smem
 
-// the sb knots and the descriptors of the flat xlns32 image (all a
-// non-negative chain reads) into shared memory at their flat-image offsets
+// the sb knots of the flat xlns32 image (all a non-negative chain reads) into
+// shared memory, asynchronously (committed with the block's other copies)
 __device__ __forceinline__ void nn_tables(const dev_tables & T, int32_t * F) {
-    if constexpr (k_mode == M_SUM32) {
-        for (int i = threadIdx.x; i < k32f_db; i += blockDim.x) F[i] = __ldg(T.flat32 + i);
-        for (int i = k32f_dsc2 + threadIdx.x; i < k32f_words; i += blockDim.x) F[i] = __ldg(T.flat32 + i);
-    }
+    if constexpr (k_mode == M_SUM32) stage_async(F, T.flat32, k32f_sb_bytes16);
+}
+// the xlns16 tables a normaliser block keeps in shared memory (sbdb16, and the
+// Monte fine tables in monte mode), asynchronously
+__device__ __forceinline__ void norm_tables(const dev_tables & T, int16_t * tab, int16_t * fine) {
+    stage_async(tab, T.sbdb16, k16_tab_bytes16);
+    if constexpr (k_mode == M_MONTE) stage_async(fine, T.monte16, 2 * k16_monte_n * 2);
 }
 // one non-negative addition of the mode: accumulator form (sum32: acc32) and term code
 __device__ __forceinline__ uint32_t nn_add(const int32_t * F, const int16_t * tab, uint32_t acc, uint32_t t) {
@@ -1205,16 +1239,13 @@ template <int FMT, bool IO_F32>
 __global__ void __launch_bounds__(128)
 k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst, int64_t ncols, int64_t nrows,
            uint32_t eps_l, uint32_t inv_n, uint32_t monte_seed, int rpb, int nn_ok) {
-    __shared__ int16_t  tab[k16_tab_bytes / 2];
-    __shared__ int16_t  fine[k_mode == M_MONTE ? 2 * k16_monte_n : 2];
+    __shared__ __align__(16) int16_t tab[k16_tab_bytes16 / 2];
+    __shared__ __align__(16) int16_t fine[k_mode == M_MONTE ? 2 * k16_monte_n : 8];
     __shared__ uint32_t s_inv[32];
-    extern __shared__ __align__(16) int32_t dyn[];          // NNCHAIN: [flat image (sum32)][squares: rpb x ncols]
+    extern __shared__ __align__(16) int32_t dyn[];          // NNCHAIN: [sb knots (sum32)][squares: rpb x ncols]
     constexpr bool NNC = FMT == 16 && NNCHAIN;
     const bool     NN  = NNC && nn_ok != 0;                 // the squares fit in shared memory
-    if constexpr (FMT == 16) {
-        for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += blockDim.x) tab[i] = T.sbdb16[i];
-        if constexpr (k_mode == M_MONTE) for (int i = threadIdx.x; i < 2 * k16_monte_n; i += blockDim.x) fine[i] = T.monte16[i];
-    }
+    if constexpr (FMT == 16) norm_tables(T, tab, fine);
     const int64_t row0 = (int64_t) blockIdx.x * rpb;
     const int64_t nr = imin64(rpb, nrows - row0);
     auto load = [&](int64_t idx) -> uint32_t {
@@ -1233,6 +1264,8 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
             sq[e] = (uint16_t) mul16(v, v);
         }
     }
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
     if (threadIdx.x < nr) {
         const int64_t row = row0 + threadIdx.x;
@@ -1291,15 +1324,18 @@ __global__ void __launch_bounds__(128)
 k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const void * __restrict__ mask,
            lnsb_shape4 ms, uint32_t scale_l, void * __restrict__ dst, void * __restrict__ work,
            uint32_t monte_seed, int rpb, int nn_ok) {
-    extern __shared__ __align__(16) int32_t dyn[];          // NNCHAIN: [flat image (sum32)][exp terms: rpb x n]
-    __shared__ int16_t  tab[k16_tab_bytes / 2];
-    __shared__ int16_t  fine[k_mode == M_MONTE ? 2 * k16_monte_n : 2];
+    extern __shared__ __align__(16) int32_t dyn[];          // NNCHAIN: [sb knots (sum32)][exp terms: rpb x n]
+    __shared__ __align__(16) int16_t tab[k16_tab_bytes16 / 2];
+    __shared__ __align__(16) int16_t fine[k_mode == M_MONTE ? 2 * k16_monte_n : 8];
     __shared__ uint32_t s_max[32][4];
     __shared__ uint32_t s_tot[32];
     constexpr uint32_t NEG_INF = FMT == 16 ? 0xFFFFu : 0xFFFFFFFFu;
+    const bool NN = FMT == 16 && NNCHAIN && nn_ok != 0;
     if constexpr (FMT == 16) {
-        for (int i = threadIdx.x; i < k16_tab_bytes / 2; i += blockDim.x) tab[i] = T.sbdb16[i];
-        if constexpr (k_mode == M_MONTE) for (int i = threadIdx.x; i < 2 * k16_monte_n; i += blockDim.x) fine[i] = T.monte16[i];
+        norm_tables(T, tab, fine);
+        if (NN) nn_tables(T, dyn);
+        cp_async_commit();
+        cp_async_wait<0>();
     }
     __syncthreads();
     const int64_t n = s.ne[0];
@@ -1355,9 +1391,7 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     }
     __syncthreads();
     // pass 2: c = exp(v - max) into work (and, for the non-negative chain, shared memory)
-    const bool NN = FMT == 16 && NNCHAIN && nn_ok != 0;
     uint16_t * cs = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + NN_TAB);
-    if (NN) nn_tables(T, dyn);
     for (int r = warp; r < nr; r += 4) {
         const int64_t row = row0 + r;
         const uint32_t mx = s_max[r][0];
@@ -1446,6 +1480,11 @@ __device__ __forceinline__ uint32_t silu16(const dev_tables & T, uint32_t x) {
     return div16(x, add16(0x4000u, e, T.sbdb16));
 }
 __device__ __forceinline__ uint32_t relu16(uint32_t x) { return ((x & 0x8000u) || (x & 0x7FFFu) == 0) ? 0u : x; }
+// xlns32: the same form, exp through float as in the xlns32 softmax
+__device__ __forceinline__ uint32_t silu32(const dev_tables & T, uint32_t x) {
+    return div32(x, add32(T, 0x40000000u, exp32(T, x ^ 0x80000000u)));
+}
+__device__ __forceinline__ uint32_t relu32(uint32_t x) { return ((x & 0x80000000u) || (x & 0x7FFFFFFFu) == 0) ? 0u : x; }
 
 #define LNSB_GRID_STRIDE(i, n) \
     for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < (n); i += (int64_t) blockDim.x * gridDim.x)
@@ -1477,20 +1516,26 @@ __global__ void k_scale(dev_tables T, const float * __restrict__ src, float * __
     }
 }
 
-template <int OP>
-__global__ void k_unary16(dev_tables T, const float * __restrict__ src, float * __restrict__ dst, int64_t n) {
+template <int FMT, int OP>
+__global__ void k_unary(dev_tables T, const float * __restrict__ src, float * __restrict__ dst, int64_t n) {
+    using A = ew<FMT>;
     LNSB_GRID_STRIDE(i, n) {
-        const uint32_t v = from_f32_16(T, src[i]);
-        dst[i] = to_f32_16(T, OP == LNSB_UNARY_SILU ? silu16(T, v) : relu16(v));
+        const uint32_t v = A::from(T, src[i]);
+        uint32_t r;
+        if constexpr (FMT == 16) r = OP == LNSB_UNARY_SILU ? silu16(T, v) : relu16(v);
+        else                     r = OP == LNSB_UNARY_SILU ? silu32(T, v) : relu32(v);
+        dst[i] = A::to(T, r);
     }
 }
 
-__global__ void k_swiglu16(dev_tables T, const float * __restrict__ gate, const float * __restrict__ up, int64_t gs,
-                           int64_t us, float * __restrict__ dst, int64_t nc, int64_t nr) {
+template <int FMT>
+__global__ void k_swiglu(dev_tables T, const float * __restrict__ gate, const float * __restrict__ up, int64_t gs,
+                         int64_t us, float * __restrict__ dst, int64_t nc, int64_t nr) {
+    using A = ew<FMT>;
     LNSB_GRID_STRIDE(i, nc * nr) {
         const int64_t r = i / nc, c = i - r * nc;
-        const uint32_t g = from_f32_16(T, gate[r * gs + c]), u = from_f32_16(T, up[r * us + c]);
-        dst[i] = to_f32_16(T, mul16(silu16(T, g), u));
+        const uint32_t g = A::from(T, gate[r * gs + c]), u = A::from(T, up[r * us + c]);
+        dst[i] = A::to(T, A::mul(FMT == 16 ? silu16(T, g) : silu32(T, g), u));
     }
 }
 
@@ -1678,8 +1723,9 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
 constexpr int NN_SMEM_MAX = 200 * 1024;      // dynamic shared memory of a normaliser block, at most
 
 // raises a kernel's dynamic shared memory limit once per device and kernel
+// (whenever it takes any: the default 48 KB covers static and dynamic together)
 int nn_smem_attr(const void * kern, int bytes) {
-    if (bytes <= 48 * 1024) return 0;
+    if (bytes <= 0) return 0;
     int dev = 0;
     const int ds = current_device(&dev);
     if (ds != 0) return ds;
@@ -2074,29 +2120,37 @@ int lnsb_scale(int fmt, const float * src, float * dst, int64_t n, float sv, flo
 
 int lnsb_unary(int fmt, int op, const float * src, float * dst, int64_t n, lnsb_stream_t stream) {
     if (!valid_fmt(fmt) || op < LNSB_UNARY_SILU || op > LNSB_UNARY_TANH || n < 0) return LNSB_E_INVALID;
-    if (fmt != LNSB_XLNS16 || (op != LNSB_UNARY_SILU && op != LNSB_UNARY_RELU)) return LNSB_E_UNSUPPORTED;
+    if (op != LNSB_UNARY_SILU && op != LNSB_UNARY_RELU) return LNSB_E_UNSUPPORTED;
     if (n == 0) return 0;
     if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
     const dev_tables * T = nullptr;
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (op == LNSB_UNARY_SILU) k_unary16<LNSB_UNARY_SILU><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
-    else                       k_unary16<LNSB_UNARY_RELU><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
+    const unsigned g = grid_for(n, 256);
+    if (fmt == LNSB_XLNS16) {
+        if (op == LNSB_UNARY_SILU) k_unary<16, LNSB_UNARY_SILU><<<g, 256, 0, s>>>(*T, src, dst, n);
+        else                       k_unary<16, LNSB_UNARY_RELU><<<g, 256, 0, s>>>(*T, src, dst, n);
+    } else {
+        if (op == LNSB_UNARY_SILU) k_unary<32, LNSB_UNARY_SILU><<<g, 256, 0, s>>>(*T, src, dst, n);
+        else                       k_unary<32, LNSB_UNARY_RELU><<<g, 256, 0, s>>>(*T, src, dst, n);
+    }
     return launch_status();
 }
 
 int lnsb_glu(int fmt, int op, const float * gate, const float * up, int64_t gate_stride, int64_t up_stride, float * dst,
              int64_t ncols, int64_t nrows, lnsb_stream_t stream) {
     if (!valid_fmt(fmt) || (op != LNSB_GLU_SWIGLU && op != LNSB_GLU_GEGLU) || ncols < 0 || nrows < 0) return LNSB_E_INVALID;
-    if (fmt != LNSB_XLNS16 || op != LNSB_GLU_SWIGLU) return LNSB_E_UNSUPPORTED;
+    if (op != LNSB_GLU_SWIGLU) return LNSB_E_UNSUPPORTED;
     if (ncols == 0 || nrows == 0) return 0;
     if (gate == nullptr || up == nullptr || dst == nullptr || gate_stride < ncols || up_stride < ncols) return LNSB_E_INVALID;
     const dev_tables * T = nullptr;
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
-    k_swiglu16<<<grid_for(ncols * nrows, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(*T, gate, up, gate_stride,
-                                                                                            up_stride, dst, ncols, nrows);
+    const unsigned g = grid_for(ncols * nrows, 256);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (fmt == LNSB_XLNS16) k_swiglu<16><<<g, 256, 0, s>>>(*T, gate, up, gate_stride, up_stride, dst, ncols, nrows);
+    else                    k_swiglu<32><<<g, 256, 0, s>>>(*T, gate, up, gate_stride, up_stride, dst, ncols, nrows);
     return launch_status();
 }
 

@@ -45,7 +45,7 @@ void build16(host_tables & t) {
         const int d = i * 4 - k16_key_max, ad = d < 0 ? -d : d;
         if (ad <= k16_key_max) t.key16s[i] = t.key16[ad / 4];
     }
-    t.sbdb16.resize((k16_tab_bytes + 15) / 16 * 8, 0);     // padded to 16 bytes for cp.async copies
+    t.sbdb16.resize(k16_tab_bytes16 / 2, 0);               // padded to 16 bytes for cp.async copies
 
     t.conv16.resize(65536);
     for (uint32_t i = 0; i < 65536; i++) {
@@ -175,6 +175,10 @@ void build_flat32(host_tables & t) {
         return true;
     };
     bool ok = true;
+    for (int s = 0; s <= 26; s++) {
+        const bool hi = s >= k32f_sb_split;
+        ok = ok && f[k32f_desc + s] == (((hi ? k32f_sb_base1 : k32f_sb) << 5) | (hi ? k32f_sb_sh1 : k32f_sb_sh0));
+    }
     for (const auto & sg : t.sb_seg) ok = ok && fits(sg, k32f_sb);
     for (const auto & sg : t.db_seg) ok = ok && fits(sg, k32f_db);
     if (!ok) f.clear();

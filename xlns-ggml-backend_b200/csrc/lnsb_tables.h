@@ -28,6 +28,7 @@ namespace lnsb {
 //                       is not representable in 16 bits; n = 0 is handled by the caller)
 constexpr int k16_sign_off   = 4096;   // byte offset of the db half == sign flag value
 constexpr int k16_tab_bytes  = 6660;
+constexpr int k16_tab_bytes16 = (k16_tab_bytes + 15) / 16 * 16;   // the device copy, padded for 16-byte copies
 constexpr int k16_ess        = 1280;
 constexpr int k16_ess_clamp2 = 2 * (k16_ess + 1);   // 2562: clamp of 2n, entry is 0
 
@@ -89,6 +90,14 @@ constexpr int     k32f_dsc2    = 25190;         // 8-byte aligned
 constexpr int     k32f_dsc2_db = 40;            // db entries on other banks than sb's
 constexpr int     k32f_dms     = 25324;
 constexpr int     k32f_words   = 25392;         // multiple of 4 (16-byte copies)
+// the sb descriptors as constants (the non-negative chains compute them
+// instead of loading them): s < k32f_sb_split: (k32f_sb, k32f_sb_sh0), else
+// (k32f_sb_base1, k32f_sb_sh1); build_flat32 checks them against the image
+constexpr int     k32f_sb_split = 8;
+constexpr int     k32f_sb_sh0   = 13;
+constexpr int     k32f_sb_sh1   = 16;
+constexpr int     k32f_sb_base1 = 7169;        // 8193 knots of the first segment - (8 << 23 >> 16)
+constexpr int     k32f_sb_bytes16 = (k32f_db * 4 + 15) / 16 * 16;   // the sb knots, in 16-byte pieces
 constexpr int32_t k32f_none    = -(1 << 30);
 
 struct host_tables {

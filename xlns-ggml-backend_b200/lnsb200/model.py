@@ -117,11 +117,13 @@ class GpuOps:
     """The graph's ops through liblnsb200_<mode>.so on one CUDA device (torch
     for memory and the non-arithmetic reshapes)."""
 
-    def __init__(self, cfg, weights, mode="sum32", n_ctx=256, stream=None):
+    def __init__(self, cfg, weights, mode="sum32", n_ctx=256, stream=None, fmt=16):
         import torch
         import lnsb200
         self.torch, self.cfg, self.n_ctx = torch, cfg, n_ctx
-        self.ks = lnsb200.KernelSet(16, mode)
+        self.fmt = fmt
+        self.cdt = torch.int16 if fmt == 16 else torch.int32             # LNS code storage
+        self.ks = lnsb200.KernelSet(fmt, mode)
         self.ks.upload_tables()
         self.stream = stream
         self.dev = torch.device("cuda", torch.cuda.current_device())
@@ -155,7 +157,7 @@ class GpuOps:
         torch = self.torch
         M, K = rows.shape
         src = torch.from_numpy(np.ascontiguousarray(rows)).to(self.dev)
-        dst = torch.empty(K * M, dtype=torch.int16, device=self.dev)
+        dst = torch.empty(K * M, dtype=self.cdt, device=self.dev)
         self.ks.to_lns_transposed(src, dst, M, K, M)
         torch.cuda.synchronize()
         return (dst, K, M)
@@ -193,7 +195,7 @@ class GpuOps:
     def linear(self, wt, x):
         codes, K, M = wt
         N = x.numel() // K
-        xl = self.torch.empty(N * K, dtype=self.torch.int16, device=self.dev)
+        xl = self.torch.empty(N * K, dtype=self.cdt, device=self.dev)
         self.ks.to_lns(x, xl, stream=self.stream)
         out = self._f32(N, M)
         self.ks.mul_mat(codes, xl, out, K, M, N, stream=self.stream)
@@ -232,24 +234,24 @@ class GpuOps:
         ks.f16_to_f32(self.vc[il][:nkv], vf, vf.numel(), stream=self.stream)
         kh = kf.view(nkv, HKV, D).permute(1, 0, 2).contiguous()          # [h][token][dim] F32
         vh = vf.view(nkv, HKV, D).permute(1, 0, 2).contiguous()
-        kl = torch.empty(HKV * D * nkv, dtype=torch.int16, device=self.dev)
-        vl = torch.empty(HKV * nkv * D, dtype=torch.int16, device=self.dev)
+        kl = torch.empty(HKV * D * nkv, dtype=self.cdt, device=self.dev)
+        vl = torch.empty(HKV * nkv * D, dtype=self.cdt, device=self.dev)
         for h in range(HKV):
             ks.to_lns_transposed(kh[h], kl[h * D * nkv:(h + 1) * D * nkv], nkv, D, nkv, stream=self.stream)
         ks.to_lns(vh, vl, stream=self.stream)
         # kq[h][t][k] = sum_d K[k][d] q[t][d], q head h on kv head h / (H / HKV)
         qh = q.view(T, H, D).permute(1, 0, 2).contiguous()                # [h][t][dim]
-        ql = torch.empty(qh.numel(), dtype=torch.int16, device=self.dev)
+        ql = torch.empty(qh.numel(), dtype=self.cdt, device=self.dev)
         ks.to_lns(qh, ql, stream=self.stream)
         kq = self._f32(H, T, nkv)
         ks.mul_mat(kl, ql, kq, D, nkv, T, (HKV, 1, H, 1), stream=self.stream)
         # causal mask rows pos0 .. pos0+T-1, scale 1/sqrt(head_dim)
         mask = self.mask_full[pos0:pos0 + T, :nkv].contiguous()
         p = self._f32(H, T, nkv)
-        work = torch.empty(p.numel(), dtype=torch.int16, device=self.dev)
+        work = torch.empty(p.numel(), dtype=self.cdt, device=self.dev)
         ks.soft_max(kq, (nkv, T, H, 1), p, work, mask, (nkv, T, 1, 1), 1.0 / math.sqrt(D), stream=self.stream)
         # o[h][t][d] = sum_k V[k][d] p[h][t][k]
-        pl = torch.empty(p.numel(), dtype=torch.int16, device=self.dev)
+        pl = torch.empty(p.numel(), dtype=self.cdt, device=self.dev)
         ks.to_lns(p, pl, stream=self.stream)
         o = self._f32(H, T, D)
         ks.mul_mat(vl, pl, o, nkv, D, T, (HKV, 1, H, 1), stream=self.stream)
@@ -318,9 +320,20 @@ class OracleOps:
     """The same ops on the CPU through the oracle (test infrastructure only:
     the checker of GpuOps)."""
 
-    def __init__(self, cfg, weights, mode="sum32", n_ctx=256, nthreads=8):
+    def __init__(self, cfg, weights, mode="sum32", n_ctx=256, nthreads=8, fmt=16):
         import oracle
-        self.o, self.cfg, self.mode, self.nt = oracle, cfg, mode, nthreads
+        self.o, self.cfg, self.mode, self.nt, self.fmt = oracle, cfg, mode, nthreads, fmt
+        o = oracle
+        if fmt == 16:
+            self.to_c, self.to_f, self.mask_c = o.from_f32_16, o.to_f32_16, o.mask16
+            self.mm = lambda w, x, **kw: o.mul_mat16(mode, w, x, **kw)
+            self.rms = lambda c, nc, nr, eps: o.rms_norm16(mode, c, nc, nr, eps, nthreads=nthreads)
+            self.smax = lambda c, shp, m, mshp, sc: o.soft_max16(mode, c, shp, m, mshp, sc, nthreads=nthreads)
+        else:
+            self.to_c, self.to_f, self.mask_c = o.from_f32_32, o.to_f32_32, o.mask32
+            self.mm = lambda w, x, **kw: o.mul_mat32(w, x, **kw)
+            self.rms = lambda c, nc, nr, eps: o.rms_norm32(c, nc, nr, eps, nthreads=nthreads)
+            self.smax = lambda c, shp, m, mshp, sc: o.soft_max32(c, shp, m, mshp, sc, nthreads=nthreads)
         self.weights = weights
         self.wc = {}
         kvd = cfg["n_head_kv"] * cfg["head_dim"]
@@ -336,7 +349,7 @@ class OracleOps:
             else:
                 v = self.weights["layers"][il][name]
             if v.ndim == 2:
-                v = self.o.from_f32_16(v)                      # weight codes, rows [M][K]
+                v = self.to_c(v)                               # weight codes, rows [M][K]
             self.wc[key] = v
         return self.wc[key]
 
@@ -344,25 +357,25 @@ class OracleOps:
         return self.weights["tok_embd"][ids].copy()
 
     def rms_norm(self, x, eps):
-        c = self.o.from_f32_16(x)
-        r = self.o.rms_norm16(self.mode, c.ravel(), x.shape[-1], x.size // x.shape[-1], eps, nthreads=self.nt)
-        return self.o.to_f32_16(r).reshape(x.shape)
+        c = self.to_c(x)
+        r = self.rms(c.ravel(), x.shape[-1], x.size // x.shape[-1], eps)
+        return self.to_f(r).reshape(x.shape)
 
     def mul(self, x, wv):
-        return self.o.binary16("mul", x, wv.reshape(1, -1))
+        return self.o.binary16("mul", x, wv.reshape(1, -1), fmt=self.fmt)
 
     def add(self, a, b):
-        return self.o.binary16("add", a, b)
+        return self.o.binary16("add", a, b, fmt=self.fmt)
 
     def linear(self, w, x):
-        xc = self.o.from_f32_16(x.reshape(-1, w.shape[1]))
-        return self.o.to_f32_16(self.o.mul_mat16(self.mode, w, xc, nthreads=self.nt)).reshape(-1, w.shape[0])
+        xc = self.to_c(x.reshape(-1, w.shape[1]))
+        return self.to_f(self.mm(w, xc, nthreads=self.nt)).reshape(-1, w.shape[0])
 
     def linears(self, il, names, x):
         return [self.linear(self.w(il, n), x) for n in names]
 
     def rope(self, x, T, nh, hd, pos0):
-        return self.o.rope16(x.reshape(1, T, nh, hd), self.rope_cs[pos0:pos0 + T], hd).reshape(T, nh * hd)
+        return self.o.rope16(x.reshape(1, T, nh, hd), self.rope_cs[pos0:pos0 + T], hd, fmt=self.fmt).reshape(T, nh * hd)
 
     def kv_store(self, il, k, v, pos0, T):
         self.kc[il][pos0:pos0 + T] = k.astype(np.float16)
@@ -373,24 +386,64 @@ class OracleOps:
         nkv = pos0 + T
         kf = self.kc[il][:nkv].astype(np.float32).reshape(nkv, HKV, D)
         vf = self.vc[il][:nkv].astype(np.float32).reshape(nkv, HKV, D)
-        kw = o.from_f32_16(np.ascontiguousarray(kf.transpose(1, 0, 2)))          # [h][token][dim]: rows M=token, K=dim
-        vw = o.from_f32_16(np.ascontiguousarray(vf.transpose(1, 2, 0)))          # [h][dim][token]: rows M=dim, K=token
-        qc = o.from_f32_16(np.ascontiguousarray(q.reshape(T, H, D).transpose(1, 0, 2)))
-        kq = o.to_f32_16(o.mul_mat16(self.mode, kw.reshape(1, HKV, nkv, D), qc.reshape(1, H, T, D),
-                                     slices=(HKV, 1, H, 1), nthreads=self.nt)).reshape(H, T, nkv)
+        kw = self.to_c(np.ascontiguousarray(kf.transpose(1, 0, 2)))            # [h][token][dim]: rows M=token, K=dim
+        vw = self.to_c(np.ascontiguousarray(vf.transpose(1, 2, 0)))            # [h][dim][token]: rows M=dim, K=token
+        qc = self.to_c(np.ascontiguousarray(q.reshape(T, H, D).transpose(1, 0, 2)))
+        kq = self.to_f(self.mm(kw.reshape(1, HKV, nkv, D), qc.reshape(1, H, T, D), slices=(HKV, 1, H, 1),
+                               nthreads=self.nt)).reshape(H, T, nkv)
         m = np.triu(np.full((T + pos0, T + pos0), -np.inf, np.float32), 1)[pos0:pos0 + T, :nkv]
-        sc = int(o.from_f32_16(np.array([1.0 / math.sqrt(D)], np.float32))[0])
-        p = o.to_f32_16(o.soft_max16(self.mode, o.from_f32_16(kq).ravel(), (nkv, T, H, 1), o.mask16(m).ravel(),
-                                     (nkv, T, 1, 1), sc, nthreads=self.nt)).reshape(H, T, nkv)
-        out = o.to_f32_16(o.mul_mat16(self.mode, vw.reshape(1, HKV, D, nkv), o.from_f32_16(p).reshape(1, H, T, nkv),
-                                      slices=(HKV, 1, H, 1), nthreads=self.nt)).reshape(H, T, D)
+        sc = int(self.to_c(np.array([1.0 / math.sqrt(D)], np.float32))[0])
+        p = self.to_f(self.smax(self.to_c(kq).ravel(), (nkv, T, H, 1), self.mask_c(m).ravel(), (nkv, T, 1, 1),
+                                sc)).reshape(H, T, nkv)
+        out = self.to_f(self.mm(vw.reshape(1, HKV, D, nkv), self.to_c(p).reshape(1, H, T, nkv), slices=(HKV, 1, H, 1),
+                                nthreads=self.nt)).reshape(H, T, D)
         return np.ascontiguousarray(out.transpose(1, 0, 2)).reshape(T, H * D)
 
     def swiglu(self, gate, up):
-        return self.o.swiglu16(gate, up)
+        return self.o.swiglu16(gate, up, fmt=self.fmt)
 
     def last_row(self, x):
         return x[-1:].copy()
 
     def argmax(self, logits):
         return int(np.argmax(logits.ravel()))
+
+
+def main(argv=None):
+    """command line: prefill a random prompt and greedy-decode on cuda:0,
+    printing the tokens and the device time of each phase"""
+    import argparse
+    import json
+    import torch
+    p = argparse.ArgumentParser(description=main.__doc__)
+    p.add_argument("--fmt", type=int, default=16, choices=(16, 32))
+    p.add_argument("--mode", default="sum32", help="xlns16 sum mode library (base, monte, lpvip, sum32)")
+    p.add_argument("--prompt", type=int, default=128)
+    p.add_argument("--gen", type=int, default=16)
+    p.add_argument("--eager", action="store_true", help="decode without CUDA graphs")
+    a = p.parse_args(argv)
+    cfg = SMOLLM2_135M
+    g = GpuOps(cfg, init_weights(cfg, seed=2), mode=a.mode, n_ctx=a.prompt + a.gen + 1, fmt=a.fmt)
+    prompt = prompt_ids(cfg, a.prompt, seed=2)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    if not a.eager:
+        dec = GraphDecoder(g, cfg)
+        dec.prepare(a.prompt, a.prompt + a.gen - 1)
+    torch.cuda.synchronize()
+    ev[0].record()
+    toks = [g.argmax(forward(g, cfg, prompt, 0))]
+    ev[1].record()
+    if a.eager:
+        for pos in range(a.prompt, a.prompt + a.gen - 1):
+            toks.append(g.argmax(forward(g, cfg, [toks[-1]], pos)))
+    else:
+        toks += dec.decode(toks[0], a.prompt, a.gen - 1)
+    ev[2].record()
+    torch.cuda.synchronize()
+    print(json.dumps({"format": "xlns%d" % a.fmt, "mode": a.mode if a.fmt == 16 else None, "tokens": toks,
+                      "prefill_ms": ev[0].elapsed_time(ev[1]),
+                      "decode_ms_per_token": ev[1].elapsed_time(ev[2]) / max(1, a.gen - 1)}))
+
+
+if __name__ == "__main__":
+    main()
