@@ -155,9 +155,36 @@ int lnsb_rms_norm(int fmt, const float * src, float * dst, int64_t ncols, int64_
 int lnsb_rms_norm_lns(int fmt, const void * src, void * dst, int64_t ncols, int64_t nrows, float eps,
                       uint16_t monte_seed, lnsb_stream_t stream);
 
-/* ---- Monte state: one LFSR per process, seed 7 (ggml-lns.h:13-24).  All
- *      return 0 on success, LNSB_E_UNSUPPORTED outside a monte build;
- *      set_state rejects 0 (absorbing). ---- */
+/* ---- MUL_MAT_ID: the expert-selected product of mixture-of-experts FFNs
+ * (lns-backend/src/lns-ops.cpp:394-462; the reference's GPU backend declines
+ * the op and ggml runs it on the CPU backend).  For token t and slot s the
+ * weight slice is expert e = ids[t * ids_stride + s] and the activation row is
+ * x[t][s % ne11] (slot-based broadcast):
+ *   dst[t][s][m] = sum_k w[e][k][m] * x[t][s % ne11][k], sequential over k
+ *   w    LNS, n_expert slices of K x M, k-major: (e, k, m) at (e * K + k) * M + m
+ *   x    LNS, [n_tokens][ne11][K], n_used % ne11 == 0
+ *   ids  int32, device memory
+ *   dst  F32 [n_tokens][n_used][M]
+ * Monte: chain (t, s, m) starts ((t * n_used + s) * M + m) * (K - 1) draws
+ * after monte_seed, the CPU loop order.  An id outside [0, n_expert) gives the
+ * zero code for its slot's outputs and is counted (lnsb_mul_mat_id_bad_ids)
+ * where the reference aborts. ---- */
+typedef struct {
+    const void *    w;
+    const void *    x;
+    const int32_t * ids;
+    float *         dst;
+    int64_t         K, M, n_expert, ne11, n_used, n_tokens, ids_stride;
+    uint16_t        monte_seed;
+} lnsb_mul_mat_id_args;
+int lnsb_mul_mat_id(int fmt, const lnsb_mul_mat_id_args * args, lnsb_stream_t stream);
+/* LNS codes out: dst_lns [n_tokens][n_used][M] (args->dst is ignored) */
+int lnsb_mul_mat_id_lns(int fmt, const lnsb_mul_mat_id_args * args, void * dst_lns, lnsb_stream_t stream);
+uint64_t lnsb_mul_mat_id_draws(int fmt, const lnsb_mul_mat_id_args * args);
+/* out-of-range ids met on the current device since the last call; reads and
+ * clears the count (synchronises with the device) */
+int lnsb_mul_mat_id_bad_ids(int64_t * count);
+
 /* ---- Elementwise ops of the model graph (kernel_set::binary / scale /
  * unary / glu / rope, lns-cuda-kernels.h:116-138; lns-backend/src/lns-ops.cpp:
  * 468-599, 786-868, 1199-1281).  F32 in and out, as at every ggml op
@@ -204,6 +231,9 @@ int lnsb_rope(int fmt, const lnsb_rope_args * args, lnsb_stream_t stream);
 int lnsb_f32_to_f16(const float * src, uint16_t * dst, int64_t n, lnsb_stream_t stream);
 int lnsb_f16_to_f32(const uint16_t * src, float * dst, int64_t n, lnsb_stream_t stream);
 
+/* ---- Monte state: one LFSR per process, seed 7 (ggml-lns.h:13-24).  All
+ *      return 0 on success, LNSB_E_UNSUPPORTED outside a monte build;
+ *      set_state rejects 0 (absorbing). ---- */
 int lnsb_monte_get_state(uint16_t * state);
 int lnsb_monte_set_state(uint16_t state);
 /* *start = current state, then advance it by `draws` steps (lns-ops.cpp:178-195) */

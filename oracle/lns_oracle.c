@@ -671,6 +671,68 @@ void orc32_mul_mat(const uint32_t * w, const uint32_t * x, uint32_t * dst,
     }
 }
 
+/* MUL_MAT_ID (lns-backend/src/lns-ops.cpp:394-462): for token t and slot s,
+ * dst[t][s][m] = vec_dot(w[ids[t][s]][m], x[t][s % ne11]) (slot-based
+ * broadcast of the activation rows), the chains in the loop order (t, s, m),
+ * so the Monte chain o = (t * n_used + s) * M + m starts o * (K - 1) draws
+ * after the seed.  w: [n_expert][M][K] weight rows, x: [n_tokens][ne11][K],
+ * ids: ids[t * ids_stride + s].  Returns the number of out-of-range ids (their
+ * outputs are the zero code; the reference aborts on them). */
+int64_t orc16_mul_mat_id(int mode, const uint16_t * w, const uint16_t * x, const int32_t * ids, uint16_t * dst,
+                         int64_t K, int64_t M, int64_t n_expert, int64_t ne11, int64_t n_used, int64_t n_tokens,
+                         int64_t ids_stride, uint16_t monte_seed, int nthreads) {
+    const int64_t total = n_tokens * n_used * M;
+    int64_t bad = 0;
+    (void)nthreads;
+#ifdef _OPENMP
+    #pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1) reduction(+:bad)
+#endif
+    for (int64_t o = 0; o < total; o++) {
+        const int64_t m = o % M, z = o / M, s = z % n_used, t = z / n_used;
+        const int32_t e = ids[t * ids_stride + s];
+        uint16_t out = X16_ZERO;
+        if (e < 0 || e >= n_expert) {
+            if (m == 0) bad++;
+        } else if (K > 0) {
+            const uint16_t * wr = w + ((int64_t)e * M + m) * K;
+            const uint16_t * xr = x + (t * ne11 + s % ne11) * K;
+            red_t r;
+            r.st = stochastic(mode) ? orc_lfsr_jump(monte_seed, (uint64_t)o * (uint64_t)(K - 1)) : 0;
+            red_from(mode, &r, orc16_mul(wr[0], xr[0]));
+            for (int64_t k = 1; k < K; k++) red_add(mode, &r, orc16_mul(wr[k], xr[k]));
+            out = red_finish(mode, &r);
+        }
+        dst[o] = out;
+    }
+    return bad;
+}
+
+int64_t orc32_mul_mat_id(const uint32_t * w, const uint32_t * x, const int32_t * ids, uint32_t * dst,
+                         int64_t K, int64_t M, int64_t n_expert, int64_t ne11, int64_t n_used, int64_t n_tokens,
+                         int64_t ids_stride, int nthreads) {
+    const int64_t total = n_tokens * n_used * M;
+    int64_t bad = 0;
+    (void)nthreads;
+#ifdef _OPENMP
+    #pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1) reduction(+:bad)
+#endif
+    for (int64_t o = 0; o < total; o++) {
+        const int64_t m = o % M, z = o / M, s = z % n_used, t = z / n_used;
+        const int32_t e = ids[t * ids_stride + s];
+        uint32_t acc = 0;
+        if (e < 0 || e >= n_expert) {
+            if (m == 0) bad++;
+        } else if (K > 0) {
+            const uint32_t * wr = w + ((int64_t)e * M + m) * K;
+            const uint32_t * xr = x + (t * ne11 + s % ne11) * K;
+            acc = mul32(wr[0], xr[0]);
+            for (int64_t k = 1; k < K; k++) acc = add32(acc, mul32(wr[k], xr[k]));
+        }
+        dst[o] = acc;
+    }
+    return bad;
+}
+
 /* k_soft_max (lns-cuda-kernels.cuh:255-325) = xlns16_softmax[_masked]
  * (lns16-sum32.h:158-198 shows the control flow) */
 void orc16_soft_max(int mode, const uint16_t * src, const int64_t ne[4], const uint16_t * mask,

@@ -86,6 +86,12 @@ uint64_t orc_rms_norm_draws(int mode, int64_t ncols, int64_t nrows);
 void orc16_mul_mat(int mode, const uint16_t * w, const uint16_t * x, uint16_t * dst,
                    int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne03, int64_t ne12, int64_t ne13,
                    uint16_t monte_seed, int nthreads);
+int64_t orc16_mul_mat_id(int mode, const uint16_t * w, const uint16_t * x, const int32_t * ids, uint16_t * dst,
+                         int64_t K, int64_t M, int64_t n_expert, int64_t ne11, int64_t n_used, int64_t n_tokens,
+                         int64_t ids_stride, uint16_t monte_seed, int nthreads);
+int64_t orc32_mul_mat_id(const uint32_t * w, const uint32_t * x, const int32_t * ids, uint32_t * dst,
+                         int64_t K, int64_t M, int64_t n_expert, int64_t ne11, int64_t n_used, int64_t n_tokens,
+                         int64_t ids_stride, int nthreads);
 void orc32_mul_mat(const uint32_t * w, const uint32_t * x, uint32_t * dst,
                    int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne03, int64_t ne12, int64_t ne13,
                    int nthreads);

@@ -31,6 +31,7 @@ def lib():
         L = ctypes.CDLL(SO)
         u16p = np.ctypeslib.ndpointer(np.uint16, flags="C")
         u32p = np.ctypeslib.ndpointer(np.uint32, flags="C")
+        i32p = np.ctypeslib.ndpointer(np.int32, flags="C")
         f32p = np.ctypeslib.ndpointer(np.float32, flags="C")
         i64 = ctypes.c_int64
         i64a = ctypes.POINTER(ctypes.c_int64)
@@ -50,6 +51,9 @@ def lib():
             "orc16_mul_mat": (None, [ctypes.c_int, u16p, u16p, u16p, i64, i64, i64, i64, i64, i64, i64,
                                      ctypes.c_uint16, ctypes.c_int]),
             "orc32_mul_mat": (None, [u32p, u32p, u32p, i64, i64, i64, i64, i64, i64, i64, ctypes.c_int]),
+            "orc16_mul_mat_id": (i64, [ctypes.c_int, u16p, u16p, i32p, u16p, i64, i64, i64, i64, i64, i64, i64,
+                                       ctypes.c_uint16, ctypes.c_int]),
+            "orc32_mul_mat_id": (i64, [u32p, u32p, i32p, u32p, i64, i64, i64, i64, i64, i64, i64, ctypes.c_int]),
             "orc16_soft_max": (None, [ctypes.c_int, u16p, i64a, ctypes.c_void_p, i64a, ctypes.c_uint16, u16p,
                                       ctypes.c_uint16, ctypes.c_int]),
             "orc32_soft_max": (None, [u32p, i64a, ctypes.c_void_p, i64a, ctypes.c_uint32, u32p, ctypes.c_int]),
@@ -209,6 +213,27 @@ def mul_mat32(w_rows, x, slices=(1, 1, 1, 1), nthreads=1):
     out = np.empty(ne12 * ne13 * N * M, np.uint32)
     lib().orc32_mul_mat(w, xx, out, K, M, N, ne02, ne03, ne12, ne13, nthreads)
     return out.reshape(ne13, ne12, N, M) if (ne12 * ne13) > 1 else out.reshape(N, M)
+
+
+def mul_mat_id(fmt, mode, w_rows, x, ids, seed=7, nthreads=1):
+    """MUL_MAT_ID: w_rows codes [n_expert][M][K], x codes [n_tokens][ne11][K],
+    ids int32 [n_tokens][n_used]; returns (codes [n_tokens][n_used][M], number
+    of out-of-range ids)."""
+    n_expert, M, K = w_rows.shape
+    n_tokens, ne11 = x.shape[0], x.shape[1]
+    ids = np.ascontiguousarray(ids, np.int32)
+    n_used = ids.shape[1]
+    dt = np.uint16 if fmt == 16 else np.uint32
+    w = np.ascontiguousarray(w_rows, dt).reshape(-1)
+    xx = np.ascontiguousarray(x, dt).reshape(-1)
+    out = np.empty(n_tokens * n_used * M, dt)
+    if fmt == 16:
+        bad = lib().orc16_mul_mat_id(MODE[mode], w, xx, ids.reshape(-1), out, K, M, n_expert, ne11, n_used, n_tokens,
+                                     n_used, seed, nthreads)
+    else:
+        bad = lib().orc32_mul_mat_id(w, xx, ids.reshape(-1), out, K, M, n_expert, ne11, n_used, n_tokens, n_used,
+                                     nthreads)
+    return out.reshape(n_tokens, n_used, M), bad
 
 
 def soft_max16(mode, src, shape, mask=None, mask_shape=None, scale_code=0x4000, seed=7, nthreads=1):

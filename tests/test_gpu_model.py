@@ -95,3 +95,21 @@ def test_graph_decode_matches_eager_xlns32():
     dec = model.GraphDecoder(g2, SMALL)
     dec.prepare(len(prompt), len(prompt) + 4)
     assert [first] + dec.decode(first, len(prompt), 4) == eager
+
+
+@pytest.mark.parametrize("policy", ["MUL_MAT:kqv-*=sum32,SOFT_MAX=lpvip,RMS_NORM=monte",
+                                    "MUL_MAT:Kcur-*=sum32,MUL_MAT:<kqv_out-*=lpvip,result_output=sum32"])
+def test_small_model_mixed_policy_bit_exact(policy):
+    """LNS16_SUM_POLICY-style mixed modes (one library per mode): the second
+    policy splits the fused q/k/v product and picks wo by its input's name"""
+    from lnsb200 import model
+    w = model.init_weights(SMALL, seed=2)
+    prompt = model.prompt_ids(SMALL, 6, seed=2)
+    g = model.GpuOps(SMALL, w, mode="base", n_ctx=32, policy=policy)
+    o = model.OracleOps(SMALL, w, mode="base", n_ctx=32, policy=policy)
+    lg, lo = model.forward(g, SMALL, prompt, 0), model.forward(o, SMALL, prompt, 0)
+    assert np.array_equal(lg.cpu().numpy().ravel().view(np.uint32), lo.ravel().view(np.uint32))
+    tg = g.argmax(lg)
+    lg, lo = model.forward(g, SMALL, [tg], 6), model.forward(o, SMALL, [tg], 6)
+    assert np.array_equal(lg.cpu().numpy().ravel().view(np.uint32), lo.ravel().view(np.uint32))
+    assert len(g.kss) > 1

@@ -1208,6 +1208,93 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
     }
 }
 
+// ============================ MUL_MAT_ID ===================================
+// The expert-selected product (lns-backend/src/lns-ops.cpp:394-462): output
+// (t, s, m) is the chain over k of w[e][k][m] * x[t][s % ne11][k] with e the
+// id of slot s of token t.  Units of work are (slot z = t * n_used + s, block
+// of 32 rows), one chain per lane, dealt to warps round-robin; the weights of
+// a warp's rows are one coalesced 64- or 128-byte row per k (k-major expert
+// slices), the activation value is the same for the warp (a broadcast load).
+// The reduction is the build's policy with its tables in shared memory: the
+// flat xlns32 image (xlns32, sum32), or the packed xlns16 table (and the Monte
+// fine tables); LPVIP's singular branch reads its global table.  Monte chain
+// (t, s, m) starts ((t * n_used + s) * M + m) * (K - 1) draws after the seed,
+// the CPU loop order.  An id out of range gives the zero code and is counted.
+__device__ unsigned long long g_bad_ids;      // one per device, as every module variable
+
+template <int FMT> __host__ __device__ constexpr bool mmid_flat() { return FMT == 32 || k_mode == M_SUM32; }
+template <int FMT> __host__ __device__ constexpr int  mmid_smem() {
+    return mmid_flat<FMT>() ? k32f_words * 4 : k16_tab_bytes16 + (k_mode == M_MONTE ? 2 * k16_monte_n * 2 : 0);
+}
+
+template <int FMT, bool OUT_F32>
+__global__ void __launch_bounds__(256)
+k_mul_mat_id(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
+             const typename a32_fmt<FMT>::elem * __restrict__ X, const int32_t * __restrict__ ids,
+             void * __restrict__ dst, int64_t K, int64_t M, int64_t n_expert, int64_t ne11, int64_t n_used,
+             int64_t n_tokens, int64_t ids_stride, uint32_t monte_seed) {
+    using E = typename a32_fmt<FMT>::elem;
+    extern __shared__ __align__(16) unsigned char mmid_sm[];
+    int32_t * F    = reinterpret_cast<int32_t *>(mmid_sm);
+    int16_t * tab  = reinterpret_cast<int16_t *>(mmid_sm);
+    int16_t * fine = reinterpret_cast<int16_t *>(mmid_sm + k16_tab_bytes16);
+    if constexpr (mmid_flat<FMT>()) {
+        stage_async(F, T.flat32, k32f_words * 4);
+    } else {
+        stage_async(tab, T.sbdb16, k16_tab_bytes16);
+        if constexpr (k_mode == M_MONTE) stage_async(fine, T.monte16, 2 * k16_monte_n * 2);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    const int     lane = threadIdx.x & 31;
+    const int64_t RB = (M + 31) / 32, units = n_tokens * n_used * RB;
+    const int64_t nwarps = (int64_t) gridDim.x * (blockDim.x / 32);
+    for (int64_t u = (int64_t) (threadIdx.x >> 5) * gridDim.x + blockIdx.x; u < units; u += nwarps) {
+        const int64_t z = u / RB, rb = u % RB, t = z / n_used, s = z % n_used;
+        const int64_t m = rb * 32 + lane;
+        const int32_t e = __ldg(ids + t * ids_stride + s);
+        uint32_t out = 0u;                              // the zero code
+        if (e < 0 || e >= n_expert) {
+            if (lane == 0 && rb == 0) atomicAdd(&g_bad_ids, 1ull);
+        } else if (K > 0) {
+            const E * wl = W + (int64_t) e * K * M + (m < M ? m : M - 1);
+            const E * xr = X + (t * ne11 + s % ne11) * K;
+            uint32_t st = 0u;
+            if constexpr (FMT == 16 && k_stochastic)
+                st = lfsr_jump(T, monte_seed, (unsigned long long) (z * M + (m < M ? m : M - 1)) * (unsigned long long) (K - 1));
+            red16 R{ &T, tab, fine };
+            uint32_t acc = 0u;
+            for (int64_t k0 = 0; k0 < K; k0 += 8) {
+                uint32_t w8[8], x8[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const bool in = k0 + j < K;
+                    w8[j] = in ? (uint32_t) __ldg(wl + (k0 + j) * M) : 0u;
+                    x8[j] = in ? (uint32_t) __ldg(xr + k0 + j) : 0u;
+                }
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int64_t k = k0 + j;
+                    if (k >= K) break;
+                    if constexpr (FMT == 32) {
+                        const uint32_t p = mul32(w8[j], x8[j]);
+                        acc = k == 0 ? p : add32f(F, acc, p);
+                    } else if constexpr (k_mode == M_SUM32) {
+                        const uint32_t p = mul16(w8[j], x8[j]) << 16;
+                        acc = k == 0 ? p : add32f(F, acc, p);
+                    } else {
+                        const uint32_t p = mul16(w8[j], x8[j]);
+                        acc = k == 0 ? R.from(p) : R.add(acc, p, st);
+                    }
+                }
+            }
+            out = FMT == 16 ? R.finish(acc) : acc;
+        }
+        if (m < M) a32_fmt<FMT>::store(T, dst, z * M + m, out, OUT_F32);
+    }
+}
+
 // ============================ RMS_NORM =====================================
 // Block = up to 32 rows (rpb).  Each lane runs its row's sum-of-squares chain
 // (n additions from zero); the scaling pass is done by the whole block,
@@ -1635,6 +1722,44 @@ int mul_mat_a32(int fmt, const dev_tables & T, const lnsb_mul_mat_args * a, void
     return launch_a32_by<32, 1>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream);
 }
 
+int mul_mat_id_impl(int fmt, const lnsb_mul_mat_id_args * a, void * dst, bool out_f32, cudaStream_t stream) {
+    if (!valid_fmt(fmt) || a == nullptr) return LNSB_E_INVALID;
+    if (a->K < 0 || a->M < 0 || a->n_expert < 0 || a->ne11 <= 0 || a->n_used < 0 || a->n_tokens < 0 ||
+        a->ids_stride < a->n_used)
+        return LNSB_E_INVALID;
+    if (a->n_used % a->ne11 != 0) return LNSB_E_INVALID;          // slot-based broadcast of the activation rows
+    if (a->M == 0 || a->n_used == 0 || a->n_tokens == 0) return 0;
+    if (dst == nullptr || a->ids == nullptr || (a->K > 0 && (a->w == nullptr || a->x == nullptr))) return LNSB_E_INVALID;
+    int dev = 0;
+    const int ds = current_device(&dev);
+    if (ds != 0) return ds;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const int64_t units = a->n_tokens * a->n_used * ((a->M + 31) / 32);
+    const int64_t grid = imin64((units + 7) / 8, (int64_t) sm_count(dev) * 2);
+    static bool attr[2][2][k_max_devices] = {};          // [xlns32][F32 out][device]
+    auto go = [&](auto kern, int smem, auto * w, auto * x) -> int {
+        bool & done = attr[fmt == LNSB_XLNS32][out_f32][dev];
+        if (!done) {
+            const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return (int) e;
+            done = true;
+        }
+        kern<<<(unsigned) grid, 256, smem, stream>>>(*T, w, x, a->ids, dst, a->K, a->M, a->n_expert, a->ne11, a->n_used,
+                                                     a->n_tokens, a->ids_stride, a->monte_seed);
+        return launch_status();
+    };
+    if (fmt == LNSB_XLNS16) {
+        const auto * w = static_cast<const uint16_t *>(a->w);
+        const auto * x = static_cast<const uint16_t *>(a->x);
+        return out_f32 ? go(k_mul_mat_id<16, true>, mmid_smem<16>(), w, x) : go(k_mul_mat_id<16, false>, mmid_smem<16>(), w, x);
+    }
+    const auto * w = static_cast<const uint32_t *>(a->w);
+    const auto * x = static_cast<const uint32_t *>(a->x);
+    return out_f32 ? go(k_mul_mat_id<32, true>, mmid_smem<32>(), w, x) : go(k_mul_mat_id<32, false>, mmid_smem<32>(), w, x);
+}
+
 int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32, cudaStream_t stream) {
     if (!valid_fmt(fmt) || a == nullptr) return LNSB_E_INVALID;
     if (a->K < 0 || a->M < 0 || a->N < 0 || a->ne02 <= 0 || a->ne03 <= 0 || a->ne12 <= 0 || a->ne13 <= 0) return LNSB_E_INVALID;
@@ -1896,6 +2021,12 @@ uint64_t lnsb_mul_mat_draws(int fmt, const lnsb_mul_mat_args * a) {
     return (uint64_t) a->ne12 * (uint64_t) a->ne13 * (uint64_t) a->M * (uint64_t) a->N * (uint64_t) (a->K - 1);
 }
 
+uint64_t lnsb_mul_mat_id_draws(int fmt, const lnsb_mul_mat_id_args * a) {
+    if (fmt != LNSB_XLNS16 || !k_stochastic || a == nullptr || a->K <= 0 || a->M < 0 || a->n_used < 0 || a->n_tokens < 0)
+        return 0;
+    return (uint64_t) a->n_tokens * (uint64_t) a->n_used * (uint64_t) a->M * (uint64_t) (a->K - 1);
+}
+
 uint64_t lnsb_soft_max_draws(int fmt, int64_t ncols, int64_t nrows) {
     return fmt == LNSB_XLNS16 && k_stochastic && ncols > 0 ? (uint64_t) nrows * (uint64_t) (ncols - 1) : 0;
 }
@@ -1997,6 +2128,27 @@ int lnsb_mul_mat(int fmt, const lnsb_mul_mat_args * args, lnsb_stream_t stream) 
 
 int lnsb_mul_mat_lns(int fmt, const lnsb_mul_mat_args * args, void * dst_lns, lnsb_stream_t stream) {
     return mul_mat_impl(fmt, args, dst_lns, false, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_mul_mat_id(int fmt, const lnsb_mul_mat_id_args * args, lnsb_stream_t stream) {
+    return mul_mat_id_impl(fmt, args, args ? args->dst : nullptr, true, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_mul_mat_id_lns(int fmt, const lnsb_mul_mat_id_args * args, void * dst_lns, lnsb_stream_t stream) {
+    return mul_mat_id_impl(fmt, args, dst_lns, false, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_mul_mat_id_bad_ids(int64_t * count) {
+    if (count == nullptr) return LNSB_E_INVALID;
+    unsigned long long v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_bad_ids, sizeof v);
+    if (e == cudaSuccess) {
+        const unsigned long long zero = 0;
+        e = cudaMemcpyToSymbol(g_bad_ids, &zero, sizeof zero);
+    }
+    if (e != cudaSuccess) return (int) e;
+    *count = (int64_t) v;
+    return 0;
 }
 
 int lnsb_soft_max(int fmt, const lnsb_soft_max_args * a, lnsb_stream_t stream) {

@@ -102,6 +102,31 @@ class KernelSet:
         a = self._mm_args(w, x, None, K, M, N, slices, monte_seed)
         _lib.check(self.lib, "lnsb_mul_mat_lns", self.lib.lnsb_mul_mat_lns(self.fmt, ctypes.byref(a), _ptr(dst), _stream(stream)))
 
+    def _mmid_args(self, w, x, ids, dst, K, M, n_expert, ne11, n_used, n_tokens, monte_seed):
+        return _lib.MulMatIdArgs(w.data_ptr(), x.data_ptr(), ids.data_ptr(), dst.data_ptr() if dst is not None else None,
+                                 K, M, n_expert, ne11, n_used, n_tokens, n_used, monte_seed)
+
+    def mul_mat_id(self, w, x, ids, dst, K, M, n_expert, ne11, n_used, n_tokens, monte_seed=7, stream=None):
+        """MUL_MAT_ID: dst (F32, [n_tokens][n_used][M]); w k-major [n_expert][K][M],
+        x [n_tokens][ne11][K], ids int32 [n_tokens][n_used] on the device."""
+        a = self._mmid_args(w, x, ids, dst, K, M, n_expert, ne11, n_used, n_tokens, monte_seed)
+        _lib.check(self.lib, "lnsb_mul_mat_id", self.lib.lnsb_mul_mat_id(self.fmt, ctypes.byref(a), _stream(stream)))
+
+    def mul_mat_id_lns(self, w, x, ids, dst, K, M, n_expert, ne11, n_used, n_tokens, monte_seed=7, stream=None):
+        a = self._mmid_args(w, x, ids, None, K, M, n_expert, ne11, n_used, n_tokens, monte_seed)
+        _lib.check(self.lib, "lnsb_mul_mat_id_lns",
+                   self.lib.lnsb_mul_mat_id_lns(self.fmt, ctypes.byref(a), _ptr(dst), _stream(stream)))
+
+    def mul_mat_id_draws(self, K, M, n_used, n_tokens):
+        a = _lib.MulMatIdArgs(None, None, None, None, K, M, 1, 1, n_used, n_tokens, n_used, 0)
+        return self.lib.lnsb_mul_mat_id_draws(self.fmt, ctypes.byref(a))
+
+    def mul_mat_id_bad_ids(self):
+        """out-of-range ids met on the current device since the last call"""
+        c = ctypes.c_int64()
+        _lib.check(self.lib, "lnsb_mul_mat_id_bad_ids", self.lib.lnsb_mul_mat_id_bad_ids(ctypes.byref(c)))
+        return c.value
+
     def soft_max(self, src, shape, dst, work, mask=None, mask_shape=None, scale=1.0, monte_seed=7, stream=None):
         a = SoftMaxArgs(src.data_ptr(), _shape4(shape), mask.data_ptr() if mask is not None else None,
                         _shape4(mask_shape or (1, 1, 1, 1)), scale, dst.data_ptr(), work.data_ptr(), monte_seed)

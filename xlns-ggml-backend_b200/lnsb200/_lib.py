@@ -27,6 +27,13 @@ class MulMatArgs(ctypes.Structure):
                 ("monte_seed", ctypes.c_uint16)]
 
 
+class MulMatIdArgs(ctypes.Structure):
+    _fields_ = [("w", ctypes.c_void_p), ("x", ctypes.c_void_p), ("ids", ctypes.c_void_p), ("dst", ctypes.c_void_p),
+                ("K", ctypes.c_int64), ("M", ctypes.c_int64), ("n_expert", ctypes.c_int64), ("ne11", ctypes.c_int64),
+                ("n_used", ctypes.c_int64), ("n_tokens", ctypes.c_int64), ("ids_stride", ctypes.c_int64),
+                ("monte_seed", ctypes.c_uint16)]
+
+
 class SoftMaxArgs(ctypes.Structure):
     _fields_ = [("src", ctypes.c_void_p), ("src_shape", Shape4), ("mask", ctypes.c_void_p), ("mask_shape", Shape4),
                 ("scale", ctypes.c_float), ("dst", ctypes.c_void_p), ("work", ctypes.c_void_p),
@@ -56,6 +63,10 @@ SIGNATURES = [
     ("lnsb_to_f32", ctypes.c_int, [ctypes.c_int, _VP, _VP, _I64, _VP]),
     ("lnsb_mul_mat", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), _VP]),
     ("lnsb_mul_mat_lns", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), _VP, _VP]),
+    ("lnsb_mul_mat_id", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatIdArgs), _VP]),
+    ("lnsb_mul_mat_id_lns", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatIdArgs), _VP, _VP]),
+    ("lnsb_mul_mat_id_draws", ctypes.c_uint64, [ctypes.c_int, ctypes.POINTER(MulMatIdArgs)]),
+    ("lnsb_mul_mat_id_bad_ids", ctypes.c_int, [ctypes.POINTER(_I64)]),
     ("lnsb_soft_max", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(SoftMaxArgs), _VP]),
     ("lnsb_soft_max_lns", ctypes.c_int, [ctypes.c_int, _VP, ctypes.POINTER(_I64), _VP, ctypes.POINTER(_I64),
                                          ctypes.c_uint32, _VP, _VP, ctypes.c_uint16, _VP]),

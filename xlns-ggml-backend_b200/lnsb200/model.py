@@ -18,6 +18,11 @@ llama.cpp's order for the LLaMA graph:
       x = x + W_down swiglu(W_gate h, W_up h)
     logits = tok_embd (rms_norm(x_last) * output_norm)        (tied output)
 
+Ops carry llama.cpp-style tensor names (norm-<il>, Qcur/Kcur/Vcur-<il>,
+kq-<il>, kq_soft_max-<il>, kqv-<il>, attn_out-<il> over kqv_out-<il>,
+ffn_up/ffn_gate/ffn_down-<il>, result_output), which a summation policy
+(lnsb200.policy, LNS16_SUM_POLICY) matches to pick each reduction's mode.
+
 `forward` is written once over an ops object: GpuOps runs it through this
 package's kernels (liblnsb200_<mode>.so), OracleOps through the CPU oracle
 (test infrastructure), so both run the same graph.  Greedy decoding takes the
@@ -84,18 +89,19 @@ def forward(ops, cfg, ids, pos0):
     H, HKV, D = cfg["n_head"], cfg["n_head_kv"], cfg["head_dim"]
     x = ops.embed(ids)                                              # [T][E]
     for il in range(cfg["n_layer"]):
-        h = ops.mul(ops.rms_norm(x, cfg["eps"]), ops.w(il, "attn_norm"))
-        q, k, v = ops.linears(il, ("wq", "wk", "wv"), h)            # [T][H*D], [T][HKV*D] x 2
+        h = ops.mul(ops.rms_norm(x, cfg["eps"], "norm-%d" % il), ops.w(il, "attn_norm"))
+        q, k, v = ops.linears(il, ("wq", "wk", "wv"), h,            # [T][H*D], [T][HKV*D] x 2
+                              ("Qcur-%d" % il, "Kcur-%d" % il, "Vcur-%d" % il), "attn_norm-%d" % il)
         q = ops.rope(q, T, H, D, pos0)
         k = ops.rope(k, T, HKV, D, pos0)
         ops.kv_store(il, k, v, pos0, T)
         a = ops.attention(il, q, T, H, HKV, D, pos0)                # [T][H*D]
-        x = ops.add(ops.linear(ops.w(il, "wo"), a), x)
-        h = ops.mul(ops.rms_norm(x, cfg["eps"]), ops.w(il, "ffn_norm"))
-        up, gate = ops.linears(il, ("w_up", "w_gate"), h)
-        x = ops.add(ops.linear(ops.w(il, "w_down"), ops.swiglu(gate, up)), x)
-    h = ops.mul(ops.rms_norm(ops.last_row(x), cfg["eps"]), ops.w(None, "output_norm"))
-    return ops.linear(ops.w(None, "output"), h)                    # [1][vocab]
+        x = ops.add(ops.linear(ops.w(il, "wo"), a, "attn_out-%d" % il, "kqv_out-%d" % il), x)
+        h = ops.mul(ops.rms_norm(x, cfg["eps"], "norm-%d" % il), ops.w(il, "ffn_norm"))
+        up, gate = ops.linears(il, ("w_up", "w_gate"), h, ("ffn_up-%d" % il, "ffn_gate-%d" % il), "ffn_norm-%d" % il)
+        x = ops.add(ops.linear(ops.w(il, "w_down"), ops.swiglu(gate, up), "ffn_down-%d" % il, "ffn_swiglu-%d" % il), x)
+    h = ops.mul(ops.rms_norm(ops.last_row(x), cfg["eps"], "norm"), ops.w(None, "output_norm"))
+    return ops.linear(ops.w(None, "output"), h, "result_output", "result_norm")   # [1][vocab]
 
 
 def generate(ops, cfg, prompt, n_gen):
@@ -117,14 +123,20 @@ class GpuOps:
     """The graph's ops through liblnsb200_<mode>.so on one CUDA device (torch
     for memory and the non-arithmetic reshapes)."""
 
-    def __init__(self, cfg, weights, mode="sum32", n_ctx=256, stream=None, fmt=16):
+    def __init__(self, cfg, weights, mode="sum32", n_ctx=256, stream=None, fmt=16, policy=None):
         import torch
         import lnsb200
+        from .policy import SumPolicy
         self.torch, self.cfg, self.n_ctx = torch, cfg, n_ctx
         self.fmt = fmt
         self.cdt = torch.int16 if fmt == 16 else torch.int32             # LNS code storage
         self.ks = lnsb200.KernelSet(fmt, mode)
         self.ks.upload_tables()
+        # xlns16 only: a summation mode per op (the default: `mode`)
+        self.policy = SumPolicy(policy, mode) if fmt == 16 and policy else None
+        self.kss = {mode: self.ks}
+        self.weights = weights
+        self.split_w = {}
         self.stream = stream
         self.dev = torch.device("cuda", torch.cuda.current_device())
         E = cfg["n_embd"]
@@ -173,9 +185,20 @@ class GpuOps:
             return self.tok_embd.index_select(0, ids.view(-1)).contiguous()
         return self.tok_embd[self.torch.tensor(ids, device=self.dev)].contiguous()
 
-    def rms_norm(self, x, eps):
+    def ks_for(self, op, name, src1=None):
+        """the kernel set of the op's summation mode"""
+        if self.policy is None:
+            return self.ks
+        mode = self.policy.mode_for(op, name, src1)
+        if mode not in self.kss:
+            import lnsb200
+            self.kss[mode] = lnsb200.KernelSet(self.fmt, mode)
+            self.kss[mode].upload_tables()
+        return self.kss[mode]
+
+    def rms_norm(self, x, eps, name=None):
         out = self._f32(*x.shape)
-        self.ks.rms_norm(x, out, x.shape[-1], x.numel() // x.shape[-1], eps, stream=self.stream)
+        self.ks_for("RMS_NORM", name).rms_norm(x, out, x.shape[-1], x.numel() // x.shape[-1], eps, stream=self.stream)
         self.launches += 1
         return out
 
@@ -192,19 +215,28 @@ class GpuOps:
         self.launches += 1
         return out
 
-    def linear(self, wt, x):
+    def linear(self, wt, x, name=None, src1=None):
         codes, K, M = wt
         N = x.numel() // K
         xl = self.torch.empty(N * K, dtype=self.cdt, device=self.dev)
         self.ks.to_lns(x, xl, stream=self.stream)
         out = self._f32(N, M)
-        self.ks.mul_mat(codes, xl, out, K, M, N, stream=self.stream)
+        self.ks_for("MUL_MAT", name, src1).mul_mat(codes, xl, out, K, M, N, stream=self.stream)
         self.launches += 2
         return out
 
-    def linears(self, il, names, x):
+    def linears(self, il, names, x, tnames=None, src1=None):
+        tnames = tnames or (None,) * len(names)
+        kss = {id(self.ks_for("MUL_MAT", t, src1)) for t in tnames}
+        if len(kss) > 1:                                # the policy splits the group: one mul_mat per weight
+            outs = []
+            for n, t in zip(names, tnames):
+                if (il, n) not in self.split_w:
+                    self.split_w[(il, n)] = self._weight(self.weights["layers"][il][n])
+                outs.append(self.linear(self.split_w[(il, n)], x, t, src1))
+            return outs
         key = "qkv" if names[0] == "wq" else "upgate"
-        y = self.linear(self.lw[il][key], x)
+        y = self.linear(self.lw[il][key], x, tnames[0], src1)
         outs, c = [], 0
         for m in self.lw[il]["split"][tuple(names)]:
             outs.append(y[:, c:c + m].contiguous())
@@ -244,17 +276,18 @@ class GpuOps:
         ql = torch.empty(qh.numel(), dtype=self.cdt, device=self.dev)
         ks.to_lns(qh, ql, stream=self.stream)
         kq = self._f32(H, T, nkv)
-        ks.mul_mat(kl, ql, kq, D, nkv, T, (HKV, 1, H, 1), stream=self.stream)
+        self.ks_for("MUL_MAT", "kq-%d" % il).mul_mat(kl, ql, kq, D, nkv, T, (HKV, 1, H, 1), stream=self.stream)
         # causal mask rows pos0 .. pos0+T-1, scale 1/sqrt(head_dim)
         mask = self.mask_full[pos0:pos0 + T, :nkv].contiguous()
         p = self._f32(H, T, nkv)
         work = torch.empty(p.numel(), dtype=self.cdt, device=self.dev)
-        ks.soft_max(kq, (nkv, T, H, 1), p, work, mask, (nkv, T, 1, 1), 1.0 / math.sqrt(D), stream=self.stream)
+        self.ks_for("SOFT_MAX", "kq_soft_max-%d" % il).soft_max(kq, (nkv, T, H, 1), p, work, mask, (nkv, T, 1, 1),
+                                                               1.0 / math.sqrt(D), stream=self.stream)
         # o[h][t][d] = sum_k V[k][d] p[h][t][k]
         pl = torch.empty(p.numel(), dtype=self.cdt, device=self.dev)
         ks.to_lns(p, pl, stream=self.stream)
         o = self._f32(H, T, D)
-        ks.mul_mat(vl, pl, o, nkv, D, T, (HKV, 1, H, 1), stream=self.stream)
+        self.ks_for("MUL_MAT", "kqv-%d" % il).mul_mat(vl, pl, o, nkv, D, T, (HKV, 1, H, 1), stream=self.stream)
         self.launches += 9 + HKV
         return o.permute(1, 0, 2).contiguous().view(T, H * D)
 
@@ -320,20 +353,22 @@ class OracleOps:
     """The same ops on the CPU through the oracle (test infrastructure only:
     the checker of GpuOps)."""
 
-    def __init__(self, cfg, weights, mode="sum32", n_ctx=256, nthreads=8, fmt=16):
+    def __init__(self, cfg, weights, mode="sum32", n_ctx=256, nthreads=8, fmt=16, policy=None):
         import oracle
+        from .policy import SumPolicy
         self.o, self.cfg, self.mode, self.nt, self.fmt = oracle, cfg, mode, nthreads, fmt
+        self.policy = SumPolicy(policy, mode) if fmt == 16 and policy else None
         o = oracle
         if fmt == 16:
             self.to_c, self.to_f, self.mask_c = o.from_f32_16, o.to_f32_16, o.mask16
-            self.mm = lambda w, x, **kw: o.mul_mat16(mode, w, x, **kw)
-            self.rms = lambda c, nc, nr, eps: o.rms_norm16(mode, c, nc, nr, eps, nthreads=nthreads)
-            self.smax = lambda c, shp, m, mshp, sc: o.soft_max16(mode, c, shp, m, mshp, sc, nthreads=nthreads)
+            self.mm = lambda md, w, x, **kw: o.mul_mat16(md, w, x, **kw)
+            self.rms = lambda md, c, nc, nr, eps: o.rms_norm16(md, c, nc, nr, eps, nthreads=nthreads)
+            self.smax = lambda md, c, shp, m, mshp, sc: o.soft_max16(md, c, shp, m, mshp, sc, nthreads=nthreads)
         else:
             self.to_c, self.to_f, self.mask_c = o.from_f32_32, o.to_f32_32, o.mask32
-            self.mm = lambda w, x, **kw: o.mul_mat32(w, x, **kw)
-            self.rms = lambda c, nc, nr, eps: o.rms_norm32(c, nc, nr, eps, nthreads=nthreads)
-            self.smax = lambda c, shp, m, mshp, sc: o.soft_max32(c, shp, m, mshp, sc, nthreads=nthreads)
+            self.mm = lambda md, w, x, **kw: o.mul_mat32(w, x, **kw)
+            self.rms = lambda md, c, nc, nr, eps: o.rms_norm32(c, nc, nr, eps, nthreads=nthreads)
+            self.smax = lambda md, c, shp, m, mshp, sc: o.soft_max32(c, shp, m, mshp, sc, nthreads=nthreads)
         self.weights = weights
         self.wc = {}
         kvd = cfg["n_head_kv"] * cfg["head_dim"]
@@ -356,9 +391,12 @@ class OracleOps:
     def embed(self, ids):
         return self.weights["tok_embd"][ids].copy()
 
-    def rms_norm(self, x, eps):
+    def mode_for(self, op, name, src1=None):
+        return self.policy.mode_for(op, name, src1) if self.policy is not None else self.mode
+
+    def rms_norm(self, x, eps, name=None):
         c = self.to_c(x)
-        r = self.rms(c.ravel(), x.shape[-1], x.size // x.shape[-1], eps)
+        r = self.rms(self.mode_for("RMS_NORM", name), c.ravel(), x.shape[-1], x.size // x.shape[-1], eps)
         return self.to_f(r).reshape(x.shape)
 
     def mul(self, x, wv):
@@ -367,12 +405,13 @@ class OracleOps:
     def add(self, a, b):
         return self.o.binary16("add", a, b, fmt=self.fmt)
 
-    def linear(self, w, x):
+    def linear(self, w, x, name=None, src1=None):
         xc = self.to_c(x.reshape(-1, w.shape[1]))
-        return self.to_f(self.mm(w, xc, nthreads=self.nt)).reshape(-1, w.shape[0])
+        return self.to_f(self.mm(self.mode_for("MUL_MAT", name, src1), w, xc, nthreads=self.nt)).reshape(-1, w.shape[0])
 
-    def linears(self, il, names, x):
-        return [self.linear(self.w(il, n), x) for n in names]
+    def linears(self, il, names, x, tnames=None, src1=None):
+        tnames = tnames or (None,) * len(names)
+        return [self.linear(self.w(il, n), x, t, src1) for n, t in zip(names, tnames)]
 
     def rope(self, x, T, nh, hd, pos0):
         return self.o.rope16(x.reshape(1, T, nh, hd), self.rope_cs[pos0:pos0 + T], hd, fmt=self.fmt).reshape(T, nh * hd)
@@ -389,14 +428,14 @@ class OracleOps:
         kw = self.to_c(np.ascontiguousarray(kf.transpose(1, 0, 2)))            # [h][token][dim]: rows M=token, K=dim
         vw = self.to_c(np.ascontiguousarray(vf.transpose(1, 2, 0)))            # [h][dim][token]: rows M=dim, K=token
         qc = self.to_c(np.ascontiguousarray(q.reshape(T, H, D).transpose(1, 0, 2)))
-        kq = self.to_f(self.mm(kw.reshape(1, HKV, nkv, D), qc.reshape(1, H, T, D), slices=(HKV, 1, H, 1),
-                               nthreads=self.nt)).reshape(H, T, nkv)
+        kq = self.to_f(self.mm(self.mode_for("MUL_MAT", "kq-%d" % il), kw.reshape(1, HKV, nkv, D),
+                               qc.reshape(1, H, T, D), slices=(HKV, 1, H, 1), nthreads=self.nt)).reshape(H, T, nkv)
         m = np.triu(np.full((T + pos0, T + pos0), -np.inf, np.float32), 1)[pos0:pos0 + T, :nkv]
         sc = int(self.to_c(np.array([1.0 / math.sqrt(D)], np.float32))[0])
-        p = self.to_f(self.smax(self.to_c(kq).ravel(), (nkv, T, H, 1), self.mask_c(m).ravel(), (nkv, T, 1, 1),
-                                sc)).reshape(H, T, nkv)
-        out = self.to_f(self.mm(vw.reshape(1, HKV, D, nkv), self.to_c(p).reshape(1, H, T, nkv), slices=(HKV, 1, H, 1),
-                                nthreads=self.nt)).reshape(H, T, D)
+        p = self.to_f(self.smax(self.mode_for("SOFT_MAX", "kq_soft_max-%d" % il), self.to_c(kq).ravel(), (nkv, T, H, 1),
+                                self.mask_c(m).ravel(), (nkv, T, 1, 1), sc)).reshape(H, T, nkv)
+        out = self.to_f(self.mm(self.mode_for("MUL_MAT", "kqv-%d" % il), vw.reshape(1, HKV, D, nkv),
+                                self.to_c(p).reshape(1, H, T, nkv), slices=(HKV, 1, H, 1), nthreads=self.nt)).reshape(H, T, D)
         return np.ascontiguousarray(out.transpose(1, 0, 2)).reshape(T, H * D)
 
     def swiglu(self, gate, up):
