@@ -105,6 +105,48 @@ int lnsb_to_lns(int fmt, const float * src, void * dst, int64_t n, lnsb_stream_t
 /* dst[c * dst_ld + r] = lns(src[r * cols + c]) */
 int lnsb_to_lns_transposed(int fmt, const float * src, void * dst, int64_t rows, int64_t cols,
                            int64_t dst_ld, lnsb_stream_t stream);
+/* ---- weights in ggml storage types.  The reference turns every weight into
+ * F32 rows on the host with ggml's to_float and converts them with
+ * to_lns_transposed (lns-cuda-context.cpp:163-195, 370-419); here one kernel
+ * decodes the rows on the device and writes the k-major LNS image.  Type ids
+ * are ggml's (ggml_type).  Rows are stored back to back, each
+ * lnsb_type_row_bytes(type, cols) bytes; block types need cols to be a whole
+ * number of blocks (32 values for Q8_0 / Q4_0, 256 for Q4_K / Q6_K). ---- */
+#define LNSB_TYPE_F32   0
+#define LNSB_TYPE_F16   1
+#define LNSB_TYPE_Q4_0  2
+#define LNSB_TYPE_Q8_0  8
+#define LNSB_TYPE_Q4_K 12
+#define LNSB_TYPE_Q6_K 14
+#define LNSB_TYPE_BF16 30
+/* bytes of one row of `cols` values; 0 for an unknown type or a partial block */
+size_t lnsb_type_row_bytes(int type, int64_t cols);
+/* dst[c * dst_ld + r] = lns(value c of row r of src), src and dst in device memory */
+int lnsb_to_lns_transposed_typed(int fmt, int type, const void * src, void * dst, int64_t rows, int64_t cols,
+                                 int64_t dst_ld, lnsb_stream_t stream);
+/* the decoded F32 rows (ggml's to_float), rows x cols */
+int lnsb_dequantize(int type, const void * src, float * dst, int64_t rows, int64_t cols, lnsb_stream_t stream);
+
+/* ---- the weight cache (lns-cuda-context.h:79-113, lns-cuda-context.cpp:
+ * 128-154, 290-300, 370-392): weights converted to LNS once and kept on the
+ * device, keyed by (data pointer, type, rows, cols); a conversion that would
+ * exceed the budget goes to the caller's scratch instead and is redone on
+ * every use, as in the reference.  src may be host or device memory (host
+ * rows are staged to the device in bounded chunks).  budget_bytes < 0 takes
+ * the reference's rule: GGML_LNS_CUDA_CACHE_MB if set, else the device's free
+ * memory less a 1 GiB reserve at creation. ---- */
+typedef struct lnsb_weight_cache lnsb_weight_cache;
+lnsb_weight_cache * lnsb_weight_cache_create(int fmt, int64_t budget_bytes);
+void lnsb_weight_cache_destroy(lnsb_weight_cache * cache);
+/* *out = the k-major LNS image (K = cols, M = rows: element (k, m) at k * rows + m).
+ * On a miss that does not fit, the image is written to `scratch` (rows * cols *
+ * value_size bytes of device memory; NULL -> LNSB_E_TOO_LARGE).  The call
+ * synchronises `stream` when it converts. */
+int lnsb_weight_cache_get(lnsb_weight_cache * cache, const void * src, int type, int64_t rows, int64_t cols,
+                          void * scratch, const void ** out, lnsb_stream_t stream);
+int lnsb_weight_cache_stats(const lnsb_weight_cache * cache, int64_t * entries, int64_t * used_bytes,
+                            int64_t * budget_bytes);
+
 /* dst[i] = float(src[i]) -- the op-boundary decode the reference fuses into
  * every kernel's store (lns-cuda-kernels.cuh:155,249,324) */
 int lnsb_to_f32(int fmt, const void * src, float * dst, int64_t n, lnsb_stream_t stream);

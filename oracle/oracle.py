@@ -290,3 +290,69 @@ def pincheck():
     standalone = {k: out.pop(k) for k in ("two_term", "ones", "long_dot", "rms_standalone")}
     out["standalone"] = standalone
     return out
+
+
+# ---- ggml storage types of weights (test restatement of ggml's block
+# layouts and its reference dequantisers; float steps as plain float32
+# multiplies and subtractions, in that order) ----
+GGML_TYPES = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 8, "q4_k": 12, "q6_k": 14, "bf16": 30}
+BLOCK = {"f32": (1, 4), "f16": (1, 2), "bf16": (1, 2), "q8_0": (32, 34), "q4_0": (32, 18), "q4_k": (256, 144),
+         "q6_k": (256, 210)}
+
+
+def _f16(b, off):
+    return b[:, off:off + 2].copy().view(np.float16).astype(np.float32)[:, 0]
+
+
+def dequant(type, raw, rows, cols):
+    """raw: uint8 [rows][row_bytes] -> float32 [rows][cols]"""
+    qk, bb = BLOCK[type]
+    nb = cols // qk
+    raw = np.ascontiguousarray(raw, np.uint8).reshape(rows, -1)
+    if type == "f32":
+        return raw.view(np.float32).reshape(rows, cols).copy()
+    if type == "f16":
+        return raw.view(np.float16).astype(np.float32).reshape(rows, cols)
+    if type == "bf16":
+        return (raw.view(np.uint16).astype(np.uint32) << 16).view(np.float32).reshape(rows, cols)
+    out = np.empty((rows, cols), np.float32)
+    for i in range(nb):
+        b = raw[:, i * bb:(i + 1) * bb]
+        y = out[:, i * qk:(i + 1) * qk]
+        if type == "q8_0":
+            y[:] = b[:, 2:34].view(np.int8).astype(np.float32) * _f16(b, 0)[:, None]
+        elif type == "q4_0":
+            d = _f16(b, 0)[:, None]
+            qs = b[:, 2:18].astype(np.int32)
+            y[:, :16] = ((qs & 0xF) - 8).astype(np.float32) * d
+            y[:, 16:] = ((qs >> 4) - 8).astype(np.float32) * d
+        elif type == "q4_k":
+            d, dmin = _f16(b, 0), _f16(b, 2)
+            sc = b[:, 4:16].astype(np.int32)
+            qs = b[:, 16:144].astype(np.int32)
+            for j in range(8):
+                if j < 4:
+                    s, m = sc[:, j] & 63, sc[:, j + 4] & 63
+                else:
+                    s = (sc[:, j + 4] & 0xF) | ((sc[:, j - 4] >> 6) << 4)
+                    m = (sc[:, j + 4] >> 4) | ((sc[:, j] >> 6) << 4)
+                d1 = (d * s.astype(np.float32))[:, None]
+                m1 = (dmin * m.astype(np.float32))[:, None]
+                q = qs[:, (j // 2) * 32:(j // 2) * 32 + 32]
+                q = (q & 0xF) if j % 2 == 0 else (q >> 4)
+                y[:, j * 32:(j + 1) * 32] = d1 * q.astype(np.float32) - m1
+        elif type == "q6_k":
+            d = _f16(b, 208)
+            for n in range(2):
+                ql = b[:, n * 64:(n + 1) * 64].astype(np.int32)
+                qh = b[:, 128 + n * 32:128 + (n + 1) * 32].astype(np.int32)
+                sc = b[:, 192 + n * 8:192 + (n + 1) * 8].view(np.int8).astype(np.float32)
+                l = np.arange(32)
+                qs = [((ql[:, l] & 0xF) | (((qh[:, l] >> 0) & 3) << 4)) - 32,
+                      ((ql[:, l + 32] & 0xF) | (((qh[:, l] >> 2) & 3) << 4)) - 32,
+                      ((ql[:, l] >> 4) | (((qh[:, l] >> 4) & 3) << 4)) - 32,
+                      ((ql[:, l + 32] >> 4) | (((qh[:, l] >> 6) & 3) << 4)) - 32]
+                for quarter in range(4):
+                    s = sc[:, (l // 16) + 2 * quarter]
+                    y[:, n * 128 + quarter * 32:n * 128 + quarter * 32 + 32] = (d[:, None] * s) * qs[quarter].astype(np.float32)
+    return out

@@ -1,0 +1,139 @@
+"""Weights in ggml storage types on the GPU (lnsb_dequantize,
+lnsb_to_lns_transposed_typed, the weight cache) against the oracle's
+restatement of ggml's block layouts, bit for bit; the reference turns weights
+into F32 with ggml's to_float on the host and converts them with
+to_lns_transposed (lns-backend/cuda/lns-cuda-context.cpp:163-195, 370-419)."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+TYPES = ["f32", "f16", "bf16", "q8_0", "q4_0", "q4_k", "q6_k"]
+
+
+def random_rows(orc, type, rows, cols, rng):
+    """raw uint8 [rows][row_bytes] of a random weight in `type`"""
+    qk, bb = orc.BLOCK[type]
+    if type in ("f32", "f16", "bf16"):
+        v = rng.normal(0, 0.05, (rows, cols)).astype(np.float32)
+        if type == "f32":
+            return v.view(np.uint8).reshape(rows, -1)
+        if type == "f16":
+            return v.astype(np.float16).view(np.uint8).reshape(rows, -1)
+        return (v.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8).reshape(rows, -1)
+    raw = rng.integers(0, 256, (rows, (cols // qk) * bb), dtype=np.uint8)
+    nb = cols // qk
+    for i in range(nb):                                  # sane f16 scales: finite, about 1e-3 .. 1e-1
+        for off in ({"q8_0": [0], "q4_0": [0], "q4_k": [0, 2], "q6_k": [208]}[type]):
+            d = rng.uniform(1e-3, 1e-1, rows).astype(np.float16).view(np.uint8).reshape(rows, 2)
+            raw[:, i * bb + off:i * bb + off + 2] = d
+    return raw
+
+
+@pytest.fixture(scope="module")
+def kss():
+    import lnsb200
+    out = {}
+    for fmt in (16, 32):
+        out[fmt] = lnsb200.KernelSet(fmt, "base")
+        out[fmt].upload_tables()
+    return out
+
+
+@pytest.mark.parametrize("type", TYPES)
+def test_dequantize(orc, kss, type):
+    rng = np.random.default_rng(len(type) * 17)
+    rows, cols = 37, 512
+    raw = random_rows(orc, type, rows, cols, rng)
+    assert raw.shape[1] == kss[16].type_row_bytes(type, cols)
+    out = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
+    kss[16].dequantize(type, torch.from_numpy(raw).cuda(), out, rows, cols)
+    torch.cuda.synchronize()
+    want = orc.dequant(type, raw, rows, cols)
+    assert np.array_equal(out.cpu().numpy().reshape(rows, cols).view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("fmt", [16, 32])
+@pytest.mark.parametrize("type", TYPES)
+def test_to_lns_transposed_typed(orc, kss, fmt, type):
+    rng = np.random.default_rng(len(type) + fmt)
+    rows, cols = 45, 768
+    raw = random_rows(orc, type, rows, cols, rng)
+    it = torch.int16 if fmt == 16 else torch.int32
+    dst = torch.empty(cols * rows, dtype=it, device="cuda")
+    kss[fmt].to_lns_transposed_typed(type, torch.from_numpy(raw).cuda(), dst, rows, cols, rows)
+    torch.cuda.synchronize()
+    f = orc.dequant(type, raw, rows, cols)
+    want = (orc.from_f32_16(f) if fmt == 16 else orc.from_f32_32(f)).T.reshape(-1)
+    got = dst.cpu().numpy().view(np.uint16 if fmt == 16 else np.uint32)
+    assert np.array_equal(got, want)
+
+
+def image_f32(ks, addr, n):
+    """the F32 decode of n LNS codes at a device address (lnsb_to_f32)"""
+    out = torch.empty(n, dtype=torch.float32, device="cuda")
+    assert ks.lib.lnsb_to_f32(ks.fmt, addr, out.data_ptr(), n, None) == 0
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def test_weight_cache(orc, kss):
+    import lnsb200
+    ks = kss[16]
+    rng = np.random.default_rng(3)
+    rows, cols = 300, 512
+    raw = random_rows(orc, "q4_k", rows, cols, rng)
+    want = orc.to_f32_16(orc.from_f32_16(orc.dequant("q4_k", raw, rows, cols)).T.reshape(-1))
+    nbytes = rows * cols * 2
+    dsrc = torch.from_numpy(raw).cuda()
+    c = lnsb200.WeightCache(ks, budget=2 * nbytes)
+    a1 = c.get(dsrc, "q4_k", rows, cols)
+    assert c.get(dsrc, "q4_k", rows, cols) == a1
+    assert c.stats() == {"entries": 1, "used": nbytes, "budget": 2 * nbytes}
+    assert np.array_equal(image_f32(ks, a1, rows * cols).view(np.uint32), want.view(np.uint32))
+    # host rows (numpy): staged to the device, their own entry
+    a2 = c.get(raw, "q4_k", rows, cols)
+    assert a2 != a1 and c.stats()["entries"] == 2
+    assert np.array_equal(image_f32(ks, a2, rows * cols).view(np.uint32), want.view(np.uint32))
+    # over budget: the image goes to the caller's scratch and is not cached
+    scratch = torch.empty(rows * cols, dtype=torch.int16, device="cuda")
+    dsrc2 = dsrc.clone()
+    assert c.get(dsrc2, "q4_k", rows, cols, scratch=scratch) == scratch.data_ptr()
+    assert c.stats()["entries"] == 2
+    assert np.array_equal(image_f32(ks, scratch.data_ptr(), rows * cols).view(np.uint32), want.view(np.uint32))
+    with pytest.raises(lnsb200.LnsbError):               # over budget and no scratch
+        c.get(dsrc2, "q4_k", rows, cols)
+    c.close()
+
+
+def test_weight_cache_xlns32_host_rows(orc, kss):
+    import lnsb200
+    ks = kss[32]
+    rng = np.random.default_rng(4)
+    rows, cols = 64, 256
+    raw = random_rows(orc, "q6_k", rows, cols, rng)
+    want = orc.to_f32_32(orc.from_f32_32(orc.dequant("q6_k", raw, rows, cols)).T.reshape(-1))
+    c = lnsb200.WeightCache(ks, budget=1 << 20)
+    addr = c.get(raw, "q6_k", rows, cols)
+    assert np.array_equal(image_f32(ks, addr, rows * cols).view(np.uint32), want.view(np.uint32))
+    tiny = lnsb200.WeightCache(ks, budget=0)             # nothing fits: always the scratch
+    scratch = torch.empty(rows * cols, dtype=torch.int32, device="cuda")
+    assert tiny.get(raw, "q6_k", rows, cols, scratch=scratch) == scratch.data_ptr()
+    assert tiny.stats()["entries"] == 0
+    assert np.array_equal(image_f32(ks, scratch.data_ptr(), rows * cols).view(np.uint32), want.view(np.uint32))
+    c.close()
+    tiny.close()
+
+
+def test_typed_errors(kss):
+    import lnsb200
+    ks = kss[16]
+    z = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    d = torch.zeros(4096, dtype=torch.int16, device="cuda")
+    with pytest.raises(lnsb200.LnsbError):
+        ks.to_lns_transposed_typed(3, z, d, 4, 32, 4)        # Q4_1: not supported
+    with pytest.raises(lnsb200.LnsbError):
+        ks.to_lns_transposed_typed("q4_k", z, d, 4, 128, 4)  # half a Q4_K block
+    assert ks.type_row_bytes("q6_k", 512) == 420 and ks.type_row_bytes("q4_k", 100) == 0

@@ -127,3 +127,32 @@ def test_report(computed, pins, capsys):
         for name, c, p in rows:
             print("%-40s %-45s %s" % (name, c, p))
     assert rows
+
+
+def test_dequant_known_blocks(orc):
+    """hand-built blocks of ggml's layouts: Q4_K with d = 1, dmin = 0.5 and
+    sub-block scale/min pairs (j + 1, j); Q6_K with d = 0.25 and scale 2"""
+    import numpy as np
+    b = np.zeros(144, np.uint8)
+    b[0:2] = np.array([1.0], np.float16).view(np.uint8)
+    b[2:4] = np.array([0.5], np.float16).view(np.uint8)
+    sc, mn = list(range(1, 9)), list(range(8))
+    for j in range(4):
+        b[4 + j] = sc[j] | ((sc[j + 4] >> 4) << 6)
+        b[8 + j] = mn[j] | ((mn[j + 4] >> 4) << 6)
+        b[12 + j] = (sc[j + 4] & 0xF) | ((mn[j + 4] & 0xF) << 4)
+    b[16:144] = 0x73                                      # low nibble 3, high nibble 7
+    y = orc.dequant("q4_k", b[None, :], 1, 256)[0]
+    for j in range(8):
+        q = 3 if j % 2 == 0 else 7
+        assert np.all(y[j * 32:(j + 1) * 32] == np.float32(sc[j] * q - 0.5 * mn[j]))
+    c = np.zeros(210, np.uint8)
+    c[0:128] = 0x21                                       # low 4 bits: 1 (first nibble) / 2 (second)
+    c[128:192] = 0b11100100                               # high 2 bits per quarter: 0, 1, 2, 3
+    c[192:208] = 2
+    c[208:210] = np.array([0.25], np.float16).view(np.uint8)
+    y = orc.dequant("q6_k", c[None, :], 1, 256)[0]
+    for quarter, (lo, hi) in enumerate([(1, 0), (1, 1), (2, 2), (2, 3)]):
+        want = np.float32(0.25 * 2 * ((lo | (hi << 4)) - 32))
+        assert np.all(y[quarter * 32:(quarter + 1) * 32] == want)
+        assert np.all(y[128 + quarter * 32:128 + (quarter + 1) * 32] == want)

@@ -13,7 +13,9 @@
 
 #include <array>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 
 #include "lnsb200.h"
@@ -117,6 +119,103 @@ __global__ void k_to_lns_transposed(dev_tables T, const float * __restrict__ src
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         const int64_t c = c0 + i, r = r0 + threadIdx.x;
         if (r < rows && c < cols) static_cast<V *>(dst)[c * dst_ld + r] = tile[threadIdx.x][i];
+    }
+}
+
+// ===================== weights in ggml storage types =======================
+// ggml's block layouts (the formats ggml writes in GGUF files), decoded one
+// value at a time: every value of a row is a function of its block's header
+// and its own quant bits, so a thread computes value (r, c) directly and the
+// transposing conversion keeps its coalesced tile structure.  Float steps are
+// plain IEEE multiplies and subtractions (no contraction), in the order of
+// ggml's reference dequantisers:
+//   F16, BF16        the value widened
+//   Q8_0  (34 B/32)  d (f16), 32 x int8 q:  d * q
+//   Q4_0  (18 B/32)  d (f16), 16 bytes: value j < 16 low nibbles, j >= 16 high:
+//                    d * (nibble - 8)
+//   Q4_K  (144 B/256) d, dmin (f16), 12 bytes of 6-bit scales/mins for 8
+//                    sub-blocks of 32, 128 bytes of nibbles (64 values per 32
+//                    bytes: low nibbles then high): (d * sc) * q - (dmin * m)
+//   Q6_K  (210 B/256) 128 bytes low 4 bits, 64 bytes high 2 bits, 16 int8
+//                    scales, d (f16): (d * sc) * (q - 32)
+__device__ __forceinline__ float f16_at(const unsigned char * p) {
+    return __half2float(__ushort_as_half((unsigned short) (p[0] | (p[1] << 8))));
+}
+__device__ __forceinline__ void q4k_scale_min(int j, const unsigned char * q, int & sc, int & m) {
+    if (j < 4) {
+        sc = q[j] & 63;
+        m  = q[j + 4] & 63;
+    } else {
+        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        m  = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+__device__ __forceinline__ float dequant_at(int type, const unsigned char * __restrict__ row, int64_t c) {
+    switch (type) {
+        case LNSB_TYPE_F32:  return reinterpret_cast<const float *>(row)[c];
+        case LNSB_TYPE_F16:  return f16_at(row + 2 * c);
+        case LNSB_TYPE_BF16: return __uint_as_float((uint32_t) (row[2 * c] | (row[2 * c + 1] << 8)) << 16);
+        case LNSB_TYPE_Q8_0: {
+            const unsigned char * b = row + (c / 32) * 34;
+            return __fmul_rn((float) (int8_t) b[2 + c % 32], f16_at(b));
+        }
+        case LNSB_TYPE_Q4_0: {
+            const unsigned char * b = row + (c / 32) * 18;
+            const int j = (int) (c % 32);
+            const int byte = b[2 + (j & 15)];
+            return __fmul_rn((float) ((j < 16 ? byte & 0xF : byte >> 4) - 8), f16_at(b));
+        }
+        case LNSB_TYPE_Q4_K: {
+            const unsigned char * b = row + (c / 256) * 144;
+            const int j = (int) (c % 256), chunk = j / 64, w = j % 64, sub = 2 * chunk + (w >= 32);
+            const int q = b[16 + chunk * 32 + (w % 32)];
+            int sc, m;
+            q4k_scale_min(sub, b + 4, sc, m);
+            const float d1 = __fmul_rn(f16_at(b), (float) sc), m1 = __fmul_rn(f16_at(b + 2), (float) m);
+            return __fsub_rn(__fmul_rn(d1, (float) (w < 32 ? q & 0xF : q >> 4)), m1);
+        }
+        case LNSB_TYPE_Q6_K: {
+            const unsigned char * b = row + (c / 256) * 210;
+            const int j = (int) (c % 256), n = j / 128, quarter = (j % 128) / 32, l = j % 32;
+            const unsigned char * ql = b + n * 64;
+            const unsigned char * qh = b + 128 + n * 32;
+            const int8_t * sc = reinterpret_cast<const int8_t *>(b + 192) + n * 8;
+            const int lo = quarter & 1 ? ql[l + 32] : ql[l];
+            const int q  = ((quarter < 2 ? lo & 0xF : lo >> 4) | (((qh[l] >> (2 * quarter)) & 3) << 4)) - 32;
+            return __fmul_rn(__fmul_rn(f16_at(b + 208), (float) sc[l / 16 + 2 * quarter]), (float) q);
+        }
+        default: return 0.0f;
+    }
+}
+
+// dst[c * dst_ld + r] = lns(dequant(row r)[c]); rows `row_bytes` apart
+template <int FMT>
+__global__ void k_to_lns_transposed_typed(dev_tables T, int type, const unsigned char * __restrict__ src,
+                                          int64_t row_bytes, void * __restrict__ dst, int64_t rows, int64_t cols,
+                                          int64_t dst_ld) {
+    using V = typename std::conditional<FMT == 16, uint16_t, uint32_t>::type;
+    __shared__ V tile[32][33];
+    const int64_t r0 = (int64_t) blockIdx.y * 32, c0 = (int64_t) blockIdx.x * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int64_t r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) {
+            const float f = dequant_at(type, src + r * row_bytes, c);
+            tile[i][threadIdx.x] = FMT == 16 ? (V) from_f32_16(T, f) : (V) from_f32_32(T, f);
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int64_t c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) static_cast<V *>(dst)[c * dst_ld + r] = tile[threadIdx.x][i];
+    }
+}
+
+__global__ void k_dequantize(int type, const unsigned char * __restrict__ src, int64_t row_bytes, float * __restrict__ dst,
+                             int64_t rows, int64_t cols) {
+    const int64_t n = rows * cols;
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t) blockDim.x * gridDim.x) {
+        const int64_t r = i / cols, c = i - r * cols;
+        dst[i] = dequant_at(type, src + r * row_bytes, c);
     }
 }
 
@@ -1985,6 +2084,29 @@ uint32_t host_from_f32_32(float x) {
 
 using namespace lnsb;
 
+// The weight cache behind lnsb_weight_cache_* (lns-cuda-context.h:79-113):
+// one map per cache from (data pointer, type, rows, cols) to a device
+// buffer, a byte budget, and a device staging buffer for host-resident rows.
+struct lnsb_weight_cache {
+    struct key {
+        const void * data;
+        int          type;
+        int64_t      rows, cols;
+        bool operator<(const key & o) const {
+            if (data != o.data) return data < o.data;
+            if (type != o.type) return type < o.type;
+            if (rows != o.rows) return rows < o.rows;
+            return cols < o.cols;
+        }
+    };
+    int                    fmt = 0, dev = 0;
+    int64_t                budget = 0, used = 0;
+    std::map<key, void *>  entries;
+    void *                 staging = nullptr;
+    size_t                 staging_bytes = 0;
+    std::mutex             mu;
+};
+
 // ================================ C ABI =====================================
 
 extern "C" {
@@ -2106,6 +2228,58 @@ int lnsb_to_lns_transposed(int fmt, const float * src, void * dst, int64_t rows,
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (fmt == LNSB_XLNS16) k_to_lns_transposed<16><<<grid, block, 0, s>>>(*T, src, dst, rows, cols, dst_ld);
     else                    k_to_lns_transposed<32><<<grid, block, 0, s>>>(*T, src, dst, rows, cols, dst_ld);
+    return launch_status();
+}
+
+static bool known_type(int type) {
+    return type == LNSB_TYPE_F32 || type == LNSB_TYPE_F16 || type == LNSB_TYPE_BF16 || type == LNSB_TYPE_Q8_0 ||
+           type == LNSB_TYPE_Q4_0 || type == LNSB_TYPE_Q4_K || type == LNSB_TYPE_Q6_K;
+}
+
+size_t lnsb_type_row_bytes(int type, int64_t cols) {
+    if (cols < 0) return 0;
+    switch (type) {
+        case LNSB_TYPE_F32:  return (size_t) cols * 4;
+        case LNSB_TYPE_F16:
+        case LNSB_TYPE_BF16: return (size_t) cols * 2;
+        case LNSB_TYPE_Q8_0: return cols % 32 ? 0 : (size_t) (cols / 32) * 34;
+        case LNSB_TYPE_Q4_0: return cols % 32 ? 0 : (size_t) (cols / 32) * 18;
+        case LNSB_TYPE_Q4_K: return cols % 256 ? 0 : (size_t) (cols / 256) * 144;
+        case LNSB_TYPE_Q6_K: return cols % 256 ? 0 : (size_t) (cols / 256) * 210;
+        default:             return 0;
+    }
+}
+
+int lnsb_to_lns_transposed_typed(int fmt, int type, const void * src, void * dst, int64_t rows, int64_t cols,
+                                 int64_t dst_ld, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || rows < 0 || cols < 0 || dst_ld < rows) return LNSB_E_INVALID;
+    if (!known_type(type)) return LNSB_E_UNSUPPORTED;
+    const size_t rb = lnsb_type_row_bytes(type, cols);
+    if (cols > 0 && rb == 0) return LNSB_E_INVALID;          // cols not a whole number of blocks
+    if (rows == 0 || cols == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    if ((cols + 31) / 32 > 0x7FFFFFFF || (rows + 31) / 32 > 65535) return LNSB_E_TOO_LARGE;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const dim3 grid((unsigned) ((cols + 31) / 32), (unsigned) ((rows + 31) / 32));
+    const dim3 block(32, 8);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const auto * p = static_cast<const unsigned char *>(src);
+    if (fmt == LNSB_XLNS16) k_to_lns_transposed_typed<16><<<grid, block, 0, s>>>(*T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
+    else                    k_to_lns_transposed_typed<32><<<grid, block, 0, s>>>(*T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
+    return launch_status();
+}
+
+int lnsb_dequantize(int type, const void * src, float * dst, int64_t rows, int64_t cols, lnsb_stream_t stream) {
+    if (rows < 0 || cols < 0) return LNSB_E_INVALID;
+    if (!known_type(type)) return LNSB_E_UNSUPPORTED;
+    const size_t rb = lnsb_type_row_bytes(type, cols);
+    if (cols > 0 && rb == 0) return LNSB_E_INVALID;
+    if (rows == 0 || cols == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    k_dequantize<<<grid_for(rows * cols, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        type, static_cast<const unsigned char *>(src), (int64_t) rb, dst, rows, cols);
     return launch_status();
 }
 
@@ -2375,6 +2549,123 @@ const char * lnsb_error_string(int status) {
         case LNSB_E_NO_DEVICE:   return "no usable CUDA device";
         default:                 return status > 0 ? cudaGetErrorString((cudaError_t) status) : "unknown error";
     }
+}
+
+lnsb_weight_cache * lnsb_weight_cache_create(int fmt, int64_t budget_bytes) {
+    if (!valid_fmt(fmt)) return nullptr;
+    int dev = 0;
+    if (current_device(&dev) != 0) return nullptr;
+    if (budget_bytes < 0) {
+        constexpr int64_t MiB = 1 << 20, reserve = 1024 * MiB;      // scratch kept free beside the cache
+        if (const char * env = std::getenv("GGML_LNS_CUDA_CACHE_MB")) {
+            const long long mb = std::atoll(env);
+            budget_bytes = (mb > 0 ? mb : 0) * MiB;
+        } else {
+            size_t fr = 0, tot = 0;
+            if (cudaMemGetInfo(&fr, &tot) != cudaSuccess) return nullptr;
+            budget_bytes = (int64_t) fr > reserve ? (int64_t) fr - reserve : 0;
+        }
+    }
+    auto * c = new (std::nothrow) lnsb_weight_cache();
+    if (c == nullptr) return nullptr;
+    c->fmt = fmt;
+    c->dev = dev;
+    c->budget = budget_bytes;
+    return c;
+}
+
+void lnsb_weight_cache_destroy(lnsb_weight_cache * c) {
+    if (c == nullptr) return;
+    int cur = 0;
+    const bool moved = cudaGetDevice(&cur) == cudaSuccess && cur != c->dev;
+    if (moved) cudaSetDevice(c->dev);
+    for (auto & e : c->entries) cudaFree(e.second);
+    if (c->staging != nullptr) cudaFree(c->staging);
+    if (moved) cudaSetDevice(cur);
+    delete c;
+}
+
+int lnsb_weight_cache_get(lnsb_weight_cache * c, const void * src, int type, int64_t rows, int64_t cols,
+                          void * scratch, const void ** out, lnsb_stream_t stream) {
+    if (c == nullptr || out == nullptr || src == nullptr || rows <= 0 || cols <= 0) return LNSB_E_INVALID;
+    if (!known_type(type)) return LNSB_E_UNSUPPORTED;
+    const size_t rb = lnsb_type_row_bytes(type, cols);
+    if (rb == 0) return LNSB_E_INVALID;
+    int dev = 0;
+    const int ds = current_device(&dev);
+    if (ds != 0) return ds;
+    if (dev != c->dev) return LNSB_E_INVALID;                        // a cache serves the device it was made on
+    std::lock_guard<std::mutex> lock(c->mu);
+    const lnsb_weight_cache::key k{ src, type, rows, cols };
+    const auto it = c->entries.find(k);
+    if (it != c->entries.end()) {
+        *out = it->second;
+        return 0;
+    }
+    const int64_t bytes = rows * cols * (int64_t) lnsb_value_size(c->fmt);
+    void * dst = nullptr;
+    if (c->used + bytes <= c->budget && cudaMalloc(&dst, (size_t) bytes) != cudaSuccess) {
+        cudaGetLastError();                                          // out of memory: not sticky, fall back
+        dst = nullptr;
+    }
+    const bool cached = dst != nullptr;
+    if (!cached) {
+        if (scratch == nullptr) return LNSB_E_TOO_LARGE;
+        dst = scratch;
+    }
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaPointerAttributes at{};
+    const bool on_device = cudaPointerGetAttributes(&at, src) == cudaSuccess &&
+                           (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged);
+    cudaGetLastError();
+    int st = 0;
+    if (on_device) {
+        st = lnsb_to_lns_transposed_typed(c->fmt, type, src, dst, rows, cols, rows, stream);
+    } else {
+        // host rows: staged through a bounded device buffer, chunk by chunk
+        constexpr size_t k_chunk = (size_t) 64 << 20;
+        const int64_t chunk_rows = rb >= k_chunk ? 1 : (int64_t) (k_chunk / rb);
+        const size_t need = (size_t) (chunk_rows < rows ? chunk_rows : rows) * rb;
+        if (c->staging_bytes < need) {
+            if (c->staging != nullptr) cudaFree(c->staging);
+            c->staging = nullptr;
+            c->staging_bytes = 0;
+            if (cudaMalloc(&c->staging, need) != cudaSuccess) st = LNSB_E_TOO_LARGE;
+            else c->staging_bytes = need;
+        }
+        const size_t vs = lnsb_value_size(c->fmt);
+        for (int64_t m0 = 0; st == 0 && m0 < rows; m0 += chunk_rows) {
+            const int64_t n = rows - m0 < chunk_rows ? rows - m0 : chunk_rows;
+            cudaError_t e = cudaMemcpyAsync(c->staging, static_cast<const unsigned char *>(src) + (size_t) m0 * rb,
+                                            (size_t) n * rb, cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) { st = (int) e; break; }
+            st = lnsb_to_lns_transposed_typed(c->fmt, type, c->staging, static_cast<unsigned char *>(dst) + (size_t) m0 * vs,
+                                              n, cols, rows, stream);
+            if (st == 0 && (e = cudaStreamSynchronize(s)) != cudaSuccess) st = (int) e;   // the staging buffer is reused
+        }
+    }
+    if (st == 0) {
+        const cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) st = (int) e;
+    }
+    if (st != 0) {
+        if (cached) cudaFree(dst);
+        return st;
+    }
+    if (cached) {
+        c->entries.emplace(k, dst);
+        c->used += bytes;
+    }
+    *out = dst;
+    return 0;
+}
+
+int lnsb_weight_cache_stats(const lnsb_weight_cache * c, int64_t * entries, int64_t * used_bytes, int64_t * budget_bytes) {
+    if (c == nullptr) return LNSB_E_INVALID;
+    if (entries != nullptr) *entries = (int64_t) c->entries.size();
+    if (used_bytes != nullptr) *used_bytes = c->used;
+    if (budget_bytes != nullptr) *budget_bytes = c->budget;
+    return 0;
 }
 
 }  // extern "C"

@@ -102,6 +102,19 @@ class KernelSet:
         a = self._mm_args(w, x, None, K, M, N, slices, monte_seed)
         _lib.check(self.lib, "lnsb_mul_mat_lns", self.lib.lnsb_mul_mat_lns(self.fmt, ctypes.byref(a), _ptr(dst), _stream(stream)))
 
+    def type_row_bytes(self, type, cols):
+        return self.lib.lnsb_type_row_bytes(_lib.TYPES.get(type, type), cols)
+
+    def to_lns_transposed_typed(self, type, src, dst, rows, cols, dst_ld, stream=None):
+        """dst[c * dst_ld + r] = lns(value c of row r); src rows in a ggml storage type (name or id)"""
+        _lib.check(self.lib, "lnsb_to_lns_transposed_typed",
+                   self.lib.lnsb_to_lns_transposed_typed(self.fmt, _lib.TYPES.get(type, type), _ptr(src), _ptr(dst),
+                                                         rows, cols, dst_ld, _stream(stream)))
+
+    def dequantize(self, type, src, dst, rows, cols, stream=None):
+        _lib.check(self.lib, "lnsb_dequantize",
+                   self.lib.lnsb_dequantize(_lib.TYPES.get(type, type), _ptr(src), _ptr(dst), rows, cols, _stream(stream)))
+
     def _mmid_args(self, w, x, ids, dst, K, M, n_expert, ne11, n_used, n_tokens, monte_seed):
         return _lib.MulMatIdArgs(w.data_ptr(), x.data_ptr(), ids.data_ptr(), dst.data_ptr() if dst is not None else None,
                                  K, M, n_expert, ne11, n_used, n_tokens, n_used, monte_seed)
@@ -202,3 +215,52 @@ def monte_reserve(draws, mode="monte"):
     s = ctypes.c_uint16()
     _lib.check(lib, "lnsb_monte_reserve", lib.lnsb_monte_reserve(draws, ctypes.byref(s)))
     return s.value
+
+
+class WeightCache:
+    """lnsb_weight_cache_*: weights converted to LNS once per (data pointer,
+    type, rows, cols) and kept on the device within a byte budget
+    (budget < 0: GGML_LNS_CUDA_CACHE_MB, else free memory less 1 GiB)."""
+
+    def __init__(self, ks, budget=-1):
+        self.ks = ks
+        self.lib = ks.lib
+        self.h = self.lib.lnsb_weight_cache_create(ks.fmt, budget)
+        if not self.h:
+            raise LnsbError(self.lib, "lnsb_weight_cache_create", -1)
+
+    def get(self, src, type, rows, cols, scratch=None, stream=None):
+        """device address of the k-major LNS image of `src` (a torch tensor
+        on the device, or a numpy array / address in host memory)"""
+        out = ctypes.c_void_p()
+        _lib.check(self.lib, "lnsb_weight_cache_get",
+                   self.lib.lnsb_weight_cache_get(self.h, _addr(src), _lib.TYPES.get(type, type), rows, cols,
+                                                  _ptr(scratch) if scratch is not None else None, ctypes.byref(out),
+                                                  _stream(stream)))
+        return out.value
+
+    def stats(self):
+        e, u, b = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        _lib.check(self.lib, "lnsb_weight_cache_stats",
+                   self.lib.lnsb_weight_cache_stats(self.h, ctypes.byref(e), ctypes.byref(u), ctypes.byref(b)))
+        return {"entries": e.value, "used": u.value, "budget": b.value}
+
+    def close(self):
+        if self.h:
+            self.lib.lnsb_weight_cache_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _addr(obj):
+    """device or host address of a torch tensor, a numpy array or an int"""
+    if hasattr(obj, "data_ptr"):
+        return obj.data_ptr()
+    if hasattr(obj, "ctypes"):
+        return obj.ctypes.data
+    return int(obj)

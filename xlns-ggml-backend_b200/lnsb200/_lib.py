@@ -9,6 +9,9 @@ LIB_DIR = os.path.join(os.path.dirname(HERE), "lib")
 
 MODES = ("base", "monte", "monte_bylpvip", "lpvip", "sum32")
 
+# ggml storage types of weights (ggml_type ids)
+TYPES = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 8, "q4_k": 12, "q6_k": 14, "bf16": 30}
+
 XLNS16 = 16
 XLNS32 = 32
 
@@ -61,6 +64,13 @@ SIGNATURES = [
     ("lnsb_to_lns", ctypes.c_int, [ctypes.c_int, _VP, _VP, _I64, _VP]),
     ("lnsb_to_lns_transposed", ctypes.c_int, [ctypes.c_int, _VP, _VP, _I64, _I64, _I64, _VP]),
     ("lnsb_to_f32", ctypes.c_int, [ctypes.c_int, _VP, _VP, _I64, _VP]),
+    ("lnsb_type_row_bytes", ctypes.c_size_t, [ctypes.c_int, _I64]),
+    ("lnsb_to_lns_transposed_typed", ctypes.c_int, [ctypes.c_int, ctypes.c_int, _VP, _VP, _I64, _I64, _I64, _VP]),
+    ("lnsb_dequantize", ctypes.c_int, [ctypes.c_int, _VP, _VP, _I64, _I64, _VP]),
+    ("lnsb_weight_cache_create", _VP, [ctypes.c_int, _I64]),
+    ("lnsb_weight_cache_destroy", None, [_VP]),
+    ("lnsb_weight_cache_get", ctypes.c_int, [_VP, _VP, ctypes.c_int, _I64, _I64, _VP, ctypes.POINTER(_VP), _VP]),
+    ("lnsb_weight_cache_stats", ctypes.c_int, [_VP, ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
     ("lnsb_mul_mat", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), _VP]),
     ("lnsb_mul_mat_lns", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), _VP, _VP]),
     ("lnsb_mul_mat_id", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatIdArgs), _VP]),
