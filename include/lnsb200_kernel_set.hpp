@@ -123,6 +123,22 @@ public:
         return ret(lnsb_rms_norm_lns(fmt_, src, dst, ncols, nrows, eps, monte_seed, stream));
     }
 
+    // MUL_MAT_ID (lns-backend/src/lns-ops.cpp:394-462; the reference's GPU
+    // backend declines it), F32 out to a.dst or LNS codes out to dst
+    cudaError_t mul_mat_id(const lnsb_mul_mat_id_args & a, cudaStream_t stream) const {
+        return ret(lnsb_mul_mat_id(fmt_, &a, stream));
+    }
+    cudaError_t mul_mat_id_lns(const lnsb_mul_mat_id_args & a, void * dst, cudaStream_t stream) const {
+        return ret(lnsb_mul_mat_id_lns(fmt_, &a, dst, stream));
+    }
+    uint64_t mul_mat_id_draws(const lnsb_mul_mat_id_args & a) const { return lnsb_mul_mat_id_draws(fmt_, &a); }
+
+    // weights in ggml storage types (LNSB_TYPE_*), decoded on the device
+    cudaError_t to_lns_transposed_typed(int type, const void * src, void * dst, int64_t rows, int64_t cols,
+                                        int64_t dst_ld, cudaStream_t stream) const {
+        return ret(lnsb_to_lns_transposed_typed(fmt_, type, src, dst, rows, cols, dst_ld, stream));
+    }
+
     // the C ABI status of this thread's last call through any kernel_set
     static int last_status() { return last_(); }
 
@@ -151,6 +167,33 @@ inline const kernel_set & xlns32_kernels() {
     static const kernel_set k(LNSB_XLNS32);
     return k;
 }
+
+// The weight cache (lns-cuda-context.h:79-113) as an owning handle: get()
+// returns the cached k-major LNS image of a weight, converting it on a miss.
+class weight_cache {
+public:
+    // budget_bytes < 0: GGML_LNS_CUDA_CACHE_MB, else free device memory less 1 GiB
+    explicit weight_cache(const kernel_set & ks, int64_t budget_bytes = -1)
+        : h_(lnsb_weight_cache_create(ks.value_size() == 2 ? LNSB_XLNS16 : LNSB_XLNS32, budget_bytes)) {}
+    ~weight_cache() { lnsb_weight_cache_destroy(h_); }
+    weight_cache(const weight_cache &) = delete;
+    weight_cache & operator=(const weight_cache &) = delete;
+
+    bool valid() const { return h_ != nullptr; }
+    // nullptr on failure (status in *st when st is given)
+    const void * get(const void * src, int type, int64_t rows, int64_t cols, void * scratch, cudaStream_t stream,
+                     cudaError_t * st = nullptr) const {
+        const void * out = nullptr;
+        const int r = lnsb_weight_cache_get(h_, src, type, rows, cols, scratch, &out, stream);
+        if (st != nullptr) *st = to_cuda(r);
+        return r == LNSB_OK ? out : nullptr;
+    }
+    int64_t entries() const { int64_t e = 0; lnsb_weight_cache_stats(h_, &e, nullptr, nullptr); return e; }
+    int64_t used() const { int64_t u = 0; lnsb_weight_cache_stats(h_, nullptr, &u, nullptr); return u; }
+
+private:
+    lnsb_weight_cache * h_;
+};
 
 // Monte LFSR state of the process (ggml_backend_lns16_monte_*, lns-backend/include/ggml-lns.h:13-24)
 inline uint16_t monte_get_state() {

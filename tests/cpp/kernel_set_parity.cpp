@@ -11,6 +11,8 @@
 #include <string>
 #include <vector>
 
+#include <cuda_fp16.h>
+
 #include "lnsb200_kernel_set.hpp"
 
 extern "C" {
@@ -160,6 +162,53 @@ void test_mul_mat32(const lnsb200::kernel_set & ks, int64_t K, int64_t M, int64_
     check(ok && dout.get() == want, buf);
 }
 
+void test_mul_mat_id16(const lnsb200::kernel_set & ks, int mode) {
+    const int64_t n_expert = 4, K = 200, M = 70, n_tokens = 3, n_used = 2, ne11 = 1;
+    rng r(21);
+    const auto w = codes16(r.normal((size_t) (n_expert * M * K), 0.02));     // [e][m][k]
+    const auto x = codes16(r.normal((size_t) (n_tokens * ne11 * K), 1.0));
+    std::vector<int32_t> ids = { 3, 1, 0, 0, 2, 3 };
+    std::vector<uint16_t> wk((size_t) (n_expert * K * M));
+    for (int64_t e = 0; e < n_expert; e++)
+        for (int64_t m = 0; m < M; m++)
+            for (int64_t k = 0; k < K; k++) wk[(size_t) ((e * K + k) * M + m)] = w[(size_t) ((e * M + m) * K + k)];
+    dev<uint16_t> dw(wk), dx(x), dout((size_t) (n_tokens * n_used * M));
+    dev<int32_t> di(ids);
+    lnsb_mul_mat_id_args a{ dw.p, dx.p, di.p, nullptr, K, M, n_expert, ne11, n_used, n_tokens, n_used, 0xB403 };
+    const bool ok = ks.mul_mat_id_lns(a, dout.p, nullptr) == cudaSuccess;
+    cudaDeviceSynchronize();
+    std::vector<uint16_t> want(dout.n);
+    orc16_mul_mat_id(mode, w.data(), x.data(), ids.data(), want.data(), K, M, n_expert, ne11, n_used, n_tokens, n_used,
+                     0xB403, 8);
+    check(ok && dout.get() == want, "mul_mat_id xlns16 4 experts, 3 tokens x 2 slots, K=200 M=70");
+}
+
+void test_weight_cache(const lnsb200::kernel_set & ks) {
+    const int64_t rows = 96, cols = 512;
+    rng r(23);
+    const auto f = r.normal((size_t) (rows * cols), 0.05);
+    std::vector<uint16_t> h16(f.size());
+    for (size_t i = 0; i < f.size(); i++) {                // F16 rows on the host (round to nearest even)
+        const __half v = __float2half_rn(f[i]);
+        std::memcpy(&h16[i], &v, 2);
+    }
+    lnsb200::weight_cache cache(ks, 1 << 20);
+    cudaError_t st = cudaErrorUnknown;
+    const void * img = cache.get(h16.data(), LNSB_TYPE_F16, rows, cols, nullptr, nullptr, &st);
+    const void * again = cache.get(h16.data(), LNSB_TYPE_F16, rows, cols, nullptr, nullptr);
+    std::vector<uint16_t> got((size_t) (rows * cols));
+    if (img != nullptr) cudaMemcpy(got.data(), img, got.size() * 2, cudaMemcpyDeviceToHost);
+    std::vector<uint16_t> want(got.size());
+    for (int64_t m = 0; m < rows; m++)
+        for (int64_t k = 0; k < cols; k++) {
+            __half hv;
+            std::memcpy(&hv, &h16[(size_t) (m * cols + k)], 2);
+            want[(size_t) (k * rows + m)] = orc16_from_f32(__half2float(hv));
+        }
+    check(st == cudaSuccess && img != nullptr && img == again && cache.entries() == 1 && got == want,
+          "weight_cache: F16 host rows, converted once, k-major image");
+}
+
 }  // namespace
 
 int main() {
@@ -196,6 +245,8 @@ int main() {
     test_mul_mat16(k16, mode, 100, 37, 5, 0xB403);     // ragged
     test_soft_max16(k16, mode);
     test_rms_norm16(k16, mode);
+    test_mul_mat_id16(k16, mode);
+    test_weight_cache(k16);
     test_mul_mat32(k32, 576, 96, 9);
     test_mul_mat32(k32, 129, 33, 4);
 

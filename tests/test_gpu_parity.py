@@ -324,13 +324,13 @@ def test_mul_mat32_slices_specials_f32(orc, ks32):
     assert np.array_equal(outf.cpu().numpy().view(np.uint32), orc.to_f32_32(want).view(np.uint32))
 
 
-def test_soft_max32_rms_norm32(orc, ks32):
-    rng = np.random.default_rng(4)
-    n, r1 = 100, 20
+@pytest.mark.parametrize("n,r1", [(100, 20), (512, 45), (60000, 3)])   # the last: rows too long for shared memory
+def test_soft_max32_rms_norm32(orc, ks32, n, r1):
+    rng = np.random.default_rng(4 + n)
     src = codes32(orc, rng, (r1, n), 3.0)
     m = np.zeros((r1, n), np.float32)
     for q in range(r1):
-        m[q, q + 81:] = -np.inf
+        m[q, q + n - r1 + 1:] = -np.inf
     mask = orc.mask32(m)
     scale_code = int(orc.from_f32_32(np.array([0.125], np.float32))[0])
     want = orc.soft_max32(src, (n, r1, 1, 1), mask, (n, r1, 1, 1), scale_code, nthreads=NT)
@@ -338,10 +338,11 @@ def test_soft_max32_rms_norm32(orc, ks32):
     w = torch.empty(src.size, dtype=torch.int32, device="cuda")
     ks32.soft_max_lns(dev32(src), (n, r1, 1, 1), d, w, dev32(mask), (n, r1, 1, 1), scale_code)
     assert np.array_equal(host32(d), want)
-    x = codes32(orc, rng, (10, 576), 1.0)
-    want = orc.rms_norm32(x, 576, 10, 1e-5, nthreads=NT)
+    x = codes32(orc, rng, (r1, n), 1.0)
+    x.ravel()[:: 17] = 0                                   # zero codes among the squares
+    want = orc.rms_norm32(x, n, r1, 1e-5, nthreads=NT)
     d = torch.empty(x.size, dtype=torch.int32, device="cuda")
-    ks32.rms_norm_lns(dev32(x), d, 576, 10, 1e-5)
+    ks32.rms_norm_lns(dev32(x), d, n, r1, 1e-5)
     assert np.array_equal(host32(d), want)
 
 

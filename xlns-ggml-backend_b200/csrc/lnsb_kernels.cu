@@ -1403,11 +1403,15 @@ k_mul_mat_id(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
 // run the general reduction policy.
 constexpr bool NNCHAIN = k_mode == M_BASE || k_mode == M_SUM32;
 constexpr int  NN_TAB  = k_mode == M_SUM32 ? k32f_sb_bytes16 : 0;   // sb knot bytes in dynamic smem
+// xlns32 normalisers: always the non-negative chain over the sb knots, 4-byte terms
+template <int FMT> __host__ __device__ constexpr int nn_tab() { return FMT == 32 ? k32f_sb_bytes16 : NN_TAB; }
+template <int FMT> __host__ __device__ constexpr int nn_term_bytes() { return FMT == 32 ? 4 : 2; }
 
 // the sb knots of the flat xlns32 image (all a non-negative chain reads) into
 // shared memory, asynchronously (committed with the block's other copies)
+template <int FMT = 16>
 __device__ __forceinline__ void nn_tables(const dev_tables & T, int32_t * F) {
-    if constexpr (k_mode == M_SUM32) stage_async(F, T.flat32, k32f_sb_bytes16);
+    if constexpr (FMT == 32 || k_mode == M_SUM32) stage_async(F, T.flat32, k32f_sb_bytes16);
 }
 // the xlns16 tables a normaliser block keeps in shared memory (sbdb16, and the
 // Monte fine tables in monte mode), asynchronously
@@ -1429,7 +1433,7 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
     __shared__ __align__(16) int16_t fine[k_mode == M_MONTE ? 2 * k16_monte_n : 8];
     __shared__ uint32_t s_inv[32];
     extern __shared__ __align__(16) int32_t dyn[];          // NNCHAIN: [sb knots (sum32)][squares: rpb x ncols]
-    constexpr bool NNC = FMT == 16 && NNCHAIN;
+    constexpr bool NNC = FMT == 32 || NNCHAIN;
     const bool     NN  = NNC && nn_ok != 0;                 // the squares fit in shared memory
     if constexpr (FMT == 16) norm_tables(T, tab, fine);
     const int64_t row0 = (int64_t) blockIdx.x * rpb;
@@ -1442,12 +1446,14 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
             return FMT == 16 ? (uint32_t) static_cast<const uint16_t *>(src)[idx] : static_cast<const uint32_t *>(src)[idx];
         }
     };
-    uint16_t * sq = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + NN_TAB);
+    uint16_t * sq   = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
+    uint32_t * sq32 = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
     if (NN) {
-        nn_tables(T, dyn);
+        nn_tables<FMT>(T, dyn);
         for (int64_t e = threadIdx.x; e < nr * ncols; e += blockDim.x) {
             const uint32_t v = load(row0 * ncols + e);
-            sq[e] = (uint16_t) mul16(v, v);
+            if constexpr (FMT == 16) sq[e] = (uint16_t) mul16(v, v);
+            else                     sq32[e] = mul32(v, v);
         }
     }
     cp_async_commit();
@@ -1455,7 +1461,13 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
     __syncthreads();
     if (threadIdx.x < nr) {
         const int64_t row = row0 + threadIdx.x;
-        if (NN) {
+        if (NN && FMT == 32) {
+            const uint32_t * q = sq32 + threadIdx.x * ncols;
+            uint32_t acc = 0u;
+            for (int64_t i = 0; i < ncols; i++) acc = padd32f(dyn, acc, q[i]);
+            const uint32_t mean = mul32(acc, inv_n);
+            s_inv[threadIdx.x] = recip32(sqrt32(add32(T, mean, eps_l)));
+        } else if (NN) {
             const uint16_t * q = sq + threadIdx.x * ncols;
             uint32_t acc = 0u;                              // the zero code (acc32 0 in sum32)
             for (int64_t i = 0; i < ncols; i++) acc = nn_add(dyn, tab, acc, q[i]);
@@ -1516,13 +1528,11 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     __shared__ uint32_t s_max[32][4];
     __shared__ uint32_t s_tot[32];
     constexpr uint32_t NEG_INF = FMT == 16 ? 0xFFFFu : 0xFFFFFFFFu;
-    const bool NN = FMT == 16 && NNCHAIN && nn_ok != 0;
-    if constexpr (FMT == 16) {
-        norm_tables(T, tab, fine);
-        if (NN) nn_tables(T, dyn);
-        cp_async_commit();
-        cp_async_wait<0>();
-    }
+    const bool NN = (FMT == 32 || NNCHAIN) && nn_ok != 0;
+    if constexpr (FMT == 16) norm_tables(T, tab, fine);
+    if (NN) nn_tables<FMT>(T, dyn);
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
     const int64_t n = s.ne[0];
     const int64_t nrows = s.ne[1] * s.ne[2] * s.ne[3];
@@ -1577,7 +1587,8 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     }
     __syncthreads();
     // pass 2: c = exp(v - max) into work (and, for the non-negative chain, shared memory)
-    uint16_t * cs = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + NN_TAB);
+    uint16_t * cs   = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
+    uint32_t * cs32 = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
     for (int r = warp; r < nr; r += 4) {
         const int64_t row = row0 + r;
         const uint32_t mx = s_max[r][0];
@@ -1588,7 +1599,9 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
                 static_cast<uint16_t *>(work)[row * n + i] = e;
                 if (NN) cs[r * n + i] = e;
             } else {
-                static_cast<uint32_t *>(work)[row * n + i] = exp32(T, sub32(T, v, mx));
+                const uint32_t e = exp32(T, sub32(T, v, mx));
+                static_cast<uint32_t *>(work)[row * n + i] = e;
+                if (NN) cs32[r * n + i] = e;
             }
         }
     }
@@ -1597,7 +1610,12 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     if (threadIdx.x < nr) {
         const int64_t row = row0 + threadIdx.x;
         const void * c = work;
-        if (NN) {
+        if (NN && FMT == 32) {
+            const uint32_t * q = cs32 + threadIdx.x * n;
+            uint32_t acc = q[0];
+            for (int64_t i = 1; i < n; i++) acc = padd32f(dyn, acc, q[i]);
+            s_tot[threadIdx.x] = acc;
+        } else if (NN) {
             const uint16_t * q = cs + threadIdx.x * n;
             red16 R{ &T, tab, fine };
             uint32_t acc = R.from(q[0]);
@@ -1984,24 +2002,22 @@ int rms_norm_impl(int fmt, const void * src, void * dst, int64_t ncols, int64_t 
     }
     // non-negative chains over shared memory (base, sum32): the block's squares must fit
     int rpb = 32, nn_ok = 0, dsmem = 0;
-    if (fmt == LNSB_XLNS16 && NNCHAIN) {
-        const int64_t fit = (NN_SMEM_MAX - NN_TAB) / (ncols * 2);
+    if (fmt == LNSB_XLNS32 || NNCHAIN) {
+        const int tabb = fmt == LNSB_XLNS32 ? nn_tab<32>() : nn_tab<16>();
+        const int tb   = fmt == LNSB_XLNS32 ? 4 : 2;
+        const int64_t fit = (NN_SMEM_MAX - tabb) / (ncols * tb);
         if (fit >= 1) {
             rpb = (int) imin64(32, fit);
             nn_ok = 1;
-            dsmem = NN_TAB + (int) (((int64_t) rpb * ncols * 2 + 15) / 16 * 16);
+            dsmem = tabb + (int) (((int64_t) rpb * ncols * tb + 15) / 16 * 16);
         }
     }
     const unsigned blocks = (unsigned) ((nrows + rpb - 1) / rpb);
-    if (fmt == LNSB_XLNS16) {
-        auto kern = io_f32 ? k_rms_norm<16, true> : k_rms_norm<16, false>;
-        const int st2 = nn_smem_attr((const void *) kern, dsmem);
-        if (st2 != 0) return st2;
-        kern<<<blocks, 128, dsmem, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, nn_ok);
-    } else {
-        if (io_f32) k_rms_norm<32, true><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, 0);
-        else        k_rms_norm<32, false><<<blocks, 128, 0, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, 0);
-    }
+    auto kern = fmt == LNSB_XLNS16 ? (io_f32 ? k_rms_norm<16, true> : k_rms_norm<16, false>)
+                                   : (io_f32 ? k_rms_norm<32, true> : k_rms_norm<32, false>);
+    const int st2 = nn_smem_attr((const void *) kern, dsmem);
+    if (st2 != 0) return st2;
+    kern<<<blocks, 128, dsmem, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, nn_ok);
     return launch_status();
 }
 
@@ -2021,24 +2037,22 @@ int soft_max_impl(int fmt, const void * src, lnsb_shape4 s, const void * mask, l
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
     int rpb = 32, nn_ok = 0, dsmem = 0;
-    if (fmt == LNSB_XLNS16 && NNCHAIN) {
-        const int64_t fit = (NN_SMEM_MAX - NN_TAB) / (s.ne[0] * 2);
+    if (fmt == LNSB_XLNS32 || NNCHAIN) {
+        const int tabb = fmt == LNSB_XLNS32 ? nn_tab<32>() : nn_tab<16>();
+        const int tb   = fmt == LNSB_XLNS32 ? 4 : 2;
+        const int64_t fit = (NN_SMEM_MAX - tabb) / (s.ne[0] * tb);
         if (fit >= 1) {
             rpb = (int) imin64(32, fit);
             nn_ok = 1;
-            dsmem = NN_TAB + (int) (((int64_t) rpb * s.ne[0] * 2 + 15) / 16 * 16);
+            dsmem = tabb + (int) (((int64_t) rpb * s.ne[0] * tb + 15) / 16 * 16);
         }
     }
     const unsigned blocks = (unsigned) ((nrows + rpb - 1) / rpb);
-    if (fmt == LNSB_XLNS16) {
-        auto kern = io_f32 ? k_soft_max<16, true> : k_soft_max<16, false>;
-        const int st2 = nn_smem_attr((const void *) kern, dsmem);
-        if (st2 != 0) return st2;
-        kern<<<blocks, 128, dsmem, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed, rpb, nn_ok);
-    } else {
-        if (io_f32) k_soft_max<32, true><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed, rpb, 0);
-        else        k_soft_max<32, false><<<blocks, 128, 0, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed, rpb, 0);
-    }
+    auto kern = fmt == LNSB_XLNS16 ? (io_f32 ? k_soft_max<16, true> : k_soft_max<16, false>)
+                                   : (io_f32 ? k_soft_max<32, true> : k_soft_max<32, false>);
+    const int st2 = nn_smem_attr((const void *) kern, dsmem);
+    if (st2 != 0) return st2;
+    kern<<<blocks, 128, dsmem, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed, rpb, nn_ok);
     return launch_status();
 }
 
