@@ -251,6 +251,43 @@ __device__ __forceinline__ uint32_t add32f_lean(const int32_t * F, uint32_t a, u
     return o.cot ? add32f_cot(F, o.mx, o.d) : o.r;
 }
 
+// add32 over the flat image for a chain's latency: the main result (sb(d),
+// or db(d) for d >= 1, by the loaded descriptor of d's octave) and the
+// cotransformed one (sb of the gap, its segment by compare) are computed
+// independently and selected, so the dependent path is two table levels
+// deep instead of three.  Same bits as add32.
+__device__ __forceinline__ int32_t interp32_sh(const int32_t * F, uint32_t z, int sh, int32_t base) {
+    const int32_t i  = (int32_t) (z >> sh) + base;
+    const int32_t f  = (int32_t) (z & ((1u << sh) - 1u));
+    const int32_t v0 = F[i], v1 = F[i + 1];
+    return v0 + (((v1 - v0) * f) >> sh);
+}
+__device__ __forceinline__ uint32_t add32f_sel(const int32_t * F, uint32_t a, uint32_t b) {
+    const uint32_t al = a & 0x7FFFFFFFu, bl = b & 0x7FFFFFFFu;
+    const bool     agt   = al > bl;
+    const uint32_t d     = agt ? al - bl : bl - al;
+    const uint32_t mx    = agt ? a : b;
+    const bool     usedb = (int32_t) (a ^ b) < 0;
+    const bool     cot   = usedb && d < k32_one;
+    // main: |mx| + sb(d) or db(d); above 0x7FFFFFFF the carry reaches the sign bit
+    const uint32_t z    = d < k32_ess ? d : k32_ess;
+    const int32_t  desc = F[k32f_desc + (int32_t) (z >> 23) + (usedb ? k32f_desc_db : 0)];
+    const uint32_t r0   = mx + (uint32_t) interp32_sh(F, z, desc & 31, desc >> 5);
+    const uint32_t rm   = (int32_t) (r0 ^ mx) < 0 ? (mx | 0x7FFFFFFFu) : r0;
+    // cot: max(la, lb) + sb(|la - lb|), clamped at zero
+    const int32_t  d2 = (int32_t) (d & 4095u);
+    const int32_t  la = F[k32f_lo + d2];
+    const int32_t  lb = F[k32f_hi + (int32_t) ((d >> 12) & 2047u)] - d2;
+    const int32_t  hi = la > lb ? la : lb;
+    uint32_t       zc = (uint32_t) (la > lb ? la - lb : lb - la);
+    zc = zc < k32_ess ? zc : k32_ess;
+    const bool     big = zc >= ((uint32_t) k32f_sb_split << 23);
+    const int32_t  p   = (int32_t) (mx & 0x7FFFFFFFu) + hi +
+                         interp32_sh(F, zc, big ? k32f_sb_sh1 : k32f_sb_sh0, big ? k32f_sb_base1 : k32f_sb);
+    const uint32_t rc  = (mx & 0x80000000u) | (uint32_t) (p > 0 ? p : 0);
+    return cot ? (d == 0 ? 0u : rc) : rm;
+}
+
 __device__ __forceinline__ uint32_t sub32(const dev_tables & T, uint32_t a, uint32_t b) {
     return add32(T, a, b ^ 0x80000000u);
 }

@@ -1076,10 +1076,10 @@ __device__ __forceinline__ void a32_step_x(const int32_t * F, const int32_t * LP
                                            uint32_t (&st)[TN], uint32_t w, const uint32_t (&x)[TN]) {
     using OP = a32_fmt<FMT>;
     if constexpr (a32_kind<FMT>() == A32_FLAT && BF) {
-        // latency regime: the branch-free adder (every lane makes the
-        // cotransformation lookups), no divergence on the dependent path
+        // latency regime: the selected adder (main and cotransformed results
+        // side by side, two table levels deep), no divergence on the dependent path
 #pragma unroll
-        for (int t = 0; t < TN; t++) acc[t] = add32f(F, acc[t], OP::term(w, x[t]));
+        for (int t = 0; t < TN; t++) acc[t] = add32f_sel(F, acc[t], OP::term(w, x[t]));
     } else if constexpr (a32_kind<FMT>() == A32_FLAT) {
         uint32_t    b[TN];
         add32f_part o[TN];
@@ -1378,10 +1378,10 @@ k_mul_mat_id(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
                     if (k >= K) break;
                     if constexpr (FMT == 32) {
                         const uint32_t p = mul32(w8[j], x8[j]);
-                        acc = k == 0 ? p : add32f(F, acc, p);
+                        acc = k == 0 ? p : add32f_sel(F, acc, p);
                     } else if constexpr (k_mode == M_SUM32) {
                         const uint32_t p = mul16(w8[j], x8[j]) << 16;
-                        acc = k == 0 ? p : add32f(F, acc, p);
+                        acc = k == 0 ? p : add32f_sel(F, acc, p);
                     } else {
                         const uint32_t p = mul16(w8[j], x8[j]);
                         acc = k == 0 ? R.from(p) : R.add(acc, p, st);
