@@ -971,8 +971,12 @@ constexpr int A32_THREADS = 512;
 // threads per CTA: 32 warps per SM where the per-warp rings fit beside the
 // table (xlns16), else 16
 __host__ __device__ constexpr int a32_threads(int fmt, bool ring) { return fmt == 16 && ring ? 1024 : A32_THREADS; }
-#ifndef LNSB_A32_LAT_BF
-#define LNSB_A32_LAT_BF 1            // one round of units (chain latency bound): branch-free adder
+#ifndef LNSB_A32_SEL_WARPS
+// at most this many units per SM: the SM is latency bound and the chains take
+// the selected adder (add32f_sel, two table levels deep, more instructions);
+// beyond it issue binds and they take the main path with a branch for the
+// cotransformed case
+#define LNSB_A32_SEL_WARPS 16
 #endif
 #ifndef LNSB_A32_TN2_MIN_UNITS
 #define LNSB_A32_TN2_MIN_UNITS 2     // two tokens per lane once each warp gets this many units
@@ -1195,7 +1199,7 @@ __global__ void __launch_bounds__(a32_threads(FMT, RING), 1)
 k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
               const typename a32_fmt<FMT>::elem * __restrict__ X, void * __restrict__ dst, int64_t K, int64_t M,
               int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3, int64_t nz, uint32_t monte_seed,
-              int vecx) {
+              int vecx, int lat_sel) {
     using E  = typename a32_fmt<FMT>::elem;
     using OP = a32_fmt<FMT>;
     using RG = a32_ring<FMT, TN>;
@@ -1259,7 +1263,8 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
                     const unsigned char * sg = ring + (int) (c % A32_STAGES) * RG::stage;
                     if (lat) {                           // few units: all 8 steps unrolled, operands in registers
                         RG::read(cur, sg, lane);
-                        a32_steps<FMT, TN, LNSB_A32_LAT_BF != 0>(F, LP, cur, acc, st, c == 0, K - c * 8);
+                        if (lat_sel) a32_steps<FMT, TN, true>(F, LP, cur, acc, st, c == 0, K - c * 8);
+                        else         a32_steps<FMT, TN, false>(F, LP, cur, acc, st, c == 0, K - c * 8);
                         continue;
                     }
                     const E * ws = reinterpret_cast<const E *>(sg) + lane;
@@ -1802,7 +1807,8 @@ int launch_a32(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, in
     const int64_t grid = units < sm_count(dev) ? units : sm_count(dev);
     kern<<<(unsigned) grid, a32_threads(FMT, RING), smem, stream>>>(T, static_cast<const E *>(a->w), static_cast<const E *>(a->x),
                                                        dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3,
-                                                       a->ne12 * a->ne13, a->monte_seed, vecx ? 1 : 0);
+                                                       a->ne12 * a->ne13, a->monte_seed, vecx ? 1 : 0,
+                                                       units <= (int64_t) sm_count(dev) * LNSB_A32_SEL_WARPS ? 1 : 0);
     return launch_status();
 }
 
