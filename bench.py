@@ -459,18 +459,18 @@ def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16):
            "first_tokens": toks[:8]}
     if cpu:
         # the CPU oracle (the reference's algorithm, host cores) on a bounded sample:
-        # prefill of 8 tokens, then 2 decode steps
+        # prefill of 8 tokens, then 16 decode steps (a few seconds)
         import time
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        o = model.OracleOps(cfg, w, mode=args.decode_mode, n_ctx=16, nthreads=os.cpu_count() or 1, fmt=fmt)
+        o = model.OracleOps(cfg, w, mode=args.decode_mode, n_ctx=32, nthreads=os.cpu_count() or 1, fmt=fmt)
         lo = model.forward(o, cfg, prompt[:8], 0)
         t0 = time.perf_counter()
         tk = o.argmax(lo)
-        for p in range(8, 10):
+        for p in range(8, 24):
             tk = o.argmax(model.forward(o, cfg, [tk], p))
         dt = time.perf_counter() - t0
-        out["cpu_baseline"] = {"decode_tok_per_s": 2 / dt, "cores": os.cpu_count() or 1, "kind": "port",
-                               "sample": "oracle model: 8-token prefill, then 2 decode steps timed (%.1f s)" % dt}
+        out["cpu_baseline"] = {"decode_tok_per_s": 16 / dt, "cores": os.cpu_count() or 1, "kind": "port",
+                               "sample": "oracle model: 8-token prefill, then 16 decode steps timed (%.1f s)" % dt}
     return out
 
 
