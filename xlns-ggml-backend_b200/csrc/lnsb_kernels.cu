@@ -17,6 +17,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <utility>
 
 #include "lnsb200.h"
 #include "lnsb_arith.cuh"
@@ -81,6 +82,38 @@ __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { retur
 int status_of(cudaError_t e) { return e == cudaSuccess ? 0 : (int) e; }
 int launch_status() { return status_of(cudaGetLastError()); }
 
+// Programmatic dependent launch.  Every kernel of this library is launched
+// with programmatic stream serialisation and begins with pdl_entry(): it
+// waits there for the grid before it in the stream to complete (and its
+// writes to be visible) before touching any data, then lets the grid after
+// it launch.  The next kernel's launch and block scheduling so overlap this
+// kernel's run instead of following its last block -- in a decode step of
+// ~1,000 dependent launches that latency is a visible share.  A kernel
+// launched without the attribute (torch's, say) is ordered as usual.
+#ifndef LNSB_PDL
+#define LNSB_PDL 1
+#endif
+__device__ __forceinline__ void pdl_entry() {
+#if LNSB_PDL
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" :::);
+#endif
+}
+template <typename... KArgs, typename... Args>
+void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args &&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = LNSB_PDL;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    (void) cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);   // an error stays in cudaGetLastError
+}
+
 bool valid_fmt(int fmt) { return fmt == LNSB_XLNS16 || fmt == LNSB_XLNS32; }
 
 unsigned grid_for(int64_t n, int block) {
@@ -94,6 +127,7 @@ unsigned grid_for(int64_t n, int block) {
 
 template <int FMT>
 __global__ void k_to_lns(dev_tables T, const float * __restrict__ src, void * __restrict__ dst, int64_t n) {
+    pdl_entry();
     for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t) blockDim.x * gridDim.x) {
         if constexpr (FMT == 16) static_cast<uint16_t *>(dst)[i] = (uint16_t) from_f32_16(T, src[i]);
         else                     static_cast<uint32_t *>(dst)[i] = from_f32_32(T, src[i]);
@@ -105,6 +139,7 @@ __global__ void k_to_lns(dev_tables T, const float * __restrict__ src, void * __
 template <int FMT>
 __global__ void k_to_lns_transposed(dev_tables T, const float * __restrict__ src, void * __restrict__ dst,
                                     int64_t rows, int64_t cols, int64_t dst_ld) {
+    pdl_entry();
     using V = typename std::conditional<FMT == 16, uint16_t, uint32_t>::type;
     __shared__ V tile[32][33];
     const int64_t r0 = (int64_t) blockIdx.y * 32, c0 = (int64_t) blockIdx.x * 32;
@@ -193,6 +228,7 @@ template <int FMT>
 __global__ void k_to_lns_transposed_typed(dev_tables T, int type, const unsigned char * __restrict__ src,
                                           int64_t row_bytes, void * __restrict__ dst, int64_t rows, int64_t cols,
                                           int64_t dst_ld) {
+    pdl_entry();
     using V = typename std::conditional<FMT == 16, uint16_t, uint32_t>::type;
     __shared__ V tile[32][33];
     const int64_t r0 = (int64_t) blockIdx.y * 32, c0 = (int64_t) blockIdx.x * 32;
@@ -212,6 +248,7 @@ __global__ void k_to_lns_transposed_typed(dev_tables T, int type, const unsigned
 
 __global__ void k_dequantize(int type, const unsigned char * __restrict__ src, int64_t row_bytes, float * __restrict__ dst,
                              int64_t rows, int64_t cols) {
+    pdl_entry();
     const int64_t n = rows * cols;
     for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t) blockDim.x * gridDim.x) {
         const int64_t r = i / cols, c = i - r * cols;
@@ -221,6 +258,7 @@ __global__ void k_dequantize(int type, const unsigned char * __restrict__ src, i
 
 template <int FMT>
 __global__ void k_to_f32(dev_tables T, const void * __restrict__ src, float * __restrict__ dst, int64_t n) {
+    pdl_entry();
     for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t) blockDim.x * gridDim.x) {
         if constexpr (FMT == 16) dst[i] = to_f32_16(T, static_cast<const uint16_t *>(src)[i]);
         else                     dst[i] = to_f32_32(T, static_cast<const uint32_t *>(src)[i]);
@@ -368,6 +406,7 @@ __global__ void __launch_bounds__(FB_THREADS, FB_MONTE ? 2 : 4)
 k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
                  void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
                  int64_t r2, int64_t r3, uint32_t monte_seed, int vec) {
+    pdl_entry();
     extern __shared__ __align__(16) unsigned char smem[];
     int *      wkeys = reinterpret_cast<int *>(smem + FB_OFF_WKEY);
     int *      xkeys = reinterpret_cast<int *>(smem + FB_OFF_XKEY);
@@ -630,6 +669,7 @@ __global__ void __launch_bounds__(LT_ROWS)
 k_mul_mat16_lat(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
                 void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
                 int64_t r2, int64_t r3, int vec) {
+    pdl_entry();
     extern __shared__ __align__(16) unsigned char smem[];
     int16_t *  tab2  = reinterpret_cast<int16_t *>(smem + LT_OFF_TAB2);
     uint16_t * wst   = reinterpret_cast<uint16_t *>(smem + LT_OFF_W);
@@ -810,6 +850,7 @@ __global__ void __launch_bounds__(128)
 k_mul_mat16_res(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
                 void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
                 int64_t r2, int64_t r3, int vec) {
+    pdl_entry();
     extern __shared__ __align__(16) unsigned char smem[];
     const int  Ki    = (int) K;
     const int  KP    = (Ki + 3) & ~3;
@@ -1207,11 +1248,12 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
     extern __shared__ __align__(16) int32_t F[];
     constexpr int NT = a32_threads(FMT, RING);
     if constexpr (KIND == A32_FLAT) {
-        stage_async(F, T.flat32, k32f_words * 4);
+        stage_async(F, T.flat32, k32f_words * 4);          // read-only tables: before the wait
         cp_async_commit();
         cp_async_wait<0>();
         __syncthreads();
     }
+    pdl_entry();
     const int32_t * LP = T.lpvip_db;
 
     const int     lane = threadIdx.x & 31;
@@ -1337,6 +1379,7 @@ k_mul_mat_id(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
              const typename a32_fmt<FMT>::elem * __restrict__ X, const int32_t * __restrict__ ids,
              void * __restrict__ dst, int64_t K, int64_t M, int64_t n_expert, int64_t ne11, int64_t n_used,
              int64_t n_tokens, int64_t ids_stride, uint32_t monte_seed) {
+    pdl_entry();
     using E = typename a32_fmt<FMT>::elem;
     extern __shared__ __align__(16) unsigned char mmid_sm[];
     int32_t * F    = reinterpret_cast<int32_t *>(mmid_sm);
@@ -1434,6 +1477,7 @@ template <int FMT, bool IO_F32>
 __global__ void __launch_bounds__(128)
 k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst, int64_t ncols, int64_t nrows,
            uint32_t eps_l, uint32_t inv_n, uint32_t monte_seed, int rpb, int nn_ok) {
+    pdl_entry();
     __shared__ __align__(16) int16_t tab[k16_tab_bytes16 / 2];
     __shared__ __align__(16) int16_t fine[k_mode == M_MONTE ? 2 * k16_monte_n : 8];
     __shared__ uint32_t s_inv[32];
@@ -1527,6 +1571,7 @@ __global__ void __launch_bounds__(128)
 k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const void * __restrict__ mask,
            lnsb_shape4 ms, uint32_t scale_l, void * __restrict__ dst, void * __restrict__ work,
            uint32_t monte_seed, int rpb, int nn_ok) {
+    pdl_entry();
     extern __shared__ __align__(16) int32_t dyn[];          // NNCHAIN: [sb knots (sum32)][exp terms: rpb x n]
     __shared__ __align__(16) int16_t tab[k16_tab_bytes16 / 2];
     __shared__ __align__(16) int16_t fine[k_mode == M_MONTE ? 2 * k16_monte_n : 8];
@@ -1701,6 +1746,7 @@ __device__ __forceinline__ uint32_t relu32(uint32_t x) { return ((x & 0x80000000
 template <int FMT, int OP>
 __global__ void k_binary(dev_tables T, const float * __restrict__ a, lnsb_shape4 as, const float * __restrict__ b,
                          lnsb_shape4 bs, float * __restrict__ dst) {
+    pdl_entry();
     using A = ew<FMT>;
     const int64_t n = as.ne[0] * as.ne[1] * as.ne[2] * as.ne[3];
     LNSB_GRID_STRIDE(i, n) {
@@ -1717,6 +1763,7 @@ __global__ void k_binary(dev_tables T, const float * __restrict__ a, lnsb_shape4
 template <int FMT>
 __global__ void k_scale(dev_tables T, const float * __restrict__ src, float * __restrict__ dst, int64_t n, uint32_t sl,
                         uint32_t bl, int has_b) {
+    pdl_entry();
     using A = ew<FMT>;
     LNSB_GRID_STRIDE(i, n) {
         uint32_t v = A::mul(A::from(T, src[i]), sl);
@@ -1727,6 +1774,7 @@ __global__ void k_scale(dev_tables T, const float * __restrict__ src, float * __
 
 template <int FMT, int OP>
 __global__ void k_unary(dev_tables T, const float * __restrict__ src, float * __restrict__ dst, int64_t n) {
+    pdl_entry();
     using A = ew<FMT>;
     LNSB_GRID_STRIDE(i, n) {
         const uint32_t v = A::from(T, src[i]);
@@ -1740,6 +1788,7 @@ __global__ void k_unary(dev_tables T, const float * __restrict__ src, float * __
 template <int FMT>
 __global__ void k_swiglu(dev_tables T, const float * __restrict__ gate, const float * __restrict__ up, int64_t gs,
                          int64_t us, float * __restrict__ dst, int64_t nc, int64_t nr) {
+    pdl_entry();
     using A = ew<FMT>;
     LNSB_GRID_STRIDE(i, nc * nr) {
         const int64_t r = i / nc, c = i - r * nc;
@@ -1752,6 +1801,7 @@ __global__ void k_swiglu(dev_tables T, const float * __restrict__ gate, const fl
 template <int FMT>
 __global__ void k_rope(dev_tables T, const float * __restrict__ src, lnsb_shape4 s, const float * __restrict__ cos_sin,
                        int n_dims, int neox, float * __restrict__ dst) {
+    pdl_entry();
     using A = ew<FMT>;
     const int64_t half = n_dims / 2, per = half + (s.ne[0] - n_dims);
     const int64_t nrows = s.ne[1] * s.ne[2] * s.ne[3];
@@ -1774,9 +1824,11 @@ __global__ void k_rope(dev_tables T, const float * __restrict__ src, lnsb_shape4
 }
 
 __global__ void k_f32_to_f16(const float * __restrict__ src, __half * __restrict__ dst, int64_t n) {
+    pdl_entry();
     LNSB_GRID_STRIDE(i, n) dst[i] = __float2half_rn(src[i]);
 }
 __global__ void k_f16_to_f32(const __half * __restrict__ src, float * __restrict__ dst, int64_t n) {
+    pdl_entry();
     LNSB_GRID_STRIDE(i, n) dst[i] = __half2float(src[i]);
 }
 
@@ -1805,7 +1857,7 @@ int launch_a32(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, in
     }
     using E = typename a32_fmt<FMT>::elem;
     const int64_t grid = units < sm_count(dev) ? units : sm_count(dev);
-    kern<<<(unsigned) grid, a32_threads(FMT, RING), smem, stream>>>(T, static_cast<const E *>(a->w), static_cast<const E *>(a->x),
+    launch_k(kern, (unsigned) grid, a32_threads(FMT, RING), smem, stream, T, static_cast<const E *>(a->w), static_cast<const E *>(a->x),
                                                        dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3,
                                                        a->ne12 * a->ne13, a->monte_seed, vecx ? 1 : 0,
                                                        units <= (int64_t) sm_count(dev) * LNSB_A32_SEL_WARPS ? 1 : 0);
@@ -1869,7 +1921,7 @@ int mul_mat_id_impl(int fmt, const lnsb_mul_mat_id_args * a, void * dst, bool ou
             if (e != cudaSuccess) return (int) e;
             done = true;
         }
-        kern<<<(unsigned) grid, 256, smem, stream>>>(*T, w, x, a->ids, dst, a->K, a->M, a->n_expert, a->ne11, a->n_used,
+        launch_k(kern, (unsigned) grid, 256, smem, stream, *T, w, x, a->ids, dst, a->K, a->M, a->n_expert, a->ne11, a->n_used,
                                                      a->n_tokens, a->ids_stride, a->monte_seed);
         return launch_status();
     };
@@ -1913,7 +1965,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
             if (e != cudaSuccess) return (int) e;
             rattr[dev][out_f32] = LR_SMEM_MAX;
         }
-        kern<<<grid, 32 * lr_tnc, smem, stream>>>(*T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
+        launch_k(kern, grid, 32 * lr_tnc, smem, stream, *T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
                                                   dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, vec ? 1 : 0);
     } else if (fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && a->K <= LT_MAX_K && a->N <= 65535) {
         // few outputs: latency form, two tokens per thread where they fit
@@ -1940,7 +1992,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
             if (e != cudaSuccess) return (int) e;
             lattr[dev][out_f32][tn - 1] = smem;
         }
-        kern<<<grid, LT_ROWS, smem, stream>>>(*T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
+        launch_k(kern, grid, LT_ROWS, smem, stream, *T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
                                               dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, vec ? 1 : 0);
     } else if (fmt == LNSB_XLNS16 && (k_mode == M_BASE || k_mode == M_MONTE)) {
         const int64_t gx = (a->M + FB_BM - 1) / FB_BM, gy = (a->N + FB_BN - 1) / FB_BN;
@@ -1957,7 +2009,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
             if (e != cudaSuccess) return (int) e;
             fattr[dev][out_f32] = true;
         }
-        kern<<<grid, FB_THREADS, FB_SMEM, stream>>>(*T, static_cast<const uint16_t *>(a->w),
+        launch_k(kern, grid, FB_THREADS, FB_SMEM, stream, *T, static_cast<const uint16_t *>(a->w),
                                                     static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
                                                     a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0);
     } else if (fmt == LNSB_XLNS32 || k_mode == M_SUM32 || k_mode == M_LPVIP || k_mode == M_MONTE_BYLPVIP) {
@@ -2023,7 +2075,7 @@ int rms_norm_impl(int fmt, const void * src, void * dst, int64_t ncols, int64_t 
                                    : (io_f32 ? k_rms_norm<32, true> : k_rms_norm<32, false>);
     const int st2 = nn_smem_attr((const void *) kern, dsmem);
     if (st2 != 0) return st2;
-    kern<<<blocks, 128, dsmem, stream>>>(*T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, nn_ok);
+    launch_k(kern, blocks, 128, dsmem, stream, *T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, nn_ok);
     return launch_status();
 }
 
@@ -2058,7 +2110,7 @@ int soft_max_impl(int fmt, const void * src, lnsb_shape4 s, const void * mask, l
                                    : (io_f32 ? k_soft_max<32, true> : k_soft_max<32, false>);
     const int st2 = nn_smem_attr((const void *) kern, dsmem);
     if (st2 != 0) return st2;
-    kern<<<blocks, 128, dsmem, stream>>>(*T, src, s, mask, ms, scale_l, dst, work, seed, rpb, nn_ok);
+    launch_k(kern, blocks, 128, dsmem, stream, *T, src, s, mask, ms, scale_l, dst, work, seed, rpb, nn_ok);
     return launch_status();
 }
 
@@ -2229,8 +2281,8 @@ int lnsb_to_lns(int fmt, const float * src, void * dst, int64_t n, lnsb_stream_t
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (fmt == LNSB_XLNS16) k_to_lns<16><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
-    else                    k_to_lns<32><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
+    if (fmt == LNSB_XLNS16) launch_k(k_to_lns<16>, grid_for(n, 256), 256, 0, s, *T, src, dst, n);
+    else                    launch_k(k_to_lns<32>, grid_for(n, 256), 256, 0, s, *T, src, dst, n);
     return launch_status();
 }
 
@@ -2246,8 +2298,8 @@ int lnsb_to_lns_transposed(int fmt, const float * src, void * dst, int64_t rows,
     const dim3 grid((unsigned) ((cols + 31) / 32), (unsigned) ((rows + 31) / 32));
     const dim3 block(32, 8);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (fmt == LNSB_XLNS16) k_to_lns_transposed<16><<<grid, block, 0, s>>>(*T, src, dst, rows, cols, dst_ld);
-    else                    k_to_lns_transposed<32><<<grid, block, 0, s>>>(*T, src, dst, rows, cols, dst_ld);
+    if (fmt == LNSB_XLNS16) launch_k(k_to_lns_transposed<16>, grid, block, 0, s, *T, src, dst, rows, cols, dst_ld);
+    else                    launch_k(k_to_lns_transposed<32>, grid, block, 0, s, *T, src, dst, rows, cols, dst_ld);
     return launch_status();
 }
 
@@ -2286,8 +2338,8 @@ int lnsb_to_lns_transposed_typed(int fmt, int type, const void * src, void * dst
     const dim3 block(32, 8);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const auto * p = static_cast<const unsigned char *>(src);
-    if (fmt == LNSB_XLNS16) k_to_lns_transposed_typed<16><<<grid, block, 0, s>>>(*T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
-    else                    k_to_lns_transposed_typed<32><<<grid, block, 0, s>>>(*T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
+    if (fmt == LNSB_XLNS16) launch_k(k_to_lns_transposed_typed<16>, grid, block, 0, s, *T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
+    else                    launch_k(k_to_lns_transposed_typed<32>, grid, block, 0, s, *T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
     return launch_status();
 }
 
@@ -2298,7 +2350,7 @@ int lnsb_dequantize(int type, const void * src, float * dst, int64_t rows, int64
     if (cols > 0 && rb == 0) return LNSB_E_INVALID;
     if (rows == 0 || cols == 0) return 0;
     if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
-    k_dequantize<<<grid_for(rows * cols, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    launch_k(k_dequantize, grid_for(rows * cols, 256), 256, 0, static_cast<cudaStream_t>(stream), 
         type, static_cast<const unsigned char *>(src), (int64_t) rb, dst, rows, cols);
     return launch_status();
 }
@@ -2311,8 +2363,8 @@ int lnsb_to_f32(int fmt, const void * src, float * dst, int64_t n, lnsb_stream_t
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (fmt == LNSB_XLNS16) k_to_f32<16><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
-    else                    k_to_f32<32><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n);
+    if (fmt == LNSB_XLNS16) launch_k(k_to_f32<16>, grid_for(n, 256), 256, 0, s, *T, src, dst, n);
+    else                    launch_k(k_to_f32<32>, grid_for(n, 256), 256, 0, s, *T, src, dst, n);
     return launch_status();
 }
 
@@ -2431,7 +2483,7 @@ int lnsb_binary(int fmt, int op, const float * a, const int64_t ane[4], const fl
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned g = grid_for(n, 256);
     const lnsb_shape4 as = shape_of(ane), bs = shape_of(bne);
-#define LNSB_BIN(F, O) k_binary<F, O><<<g, 256, 0, s>>>(*T, a, as, b, bs, dst)
+#define LNSB_BIN(F, O) launch_k(k_binary<F, O>, g, 256, 0, s, *T, a, as, b, bs, dst)
     if (fmt == LNSB_XLNS16) {
         if (op == LNSB_BINARY_ADD) LNSB_BIN(16, LNSB_BINARY_ADD); else if (op == LNSB_BINARY_MUL) LNSB_BIN(16, LNSB_BINARY_MUL); else LNSB_BIN(16, LNSB_BINARY_DIV);
     } else {
@@ -2455,11 +2507,11 @@ int lnsb_scale(int fmt, const float * src, float * dst, int64_t n, float sv, flo
         uint32_t u;
         std::memcpy(&u, &sv, 4); sl = H.conv16[u >> 16];
         std::memcpy(&u, &bv, 4); bl = H.conv16[u >> 16];
-        k_scale<16><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n, sl, bl, bv != 0.0f ? 1 : 0);
+        launch_k(k_scale<16>, grid_for(n, 256), 256, 0, s, *T, src, dst, n, sl, bl, bv != 0.0f ? 1 : 0);
     } else {
         sl = host_from_f32_32(sv);
         bl = host_from_f32_32(bv);
-        k_scale<32><<<grid_for(n, 256), 256, 0, s>>>(*T, src, dst, n, sl, bl, bv != 0.0f ? 1 : 0);
+        launch_k(k_scale<32>, grid_for(n, 256), 256, 0, s, *T, src, dst, n, sl, bl, bv != 0.0f ? 1 : 0);
     }
     return launch_status();
 }
@@ -2475,11 +2527,11 @@ int lnsb_unary(int fmt, int op, const float * src, float * dst, int64_t n, lnsb_
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned g = grid_for(n, 256);
     if (fmt == LNSB_XLNS16) {
-        if (op == LNSB_UNARY_SILU) k_unary<16, LNSB_UNARY_SILU><<<g, 256, 0, s>>>(*T, src, dst, n);
-        else                       k_unary<16, LNSB_UNARY_RELU><<<g, 256, 0, s>>>(*T, src, dst, n);
+        if (op == LNSB_UNARY_SILU) launch_k(k_unary<16, LNSB_UNARY_SILU>, g, 256, 0, s, *T, src, dst, n);
+        else                       launch_k(k_unary<16, LNSB_UNARY_RELU>, g, 256, 0, s, *T, src, dst, n);
     } else {
-        if (op == LNSB_UNARY_SILU) k_unary<32, LNSB_UNARY_SILU><<<g, 256, 0, s>>>(*T, src, dst, n);
-        else                       k_unary<32, LNSB_UNARY_RELU><<<g, 256, 0, s>>>(*T, src, dst, n);
+        if (op == LNSB_UNARY_SILU) launch_k(k_unary<32, LNSB_UNARY_SILU>, g, 256, 0, s, *T, src, dst, n);
+        else                       launch_k(k_unary<32, LNSB_UNARY_RELU>, g, 256, 0, s, *T, src, dst, n);
     }
     return launch_status();
 }
@@ -2495,8 +2547,8 @@ int lnsb_glu(int fmt, int op, const float * gate, const float * up, int64_t gate
     if (st != 0) return st;
     const unsigned g = grid_for(ncols * nrows, 256);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (fmt == LNSB_XLNS16) k_swiglu<16><<<g, 256, 0, s>>>(*T, gate, up, gate_stride, up_stride, dst, ncols, nrows);
-    else                    k_swiglu<32><<<g, 256, 0, s>>>(*T, gate, up, gate_stride, up_stride, dst, ncols, nrows);
+    if (fmt == LNSB_XLNS16) launch_k(k_swiglu<16>, g, 256, 0, s, *T, gate, up, gate_stride, up_stride, dst, ncols, nrows);
+    else                    launch_k(k_swiglu<32>, g, 256, 0, s, *T, gate, up, gate_stride, up_stride, dst, ncols, nrows);
     return launch_status();
 }
 
@@ -2511,8 +2563,8 @@ int lnsb_rope(int fmt, const lnsb_rope_args * a, lnsb_stream_t stream) {
     if (st != 0) return st;
     const int64_t per = a->n_dims / 2 + (a->shape.ne[0] - a->n_dims);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (fmt == LNSB_XLNS16) k_rope<16><<<grid_for(nrows * per, 256), 256, 0, s>>>(*T, a->src, a->shape, a->cos_sin, a->n_dims, a->neox, a->dst);
-    else                    k_rope<32><<<grid_for(nrows * per, 256), 256, 0, s>>>(*T, a->src, a->shape, a->cos_sin, a->n_dims, a->neox, a->dst);
+    if (fmt == LNSB_XLNS16) launch_k(k_rope<16>, grid_for(nrows * per, 256), 256, 0, s, *T, a->src, a->shape, a->cos_sin, a->n_dims, a->neox, a->dst);
+    else                    launch_k(k_rope<32>, grid_for(nrows * per, 256), 256, 0, s, *T, a->src, a->shape, a->cos_sin, a->n_dims, a->neox, a->dst);
     return launch_status();
 }
 
@@ -2520,7 +2572,7 @@ int lnsb_f32_to_f16(const float * src, uint16_t * dst, int64_t n, lnsb_stream_t 
     if (n < 0) return LNSB_E_INVALID;
     if (n == 0) return 0;
     if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
-    k_f32_to_f16<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, reinterpret_cast<__half *>(dst), n);
+    launch_k(k_f32_to_f16, grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream), src, reinterpret_cast<__half *>(dst), n);
     return launch_status();
 }
 
@@ -2528,7 +2580,7 @@ int lnsb_f16_to_f32(const uint16_t * src, float * dst, int64_t n, lnsb_stream_t 
     if (n < 0) return LNSB_E_INVALID;
     if (n == 0) return 0;
     if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
-    k_f16_to_f32<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(reinterpret_cast<const __half *>(src), dst, n);
+    launch_k(k_f16_to_f32, grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream), reinterpret_cast<const __half *>(src), dst, n);
     return launch_status();
 }
 
