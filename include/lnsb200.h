@@ -268,6 +268,33 @@ typedef struct {
 } lnsb_rope_args;
 int lnsb_rope(int fmt, const lnsb_rope_args * args, lnsb_stream_t stream);
 
+/* One decode step's attention (a query at the last cache position, every
+ * cached key visible), fused: for each query head h (kv head h / (n_head /
+ * n_head_kv)), the ops the graph runs as F16 -> F32 of the caches, to_lns,
+ * mul_mat kq, soft_max (scale, the all-zero causal mask row), to_lns and
+ * mul_mat kqv, with every op-boundary conversion kept, so the output is
+ * bit-identical to those ops run one by one (monte_seed for each of the
+ * three, as in lnsb_mul_mat / lnsb_soft_max).
+ *   q        F32 [n_head][head_dim]
+ *   k_cache  F16 [nkv][kv_ld], kv head j at columns [j * head_dim, (j+1) * head_dim)
+ *   v_cache  F16, same layout
+ *   dst      F32 [n_head][head_dim]
+ * LNSB_E_TOO_LARGE when nkv exceeds lnsb_attn_decode_max_keys (the
+ * kernel's shared memory: about 5,700 keys at head_dim 64 beside the 101 KB
+ * flat xlns32 image of sum32 and xlns32, about 19,000 in the other modes). */
+typedef struct {
+    const float *    q;
+    const uint16_t * k_cache;
+    const uint16_t * v_cache;
+    int64_t          kv_ld, nkv;
+    int              n_head, n_head_kv, head_dim;
+    float            scale;
+    float *          dst;
+    uint16_t         monte_seed;
+} lnsb_attn_decode_args;
+int lnsb_attn_decode(int fmt, const lnsb_attn_decode_args * args, lnsb_stream_t stream);
+int64_t lnsb_attn_decode_max_keys(int fmt, int head_dim);
+
 /* F16 storage of F32 values (KV caches): IEEE binary16, round to nearest
  * even, and back (exact).  No LNS involved; not part of kernel_set. */
 int lnsb_f32_to_f16(const float * src, uint16_t * dst, int64_t n, lnsb_stream_t stream);

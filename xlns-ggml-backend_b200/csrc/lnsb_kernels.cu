@@ -1703,6 +1703,175 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     }
 }
 
+// ===================== decode attention, one query position =================
+// One decode step's attention for one head in one CTA: what the model graph
+// runs as F16 -> F32 K/V conversions, to_lns, mul_mat (kq), soft_max (scale,
+// causal mask, normaliser), to_lns and mul_mat (kqv), with every op-boundary
+// conversion kept (codes -> F32 -> codes between the ops), so the bits are
+// those of the unfused ops:
+//   kq[k]  = sum_d K[k][d] q[d]        (K codes from F16 via F32; chains over d)
+//   p      = soft_max(kq * scale)      (every key visible: the mask row is zero)
+//   out[d] = sum_k V[k][d] p[k]        (chains over k)
+// Monte chains start where the unfused calls' chains start: kq chain (h, k)
+// at (h * nkv + k) * (D - 1), the softmax row h at h * (nkv - 1), kqv chain
+// (h, d) at (h * D + d) * (nkv - 1) draws after the seed.  Chains take the
+// build's policy: the selected flat adder (xlns32, sum32) or red16.
+template <int FMT> __host__ __device__ constexpr bool attn_flat() { return FMT == 32 || k_mode == M_SUM32; }
+template <int FMT> __host__ __device__ constexpr int  attn_tab() {
+    return (attn_flat<FMT>() ? k32f_words * 4 : 0) +
+           (FMT == 16 ? k16_tab_bytes16 + (k_mode == M_MONTE ? 2 * k16_monte_n * 2 : 0) : 0);
+}
+
+template <int FMT>
+struct attn_ops {
+    const dev_tables & T;
+    const int32_t *    F;      // flat image (attn_flat)
+    const int16_t *    tab;    // packed xlns16 table
+    const int16_t *    fine;   // Monte fine tables
+    __device__ uint32_t from(float f) const { return FMT == 16 ? from_f32_16(T, f) : from_f32_32(T, f); }
+    __device__ float    to(uint32_t v) const { return FMT == 16 ? to_f32_16(T, v) : to_f32_32(T, v); }
+    __device__ uint32_t mul(uint32_t a, uint32_t b) const { return FMT == 16 ? mul16(a, b) : mul32(a, b); }
+    // a mul_mat chain: start with the first product, step, finish (the build's policy)
+    __device__ uint32_t start(uint32_t p) const {
+        if constexpr (FMT == 32) return p;
+        else if constexpr (k_mode == M_SUM32) return p << 16;
+        else return red16{ &T, tab, fine }.from(p);
+    }
+    __device__ uint32_t step(uint32_t acc, uint32_t p, uint32_t & st) const {
+        if constexpr (FMT == 32) return add32f_sel(F, acc, p);
+        else if constexpr (k_mode == M_SUM32) return add32f_sel(F, acc, p << 16);
+        else return red16{ &T, tab, fine }.add(acc, p, st);
+    }
+    __device__ uint32_t finish(uint32_t acc) const {
+        if constexpr (FMT == 32) return acc;
+        else return red16{ &T, tab, fine }.finish(acc);
+    }
+};
+
+// keys per tile: the K (then V) codes of a tile of keys sit in shared memory,
+// converted by the whole block with coalesced reads of the F16 caches
+constexpr int ATTN_KT = 256;
+
+template <int FMT>
+__global__ void __launch_bounds__(256)
+k_attn_decode(dev_tables T, const float * __restrict__ q, const __half * __restrict__ kc, const __half * __restrict__ vc,
+              int64_t kv_ld, int64_t nkv, int H, int HKV, int D, uint32_t scale_l, float * __restrict__ out,
+              uint32_t seed) {
+    extern __shared__ __align__(16) unsigned char attn_sm[];
+    constexpr int TAB = attn_tab<FMT>();
+    constexpr int KTP = ATTN_KT + 1;                                // [d][k] rows, padded
+    int32_t * F    = reinterpret_cast<int32_t *>(attn_sm);
+    int16_t * tab  = reinterpret_cast<int16_t *>(attn_sm + (attn_flat<FMT>() ? k32f_words * 4 : 0));
+    int16_t * fine = tab + k16_tab_bytes16 / 2;
+    uint32_t * tile = reinterpret_cast<uint32_t *>(attn_sm + TAB);  // K: [d][KTP]; V: [k][D]
+    uint32_t * qc = tile + (int64_t) D * KTP;                       // q codes [D]
+    uint32_t * sv = qc + D;                                         // scaled logits, then exp terms [nkv]
+    uint32_t * pc = sv + nkv;                                       // p codes [nkv]
+    __shared__ uint32_t s_red[8];
+    __shared__ uint32_t s_tot;
+    if constexpr (attn_flat<FMT>()) stage_async(F, T.flat32, k32f_words * 4);
+    if constexpr (FMT == 16) {
+        stage_async(tab, T.sbdb16, k16_tab_bytes16);
+        if constexpr (k_mode == M_MONTE) stage_async(fine, T.monte16, 2 * k16_monte_n * 2);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    pdl_entry();
+    const attn_ops<FMT> O{ T, F, tab, fine };
+    constexpr uint32_t NEG_INF = FMT == 16 ? 0xFFFFu : 0xFFFFFFFFu;
+    const int h = blockIdx.x, kvh = h / (H / HKV);
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const __half * kh = kc + (int64_t) kvh * D;
+    const __half * vh = vc + (int64_t) kvh * D;
+    for (int d = tid; d < D; d += nt) qc[d] = O.from(q[(int64_t) h * D + d]);
+    // kq: one chain over d per key, a tile of keys at a time
+    for (int64_t t0 = 0; t0 < nkv; t0 += ATTN_KT) {
+        const int64_t nk = nkv - t0 < ATTN_KT ? nkv - t0 : ATTN_KT;
+        __syncthreads();                                             // the previous tile's chains are done
+        for (int64_t i = tid; i < nk * D; i += nt) {
+            const int64_t kk = i / D, d = i - kk * D;
+            tile[d * KTP + kk] = O.from(__half2float(kh[(t0 + kk) * kv_ld + d]));
+        }
+        __syncthreads();
+        for (int64_t kk = tid; kk < nk; kk += nt) {
+            const int64_t k = t0 + kk;
+            uint32_t st = FMT == 16 && k_stochastic && D > 1
+                              ? lfsr_jump(T, seed, (unsigned long long) ((int64_t) h * nkv + k) * (unsigned long long) (D - 1)) : 0u;
+            uint32_t acc = O.start(O.mul(tile[kk], qc[0]));
+            for (int d = 1; d < D; d++) acc = O.step(acc, O.mul(tile[d * KTP + kk], qc[d]), st);
+            uint32_t v = O.from(O.to(O.finish(acc)));            // mul_mat F32 out -> soft_max F32 in
+            if (v != NEG_INF) v = O.mul(v, scale_l);
+            sv[k] = v;
+        }
+    }
+    __syncthreads();
+    // soft_max: row max, exp terms, the normaliser chain in key order, p
+    uint32_t mx = NEG_INF;
+    for (int64_t k = tid; k < nkv; k += nt) {
+        const uint32_t v = sv[k];
+        if (FMT == 16 ? gt16(v, mx) : gt32(v, mx)) mx = v;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const uint32_t o = __shfl_xor_sync(0xFFFFFFFFu, mx, off);
+        if (FMT == 16 ? gt16(o, mx) : gt32(o, mx)) mx = o;
+    }
+    if ((tid & 31) == 0) s_red[tid >> 5] = mx;
+    __syncthreads();
+    mx = s_red[0];
+    for (int w = 1; w < nt / 32; w++) if (FMT == 16 ? gt16(s_red[w], mx) : gt32(s_red[w], mx)) mx = s_red[w];
+    for (int64_t k = tid; k < nkv; k += nt) {
+        const uint32_t v = sv[k];
+        if constexpr (FMT == 16) sv[k] = __ldg(T.exp16 + sub16(v, mx, tab));
+        else                     sv[k] = exp32(T, sub32(T, v, mx));
+    }
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t acc;
+        if constexpr (FMT == 32) {
+            acc = sv[0];
+            for (int64_t k = 1; k < nkv; k++) acc = padd32f(F, acc, sv[k]);
+        } else if constexpr (NNCHAIN) {
+            red16 R{ &T, tab, fine };
+            acc = R.from(sv[0]);
+            for (int64_t k = 1; k < nkv; k++) acc = nn_add(F, tab, acc, sv[k]);
+            acc = R.finish(acc);
+        } else {
+            red16 R{ &T, tab, fine };
+            uint32_t st = k_stochastic && nkv > 1 ? lfsr_jump(T, seed, (unsigned long long) h * (unsigned long long) (nkv - 1)) : 0u;
+            acc = R.from(sv[0]);
+            for (int64_t k = 1; k < nkv; k++) acc = R.add(acc, sv[k], st);
+            acc = R.finish(acc);
+        }
+        s_tot = acc;
+    }
+    __syncthreads();
+    const uint32_t tot = s_tot;
+    for (int64_t k = tid; k < nkv; k += nt)             // soft_max F32 out -> to_lns for kqv
+        pc[k] = O.from(O.to(FMT == 16 ? div16(sv[k], tot) : div32(sv[k], tot)));
+    // kqv: one chain over the keys per d, continued across the tiles
+    uint32_t acc = 0u, st = 0u;
+    if (tid < D && FMT == 16 && k_stochastic && nkv > 1)
+        st = lfsr_jump(T, seed, (unsigned long long) ((int64_t) h * D + tid) * (unsigned long long) (nkv - 1));
+    for (int64_t t0 = 0; t0 < nkv; t0 += ATTN_KT) {
+        const int64_t nk = nkv - t0 < ATTN_KT ? nkv - t0 : ATTN_KT;
+        __syncthreads();
+        for (int64_t i = tid; i < nk * D; i += nt) {
+            const int64_t kk = i / D, d = i - kk * D;
+            tile[kk * D + d] = O.from(__half2float(vh[(t0 + kk) * kv_ld + d]));
+        }
+        __syncthreads();
+        if (tid < D) {
+            for (int64_t kk = 0; kk < nk; kk++) {
+                const uint32_t p = O.mul(tile[kk * D + tid], pc[t0 + kk]);
+                acc = t0 + kk == 0 ? O.start(p) : O.step(acc, p, st);
+            }
+        }
+    }
+    if (tid < D) out[(int64_t) h * D + tid] = O.to(O.finish(acc));
+}
+
 // ===================== elementwise ops of the model graph ===================
 //
 // F32 in and out, as at every ggml op boundary of the reference's backends
@@ -2565,6 +2734,50 @@ int lnsb_rope(int fmt, const lnsb_rope_args * a, lnsb_stream_t stream) {
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (fmt == LNSB_XLNS16) launch_k(k_rope<16>, grid_for(nrows * per, 256), 256, 0, s, *T, a->src, a->shape, a->cos_sin, a->n_dims, a->neox, a->dst);
     else                    launch_k(k_rope<32>, grid_for(nrows * per, 256), 256, 0, s, *T, a->src, a->shape, a->cos_sin, a->n_dims, a->neox, a->dst);
+    return launch_status();
+}
+
+int64_t lnsb_attn_decode_max_keys(int fmt, int head_dim) {
+    if (!valid_fmt(fmt) || head_dim <= 0) return 0;
+    const int64_t fixed = (fmt == LNSB_XLNS16 ? attn_tab<16>() : attn_tab<32>()) + 4 * ((int64_t) head_dim * (ATTN_KT + 2));
+    return fixed >= 220 * 1024 ? 0 : (220 * 1024 - fixed) / 8;
+}
+
+int lnsb_attn_decode(int fmt, const lnsb_attn_decode_args * a, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || a == nullptr) return LNSB_E_INVALID;
+    if (a->nkv <= 0 || a->n_head <= 0 || a->n_head_kv <= 0 || a->head_dim <= 0 || a->n_head % a->n_head_kv != 0 ||
+        a->kv_ld < (int64_t) a->n_head_kv * a->head_dim)
+        return LNSB_E_INVALID;
+    if (a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr || a->dst == nullptr) return LNSB_E_INVALID;
+    const int64_t bytes = (fmt == LNSB_XLNS16 ? attn_tab<16>() : attn_tab<32>()) +
+                          4 * ((int64_t) a->head_dim * (ATTN_KT + 2) + 2 * a->nkv);
+    if (a->nkv > lnsb_attn_decode_max_keys(fmt, a->head_dim) || a->n_head > 65535) return LNSB_E_TOO_LARGE;
+    int dev = 0;
+    const int ds = current_device(&dev);
+    if (ds != 0) return ds;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    uint32_t scale_l;
+    if (fmt == LNSB_XLNS16) {
+        const host_tables & H = get_host_tables(false, false);
+        uint32_t b;
+        std::memcpy(&b, &a->scale, 4);
+        scale_l = H.conv16[b >> 16];
+    } else {
+        scale_l = host_from_f32_32(a->scale);
+    }
+    static int attr[2][k_max_devices] = {};
+    auto kern = fmt == LNSB_XLNS16 ? k_attn_decode<16> : k_attn_decode<32>;
+    int & done = attr[fmt == LNSB_XLNS32][dev];
+    if (done < bytes) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        if (e != cudaSuccess) return (int) e;
+        done = 220 * 1024;
+    }
+    launch_k(kern, dim3((unsigned) a->n_head), dim3(256), (size_t) bytes, static_cast<cudaStream_t>(stream), *T, a->q,
+             reinterpret_cast<const __half *>(a->k_cache), reinterpret_cast<const __half *>(a->v_cache), a->kv_ld, a->nkv,
+             a->n_head, a->n_head_kv, a->head_dim, scale_l, a->dst, (uint32_t) a->monte_seed);
     return launch_status();
 }
 

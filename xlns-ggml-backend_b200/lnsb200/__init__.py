@@ -102,6 +102,17 @@ class KernelSet:
         a = self._mm_args(w, x, None, K, M, N, slices, monte_seed)
         _lib.check(self.lib, "lnsb_mul_mat_lns", self.lib.lnsb_mul_mat_lns(self.fmt, ctypes.byref(a), _ptr(dst), _stream(stream)))
 
+    def attn_decode(self, q, k_cache, v_cache, kv_ld, nkv, n_head, n_head_kv, head_dim, scale, dst, monte_seed=7,
+                    stream=None):
+        """one decode step's attention (lnsb_attn_decode): q F32 [n_head][head_dim], caches F16
+        [nkv][kv_ld], dst F32 [n_head][head_dim]"""
+        a = _lib.AttnDecodeArgs(_ptr(q), _ptr(k_cache), _ptr(v_cache), kv_ld, nkv, n_head, n_head_kv, head_dim, scale,
+                                _ptr(dst), monte_seed)
+        _lib.check(self.lib, "lnsb_attn_decode", self.lib.lnsb_attn_decode(self.fmt, ctypes.byref(a), _stream(stream)))
+
+    def attn_decode_max_keys(self, head_dim):
+        return self.lib.lnsb_attn_decode_max_keys(self.fmt, head_dim)
+
     def type_row_bytes(self, type, cols):
         return self.lib.lnsb_type_row_bytes(_lib.TYPES.get(type, type), cols)
 

@@ -37,6 +37,13 @@ class MulMatIdArgs(ctypes.Structure):
                 ("monte_seed", ctypes.c_uint16)]
 
 
+class AttnDecodeArgs(ctypes.Structure):
+    _fields_ = [("q", ctypes.c_void_p), ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+                ("kv_ld", ctypes.c_int64), ("nkv", ctypes.c_int64), ("n_head", ctypes.c_int), ("n_head_kv", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("scale", ctypes.c_float), ("dst", ctypes.c_void_p),
+                ("monte_seed", ctypes.c_uint16)]
+
+
 class SoftMaxArgs(ctypes.Structure):
     _fields_ = [("src", ctypes.c_void_p), ("src_shape", Shape4), ("mask", ctypes.c_void_p), ("mask_shape", Shape4),
                 ("scale", ctypes.c_float), ("dst", ctypes.c_void_p), ("work", ctypes.c_void_p),
@@ -90,6 +97,8 @@ SIGNATURES = [
     ("lnsb_unary", ctypes.c_int, [ctypes.c_int, ctypes.c_int, _VP, _VP, _I64, _VP]),
     ("lnsb_glu", ctypes.c_int, [ctypes.c_int, ctypes.c_int, _VP, _VP, _I64, _I64, _VP, _I64, _I64, _VP]),
     ("lnsb_rope", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(RopeArgs), _VP]),
+    ("lnsb_attn_decode", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(AttnDecodeArgs), _VP]),
+    ("lnsb_attn_decode_max_keys", _I64, [ctypes.c_int, ctypes.c_int]),
     ("lnsb_f32_to_f16", ctypes.c_int, [_VP, _VP, _I64, _VP]),
     ("lnsb_f16_to_f32", ctypes.c_int, [_VP, _VP, _I64, _VP]),
     ("lnsb_monte_get_state", ctypes.c_int, [ctypes.POINTER(ctypes.c_uint16)]),

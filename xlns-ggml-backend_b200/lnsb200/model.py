@@ -137,6 +137,7 @@ class GpuOps:
         self.kss = {mode: self.ks}
         self.weights = weights
         self.split_w = {}
+        self.fuse_attn = True           # decode steps (T = 1) through lnsb_attn_decode
         self.stream = stream
         self.dev = torch.device("cuda", torch.cuda.current_device())
         E = cfg["n_embd"]
@@ -258,6 +259,14 @@ class GpuOps:
     def attention(self, il, q, T, H, HKV, D, pos0):
         torch, ks = self.torch, self.ks
         nkv = pos0 + T
+        if T == 1 and self.fuse_attn and nkv <= ks.attn_decode_max_keys(D) and all(self.ks_for(op, n) is ks for op, n in (
+                ("MUL_MAT", "kq-%d" % il), ("SOFT_MAX", "kq_soft_max-%d" % il), ("MUL_MAT", "kqv-%d" % il))):
+            # one decode step: the fused kernel runs the same ops with the same conversions
+            o = self._f32(1, H * D)
+            ks.attn_decode(q, self.kc[il], self.vc[il], HKV * D, nkv, H, HKV, D, 1.0 / math.sqrt(D), o,
+                           stream=self.stream)
+            self.launches += 1
+            return o
         # K and V of the cache, F16 -> F32 -> xlns16 codes, laid out as mul_mat weights per kv head:
         # K: [h][dim][token] (reduce over dim), V: [h][token][dim] (reduce over tokens)
         kf = self._f32(nkv, HKV * D)
