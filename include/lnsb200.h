@@ -278,7 +278,8 @@ int lnsb_rope(int fmt, const lnsb_rope_args * args, lnsb_stream_t stream);
  *   q        F32 [n_head][head_dim]
  *   k_cache  F16 [nkv][kv_ld], kv head j at columns [j * head_dim, (j+1) * head_dim)
  *   v_cache  F16, same layout
- *   dst      F32 [n_head][head_dim]
+ *   dst      F32 [n_head][head_dim] (may be NULL when dst_lns is given)
+ *   dst_lns  optional: the codes of dst (to_lns of it, the next mat-vec's input)
  * LNSB_E_TOO_LARGE when nkv exceeds lnsb_attn_decode_max_keys (the
  * kernel's shared memory: about 5,700 keys at head_dim 64 beside the 101 KB
  * flat xlns32 image of sum32 and xlns32, about 19,000 in the other modes). */
@@ -291,9 +292,45 @@ typedef struct {
     float            scale;
     float *          dst;
     uint16_t         monte_seed;
+    void *           dst_lns;
 } lnsb_attn_decode_args;
 int lnsb_attn_decode(int fmt, const lnsb_attn_decode_args * args, lnsb_stream_t stream);
 int64_t lnsb_attn_decode_max_keys(int fmt, int head_dim);
+
+/* ---- The decode graph's other steps fused, each op boundary kept (the
+ * results are bit-identical to the ops run one by one):
+ * lnsb_norm_block: x = src (+ residual: the residual add), rms_norm(x), times
+ *   the norm weight (if given), to_lns -> dst_lns; x_out (if given) gets x (F32)
+ * lnsb_glu_lns: lnsb_glu followed by to_lns of its output
+ * lnsb_rope_qkv: from the q/k/v mat-vec's output rows [n_tokens][ld] (q heads,
+ *   k heads, v heads): rope of q (F32 -> q_out [n_tokens][n_head * head_dim])
+ *   and of k, k and v into the F16 caches (rows [n_tokens][kv_ld]); cos_sin
+ *   as lnsb_rope's, one position per token ---- */
+typedef struct {
+    const float * src;
+    const float * residual;
+    float *       x_out;
+    const float * weight;
+    void *        dst_lns;
+    int64_t       ncols, nrows;
+    float         eps;
+    uint16_t      monte_seed;
+} lnsb_norm_block_args;
+int lnsb_norm_block(int fmt, const lnsb_norm_block_args * args, lnsb_stream_t stream);
+int lnsb_glu_lns(int fmt, int op, const float * gate, const float * up, int64_t gate_stride, int64_t up_stride,
+                 void * dst_lns, int64_t ncols, int64_t nrows, lnsb_stream_t stream);
+typedef struct {
+    const float * qkv;
+    int64_t       ld;
+    const float * cos_sin;
+    int           n_dims, neox, n_head, n_head_kv, head_dim;
+    int64_t       n_tokens;
+    float *       q_out;
+    uint16_t *    k_cache;
+    uint16_t *    v_cache;
+    int64_t       kv_ld;
+} lnsb_rope_qkv_args;
+int lnsb_rope_qkv(int fmt, const lnsb_rope_qkv_args * args, lnsb_stream_t stream);
 
 /* F16 storage of F32 values (KV caches): IEEE binary16, round to nearest
  * even, and back (exact).  No LNS involved; not part of kernel_set. */

@@ -113,3 +113,23 @@ def test_small_model_mixed_policy_bit_exact(policy):
     lg, lo = model.forward(g, SMALL, [tg], 6), model.forward(o, SMALL, [tg], 6)
     assert np.array_equal(lg.cpu().numpy().ravel().view(np.uint32), lo.ravel().view(np.uint32))
     assert len(g.kss) > 1
+
+
+@pytest.mark.parametrize("fmt,mode", [(16, "base"), (16, "monte"), (16, "monte_bylpvip"), (16, "lpvip"), (16, "sum32"),
+                                      (32, "base")])
+def test_fused_step_matches_op_by_op(fmt, mode):
+    """GpuOps' fused forward (norm blocks, rope + KV store, fused attention,
+    glu + to_lns) against the op-by-op graph on the same GPU, prefill and two
+    decode steps, in every summation mode and xlns32"""
+    from lnsb200 import model
+    w = model.init_weights(SMALL, seed=2)
+    prompt = model.prompt_ids(SMALL, 5, seed=3)
+    a = model.GpuOps(SMALL, w, mode=mode, n_ctx=16, fmt=fmt)
+    b = model.GpuOps(SMALL, w, mode=mode, n_ctx=16, fmt=fmt)
+    b.fused, b.fuse_attn = False, False
+    la, lb = a.forward_fused(SMALL, prompt, 0), model.forward(b, SMALL, prompt, 0)   # the fused ops at T = 5 too
+    for pos in (5, 6):
+        assert np.array_equal(la.cpu().numpy().view(np.uint32), lb.cpu().numpy().view(np.uint32)), pos
+        t = a.argmax(la)
+        la, lb = model.forward(a, SMALL, [t], pos), model.forward(b, SMALL, [t], pos)
+    assert np.array_equal(la.cpu().numpy().view(np.uint32), lb.cpu().numpy().view(np.uint32))

@@ -1473,10 +1473,15 @@ __device__ __forceinline__ uint32_t nn_add(const int32_t * F, const int16_t * ta
     else                             return padd16(acc, t, tab);
 }
 
-template <int FMT, bool IO_F32>
-__global__ void __launch_bounds__(128)
+// FUSE: the decode graph's norm block in one kernel, each op boundary kept --
+// x = src (+ res: the residual add, F32 out), rms_norm(x) (F32 out), times the
+// norm weight nw (F32 out), to_lns -> dst codes; x_out (if given) gets x.
+template <int FMT, bool IO_F32, bool FUSE = false>
+__global__ void __launch_bounds__(256)
 k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst, int64_t ncols, int64_t nrows,
-           uint32_t eps_l, uint32_t inv_n, uint32_t monte_seed, int rpb, int nn_ok) {
+           uint32_t eps_l, uint32_t inv_n, uint32_t monte_seed, int rpb, int nn_ok,
+           const float * __restrict__ res = nullptr, float * __restrict__ x_out = nullptr,
+           const float * __restrict__ nw = nullptr) {
     pdl_entry();
     __shared__ __align__(16) int16_t tab[k16_tab_bytes16 / 2];
     __shared__ __align__(16) int16_t fine[k_mode == M_MONTE ? 2 * k16_monte_n : 8];
@@ -1487,20 +1492,39 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
     if constexpr (FMT == 16) norm_tables(T, tab, fine);
     const int64_t row0 = (int64_t) blockIdx.x * rpb;
     const int64_t nr = imin64(rpb, nrows - row0);
+    auto f2c = [&](float f) -> uint32_t { return FMT == 16 ? from_f32_16(T, f) : from_f32_32(T, f); };
+    auto c2f = [&](uint32_t c) -> float { return FMT == 16 ? to_f32_16(T, c) : to_f32_32(T, c); };
+    auto xval = [&](int64_t idx) -> float {              // x: src, or the residual add's F32 result
+        const float f = static_cast<const float *>(src)[idx];
+        if (!FUSE || res == nullptr) return f;
+        const uint32_t a = f2c(f), b = f2c(res[idx]);
+        return c2f(FMT == 16 ? add16(a, b, tab) : add32(T, a, b));
+    };
     auto load = [&](int64_t idx) -> uint32_t {
         if constexpr (IO_F32) {
-            const float f = static_cast<const float *>(src)[idx];
-            return FMT == 16 ? from_f32_16(T, f) : from_f32_32(T, f);
+            return f2c(xval(idx));
         } else {
             return FMT == 16 ? (uint32_t) static_cast<const uint16_t *>(src)[idx] : static_cast<const uint32_t *>(src)[idx];
         }
     };
     uint16_t * sq   = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
     uint32_t * sq32 = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
+    if (NN) nn_tables<FMT>(T, dyn);
+    if constexpr (FUSE) {                                // the residual add reads the packed table
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+    }
     if (NN) {
-        nn_tables<FMT>(T, dyn);
         for (int64_t e = threadIdx.x; e < nr * ncols; e += blockDim.x) {
-            const uint32_t v = load(row0 * ncols + e);
+            uint32_t v;
+            if (FUSE && x_out != nullptr) {              // x once: the scaling pass reads it back
+                const float xf = xval(row0 * ncols + e);
+                x_out[row0 * ncols + e] = xf;
+                v = f2c(xf);
+            } else {
+                v = load(row0 * ncols + e);
+            }
             if constexpr (FMT == 16) sq[e] = (uint16_t) mul16(v, v);
             else                     sq32[e] = mul32(v, v);
         }
@@ -1548,6 +1572,24 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
         const int64_t r = e / ncols;
         const int64_t idx = (row0 + r) * ncols + (e - r * ncols);
         const uint32_t inv = s_inv[r];
+        if constexpr (FUSE) {
+            float xf;
+            if (x_out != nullptr && NN) {
+                xf = x_out[idx];                         // written by the squares pass (same block)
+            } else {
+                xf = xval(idx);
+                if (x_out != nullptr) x_out[idx] = xf;
+            }
+            const uint32_t v = f2c(xf);
+            float yf = c2f(FMT == 16 ? mul16(v, inv) : mul32(v, inv));
+            if (nw != nullptr) {
+                const uint32_t yc = f2c(yf), wc = f2c(nw[e - r * ncols]);
+                yf = c2f(FMT == 16 ? mul16(yc, wc) : mul32(yc, wc));
+            }
+            if constexpr (FMT == 16) static_cast<uint16_t *>(dst)[idx] = (uint16_t) f2c(yf);
+            else                     static_cast<uint32_t *>(dst)[idx] = f2c(yf);
+            continue;
+        }
         const uint32_t v = load(idx);
         if constexpr (FMT == 16) {
             const uint32_t y = mul16(v, inv);
@@ -1756,7 +1798,7 @@ template <int FMT>
 __global__ void __launch_bounds__(256)
 k_attn_decode(dev_tables T, const float * __restrict__ q, const __half * __restrict__ kc, const __half * __restrict__ vc,
               int64_t kv_ld, int64_t nkv, int H, int HKV, int D, uint32_t scale_l, float * __restrict__ out,
-              uint32_t seed) {
+              uint32_t seed, void * __restrict__ out_lns) {
     extern __shared__ __align__(16) unsigned char attn_sm[];
     constexpr int TAB = attn_tab<FMT>();
     constexpr int KTP = ATTN_KT + 1;                                // [d][k] rows, padded
@@ -1869,7 +1911,14 @@ k_attn_decode(dev_tables T, const float * __restrict__ q, const __half * __restr
             }
         }
     }
-    if (tid < D) out[(int64_t) h * D + tid] = O.to(O.finish(acc));
+    if (tid < D) {
+        const float y = O.to(O.finish(acc));
+        if (out != nullptr) out[(int64_t) h * D + tid] = y;
+        if (out_lns != nullptr) {                        // to_lns of the output (the wo mat-vec's input)
+            if constexpr (FMT == 16) static_cast<uint16_t *>(out_lns)[(int64_t) h * D + tid] = (uint16_t) O.from(y);
+            else                     static_cast<uint32_t *>(out_lns)[(int64_t) h * D + tid] = O.from(y);
+        }
+    }
 }
 
 // ===================== elementwise ops of the model graph ===================
@@ -1954,15 +2003,64 @@ __global__ void k_unary(dev_tables T, const float * __restrict__ src, float * __
     }
 }
 
-template <int FMT>
+// OUT_LNS: the glu op's F32 result converted again (to_lns of the next mul_mat)
+template <int FMT, bool OUT_LNS = false>
 __global__ void k_swiglu(dev_tables T, const float * __restrict__ gate, const float * __restrict__ up, int64_t gs,
-                         int64_t us, float * __restrict__ dst, int64_t nc, int64_t nr) {
+                         int64_t us, void * __restrict__ dst, int64_t nc, int64_t nr) {
     pdl_entry();
     using A = ew<FMT>;
     LNSB_GRID_STRIDE(i, nc * nr) {
         const int64_t r = i / nc, c = i - r * nc;
         const uint32_t g = A::from(T, gate[r * gs + c]), u = A::from(T, up[r * us + c]);
-        dst[i] = A::to(T, A::mul(FMT == 16 ? silu16(T, g) : silu32(T, g), u));
+        const float y = A::to(T, A::mul(FMT == 16 ? silu16(T, g) : silu32(T, g), u));
+        if constexpr (!OUT_LNS)    static_cast<float *>(dst)[i] = y;
+        else if constexpr (FMT == 16) static_cast<uint16_t *>(dst)[i] = (uint16_t) A::from(T, y);
+        else                          static_cast<uint32_t *>(dst)[i] = A::from(T, y);
+    }
+}
+
+// the decode graph's step after the q/k/v mat-vec, one kernel: rope of the q
+// and k heads (F32 out, as lnsb_rope), k and v into the F16 caches (as
+// lnsb_f32_to_f16).  qkv rows [T][ld]: q heads, then k heads, then v heads.
+template <int FMT>
+__global__ void k_rope_qkv(dev_tables T, const float * __restrict__ qkv, int64_t ld, const float * __restrict__ cos_sin,
+                           int n_dims, int neox, int H, int HKV, int D, int64_t nt, float * __restrict__ q_out,
+                           __half * __restrict__ kc, __half * __restrict__ vc, int64_t kv_ld) {
+    pdl_entry();
+    using A = ew<FMT>;
+    const int64_t half = n_dims / 2, per = half + (D - n_dims);
+    const int64_t nrope = nt * (H + HKV) * per, nv = nt * (int64_t) HKV * D;
+    LNSB_GRID_STRIDE(i, nrope + nv) {
+        if (i >= nrope) {                                    // v -> F16 cache
+            const int64_t e = i - nrope, t = e / ((int64_t) HKV * D), c = e - t * HKV * D;
+            vc[t * kv_ld + c] = __float2half_rn(qkv[t * ld + (int64_t) (H + HKV) * D + c]);
+            continue;
+        }
+        const int64_t row = i / per, j = i - row * per;      // row = t * (H + HKV) + head
+        const int64_t t = row / (H + HKV), hd = row - t * (H + HKV);
+        const float * x = qkv + t * ld + hd * D;
+        float y0, y1 = 0.0f;
+        int64_t a0, a1 = -1;
+        if (j < half) {
+            a0 = neox ? j : 2 * j;
+            a1 = neox ? j + half : 2 * j + 1;
+            const uint32_t c = A::from(T, cos_sin[(t * half + j) * 2]), sn = A::from(T, cos_sin[(t * half + j) * 2 + 1]);
+            const uint32_t x0 = A::from(T, x[a0]), x1 = A::from(T, x[a1]);
+            y0 = A::to(T, A::sub(T, A::mul(x0, c), A::mul(x1, sn)));
+            y1 = A::to(T, A::add(T, A::mul(x0, sn), A::mul(x1, c)));
+        } else {
+            a0 = n_dims + (j - half);
+            y0 = A::to(T, A::from(T, x[a0]));
+        }
+        if (hd < H) {
+            float * y = q_out + t * (int64_t) H * D + hd * D;
+            y[a0] = y0;
+            if (a1 >= 0) y[a1] = y1;
+        } else {
+            __half * y = kc + t * kv_ld + (hd - H) * D;
+            y[a0] = __float2half_rn(y0);
+            if (a1 >= 0) y[a1] = __float2half_rn(y1);
+        }
     }
 }
 
@@ -2209,7 +2307,8 @@ int nn_smem_attr(const void * kern, int bytes) {
 }
 
 int rms_norm_impl(int fmt, const void * src, void * dst, int64_t ncols, int64_t nrows, float eps, uint16_t seed,
-                  bool io_f32, cudaStream_t stream) {
+                  bool io_f32, cudaStream_t stream, bool fuse = false, const float * res = nullptr,
+                  float * x_out = nullptr, const float * nw = nullptr) {
     if (!valid_fmt(fmt) || ncols < 0 || nrows < 0) return LNSB_E_INVALID;
     if (nrows == 0 || ncols == 0) return 0;
     if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
@@ -2239,12 +2338,20 @@ int rms_norm_impl(int fmt, const void * src, void * dst, int64_t ncols, int64_t 
             dsmem = tabb + (int) (((int64_t) rpb * ncols * tb + 15) / 16 * 16);
         }
     }
+    // the fused block does more per element (the residual add, the weight, two
+    // conversions): rows over more blocks, 256 threads each
+    if (fuse) rpb = (int) imin64(rpb, imin64(32, (nrows + 2 * 148 - 1) / (2 * 148)));
+    if (rpb < 1) rpb = 1;
+    if (fuse && nn_ok) dsmem = (fmt == LNSB_XLNS32 ? nn_tab<32>() : nn_tab<16>()) +
+                               (int) (((int64_t) rpb * ncols * (fmt == LNSB_XLNS32 ? 4 : 2) + 15) / 16 * 16);
     const unsigned blocks = (unsigned) ((nrows + rpb - 1) / rpb);
-    auto kern = fmt == LNSB_XLNS16 ? (io_f32 ? k_rms_norm<16, true> : k_rms_norm<16, false>)
-                                   : (io_f32 ? k_rms_norm<32, true> : k_rms_norm<32, false>);
+    auto kern = fuse ? (fmt == LNSB_XLNS16 ? k_rms_norm<16, true, true> : k_rms_norm<32, true, true>)
+                     : fmt == LNSB_XLNS16 ? (io_f32 ? k_rms_norm<16, true> : k_rms_norm<16, false>)
+                                          : (io_f32 ? k_rms_norm<32, true> : k_rms_norm<32, false>);
     const int st2 = nn_smem_attr((const void *) kern, dsmem);
     if (st2 != 0) return st2;
-    launch_k(kern, blocks, 128, dsmem, stream, *T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, nn_ok);
+    launch_k(kern, blocks, fuse ? 256 : 128, dsmem, stream, *T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, nn_ok, res,
+             x_out, nw);
     return launch_status();
 }
 
@@ -2629,6 +2736,12 @@ int lnsb_rms_norm_lns(int fmt, const void * src, void * dst, int64_t ncols, int6
     return rms_norm_impl(fmt, src, dst, ncols, nrows, eps, monte_seed, false, static_cast<cudaStream_t>(stream));
 }
 
+int lnsb_norm_block(int fmt, const lnsb_norm_block_args * a, lnsb_stream_t stream) {
+    if (a == nullptr || a->src == nullptr || a->dst_lns == nullptr) return LNSB_E_INVALID;
+    return rms_norm_impl(fmt, a->src, a->dst_lns, a->ncols, a->nrows, a->eps, a->monte_seed, true,
+                         static_cast<cudaStream_t>(stream), true, a->residual, a->x_out, a->weight);
+}
+
 namespace {
 bool shape_ok(const int64_t ne[4]) {
     if (ne == nullptr) return false;
@@ -2721,6 +2834,44 @@ int lnsb_glu(int fmt, int op, const float * gate, const float * up, int64_t gate
     return launch_status();
 }
 
+int lnsb_glu_lns(int fmt, int op, const float * gate, const float * up, int64_t gate_stride, int64_t up_stride,
+                 void * dst_lns, int64_t ncols, int64_t nrows, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || (op != LNSB_GLU_SWIGLU && op != LNSB_GLU_GEGLU) || ncols < 0 || nrows < 0) return LNSB_E_INVALID;
+    if (op != LNSB_GLU_SWIGLU) return LNSB_E_UNSUPPORTED;
+    if (ncols == 0 || nrows == 0) return 0;
+    if (gate == nullptr || up == nullptr || dst_lns == nullptr || gate_stride < ncols || up_stride < ncols) return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const unsigned g = grid_for(ncols * nrows, 256);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (fmt == LNSB_XLNS16) launch_k(k_swiglu<16, true>, g, 256, 0, s, *T, gate, up, gate_stride, up_stride, dst_lns, ncols, nrows);
+    else                    launch_k(k_swiglu<32, true>, g, 256, 0, s, *T, gate, up, gate_stride, up_stride, dst_lns, ncols, nrows);
+    return launch_status();
+}
+
+int lnsb_rope_qkv(int fmt, const lnsb_rope_qkv_args * a, lnsb_stream_t stream) {
+    if (!valid_fmt(fmt) || a == nullptr) return LNSB_E_INVALID;
+    if (a->n_tokens < 0 || a->n_head <= 0 || a->n_head_kv <= 0 || a->head_dim <= 0 || a->n_dims < 0 ||
+        a->n_dims > a->head_dim || a->n_dims % 2 != 0 || a->ld < (int64_t) (a->n_head + 2 * a->n_head_kv) * a->head_dim ||
+        a->kv_ld < (int64_t) a->n_head_kv * a->head_dim)
+        return LNSB_E_INVALID;
+    if (a->n_tokens == 0) return 0;
+    if (a->qkv == nullptr || a->cos_sin == nullptr || a->q_out == nullptr || a->k_cache == nullptr || a->v_cache == nullptr)
+        return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(fmt, &T);
+    if (st != 0) return st;
+    const int64_t per = a->n_dims / 2 + (a->head_dim - a->n_dims);
+    const int64_t n = a->n_tokens * ((int64_t) (a->n_head + a->n_head_kv) * per + (int64_t) a->n_head_kv * a->head_dim);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    auto kern = fmt == LNSB_XLNS16 ? k_rope_qkv<16> : k_rope_qkv<32>;
+    launch_k(kern, grid_for(n, 256), 256, 0, s, *T, a->qkv, a->ld, a->cos_sin, a->n_dims, a->neox, a->n_head, a->n_head_kv,
+             a->head_dim, a->n_tokens, a->q_out, reinterpret_cast<__half *>(a->k_cache), reinterpret_cast<__half *>(a->v_cache),
+             a->kv_ld);
+    return launch_status();
+}
+
 int lnsb_rope(int fmt, const lnsb_rope_args * a, lnsb_stream_t stream) {
     if (!valid_fmt(fmt) || a == nullptr || !shape_ok(a->shape.ne)) return LNSB_E_INVALID;
     if (a->n_dims <= 0 || a->n_dims % 2 != 0 || a->n_dims > a->shape.ne[0]) return LNSB_E_INVALID;
@@ -2748,7 +2899,8 @@ int lnsb_attn_decode(int fmt, const lnsb_attn_decode_args * a, lnsb_stream_t str
     if (a->nkv <= 0 || a->n_head <= 0 || a->n_head_kv <= 0 || a->head_dim <= 0 || a->n_head % a->n_head_kv != 0 ||
         a->kv_ld < (int64_t) a->n_head_kv * a->head_dim)
         return LNSB_E_INVALID;
-    if (a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr || a->dst == nullptr) return LNSB_E_INVALID;
+    if (a->q == nullptr || a->k_cache == nullptr || a->v_cache == nullptr || (a->dst == nullptr && a->dst_lns == nullptr))
+        return LNSB_E_INVALID;
     const int64_t bytes = (fmt == LNSB_XLNS16 ? attn_tab<16>() : attn_tab<32>()) +
                           4 * ((int64_t) a->head_dim * (ATTN_KT + 2) + 2 * a->nkv);
     if (a->nkv > lnsb_attn_decode_max_keys(fmt, a->head_dim) || a->n_head > 65535) return LNSB_E_TOO_LARGE;
@@ -2777,7 +2929,7 @@ int lnsb_attn_decode(int fmt, const lnsb_attn_decode_args * a, lnsb_stream_t str
     }
     launch_k(kern, dim3((unsigned) a->n_head), dim3(256), (size_t) bytes, static_cast<cudaStream_t>(stream), *T, a->q,
              reinterpret_cast<const __half *>(a->k_cache), reinterpret_cast<const __half *>(a->v_cache), a->kv_ld, a->nkv,
-             a->n_head, a->n_head_kv, a->head_dim, scale_l, a->dst, (uint32_t) a->monte_seed);
+             a->n_head, a->n_head_kv, a->head_dim, scale_l, a->dst, (uint32_t) a->monte_seed, a->dst_lns);
     return launch_status();
 }
 

@@ -103,12 +103,32 @@ class KernelSet:
         _lib.check(self.lib, "lnsb_mul_mat_lns", self.lib.lnsb_mul_mat_lns(self.fmt, ctypes.byref(a), _ptr(dst), _stream(stream)))
 
     def attn_decode(self, q, k_cache, v_cache, kv_ld, nkv, n_head, n_head_kv, head_dim, scale, dst, monte_seed=7,
-                    stream=None):
+                    stream=None, dst_lns=None):
         """one decode step's attention (lnsb_attn_decode): q F32 [n_head][head_dim], caches F16
-        [nkv][kv_ld], dst F32 [n_head][head_dim]"""
+        [nkv][kv_ld], dst F32 [n_head][head_dim] (or None), dst_lns its codes (optional)"""
         a = _lib.AttnDecodeArgs(_ptr(q), _ptr(k_cache), _ptr(v_cache), kv_ld, nkv, n_head, n_head_kv, head_dim, scale,
-                                _ptr(dst), monte_seed)
+                                _ptr(dst) if dst is not None else None, monte_seed,
+                                _ptr(dst_lns) if dst_lns is not None else None)
         _lib.check(self.lib, "lnsb_attn_decode", self.lib.lnsb_attn_decode(self.fmt, ctypes.byref(a), _stream(stream)))
+
+    def norm_block(self, src, dst_lns, ncols, nrows, eps, residual=None, x_out=None, weight=None, monte_seed=7,
+                   stream=None):
+        """lnsb_norm_block: [residual add,] rms_norm, [times weight,] to_lns"""
+        opt = lambda t: _ptr(t) if t is not None else None
+        a = _lib.NormBlockArgs(_ptr(src), opt(residual), opt(x_out), opt(weight), _ptr(dst_lns), ncols, nrows, eps,
+                               monte_seed)
+        _lib.check(self.lib, "lnsb_norm_block", self.lib.lnsb_norm_block(self.fmt, ctypes.byref(a), _stream(stream)))
+
+    def glu_lns(self, gate, up, gate_stride, up_stride, dst_lns, ncols, nrows, op="swiglu", stream=None):
+        _lib.check(self.lib, "lnsb_glu_lns", self.lib.lnsb_glu_lns(self.fmt, 0 if op == "swiglu" else 1, _ptr(gate),
+                                                                   _ptr(up), gate_stride, up_stride, _ptr(dst_lns),
+                                                                   ncols, nrows, _stream(stream)))
+
+    def rope_qkv(self, qkv, ld, cos_sin, n_dims, n_head, n_head_kv, head_dim, n_tokens, q_out, k_cache, v_cache, kv_ld,
+                 neox=False, stream=None):
+        a = _lib.RopeQkvArgs(_ptr(qkv), ld, _ptr(cos_sin), n_dims, 1 if neox else 0, n_head, n_head_kv, head_dim,
+                             n_tokens, _ptr(q_out), _ptr(k_cache), _ptr(v_cache), kv_ld)
+        _lib.check(self.lib, "lnsb_rope_qkv", self.lib.lnsb_rope_qkv(self.fmt, ctypes.byref(a), _stream(stream)))
 
     def attn_decode_max_keys(self, head_dim):
         return self.lib.lnsb_attn_decode_max_keys(self.fmt, head_dim)

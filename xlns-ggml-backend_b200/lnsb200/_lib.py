@@ -41,7 +41,20 @@ class AttnDecodeArgs(ctypes.Structure):
     _fields_ = [("q", ctypes.c_void_p), ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
                 ("kv_ld", ctypes.c_int64), ("nkv", ctypes.c_int64), ("n_head", ctypes.c_int), ("n_head_kv", ctypes.c_int),
                 ("head_dim", ctypes.c_int), ("scale", ctypes.c_float), ("dst", ctypes.c_void_p),
-                ("monte_seed", ctypes.c_uint16)]
+                ("monte_seed", ctypes.c_uint16), ("dst_lns", ctypes.c_void_p)]
+
+
+class NormBlockArgs(ctypes.Structure):
+    _fields_ = [("src", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("x_out", ctypes.c_void_p),
+                ("weight", ctypes.c_void_p), ("dst_lns", ctypes.c_void_p), ("ncols", ctypes.c_int64),
+                ("nrows", ctypes.c_int64), ("eps", ctypes.c_float), ("monte_seed", ctypes.c_uint16)]
+
+
+class RopeQkvArgs(ctypes.Structure):
+    _fields_ = [("qkv", ctypes.c_void_p), ("ld", ctypes.c_int64), ("cos_sin", ctypes.c_void_p), ("n_dims", ctypes.c_int),
+                ("neox", ctypes.c_int), ("n_head", ctypes.c_int), ("n_head_kv", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("n_tokens", ctypes.c_int64), ("q_out", ctypes.c_void_p), ("k_cache", ctypes.c_void_p),
+                ("v_cache", ctypes.c_void_p), ("kv_ld", ctypes.c_int64)]
 
 
 class SoftMaxArgs(ctypes.Structure):
@@ -99,6 +112,9 @@ SIGNATURES = [
     ("lnsb_rope", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(RopeArgs), _VP]),
     ("lnsb_attn_decode", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(AttnDecodeArgs), _VP]),
     ("lnsb_attn_decode_max_keys", _I64, [ctypes.c_int, ctypes.c_int]),
+    ("lnsb_norm_block", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(NormBlockArgs), _VP]),
+    ("lnsb_glu_lns", ctypes.c_int, [ctypes.c_int, ctypes.c_int, _VP, _VP, _I64, _I64, _VP, _I64, _I64, _VP]),
+    ("lnsb_rope_qkv", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(RopeQkvArgs), _VP]),
     ("lnsb_f32_to_f16", ctypes.c_int, [_VP, _VP, _I64, _VP]),
     ("lnsb_f16_to_f32", ctypes.c_int, [_VP, _VP, _I64, _VP]),
     ("lnsb_monte_get_state", ctypes.c_int, [ctypes.POINTER(ctypes.c_uint16)]),

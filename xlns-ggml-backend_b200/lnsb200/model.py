@@ -85,6 +85,8 @@ def rope_table(n_ctx, n_dims, base):
 def forward(ops, cfg, ids, pos0):
     """logits (F32, [vocab]) of the last of `ids`, which sit at positions
     pos0 .. pos0 + len(ids) - 1; the KV cache holds positions < pos0."""
+    if getattr(ops, "fused", False) and (ids.numel() if hasattr(ids, "numel") else len(ids)) == 1:
+        return ops.forward_fused(cfg, ids, pos0)            # a decode step: the fused ops
     T, E = (ids.numel() if hasattr(ids, "numel") else len(ids)), cfg["n_embd"]
     H, HKV, D = cfg["n_head"], cfg["n_head_kv"], cfg["head_dim"]
     x = ops.embed(ids)                                              # [T][E]
@@ -138,6 +140,9 @@ class GpuOps:
         self.weights = weights
         self.split_w = {}
         self.fuse_attn = True           # decode steps (T = 1) through lnsb_attn_decode
+        # the whole step through the fused ops (norm block, rope + KV store, attention,
+        # glu + to_lns) when one summation mode serves every op
+        self.fused = self.policy is None
         self.stream = stream
         self.dev = torch.device("cuda", torch.cuda.current_device())
         E = cfg["n_embd"]
@@ -312,6 +317,59 @@ class GpuOps:
 
     def argmax(self, logits):
         return int(self.torch.argmax(logits.view(-1)).item())
+
+    def _codes(self, *shape):
+        return self.torch.empty(shape, dtype=self.cdt, device=self.dev)
+
+    def _mv(self, wt, xc, N):
+        codes, K, M = wt
+        out = self._f32(N, M)
+        self.ks.mul_mat(codes, xc, out, K, M, N, stream=self.stream)
+        return out
+
+    def forward_fused(self, cfg, ids, pos0):
+        """forward() with the fused steps: per layer a norm block (residual add,
+        rms_norm, weight, to_lns), the q/k/v mat-vec, rope + KV store, the
+        attention (fused for a decode step), wo, a norm block, up/gate, glu +
+        to_lns, down -- nine launches, the same bits as the op-by-op graph"""
+        ks, torch = self.ks, self.torch
+        T = ids.numel() if hasattr(ids, "numel") else len(ids)
+        E, H, HKV, D, F = cfg["n_embd"], cfg["n_head"], cfg["n_head_kv"], cfg["head_dim"], cfg["n_ff"]
+        eps, kvd, nkv, s = cfg["eps"], HKV * D, pos0 + T, self.stream
+        x = self.embed(ids)                                          # [T][E]
+        res = None                                                   # the pending residual add (a, x)
+        for il in range(cfg["n_layer"]):
+            lw = self.lw[il]
+            hc = self._codes(T * E)
+            if res is None:
+                ks.norm_block(x, hc, E, T, eps, weight=lw["attn_norm"], stream=s)
+            else:
+                xn = self._f32(T, E)
+                ks.norm_block(res[0], hc, E, T, eps, residual=res[1], x_out=xn, weight=lw["attn_norm"], stream=s)
+                x = xn
+            qkv = self._mv(lw["qkv"], hc, T)                         # [T][(H + 2 HKV) D]
+            q = self._f32(T, H * D)
+            ks.rope_qkv(qkv, (H + 2 * HKV) * D, self.rope_cs[pos0:pos0 + T], D, H, HKV, D, T, q,
+                        self.kc[il][pos0:pos0 + T], self.vc[il][pos0:pos0 + T], kvd, stream=s)
+            ac = self._codes(T * H * D)
+            if T == 1 and self.fuse_attn and nkv <= ks.attn_decode_max_keys(D):
+                ks.attn_decode(q, self.kc[il], self.vc[il], kvd, nkv, H, HKV, D, 1.0 / math.sqrt(D), None,
+                               stream=s, dst_lns=ac)
+            else:
+                ks.to_lns(self.attention(il, q, T, H, HKV, D, pos0), ac, stream=s)
+            wo = self._mv(lw["wo"], ac, T)
+            hc = self._codes(T * E)
+            xn = self._f32(T, E)
+            ks.norm_block(wo, hc, E, T, eps, residual=x, x_out=xn, weight=lw["ffn_norm"], stream=s)
+            x = xn
+            ug = self._mv(lw["upgate"], hc, T)                       # [T][up | gate]
+            sc = self._codes(T * F)
+            ks.glu_lns(ug[:, F:], ug, 2 * F, 2 * F, sc, F, T, stream=s)
+            res = (self._mv(lw["w_down"], sc, T), x)
+        hc = self._codes(E)
+        ks.norm_block(res[0][T - 1:], hc, E, 1, eps, residual=res[1][T - 1:], weight=self.gw["output_norm"], stream=s)
+        self.launches += 9 * cfg["n_layer"] + 2
+        return self._mv(self.gw["output"], hc, 1)                    # [1][vocab]
 
 
 class GraphDecoder:
