@@ -366,6 +366,9 @@ def run_ours(args, wl):
     if world == 1 and args.workload == "configs1":
         # BASELINE's metric is quoted at K=1536: configs[0], timed the same way, beside the main line
         line["k1536"] = time_secondary(lib, lnsb200, torch, np, WORKLOADS["configs0"], args, flush, stream)
+        # the rows beside the path: MUL_MAT_ID and the typed weight decode
+        line["mul_mat_id"] = time_mul_mat_id(lnsb200, torch, np, args, flush, stream, int_peak)
+        line["weights"] = time_weights(lnsb200, torch, np, args, flush, stream, hbm)
     if args.workload == "configs1" and not args.no_decode:
         # the metric's second half: model decode tok/s, one sequence per GPU
         line["decode"] = run_decode(torch, dist, rank, world, args, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
@@ -416,6 +419,77 @@ def time_secondary(lib, lnsb200, torch, np, wl, args, flush, stream):
             "value": adds / (ms / 1000) / 1e9, "unit": UNIT,
             "bound": "chain latency: %d dependent additions per output" % (K - 1),
             "l2": "flushed (256 MB write) before every timed step"}
+
+
+def time_mul_mat_id(lnsb200, torch, np, args, flush, stream, int_peak):
+    """MUL_MAT_ID on a mixture-of-experts FFN shape (8 experts of 1536 x 576,
+    128 tokens, 2 experts per token; synthetic N(0,0.02) / N(0,1) codes, seed
+    4), device-timed, L2 flushed before every step; roofline as the main
+    line's (integer issue at the mode's c_mode)."""
+    n_exp, K, M, n_tok, n_used = 8, 576, 1536, 128, 2
+    ks = lnsb200.KernelSet(16, args.mode)
+    rng = np.random.default_rng(4)
+    w = torch.empty(n_exp * K * M, dtype=torch.int16, device="cuda")
+    for e in range(n_exp):
+        wf = torch.from_numpy(rng.normal(0, 0.02, (M, K)).astype(np.float32)).cuda()
+        ks.to_lns_transposed(wf, w[e * K * M:(e + 1) * K * M], M, K, M)
+    xf = torch.from_numpy(rng.normal(0, 1, (n_tok, K)).astype(np.float32)).cuda()
+    x = torch.empty(n_tok * K, dtype=torch.int16, device="cuda")
+    ks.to_lns(xf, x)
+    ids = torch.from_numpy(rng.integers(0, n_exp, (n_tok, n_used)).astype(np.int32)).cuda()
+    out = torch.empty(n_tok * n_used * M, dtype=torch.int16, device="cuda")
+    for _ in range(max(3, args.warmup)):
+        ks.mul_mat_id_lns(w, x, ids, out, K, M, n_exp, 1, n_used, n_tok, stream=stream)
+    torch.cuda.synchronize()
+    steps = max(args.steps, 10)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        ks.mul_mat_id_lns(w, x, ids, out, K, M, n_exp, 1, n_used, n_tok, stream=stream)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(b.elapsed_time(e) for b, e in ev) / steps
+    adds = n_tok * n_used * M * (K - 1)
+    val = adds / (ms / 1000) / 1e9
+    return {"workload": "MUL_MAT_ID: 8 experts of 1536x576, 128 tokens x 2 experts (synthetic, seed 4)",
+            "mode": args.mode, "steps": steps, "ms_per_step": ms, "value": val, "unit": UNIT,
+            "roofline": {"bound": "int", "achieved": val, "peak": int_peak, "frac": val / int_peak, "unit": UNIT},
+            "l2": "flushed (256 MB write) before every timed step"}
+
+
+def time_weights(lnsb200, torch, np, args, flush, stream, hbm):
+    """Weights in ggml storage types decoded on the device into the k-major LNS
+    image (lnsb_to_lns_transposed_typed), 8192 x 4096 per type; algorithmic
+    bytes = the packed rows read + the codes written; bound HBM."""
+    ks = lnsb200.KernelSet(16, args.mode)
+    rows, cols = 8192, 4096
+    rng = np.random.default_rng(5)
+    out = {}
+    dst = torch.empty(rows * cols, dtype=torch.int16, device="cuda")
+    for t in ("f16", "q8_0", "q4_k", "q6_k"):
+        rb = ks.type_row_bytes(t, cols)
+        raw = torch.from_numpy(rng.integers(0, 256, (rows, rb), dtype=np.uint8)).cuda()
+        if t == "f16":
+            raw = torch.from_numpy(rng.normal(0, 0.05, (rows, cols)).astype(np.float16).view(np.uint8)).cuda()
+        for _ in range(3):
+            ks.to_lns_transposed_typed(t, raw, dst, rows, cols, rows, stream=stream)
+        torch.cuda.synchronize()
+        n = 10
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i in range(n):
+            flush.zero_()
+            ev[i][0].record(stream)
+            ks.to_lns_transposed_typed(t, raw, dst, rows, cols, rows, stream=stream)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        ms = sum(b.elapsed_time(e) for b, e in ev) / n
+        by = rows * rb + rows * cols * 2
+        out[t] = {"ms": ms, "gbs": by / (ms / 1000) / 1e9, "frac_hbm": by / (ms / 1000) / 1e9 / hbm,
+                  "bytes": by}
+    return {"workload": "8192 x 4096 weight -> xlns16 k-major image, per storage type", "bound": "hbm",
+            "peak_gbs": hbm, "types": out,
+            "l2": "flushed (256 MB write) before every timed launch", "launches_per_type": 10}
 
 
 def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16):

@@ -231,18 +231,23 @@ __global__ void k_to_lns_transposed_typed(dev_tables T, int type, const unsigned
     pdl_entry();
     using V = typename std::conditional<FMT == 16, uint16_t, uint32_t>::type;
     __shared__ V tile[32][33];
-    const int64_t r0 = (int64_t) blockIdx.y * 32, c0 = (int64_t) blockIdx.x * 32;
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int64_t r = r0 + i, c = c0 + threadIdx.x;
-        if (r < rows && c < cols) {
-            const float f = dequant_at(type, src + r * row_bytes, c);
-            tile[i][threadIdx.x] = FMT == 16 ? (V) from_f32_16(T, f) : (V) from_f32_32(T, f);
+    // persistent over the 32 x 32 tiles (a grid of a few per SM, not one CTA per tile)
+    const int64_t tc = (cols + 31) / 32, ntiles = tc * ((rows + 31) / 32);
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const int64_t r0 = (t / tc) * 32, c0 = (t % tc) * 32;
+        for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+            const int64_t r = r0 + i, c = c0 + threadIdx.x;
+            if (r < rows && c < cols) {
+                const float f = dequant_at(type, src + r * row_bytes, c);
+                tile[i][threadIdx.x] = FMT == 16 ? (V) from_f32_16(T, f) : (V) from_f32_32(T, f);
+            }
         }
-    }
-    __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int64_t c = c0 + i, r = r0 + threadIdx.x;
-        if (r < rows && c < cols) static_cast<V *>(dst)[c * dst_ld + r] = tile[threadIdx.x][i];
+        __syncthreads();
+        for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+            const int64_t c = c0 + i, r = r0 + threadIdx.x;
+            if (r < rows && c < cols) static_cast<V *>(dst)[c * dst_ld + r] = tile[threadIdx.x][i];
+        }
+        __syncthreads();                                 // the tile is reused
     }
 }
 
@@ -2610,7 +2615,11 @@ int lnsb_to_lns_transposed_typed(int fmt, int type, const void * src, void * dst
     const dev_tables * T = nullptr;
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
-    const dim3 grid((unsigned) ((cols + 31) / 32), (unsigned) ((rows + 31) / 32));
+    int dev = 0;
+    const int ds = current_device(&dev);
+    if (ds != 0) return ds;
+    const int64_t ntiles = ((cols + 31) / 32) * ((rows + 31) / 32);
+    const dim3 grid((unsigned) imin64(ntiles, (int64_t) sm_count(dev) * 16));
     const dim3 block(32, 8);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const auto * p = static_cast<const unsigned char *>(src);
