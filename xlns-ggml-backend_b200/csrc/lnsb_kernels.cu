@@ -185,6 +185,8 @@ __device__ __forceinline__ void q4k_scale_min(int j, const unsigned char * q, in
         m  = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
     }
 }
+template <int TYPE>
+__device__ __forceinline__ float dequant_at_t(const unsigned char * __restrict__ row, int64_t c);
 __device__ __forceinline__ float dequant_at(int type, const unsigned char * __restrict__ row, int64_t c) {
     switch (type) {
         case LNSB_TYPE_F32:  return reinterpret_cast<const float *>(row)[c];
@@ -222,9 +224,21 @@ __device__ __forceinline__ float dequant_at(int type, const unsigned char * __re
         default: return 0.0f;
     }
 }
+template <int TYPE>
+__device__ __forceinline__ float dequant_at_t(const unsigned char * __restrict__ row, int64_t c) {
+    if constexpr (TYPE == LNSB_TYPE_F32) {
+        return reinterpret_cast<const float *>(row)[c];
+    } else if constexpr (TYPE == LNSB_TYPE_F16) {
+        return __half2float(reinterpret_cast<const __half *>(row)[c]);          // rows are 2-byte aligned
+    } else if constexpr (TYPE == LNSB_TYPE_BF16) {
+        return __uint_as_float((uint32_t) reinterpret_cast<const uint16_t *>(row)[c] << 16);
+    } else {
+        return dequant_at(TYPE, row, c);
+    }
+}
 
 // dst[c * dst_ld + r] = lns(dequant(row r)[c]); rows `row_bytes` apart
-template <int FMT>
+template <int FMT, int TYPE>
 __global__ void k_to_lns_transposed_typed(dev_tables T, int type, const unsigned char * __restrict__ src,
                                           int64_t row_bytes, void * __restrict__ dst, int64_t rows, int64_t cols,
                                           int64_t dst_ld) {
@@ -238,7 +252,7 @@ __global__ void k_to_lns_transposed_typed(dev_tables T, int type, const unsigned
         for (int i = threadIdx.y; i < 32; i += blockDim.y) {
             const int64_t r = r0 + i, c = c0 + threadIdx.x;
             if (r < rows && c < cols) {
-                const float f = dequant_at(type, src + r * row_bytes, c);
+                const float f = dequant_at_t<TYPE>(src + r * row_bytes, c);
                 tile[i][threadIdx.x] = FMT == 16 ? (V) from_f32_16(T, f) : (V) from_f32_32(T, f);
             }
         }
@@ -2623,8 +2637,19 @@ int lnsb_to_lns_transposed_typed(int fmt, int type, const void * src, void * dst
     const dim3 block(32, 8);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const auto * p = static_cast<const unsigned char *>(src);
-    if (fmt == LNSB_XLNS16) launch_k(k_to_lns_transposed_typed<16>, grid, block, 0, s, *T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
-    else                    launch_k(k_to_lns_transposed_typed<32>, grid, block, 0, s, *T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
+    auto go = [&](auto k16, auto k32) {
+        if (fmt == LNSB_XLNS16) launch_k(k16, grid, block, 0, s, *T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
+        else                    launch_k(k32, grid, block, 0, s, *T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
+    };
+    switch (type) {
+        case LNSB_TYPE_F32:  go(k_to_lns_transposed_typed<16, LNSB_TYPE_F32>, k_to_lns_transposed_typed<32, LNSB_TYPE_F32>); break;
+        case LNSB_TYPE_F16:  go(k_to_lns_transposed_typed<16, LNSB_TYPE_F16>, k_to_lns_transposed_typed<32, LNSB_TYPE_F16>); break;
+        case LNSB_TYPE_BF16: go(k_to_lns_transposed_typed<16, LNSB_TYPE_BF16>, k_to_lns_transposed_typed<32, LNSB_TYPE_BF16>); break;
+        case LNSB_TYPE_Q8_0: go(k_to_lns_transposed_typed<16, LNSB_TYPE_Q8_0>, k_to_lns_transposed_typed<32, LNSB_TYPE_Q8_0>); break;
+        case LNSB_TYPE_Q4_0: go(k_to_lns_transposed_typed<16, LNSB_TYPE_Q4_0>, k_to_lns_transposed_typed<32, LNSB_TYPE_Q4_0>); break;
+        case LNSB_TYPE_Q4_K: go(k_to_lns_transposed_typed<16, LNSB_TYPE_Q4_K>, k_to_lns_transposed_typed<32, LNSB_TYPE_Q4_K>); break;
+        default:             go(k_to_lns_transposed_typed<16, LNSB_TYPE_Q6_K>, k_to_lns_transposed_typed<32, LNSB_TYPE_Q6_K>); break;
+    }
     return launch_status();
 }
 
