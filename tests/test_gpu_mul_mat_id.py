@@ -92,3 +92,14 @@ def test_mul_mat_id_invalid(ks16):
     with pytest.raises(lnsb200.LnsbError):                 # n_used % ne11 != 0
         ks16.mul_mat_id_lns(z, z, ids, z, 4, 4, 1, 3, 2, 2)
     assert ks16.mul_mat_id_draws(10, 4, 2, 3) == (3 * 2 * 4 * 9 if ks16.mode in ("monte", "monte_bylpvip") else 0)
+
+
+def test_mul_mat_id_k0_and_empty(orc, ks16):
+    """K = 0 gives the zero code (the oracle's empty chain); no tokens is a no-op"""
+    z = torch.zeros(64, dtype=torch.int16, device="cuda")
+    ids = torch.zeros(4, dtype=torch.int32, device="cuda")
+    out = torch.full((2 * 2 * 8,), 0x1234, dtype=torch.int16, device="cuda")
+    ks16.mul_mat_id_lns(z, z, ids, out, 0, 8, 1, 1, 2, 2)
+    torch.cuda.synchronize()
+    assert (out.cpu().numpy() == 0).all()
+    ks16.mul_mat_id_lns(z, z, ids, out, 4, 8, 1, 1, 2, 0)     # n_tokens = 0

@@ -74,3 +74,15 @@ def test_model_policy_reaches_the_ops():
     assert not np.array_equal(base, _logits("MUL_MAT:kqv-*=sum32"))
     assert not np.array_equal(base, _logits("RMS_NORM=lpvip"))
     assert np.array_equal(base, _logits("MUL_MAT:nothing-*=sum32"))
+
+
+def test_op_bisection():
+    from lnsb200.policy import op_disabled
+    assert not op_disabled("MUL_MAT", "ffn_down-3", env={})
+    assert op_disabled("MUL_MAT", "ffn_down-3", env={"LNS_DISABLE_OPS": "MUL_MAT,ffn_down"})
+    assert op_disabled("ADD", "ffn_down-3", env={"LNS_DISABLE_OPS": "ffn_down"})          # substring of the name
+    assert not op_disabled("ADD", "ffn_out-3", env={"LNS_DISABLE_OPS": "ffn_down"})
+    assert op_disabled("SOFT_MAX", "kq_soft_max-0", env={"LNS_ENABLE_OPS": "MUL_MAT"})  # only matching ops run in LNS
+    assert not op_disabled("MUL_MAT", "kq-0", env={"LNS_ENABLE_OPS": "MUL_MAT"})
+    assert op_disabled("MUL_MAT", "kq-0", env={"LNS_ENABLE_OPS": ""})                   # set but empty: none
+    assert op_disabled("MUL_MAT", "kq-0", env={"LNS_ENABLE_OPS": "MUL_MAT", "LNS_DISABLE_OPS": "kq-*"})

@@ -86,3 +86,16 @@ class SumPolicy:
 
     def modes(self):
         return sorted({self.default} | {m for _, m in self.rules})
+
+
+def op_disabled(op, name, src1_name=None, env=None):
+    """LNS_DISABLE_OPS / LNS_ENABLE_OPS op bisection (lns-backend/common/
+    lns-backend-config.h:186-199): with LNS_ENABLE_OPS set, an op runs in LNS
+    only if a token of it matches (set but empty: no op does); an op matching
+    a token of LNS_DISABLE_OPS falls back.  Same token syntax as the sum
+    policy's selectors.  True means "not in LNS"."""
+    env = os.environ if env is None else env
+    if "LNS_ENABLE_OPS" in env:
+        if not any(op_matches(t, op, name, src1_name) for t in split_list(env["LNS_ENABLE_OPS"])):
+            return True
+    return any(op_matches(t, op, name, src1_name) for t in split_list(env.get("LNS_DISABLE_OPS", "")))
