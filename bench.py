@@ -251,15 +251,66 @@ def run_ours(args, wl):
     mm = lib.lnsb_mul_mat_lns
     status = [0]
 
+    # N > 1, weak scaling: the all-gather of the output-row shards fused into
+    # the mul_mat's store over NVLink peer memory (a symmetric-memory buffer
+    # on every GPU, plain stores), then a device-side barrier; NCCL's
+    # all-gather where the fused store does not apply
+    gather = "nccl all_gather_into_tensor + permute"
+    peer = None
+    if world > 1 and not strong and args.mode in ("base", "monte"):
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+            gbuf = symm_mem.empty(N * M * world, dtype=torch.int16, device="cuda")
+            hdl = symm_mem.rendezvous(gbuf, dist.group.WORLD)
+            fbuf = symm_mem.empty(world, dtype=torch.int32, device="cuda")
+            fbuf.zero_()
+            fhdl = symm_mem.rendezvous(fbuf, dist.group.WORLD)
+            berr = torch.zeros(1, dtype=torch.int32, device="cuda")
+            torch.cuda.synchronize()
+            dist.barrier()
+            peer = lnsb200._lib.PeerOut(hdl.buffer_ptrs_dev, world, M * world, rank * M)
+            peer_p = ctypes.byref(peer)
+            mmp = lib.lnsb_mul_mat_lns_peers
+            epoch = [0]
+            gather = "fused into the mul_mat store: peer-memory stores over NVLink + a bounded peer-flag barrier"
+        except Exception as e:                                     # noqa: BLE001
+            peer = None
+            gather = "nccl all_gather_into_tensor + permute (symmetric memory unavailable: %s)" % str(e).splitlines()[0][:120]
+
     def launch():
-        st = mm(16, mm_argp, out_p, stream_p)
+        st = mmp(16, mm_argp, peer_p, stream_p) if peer is not None else mm(16, mm_argp, out_p, stream_p)
         if st != 0:
             status[0] = st
+
+    def gather_step():
+        if peer is not None:
+            epoch[0] += 1
+            st = lib.lnsb_group_barrier(ctypes.c_void_p(fhdl.buffer_ptrs_dev), world, rank, epoch[0],
+                                        ctypes.c_void_p(berr.data_ptr()), stream_p)
+            if st != 0:
+                status[0] = st
+        else:
+            shard.all_gather_rows(out.view(N, M), world).contiguous()
 
     def step():
         launch()
         if world > 1:
-            shard.all_gather_rows(out.view(N, M), world).contiguous()
+            gather_step()
+
+    if peer is not None:
+        # the fused gather must give what NCCL's does, bit for bit
+        gbuf.fill_(-1)
+        torch.cuda.synchronize()
+        dist.barrier()
+        launch()
+        gather_step()
+        mm(16, mm_argp, out_p, stream_p)
+        want = shard.all_gather_rows(out.view(N, M), world).contiguous().view(-1)
+        torch.cuda.synchronize()
+        if berr.item() != 0:
+            raise SystemExit("peer barrier timed out")
+        if not torch.equal(gbuf, want):
+            raise SystemExit("fused peer all-gather differs from the NCCL all-gather")
 
     for _ in range(args.warmup):
         flush.zero_()
@@ -286,7 +337,7 @@ def run_ours(args, wl):
         launch()
         ev[i][1].record(stream)
         if world > 1:
-            shard.all_gather_rows(out.view(N, M), world).contiguous()    # ggml [N][M*world] order
+            gather_step()                  # ggml [N][M*world] order on every GPU
         ev[i][2].record(stream)
     torch.cuda.synchronize()
     if dist:
@@ -294,6 +345,8 @@ def run_ours(args, wl):
     clocks = sampler.stop()
     if status[0] != 0:
         raise lnsb200.LnsbError(lib, "lnsb_mul_mat_lns", status[0])
+    if peer is not None and berr.item() != 0:
+        raise SystemExit("peer barrier timed out")
     step_ms = sum(a.elapsed_time(c) for a, b, c in ev)
     kern_ms = sum(a.elapsed_time(b) for a, b, c in ev)
     if dist:
@@ -350,8 +403,8 @@ def run_ours(args, wl):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": step_ms / args.steps, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
         "dtype": "u16 (xlns16 codes; integer LNS arithmetic)", "data": "synthetic",
-        "config": {"workload": wl["desc"] + ((" per rank" if not strong else "") + ", output rows sharded + NCCL all_gather" if world > 1 else ""),
-                   "K": K, "M": M, "N": N, "mode": args.mode, "parallelism": "rowshard%d" % world,
+        "config": {"workload": wl["desc"] + ((" per rank" if not strong else "") + ", output rows sharded + all-gather (config.gather)" if world > 1 else ""),
+                   "K": K, "M": M, "N": N, "mode": args.mode, "parallelism": "rowshard%d" % world, "gather": gather if world > 1 else None,
                    "l2": "flushed (256 MB write) before every timed step"},
         "roofline": {"bound": "int", "achieved": achieved, "peak": int_peak, "unit": UNIT, "frac": achieved / int_peak,
                      "traffic": traffic_of(pkey), "traffic_source": PROFILE.get(pkey),

@@ -160,6 +160,27 @@ int lnsb_mul_mat(int fmt, const lnsb_mul_mat_args * args, lnsb_stream_t stream);
  * lns-ops.cpp:374-379. */
 int lnsb_mul_mat_lns(int fmt, const lnsb_mul_mat_args * args, void * dst_lns, lnsb_stream_t stream);
 
+/* mul_mat with the all-gather of output-row shards fused into the store (no
+ * counterpart in the reference): the caller owns rows [offset, offset + M)
+ * of a [slices][N][ld] codes result that lives on every GPU of the group; the
+ * kernel stores each code into all `n` peer buffers (device pointers valid in
+ * this process, e.g. a symmetric-memory allocation's buffer_ptrs_dev, own
+ * buffer included) over NVLink, plain stores.  The caller synchronises the
+ * group (a barrier) before reading.  xlns16 base / monte builds (the tiled
+ * kernel, whatever the size); otherwise LNSB_E_UNSUPPORTED. */
+typedef struct {
+    void * const * ptrs;       /* device array of n buffer pointers */
+    int            n;
+    int64_t        ld, offset;
+} lnsb_peer_out;
+int lnsb_mul_mat_lns_peers(int fmt, const lnsb_mul_mat_args * args, const lnsb_peer_out * peers, lnsb_stream_t stream);
+/* the barrier to follow it: flags is a device array of `world` pointers to
+ * each GPU's int32[world] flag array (zeroed once; peer memory), epoch counts
+ * the calls from 1.  Each GPU signals every peer and waits for every peer's
+ * signal of this epoch; a wait that runs past about two seconds sets *err
+ * (device memory) to 1 and returns instead of hanging. */
+int lnsb_group_barrier(int32_t * const * flags, int world, int rank, int32_t epoch, int32_t * err, lnsb_stream_t stream);
+
 /* kernel_set::soft_max (lns-cuda-kernels.h:136) */
 int lnsb_soft_max(int fmt, const lnsb_soft_max_args * args, lnsb_stream_t stream);
 /* codes in, codes out: src [ne3][ne2][ne1][ne0], mask (may be NULL) codes

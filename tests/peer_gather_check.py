@@ -1,0 +1,64 @@
+"""Helper run by tests/test_gpu_peer_gather.py under torchrun (one process per
+GPU): lnsb_mul_mat_lns_peers + lnsb_group_barrier against NCCL's all-gather
+of the same output-row shards, bit for bit; exit status 0 = equal."""
+import ctypes
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "xlns-ggml-backend_b200"))
+
+
+def main():
+    import datetime
+    import lnsb200
+    from lnsb200 import shard
+    import torch.distributed._symmetric_memory as symm_mem
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60))
+    mode = sys.argv[1] if len(sys.argv) > 1 else "base"
+    ks = lnsb200.KernelSet(16, mode)
+    ks.upload_tables()
+    K, M, N = 256, 640, 96                                 # per rank: 640 rows (10 tiles) x 96 tokens
+    rng = np.random.default_rng(7 + rank)
+    wf = torch.from_numpy(rng.normal(0, 0.02, (M, K)).astype(np.float32)).cuda()
+    xf = torch.from_numpy(np.random.default_rng(1).normal(0, 1, (N, K)).astype(np.float32)).cuda()
+    w = torch.empty(K * M, dtype=torch.int16, device="cuda")
+    x = torch.empty(N * K, dtype=torch.int16, device="cuda")
+    ks.to_lns_transposed(wf, w, M, K, M)
+    ks.to_lns(xf, x)
+    out = torch.empty(N * M, dtype=torch.int16, device="cuda")
+    ks.mul_mat_lns(w, x, out, K, M, N)
+    want = shard.all_gather_rows(out.view(N, M), world).contiguous().view(-1)
+    gbuf = symm_mem.empty(N * M * world, dtype=torch.int16, device="cuda")
+    gbuf.fill_(-1)
+    hdl = symm_mem.rendezvous(gbuf, dist.group.WORLD)
+    fbuf = symm_mem.empty(world, dtype=torch.int32, device="cuda")
+    fbuf.zero_()
+    fhdl = symm_mem.rendezvous(fbuf, dist.group.WORLD)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    dist.barrier()
+    ok = True
+    for epoch in (1, 2):
+        ks.mul_mat_lns_peers(w, x, hdl.buffer_ptrs_dev, world, M * world, rank * M, K, M, N)
+        st = ks.lib.lnsb_group_barrier(ctypes.c_void_p(fhdl.buffer_ptrs_dev), world, rank, epoch,
+                                       ctypes.c_void_p(err.data_ptr()), None)
+        torch.cuda.synchronize()
+        good = st == 0 and err.item() == 0 and torch.equal(gbuf, want)
+        if not good:
+            print("rank %d epoch %d: status %d, barrier error %d, equal %s" % (rank, epoch, st, err.item(),
+                                                                              torch.equal(gbuf, want)), flush=True)
+        ok = ok and good
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if ok else 1)
+
+
+if __name__ == "__main__":
+    main()

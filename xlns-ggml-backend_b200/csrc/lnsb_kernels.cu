@@ -420,11 +420,20 @@ __device__ __forceinline__ uint32_t code_of_key(int key) {
 }
 __device__ __forceinline__ int key_of_code(uint32_t c) { return key_of_code_w(c); }
 
+// the all-gather of output-row shards fused into the store: every code goes
+// to each peer's buffer (peer memory over NVLink, plain stores) at
+// [z][n][off + m] with rows of ld codes; n == 0: the local dst as usual
+struct peer_out_dev {
+    uint16_t * const * ptrs;     // device array of n buffer pointers
+    int                n;
+    int64_t            ld, off;
+};
+
 template <bool OUT_F32>
 __global__ void __launch_bounds__(FB_THREADS, FB_MONTE ? 2 : 4)
 k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
                  void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
-                 int64_t r2, int64_t r3, uint32_t monte_seed, int vec) {
+                 int64_t r2, int64_t r3, uint32_t monte_seed, int vec, peer_out_dev peers) {
     pdl_entry();
     extern __shared__ __align__(16) unsigned char smem[];
     int *      wkeys = reinterpret_cast<int *>(smem + FB_OFF_WKEY);
@@ -610,6 +619,31 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
         __syncthreads();
     }
 
+    if (!OUT_F32 && peers.n > 0) {
+        // 4 consecutive rows per thread and token: one 8-byte store per peer
+        // (16 threads cover a token's 64 rows: 128 contiguous bytes)
+#pragma unroll
+        for (int j = 0; j < FB_TN; j++) {
+            const int64_t n = n0 + tn + 8 * j;
+            if (n >= N) continue;
+            uint32_t v[FB_TM];
+#pragma unroll
+            for (int i = 0; i < FB_TM; i++) v[i] = K == 0 ? 0u : (fast ? code_of_key(akey[i][j]) : acc[i][j]);
+            const int64_t o = (z * N + n) * peers.ld + peers.off + m0 + mloc;
+            const bool whole = m0 + mloc + FB_TM <= M && (o & 3) == 0;
+            for (int p = 0; p < peers.n; p++) {
+                uint16_t * d = peers.ptrs[p];
+                if (whole) {
+                    *reinterpret_cast<uint2 *>(d + o) = make_uint2(v[0] | (v[1] << 16), v[2] | (v[3] << 16));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < FB_TM; i++)
+                        if (m0 + mloc + i < M) d[o + i] = (uint16_t) v[i];
+                }
+            }
+        }
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < FB_TM; i++) {
         const int64_t m = m0 + mloc + i;
@@ -1940,6 +1974,29 @@ k_attn_decode(dev_tables T, const float * __restrict__ q, const __half * __restr
     }
 }
 
+// ===================== group barrier over peer memory ========================
+// After lnsb_mul_mat_lns_peers: thread p stores the epoch into peer p's flag
+// slot for this rank (system-scope release; the kernel starts after the
+// mul_mat has completed, pdl_entry) and waits for peer p's store into this
+// rank's slot p (system-scope acquire).  The wait is bounded: past `limit`
+// polls it records an error and returns, so a missing peer cannot hang the GPU.
+__global__ void k_group_barrier(int32_t * const * __restrict__ flags, int world, int rank, int32_t epoch,
+                                int32_t * __restrict__ err, long long limit) {
+    pdl_entry();
+    const int p = threadIdx.x;
+    if (p >= world) return;
+    int32_t * peer = flags[p] + rank;
+    asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(peer), "r"(epoch) : "memory");
+    const int32_t * mine = flags[rank] + p;
+    int32_t v = 0;
+    for (long long it = 0; it < limit; it++) {
+        asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(mine) : "memory");
+        if (v >= epoch) return;
+        __nanosleep(100);
+    }
+    atomicExch(err, 1);
+}
+
 // ===================== elementwise ops of the model graph ===================
 //
 // F32 in and out, as at every ggml op boundary of the reference's backends
@@ -2221,21 +2278,25 @@ int mul_mat_id_impl(int fmt, const lnsb_mul_mat_id_args * a, void * dst, bool ou
     return out_f32 ? go(k_mul_mat_id<32, true>, mmid_smem<32>(), w, x) : go(k_mul_mat_id<32, false>, mmid_smem<32>(), w, x);
 }
 
-int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32, cudaStream_t stream) {
+int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32, cudaStream_t stream,
+                 const peer_out_dev * peers = nullptr) {
     if (!valid_fmt(fmt) || a == nullptr) return LNSB_E_INVALID;
     if (a->K < 0 || a->M < 0 || a->N < 0 || a->ne02 <= 0 || a->ne03 <= 0 || a->ne12 <= 0 || a->ne13 <= 0) return LNSB_E_INVALID;
     if (a->ne12 % a->ne02 != 0 || a->ne13 % a->ne03 != 0) return LNSB_E_INVALID;
     if (a->M == 0 || a->N == 0) return 0;
-    if (dst == nullptr || (a->K > 0 && (a->w == nullptr || a->x == nullptr))) return LNSB_E_INVALID;
+    if ((dst == nullptr && peers == nullptr) || (a->K > 0 && (a->w == nullptr || a->x == nullptr))) return LNSB_E_INVALID;
     if (a->ne12 * a->ne13 > 65535) return LNSB_E_TOO_LARGE;
     const dev_tables * T = nullptr;
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
     const int64_t r2 = a->ne12 / a->ne02, r3 = a->ne13 / a->ne03;
     const int64_t tiles = ((a->M + FB_BM - 1) / FB_BM) * ((a->N + FB_BN - 1) / FB_BN) * a->ne12 * a->ne13;
+    const peer_out_dev no_peers{ nullptr, 0, 0, 0 };
+    if (peers != nullptr && !(fmt == LNSB_XLNS16 && (k_mode == M_BASE || k_mode == M_MONTE)))
+        return LNSB_E_UNSUPPORTED;                       // the gather is fused into the tiled kernel (any size) only
     int lr_tnc = (int) (a->N < 4 ? a->N : 4);
     while (lr_tnc > 1 && lr_smem(a->K, lr_tnc) > LR_SMEM_MAX) lr_tnc--;
-    if (fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && lr_smem(a->K, lr_tnc) <= LR_SMEM_MAX &&
+    if (peers == nullptr && fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && lr_smem(a->K, lr_tnc) <= LR_SMEM_MAX &&
         a->K <= (int64_t) LR_SEG * LR_MAXSEG && (a->N + lr_tnc - 1) / lr_tnc <= 65535) {
         // few outputs, weight slices resident in shared memory
         const dim3 grid((unsigned) ((a->M + 31) / 32), (unsigned) ((a->N + lr_tnc - 1) / lr_tnc), (unsigned) (a->ne12 * a->ne13));
@@ -2253,7 +2314,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         }
         launch_k(kern, grid, 32 * lr_tnc, smem, stream, *T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
                                                   dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, vec ? 1 : 0);
-    } else if (fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && a->K <= LT_MAX_K && a->N <= 65535) {
+    } else if (peers == nullptr && fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && a->K <= LT_MAX_K && a->N <= 65535) {
         // few outputs: latency form, two tokens per thread where they fit
 #ifndef LNSB_LT_TN2
 #define LNSB_LT_TN2 1
@@ -2297,7 +2358,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         }
         launch_k(kern, grid, FB_THREADS, FB_SMEM, stream, *T, static_cast<const uint16_t *>(a->w),
                                                     static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
-                                                    a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0);
+                                                    a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0, peers ? *peers : no_peers);
     } else if (fmt == LNSB_XLNS32 || k_mode == M_SUM32 || k_mode == M_LPVIP || k_mode == M_MONTE_BYLPVIP) {
         return mul_mat_a32(fmt, *T, a, dst, out_f32, r2, r3, stream);
     } else {
@@ -2684,6 +2745,22 @@ int lnsb_mul_mat(int fmt, const lnsb_mul_mat_args * args, lnsb_stream_t stream) 
 
 int lnsb_mul_mat_lns(int fmt, const lnsb_mul_mat_args * args, void * dst_lns, lnsb_stream_t stream) {
     return mul_mat_impl(fmt, args, dst_lns, false, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_mul_mat_lns_peers(int fmt, const lnsb_mul_mat_args * args, const lnsb_peer_out * peers, lnsb_stream_t stream) {
+    if (peers == nullptr || peers->ptrs == nullptr || peers->n <= 0 || peers->offset < 0 || args == nullptr ||
+        peers->ld < peers->offset + args->M)
+        return LNSB_E_INVALID;
+    const peer_out_dev p{ reinterpret_cast<uint16_t * const *>(peers->ptrs), peers->n, peers->ld, peers->offset };
+    return mul_mat_impl(fmt, args, nullptr, false, static_cast<cudaStream_t>(stream), &p);
+}
+
+int lnsb_group_barrier(int32_t * const * flags, int world, int rank, int32_t epoch, int32_t * err, lnsb_stream_t stream) {
+    if (flags == nullptr || err == nullptr || world <= 0 || world > 1024 || rank < 0 || rank >= world || epoch <= 0)
+        return LNSB_E_INVALID;
+    launch_k(k_group_barrier, dim3(1), dim3((unsigned) ((world + 31) / 32 * 32)), 0, static_cast<cudaStream_t>(stream),
+             flags, world, rank, epoch, err, (long long) 1 << 21);
+    return launch_status();
 }
 
 int lnsb_mul_mat_id(int fmt, const lnsb_mul_mat_id_args * args, lnsb_stream_t stream) {

@@ -146,6 +146,16 @@ class KernelSet:
         _lib.check(self.lib, "lnsb_dequantize",
                    self.lib.lnsb_dequantize(_lib.TYPES.get(type, type), _ptr(src), _ptr(dst), rows, cols, _stream(stream)))
 
+    def mul_mat_lns_peers(self, w, x, ptrs_dev, n_peers, ld, offset, K, M, N, slices=(1, 1, 1, 1), monte_seed=7,
+                          stream=None):
+        """mul_mat with the output-row all-gather fused into the store: codes
+        into every peer buffer (ptrs_dev: device address of an array of
+        n_peers pointers) at [N][ld] columns [offset, offset + M)"""
+        a = self._mm_args(w, x, None, K, M, N, slices, monte_seed)
+        p = _lib.PeerOut(ptrs_dev, n_peers, ld, offset)
+        _lib.check(self.lib, "lnsb_mul_mat_lns_peers",
+                   self.lib.lnsb_mul_mat_lns_peers(self.fmt, ctypes.byref(a), ctypes.byref(p), _stream(stream)))
+
     def _mmid_args(self, w, x, ids, dst, K, M, n_expert, ne11, n_used, n_tokens, monte_seed):
         return _lib.MulMatIdArgs(w.data_ptr(), x.data_ptr(), ids.data_ptr(), dst.data_ptr() if dst is not None else None,
                                  K, M, n_expert, ne11, n_used, n_tokens, n_used, monte_seed)

@@ -57,6 +57,10 @@ class RopeQkvArgs(ctypes.Structure):
                 ("v_cache", ctypes.c_void_p), ("kv_ld", ctypes.c_int64)]
 
 
+class PeerOut(ctypes.Structure):
+    _fields_ = [("ptrs", ctypes.c_void_p), ("n", ctypes.c_int), ("ld", ctypes.c_int64), ("offset", ctypes.c_int64)]
+
+
 class SoftMaxArgs(ctypes.Structure):
     _fields_ = [("src", ctypes.c_void_p), ("src_shape", Shape4), ("mask", ctypes.c_void_p), ("mask_shape", Shape4),
                 ("scale", ctypes.c_float), ("dst", ctypes.c_void_p), ("work", ctypes.c_void_p),
@@ -93,6 +97,8 @@ SIGNATURES = [
     ("lnsb_weight_cache_stats", ctypes.c_int, [_VP, ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
     ("lnsb_mul_mat", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), _VP]),
     ("lnsb_mul_mat_lns", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), _VP, _VP]),
+    ("lnsb_mul_mat_lns_peers", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), ctypes.POINTER(PeerOut), _VP]),
+    ("lnsb_group_barrier", ctypes.c_int, [_VP, ctypes.c_int, ctypes.c_int, ctypes.c_int32, _VP, _VP]),
     ("lnsb_mul_mat_id", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatIdArgs), _VP]),
     ("lnsb_mul_mat_id_lns", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatIdArgs), _VP, _VP]),
     ("lnsb_mul_mat_id_draws", ctypes.c_uint64, [ctypes.c_int, ctypes.POINTER(MulMatIdArgs)]),
