@@ -22,3 +22,29 @@ def test_peer_gather_two_gpus(mode):
            os.path.join(here, "peer_gather_check.py"), mode]
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def test_group_barrier_times_out_without_a_peer():
+    """the peer-flag barrier's wait is bounded: with a peer that never signals
+    (two flag arrays on this GPU, rank 1 never runs) the call returns and sets
+    the error word instead of hanging"""
+    import ctypes
+    import time
+    import lnsb200
+    ks = lnsb200.KernelSet(16, "base")
+    f0 = torch.zeros(2, dtype=torch.int32, device="cuda")
+    f1 = torch.zeros(2, dtype=torch.int32, device="cuda")
+    ptrs = torch.tensor([f0.data_ptr(), f1.data_ptr()], dtype=torch.int64, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    t0 = time.time()
+    st = ks.lib.lnsb_group_barrier(ctypes.c_void_p(ptrs.data_ptr()), 2, 0, 1, ctypes.c_void_p(err.data_ptr()), None)
+    torch.cuda.synchronize()
+    assert st == 0 and err.item() == 1
+    assert f1.cpu().tolist() == [1, 0]                    # rank 0's signal reached "peer" 1's slot
+    assert time.time() - t0 < 30
+    # with both signals present the barrier passes
+    f0.fill_(2)
+    err.zero_()
+    st = ks.lib.lnsb_group_barrier(ctypes.c_void_p(ptrs.data_ptr()), 2, 0, 2, ctypes.c_void_p(err.data_ptr()), None)
+    torch.cuda.synchronize()
+    assert st == 0 and err.item() == 0
