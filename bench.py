@@ -413,7 +413,7 @@ def run_ours(args, wl):
                      "hbm": {"achieved_gbs": bytes_alg / kern_s / 1e9, "peak_gbs": hbm, "frac": bytes_alg / kern_s / 1e9 / hbm,
                              "algorithmic_bytes": bytes_alg}},
         "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": N * K * 4, "d2h_bytes_per_step": N * M * 4},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if peer is not None else 1),   # mul_mat (+ the peer barrier)
         "clocks": clocks,
     }
     if world == 1 and args.workload == "configs1":
