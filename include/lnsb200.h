@@ -192,9 +192,9 @@ int lnsb_soft_max_lns(int fmt, const void * src, const int64_t ne[4], const void
                       uint16_t monte_seed, lnsb_stream_t stream);
 
 /* Allocation-free variant of lnsb_soft_max_lns.  No counterpart in the
- * reference: it is for callers that must not call cudaMalloc (code running
- * inside a CUDA-graph capture, a host allocator that owns all device memory,
- * a latency-critical loop that may not hit the driver's allocator).  The
+ * reference: it is for callers that must not call cudaMalloc (a host framework
+ * whose own pool owns all device memory, a latency-critical loop that may not
+ * take the driver allocator's implicit synchronisation).  The
  * per-element scratch the normaliser needs lives in one static device array
  * of LNSB_NOALLOC_SCRATCH_BYTES built into this library, so
  * nelements(src) * value_size must not exceed that (else LNSB_E_TOO_LARGE).

@@ -1,8 +1,9 @@
 """lnsb_soft_max_lns_noalloc: the allocation-free softmax entry point.
 
-Some callers cannot call cudaMalloc at the point where they run the op --
-inside a CUDA-graph capture, under a host framework that owns every device
-allocation, or in a latency-critical loop.  This entry point takes the
+Some callers cannot call cudaMalloc at the point where they run the op:
+a host framework whose own pool owns every device allocation, or a
+latency-critical loop that may not take the allocator's implicit
+synchronisation.  This entry point takes the
 softmax scratch from a static device array compiled into the library instead
 of a caller-provided work buffer.  The test calls it through the C ABI twice
 in a row (different inputs, so the second call reuses the array the first
