@@ -522,9 +522,16 @@ def time_weights(lnsb200, torch, np, args, flush, stream, hbm):
     dst = torch.empty(rows * cols, dtype=torch.int16, device="cuda")
     for t in ("f16", "q8_0", "q4_k", "q6_k"):
         rb = ks.type_row_bytes(t, cols)
-        raw = torch.from_numpy(rng.integers(0, 256, (rows, rb), dtype=np.uint8)).cuda()
         if t == "f16":
             raw = torch.from_numpy(rng.normal(0, 0.05, (rows, cols)).astype(np.float16).view(np.uint8)).cuda()
+        else:
+            # random quants under finite f16 block scales (1e-3 .. 1e-1), as a quantiser writes them
+            qk, bb = {"q8_0": (32, 34), "q4_k": (256, 144), "q6_k": (256, 210)}[t]
+            blocks = rng.integers(0, 256, (rows, cols // qk, bb), dtype=np.uint8)
+            for off in {"q8_0": [0], "q4_k": [0, 2], "q6_k": [208]}[t]:
+                d = rng.uniform(1e-3, 1e-1, (rows, cols // qk)).astype(np.float16)
+                blocks[:, :, off:off + 2] = d.view(np.uint8).reshape(rows, cols // qk, 2)
+            raw = torch.from_numpy(blocks.reshape(rows, rb)).cuda()
         for _ in range(3):
             ks.to_lns_transposed_typed(t, raw, dst, rows, cols, rows, stream=stream)
         torch.cuda.synchronize()

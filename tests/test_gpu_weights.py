@@ -71,6 +71,54 @@ def test_to_lns_transposed_typed(orc, kss, fmt, type):
     assert np.array_equal(got, want)
 
 
+def _specials(type, raw, rng):
+    """plants zeros, subnormals, infinities, NaNs and extremes in element-type rows"""
+    if type == "f16":
+        pats = np.array([0x0000, 0x8000, 0x0001, 0x83FF, 0x0400, 0x7BFF, 0xFBFF, 0x7C00, 0xFC00, 0x7E00, 0x3C00, 0xBC00],
+                        np.uint16)
+        v = raw.view(np.uint16)
+    elif type == "bf16":
+        pats = np.array([0x0000, 0x8000, 0x0001, 0x807F, 0x0080, 0x7F7F, 0xFF7F, 0x7F80, 0xFF80, 0x7FC0, 0x3F80, 0x0100],
+                        np.uint16)
+        v = raw.view(np.uint16)
+    elif type == "f32":
+        pats = np.array([0x00000000, 0x80000000, 0x00000001, 0x807FFFFF, 0x00800000, 0x7F7FFFFF, 0xFF7FFFFF, 0x7F800000,
+                         0xFF800000, 0x7FC00000, 0x3F800000, 0x01000000], np.uint32)
+        v = raw.view(np.uint32)
+    else:
+        return raw
+    idx = rng.integers(0, v.size, 400)
+    v.reshape(-1)[idx] = rng.choice(pats, 400)
+    return raw
+
+
+@pytest.mark.parametrize("type,rows,cols,dst_ld,misalign", [
+    ("f16", 130, 576, 136, 0),     # 16-byte stores, a partial row tile and a partial column tile
+    ("f16", 64, 512, 64, 2),       # source not 16-byte aligned: byte staging
+    ("bf16", 129, 300, 129, 0),
+    ("f32", 70, 200, 72, 0),
+    ("q8_0", 96, 576, 96, 0),
+    ("q4_0", 65, 288, 72, 0),
+    ("q4_k", 70, 1024, 72, 0),
+    ("q6_k", 70, 2048, 72, 0),     # 16-byte rows: staged windows that start inside a 16-byte piece
+    ("q6_k", 33, 768, 40, 0),
+])
+def test_to_lns_transposed_typed_tiles(orc, kss, type, rows, cols, dst_ld, misalign):
+    """the tiled xlns16 conversion: every tile edge, both copy paths, both
+    store paths, and (element types) zeros, subnormals, infinities, NaNs"""
+    rng = np.random.default_rng(rows * 7 + cols)
+    raw = _specials(type, np.ascontiguousarray(random_rows(orc, type, rows, cols, rng)), rng)
+    buf = torch.zeros(raw.size + 16, dtype=torch.uint8, device="cuda")
+    buf[misalign:misalign + raw.size] = torch.from_numpy(raw.reshape(-1)).cuda()
+    dst = torch.full((cols * dst_ld,), 0x1234, dtype=torch.int16, device="cuda")
+    kss[16].to_lns_transposed_typed(type, buf[misalign:], dst, rows, cols, dst_ld)
+    torch.cuda.synchronize()
+    want = orc.from_f32_16(orc.dequant(type, raw, rows, cols)).T                       # [cols][rows]
+    got = dst.cpu().numpy().view(np.uint16).reshape(cols, dst_ld)
+    assert np.array_equal(got[:, :rows], want)
+    assert np.all(got[:, rows:] == 0x1234)                                                # padding untouched
+
+
 def image_f32(ks, addr, n):
     """the F32 decode of n LNS codes at a device address (lnsb_to_f32)"""
     out = torch.empty(n, dtype=torch.float32, device="cuda")

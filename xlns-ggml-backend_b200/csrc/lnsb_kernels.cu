@@ -312,6 +312,195 @@ __device__ __forceinline__ void stage_async(void * smem, const void * gmem, int 
         cp_async16(static_cast<unsigned char *>(smem) + 16 * i, static_cast<const unsigned char *>(gmem) + 16 * i);
 }
 
+// ---- the xlns16 image of a typed weight at HBM speed ----------------------
+//
+// float -> xlns16 without the 128 KB table: for a normal float (biased
+// exponent e in 1..254, top mantissa bits m) the table entry is
+//     clamp(128 (e - 127) + G[m] + 0x4000, 0, 0x7FFF) | sign,
+// G[m] = 128 log2(1 + m/128) truncated toward zero: floored for |x| >= 1,
+// rounded up below.  G is read off the table itself (entries at e = 127 and
+// e = 126) and the split is checked against all 65536 entries on the host
+// before this path is used (conv16_splits); subnormals, infinities and NaNs
+// keep the table lookup.  A CTA keeps G in shared memory, one copy per bank
+// (word m * 32 + lane holds G for |x| >= 1 in byte 0, for |x| < 1 in byte 1),
+// so a warp's lookups never conflict.
+constexpr int TW_ROWS = 64, TW_THREADS = 1024, TW_STAGES = 4;
+constexpr int TW_OP = TW_ROWS + 2;                       // codes per column of the transposed tile (33 words)
+constexpr int TW_GTAB = 128 * 32 * 4;
+
+template <int TYPE> struct tw_geom {
+    static constexpr int cols  = TYPE == LNSB_TYPE_F32 ? 128 : 256;     // a tile's columns: whole blocks
+    static constexpr int blk   = (TYPE == LNSB_TYPE_Q4_K || TYPE == LNSB_TYPE_Q6_K) ? 256
+                               : (TYPE == LNSB_TYPE_Q8_0 || TYPE == LNSB_TYPE_Q4_0) ? 32 : 1;
+    static constexpr int bb    = TYPE == LNSB_TYPE_F32 ? 4 : TYPE == LNSB_TYPE_Q8_0 ? 34 : TYPE == LNSB_TYPE_Q4_0 ? 18
+                               : TYPE == LNSB_TYPE_Q4_K ? 144 : TYPE == LNSB_TYPE_Q6_K ? 210 : 2;
+    static constexpr int seg   = cols / blk * bb;                           // raw bytes of a tile row
+    static constexpr int rawp  = (seg + 15 + 15) / 16 * 16;                 // staged row pitch (16-byte window slack)
+    static constexpr int stage = TW_ROWS * rawp;
+    static constexpr int smem  = TW_GTAB + TW_STAGES * stage + cols * TW_OP * 2;
+};
+
+// a normal float's upper 16 bits -> xlns16 through the shared copies of G
+__device__ __forceinline__ uint32_t conv16_fast(const uint32_t * __restrict__ glane, uint32_t u) {
+    const uint32_t g = __byte_perm(glane[(u & 0x7Fu) << 5], 0u, (u & 0x7FFFu) < (127u << 7) ? 0x4441u : 0x4440u);
+    return (u & 0x8000u) | min((u & 0x7F80u) + g + 128u, 0x7FFFu);    // 128 (e - 127) + 0x4000 = 128 e + 128
+}
+__device__ __forceinline__ bool conv16_normal(uint32_t u) { return (u & 0x7F80u) - 0x80u < 0x7F00u; }
+__device__ __forceinline__ uint32_t conv16_split(const dev_tables & T, const uint32_t * __restrict__ glane, uint32_t u) {
+    return conv16_normal(u) ? conv16_fast(glane, u) : (uint32_t) __ldg(T.conv16 + u);
+}
+
+// the upper 16 bits of value c's float (the conversion table's index)
+template <int TYPE>
+__device__ __forceinline__ uint32_t f32_hi_at(const unsigned char * row, int c) {
+    if constexpr (TYPE == LNSB_TYPE_BF16) {
+        return reinterpret_cast<const uint16_t *>(row)[c];
+    } else if constexpr (TYPE == LNSB_TYPE_F16) {
+        return __float_as_uint(__half2float(reinterpret_cast<const __half *>(row)[c])) >> 16;   // exact widening
+    } else {
+        return __float_as_uint(dequant_at_t<TYPE>(row, c)) >> 16;
+    }
+}
+
+// dst[c * dst_ld + r] = xlns16(dequant(row r)[c]), rows `row_bytes` apart.
+// One CTA per SM walks tiles of 64 rows x tw_geom::cols columns through a
+// ring of TW_STAGES staging buffers: each tile's raw row segments are copied
+// with 16-byte cp.async (vec_in: src and row_bytes 16-byte aligned; the
+// window is rounded out to 16 bytes, never past the row), so the next
+// TW_STAGES - 1 tiles' copies are in flight while one tile is decoded and
+// converted from shared memory into a transposed tile (33-word column pitch:
+// conflict-free both ways) and stored, each column's 64 codes as 128
+// contiguous bytes (vec_out: dst and dst_ld 16-byte aligned).
+template <int TYPE>
+__global__ void __launch_bounds__(TW_THREADS, 1)
+k_to_lns16_typed_tiled(dev_tables T, const unsigned char * __restrict__ src, int64_t row_bytes,
+                       uint16_t * __restrict__ dst, int64_t rows, int64_t cols, int64_t dst_ld, int vec_in, int vec_out) {
+    using G = tw_geom<TYPE>;
+    pdl_entry();
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint32_t *      gtab = reinterpret_cast<uint32_t *>(smem);
+    unsigned char * raw  = smem + TW_GTAB;
+    uint16_t *      tile = reinterpret_cast<uint16_t *>(smem + TW_GTAB + TW_STAGES * G::stage);
+    const int tid = threadIdx.x, lane = tid & 31;
+
+    // G from the table's entries at e = 127 (|x| >= 1) and e = 126 (|x| < 1):
+    // one load each by the first 128 threads, then one copy per bank
+    uint32_t * g0 = reinterpret_cast<uint32_t *>(tile);
+    if (tid < 128) {
+        const uint32_t gp = (uint32_t) __ldg(T.conv16 + ((127 << 7) | tid)) - 0x4000u;
+        const uint32_t gn = (uint32_t) __ldg(T.conv16 + ((126 << 7) | tid)) - 0x4000u + 128u;
+        g0[tid] = gp | (gn << 8);
+    }
+
+    // tile t: row block t / nct, column block t % nct (the launcher keeps the tile count below 2^31)
+    const uint32_t nct = (uint32_t) ((cols + G::cols - 1) / G::cols);
+    const int64_t ntiles = (int64_t) nct * ((rows + TW_ROWS - 1) / TW_ROWS);
+    // window of a tile's row segment: bytes [cb0, cb1) of each row
+    auto window = [&](int64_t t, int64_t & r0, int64_t & c0, int64_t & a0, int & nch, int & off) {
+        const uint32_t rt = (uint32_t) t / nct;
+        r0 = (int64_t) rt * TW_ROWS;
+        c0 = (int64_t) ((uint32_t) t - rt * nct) * G::cols;
+        const int64_t cb0 = c0 / G::blk * G::bb, cb1 = imin64(cb0 + G::seg, row_bytes);
+        if (vec_in) {
+            a0 = cb0 & ~(int64_t) 15;
+            nch = (int) ((((cb1 + 15) & ~(int64_t) 15) - a0) >> 4);
+            off = (int) (cb0 - a0);
+        } else {
+            a0 = cb0;
+            nch = (int) (cb1 - cb0);        // bytes
+            off = 0;
+        }
+    };
+    // stages tile t (when it exists) into ring slot `slot`; always closes a
+    // cp.async group, so the groups in flight count tiles
+    auto stage = [&](int64_t t, int slot) {
+        if (t < ntiles) {
+            int64_t r0, c0, a0; int nch, off;
+            window(t, r0, c0, a0, nch, off);
+            const int rv = (int) imin64(TW_ROWS, rows - r0);
+            unsigned char * rs = raw + slot * G::stage;
+            if (vec_in) {                                  // a warp per row
+                for (int r = tid >> 5; r < rv; r += TW_THREADS / 32)
+                    for (int q = lane; q < nch; q += 32)
+                        cp_async16(rs + r * G::rawp + 16 * q, src + (r0 + r) * row_bytes + a0 + 16 * q);
+            } else {
+                for (int r = tid >> 5; r < rv; r += TW_THREADS / 32)
+                    for (int q = lane; q < nch; q += 32) rs[r * G::rawp + q] = src[(r0 + r) * row_bytes + a0 + q];
+            }
+        }
+        cp_async_commit();
+    };
+
+#pragma unroll
+    for (int k = 0; k < TW_STAGES - 1; k++) stage((int64_t) blockIdx.x + (int64_t) k * gridDim.x, k);
+    __syncthreads();                                       // g0 written
+    uint32_t gw[128 * 32 / TW_THREADS];
+#pragma unroll
+    for (int j = 0; j < 128 * 32 / TW_THREADS; j++) gw[j] = g0[(tid + j * TW_THREADS) >> 5];
+    __syncthreads();                                       // g0 read: the tile is free
+#pragma unroll
+    for (int j = 0; j < 128 * 32 / TW_THREADS; j++) gtab[tid + j * TW_THREADS] = gw[j];
+    const uint32_t * glane = gtab + lane;
+
+    int slot = 0;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        int64_t r0, c0, a0; int nch, off;
+        window(t, r0, c0, a0, nch, off);
+        const int rv = (int) imin64(TW_ROWS, rows - r0), cv = (int) imin64(G::cols, cols - c0);
+        cp_async_wait<TW_STAGES - 2>();                    // this tile's group has landed
+        __syncthreads();                                   // ... for every thread; the tile and the slot
+                                                           // read last time are free again
+        stage(t + (int64_t) (TW_STAGES - 1) * gridDim.x, slot == 0 ? TW_STAGES - 1 : slot - 1);
+        const unsigned char * rs = raw + slot * G::stage + off;
+        // a thread converts column c of row pairs p0, p0 + TW_PPS, ... and
+        // writes each pair as one word of the transposed tile; a warp covers
+        // 32 consecutive columns.  The branch-free path covers zeros and every
+        // value whose float is normal (subnormal halves widen to normal
+        // floats); a value outside it (infinity, NaN, a subnormal float) is
+        // patched afterwards from the table.  Rows past the matrix hold stale
+        // bytes: harmless, they are never stored.
+        constexpr int TW_PPS = TW_THREADS / G::cols;       // row pairs per step
+        constexpr int TW_NP  = TW_ROWS / 2 / TW_PPS;       // steps
+        const int c = tid % G::cols, p0 = tid / G::cols;
+        if (c < cv) {
+            uint32_t bad = 0;                              // bit k: pair k holds a value outside the fast path
+#pragma unroll 4
+            for (int k = 0; k < TW_NP; k++) {
+                const int r = 2 * (p0 + k * TW_PPS);
+                const uint32_t u0 = f32_hi_at<TYPE>(rs + r * G::rawp, c), u1 = f32_hi_at<TYPE>(rs + (r + 1) * G::rawp, c);
+                const bool ok = (conv16_normal(u0) || (u0 & 0x7FFFu) == 0) && (conv16_normal(u1) || (u1 & 0x7FFFu) == 0);
+                bad |= ok ? 0u : 1u << k;
+                const uint32_t v0 = (u0 & 0x7FFFu) ? conv16_fast(glane, u0) : 0u;
+                const uint32_t v1 = (u1 & 0x7FFFu) ? conv16_fast(glane, u1) : 0u;
+                *reinterpret_cast<uint32_t *>(tile + c * TW_OP + r) = v0 | (v1 << 16);
+            }
+            while (bad) {
+                const int k = __ffs(bad) - 1;
+                bad &= bad - 1;
+                const int r = 2 * (p0 + k * TW_PPS);
+                const uint32_t v0 = conv16_split(T, glane, f32_hi_at<TYPE>(rs + r * G::rawp, c));
+                const uint32_t v1 = conv16_split(T, glane, f32_hi_at<TYPE>(rs + (r + 1) * G::rawp, c));
+                *reinterpret_cast<uint32_t *>(tile + c * TW_OP + r) = v0 | (v1 << 16);
+            }
+        }
+        __syncthreads();                                   // the tile complete
+        slot = slot == TW_STAGES - 1 ? 0 : slot + 1;
+        if (vec_out && rv == TW_ROWS) {
+            for (int i = tid; i < cv * 8; i += TW_THREADS) {
+                const int c = i >> 3, j = i & 7;
+                const uint32_t * w = reinterpret_cast<const uint32_t *>(tile) + c * (TW_OP / 2) + 4 * j;
+                *reinterpret_cast<uint4 *>(dst + (c0 + c) * dst_ld + r0 + 8 * j) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        } else {
+            for (int i = tid; i < cv * TW_ROWS; i += TW_THREADS) {
+                const int c = i / TW_ROWS, r = i % TW_ROWS;
+                if (r < rv) dst[(c0 + c) * dst_ld + r0 + r] = tile[c * TW_OP + r];
+            }
+        }
+    }
+    cp_async_wait<0>();
+}
+
 // ===================== MUL_MAT (xlns16, base mode, key form) ================
 //
 // The base-mode hot kernel.  Every chain carries its accumulator as a key
@@ -2386,6 +2575,26 @@ int nn_smem_attr(const void * kern, int bytes) {
     return 0;
 }
 
+// true when the float -> xlns16 table is, for every normal float, the
+// exponent-plus-mantissa split that conv16_split computes (G read off the
+// entries at e = 127 and e = 126); checked once over all 65536 entries
+bool conv16_splits() {
+    static const bool ok = [] {
+        const std::vector<uint16_t> & c = get_host_tables(false, false).conv16;
+        for (uint32_t u = 0; u < 65536; u++) {
+            const uint32_t e = (u >> 7) & 0xFFu, m = u & 0x7Fu;
+            if (e == 0 || e == 255) continue;
+            const int gp = (int) c[(127u << 7) | m] - 0x4000, gn = (int) c[(126u << 7) | m] - 0x4000 + 128;
+            if (gp < 0 || gp > 255 || gn < 0 || gn > 255) return false;
+            int v = 128 * ((int) e - 127) + (e < 127 ? gn : gp) + 0x4000;
+            v = v < 0 ? 0 : (v > 0x7FFF ? 0x7FFF : v);
+            if (c[u] != ((u & 0x8000u) | (uint32_t) v)) return false;
+        }
+        return true;
+    }();
+    return ok;
+}
+
 int rms_norm_impl(int fmt, const void * src, void * dst, int64_t ncols, int64_t nrows, float eps, uint16_t seed,
                   bool io_f32, cudaStream_t stream, bool fuse = false, const float * res = nullptr,
                   float * x_out = nullptr, const float * nw = nullptr) {
@@ -2693,11 +2902,34 @@ int lnsb_to_lns_transposed_typed(int fmt, int type, const void * src, void * dst
     int dev = 0;
     const int ds = current_device(&dev);
     if (ds != 0) return ds;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const auto * p = static_cast<const unsigned char *>(src);
+    if (fmt == LNSB_XLNS16 && conv16_splits() && ((rows + TW_ROWS - 1) / TW_ROWS) * ((cols + 127) / 128) < 0x7FFFFFFF) {
+        auto tiled = [&](auto kern, int smem, int tcols) {
+            const int as = nn_smem_attr(reinterpret_cast<const void *>(kern), smem);
+            if (as != 0) return as;
+            const int64_t ntiles = ((rows + TW_ROWS - 1) / TW_ROWS) * ((cols + tcols - 1) / tcols);
+            const int vin = (uintptr_t) p % 16 == 0 && rb % 16 == 0;
+            const int vout = (uintptr_t) dst % 16 == 0 && dst_ld % 8 == 0;
+            launch_k(kern, dim3((unsigned) imin64(ntiles, (int64_t) sm_count(dev))), TW_THREADS, (size_t) smem, s, *T,
+                     p, (int64_t) rb, static_cast<uint16_t *>(dst), rows, cols, dst_ld, vin, vout);
+            return launch_status();
+        };
+#define LNSB_TW(TY) tiled(k_to_lns16_typed_tiled<TY>, tw_geom<TY>::smem, tw_geom<TY>::cols)
+        switch (type) {
+            case LNSB_TYPE_F32:  return LNSB_TW(LNSB_TYPE_F32);
+            case LNSB_TYPE_F16:  return LNSB_TW(LNSB_TYPE_F16);
+            case LNSB_TYPE_BF16: return LNSB_TW(LNSB_TYPE_BF16);
+            case LNSB_TYPE_Q8_0: return LNSB_TW(LNSB_TYPE_Q8_0);
+            case LNSB_TYPE_Q4_0: return LNSB_TW(LNSB_TYPE_Q4_0);
+            case LNSB_TYPE_Q4_K: return LNSB_TW(LNSB_TYPE_Q4_K);
+            default:             return LNSB_TW(LNSB_TYPE_Q6_K);
+        }
+#undef LNSB_TW
+    }
     const int64_t ntiles = ((cols + 31) / 32) * ((rows + 31) / 32);
     const dim3 grid((unsigned) imin64(ntiles, (int64_t) sm_count(dev) * 16));
     const dim3 block(32, 8);
-    const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const auto * p = static_cast<const unsigned char *>(src);
     auto go = [&](auto k16, auto k32) {
         if (fmt == LNSB_XLNS16) launch_k(k16, grid, block, 0, s, *T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
         else                    launch_k(k32, grid, block, 0, s, *T, type, p, (int64_t) rb, dst, rows, cols, dst_ld);
