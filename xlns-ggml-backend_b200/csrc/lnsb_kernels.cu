@@ -546,6 +546,7 @@ constexpr int FB_OFF_RED  = FB_OFF_XKEY + FB_BN * FB_XKP * 4;
 constexpr int FB_OFF_CODE = FB_OFF_RED + 128;
 constexpr int FB_SMEM     = FB_OFF_CODE + 2 * (FB_WCODES + FB_XCODES) * 2;
 
+template <int BN>
 __device__ __forceinline__ void fb_stage(uint16_t * wc, uint16_t * xc, const uint16_t * __restrict__ W,
                                          const uint16_t * __restrict__ X, int64_t K, int64_t M, int64_t N,
                                          int64_t m0, int64_t n0, int64_t k0, bool vec) {
@@ -557,9 +558,9 @@ __device__ __forceinline__ void fb_stage(uint16_t * wc, uint16_t * xc, const uin
             const int r = c >> 3, q = c & 7;
             if (k0 + r < K) cp_async16(wc + r * FB_BM + q * 8, W + (k0 + r) * M + m0 + q * 8);
         }
-        {                                          // tokens: 32 rows x 64 B = 128 x 16 B
+        {                                          // tokens: BN rows x 64 B (at most 128 x 16 B)
             const int r = tid >> 2, q = tid & 3;
-            if (n0 + r < N && k0 + q * 8 < K) cp_async16(xc + r * FB_XP + q * 8, X + (n0 + r) * K + k0 + q * 8);
+            if (r < BN && n0 + r < N && k0 + q * 8 < K) cp_async16(xc + r * FB_XP + q * 8, X + (n0 + r) * K + k0 + q * 8);
         }
     } else {
         for (int i = tid; i < FB_WCODES; i += FB_THREADS) {
@@ -567,7 +568,7 @@ __device__ __forceinline__ void fb_stage(uint16_t * wc, uint16_t * xc, const uin
             const int64_t k = k0 + r, m = m0 + c;
             wc[r * FB_BM + c] = (k < K && m < M) ? W[k * M + m] : (uint16_t) 0x4000;
         }
-        for (int i = tid; i < FB_BN * FB_KC; i += FB_THREADS) {
+        for (int i = tid; i < BN * FB_KC; i += FB_THREADS) {
             const int r = i / FB_KC, c = i % FB_KC;
             const int64_t n = n0 + r, k = k0 + c;
             xc[r * FB_XP + c] = (n < N && k < K) ? X[n * K + k] : (uint16_t) 0x4000;
@@ -618,13 +619,15 @@ struct peer_out_dev {
     int64_t            ld, off;
 };
 
-template <bool OUT_F32>
-__global__ void __launch_bounds__(FB_THREADS, FB_MONTE ? 2 : 4)
-k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
-                 void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
-                 int64_t r2, int64_t r3, uint32_t monte_seed, int vec, peer_out_dev peers) {
-    pdl_entry();
-    extern __shared__ __align__(16) unsigned char smem[];
+// One tile: 64 weight rows x 8 * TN tokens from (m0, n0) of slice z; a
+// thread runs 4 rows x TN tokens (tokens tn, tn + 8, ...).
+template <bool OUT_F32, int TN>
+__device__ __forceinline__ void fb_tile(const dev_tables & T, unsigned char * smem, const uint16_t * __restrict__ W,
+                                        const uint16_t * __restrict__ X, void * __restrict__ dst, int64_t K, int64_t M,
+                                        int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3,
+                                        uint32_t monte_seed, int vec, const peer_out_dev & peers, int64_t z,
+                                        int64_t m0, int64_t n0) {
+    constexpr int BN = 8 * TN;                          // tokens of the tile
     int *      wkeys = reinterpret_cast<int *>(smem + FB_OFF_WKEY);
     int *      xkeys = reinterpret_cast<int *>(smem + FB_OFF_XKEY);
     int *      red   = reinterpret_cast<int *>(smem + FB_OFF_RED);
@@ -640,8 +643,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
     }
     const int rbase = (threadIdx.x & 1) * FB_REPL;
 
-    const int64_t z = blockIdx.z, i12 = z % ne12, i13 = z / ne12;
-    const int64_t m0 = (int64_t) blockIdx.x * FB_BM, n0 = (int64_t) blockIdx.y * FB_BN;
+    const int64_t i12 = z % ne12, i13 = z / ne12;
     const uint16_t * Wz = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
     const uint16_t * Xz = X + z * N * K;
     const int tm = threadIdx.x % (FB_BM / FB_TM), tn = threadIdx.x / (FB_BM / FB_TM);
@@ -649,17 +651,17 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
     const int warp = threadIdx.x >> 5;
     // tokens tn, tn + 8, tn + 16, tn + 24
 
-    int      akey[FB_TM][FB_TN];
-    uint32_t acc[FB_TM][FB_TN];
-    uint32_t st[FB_TM][FB_TN];                          // Monte: each chain's LFSR state
+    int      akey[FB_TM][TN];
+    uint32_t acc[FB_TM][TN];
+    uint32_t st[FB_TM][TN];                          // Monte: each chain's LFSR state
     bool fast = true;                                   // uniform across the block
     const int nchunks = (int) ((K + FB_KC - 1) / FB_KC);
-    const int64_t nvalid = imin64(FB_BN, N - n0);
+    const int64_t nvalid = imin64(BN, N - n0);
     red16 R{ &T, T.sbdb16, T.monte16 };                 // slow path reads the packed tables from L1/L2
 #pragma unroll
     for (int i = 0; i < FB_TM; i++)
 #pragma unroll
-        for (int j = 0; j < FB_TN; j++) {
+        for (int j = 0; j < TN; j++) {
             st[i][j] = 0;
             if constexpr (FB_MONTE) {
                 // the chain of output (z, m, n) starts (its index in the CPU's loop
@@ -672,7 +674,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
         }
 
     if (nchunks > 0) {
-        fb_stage(codes, codes + FB_WCODES, Wz, Xz, K, M, N, m0, n0, 0, vec != 0);
+        fb_stage<BN>(codes, codes + FB_WCODES, Wz, Xz, K, M, N, m0, n0, 0, vec != 0);
         cp_async_commit();
     }
     for (int c = 0; c < nchunks; c++) {
@@ -680,7 +682,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
         uint16_t * xc = wc + FB_WCODES;
         if (c + 1 < nchunks) {
             uint16_t * wn = codes + ((c + 1) & 1) * (FB_WCODES + FB_XCODES);
-            fb_stage(wn, wn + FB_WCODES, Wz, Xz, K, M, N, m0, n0, (int64_t) (c + 1) * FB_KC, vec != 0);
+            fb_stage<BN>(wn, wn + FB_WCODES, Wz, Xz, K, M, N, m0, n0, (int64_t) (c + 1) * FB_KC, vec != 0);
             cp_async_commit();
             cp_async_wait<1>();
         } else {
@@ -697,7 +699,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
                 wkeys[i] = key_of_code_w(cw);
                 if (r < kvalid) { const int l = (int) (cw & 0x7FFFu); wmin = min(wmin, l); wmax = max(wmax, l); }
             }
-            for (int i = threadIdx.x; i < FB_BN * FB_KC; i += FB_THREADS) {
+            for (int i = threadIdx.x; i < BN * FB_KC; i += FB_THREADS) {
                 const int r = i / FB_KC, col = i % FB_KC;
                 const uint32_t cx = xc[r * FB_XP + col];
                 xkeys[r * FB_XKP + col] = key_of_code_x(cx);
@@ -709,7 +711,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 #pragma unroll
                 for (int i = 0; i < FB_TM; i++)
 #pragma unroll
-                    for (int j = 0; j < FB_TN; j++) amax = max(amax, akey[i][j] >> 4);
+                    for (int j = 0; j < TN; j++) amax = max(amax, akey[i][j] >> 4);
             }
             wmin = __reduce_min_sync(0xFFFFFFFFu, wmin);
             wmax = __reduce_max_sync(0xFFFFFFFFu, wmax);
@@ -737,7 +739,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 #pragma unroll
                     for (int i = 0; i < FB_TM; i++)
 #pragma unroll
-                        for (int j = 0; j < FB_TN; j++) acc[i][j] = code_of_key(akey[i][j]);
+                        for (int j = 0; j < TN; j++) acc[i][j] = code_of_key(akey[i][j]);
                 }
             }
         }
@@ -749,7 +751,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 #pragma unroll
                 for (int i = 0; i < FB_TM; i++)
 #pragma unroll
-                    for (int j = 0; j < FB_TN; j++) akey[i][j] = key_of_product(wv[i], xkeys[(tn + 8 * j) * FB_XKP]);
+                    for (int j = 0; j < TN; j++) akey[i][j] = key_of_product(wv[i], xkeys[(tn + 8 * j) * FB_XKP]);
                 k = 1;
                 for (; k < 4 && k < kvalid; k++) {
                     const int4 wk = *reinterpret_cast<const int4 *>(wkeys + k * FB_BM + mloc);
@@ -757,14 +759,14 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 #pragma unroll
                     for (int i = 0; i < FB_TM; i++)
 #pragma unroll
-                        for (int j = 0; j < FB_TN; j++)
+                        for (int j = 0; j < TN; j++)
                             akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem, rbase, st[i][j]);
                 }
             }
             for (; k + 4 <= kvalid; k += 4) {
-                int4 xv[FB_TN];
+                int4 xv[TN];
 #pragma unroll
-                for (int j = 0; j < FB_TN; j++) xv[j] = *reinterpret_cast<const int4 *>(xkeys + (tn + 8 * j) * FB_XKP + k);
+                for (int j = 0; j < TN; j++) xv[j] = *reinterpret_cast<const int4 *>(xkeys + (tn + 8 * j) * FB_XKP + k);
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
                     const int4 wk = *reinterpret_cast<const int4 *>(wkeys + (k + u) * FB_BM + mloc);
@@ -772,7 +774,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 #pragma unroll
                     for (int i = 0; i < FB_TM; i++)
 #pragma unroll
-                        for (int j = 0; j < FB_TN; j++) {
+                        for (int j = 0; j < TN; j++) {
                             const int xk = u == 0 ? xv[j].x : u == 1 ? xv[j].y : u == 2 ? xv[j].z : xv[j].w;
                             akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xk), smem, rbase, st[i][j]);
                         }
@@ -784,7 +786,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 #pragma unroll
                 for (int i = 0; i < FB_TM; i++)
 #pragma unroll
-                    for (int j = 0; j < FB_TN; j++)
+                    for (int j = 0; j < TN; j++)
                         akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem, rbase, st[i][j]);
             }
         } else {
@@ -793,7 +795,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 #pragma unroll
                 for (int i = 0; i < FB_TM; i++)
 #pragma unroll
-                    for (int j = 0; j < FB_TN; j++) acc[i][j] = mul16(wc[mloc + i], xc[(tn + 8 * j) * FB_XP]);
+                    for (int j = 0; j < TN; j++) acc[i][j] = mul16(wc[mloc + i], xc[(tn + 8 * j) * FB_XP]);
                 k = 1;
             }
             for (; k < kvalid; k++) {
@@ -801,7 +803,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
                 for (int i = 0; i < FB_TM; i++) {
                     const uint32_t w = wc[k * FB_BM + mloc + i];
 #pragma unroll
-                    for (int j = 0; j < FB_TN; j++) acc[i][j] = R.add(acc[i][j], mul16(w, xc[(tn + 8 * j) * FB_XP + k]), st[i][j]);
+                    for (int j = 0; j < TN; j++) acc[i][j] = R.add(acc[i][j], mul16(w, xc[(tn + 8 * j) * FB_XP + k]), st[i][j]);
                 }
             }
         }
@@ -812,7 +814,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
         // 4 consecutive rows per thread and token: one 8-byte store per peer
         // (16 threads cover a token's 64 rows: 128 contiguous bytes)
 #pragma unroll
-        for (int j = 0; j < FB_TN; j++) {
+        for (int j = 0; j < TN; j++) {
             const int64_t n = n0 + tn + 8 * j;
             if (n >= N) continue;
             uint32_t v[FB_TM];
@@ -838,7 +840,7 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
         const int64_t m = m0 + mloc + i;
         if (m >= M) continue;
 #pragma unroll
-        for (int j = 0; j < FB_TN; j++) {
+        for (int j = 0; j < TN; j++) {
             const int64_t n = n0 + tn + 8 * j;
             if (n >= N) continue;
             const uint32_t v = K == 0 ? 0u : (fast ? code_of_key(akey[i][j]) : acc[i][j]);
@@ -846,6 +848,31 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
             if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
             else                   static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
         }
+    }
+}
+
+// Blocks [0, nfull) run whole 64 x 32 tiles (tile b at (b % gx, b / gx));
+// the blocks after them run the remaining tiles in quarters of 8 tokens (one
+// token per thread).  The launcher makes nfull a multiple of the SM count, so
+// whole tiles fill whole waves and the last, partial wave is dealt out in
+// quarter-size pieces that even out the work per SM.
+template <bool OUT_F32>
+__global__ void __launch_bounds__(FB_THREADS, FB_MONTE ? 2 : 4)
+k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
+                 void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
+                 int64_t r2, int64_t r3, uint32_t monte_seed, int vec, peer_out_dev peers, int64_t gx, int64_t nfull) {
+    pdl_entry();
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int64_t b = blockIdx.x, z = blockIdx.z;
+    if (b < nfull) {
+        fb_tile<OUT_F32, FB_TN>(T, smem, W, X, dst, K, M, N, ne02, ne12, r2, r3, monte_seed, vec, peers, z,
+                                (b % gx) * FB_BM, (b / gx) * FB_BN);
+    } else {
+        const int64_t q = b - nfull, t = nfull + q / 4;
+        const int64_t n0 = (t / gx) * FB_BN + (q % 4) * 8;
+        if (n0 < N)
+            fb_tile<OUT_F32, 1>(T, smem, W, X, dst, K, M, N, ne02, ne12, r2, r3, monte_seed, vec, peers, z,
+                                (t % gx) * FB_BM, n0);
     }
 }
 
@@ -2531,9 +2558,16 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         launch_k(kern, grid, LT_ROWS, smem, stream, *T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
                                               dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, vec ? 1 : 0);
     } else if (fmt == LNSB_XLNS16 && (k_mode == M_BASE || k_mode == M_MONTE)) {
-        const int64_t gx = (a->M + FB_BM - 1) / FB_BM, gy = (a->N + FB_BN - 1) / FB_BN;
-        if (gx > 0x7FFFFFFF || gy > 65535) return LNSB_E_TOO_LARGE;
-        const dim3 grid((unsigned) gx, (unsigned) gy, (unsigned) (a->ne12 * a->ne13));
+        const int64_t gx = (a->M + FB_BM - 1) / FB_BM, gy = (a->N + FB_BN - 1) / FB_BN, nz = a->ne12 * a->ne13;
+        int dev0 = 0;
+        const int ds0 = current_device(&dev0);
+        if (ds0 != 0) return ds0;
+        // one slice: whole tiles in whole waves of SMs, the rest in quarter tiles
+        const int64_t nt = gx * gy, sms = sm_count(dev0);
+        const int64_t nfull = nz == 1 ? nt / sms * sms : nt;
+        const int64_t nblk = nfull + 4 * (nt - nfull);
+        if (nblk > 0x7FFFFFFF) return LNSB_E_TOO_LARGE;
+        const dim3 grid((unsigned) nblk, 1u, (unsigned) nz);
         const bool vec = a->M % FB_BM == 0 && a->K % 8 == 0 && ((uintptr_t) a->w % 16) == 0 && ((uintptr_t) a->x % 16) == 0;
         static bool fattr[k_max_devices][2] = {};
         auto kern = out_f32 ? k_mul_mat16_fast<true> : k_mul_mat16_fast<false>;
@@ -2547,7 +2581,8 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         }
         launch_k(kern, grid, FB_THREADS, FB_SMEM, stream, *T, static_cast<const uint16_t *>(a->w),
                                                     static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N, a->ne02,
-                                                    a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0, peers ? *peers : no_peers);
+                                                    a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0, peers ? *peers : no_peers,
+                                                    gx, nfull);
     } else if (fmt == LNSB_XLNS32 || k_mode == M_SUM32 || k_mode == M_LPVIP || k_mode == M_MONTE_BYLPVIP) {
         return mul_mat_a32(fmt, *T, a, dst, out_f32, r2, r3, stream);
     } else {
