@@ -549,8 +549,7 @@ constexpr int FB_SMEM     = FB_OFF_CODE + 2 * (FB_WCODES + FB_XCODES) * 2;
 template <int BN>
 __device__ __forceinline__ void fb_stage(uint16_t * wc, uint16_t * xc, const uint16_t * __restrict__ W,
                                          const uint16_t * __restrict__ X, int64_t K, int64_t M, int64_t N,
-                                         int64_t m0, int64_t n0, int64_t k0, bool vec) {
-    const int tid = threadIdx.x;
+                                         int64_t m0, int64_t n0, int64_t k0, bool vec, int tid) {
     if (vec) {
 #pragma unroll
         for (int it = 0; it < 2; it++) {           // weights: 32 k-rows x 128 B = 256 x 16 B
@@ -619,36 +618,39 @@ struct peer_out_dev {
     int64_t            ld, off;
 };
 
-// One tile: 64 weight rows x 8 * TN tokens from (m0, n0) of slice z; a
-// thread runs 4 rows x TN tokens (tokens tn, tn + 8, ...).
-template <bool OUT_F32, int TN>
-__device__ __forceinline__ void fb_tile(const dev_tables & T, unsigned char * smem, const uint16_t * __restrict__ W,
+// A group of FB_THREADS threads synchronises on its own named barrier when
+// several groups share a CTA (bar: 1 + group), on the CTA barrier otherwise.
+template <int NG>
+__device__ __forceinline__ void fb_sync(int bar) {
+    if constexpr (NG == 1) __syncthreads();
+    else asm volatile("bar.sync %0, %1;\n" ::"r"(bar), "n"(FB_THREADS) : "memory");
+}
+
+// One tile: 64 weight rows x 8 * TN tokens from (m0, n0) of slice z, run by
+// one group of FB_THREADS threads (tid: the thread's index in the group); a
+// thread runs 4 rows x TN tokens (tokens tn, tn + 8, ...).  tab: the key
+// table replicas, rbase: the byte offset of this thread's replica; gsm: the
+// group's operand buffers (the layout from FB_OFF_WKEY on).
+template <bool OUT_F32, int TN, int NG>
+__device__ __forceinline__ void fb_tile(const dev_tables & T, const unsigned char * tab, unsigned char * gsm, int tid,
+                                        int rbase, int bar, const uint16_t * __restrict__ W,
                                         const uint16_t * __restrict__ X, void * __restrict__ dst, int64_t K, int64_t M,
                                         int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3,
                                         uint32_t monte_seed, int vec, const peer_out_dev & peers, int64_t z,
                                         int64_t m0, int64_t n0) {
     constexpr int BN = 8 * TN;                          // tokens of the tile
-    int *      wkeys = reinterpret_cast<int *>(smem + FB_OFF_WKEY);
-    int *      xkeys = reinterpret_cast<int *>(smem + FB_OFF_XKEY);
-    int *      red   = reinterpret_cast<int *>(smem + FB_OFF_RED);
-    uint16_t * codes = reinterpret_cast<uint16_t *>(smem + FB_OFF_CODE);
+    int *      wkeys = reinterpret_cast<int *>(gsm);
+    int *      xkeys = reinterpret_cast<int *>(gsm + (FB_OFF_XKEY - FB_OFF_WKEY));
+    int *      red   = reinterpret_cast<int *>(gsm + (FB_OFF_RED - FB_OFF_WKEY));
+    uint16_t * codes = reinterpret_cast<uint16_t *>(gsm + (FB_OFF_CODE - FB_OFF_WKEY));
 
-    // two replicas of the key table, one per lane parity: same-sign lookups
-    // of one replica fall in banks 4j, the other's in 4j + 1
-    const int32_t * keytab = FB_MONTE ? T.mkey16 : T.key16;
-    for (int i = threadIdx.x; i < FB_KEYB / 4; i += FB_THREADS) {
-        const int v = keytab[i];
-        reinterpret_cast<int *>(smem)[i] = v;
-        reinterpret_cast<int *>(smem + FB_REPL)[i] = v;
-    }
-    const int rbase = (threadIdx.x & 1) * FB_REPL;
 
     const int64_t i12 = z % ne12, i13 = z / ne12;
     const uint16_t * Wz = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
     const uint16_t * Xz = X + z * N * K;
-    const int tm = threadIdx.x % (FB_BM / FB_TM), tn = threadIdx.x / (FB_BM / FB_TM);
+    const int tm = tid % (FB_BM / FB_TM), tn = tid / (FB_BM / FB_TM);
     const int mloc = tm * FB_TM;                        // rows mloc .. mloc+3
-    const int warp = threadIdx.x >> 5;
+    const int warp = tid >> 5;
     // tokens tn, tn + 8, tn + 16, tn + 24
 
     int      akey[FB_TM][TN];
@@ -674,7 +676,7 @@ __device__ __forceinline__ void fb_tile(const dev_tables & T, unsigned char * sm
         }
 
     if (nchunks > 0) {
-        fb_stage<BN>(codes, codes + FB_WCODES, Wz, Xz, K, M, N, m0, n0, 0, vec != 0);
+        fb_stage<BN>(codes, codes + FB_WCODES, Wz, Xz, K, M, N, m0, n0, 0, vec != 0, tid);
         cp_async_commit();
     }
     for (int c = 0; c < nchunks; c++) {
@@ -682,24 +684,24 @@ __device__ __forceinline__ void fb_tile(const dev_tables & T, unsigned char * sm
         uint16_t * xc = wc + FB_WCODES;
         if (c + 1 < nchunks) {
             uint16_t * wn = codes + ((c + 1) & 1) * (FB_WCODES + FB_XCODES);
-            fb_stage<BN>(wn, wn + FB_WCODES, Wz, Xz, K, M, N, m0, n0, (int64_t) (c + 1) * FB_KC, vec != 0);
+            fb_stage<BN>(wn, wn + FB_WCODES, Wz, Xz, K, M, N, m0, n0, (int64_t) (c + 1) * FB_KC, vec != 0, tid);
             cp_async_commit();
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
-        __syncthreads();
+        fb_sync<NG>(bar);
         const int kvalid = (int) imin64(FB_KC, K - (int64_t) c * FB_KC);
         if (fast) {
             // convert this chunk to key form; operand log ranges for the range check
             int wmin = 0x7FFF, wmax = 0, xmin = 0x7FFF, xmax = 0;
-            for (int i = threadIdx.x; i < FB_KC * FB_BM; i += FB_THREADS) {
+            for (int i = tid; i < FB_KC * FB_BM; i += FB_THREADS) {
                 const int r = i / FB_BM;
                 const uint32_t cw = wc[i];
                 wkeys[i] = key_of_code_w(cw);
                 if (r < kvalid) { const int l = (int) (cw & 0x7FFFu); wmin = min(wmin, l); wmax = max(wmax, l); }
             }
-            for (int i = threadIdx.x; i < BN * FB_KC; i += FB_THREADS) {
+            for (int i = tid; i < BN * FB_KC; i += FB_THREADS) {
                 const int r = i / FB_KC, col = i % FB_KC;
                 const uint32_t cx = xc[r * FB_XP + col];
                 xkeys[r * FB_XKP + col] = key_of_code_x(cx);
@@ -718,11 +720,11 @@ __device__ __forceinline__ void fb_tile(const dev_tables & T, unsigned char * sm
             xmin = __reduce_min_sync(0xFFFFFFFFu, xmin);
             xmax = __reduce_max_sync(0xFFFFFFFFu, xmax);
             amax = __reduce_max_sync(0xFFFFFFFFu, amax);
-            if ((threadIdx.x & 31) == 0) {
+            if ((tid & 31) == 0) {
                 red[warp * 8 + 0] = wmin; red[warp * 8 + 1] = wmax; red[warp * 8 + 2] = xmin; red[warp * 8 + 3] = xmax;
                 red[warp * 8 + 4] = amax;
             }
-            __syncthreads();
+            fb_sync<NG>(bar);
             int a0 = 0x7FFF, a1 = 0, b0 = 0x7FFF, b1 = 0, am = 0;
 #pragma unroll
             for (int w = 0; w < FB_THREADS / 32; w++) {
@@ -760,7 +762,7 @@ __device__ __forceinline__ void fb_tile(const dev_tables & T, unsigned char * sm
                     for (int i = 0; i < FB_TM; i++)
 #pragma unroll
                         for (int j = 0; j < TN; j++)
-                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem, rbase, st[i][j]);
+                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), tab, rbase, st[i][j]);
                 }
             }
             for (; k + 4 <= kvalid; k += 4) {
@@ -776,7 +778,7 @@ __device__ __forceinline__ void fb_tile(const dev_tables & T, unsigned char * sm
 #pragma unroll
                         for (int j = 0; j < TN; j++) {
                             const int xk = u == 0 ? xv[j].x : u == 1 ? xv[j].y : u == 2 ? xv[j].z : xv[j].w;
-                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xk), smem, rbase, st[i][j]);
+                            akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xk), tab, rbase, st[i][j]);
                         }
                 }
             }
@@ -787,7 +789,7 @@ __device__ __forceinline__ void fb_tile(const dev_tables & T, unsigned char * sm
                 for (int i = 0; i < FB_TM; i++)
 #pragma unroll
                     for (int j = 0; j < TN; j++)
-                        akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), smem, rbase, st[i][j]);
+                        akey[i][j] = key_step(akey[i][j], key_of_product(w2[i], xkeys[(tn + 8 * j) * FB_XKP + k]), tab, rbase, st[i][j]);
             }
         } else {
             // packed codes, full xlns16 semantics
@@ -807,7 +809,7 @@ __device__ __forceinline__ void fb_tile(const dev_tables & T, unsigned char * sm
                 }
             }
         }
-        __syncthreads();
+        fb_sync<NG>(bar);
     }
 
     if (!OUT_F32 && peers.n > 0) {
@@ -863,16 +865,72 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
                  int64_t r2, int64_t r3, uint32_t monte_seed, int vec, peer_out_dev peers, int64_t gx, int64_t nfull) {
     pdl_entry();
     extern __shared__ __align__(16) unsigned char smem[];
+    // two replicas of the key table, one per lane parity: same-sign lookups
+    // of one replica fall in banks 4j, the other's in 4j + 1 (made visible by
+    // the tile's first barrier)
+    const int32_t * keytab = FB_MONTE ? T.mkey16 : T.key16;
+    for (int i = threadIdx.x; i < FB_KEYB / 4; i += FB_THREADS) {
+        const int v = keytab[i];
+        reinterpret_cast<int *>(smem)[i] = v;
+        reinterpret_cast<int *>(smem + FB_REPL)[i] = v;
+    }
+    const int rbase = (threadIdx.x & 1) * FB_REPL;
+    unsigned char * gsm = smem + FB_OFF_WKEY;
     const int64_t b = blockIdx.x, z = blockIdx.z;
     if (b < nfull) {
-        fb_tile<OUT_F32, FB_TN>(T, smem, W, X, dst, K, M, N, ne02, ne12, r2, r3, monte_seed, vec, peers, z,
-                                (b % gx) * FB_BM, (b / gx) * FB_BN);
+        fb_tile<OUT_F32, FB_TN, 1>(T, smem, gsm, threadIdx.x, rbase, 0, W, X, dst, K, M, N, ne02, ne12, r2, r3,
+                                   monte_seed, vec, peers, z, (b % gx) * FB_BM, (b / gx) * FB_BN);
     } else {
         const int64_t q = b - nfull, t = nfull + q / 4;
         const int64_t n0 = (t / gx) * FB_BN + (q % 4) * 8;
         if (n0 < N)
-            fb_tile<OUT_F32, 1>(T, smem, W, X, dst, K, M, N, ne02, ne12, r2, r3, monte_seed, vec, peers, z,
-                                (t % gx) * FB_BM, n0);
+            fb_tile<OUT_F32, 1, 1>(T, smem, gsm, threadIdx.x, rbase, 0, W, X, dst, K, M, N, ne02, ne12, r2, r3,
+                                   monte_seed, vec, peers, z, (t % gx) * FB_BM, n0);
+    }
+}
+
+// Base mode, one CTA per SM: four groups of FB_THREADS threads share four
+// replicas of the key table, chosen by lane & 3.  Replica r starts r words
+// past a multiple of 4 (mod 32: 0, 17, 2, 19), so the same-sign entries
+// (words 4n) of the four lane groups fall in four disjoint sets of 8 banks and
+// a warp's 32 random lookups spread over all 32 banks rather than crowding
+// into half of them.  Items (whole tiles; from nfull on, quarter tiles as in
+// k_mul_mat16_fast -- the launcher passes whole tiles only) are dealt to the
+// CTAs round-robin and taken in turn by each CTA's groups.
+constexpr int FB4_GROUPS = 4, FB4_THREADS = FB4_GROUPS * FB_THREADS;
+constexpr int FB4_OFF_GROUP = (4 * FB_REPL + 15) / 16 * 16;
+constexpr int FB_GROUP_BYTES = FB_SMEM - FB_OFF_WKEY;                 // one group's operand buffers
+constexpr int FB4_SMEM = FB4_OFF_GROUP + FB4_GROUPS * FB_GROUP_BYTES;
+
+template <bool OUT_F32>
+__global__ void __launch_bounds__(FB4_THREADS, 1)
+k_mul_mat16_fast4(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
+                  void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
+                  int64_t r2, int64_t r3, int vec, peer_out_dev peers, int64_t gx, int64_t nfull, int64_t nblk) {
+    pdl_entry();
+    extern __shared__ __align__(16) unsigned char smem[];
+    for (int i = threadIdx.x; i < k16_key_bytes / 4; i += FB4_THREADS) {
+        const int v = T.key16[i];
+#pragma unroll
+        for (int r = 0; r < 4; r++) reinterpret_cast<int *>(smem + r * FB_REPL)[i] = v;
+    }
+    __syncthreads();
+    const int g = threadIdx.x / FB_THREADS, tid = threadIdx.x % FB_THREADS;
+    const int rbase = (threadIdx.x & 3) * FB_REPL;
+    unsigned char * gsm = smem + FB4_OFF_GROUP + g * FB_GROUP_BYTES;
+    const int64_t z = blockIdx.z;
+    for (int64_t b = blockIdx.x + (int64_t) g * gridDim.x; b < nblk; b += (int64_t) FB4_GROUPS * gridDim.x) {
+        if (b < nfull) {
+            fb_tile<OUT_F32, FB_TN, FB4_GROUPS>(T, smem, gsm, tid, rbase, 1 + g, W, X, dst, K, M, N, ne02, ne12, r2,
+                                                r3, 0u, vec, peers, z, (b % gx) * FB_BM, (b / gx) * FB_BN);
+        } else {
+            const int64_t q = b - nfull, t = nfull + q / 4;
+            const int64_t n0 = (t / gx) * FB_BN + (q % 4) * 8;
+            if (n0 < N)
+                fb_tile<OUT_F32, 1, FB4_GROUPS>(T, smem, gsm, tid, rbase, 1 + g, W, X, dst, K, M, N, ne02, ne12, r2,
+                                                r3, 0u, vec, peers, z, (t % gx) * FB_BM, n0);
+        }
+        fb_sync<FB4_GROUPS>(1 + g);                     // the group's buffers are reused by its next item
     }
 }
 
@@ -2569,6 +2627,24 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         if (nblk > 0x7FFFFFFF) return LNSB_E_TOO_LARGE;
         const dim3 grid((unsigned) nblk, 1u, (unsigned) nz);
         const bool vec = a->M % FB_BM == 0 && a->K % 8 == 0 && ((uintptr_t) a->w % 16) == 0 && ((uintptr_t) a->x % 16) == 0;
+        if (k_mode == M_BASE && peers == nullptr) {
+            // four groups per SM over four table replicas, whole tiles only: a
+            // quarter tile's four chains per thread hide the table latency
+            // worse than the balance they buy is worth (measured)
+            const int64_t nfull4 = nt, nblk4 = nt;
+            if (nblk4 > 0x7FFFFFFF) return LNSB_E_TOO_LARGE;
+            static bool f4attr[k_max_devices][2] = {};
+            auto kern4 = out_f32 ? k_mul_mat16_fast4<true> : k_mul_mat16_fast4<false>;
+            if (!f4attr[dev0][out_f32]) {
+                const cudaError_t e = cudaFuncSetAttribute(kern4, cudaFuncAttributeMaxDynamicSharedMemorySize, FB4_SMEM);
+                if (e != cudaSuccess) return (int) e;
+                f4attr[dev0][out_f32] = true;
+            }
+            launch_k(kern4, dim3((unsigned) imin64(sms, nblk4), 1u, (unsigned) nz), FB4_THREADS, FB4_SMEM, stream, *T,
+                     static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N,
+                     a->ne02, a->ne12, r2, r3, vec ? 1 : 0, no_peers, gx, nfull4, nblk4);
+            return launch_status();
+        }
         static bool fattr[k_max_devices][2] = {};
         auto kern = out_f32 ? k_mul_mat16_fast<true> : k_mul_mat16_fast<false>;
         int dev = 0;
