@@ -136,6 +136,26 @@ def test_mul_mat16_special_codes(orc, ks16):
     assert np.array_equal(got, want)
 
 
+def test_mul_mat16_tiled_slices_ragged(orc, ks16):
+    """Enough outputs for the tiled kernels (base: the four-group kernel) with
+    two activation slices over one weight slice, M not a multiple of the
+    64-row tile and K not a multiple of 8 (the unaligned staging path),
+    scattered special codes, codes and F32 out."""
+    rng = np.random.default_rng(29)
+    ne02, ne03, ne12, ne13 = 1, 1, 2, 1
+    M, K, N = 1000, 70, 600
+    w = codes16(orc, rng, (ne03, ne02, M, K), 0.02)
+    x = codes16(orc, rng, (ne13, ne12, N, K), 1.0)
+    specials = np.array([0x0000, 0x8000, 0x7FFF, 0xFFFF, 0x4000, 0xC000], np.uint16)
+    w.ravel()[rng.integers(0, w.size, 50)] = rng.choice(specials, 50)
+    x.ravel()[rng.integers(0, x.size, 50)] = rng.choice(specials, 50)
+    sl = (ne02, ne03, ne12, ne13)
+    want = orc.mul_mat16(ks16.mode, w, x, slices=sl, seed=41, nthreads=NT).ravel()
+    assert np.array_equal(run_mm16(ks16, w, x, slices=sl, seed=41), want)
+    got = run_mm16(ks16, w, x, slices=sl, seed=41, f32=True)
+    assert np.array_equal(got.view(np.uint32), orc.to_f32_16(want).view(np.uint32))
+
+
 @pytest.mark.parametrize("where", ["early", "late", "none"])
 @pytest.mark.parametrize("M,K,N", [(128, 300, 40), (1024, 100, 640)])
 def test_mul_mat16_range_fallback(orc, ks16, where, M, K, N):

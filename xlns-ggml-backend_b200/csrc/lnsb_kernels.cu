@@ -889,28 +889,32 @@ k_mul_mat16_fast(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
     }
 }
 
-// Base mode, one CTA per SM: four groups of FB_THREADS threads share four
-// replicas of the key table, chosen by lane & 3.  Replica r starts r words
-// past a multiple of 4 (mod 32: 0, 17, 2, 19), so the same-sign entries
-// (words 4n) of the four lane groups fall in four disjoint sets of 8 banks and
-// a warp's 32 random lookups spread over all 32 banks rather than crowding
-// into half of them.  Items (whole tiles; from nfull on, quarter tiles as in
-// k_mul_mat16_fast -- the launcher passes whole tiles only) are dealt to the
-// CTAs round-robin and taken in turn by each CTA's groups.
-constexpr int FB4_GROUPS = 4, FB4_THREADS = FB4_GROUPS * FB_THREADS;
+// One CTA per SM: FB4_GROUPS groups of FB_THREADS threads share
+// four replicas of the key table, chosen by lane & 3.  Replica r starts r
+// words past a multiple of 4 (0, 17, 2, 19 mod 32),
+// so the same-sign entries (words 4n) of the four lane groups fall in four
+// disjoint sets of 8 banks and a warp's 32 random lookups spread over all 32
+// banks rather than crowding into half of them.  Items (whole tiles; from
+// nfull on, quarter tiles as in k_mul_mat16_fast) are dealt to the CTAs
+// round-robin and taken in turn by each CTA's groups.
 constexpr int FB4_OFF_GROUP = (4 * FB_REPL + 15) / 16 * 16;
 constexpr int FB_GROUP_BYTES = FB_SMEM - FB_OFF_WKEY;                 // one group's operand buffers
+constexpr int FB4_GROUPS = FB_MONTE ? 2 : 4;                          // as many as fit beside the replicas
+                                                                      // (the launcher uses it for base only)
+constexpr int FB4_THREADS = FB4_GROUPS * FB_THREADS;
 constexpr int FB4_SMEM = FB4_OFF_GROUP + FB4_GROUPS * FB_GROUP_BYTES;
 
 template <bool OUT_F32>
 __global__ void __launch_bounds__(FB4_THREADS, 1)
 k_mul_mat16_fast4(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
                   void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
-                  int64_t r2, int64_t r3, int vec, peer_out_dev peers, int64_t gx, int64_t nfull, int64_t nblk) {
+                  int64_t r2, int64_t r3, uint32_t monte_seed, int vec, peer_out_dev peers, int64_t gx,
+                  int64_t nfull, int64_t nblk) {
     pdl_entry();
     extern __shared__ __align__(16) unsigned char smem[];
-    for (int i = threadIdx.x; i < k16_key_bytes / 4; i += FB4_THREADS) {
-        const int v = T.key16[i];
+    const int32_t * keytab = FB_MONTE ? T.mkey16 : T.key16;
+    for (int i = threadIdx.x; i < FB_KEYB / 4; i += FB4_THREADS) {
+        const int v = keytab[i];
 #pragma unroll
         for (int r = 0; r < 4; r++) reinterpret_cast<int *>(smem + r * FB_REPL)[i] = v;
     }
@@ -922,13 +926,13 @@ k_mul_mat16_fast4(dev_tables T, const uint16_t * __restrict__ W, const uint16_t 
     for (int64_t b = blockIdx.x + (int64_t) g * gridDim.x; b < nblk; b += (int64_t) FB4_GROUPS * gridDim.x) {
         if (b < nfull) {
             fb_tile<OUT_F32, FB_TN, FB4_GROUPS>(T, smem, gsm, tid, rbase, 1 + g, W, X, dst, K, M, N, ne02, ne12, r2,
-                                                r3, 0u, vec, peers, z, (b % gx) * FB_BM, (b / gx) * FB_BN);
+                                                r3, monte_seed, vec, peers, z, (b % gx) * FB_BM, (b / gx) * FB_BN);
         } else {
             const int64_t q = b - nfull, t = nfull + q / 4;
             const int64_t n0 = (t / gx) * FB_BN + (q % 4) * 8;
             if (n0 < N)
                 fb_tile<OUT_F32, 1, FB4_GROUPS>(T, smem, gsm, tid, rbase, 1 + g, W, X, dst, K, M, N, ne02, ne12, r2,
-                                                r3, 0u, vec, peers, z, (t % gx) * FB_BM, n0);
+                                                r3, monte_seed, vec, peers, z, (t % gx) * FB_BM, n0);
         }
         fb_sync<FB4_GROUPS>(1 + g);                     // the group's buffers are reused by its next item
     }
@@ -2627,11 +2631,13 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         if (nblk > 0x7FFFFFFF) return LNSB_E_TOO_LARGE;
         const dim3 grid((unsigned) nblk, 1u, (unsigned) nz);
         const bool vec = a->M % FB_BM == 0 && a->K % 8 == 0 && ((uintptr_t) a->w % 16) == 0 && ((uintptr_t) a->x % 16) == 0;
-        if (k_mode == M_BASE && peers == nullptr) {
-            // four groups per SM over four table replicas, whole tiles only: a
-            // quarter tile's four chains per thread hide the table latency
-            // worse than the balance they buy is worth (measured)
-            const int64_t nfull4 = nt, nblk4 = nt;
+        if (peers == nullptr && !FB_MONTE) {
+            // base: one CTA per SM over four table replicas, whole tiles only --
+            // a quarter tile's four chains per thread hide the table latency
+            // worse than the balance they buy is worth (measured).  The Monte
+            // build measured slower on it (two groups: 1164 against 1188-1199
+            // G-LNSadd/s on configs[1]) and keeps the two-replica kernel.
+            const int64_t nfull4 = (FB_MONTE && nz == 1) ? nt / sms * sms : nt, nblk4 = nfull4 + 4 * (nt - nfull4);
             if (nblk4 > 0x7FFFFFFF) return LNSB_E_TOO_LARGE;
             static bool f4attr[k_max_devices][2] = {};
             auto kern4 = out_f32 ? k_mul_mat16_fast4<true> : k_mul_mat16_fast4<false>;
@@ -2642,7 +2648,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
             }
             launch_k(kern4, dim3((unsigned) imin64(sms, nblk4), 1u, (unsigned) nz), FB4_THREADS, FB4_SMEM, stream, *T,
                      static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N,
-                     a->ne02, a->ne12, r2, r3, vec ? 1 : 0, no_peers, gx, nfull4, nblk4);
+                     a->ne02, a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0, no_peers, gx, nfull4, nblk4);
             return launch_status();
         }
         static bool fattr[k_max_devices][2] = {};
