@@ -460,6 +460,7 @@ def run_ours(args, wl):
         # the rows beside the path: MUL_MAT_ID and the typed weight decode
         line["mul_mat_id"] = time_mul_mat_id(lnsb200, torch, np, args, flush, stream, int_peak)
         line["weights"] = time_weights(lnsb200, torch, np, args, flush, stream, hbm)
+        line["normalisers"] = time_norms(lnsb200, torch, np, args, flush, stream)
     if args.workload == "configs1" and not args.no_decode:
         # the metric's second half: model decode tok/s, one sequence per GPU
         line["decode"] = run_decode(torch, dist, rank, world, args, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
@@ -510,6 +511,64 @@ def time_secondary(lib, lnsb200, torch, np, wl, args, flush, stream):
             "value": adds / (ms / 1000) / 1e9, "unit": UNIT,
             "bound": "chain latency: %d dependent additions per output" % (K - 1),
             "l2": "flushed (256 MB write) before every timed step"}
+
+
+def time_norms(lnsb200, torch, np, args, flush, stream):
+    """BASELINE configs[1]'s normalisers on xlns16 codes, device-timed, L2
+    flushed before every step: soft_max over logits N(0, 3) shaped [9 heads]
+    [512 queries][512 keys] with a causal mask (keys after the query are
+    -inf) and scale 1.0 (4,608 rows x 511 additions, masked zeros included),
+    and rms_norm over 512 rows of 576 N(0, 1) values, eps 1e-5 (576 additions
+    per row); inputs numpy default_rng(1), converted to codes on the device."""
+    ks = lnsb200.KernelSet(16, args.mode)
+    lib = ks.lib
+    rng = np.random.default_rng(1)
+    n, q, h = 512, 512, 9
+    logits = torch.from_numpy(rng.normal(0, 3, (h, q, n)).astype(np.float32)).cuda()
+    sm_src = torch.empty(h * q * n, dtype=torch.int16, device="cuda")
+    ks.to_lns(logits.view(-1), sm_src)
+    mask_np = np.zeros((q, n), np.uint16)
+    mask_np[np.triu_indices(q, 1, n)] = 0xFFFF                       # xlns16 -inf after the query
+    mask = torch.from_numpy(mask_np.view(np.int16)).cuda()
+    sm_dst = torch.empty_like(sm_src)
+    sm_work = torch.empty_like(sm_src)
+    rows, cols = 512, 576
+    x = torch.from_numpy(rng.normal(0, 1, (rows, cols)).astype(np.float32)).cuda()
+    rn_src = torch.empty(rows * cols, dtype=torch.int16, device="cuda")
+    ks.to_lns(x.view(-1), rn_src)
+    rn_dst = torch.empty_like(rn_src)
+    ne = (ctypes.c_int64 * 4)(n, q, h, 1)
+    mne = (ctypes.c_int64 * 4)(n, q, 1, 1)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())                        # noqa: E731
+    calls = {
+        "soft_max": (lambda: lib.lnsb_soft_max_lns(16, P(sm_src), ne, P(mask), mne, 0x4000, P(sm_dst), P(sm_work), 7, sp),
+                     h * q * (n - 1), "chain latency: %d dependent additions per row, %d rows" % (n - 1, h * q),
+                     "[9][512][512] xlns16 logits N(0,3), causal mask, scale 1.0"),
+        "rms_norm": (lambda: lib.lnsb_rms_norm_lns(16, P(rn_src), P(rn_dst), cols, rows, ctypes.c_float(1e-5), 7, sp),
+                     rows * cols, "chain latency: %d dependent additions per row, %d rows" % (cols, rows),
+                     "512 x 576 xlns16 values N(0,1), eps 1e-5"),
+    }
+    out = {}
+    steps = max(args.steps, 20)
+    for name, (call, adds, bound, what) in calls.items():
+        for _ in range(args.warmup):
+            flush.zero_()
+            if call() != 0:
+                raise RuntimeError("lnsb_%s_lns failed" % name)
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            call()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        ms = sum(b.elapsed_time(e) for b, e in ev) / steps
+        out[name] = {"workload": "BASELINE configs[1] %s: %s" % (name, what), "mode": args.mode, "steps": steps,
+                     "ms_per_step": ms, "value": adds / (ms / 1000) / 1e9, "unit": UNIT, "adds": adds, "bound": bound,
+                     "l2": "flushed (256 MB write) before every timed step"}
+    return out
 
 
 def time_mul_mat_id(lnsb200, torch, np, args, flush, stream, int_peak):

@@ -1785,6 +1785,15 @@ constexpr int  NN_TAB  = k_mode == M_SUM32 ? k32f_sb_bytes16 : 0;   // sb knot b
 // xlns32 normalisers: always the non-negative chain over the sb knots, 4-byte terms
 template <int FMT> __host__ __device__ constexpr int nn_tab() { return FMT == 32 ? k32f_sb_bytes16 : NN_TAB; }
 template <int FMT> __host__ __device__ constexpr int nn_term_bytes() { return FMT == 32 ? 4 : 2; }
+// Row pitch (terms) of a normaliser block's shared terms: each lane runs one
+// row's chain, so the rows must start in different banks -- an odd number of
+// words apart (a pitch of n itself puts every lane of a 512- or 576-term row
+// in one bank: a 32-way conflict on every step).
+__host__ __device__ inline int64_t nn_pitch(int64_t n, int term_bytes) {
+    if (term_bytes == 4) return n | 1;
+    int64_t p = (n + 1) & ~(int64_t) 1;
+    return ((p >> 1) & 1) ? p : p + 2;
+}
 
 // the sb knots of the flat xlns32 image (all a non-negative chain reads) into
 // shared memory, asynchronously (committed with the block's other copies)
@@ -1846,6 +1855,7 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
         cp_async_wait<0>();
         __syncthreads();
     }
+    const int64_t P = nn_pitch(ncols, nn_term_bytes<FMT>());   // row pitch of the squares
     if (NN) {
         for (int64_t e = threadIdx.x; e < nr * ncols; e += blockDim.x) {
             uint32_t v;
@@ -1856,8 +1866,10 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
             } else {
                 v = load(row0 * ncols + e);
             }
-            if constexpr (FMT == 16) sq[e] = (uint16_t) mul16(v, v);
-            else                     sq32[e] = mul32(v, v);
+            const int r = (int) e / (int) ncols;         // nr * ncols fits the block's shared memory
+            const int64_t o = r * P + ((int) e - r * (int) ncols);
+            if constexpr (FMT == 16) sq[o] = (uint16_t) mul16(v, v);
+            else                     sq32[o] = mul32(v, v);
         }
     }
     cp_async_commit();
@@ -1866,13 +1878,13 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
     if (threadIdx.x < nr) {
         const int64_t row = row0 + threadIdx.x;
         if (NN && FMT == 32) {
-            const uint32_t * q = sq32 + threadIdx.x * ncols;
+            const uint32_t * q = sq32 + threadIdx.x * P;
             uint32_t acc = 0u;
             for (int64_t i = 0; i < ncols; i++) acc = padd32f(dyn, acc, q[i]);
             const uint32_t mean = mul32(acc, inv_n);
             s_inv[threadIdx.x] = recip32(sqrt32(add32(T, mean, eps_l)));
         } else if (NN) {
-            const uint16_t * q = sq + threadIdx.x * ncols;
+            const uint16_t * q = sq + threadIdx.x * P;
             uint32_t acc = 0u;                              // the zero code (acc32 0 in sum32)
             for (int64_t i = 0; i < ncols; i++) acc = nn_add(dyn, tab, acc, q[i]);
             red16 R{ &T, tab, fine };
@@ -1935,12 +1947,13 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
 }
 
 // ============================ SOFT_MAX =====================================
-// Block = 32 rows, 128 threads.  Pass 1 (whole block): scale, mask, row max;
+// Block = up to 32 rows, SM_THREADS threads.  Pass 1 (whole block): scale, mask, row max;
 // pass 2 (whole block): c = exp(v - max) into the work buffer; pass 3 (one
 // lane per row): the normaliser chain over c in element order; pass 4 (whole
 // block): dst = c / total.
+constexpr int SM_THREADS = 512;
 template <int FMT, bool IO_F32>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(SM_THREADS)
 k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const void * __restrict__ mask,
            lnsb_shape4 ms, uint32_t scale_l, void * __restrict__ dst, void * __restrict__ work,
            uint32_t monte_seed, int rpb, int nn_ok) {
@@ -1961,7 +1974,7 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     const int64_t nrows = s.ne[1] * s.ne[2] * s.ne[3];
     const int64_t row0 = (int64_t) blockIdx.x * rpb;
     const int64_t nr = imin64(rpb, nrows - row0);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
 
     auto ld = [&](const void * p, int64_t idx) -> uint32_t {
         return FMT == 16 ? (uint32_t) static_cast<const uint16_t *>(p)[idx] : static_cast<const uint32_t *>(p)[idx];
@@ -1993,8 +2006,8 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         return v;
     };
 
-    // pass 1: row max (each warp takes rows warp, warp + 4, ...)
-    for (int r = warp; r < nr; r += 4) {
+    // pass 1: row max (each warp takes rows warp, warp + nw, ...)
+    for (int r = warp; r < nr; r += nw) {
         const int64_t row = row0 + r;
         uint32_t mx = NEG_INF;
         for (int64_t i = lane; i < n; i += 32) {
@@ -2012,7 +2025,8 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     // pass 2: c = exp(v - max) into work (and, for the non-negative chain, shared memory)
     uint16_t * cs   = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
     uint32_t * cs32 = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
-    for (int r = warp; r < nr; r += 4) {
+    const int64_t P = nn_pitch(n, nn_term_bytes<FMT>());       // row pitch of the shared terms
+    for (int r = warp; r < nr; r += nw) {
         const int64_t row = row0 + r;
         const uint32_t mx = s_max[r][0];
         for (int64_t i = lane; i < n; i += 32) {
@@ -2020,11 +2034,11 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
             if constexpr (FMT == 16) {
                 const uint16_t e = __ldg(T.exp16 + sub16(v, mx, tab));
                 static_cast<uint16_t *>(work)[row * n + i] = e;
-                if (NN) cs[r * n + i] = e;
+                if (NN) cs[r * P + i] = e;
             } else {
                 const uint32_t e = exp32(T, sub32(T, v, mx));
                 static_cast<uint32_t *>(work)[row * n + i] = e;
-                if (NN) cs32[r * n + i] = e;
+                if (NN) cs32[r * P + i] = e;
             }
         }
     }
@@ -2034,12 +2048,12 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         const int64_t row = row0 + threadIdx.x;
         const void * c = work;
         if (NN && FMT == 32) {
-            const uint32_t * q = cs32 + threadIdx.x * n;
+            const uint32_t * q = cs32 + threadIdx.x * P;
             uint32_t acc = q[0];
             for (int64_t i = 1; i < n; i++) acc = padd32f(dyn, acc, q[i]);
             s_tot[threadIdx.x] = acc;
         } else if (NN) {
-            const uint16_t * q = cs + threadIdx.x * n;
+            const uint16_t * q = cs + threadIdx.x * P;
             red16 R{ &T, tab, fine };
             uint32_t acc = R.from(q[0]);
             for (int64_t i = 1; i < n; i++) acc = nn_add(dyn, tab, acc, q[i]);
@@ -2058,7 +2072,7 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     }
     __syncthreads();
     // pass 4: dst = c / total
-    for (int r = warp; r < nr; r += 4) {
+    for (int r = warp; r < nr; r += nw) {
         const int64_t row = row0 + r;
         const uint32_t tot = s_tot[r];
         for (int64_t i = lane; i < n; i += 32) {
@@ -2737,26 +2751,29 @@ int rms_norm_impl(int fmt, const void * src, void * dst, int64_t ncols, int64_t 
     if (fmt == LNSB_XLNS32 || NNCHAIN) {
         const int tabb = fmt == LNSB_XLNS32 ? nn_tab<32>() : nn_tab<16>();
         const int tb   = fmt == LNSB_XLNS32 ? 4 : 2;
-        const int64_t fit = (NN_SMEM_MAX - tabb) / (ncols * tb);
+        const int64_t fit = (NN_SMEM_MAX - tabb) / (nn_pitch(ncols, tb) * tb);
         if (fit >= 1) {
             rpb = (int) imin64(32, fit);
             nn_ok = 1;
-            dsmem = tabb + (int) (((int64_t) rpb * ncols * tb + 15) / 16 * 16);
+            dsmem = tabb + (int) (((int64_t) rpb * nn_pitch(ncols, tb) * tb + 15) / 16 * 16);
         }
     }
-    // the fused block does more per element (the residual add, the weight, two
-    // conversions): rows over more blocks, 256 threads each
-    if (fuse) rpb = (int) imin64(rpb, imin64(32, (nrows + 2 * 148 - 1) / (2 * 148)));
+    // rows over about two blocks per SM, 256 threads each: the element passes
+    // (and the fused block's residual add, weight and conversions) are latency
+    // bound, so more blocks with fewer rows each finish sooner
+    rpb = (int) imin64(rpb, imin64(32, (nrows + 2 * 148 - 1) / (2 * 148)));
     if (rpb < 1) rpb = 1;
-    if (fuse && nn_ok) dsmem = (fmt == LNSB_XLNS32 ? nn_tab<32>() : nn_tab<16>()) +
-                               (int) (((int64_t) rpb * ncols * (fmt == LNSB_XLNS32 ? 4 : 2) + 15) / 16 * 16);
+    if (nn_ok) {
+        const int tb = fmt == LNSB_XLNS32 ? 4 : 2;
+        dsmem = (fmt == LNSB_XLNS32 ? nn_tab<32>() : nn_tab<16>()) + (int) (((int64_t) rpb * nn_pitch(ncols, tb) * tb + 15) / 16 * 16);
+    }
     const unsigned blocks = (unsigned) ((nrows + rpb - 1) / rpb);
     auto kern = fuse ? (fmt == LNSB_XLNS16 ? k_rms_norm<16, true, true> : k_rms_norm<32, true, true>)
                      : fmt == LNSB_XLNS16 ? (io_f32 ? k_rms_norm<16, true> : k_rms_norm<16, false>)
                                           : (io_f32 ? k_rms_norm<32, true> : k_rms_norm<32, false>);
     const int st2 = nn_smem_attr((const void *) kern, dsmem);
     if (st2 != 0) return st2;
-    launch_k(kern, blocks, fuse ? 256 : 128, dsmem, stream, *T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, nn_ok, res,
+    launch_k(kern, blocks, 256, dsmem, stream, *T, src, dst, ncols, nrows, eps_l, inv_n, seed, rpb, nn_ok, res,
              x_out, nw);
     return launch_status();
 }
@@ -2776,15 +2793,21 @@ int soft_max_impl(int fmt, const void * src, lnsb_shape4 s, const void * mask, l
     const dev_tables * T = nullptr;
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
-    int rpb = 32, nn_ok = 0, dsmem = 0;
+    // rows over about two blocks per SM: a block's element passes are latency
+    // bound, so more blocks with fewer rows each finish sooner (each row's
+    // chain is one lane whatever the split)
+    int dev = 0;
+    const int ds = current_device(&dev);
+    if (ds != 0) return ds;
+    int rpb = (int) imin64(32, (nrows + 2 * sm_count(dev) - 1) / (2 * sm_count(dev))), nn_ok = 0, dsmem = 0;
     if (fmt == LNSB_XLNS32 || NNCHAIN) {
         const int tabb = fmt == LNSB_XLNS32 ? nn_tab<32>() : nn_tab<16>();
         const int tb   = fmt == LNSB_XLNS32 ? 4 : 2;
-        const int64_t fit = (NN_SMEM_MAX - tabb) / (s.ne[0] * tb);
+        const int64_t fit = (NN_SMEM_MAX - tabb) / (nn_pitch(s.ne[0], tb) * tb);
         if (fit >= 1) {
-            rpb = (int) imin64(32, fit);
+            rpb = (int) imin64(rpb, fit);
             nn_ok = 1;
-            dsmem = tabb + (int) (((int64_t) rpb * s.ne[0] * tb + 15) / 16 * 16);
+            dsmem = tabb + (int) (((int64_t) rpb * nn_pitch(s.ne[0], tb) * tb + 15) / 16 * 16);
         }
     }
     const unsigned blocks = (unsigned) ((nrows + rpb - 1) / rpb);
@@ -2792,7 +2815,7 @@ int soft_max_impl(int fmt, const void * src, lnsb_shape4 s, const void * mask, l
                                    : (io_f32 ? k_soft_max<32, true> : k_soft_max<32, false>);
     const int st2 = nn_smem_attr((const void *) kern, dsmem);
     if (st2 != 0) return st2;
-    launch_k(kern, blocks, 128, dsmem, stream, *T, src, s, mask, ms, scale_l, dst, work, seed, rpb, nn_ok);
+    launch_k(kern, blocks, SM_THREADS, dsmem, stream, *T, src, s, mask, ms, scale_l, dst, work, seed, rpb, nn_ok);
     return launch_status();
 }
 
