@@ -29,11 +29,16 @@ def ks32():
     return k
 
 
-def run(ks, orc, fmt, n_expert, K, M, n_tokens, n_used, ne11, seed=7, bad_slot=None, f32=False):
+def run(ks, orc, fmt, n_expert, K, M, n_tokens, n_used, ne11, seed=7, bad_slot=None, f32=False, specials=False):
     rng = np.random.default_rng(K * 131 + M * 7 + n_tokens + n_used)
     tof = orc.from_f32_16 if fmt == 16 else orc.from_f32_32
     w_rows = tof(rng.normal(0, 0.02, (n_expert, M, K)).astype(np.float32))      # [e][m][k]
     x = tof(rng.normal(0, 1, (n_tokens, ne11, K)).astype(np.float32))
+    if specials:                                          # zeros, saturations, exact opposites along K
+        sp = np.array([0x0000, 0x8000, 0x7FFF, 0xFFFF, 0x0001], np.uint16)
+        w_rows.ravel()[rng.integers(0, w_rows.size, 200)] = rng.choice(sp, 200)
+        x.ravel()[rng.integers(0, x.size, 20)] = rng.choice(sp, 20)
+        x[0, 0, K // 2] = x[0, 0, K // 2 - 1] ^ 0x8000
     ids = rng.integers(0, n_expert, (n_tokens, n_used)).astype(np.int32)
     if n_tokens > 1:
         ids[1, :] = ids[0, 0]                               # one expert in every slot of a token
@@ -69,6 +74,14 @@ def run(ks, orc, fmt, n_expert, K, M, n_tokens, n_used, ne11, seed=7, bad_slot=N
 ])
 def test_mul_mat_id16(orc, ks16, n_expert, K, M, n_tokens, n_used, ne11):
     ok, bad_gpu, bad_orc = run(ks16, orc, 16, n_expert, K, M, n_tokens, n_used, ne11, seed=0xB403)
+    assert ok and bad_gpu == bad_orc == 0
+
+
+def test_mul_mat_id16_special_codes(orc, ks16):
+    """zeros, saturated codes and cancelling terms part-way along the chains:
+    in base mode they move a chain from the key form to packed codes and
+    back, bit-exact either way"""
+    ok, bad_gpu, bad_orc = run(ks16, orc, 16, 6, 300, 200, 4, 2, 1, seed=5, specials=True)
     assert ok and bad_gpu == bad_orc == 0
 
 

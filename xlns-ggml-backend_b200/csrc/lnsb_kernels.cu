@@ -1979,7 +1979,11 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     auto ld = [&](const void * p, int64_t idx) -> uint32_t {
         return FMT == 16 ? (uint32_t) static_cast<const uint16_t *>(p)[idx] : static_cast<const uint32_t *>(p)[idx];
     };
-    auto value = [&](int64_t row, int64_t i) -> uint32_t {   // scaled, masked logit
+    auto mask_row = [&](int64_t row) -> int64_t {           // the mask row a row reads (dims 2, 3 broadcast)
+        const int64_t i1 = row % s.ne[1], i2 = (row / s.ne[1]) % s.ne[2], i3 = row / (s.ne[1] * s.ne[2]);
+        return ((i3 % ms.ne[3]) * ms.ne[2] + i2 % ms.ne[2]) * ms.ne[1] + i1;
+    };
+    auto value = [&](int64_t row, int64_t mrow, int64_t i) -> uint32_t {   // scaled, masked logit
         uint32_t v;
         if constexpr (IO_F32) {
             const float f = static_cast<const float *>(src)[row * n + i];
@@ -1990,8 +1994,6 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         if (v != NEG_INF) {
             v = FMT == 16 ? mul16(v, scale_l) : mul32(v, scale_l);
             if (mask != nullptr) {
-                const int64_t i1 = row % s.ne[1], i2 = (row / s.ne[1]) % s.ne[2], i3 = row / (s.ne[1] * s.ne[2]);
-                const int64_t mrow = ((i3 % ms.ne[3]) * ms.ne[2] + i2 % ms.ne[2]) * ms.ne[1] + i1;
                 uint32_t mk;
                 if constexpr (IO_F32) {
                     const float mf = static_cast<const float *>(mask)[mrow * n + i];
@@ -2008,10 +2010,10 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
 
     // pass 1: row max (each warp takes rows warp, warp + nw, ...)
     for (int r = warp; r < nr; r += nw) {
-        const int64_t row = row0 + r;
+        const int64_t row = row0 + r, mrow = mask != nullptr ? mask_row(row) : 0;
         uint32_t mx = NEG_INF;
         for (int64_t i = lane; i < n; i += 32) {
-            const uint32_t v = value(row, i);
+            const uint32_t v = value(row, mrow, i);
             if (FMT == 16 ? gt16(v, mx) : gt32(v, mx)) mx = v;
         }
 #pragma unroll
@@ -2027,10 +2029,10 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     uint32_t * cs32 = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
     const int64_t P = nn_pitch(n, nn_term_bytes<FMT>());       // row pitch of the shared terms
     for (int r = warp; r < nr; r += nw) {
-        const int64_t row = row0 + r;
+        const int64_t row = row0 + r, mrow = mask != nullptr ? mask_row(row) : 0;
         const uint32_t mx = s_max[r][0];
         for (int64_t i = lane; i < n; i += 32) {
-            const uint32_t v = value(row, i);
+            const uint32_t v = value(row, mrow, i);
             if constexpr (FMT == 16) {
                 const uint16_t e = __ldg(T.exp16 + sub16(v, mx, tab));
                 static_cast<uint16_t *>(work)[row * n + i] = e;
