@@ -503,7 +503,7 @@ k_to_lns16_typed_tiled(dev_tables T, const unsigned char * __restrict__ src, int
 
 // ===================== MUL_MAT (xlns16, base mode, key form) ================
 //
-// The base-mode hot kernel.  Every chain carries its accumulator as a key
+// The base-mode (and Monte) tiled kernels.  Every chain carries its accumulator as a key
 // (lnsb_tables.h): key = 16 * log + 4 * sign.  One LNS addition of a
 // product p is then
 //     d   = |a - p|                 one signed difference gives n and the sign case
@@ -523,8 +523,12 @@ k_to_lns16_typed_tiled(dev_tables T, const unsigned char * __restrict__ src, int
 //
 // Tile: 64 weight rows x 32 tokens, 128 threads, 4 x 4 chains per thread;
 // K chunks of 32 staged with cp.async (double buffered) and converted to key
-// form once per chunk in shared memory; the 20 KB key table sits at shared
-// offset 0, so its byte index needs no address arithmetic.
+// form once per chunk in shared memory; the 20 KB key table replicas sit from
+// shared offset 0, so a byte index needs no address arithmetic beyond the
+// replica offset folded into its clamp.  k_mul_mat16_fast runs one tile body
+// per CTA with two replicas (the Monte build, and the peer-store gather);
+// k_mul_mat16_fast4 runs four tile bodies per CTA, one CTA per SM, over four
+// replicas (the base build).
 constexpr int FB_BM = 64, FB_BN = 32, FB_KC = 32, FB_TM = 4, FB_TN = 4;
 constexpr int FB_THREADS = (FB_BM / FB_TM) * (FB_BN / FB_TN);      // 128
 constexpr int FB_XP  = FB_KC + 8;                                  // x code pitch, halfwords
