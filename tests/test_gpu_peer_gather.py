@@ -48,3 +48,30 @@ def test_group_barrier_times_out_without_a_peer():
     st = ks.lib.lnsb_group_barrier(ctypes.c_void_p(ptrs.data_ptr()), 2, 0, 2, ctypes.c_void_p(err.data_ptr()), None)
     torch.cuda.synchronize()
     assert st == 0 and err.item() == 0
+
+
+@pytest.mark.parametrize("mode", ["base", "monte"])
+@pytest.mark.parametrize("K,M,N", [(576, 1536, 512), (70, 1000, 600)])
+def test_peer_store_on_one_gpu(orc, mode, K, M, N):
+    """the fused gather's stores without NVLink: two buffers on this GPU stand
+    for two ranks' gather buffers, this call is rank 1 of 2 (columns
+    [M, 2M) of rows of 2M codes); both must hold exactly lnsb_mul_mat_lns's
+    result there and keep their other columns"""
+    import numpy as np
+    import lnsb200
+    ks = lnsb200.KernelSet(16, mode)
+    ks.upload_tables()
+    rng = np.random.default_rng(K + M + N)
+    w = orc.from_f32_16(rng.normal(0, 0.02, (M, K)).astype(np.float32))
+    x = orc.from_f32_16(rng.normal(0, 1, (N, K)).astype(np.float32))
+    wd = torch.from_numpy(np.ascontiguousarray(w.T).view(np.int16)).cuda()
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    want = torch.empty(N * M, dtype=torch.int16, device="cuda")
+    ks.mul_mat_lns(wd, xd, want, K, M, N, monte_seed=11)
+    bufs = [torch.full((N, 2 * M), 0x1234, dtype=torch.int16, device="cuda") for _ in range(2)]
+    ptrs = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    ks.mul_mat_lns_peers(wd, xd, ptrs.data_ptr(), 2, 2 * M, M, K, M, N, monte_seed=11)
+    torch.cuda.synchronize()
+    for b in bufs:
+        assert torch.equal(b[:, M:].contiguous().view(-1), want)
+        assert bool((b[:, :M] == 0x1234).all())

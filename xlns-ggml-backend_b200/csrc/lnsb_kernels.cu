@@ -526,9 +526,9 @@ k_to_lns16_typed_tiled(dev_tables T, const unsigned char * __restrict__ src, int
 // form once per chunk in shared memory; the 20 KB key table replicas sit from
 // shared offset 0, so a byte index needs no address arithmetic beyond the
 // replica offset folded into its clamp.  k_mul_mat16_fast runs one tile body
-// per CTA with two replicas (the Monte build, and the peer-store gather);
-// k_mul_mat16_fast4 runs four tile bodies per CTA, one CTA per SM, over four
-// replicas (the base build).
+// per CTA with two replicas (the Monte build); k_mul_mat16_fast4 runs four
+// tile bodies per CTA, one CTA per SM, over four replicas (the base build,
+// the peer-store gather included).
 constexpr int FB_BM = 64, FB_BN = 32, FB_KC = 32, FB_TM = 4, FB_TN = 4;
 constexpr int FB_THREADS = (FB_BM / FB_TM) * (FB_BN / FB_TN);      // 128
 constexpr int FB_XP  = FB_KC + 8;                                  // x code pitch, halfwords
@@ -2651,7 +2651,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
         if (nblk > 0x7FFFFFFF) return LNSB_E_TOO_LARGE;
         const dim3 grid((unsigned) nblk, 1u, (unsigned) nz);
         const bool vec = a->M % FB_BM == 0 && a->K % 8 == 0 && ((uintptr_t) a->w % 16) == 0 && ((uintptr_t) a->x % 16) == 0;
-        if (peers == nullptr && !FB_MONTE) {
+        if (!FB_MONTE) {
             // base: one CTA per SM over four table replicas, whole tiles only --
             // a quarter tile's four chains per thread hide the table latency
             // worse than the balance they buy is worth (measured).  The Monte
@@ -2668,7 +2668,8 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
             }
             launch_k(kern4, dim3((unsigned) imin64(sms, nblk4), 1u, (unsigned) nz), FB4_THREADS, FB4_SMEM, stream, *T,
                      static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x), dst, a->K, a->M, a->N,
-                     a->ne02, a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0, no_peers, gx, nfull4, nblk4);
+                     a->ne02, a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0, peers ? *peers : no_peers, gx, nfull4,
+                     nblk4);
             return launch_status();
         }
         static bool fattr[k_max_devices][2] = {};
