@@ -470,6 +470,9 @@ def run_ours(args, wl):
                                               cpu=(rank == 0 and not args.no_cpu_baseline), fmt=32)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not strong:
         line["cpu_baseline"] = cpu_leg(wl, args.mode, 10.0, os.cpu_count() or 1)
+        # the reference's CPU backend runs one thread (its ops are sequential loops): the
+        # same port on one core, beside the all-cores figure
+        line["cpu_baseline"]["single_thread"] = cpu_leg(wl, args.mode, 5.0, 1)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:
