@@ -253,8 +253,7 @@ int lnsb_mul_mat_id_bad_ids(int64_t * count);
  * 468-599, 786-868, 1199-1281).  F32 in and out, as at every ggml op
  * boundary: each operand is converted to LNS (lnsb_to_lns's table), the op
  * runs in LNS, the result is written back as F32.  Contiguous tensors.
- * Unsupported combinations return LNSB_E_UNSUPPORTED: gelu, tanh and geglu
- * (their xlnscpp definitions are not pinned). */
+ * An op code outside the lists below returns LNSB_E_INVALID. */
 #define LNSB_BINARY_ADD 0
 #define LNSB_BINARY_MUL 1
 #define LNSB_BINARY_DIV 2
@@ -270,9 +269,15 @@ int lnsb_binary(int fmt, int op, const float * a, const int64_t ane[4], const fl
                 float * dst, lnsb_stream_t stream);
 /* dst = src * s, plus b when b != 0 (ggml_scale_bias) */
 int lnsb_scale(int fmt, const float * src, float * dst, int64_t n, float s, float b, lnsb_stream_t stream);
-/* silu(x) = x / (1 + exp(-x)) in LNS arithmetic (xlns32: exp through float, as in its softmax); relu */
+/* xlns16: silu(x) = x * sigmoid(x), sigmoid a 65536-entry table (the float
+ * 1 / (1 + e^-x) of each code, converted); tanh(x) = (e^2x - 1) / (e^2x + 1)
+ * and gelu(x) = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) in xlns16
+ * arithmetic over the exp table (lns-backend/cuda/lns-cuda-kernels.cuh:191-206,
+ * lns-ops.cpp:783-1000).  xlns32: silu in xlns32 arithmetic with exp through
+ * float; tanh and gelu evaluated in double precision and converted.  relu. */
 int lnsb_unary(int fmt, int op, const float * src, float * dst, int64_t n, lnsb_stream_t stream);
-/* dst[r][c] = act(gate[r * gate_stride + c]) * up[r * up_stride + c] */
+/* dst[r][c] = act(gate[r * gate_stride + c]) * up[r * up_stride + c], act =
+ * silu (LNSB_GLU_SWIGLU) or gelu (LNSB_GLU_GEGLU) as in lnsb_unary */
 int lnsb_glu(int fmt, int op, const float * gate, const float * up, int64_t gate_stride, int64_t up_stride,
              float * dst, int64_t ncols, int64_t nrows, lnsb_stream_t stream);
 

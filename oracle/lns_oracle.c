@@ -37,9 +37,10 @@
 static int      g_ready;
 static uint16_t g_sb16[X16_ESSZER + 1];      /* sb(-n), n = 0..1280            */
 static int16_t  g_db16[X16_ESSZER + 1];      /* db(-n) adjustment, n = 1..1280 */
-static uint16_t g_conv16[65536];             /* bf16 pattern -> xlns16         */
+static uint16_t g_conv16[65536];             /* |float| bits 30..15 -> log field */
 static float    g_dec16[65536];              /* xlns16 -> float                */
 static uint16_t g_exp16[65536];              /* xlns16 exp                     */
+static uint16_t g_sig16[65536];              /* xlns16 sigmoid                 */
 
 /*
  * Gaussian logarithms at F=7.  The reference adds through a table of the
@@ -63,69 +64,97 @@ static void build16(void) {
         }
     }
     /*
-     * float -> xlns16: a 65536-entry table indexed by the float's upper 16
-     * bits (README.md:75-76 "65536-entry lookup table"), each entry the
-     * truncating conversion (int)(log2|b| * 128) of that bfloat16 value b.
-     * Out-of-range logs saturate (|x| >= 2^128 -> 0x7FFF, below 2^-128 -> 0).
+     * float -> xlns16: a 65536-entry table (README.md:75-76 "65536-entry
+     * lookup table") indexed by the float's 8 exponent bits and its top 8
+     * mantissa bits, (bits >> 15) & 0xFFFF; the sign bit is copied, not
+     * looked up.  Each entry is the truncating conversion (int)(log2(b)*128)
+     * of the bucket's lower edge b = the float with those 16 bits and zeros
+     * below.  This is the construction that reproduces every figure of the
+     * reference's conversion statistics over 4 M log-uniform values
+     * (experiments/dot-product-scaling/results/convert.jsonl:1, protocol
+     * dot-bench.cpp:186-213): mean log2 error -2.07e-3, 63.4 % rounded down,
+     * rms relative error 3.54e-3, 49.4 % / 49.2 % of codes changed by a second /
+     * third round trip, each change exactly one ulp down.  Indexing by the
+     * bfloat16 pattern instead (7 mantissa bits) gives -4.2e-3 and 76 %.
+     * Out-of-range logs saturate (|x| >= 2^128 -> 0x7FFF, below 2^-128 -> 0,
+     * keeping the sign); zeros and NaNs whose top 8 mantissa bits are not all
+     * zero convert to the unsigned zero code, marked 0xFFFF in the table.
      */
     for (uint32_t i = 0; i < 65536; i++) {
-        uint32_t bits = i << 16;
-        float f;
-        memcpy(&f, &bits, 4);
-        uint16_t sign = (i & 0x8000u) ? X16_SIGNMASK : 0;
-        float a = fabsf(f);
+        uint32_t bits = i << 15;
+        float a;
+        memcpy(&a, &bits, 4);
         uint16_t code;
         if (a == 0.0f || a != a) {
-            code = X16_ZERO;
+            code = 0xFFFFu;                       /* unsigned zero */
         } else if (isinf(a)) {
-            code = (uint16_t)(sign | X16_LOGMASK);
+            code = X16_LOGMASK;
         } else {
             double l = log((double)a) / log(2.0) * 128.0;
             long t = (long)l;                     /* truncation toward zero */
             long c = t + (long)X16_OFFSET;
             if (c < 0) c = 0;
             if (c > (long)X16_LOGMASK) c = X16_LOGMASK;
-            code = (uint16_t)(sign | (uint16_t)c);
+            code = (uint16_t)c;
         }
         g_conv16[i] = code;
     }
     /*
-     * xlns16 -> float: 2^(l/128) held to 7 significant decimal digits, then
-     * rounded to float; zero log field -> 0.0f.  The reference's printed
-     * decodes carry that precision, not the correctly rounded float:
-     * 2^(491/128) prints as 14.280130 (results/sum32-evidence/
-     * unit-tests-lns16-base.txt:23, correctly rounded: 14.280133) and
-     * 2^(1355/128) as 1537.0380 (standalone-sum32-invariants.txt:9).
+     * xlns16 -> float: 2^(l/128) rounded to float, that float held to 7
+     * significant decimal digits, then rounded to float again; zero log field
+     * -> 0.0f.  The reference's decodes carry that precision, not the
+     * correctly rounded float: 2^(491/128) prints as 14.280130 (results/
+     * sum32-evidence/unit-tests-lns16-base.txt:23, correctly rounded:
+     * 14.280133) and 2^(1355/128) as 1537.0380 (standalone-sum32-
+     * invariants.txt:9).  Rounding to float before taking the 7 digits is
+     * what reproduces the reference's conversion statistics exactly
+     * (convert.jsonl:1: 28 of 4,194,304 values round-trip to themselves, 63.3988 %
+     * round down); taking the digits of the double gives 30 and 63.3989 %.  A
+     * float powf in place of the double pow gives the same statistics (116
+     * codes differ; the evidence does not decide between the two).
      */
     for (uint32_t c = 0; c < 65536; c++) {
         if ((c & X16_LOGMASK) == 0) {
             g_dec16[c] = 0.0f;
         } else {
-            double v = pow(2.0, (double)((int)(c & X16_LOGMASK) - (int)X16_OFFSET) / 128.0);
+            const float f = (float) pow(2.0, (double)((int)(c & X16_LOGMASK) - (int)X16_OFFSET) / 128.0);
             char buf[32];
-            snprintf(buf, sizeof buf, "%.7g", v);    /* 7 significant digits */
-            v = strtod(buf, NULL);
+            snprintf(buf, sizeof buf, "%.7g", (double) f);    /* 7 significant digits */
+            const double v = strtod(buf, NULL);
             g_dec16[c] = (float)((c & X16_SIGNMASK) ? -v : v);
         }
     }
-    /* exp as a 65536-entry table (docs/CUDA.md:138-140): the log of e^x is
-     * x log2(e), taken to F=7 by floor from the value's float, x =
-     * xlns162fp(c).  Pinned by the reference's swiglu printout
-     * (results/sum32-evidence/unit-tests-lns16-base.txt:44-63), which silu =
-     * x / (1 + exp(-x)) in xlns16 arithmetic reproduces to every digit with
-     * this rule and not with a float expf converted through fp2xlns16. */
+    /* exp as a 65536-entry table (docs/CUDA.md:138-140, "exp ... table
+     * lookups"): the log of e^x is x log2(e), taken to F=7 by truncation
+     * toward zero -- the same truncation as the conversion table -- from the
+     * code's float x = xlns162fp(c).  Pinned by the reference's softmax
+     * printouts (results/sum32-evidence/unit-tests-lns16-{base,sum32}.txt:
+     * short/long/scaled/masked/masked-scaled max abs error, all ten figures)
+     * and by its tanh and geglu printouts (unit-tests-lns16-base.txt:65-86),
+     * which go through exp; flooring instead misses four of those figures. */
     for (uint32_t c = 0; c < 65536; c++) {
-        long q = (long) floor((double) g_dec16[c] * 1.4426950408889634 * 128.0) + (long) X16_OFFSET;
+        long q = (long) ((double) g_dec16[c] * 1.4426950408889634 * 128.0) + (long) X16_OFFSET;
         if (q < 0) q = 0;
         if (q > (long) X16_LOGMASK) q = (long) X16_LOGMASK;
         g_exp16[c] = (uint16_t) q;
+    }
+    /* sigmoid as a 65536-entry table (docs/CUDA.md:138-140, "sigmoid ...
+     * table lookups"): entry c = fp2xlns16 of the float 1 / (1 + e^-x), x =
+     * xlns162fp(c), e^-x from this file's own float exp.  silu(x) = x *
+     * sigmoid(x) through it reproduces the reference's swiglu printout
+     * (unit-tests-lns16-base.txt:44-63) to every digit; x / (1 + exp(-x)) in
+     * xlns16 arithmetic misses one of the eight values. */
+    for (uint32_t c = 0; c < 65536; c++) {
+        const float x = g_dec16[c];
+        g_sig16[c] = orc16_from_f32(1.0f / (1.0f + orc_expf(-x)));
     }
 }
 
 uint16_t orc16_from_f32(float x) {
     uint32_t bits;
     memcpy(&bits, &x, 4);
-    return g_conv16[bits >> 16];
+    uint16_t m = g_conv16[(bits >> 15) & 0xFFFFu];
+    return m == 0xFFFFu ? (uint16_t)X16_ZERO : (uint16_t)(m | ((bits >> 16) & X16_SIGNMASK));
 }
 
 float orc16_to_f32(uint16_t v) { return g_dec16[v]; }
@@ -865,9 +894,23 @@ int orc_init(void) {
 /* the op runs in xlns16 and the result is written back with xlns162fp.   */
 /* ===================================================================== */
 
-/* silu(x) = x / (1 + exp(-x)) in xlns16 arithmetic (see the exp table) */
-uint16_t orc16_silu(uint16_t x) {
-    return orc16_div(x, orc16_add((uint16_t) X16_OFFSET, orc16_exp((uint16_t) (x ^ X16_SIGNMASK))));
+/* silu(x) = x * sigmoid(x), the sigmoid from its table (see build16) */
+uint16_t orc16_silu(uint16_t x) { return orc16_mul(x, g_sig16[x]); }
+/* tanh(x) = (e^2x - 1) / (e^2x + 1) in xlns16 arithmetic over the exp table;
+ * reproduces the reference's tanh printout (unit-tests-lns16-base.txt:86),
+ * including tanh(-0.01) = -0.008158 */
+uint16_t orc16_tanh(uint16_t x) {
+    const uint16_t e = orc16_exp(orc16_mul(x, (uint16_t) (X16_OFFSET + 128)));
+    return orc16_div(orc16_sub(e, (uint16_t) X16_OFFSET), orc16_add(e, (uint16_t) X16_OFFSET));
+}
+/* gelu(x) = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), ggml's tanh
+ * form, in xlns16 arithmetic with the constants converted by fp2xlns16;
+ * reproduces the reference's geglu printout (unit-tests-lns16-base.txt:65-84) */
+uint16_t orc16_gelu(uint16_t x) {
+    const uint16_t s = orc16_from_f32(0.79788456080286535588f), a = orc16_from_f32(0.044715f), h = orc16_from_f32(0.5f);
+    const uint16_t x3 = orc16_mul(orc16_mul(x, x), x);
+    const uint16_t in = orc16_mul(s, orc16_add(x, orc16_mul(a, x3)));
+    return orc16_mul(orc16_mul(h, x), orc16_add((uint16_t) X16_OFFSET, orc16_tanh(in)));
 }
 /* relu(x): x where x > 0, else the zero code */
 uint16_t orc16_relu(uint16_t x) {
@@ -905,7 +948,8 @@ void orc16_scale_f32(const float * src, float * dst, int64_t n, float s, float b
 void orc16_unary_f32(int op, const float * src, float * dst, int64_t n) {
     for (int64_t i = 0; i < n; i++) {
         const uint16_t v = f2c(src[i]);
-        dst[i] = c2f(op == ORC_SILU ? orc16_silu(v) : orc16_relu(v));
+        dst[i] = c2f(op == ORC_SILU ? orc16_silu(v) : op == ORC_GELU ? orc16_gelu(v) : op == ORC_TANH ? orc16_tanh(v)
+                                                                                             : orc16_relu(v));
     }
 }
 
@@ -914,6 +958,13 @@ void orc16_swiglu_f32(const float * gate, const float * up, int64_t gs, int64_t 
     for (int64_t r = 0; r < nr; r++)
         for (int64_t c = 0; c < nc; c++)
             dst[r * nc + c] = c2f(orc16_mul(orc16_silu(f2c(gate[r * gs + c])), f2c(up[r * us + c])));
+}
+
+/* dst[r][c] = gelu(gate[r*gs + c]) * up[r*us + c] (lns_geglu, lns-ops.cpp:865-918) */
+void orc16_geglu_f32(const float * gate, const float * up, int64_t gs, int64_t us, float * dst, int64_t nc, int64_t nr) {
+    for (int64_t r = 0; r < nr; r++)
+        for (int64_t c = 0; c < nc; c++)
+            dst[r * nc + c] = c2f(orc16_mul(orc16_gelu(f2c(gate[r * gs + c])), f2c(up[r * us + c])));
 }
 
 /* rotary embedding of rows of ne[0] (lns_rope): pairs (2j, 2j+1), or (j, j +
@@ -947,6 +998,41 @@ uint32_t orc32_silu(uint32_t x) {
 static inline uint32_t f2c32(float f) { return orc32_from_f32(f); }
 static inline float c2f32(uint32_t c) { return orc32_to_f32(c); }
 
+/* e^x in double: the same range reduction and degree-14 Taylor series as
+ * orc_expf, without the float rounding; |x| clamped to 700 */
+double orc_exp_d(double xd) {
+    if (xd != xd) return xd;
+    if (xd > 700.0) xd = 700.0;
+    if (xd < -700.0) xd = -700.0;
+    const double t = xd * 1.4426950408889634074;
+    const double n = nearbyint(t);
+    const double r = (t - n) * 0.69314718055994530942;
+    static const double c[15] = {
+        1.0, 1.0, 1.0 / 2, 1.0 / 6, 1.0 / 24, 1.0 / 120, 1.0 / 720, 1.0 / 5040, 1.0 / 40320,
+        1.0 / 362880, 1.0 / 3628800, 1.0 / 39916800, 1.0 / 479001600, 1.0 / 6227020800.0,
+        1.0 / 87178291200.0 };
+    double p = c[14];
+    for (int i = 13; i >= 0; i--) p = fma(p, r, c[i]);
+    return ldexp(p, (int)n);
+}
+/* tanh(y) = (e^2y - 1) / (e^2y + 1) in double */
+double orc_tanh_d(double y) {
+    const double e = orc_exp_d(2.0 * y);
+    return (e - 1.0) / (e + 1.0);
+}
+/* xlns32 tanh and gelu go through floating point, as xlns32's activations do
+ * in the reference (docs/CUDA.md:159-166: float tanhf there; this build's
+ * own double tanh, identical on host and device, so the GPU is bit-exact).
+ * Both reproduce the reference's LNS32 tanh and geglu printouts
+ * (results/sum32-evidence/unit-tests-lns32.txt); gelu in xlns32 arithmetic
+ * misses one geglu digit. */
+uint32_t orc32_tanh(uint32_t x) { return orc32_from_f32((float) orc_tanh_d((double) orc32_to_f32(x))); }
+uint32_t orc32_gelu(uint32_t x) {
+    const double d = (double) orc32_to_f32(x);
+    const double u = 0.79788456080286535588 * (d + 0.044715 * d * d * d);
+    return orc32_from_f32((float) (0.5 * d * (1.0 + orc_tanh_d(u))));
+}
+
 uint32_t orc32_relu(uint32_t x) {
     return ((x & X32_SIGNMASK) || (x & ~X32_SIGNMASK) == 0) ? 0u : x;
 }
@@ -954,7 +1040,8 @@ uint32_t orc32_relu(uint32_t x) {
 void orc32_unary_f32(int op, const float * src, float * dst, int64_t n) {
     for (int64_t i = 0; i < n; i++) {
         const uint32_t v = f2c32(src[i]);
-        dst[i] = c2f32(op == ORC_SILU ? orc32_silu(v) : orc32_relu(v));
+        dst[i] = c2f32(op == ORC_SILU ? orc32_silu(v) : op == ORC_GELU ? orc32_gelu(v) : op == ORC_TANH ? orc32_tanh(v)
+                                                                                                : orc32_relu(v));
     }
 }
 
@@ -985,6 +1072,12 @@ void orc32_swiglu_f32(const float * gate, const float * up, int64_t gs, int64_t 
     for (int64_t r = 0; r < nr; r++)
         for (int64_t c = 0; c < nc; c++)
             dst[r * nc + c] = c2f32(mul32(orc32_silu(f2c32(gate[r * gs + c])), f2c32(up[r * us + c])));
+}
+
+void orc32_geglu_f32(const float * gate, const float * up, int64_t gs, int64_t us, float * dst, int64_t nc, int64_t nr) {
+    for (int64_t r = 0; r < nr; r++)
+        for (int64_t c = 0; c < nc; c++)
+            dst[r * nc + c] = c2f32(mul32(orc32_gelu(f2c32(gate[r * gs + c])), f2c32(up[r * us + c])));
 }
 
 void orc32_rope_f32(const float * src, const int64_t ne[4], const float * cos_sin, int n_dims, int neox, float * dst) {

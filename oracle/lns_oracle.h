@@ -110,21 +110,29 @@ uint32_t orc32_mask_from_f32(float m);
 
 /* elementwise ops at the F32 op boundary (lns-ops.cpp:468-599, 786-868, 1199-1281) */
 enum { ORC_ADD = 0, ORC_MUL = 1, ORC_DIV = 2 };
-enum { ORC_SILU = 0, ORC_RELU = 2 };
+enum { ORC_SILU = 0, ORC_GELU = 1, ORC_RELU = 2, ORC_TANH = 3 };
 uint16_t orc16_silu(uint16_t x);
+uint16_t orc16_gelu(uint16_t x);
+uint16_t orc16_tanh(uint16_t x);
 uint16_t orc16_relu(uint16_t x);
 void orc16_binary_f32(int op, const float * a, const int64_t ane[4], const float * b, const int64_t bne[4], float * dst);
 void orc16_scale_f32(const float * src, float * dst, int64_t n, float s, float b);
 void orc16_unary_f32(int op, const float * src, float * dst, int64_t n);
 void orc16_swiglu_f32(const float * gate, const float * up, int64_t gs, int64_t us, float * dst, int64_t nc, int64_t nr);
+void orc16_geglu_f32(const float * gate, const float * up, int64_t gs, int64_t us, float * dst, int64_t nc, int64_t nr);
 void orc16_rope_f32(const float * src, const int64_t ne[4], const float * cos_sin, int n_dims, int neox, float * dst);
 
 uint32_t orc32_silu(uint32_t x);
 uint32_t orc32_relu(uint32_t x);
+uint32_t orc32_gelu(uint32_t x);
+uint32_t orc32_tanh(uint32_t x);
+double orc_exp_d(double x);
+double orc_tanh_d(double y);
 void orc32_unary_f32(int op, const float * src, float * dst, int64_t n);
 void orc32_binary_f32(int op, const float * a, const int64_t ane[4], const float * b, const int64_t bne[4], float * dst);
 void orc32_scale_f32(const float * src, float * dst, int64_t n, float s, float b);
 void orc32_swiglu_f32(const float * gate, const float * up, int64_t gs, int64_t us, float * dst, int64_t nc, int64_t nr);
+void orc32_geglu_f32(const float * gate, const float * up, int64_t gs, int64_t us, float * dst, int64_t nc, int64_t nr);
 void orc32_rope_f32(const float * src, const int64_t ne[4], const float * cos_sin, int n_dims, int neox, float * dst);
 
 /* batch conversions */

@@ -75,6 +75,8 @@ def lib():
             "orc32_binary_f32": (None, [ctypes.c_int, f32p, i64a, f32p, i64a, f32p]),
             "orc32_scale_f32": (None, [f32p, f32p, i64, ctypes.c_float, ctypes.c_float]),
             "orc32_swiglu_f32": (None, [f32p, f32p, i64, i64, f32p, i64, i64]),
+            "orc16_geglu_f32": (None, [f32p, f32p, i64, i64, f32p, i64, i64]),
+            "orc32_geglu_f32": (None, [f32p, f32p, i64, i64, f32p, i64, i64]),
             "orc32_rope_f32": (None, [f32p, i64a, f32p, ctypes.c_int, ctypes.c_int, f32p]),
         }
         for name, (res, args) in sig.items():
@@ -88,7 +90,7 @@ def lib():
 
 
 BINARY = {"add": 0, "mul": 1, "div": 2}
-UNARY = {"silu": 0, "relu": 2}
+UNARY = {"silu": 0, "gelu": 1, "relu": 2, "tanh": 3}
 
 
 def binary16(op, a, b, fmt=16):
@@ -115,14 +117,15 @@ def unary16(op, src, fmt=16):
     return out
 
 
-def swiglu16(gate, up, fmt=16):
-    """silu(gate) * up, rows of gate.shape[-1]"""
+def swiglu16(gate, up, fmt=16, op="swiglu"):
+    """act(gate) * up, rows of gate.shape[-1]; act = silu (swiglu) or gelu (geglu)"""
     gate = np.ascontiguousarray(gate, np.float32)
     up = np.ascontiguousarray(up, np.float32)
     nc = gate.shape[-1]
     out = np.empty_like(gate)
-    (lib().orc16_swiglu_f32 if fmt == 16 else lib().orc32_swiglu_f32)(gate.ravel(), up.ravel(), nc, nc, out.ravel(),
-                                                                       nc, gate.size // nc)
+    fn = {("swiglu", 16): lib().orc16_swiglu_f32, ("swiglu", 32): lib().orc32_swiglu_f32,
+          ("geglu", 16): lib().orc16_geglu_f32, ("geglu", 32): lib().orc32_geglu_f32}[(op, fmt)]
+    fn(gate.ravel(), up.ravel(), nc, nc, out.ravel(), nc, gate.size // nc)
     return out
 
 
@@ -280,6 +283,18 @@ def mask32(m):
 
 def lfsr_jump(s, n):
     return lib().orc_lfsr_jump(s, n)
+
+
+def convstat(fmt, n=4194304, order=1):
+    """the reference's conversion statistics (dot-bench.cpp convert()) replayed
+    through this oracle's conversions (oracle/convstat.cpp); order 1 draws the
+    sign before the exponent"""
+    import json
+    exe = os.path.join(os.path.dirname(PINCHECK), "convstat")
+    if not os.path.exists(exe):
+        build()
+    return json.loads(subprocess.run([exe, str(fmt), str(n), str(order)], capture_output=True, text=True,
+                                     check=True).stdout)
 
 
 def pincheck():

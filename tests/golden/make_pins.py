@@ -61,6 +61,16 @@ def parse_swiglu(text, test_src):
             "source": "lns-backend/tests/test-lns-backend.cpp run_swiglu_test; unit-tests-lns16-base.txt"}
 
 
+def parse_geglu_tanh(text, test_src):
+    """The geglu case (run_geglu_test: the swiglu case's gate/up with gelu)
+    and the tanh case (run_tanh_test: its 8 inputs from the test source)."""
+    gg = re.search(r"LNS geglu split \(4 x 2\):\s*\[([^\]]*)\]", text)
+    th = re.search(r"LNS tanh: \[([^\]]*)\]", text)
+    m = re.search(r"static bool run_tanh_test.*?const float a\[n\] = \{([^}]*)\}", test_src, re.S)
+    tin = [float(v.rstrip("f")) for v in re.findall(r"-?\d+\.\d+f?", m.group(1))]
+    return {"geglu": floats(gg.group(1)), "tanh": floats(th.group(1)), "tanh_in": tin}
+
+
 def main(ref):
     ev = os.path.join(ref, "results", "sum32-evidence")
     with open(os.path.join(ev, "standalone-sum32-invariants.txt")) as f:
@@ -77,6 +87,20 @@ def main(ref):
         swiglu = parse_swiglu(f.read(), test_src)
     with open(os.path.join(ev, "unit-tests-lns32.txt")) as f:
         swiglu["out_lns32"] = parse_swiglu(f.read(), test_src)["out"]
+    acts = {}
+    for name, fn in (("lns16", "unit-tests-lns16-base.txt"), ("lns32", "unit-tests-lns32.txt")):
+        with open(os.path.join(ev, fn)) as f:
+            acts[name] = parse_geglu_tanh(f.read(), test_src)
+    acts["source"] = ("lns-backend/tests/test-lns-backend.cpp run_geglu_test / run_tanh_test; "
+                      "unit-tests-lns16-base.txt, unit-tests-lns32.txt")
+    convert = {}
+    with open(os.path.join(ref, "experiments", "dot-product-scaling", "results", "convert.jsonl")) as f:
+        for line in f:
+            if line.strip():
+                rec = json.loads(line)
+                convert[rec.pop("format")] = rec
+    convert["source"] = ("experiments/dot-product-scaling/results/convert.jsonl "
+                         "(protocol: experiments/dot-product-scaling/dot-bench.cpp convert())")
     pins = {
         "swiglu": swiglu,
         "source": "xlnsresearch/xlns-ggml-backend results/sum32-evidence/*.txt (outputs of "
@@ -84,8 +108,8 @@ def main(ref):
         "standalone": standalone,
         "suite": suite,
         "lfsr": {"step7": 0xB403, "period": 65535},
-        "convert_xlns16": {"source": "experiments/dot-product-scaling/results/convert.jsonl",
-                           "frac_exact": 6.67572e-06, "frac_changed_round2": 0.494361},
+        "convert": convert,
+        "activations": acts,
     }
     out = os.path.join(os.path.dirname(os.path.abspath(__file__)), "reference_pins.json")
     with open(out, "w") as f:
@@ -94,4 +118,6 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_pins.py <reference checkout>")
+    main(sys.argv[1])

@@ -72,7 +72,7 @@ def test_scale(orc, kss, fmt, s, b):
 
 
 @FMTS
-@pytest.mark.parametrize("op", ["silu", "relu"])
+@pytest.mark.parametrize("op", ["silu", "gelu", "relu", "tanh"])
 def test_unary(orc, kss, fmt, op):
     rng = np.random.default_rng(5)
     x = np.concatenate([f32(rng, (8192,), 3.0), np.array([0.0, -0.0, 1e-30, -1e-30, 60.0, -60.0, 1e30, -1e30], np.float32)])
@@ -82,20 +82,25 @@ def test_unary(orc, kss, fmt, op):
 
 
 @FMTS
-def test_swiglu_split_and_fused(orc, kss, fmt):
+@pytest.mark.parametrize("op", ["swiglu", "geglu"])
+def test_glu_split_and_fused(orc, kss, fmt, op):
     ks = kss[fmt]
     rng = np.random.default_rng(7)
     nc, nr = 1536, 6
     gate = f32(rng, (nr, nc), 2.0)
     up = f32(rng, (nr, nc), 1.0)
-    want = orc.swiglu16(gate, up, fmt=fmt)
+    want = orc.swiglu16(gate, up, fmt=fmt, op=op)
     out = torch.empty((nr, nc), dtype=torch.float32, device="cuda")
-    ks.glu(dev(gate), dev(up), nc, nc, out, nc, nr)
+    ks.glu(dev(gate), dev(up), nc, nc, out, nc, nr, op=op)
     assert same(host(out), want)
     fused = np.concatenate([gate, up], axis=1)          # [gate | up] per row, stride 2 * nc
     fd = dev(fused)
-    ks.glu(fd, fd[:, nc:], 2 * nc, 2 * nc, out, nc, nr)
+    ks.glu(fd, fd[:, nc:], 2 * nc, 2 * nc, out, nc, nr, op=op)
     assert same(host(out), want)
+    lns = torch.empty((nr, nc), dtype=torch.int16 if fmt == 16 else torch.int32, device="cuda")
+    ks.glu_lns(dev(gate), dev(up), nc, nc, lns, nc, nr, op=op)
+    codes = orc.from_f32_16(want) if fmt == 16 else orc.from_f32_32(want)
+    assert np.array_equal(host(lns).view(codes.dtype), codes)
 
 
 @FMTS
@@ -112,6 +117,27 @@ def test_swiglu_reference_pin(kss, fmt):
     kss[fmt].glu(dev(gate), dev(up), 4, 4, out, 4, 2)
     want = p["out"] if fmt == 16 else p["out_lns32"]
     assert ["%.6f" % v for v in host(out).ravel()] == ["%.6f" % v for v in want]
+
+
+@FMTS
+def test_geglu_tanh_reference_pins(kss, fmt):
+    """the reference's printed geglu and tanh (test-lns-backend.cpp
+    run_geglu_test / run_tanh_test, the LNS16 and LNS32 runs) through the GPU"""
+    import json
+    import os
+    from conftest import ROOT
+    pins = json.load(open(os.path.join(ROOT, "tests", "golden", "reference_pins.json")))
+    p = pins["activations"]["lns16" if fmt == 16 else "lns32"]
+    gate = np.array(pins["swiglu"]["gate"], np.float32).reshape(2, 4)
+    up = np.array(pins["swiglu"]["up"], np.float32).reshape(2, 4)
+    out = torch.empty((2, 4), dtype=torch.float32, device="cuda")
+    kss[fmt].glu(dev(gate), dev(up), 4, 4, out, 4, 2, op="geglu")
+    fmt6 = lambda vs: ["%.6f" % (0.0 if v == 0 else v) for v in vs]
+    assert fmt6(host(out).ravel()) == fmt6(p["geglu"])
+    x = np.array(p["tanh_in"], np.float32)
+    t = torch.empty(8, dtype=torch.float32, device="cuda")
+    kss[fmt].unary("tanh", dev(x), t, 8)
+    assert fmt6(host(t)) == fmt6(p["tanh"])
 
 
 @FMTS
@@ -141,19 +167,13 @@ def test_f16_conversions(ks):
     assert same(host(back), x.astype(np.float16).astype(np.float32))
 
 
-def test_unsupported_and_invalid(ks):
+def test_invalid(kss):
     import lnsb200
     x = torch.zeros(16, dtype=torch.float32, device="cuda")
-    with pytest.raises(lnsb200.LnsbError):
-        ks.unary("gelu", x, x, 16)                      # gelu not pinned: LNSB_E_UNSUPPORTED
-    with pytest.raises(lnsb200.LnsbError):
-        ks.binary("add", x, (16, 1, 1, 1), x, (3, 1, 1, 1), x)   # b does not repeat to a
-
-
-def test_unsupported_xlns32(kss):
-    import lnsb200
-    x = torch.zeros(16, dtype=torch.float32, device="cuda")
-    with pytest.raises(lnsb200.LnsbError):
-        kss[32].unary("tanh", x, x, 16)
-    with pytest.raises(lnsb200.LnsbError):
-        kss[32].glu(x, x, 4, 4, x, 4, 4, op="geglu")
+    for fmt in (16, 32):
+        ks = kss[fmt]
+        with pytest.raises(lnsb200.LnsbError):
+            ks.binary("add", x, (16, 1, 1, 1), x, (3, 1, 1, 1), x)   # b does not repeat to a
+        with pytest.raises(lnsb200.LnsbError):
+            ks.glu(x, x, 2, 4, x, 4, 4)                               # gate stride shorter than a row
+        assert ks.lib.lnsb_unary(fmt, 4, x.data_ptr(), x.data_ptr(), 16, None) == -1      # no such op: LNSB_E_INVALID

@@ -2,11 +2,14 @@
 
 pincheck replays the reference's deterministic test programs
 (lns-backend/tests/test-lns16-sum32.cpp, test-lns-backend.cpp) through the
-oracle; tests/golden/reference_pins.json holds what the reference printed
+oracle, and convstat its conversion-statistics run
+(experiments/dot-product-scaling/dot-bench.cpp convert(), seed 1, 4 M
+values); tests/golden/reference_pins.json holds what the reference printed
 (tests/golden/make_pins.py).  PINNED lists every figure the restatement
-reproduces digit for digit -- each is asserted exactly.  The remaining
-figures depend on parts of the absent xlnscpp library that the evidence does
-not determine (the conversion table's bias, the Monte dither rule, the LPVIP
+reproduces digit for digit -- each is asserted exactly, and so are the
+conversion statistics and the activation printouts.  The remaining figures
+depend on parts of the absent xlnscpp library that the evidence does not
+determine (the xlns32 adder's table layout, the Monte dither rule, the LPVIP
 adder); they are printed beside the reference's by test_report, and bounded
 where the reference states a gate.
 """
@@ -33,11 +36,21 @@ PINNED = [
     ("suite", "sum32", "mm4x3_err"),
     ("suite", "lns32", "mm4x3"),
     ("suite", "lns32", "mm4x3_err"),
-    ("suite", "base", "rms_norm", 1),
+    ("suite", "base", "rms_norm"),
+    ("suite", "base", "softmax"),
+    ("suite", "base", "mm_long"),
+    ("suite", "sum32", "rms_norm"),
+    ("suite", "sum32", "softmax"),
+    ("suite", "sum32", "mm_long", 0),
+    ("suite", "sum32", "mm_long", 1),
     ("suite", "lns32", "rms_norm"),
     ("suite", "lns32", "softmax"),
-    ("suite", "base", "softmax", 1),
-    ("suite", "base", "mm_long", 1),
+    ("suite", "lns32", "mm_long", 1),
+    ("suite", "monte", "rms_norm", 0),
+    ("standalone", "rms_standalone", "576"),
+    ("standalone", "rms_standalone", "1536"),
+    ("standalone", "long_dot", "1536", 0),
+    ("standalone", "long_dot", "8960", 0),
 ]
 
 
@@ -65,6 +78,29 @@ def test_pinned(computed, pins, path):
         assert [round(v, 4) for v in got] == [round(v, 4) for v in want]
     else:
         assert round(got, 4) == round(want, 4)
+
+
+@pytest.mark.parametrize("fmt", [16, 32])
+def test_conversion_statistics(orc, pins, fmt):
+    """F32 -> LNS -> F32 over the reference's own 4 M inputs: every statistic
+    its run printed (results/convert.jsonl, %.6g), digit for digit"""
+    got = orc.convstat(fmt)
+    want = pins["convert"]["xlns%d" % fmt]
+    for k, v in want.items():
+        assert "%.6g" % got[k] == "%.6g" % v, k
+
+
+@pytest.mark.parametrize("fmt", [16, 32])
+def test_geglu_tanh_pins(orc, pins, fmt):
+    """gelu (through geglu) and tanh: the reference's printouts
+    (test-lns-backend.cpp run_geglu_test / run_tanh_test) to every digit"""
+    import numpy as np
+    p = pins["activations"]["lns16" if fmt == 16 else "lns32"]
+    gate = np.array(pins["swiglu"]["gate"], np.float32).reshape(2, 4)
+    up = np.array(pins["swiglu"]["up"], np.float32).reshape(2, 4)
+    fmt6 = lambda vs: ["%.6f" % (0.0 if v == 0 else v) for v in vs]
+    assert fmt6(orc.swiglu16(gate, up, fmt=fmt, op="geglu").ravel()) == fmt6(p["geglu"])
+    assert fmt6(orc.unary16("tanh", np.array(p["tanh_in"], np.float32), fmt=fmt)) == fmt6(p["tanh"])
 
 
 def test_roundtrip_and_lfsr(computed, pins):

@@ -24,9 +24,10 @@ constexpr bool k_acc32      = k_mode == M_LPVIP || k_mode == M_SUM32;
 // Device copies of the tables, one set per GPU (lnsb_upload_tables).
 struct dev_tables {
     const int16_t *  sbdb16;     // k16_tab_bytes, see lnsb_tables.h
-    const uint16_t * conv16;     // 65536
+    const uint16_t * conv16;     // 131072, indexed by a float's bits >> 15
     const float *    dec16;      // 65536
     const uint16_t * exp16;      // 65536
+    const uint16_t * sig16;      // 65536
     const int16_t *  monte16;    // 2 * k16_monte_n
     const int32_t *  key16;      // k16_key_bytes / 4
     const int32_t *  mkey16;     // k16m_key_bytes / 4
@@ -94,7 +95,7 @@ __device__ __forceinline__ bool gt16(uint32_t a, uint32_t b) { return canon16(a)
 __device__ __forceinline__ bool is_zero16(uint32_t v) { return (v & 0x7FFFu) == 0; }
 
 __device__ __forceinline__ uint32_t from_f32_16(const dev_tables & T, float x) {
-    return __ldg(T.conv16 + (__float_as_uint(x) >> 16));
+    return __ldg(T.conv16 + (__float_as_uint(x) >> 15));
 }
 __device__ __forceinline__ float to_f32_16(const dev_tables & T, uint32_t v) { return __ldg(T.dec16 + (v & 0xFFFFu)); }
 
@@ -371,6 +372,30 @@ __device__ __forceinline__ float lnsb_expf(float x) {
 #pragma unroll
     for (int i = 13; i >= 0; i--) p = __fma_rn(p, r, c[i]);
     return __double2float_rn(scalbn(p, (int) n));
+}
+
+// e^x in double: the same series as lnsb_expf without the float rounding,
+// |x| clamped to 700 (the device twin of host_exp_d)
+__device__ __forceinline__ double lnsb_exp_d(double xd) {
+    if (xd != xd) return xd;
+    xd = xd > 700.0 ? 700.0 : (xd < -700.0 ? -700.0 : xd);
+    const double t = __dmul_rn(xd, 1.4426950408889634074);
+    const double n = rint(t);
+    const double r = __dmul_rn(__dsub_rn(t, n), 0.69314718055994530942);
+    const double c[15] = {
+        1.0, 1.0, 1.0 / 2, 1.0 / 6, 1.0 / 24, 1.0 / 120, 1.0 / 720, 1.0 / 5040, 1.0 / 40320,
+        1.0 / 362880, 1.0 / 3628800, 1.0 / 39916800, 1.0 / 479001600, 1.0 / 6227020800.0,
+        1.0 / 87178291200.0 };
+    double p = c[14];
+#pragma unroll
+    for (int i = 13; i >= 0; i--) p = __fma_rn(p, r, c[i]);
+    return scalbn(p, (int) n);
+}
+
+// tanh(y) = (e^2y - 1) / (e^2y + 1) in double
+__device__ __forceinline__ double lnsb_tanh_d(double y) {
+    const double e = lnsb_exp_d(__dmul_rn(2.0, y));
+    return __ddiv_rn(__dsub_rn(e, 1.0), __dadd_rn(e, 1.0));
 }
 
 __device__ __forceinline__ uint32_t exp32(const dev_tables & T, uint32_t v) {

@@ -314,19 +314,20 @@ __device__ __forceinline__ void stage_async(void * smem, const void * gmem, int 
 
 // ---- the xlns16 image of a typed weight at HBM speed ----------------------
 //
-// float -> xlns16 without the 128 KB table: for a normal float (biased
-// exponent e in 1..254, top mantissa bits m) the table entry is
+// float -> xlns16 without the 256 KB table: for a normal float (biased
+// exponent e in 1..254, top 8 mantissa bits m) the table entry is
 //     clamp(128 (e - 127) + G[m] + 0x4000, 0, 0x7FFF) | sign,
-// G[m] = 128 log2(1 + m/128) truncated toward zero: floored for |x| >= 1,
+// G[m] = 128 log2(1 + m/256) truncated toward zero: floored for |x| >= 1,
 // rounded up below.  G is read off the table itself (entries at e = 127 and
-// e = 126) and the split is checked against all 65536 entries on the host
-// before this path is used (conv16_splits); subnormals, infinities and NaNs
-// keep the table lookup.  A CTA keeps G in shared memory, one copy per bank
-// (word m * 32 + lane holds G for |x| >= 1 in byte 0, for |x| < 1 in byte 1),
-// so a warp's lookups never conflict.
+// e = 126) and the split is checked against every entry on the host before
+// this path is used (conv16_splits); subnormals, infinities and NaNs keep the
+// table lookup.  A CTA keeps G in shared memory, one copy per bank (word
+// m * 32 + lane holds G for |x| >= 1 in byte 0, for |x| < 1 in byte 1), so a
+// warp's lookups never conflict.  A value's index u is its float's bits >> 15
+// (17 bits: sign, exponent, top 8 mantissa bits).
 constexpr int TW_ROWS = 64, TW_THREADS = 1024, TW_STAGES = 4;
 constexpr int TW_OP = TW_ROWS + 2;                       // codes per column of the transposed tile (33 words)
-constexpr int TW_GTAB = 128 * 32 * 4;
+constexpr int TW_GTAB = 256 * 32 * 4;
 
 template <int TYPE> struct tw_geom {
     static constexpr int cols  = TYPE == LNSB_TYPE_F32 ? 128 : 256;     // a tile's columns: whole blocks
@@ -340,25 +341,25 @@ template <int TYPE> struct tw_geom {
     static constexpr int smem  = TW_GTAB + TW_STAGES * stage + cols * TW_OP * 2;
 };
 
-// a normal float's upper 16 bits -> xlns16 through the shared copies of G
+// a normal float's index u = bits >> 15 -> xlns16 through the shared copies of G
 __device__ __forceinline__ uint32_t conv16_fast(const uint32_t * __restrict__ glane, uint32_t u) {
-    const uint32_t g = __byte_perm(glane[(u & 0x7Fu) << 5], 0u, (u & 0x7FFFu) < (127u << 7) ? 0x4441u : 0x4440u);
-    return (u & 0x8000u) | min((u & 0x7F80u) + g + 128u, 0x7FFFu);    // 128 (e - 127) + 0x4000 = 128 e + 128
+    const uint32_t g = __byte_perm(glane[(u & 0xFFu) << 5], 0u, (u & 0xFFFFu) < (127u << 8) ? 0x4441u : 0x4440u);
+    return ((u >> 1) & 0x8000u) | min(((u & 0xFF00u) >> 1) + g + 128u, 0x7FFFu);   // 128 (e - 127) + 0x4000 = 128 e + 128
 }
-__device__ __forceinline__ bool conv16_normal(uint32_t u) { return (u & 0x7F80u) - 0x80u < 0x7F00u; }
+__device__ __forceinline__ bool conv16_normal(uint32_t u) { return (u & 0xFF00u) - 0x100u < 0xFE00u; }
 __device__ __forceinline__ uint32_t conv16_split(const dev_tables & T, const uint32_t * __restrict__ glane, uint32_t u) {
     return conv16_normal(u) ? conv16_fast(glane, u) : (uint32_t) __ldg(T.conv16 + u);
 }
 
-// the upper 16 bits of value c's float (the conversion table's index)
+// the upper 17 bits of value c's float (the conversion table's index)
 template <int TYPE>
 __device__ __forceinline__ uint32_t f32_hi_at(const unsigned char * row, int c) {
     if constexpr (TYPE == LNSB_TYPE_BF16) {
-        return reinterpret_cast<const uint16_t *>(row)[c];
+        return (uint32_t) reinterpret_cast<const uint16_t *>(row)[c] << 1;
     } else if constexpr (TYPE == LNSB_TYPE_F16) {
-        return __float_as_uint(__half2float(reinterpret_cast<const __half *>(row)[c])) >> 16;   // exact widening
+        return __float_as_uint(__half2float(reinterpret_cast<const __half *>(row)[c])) >> 15;   // exact widening
     } else {
-        return __float_as_uint(dequant_at_t<TYPE>(row, c)) >> 16;
+        return __float_as_uint(dequant_at_t<TYPE>(row, c)) >> 15;
     }
 }
 
@@ -386,9 +387,9 @@ k_to_lns16_typed_tiled(dev_tables T, const unsigned char * __restrict__ src, int
     // G from the table's entries at e = 127 (|x| >= 1) and e = 126 (|x| < 1):
     // one load each by the first 128 threads, then one copy per bank
     uint32_t * g0 = reinterpret_cast<uint32_t *>(tile);
-    if (tid < 128) {
-        const uint32_t gp = (uint32_t) __ldg(T.conv16 + ((127 << 7) | tid)) - 0x4000u;
-        const uint32_t gn = (uint32_t) __ldg(T.conv16 + ((126 << 7) | tid)) - 0x4000u + 128u;
+    if (tid < 256) {
+        const uint32_t gp = (uint32_t) __ldg(T.conv16 + ((127 << 8) | tid)) - 0x4000u;
+        const uint32_t gn = (uint32_t) __ldg(T.conv16 + ((126 << 8) | tid)) - 0x4000u + 128u;
         g0[tid] = gp | (gn << 8);
     }
 
@@ -434,12 +435,12 @@ k_to_lns16_typed_tiled(dev_tables T, const unsigned char * __restrict__ src, int
 #pragma unroll
     for (int k = 0; k < TW_STAGES - 1; k++) stage((int64_t) blockIdx.x + (int64_t) k * gridDim.x, k);
     __syncthreads();                                       // g0 written
-    uint32_t gw[128 * 32 / TW_THREADS];
+    uint32_t gw[256 * 32 / TW_THREADS];
 #pragma unroll
-    for (int j = 0; j < 128 * 32 / TW_THREADS; j++) gw[j] = g0[(tid + j * TW_THREADS) >> 5];
+    for (int j = 0; j < 256 * 32 / TW_THREADS; j++) gw[j] = g0[(tid + j * TW_THREADS) >> 5];
     __syncthreads();                                       // g0 read: the tile is free
 #pragma unroll
-    for (int j = 0; j < 128 * 32 / TW_THREADS; j++) gtab[tid + j * TW_THREADS] = gw[j];
+    for (int j = 0; j < 256 * 32 / TW_THREADS; j++) gtab[tid + j * TW_THREADS] = gw[j];
     const uint32_t * glane = gtab + lane;
 
     int slot = 0;
@@ -468,10 +469,10 @@ k_to_lns16_typed_tiled(dev_tables T, const unsigned char * __restrict__ src, int
             for (int k = 0; k < TW_NP; k++) {
                 const int r = 2 * (p0 + k * TW_PPS);
                 const uint32_t u0 = f32_hi_at<TYPE>(rs + r * G::rawp, c), u1 = f32_hi_at<TYPE>(rs + (r + 1) * G::rawp, c);
-                const bool ok = (conv16_normal(u0) || (u0 & 0x7FFFu) == 0) && (conv16_normal(u1) || (u1 & 0x7FFFu) == 0);
+                const bool ok = (conv16_normal(u0) || (u0 & 0xFFFFu) == 0) && (conv16_normal(u1) || (u1 & 0xFFFFu) == 0);
                 bad |= ok ? 0u : 1u << k;
-                const uint32_t v0 = (u0 & 0x7FFFu) ? conv16_fast(glane, u0) : 0u;
-                const uint32_t v1 = (u1 & 0x7FFFu) ? conv16_fast(glane, u1) : 0u;
+                const uint32_t v0 = (u0 & 0xFFFFu) ? conv16_fast(glane, u0) : 0u;
+                const uint32_t v1 = (u1 & 0xFFFFu) ? conv16_fast(glane, u1) : 0u;
                 *reinterpret_cast<uint32_t *>(tile + c * TW_OP + r) = v0 | (v1 << 16);
             }
             while (bad) {
@@ -2301,7 +2302,7 @@ __global__ void k_group_barrier(int32_t * const * __restrict__ flags, int world,
 // (lns-backend/cuda/lns-cuda-kernels.cuh:162-355, lns-backend/src/lns-ops.cpp):
 // convert with the F32 -> LNS table, compute in LNS, write back through the
 // decode table.  Grid-stride loops over elements; the tables are read through
-// the read-only cache (conv16 128 KB, dec16 256 KB, sbdb16 6.7 KB).
+// the read-only cache (conv16 256 KB, dec16 256 KB, sbdb16 6.7 KB).
 template <int FMT> struct ew;
 template <> struct ew<16> {
     __device__ static __forceinline__ uint32_t from(const dev_tables & T, float x) { return from_f32_16(T, x); }
@@ -2320,17 +2321,54 @@ template <> struct ew<32> {
     __device__ static __forceinline__ uint32_t div(uint32_t a, uint32_t b) { return div32(a, b); }
 };
 
-// silu(x) = x / (1 + exp(-x)) in xlns16 arithmetic over the exp table
+// silu(x) = x * sigmoid(x), the sigmoid from its table (entry c: the float
+// 1 / (1 + e^-x) of code c's value, converted)
 __device__ __forceinline__ uint32_t silu16(const dev_tables & T, uint32_t x) {
-    const uint32_t e = __ldg(T.exp16 + (x ^ 0x8000u));
-    return div16(x, add16(0x4000u, e, T.sbdb16));
+    return mul16(x, __ldg(T.sig16 + x));
 }
 __device__ __forceinline__ uint32_t relu16(uint32_t x) { return ((x & 0x8000u) || (x & 0x7FFFu) == 0) ? 0u : x; }
-// xlns32: the same form, exp through float as in the xlns32 softmax
+// tanh(x) = (e^2x - 1) / (e^2x + 1) in xlns16 arithmetic over the exp table
+__device__ __forceinline__ uint32_t tanh16(const dev_tables & T, uint32_t x) {
+    const uint32_t e = __ldg(T.exp16 + mul16(x, 0x4080u));
+    return div16(add16(e, 0xC000u, T.sbdb16), add16(e, 0x4000u, T.sbdb16));
+}
+// gelu(x) = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) in xlns16
+// arithmetic, the constants converted from float like any operand
+__device__ __forceinline__ uint32_t gelu16(const dev_tables & T, uint32_t x) {
+    const uint32_t s = from_f32_16(T, 0.79788456080286535588f), a = from_f32_16(T, 0.044715f), h = from_f32_16(T, 0.5f);
+    const uint32_t x3 = mul16(mul16(x, x), x);
+    const uint32_t in = mul16(s, add16(x, mul16(a, x3), T.sbdb16));
+    return mul16(mul16(h, x), add16(0x4000u, tanh16(T, in), T.sbdb16));
+}
+// xlns32: silu in xlns32 arithmetic with exp through float, as in the xlns32
+// softmax; tanh and gelu through double precision (lnsb_tanh_d), as xlns32's
+// activations go through floating point in the reference
 __device__ __forceinline__ uint32_t silu32(const dev_tables & T, uint32_t x) {
     return div32(x, add32(T, 0x40000000u, exp32(T, x ^ 0x80000000u)));
 }
 __device__ __forceinline__ uint32_t relu32(uint32_t x) { return ((x & 0x80000000u) || (x & 0x7FFFFFFFu) == 0) ? 0u : x; }
+__device__ __forceinline__ uint32_t tanh32(const dev_tables & T, uint32_t x) {
+    return from_f32_32(T, __double2float_rn(lnsb_tanh_d((double) to_f32_32(T, x))));
+}
+__device__ __forceinline__ uint32_t gelu32(const dev_tables & T, uint32_t x) {
+    const double d = (double) to_f32_32(T, x);
+    const double u = __dmul_rn(0.79788456080286535588, __dadd_rn(d, __dmul_rn(__dmul_rn(__dmul_rn(0.044715, d), d), d)));
+    return from_f32_32(T, __double2float_rn(__dmul_rn(__dmul_rn(0.5, d), __dadd_rn(1.0, lnsb_tanh_d(u)))));
+}
+template <int FMT, int OP>
+__device__ __forceinline__ uint32_t unary_op(const dev_tables & T, uint32_t v) {
+    if constexpr (FMT == 16) {
+        if constexpr (OP == LNSB_UNARY_SILU) return silu16(T, v);
+        else if constexpr (OP == LNSB_UNARY_GELU) return gelu16(T, v);
+        else if constexpr (OP == LNSB_UNARY_TANH) return tanh16(T, v);
+        else return relu16(v);
+    } else {
+        if constexpr (OP == LNSB_UNARY_SILU) return silu32(T, v);
+        else if constexpr (OP == LNSB_UNARY_GELU) return gelu32(T, v);
+        else if constexpr (OP == LNSB_UNARY_TANH) return tanh32(T, v);
+        else return relu32(v);
+    }
+}
 
 #define LNSB_GRID_STRIDE(i, n) \
     for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < (n); i += (int64_t) blockDim.x * gridDim.x)
@@ -2369,16 +2407,13 @@ __global__ void k_unary(dev_tables T, const float * __restrict__ src, float * __
     pdl_entry();
     using A = ew<FMT>;
     LNSB_GRID_STRIDE(i, n) {
-        const uint32_t v = A::from(T, src[i]);
-        uint32_t r;
-        if constexpr (FMT == 16) r = OP == LNSB_UNARY_SILU ? silu16(T, v) : relu16(v);
-        else                     r = OP == LNSB_UNARY_SILU ? silu32(T, v) : relu32(v);
-        dst[i] = A::to(T, r);
+        dst[i] = A::to(T, unary_op<FMT, OP>(T, A::from(T, src[i])));
     }
 }
 
-// OUT_LNS: the glu op's F32 result converted again (to_lns of the next mul_mat)
-template <int FMT, bool OUT_LNS = false>
+// act(gate) * up with act = silu (swiglu) or gelu (geglu).  OUT_LNS: the glu
+// op's F32 result converted again (to_lns of the next mul_mat)
+template <int FMT, bool OUT_LNS = false, int ACT = LNSB_UNARY_SILU>
 __global__ void k_swiglu(dev_tables T, const float * __restrict__ gate, const float * __restrict__ up, int64_t gs,
                          int64_t us, void * __restrict__ dst, int64_t nc, int64_t nr) {
     pdl_entry();
@@ -2386,7 +2421,7 @@ __global__ void k_swiglu(dev_tables T, const float * __restrict__ gate, const fl
     LNSB_GRID_STRIDE(i, nc * nr) {
         const int64_t r = i / nc, c = i - r * nc;
         const uint32_t g = A::from(T, gate[r * gs + c]), u = A::from(T, up[r * us + c]);
-        const float y = A::to(T, A::mul(FMT == 16 ? silu16(T, g) : silu32(T, g), u));
+        const float y = A::to(T, A::mul(unary_op<FMT, ACT>(T, g), u));
         if constexpr (!OUT_LNS)    static_cast<float *>(dst)[i] = y;
         else if constexpr (FMT == 16) static_cast<uint16_t *>(dst)[i] = (uint16_t) A::from(T, y);
         else                          static_cast<uint32_t *>(dst)[i] = A::from(T, y);
@@ -2715,18 +2750,18 @@ int nn_smem_attr(const void * kern, int bytes) {
 
 // true when the float -> xlns16 table is, for every normal float, the
 // exponent-plus-mantissa split that conv16_split computes (G read off the
-// entries at e = 127 and e = 126); checked once over all 65536 entries
+// entries at e = 127 and e = 126); checked once over all 131072 entries
 bool conv16_splits() {
     static const bool ok = [] {
         const std::vector<uint16_t> & c = get_host_tables(false, false).conv16;
-        for (uint32_t u = 0; u < 65536; u++) {
-            const uint32_t e = (u >> 7) & 0xFFu, m = u & 0x7Fu;
+        for (uint32_t u = 0; u < 131072; u++) {
+            const uint32_t e = (u >> 8) & 0xFFu, m = u & 0xFFu;
             if (e == 0 || e == 255) continue;
-            const int gp = (int) c[(127u << 7) | m] - 0x4000, gn = (int) c[(126u << 7) | m] - 0x4000 + 128;
+            const int gp = (int) c[(127u << 8) | m] - 0x4000, gn = (int) c[(126u << 8) | m] - 0x4000 + 128;
             if (gp < 0 || gp > 255 || gn < 0 || gn > 255) return false;
             int v = 128 * ((int) e - 127) + (e < 127 ? gn : gp) + 0x4000;
             v = v < 0 ? 0 : (v > 0x7FFF ? 0x7FFF : v);
-            if (c[u] != ((u & 0x8000u) | (uint32_t) v)) return false;
+            if (c[u] != (((u >> 1) & 0x8000u) | (uint32_t) v)) return false;
         }
         return true;
     }();
@@ -2747,8 +2782,8 @@ int rms_norm_impl(int fmt, const void * src, void * dst, int64_t ncols, int64_t 
     const float invf = 1.0f / (float) ncols;
     if (fmt == LNSB_XLNS16) {
         uint32_t b;
-        std::memcpy(&b, &eps, 4);  eps_l = H.conv16[b >> 16];
-        std::memcpy(&b, &invf, 4); inv_n = H.conv16[b >> 16];
+        std::memcpy(&b, &eps, 4);  eps_l = H.conv16[b >> 15];
+        std::memcpy(&b, &invf, 4); inv_n = H.conv16[b >> 15];
     } else {
         eps_l = host_from_f32_32(eps);
         inv_n = host_from_f32_32(invf);
@@ -2891,6 +2926,14 @@ struct lnsb_weight_cache {
     std::mutex             mu;
 };
 
+// the glu kernels by format, output form and activation
+template <int FMT, bool OUT_LNS>
+void launch_glu(int op, unsigned g, cudaStream_t s, const dev_tables & T, const float * gate, const float * up,
+                int64_t gs, int64_t us, void * dst, int64_t nc, int64_t nr) {
+    if (op == LNSB_GLU_SWIGLU) launch_k(k_swiglu<FMT, OUT_LNS, LNSB_UNARY_SILU>, g, 256, 0, s, T, gate, up, gs, us, dst, nc, nr);
+    else                       launch_k(k_swiglu<FMT, OUT_LNS, LNSB_UNARY_GELU>, g, 256, 0, s, T, gate, up, gs, us, dst, nc, nr);
+}
+
 // ================================ C ABI =====================================
 
 extern "C" {
@@ -2960,6 +3003,7 @@ int lnsb_upload_tables(int fmt) {
         if (e == cudaSuccess) e = upload(H.conv16, &t.conv16);
         if (e == cudaSuccess) e = upload(H.dec16, &t.dec16);
         if (e == cudaSuccess) e = upload(H.exp16, &t.exp16);
+        if (e == cudaSuccess) e = upload(H.sig16, &t.sig16);
         if (e == cudaSuccess) e = upload(H.monte16, &t.monte16);
         if (e == cudaSuccess) e = upload(H.key16, &t.key16);
         if (e == cudaSuccess) e = upload(H.mkey16, &t.mkey16);
@@ -3170,7 +3214,7 @@ int lnsb_soft_max(int fmt, const lnsb_soft_max_args * a, lnsb_stream_t stream) {
         const host_tables & H = get_host_tables(false, false);
         uint32_t b;
         std::memcpy(&b, &a->scale, 4);
-        scale_l = H.conv16[b >> 16];
+        scale_l = H.conv16[b >> 15];
     } else {
         scale_l = host_from_f32_32(a->scale);
     }
@@ -3277,8 +3321,8 @@ int lnsb_scale(int fmt, const float * src, float * dst, int64_t n, float sv, flo
     if (fmt == LNSB_XLNS16) {
         const host_tables & H = get_host_tables(false, false);
         uint32_t u;
-        std::memcpy(&u, &sv, 4); sl = H.conv16[u >> 16];
-        std::memcpy(&u, &bv, 4); bl = H.conv16[u >> 16];
+        std::memcpy(&u, &sv, 4); sl = H.conv16[u >> 15];
+        std::memcpy(&u, &bv, 4); bl = H.conv16[u >> 15];
         launch_k(k_scale<16>, grid_for(n, 256), 256, 0, s, *T, src, dst, n, sl, bl, bv != 0.0f ? 1 : 0);
     } else {
         sl = host_from_f32_32(sv);
@@ -3290,7 +3334,6 @@ int lnsb_scale(int fmt, const float * src, float * dst, int64_t n, float sv, flo
 
 int lnsb_unary(int fmt, int op, const float * src, float * dst, int64_t n, lnsb_stream_t stream) {
     if (!valid_fmt(fmt) || op < LNSB_UNARY_SILU || op > LNSB_UNARY_TANH || n < 0) return LNSB_E_INVALID;
-    if (op != LNSB_UNARY_SILU && op != LNSB_UNARY_RELU) return LNSB_E_UNSUPPORTED;
     if (n == 0) return 0;
     if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
     const dev_tables * T = nullptr;
@@ -3299,11 +3342,19 @@ int lnsb_unary(int fmt, int op, const float * src, float * dst, int64_t n, lnsb_
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned g = grid_for(n, 256);
     if (fmt == LNSB_XLNS16) {
-        if (op == LNSB_UNARY_SILU) launch_k(k_unary<16, LNSB_UNARY_SILU>, g, 256, 0, s, *T, src, dst, n);
-        else                       launch_k(k_unary<16, LNSB_UNARY_RELU>, g, 256, 0, s, *T, src, dst, n);
+        switch (op) {
+            case LNSB_UNARY_SILU: launch_k(k_unary<16, LNSB_UNARY_SILU>, g, 256, 0, s, *T, src, dst, n); break;
+            case LNSB_UNARY_GELU: launch_k(k_unary<16, LNSB_UNARY_GELU>, g, 256, 0, s, *T, src, dst, n); break;
+            case LNSB_UNARY_RELU: launch_k(k_unary<16, LNSB_UNARY_RELU>, g, 256, 0, s, *T, src, dst, n); break;
+            default:              launch_k(k_unary<16, LNSB_UNARY_TANH>, g, 256, 0, s, *T, src, dst, n); break;
+        }
     } else {
-        if (op == LNSB_UNARY_SILU) launch_k(k_unary<32, LNSB_UNARY_SILU>, g, 256, 0, s, *T, src, dst, n);
-        else                       launch_k(k_unary<32, LNSB_UNARY_RELU>, g, 256, 0, s, *T, src, dst, n);
+        switch (op) {
+            case LNSB_UNARY_SILU: launch_k(k_unary<32, LNSB_UNARY_SILU>, g, 256, 0, s, *T, src, dst, n); break;
+            case LNSB_UNARY_GELU: launch_k(k_unary<32, LNSB_UNARY_GELU>, g, 256, 0, s, *T, src, dst, n); break;
+            case LNSB_UNARY_RELU: launch_k(k_unary<32, LNSB_UNARY_RELU>, g, 256, 0, s, *T, src, dst, n); break;
+            default:              launch_k(k_unary<32, LNSB_UNARY_TANH>, g, 256, 0, s, *T, src, dst, n); break;
+        }
     }
     return launch_status();
 }
@@ -3311,7 +3362,6 @@ int lnsb_unary(int fmt, int op, const float * src, float * dst, int64_t n, lnsb_
 int lnsb_glu(int fmt, int op, const float * gate, const float * up, int64_t gate_stride, int64_t up_stride, float * dst,
              int64_t ncols, int64_t nrows, lnsb_stream_t stream) {
     if (!valid_fmt(fmt) || (op != LNSB_GLU_SWIGLU && op != LNSB_GLU_GEGLU) || ncols < 0 || nrows < 0) return LNSB_E_INVALID;
-    if (op != LNSB_GLU_SWIGLU) return LNSB_E_UNSUPPORTED;
     if (ncols == 0 || nrows == 0) return 0;
     if (gate == nullptr || up == nullptr || dst == nullptr || gate_stride < ncols || up_stride < ncols) return LNSB_E_INVALID;
     const dev_tables * T = nullptr;
@@ -3319,15 +3369,14 @@ int lnsb_glu(int fmt, int op, const float * gate, const float * up, int64_t gate
     if (st != 0) return st;
     const unsigned g = grid_for(ncols * nrows, 256);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (fmt == LNSB_XLNS16) launch_k(k_swiglu<16>, g, 256, 0, s, *T, gate, up, gate_stride, up_stride, dst, ncols, nrows);
-    else                    launch_k(k_swiglu<32>, g, 256, 0, s, *T, gate, up, gate_stride, up_stride, dst, ncols, nrows);
+    if (fmt == LNSB_XLNS16) launch_glu<16, false>(op, g, s, *T, gate, up, gate_stride, up_stride, dst, ncols, nrows);
+    else                    launch_glu<32, false>(op, g, s, *T, gate, up, gate_stride, up_stride, dst, ncols, nrows);
     return launch_status();
 }
 
 int lnsb_glu_lns(int fmt, int op, const float * gate, const float * up, int64_t gate_stride, int64_t up_stride,
                  void * dst_lns, int64_t ncols, int64_t nrows, lnsb_stream_t stream) {
     if (!valid_fmt(fmt) || (op != LNSB_GLU_SWIGLU && op != LNSB_GLU_GEGLU) || ncols < 0 || nrows < 0) return LNSB_E_INVALID;
-    if (op != LNSB_GLU_SWIGLU) return LNSB_E_UNSUPPORTED;
     if (ncols == 0 || nrows == 0) return 0;
     if (gate == nullptr || up == nullptr || dst_lns == nullptr || gate_stride < ncols || up_stride < ncols) return LNSB_E_INVALID;
     const dev_tables * T = nullptr;
@@ -3335,8 +3384,8 @@ int lnsb_glu_lns(int fmt, int op, const float * gate, const float * up, int64_t 
     if (st != 0) return st;
     const unsigned g = grid_for(ncols * nrows, 256);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (fmt == LNSB_XLNS16) launch_k(k_swiglu<16, true>, g, 256, 0, s, *T, gate, up, gate_stride, up_stride, dst_lns, ncols, nrows);
-    else                    launch_k(k_swiglu<32, true>, g, 256, 0, s, *T, gate, up, gate_stride, up_stride, dst_lns, ncols, nrows);
+    if (fmt == LNSB_XLNS16) launch_glu<16, true>(op, g, s, *T, gate, up, gate_stride, up_stride, dst_lns, ncols, nrows);
+    else                    launch_glu<32, true>(op, g, s, *T, gate, up, gate_stride, up_stride, dst_lns, ncols, nrows);
     return launch_status();
 }
 
@@ -3405,7 +3454,7 @@ int lnsb_attn_decode(int fmt, const lnsb_attn_decode_args * a, lnsb_stream_t str
         const host_tables & H = get_host_tables(false, false);
         uint32_t b;
         std::memcpy(&b, &a->scale, 4);
-        scale_l = H.conv16[b >> 16];
+        scale_l = H.conv16[b >> 15];
     } else {
         scale_l = host_from_f32_32(a->scale);
     }

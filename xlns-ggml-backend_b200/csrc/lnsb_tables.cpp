@@ -10,6 +10,38 @@
 #include <mutex>
 
 namespace lnsb {
+
+// e^x in double: range reduction by 2^n (n = x log2(e) rounded to nearest),
+// then the Taylor series of e^r, r = (x log2(e) - n) ln 2, to degree 14 by
+// Horner's rule with explicit fused multiply-adds; |x| clamped to 700.  The
+// device's lnsb_exp_d is the same sequence of correctly rounded operations,
+// so both give the same bits.
+double host_exp_d(double xd) {
+    if (xd != xd) return xd;
+    if (xd > 700.0) xd = 700.0;
+    if (xd < -700.0) xd = -700.0;
+    const double t = xd * 1.4426950408889634074;
+    const double n = std::nearbyint(t);
+    const double r = (t - n) * 0.69314718055994530942;
+    static const double c[15] = {
+        1.0, 1.0, 1.0 / 2, 1.0 / 6, 1.0 / 24, 1.0 / 120, 1.0 / 720, 1.0 / 5040, 1.0 / 40320,
+        1.0 / 362880, 1.0 / 3628800, 1.0 / 39916800, 1.0 / 479001600, 1.0 / 6227020800.0,
+        1.0 / 87178291200.0 };
+    double p = c[14];
+    for (int i = 13; i >= 0; i--) p = std::fma(p, r, c[i]);
+    return std::ldexp(p, (int) n);
+}
+
+// float e^x: the same series from the float argument clamped to 200, one
+// rounding to float (the host twin of the device's lnsb_expf)
+float host_expf(float x) {
+    if (x != x) return x;
+    double xd = (double) x;
+    if (xd > 200.0) xd = 200.0;
+    if (xd < -200.0) xd = -200.0;
+    return (float) host_exp_d(xd);
+}
+
 namespace {
 
 constexpr long double k_ln2 = 0.693147180559945309417232121458176568L;
@@ -47,13 +79,20 @@ void build16(host_tables & t) {
     }
     t.sbdb16.resize(k16_tab_bytes16 / 2, 0);               // padded to 16 bytes for cp.async copies
 
-    t.conv16.resize(65536);
-    for (uint32_t i = 0; i < 65536; i++) {
-        const uint32_t bits = i << 16;
-        float f;
-        std::memcpy(&f, &bits, 4);
-        const uint16_t sign = (i & 0x8000u) ? 0x8000u : 0;
-        const float a = std::fabs(f);
+    // float -> xlns16, indexed by the float's upper 17 bits (bits >> 15: the
+    // sign, the 8 exponent bits and the top 8 mantissa bits).  The log field
+    // is the truncating conversion (int)(log2(b) * 128) of the bucket's lower
+    // edge b; the sign is the float's.  This is the reference's 65536-entry
+    // magnitude table (README.md:75-76) with the sign folded in, so a
+    // conversion is one load; it reproduces the reference's conversion
+    // statistics (experiments/dot-product-scaling/results/convert.jsonl:1).
+    // Zeros and NaNs give the unsigned zero code; |x| >= 2^128 saturates.
+    t.conv16.resize(131072);
+    for (uint32_t i = 0; i < 131072; i++) {
+        const uint32_t bits = (i & 0xFFFFu) << 15;
+        float a;
+        std::memcpy(&a, &bits, 4);
+        const uint16_t sign = (i & 0x10000u) ? 0x8000u : 0;
         uint16_t code;
         if (a == 0.0f || a != a) {
             code = 0;
@@ -69,27 +108,42 @@ void build16(host_tables & t) {
         t.conv16[i] = code;
     }
 
+    // xlns16 -> float: 2^(l/128) rounded to float, held to 7 significant
+    // decimal digits, rounded to float again (the precision the reference's
+    // decodes carry: 2^(491/128) reads 14.280130)
     t.dec16.resize(65536);
     for (uint32_t c = 0; c < 65536; c++) {
         if ((c & 0x7FFFu) == 0) {
             t.dec16[c] = 0.0f;
             continue;
         }
-        double v = std::pow(2.0, (double) ((int) (c & 0x7FFFu) - 0x4000) / 128.0);
+        const float f = (float) std::pow(2.0, (double) ((int) (c & 0x7FFFu) - 0x4000) / 128.0);
         char buf[32];
-        std::snprintf(buf, sizeof buf, "%.7g", v);
-        v = std::strtod(buf, nullptr);
+        std::snprintf(buf, sizeof buf, "%.7g", (double) f);
+        const double v = std::strtod(buf, nullptr);
         t.dec16[c] = (float) ((c & 0x8000u) ? -v : v);
     }
 
-    // exp: the log of e^x is x log2(e), taken to F=7 by floor from the value's
-    // float x = xlns162fp(c) (the rule the reference's printed swiglu pins)
+    // exp: the log of e^x is x log2(e), taken to F=7 by truncation toward zero
+    // from the value's float x = xlns162fp(c) (the rule the reference's
+    // printed softmax, tanh and geglu figures pin)
     t.exp16.resize(65536);
     for (uint32_t c = 0; c < 65536; c++) {
-        long q = (long) std::floor((double) t.dec16[c] * 1.4426950408889634 * 128.0) + 0x4000L;
+        long q = (long) ((double) t.dec16[c] * 1.4426950408889634 * 128.0) + 0x4000L;
         if (q < 0) q = 0;
         if (q > 0x7FFF) q = 0x7FFF;
         t.exp16[c] = (uint16_t) q;
+    }
+
+    // sigmoid: entry c = the float 1 / (1 + e^-x), x = xlns162fp(c), through
+    // the conversion table (e^-x from host_expf); silu(x) = x * sigmoid(x)
+    // reproduces the reference's printed swiglu
+    t.sig16.resize(65536);
+    for (uint32_t c = 0; c < 65536; c++) {
+        const float sg = 1.0f / (1.0f + host_expf(-t.dec16[c]));
+        uint32_t b;
+        std::memcpy(&b, &sg, 4);
+        t.sig16[c] = t.conv16[b >> 15];
     }
 
     t.monte16.assign(2 * k16_monte_n, 0);

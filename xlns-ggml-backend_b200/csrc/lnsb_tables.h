@@ -103,9 +103,10 @@ constexpr int32_t k32f_none    = -(1 << 30);
 struct host_tables {
     // xlns16
     std::vector<int16_t>  sbdb16;      // k16_tab_bytes / 2 entries, smem image
-    std::vector<uint16_t> conv16;      // 65536
+    std::vector<uint16_t> conv16;      // 131072, indexed by a float's bits >> 15
     std::vector<float>    dec16;       // 65536
     std::vector<uint16_t> exp16;       // 65536
+    std::vector<uint16_t> sig16;       // 65536
     std::vector<int16_t>  monte16;     // [2 * k16_monte_n]: sb fine, then db fine
     std::vector<int32_t>  key16;       // k16_key_bytes / 4 entries, see k16_key_max
     std::vector<int32_t>  mkey16;      // k16m_key_bytes / 4 entries, see k16m_key_max
@@ -122,6 +123,11 @@ struct host_tables {
     std::vector<uint16_t> lfsr_log;    // 65536 (Monte jump-ahead)
     std::vector<uint16_t> lfsr_alog;   // 65535
 };
+
+// e^x in double and float, the host twins of the device's lnsb_exp_d and
+// lnsb_expf (bit-identical: the same correctly rounded operations)
+double host_exp_d(double x);
+float host_expf(float x);
 
 // Builds (once) and returns the tables.  need32: LNS32 conversion tables;
 // need_lpvip: the 2^23-entry LPVIP singular-branch table.
