@@ -2,22 +2,31 @@
 """Benchmark of the LNS16 mul_mat hot path (G-LNSadd/s), one JSON line.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--mode base]
-                    [--workload configs1|configs0]
+                    [--workload configs0|configs1]
 
-Workload (default configs1): BASELINE configs[1]'s mul_mat -- weights
-1536 x 576 (ggml src0 ne=(576,1536)), activations 576 x 512 (src1 ne=(576,512)),
-xlns16 codes converted from numpy default_rng(1) N(0,0.02) / N(0,1) values;
-dst 512 x 1536 xlns16 codes.  One step = one lnsb_mul_mat_lns call (the whole
-op, every chain in element order).  configs0 is the reference's own CPU case
-(576 x 1536 by 1536 x 8, K = 1536).
+Headline workload (default configs0): BASELINE configs[0], the case the
+metric is quoted on ("@K=1536") -- weights 576 x 1536 (ggml src0
+ne=(1536,576)), activations 1536 x 8 (src1 ne=(1536,8)), xlns16 codes
+converted from numpy default_rng(0) N(0,0.02) / N(0,1) values; dst 8 x 576
+xlns16 codes.  One step = one lnsb_mul_mat_lns call (the whole op, every
+chain in element order).  configs1 (BASELINE configs[1]'s mul_mat, 1536 x 576
+by 576 x 512) is reported beside it, and can be the headline instead.
 
-N > 1 (torchrun): weak scaling by output-row sharding -- each rank owns 1536
-different weight rows of a (1536 * N)-row matrix, computes its shard and the
-step ends with an NCCL all-gather of the output shards (the exchange step).
+Beside the headline: configs[1] with its own roofline, MUL_MAT_ID, the typed
+weight decode, configs[1]'s normalisers against their chain bounds, the
+configs[4] sweep points (8192 x 14336, N in {1, 16, 128}, sum32, output rows
+split across the GPUs) and the model decodes of configs[2] / configs[3].
+
+N > 1 (torchrun): weak scaling of the headline by output-row sharding -- each
+rank owns its own weight rows of a (M * N)-row matrix, computes its shard,
+and the step ends with the all-gather of the output shards fused into the
+mul_mat's store (peer-memory stores over NVLink into two gather buffers used
+by step parity, then a bounded peer-flag barrier).  configs[4] is strong
+scaling: its 8192 rows are split N ways, gathered the same way.
 
 --impl reference: the reference's CPU algorithm (the oracle restatement under
 oracle/, the reference itself cannot be built: its arithmetic library is
-absent) timed on this host's cores on a bounded sample of the same workload.
+absent) timed on this host's cores on the same workload.
 """
 import argparse
 import ctypes
@@ -35,10 +44,10 @@ sys.path.insert(0, os.path.join(ROOT, "xlns-ggml-backend_b200"))
 METRIC = "LNS16 mul_mat G-LNSadd/s"
 UNIT = "G-LNSadd/s"
 WORKLOADS = {
+    "configs0": dict(desc="BASELINE configs[0] LNS16 mul_mat (K=1536): W 576x1536 x X 1536x8 -> 8x576 codes",
+                     K=1536, M=576, N=8, seed=0),
     "configs1": dict(desc="BASELINE configs[1] LNS16 mul_mat: W 1536x576 (k-major codes) x X 576x512 -> 512x1536 codes",
                      K=576, M=1536, N=512, seed=1),
-    "configs0": dict(desc="BASELINE configs[0] LNS16 mul_mat: W 576x1536 x X 1536x8 -> 8x576 codes",
-                     K=1536, M=576, N=8, seed=0),
 }
 # Primitive integer operations of one LNS addition (including the operand
 # product and the table load) in this build's restated algorithm, fixed per
@@ -54,12 +63,11 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--mode", default=None, help="sum mode library (default: base; sum32 for configs4)")
-    p.add_argument("--workload", default="configs1", choices=sorted(WORKLOADS) + ["configs4"])
-    p.add_argument("--sweep-k", type=int, default=4096, help="configs4: K in {2048, 4096, 8192, 14336}")
-    p.add_argument("--sweep-n", type=int, default=16, help="configs4: tokens in {1, 16, 128}")
+    p.add_argument("--mode", default="base", help="sum mode library of the headline (default base)")
+    p.add_argument("--workload", default="configs0", choices=sorted(WORKLOADS))
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--no-decode", action="store_true", help="skip the model decode measurement")
+    p.add_argument("--no-decode", action="store_true", help="skip the model decode measurements")
+    p.add_argument("--no-sides", action="store_true", help="the headline only (no side objects)")
     p.add_argument("--decode-mode", default="sum32", help="sum mode of the decode (BASELINE configs[2]: sum32)")
     return p.parse_args()
 
@@ -75,13 +83,12 @@ def peaks():
 
 # ncu capture summary of the kernel each (workload, mode) runs (DRAM bytes of one launch)
 PROFILE = {
+    ("configs0", "base"): "profiles/k_mul_mat16_res2_configs0.md",
     ("configs1", "base"): "profiles/k_mul_mat16_fast4_configs1.md",
-    ("configs0", "base"): "profiles/k_mul_mat16_res_configs0.md",
     ("configs1", "monte"): "profiles/k_mul_mat16_fast_monte_configs1.md",
     ("configs1", "sum32"): "profiles/k_mul_mat_a32_sum32_configs1.md",
     ("configs1", "lpvip"): "profiles/k_mul_mat_a32_lpvip_configs1.md",
     ("configs1", "monte_bylpvip"): "profiles/k_mul_mat_a32_monte_bylpvip_configs1.md",
-    ("configs4:4096:16", "sum32"): "profiles/k_mul_mat_a32_sum32_configs4_K4096_N16.md",
 }
 
 
@@ -154,8 +161,9 @@ class ClockSampler:
 # ------------------------------------------------------------------ CPU baseline (the checker's port)
 
 def cpu_leg(wl, mode, seconds, nthreads):
-    """Times the oracle's mul_mat (the reference algorithm restated in C) on a
-    bounded sample of the workload: the first R weight rows against all tokens."""
+    """Times the oracle's mul_mat (the reference algorithm restated in C) on the
+    workload: the whole op, repeated to about `seconds`, or its first R weight
+    rows against every token where one op takes longer than that."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import oracle
@@ -168,12 +176,19 @@ def cpu_leg(wl, mode, seconds, nthreads):
     oracle.mul_mat16(mode, w[:rows], x, nthreads=nthreads)
     dt = time.perf_counter() - t0
     rows = int(max(1, min(M, rows * seconds / max(dt, 1e-6))))
+    reps = 1
+    if rows == M:
+        t0 = time.perf_counter()
+        oracle.mul_mat16(mode, w, x, nthreads=nthreads)
+        reps = max(1, int(seconds / max(time.perf_counter() - t0, 1e-6)))
     t0 = time.perf_counter()
-    oracle.mul_mat16(mode, w[:rows], x, nthreads=nthreads)
+    for _ in range(reps):
+        oracle.mul_mat16(mode, w[:rows], x, nthreads=nthreads)
     dt = time.perf_counter() - t0
-    adds = adds_of(K, rows, N)
+    adds = adds_of(K, rows, N) * reps
+    what = ("the whole op x %d" % reps) if rows == M else ("first %d of %d weight rows x all %d tokens" % (rows, M, N))
     return {"value": adds / dt / 1e9, "unit": UNIT, "cores": nthreads, "kind": "port",
-            "sample": "first %d of %d weight rows x all %d tokens x K=%d (%d LNS adds, %.1f s)" % (rows, M, N, K, adds, dt)}
+            "sample": "%s, K=%d (%d LNS adds, %.1f s)" % (what, K, adds, dt)}
 
 
 def run_reference(args, wl):
@@ -183,7 +198,7 @@ def run_reference(args, wl):
     nthreads = os.cpu_count() or 1
     vals = []
     for _ in range(args.warmup):
-        cpu_leg(wl, args.mode, 0.5, nthreads)
+        cpu_leg(wl, args.mode, 0.3, nthreads)
     t0 = time.perf_counter()
     leg = None
     for _ in range(args.steps):
@@ -196,13 +211,122 @@ def run_reference(args, wl):
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": wall * 1000 / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u16 (xlns16 codes)", "data": "synthetic",
-        "config": {"workload": wl["desc"] + " [bounded sample per step on host cores]", "mode": args.mode},
+        "config": {"workload": wl["desc"], "mode": args.mode, "sample": "per step: " + leg["sample"]},
         "cpu_baseline": leg, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
     return 0
 
 
-# ------------------------------------------------------------------ GPU
+# ------------------------------------------------------------------ GPU helpers
+
+class Ctx:
+    """Per-process state: the rank, the process group, the L2 flush buffer,
+    the stream and (N > 1) the peer-flag barrier of the fused all-gathers,
+    whose epoch counts every barrier of the run (all ranks take the same
+    steps in the same order)."""
+
+    def __init__(self, torch, dist, rank, world):
+        self.torch, self.dist, self.rank, self.world = torch, dist, rank, world
+        self.flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device="cuda")   # 256 MB > L2 (126 MB)
+        self.stream = torch.cuda.current_stream()
+        self.sp = ctypes.c_void_p(self.stream.cuda_stream)
+        self.epoch = 0
+        self.launches = 0
+        if world > 1:
+            import torch.distributed._symmetric_memory as symm_mem
+            self.symm = symm_mem
+            self.fbuf = symm_mem.empty(world, dtype=torch.int32, device="cuda")
+            self.fbuf.zero_()
+            self.fhdl = symm_mem.rendezvous(self.fbuf, dist.group.WORLD)
+            self.berr = torch.zeros(1, dtype=torch.int32, device="cuda")
+            torch.cuda.synchronize()
+            dist.barrier()
+
+    def barrier(self, lib):
+        self.epoch += 1
+        return lib.lnsb_group_barrier(ctypes.c_void_p(self.fhdl.buffer_ptrs_dev), self.world, self.rank, self.epoch,
+                                      ctypes.c_void_p(self.berr.data_ptr()), self.sp)
+
+    def check_barrier(self):
+        if self.world > 1 and self.berr.item() != 0:
+            raise SystemExit("peer barrier timed out")
+
+    def max_over_ranks(self, *vals):
+        if self.world == 1:
+            return list(vals)
+        t = self.torch.tensor(list(vals), dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return t.tolist()
+
+
+class FusedGather:
+    """Two symmetric-memory gather buffers of [N][M * world] codes used by step
+    parity (the write-after-read rule of lnsb_mul_mat_lns_peers: each step's
+    result is read on this rank's stream before its next call)."""
+
+    def __init__(self, ctx, lib, fmt, N, M):
+        torch = ctx.torch
+        dt = torch.int16 if fmt == 16 else torch.int32
+        self.ctx, self.lib, self.fmt, self.N, self.M = ctx, lib, fmt, N, M
+        self.bufs = [ctx.symm.empty(N * M * ctx.world, dtype=dt, device="cuda") for _ in range(2)]
+        for b in self.bufs:
+            b.fill_(-1)
+        self.hdls = [ctx.symm.rendezvous(b, ctx.dist.group.WORLD) for b in self.bufs]
+        import lnsb200
+        self.peers = [lnsb200._lib.PeerOut(h.buffer_ptrs_dev, ctx.world, M * ctx.world, ctx.rank * M) for h in self.hdls]
+        self.i = 0
+        torch.cuda.synchronize()
+        ctx.dist.barrier()
+
+    def step(self, argp, status):
+        """one mul_mat with the gather fused into its store, then the barrier;
+        returns the buffer that holds the gathered result"""
+        b = self.i % 2
+        self.i += 1
+        st = self.lib.lnsb_mul_mat_lns_peers(self.fmt, argp, ctypes.byref(self.peers[b]), self.ctx.sp)
+        st2 = self.ctx.barrier(self.lib)
+        if st != 0 or st2 != 0:
+            status[0] = st or st2
+        self.ctx.launches += 2
+        return self.bufs[b]
+
+
+def timed(ctx, fn, steps, warmup, flush=True):
+    """device time of `steps` calls of fn (ms, list), L2 flushed before each,
+    after `warmup` untimed calls; max over ranks of the total"""
+    torch = ctx.torch
+    for _ in range(warmup):
+        if flush:
+            ctx.flush.zero_()
+        fn()
+    torch.cuda.synchronize()
+    if ctx.dist:
+        ctx.dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        if flush:
+            ctx.flush.zero_()
+        ev[i][0].record(ctx.stream)
+        fn()
+        ev[i][1].record(ctx.stream)
+    torch.cuda.synchronize()
+    ms = [b.elapsed_time(e) for b, e in ev]
+    total, = ctx.max_over_ranks(sum(ms))
+    return total / steps
+
+
+def lns_operands(torch, np, ks, K, M, N, seed, rank=0):
+    rng = np.random.default_rng(seed + 1000 * rank)
+    w_f32 = torch.from_numpy(rng.normal(0, 0.02, (M, K)).astype(np.float32)).cuda()    # ggml src0 rows
+    x_f32 = torch.from_numpy(rng.normal(0, 1, (N, K)).astype(np.float32)).cuda()
+    w = torch.empty(K * M, dtype=torch.int16, device="cuda")                          # k-major codes
+    x = torch.empty(N * K, dtype=torch.int16, device="cuda")
+    ks.to_lns_transposed(w_f32, w, M, K, M)
+    ks.to_lns(x_f32, x)
+    return w, x, rng
+
+
+# ------------------------------------------------------------------ the headline
 
 def run_ours(args, wl):
     import numpy as np
@@ -219,103 +343,43 @@ def run_ours(args, wl):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+    ctx = Ctx(torch, dist, rank, world)
 
     K, M, N = wl["K"], wl["M"], wl["N"]
-    strong = wl.get("strong", False)
-    if strong:
-        from lnsb200 import shard
-        if M % world:
-            raise SystemExit("configs4 needs the 8192 rows to divide by the GPU count")
-        M = M // world                       # this rank's rows
     ks = lnsb200.KernelSet(16, args.mode)
     ks.upload_tables()
-    rng = np.random.default_rng(wl["seed"] + 1000 * rank)
-    w_f32 = torch.from_numpy(rng.normal(0, 0.02, (M, K)).astype(np.float32)).cuda()    # ggml src0 rows
-    x_f32 = torch.from_numpy(rng.normal(0, 1, (N, K)).astype(np.float32)).cuda()
-    w = torch.empty(K * M, dtype=torch.int16, device="cuda")                          # k-major codes
-    x = torch.empty(N * K, dtype=torch.int16, device="cuda")
-    ks.to_lns_transposed(w_f32, w, M, K, M)
-    ks.to_lns(x_f32, x)
+    lib = ks.lib
+    w, x, rng = lns_operands(torch, np, ks, K, M, N, wl["seed"], rank)
     out = torch.empty(N * M, dtype=torch.int16, device="cuda")
-    from lnsb200 import shard
-    flush = torch.empty(64 * 1024 * 1024, dtype=torch.int32, device="cuda")          # 256 MB > L2 (126 MB)
-    stream = torch.cuda.current_stream()
-
     # the timed call goes straight to the C ABI with prebuilt arguments, so
     # host-side Python work cannot open gaps inside the event-timed region
-    lib = ks.lib
     mm_args = lnsb200.MulMatArgs(w.data_ptr(), x.data_ptr(), None, K, M, N, 1, 1, 1, 1, 7)
     mm_argp = ctypes.byref(mm_args)
     out_p = ctypes.c_void_p(out.data_ptr())
-    stream_p = ctypes.c_void_p(stream.cuda_stream)
-    mm = lib.lnsb_mul_mat_lns
     status = [0]
 
-    # N > 1, weak scaling: the all-gather of the output-row shards fused into
-    # the mul_mat's store over NVLink peer memory (a symmetric-memory buffer
-    # on every GPU, plain stores), then a device-side barrier; NCCL's
-    # all-gather where the fused store does not apply
-    gather = "nccl all_gather_into_tensor + permute"
-    peer = None
-    if world > 1 and not strong and args.mode in ("base", "monte"):
-        try:
-            import torch.distributed._symmetric_memory as symm_mem
-            gbuf = symm_mem.empty(N * M * world, dtype=torch.int16, device="cuda")
-            hdl = symm_mem.rendezvous(gbuf, dist.group.WORLD)
-            fbuf = symm_mem.empty(world, dtype=torch.int32, device="cuda")
-            fbuf.zero_()
-            fhdl = symm_mem.rendezvous(fbuf, dist.group.WORLD)
-            berr = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gather = None
+    if world > 1:
+        from lnsb200 import shard
+        gather = FusedGather(ctx, lib, 16, N, M)
+        # the fused gather must give what NCCL's does, bit for bit, on two steps
+        for _ in range(2):
+            g = gather.step(mm_argp, status)
+            lib.lnsb_mul_mat_lns(16, mm_argp, out_p, ctx.sp)
+            want = shard.all_gather_rows(out.view(N, M), world).contiguous().view(-1)
             torch.cuda.synchronize()
-            dist.barrier()
-            peer = lnsb200._lib.PeerOut(hdl.buffer_ptrs_dev, world, M * world, rank * M)
-            peer_p = ctypes.byref(peer)
-            mmp = lib.lnsb_mul_mat_lns_peers
-            epoch = [0]
-            gather = "fused into the mul_mat store: peer-memory stores over NVLink + a bounded peer-flag barrier"
-        except Exception as e:                                     # noqa: BLE001
-            peer = None
-            gather = "nccl all_gather_into_tensor + permute (symmetric memory unavailable: %s)" % str(e).splitlines()[0][:120]
-
-    def launch():
-        st = mmp(16, mm_argp, peer_p, stream_p) if peer is not None else mm(16, mm_argp, out_p, stream_p)
-        if st != 0:
-            status[0] = st
-
-    def gather_step():
-        if peer is not None:
-            epoch[0] += 1
-            st = lib.lnsb_group_barrier(ctypes.c_void_p(fhdl.buffer_ptrs_dev), world, rank, epoch[0],
-                                        ctypes.c_void_p(berr.data_ptr()), stream_p)
-            if st != 0:
-                status[0] = st
-        else:
-            shard.all_gather_rows(out.view(N, M), world).contiguous()
+            ctx.check_barrier()
+            if not torch.equal(g, want):
+                raise SystemExit("fused peer all-gather differs from the NCCL all-gather")
 
     def step():
-        launch()
-        if world > 1:
-            gather_step()
-
-    if peer is not None:
-        # the fused gather must give what NCCL's does, bit for bit
-        gbuf.fill_(-1)
-        torch.cuda.synchronize()
-        dist.barrier()
-        launch()
-        gather_step()
-        mm(16, mm_argp, out_p, stream_p)
-        want = shard.all_gather_rows(out.view(N, M), world).contiguous().view(-1)
-        torch.cuda.synchronize()
-        if berr.item() != 0:
-            raise SystemExit("peer barrier timed out")
-        if not torch.equal(gbuf, want):
-            raise SystemExit("fused peer all-gather differs from the NCCL all-gather")
-
-    for _ in range(args.warmup):
-        flush.zero_()
-        step()
-    torch.cuda.synchronize()
+        if gather is not None:
+            gather.step(mm_argp, status)
+        else:
+            st = lib.lnsb_mul_mat_lns(16, mm_argp, out_p, ctx.sp)
+            if st != 0:
+                status[0] = st
+            ctx.launches += 1
 
     bus = None
     try:
@@ -323,55 +387,135 @@ def run_ours(args, wl):
         bus = "%02x:%02x.0" % (p.pci_bus_id, p.pci_device_id)
     except Exception:
         pass
+    # the launch count of the timed region: this step's kernels only
     sampler = ClockSampler(bus)
     sampler.start()
     time.sleep(0.4)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    if dist:
-        dist.barrier()
+    for _ in range(args.warmup):
+        ctx.flush.zero_()
+        step()
     torch.cuda.synchronize()
-    for i in range(args.steps):
-        flush.zero_()                      # untimed: L2 flushed before every step
-        ev[i][0].record(stream)
-        launch()
-        ev[i][1].record(stream)
-        if world > 1:
-            gather_step()                  # ggml [N][M*world] order on every GPU
-        ev[i][2].record(stream)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
+    ctx.launches = 0
+    step_ms = timed(ctx, step, args.steps, 0)
+    launches = ctx.launches
     clocks = sampler.stop()
     if status[0] != 0:
         raise lnsb200.LnsbError(lib, "lnsb_mul_mat_lns", status[0])
-    if peer is not None and berr.item() != 0:
-        raise SystemExit("peer barrier timed out")
-    step_ms = sum(a.elapsed_time(c) for a, b, c in ev)
-    kern_ms = sum(a.elapsed_time(b) for a, b, c in ev)
-    if dist:
-        t = torch.tensor([step_ms, kern_ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        step_ms, kern_ms = t.tolist()
+    ctx.check_barrier()
+    # the mul_mat alone (N > 1: without its gather stores and barrier)
+    kern_ms = step_ms if world == 1 else timed(ctx, lambda: lib.lnsb_mul_mat_lns(16, mm_argp, out_p, ctx.sp), args.steps, 2)
 
-    # e2e through the C ABI with host buffers: every step uploads its F32
-    # activations from pinned host memory (H2D), converts them (to_lns), runs
-    # mul_mat with F32 out and reads the F32 result back into pinned host
-    # memory (D2H); the weights stay resident, as the reference's weight cache
-    # keeps them.  Steps are double buffered the way a serving loop runs them:
-    # step i+1's upload and step i's read-back go on their own copy streams,
-    # so the copies overlap the kernels of the neighbouring steps.
-    NB = 2
+    e2e_ms, h2d, d2h = e2e_run(ctx, ks, w, rng, K, M, N, gather, mm_args, args)
+
+    adds = adds_of(K, M, N)
+    value = adds * world / (step_ms / 1000) / 1e9
+    e2e_val = adds * world / (e2e_ms / 1000) / 1e9
+    hbm, smmax, src = peaks()
+    f_mhz = clocks.get("sm_mhz") or smmax
+    c = C_MODE.get(args.mode, 18)
+    int_peak = SMS * LANES_PER_SM * f_mhz * 1e6 / c / 1e9
+    kern_s = kern_ms / 1000
+    achieved = adds / kern_s / 1e9
+    bytes_alg = algorithmic_bytes(K, M, N)
+    roof = {"bound": "int", "achieved": achieved, "peak": int_peak, "unit": UNIT, "frac": achieved / int_peak,
+            "traffic": traffic_of((args.workload, args.mode)), "traffic_source": PROFILE.get((args.workload, args.mode)),
+            "c_mode": c, "sm_mhz_used": f_mhz,
+            "note": "integer-issue bound: %d SMs x %d lanes x f_sm / c_mode (%s SM clock)" % (
+                SMS, LANES_PER_SM, "sampled" if clocks.get("sm_mhz") else src),
+            "hbm": {"achieved_gbs": bytes_alg / kern_s / 1e9, "peak_gbs": hbm, "frac": bytes_alg / kern_s / 1e9 / hbm,
+                    "algorithmic_bytes": bytes_alg}}
+    if args.mode == "base" and args.workload == "configs0":
+        # the chain bound: K - 1 dependent additions per output, every output in
+        # parallel; L_add measured live on this GPU (lnsb_add_latency, key form, 16
+        # distinct chains per warp as the latency kernel runs configs[0])
+        l_add = ks.add_latency(0, 16, 4096)
+        t_chain = (K - 1) * l_add / (f_mhz * 1e6)
+        roof["chain"] = {"l_add_cycles": l_add, "lanes": 16, "t_chain_us": t_chain * 1e6, "kernel_us": kern_ms * 1000,
+                         "frac": t_chain / kern_s,
+                         "note": "diagnostic bound T_chain = (K-1) L_add / f_sm; the event-timed kernel includes its launch"}
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u16 (xlns16 codes; integer LNS arithmetic)", "data": "synthetic",
+        "config": {"workload": wl["desc"] + (" per rank, output rows sharded + fused all-gather" if world > 1 else ""),
+                   "K": K, "M": M, "N": N, "mode": args.mode, "parallelism": "rowshard%d" % world,
+                   "gather": ("fused into the mul_mat store: peer-memory stores over NVLink into two gather buffers "
+                              "by step parity + a bounded peer-flag barrier (checked bit for bit against NCCL)")
+                   if world > 1 else None,
+                   "l2": "flushed (256 MB write) before every timed step"},
+        "roofline": roof,
+        "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "per step: H2D of F32 activations (pinned), lnsb_to_lns, " +
+                        ("lnsb_mul_mat (F32 out)" if world == 1 else
+                         "lnsb_mul_mat_lns_peers + lnsb_group_barrier (the fused all-gather), lnsb_to_f32 of the gathered codes") +
+                        ", D2H of the F32 result (pinned); double buffered, copies on their own streams"},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if not args.no_sides:
+        other = "configs1" if args.workload == "configs0" else "configs0"
+        line[other] = time_side_mul_mat(ctx, lnsb200, torch, np, WORKLOADS[other], args, int_peak, f_mhz)
+        line["configs4"] = time_configs4(ctx, lnsb200, torch, np, args, f_mhz)
+        if world == 1:
+            line["mul_mat_id"] = time_mul_mat_id(ctx, lnsb200, torch, np, args, int_peak)
+            line["weights"] = time_weights(ctx, lnsb200, torch, np, args, hbm)
+            line["normalisers"] = time_norms(ctx, lnsb200, torch, np, args, f_mhz)
+    if not args.no_decode:
+        # the metric's second half: model decode tok/s (BASELINE configs[2]), one sequence per GPU
+        line["decode"] = run_decode(torch, dist, rank, world, args, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
+        if world == 1:
+            # BASELINE configs[3]: the same model and prompt in LNS32, on 1 GPU
+            line["decode_lns32"] = run_decode(torch, dist, rank, world, args,
+                                              cpu=(rank == 0 and not args.no_cpu_baseline), fmt=32)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_leg(wl, args.mode, 10.0, os.cpu_count() or 1)
+        # the reference's CPU backend runs one thread (its ops are sequential loops): the
+        # same port on one core, beside the all-cores figure, and the GPU's ratio to each
+        st = cpu_leg(wl, args.mode, 5.0, 1)
+        line["cpu_baseline"]["single_thread"] = st
+        line["cpu_baseline"]["gpu_ratio"] = {"all_cores": value / line["cpu_baseline"]["value"],
+                                             "single_thread": value / st["value"],
+                                             "e2e_all_cores": e2e_val / line["cpu_baseline"]["value"],
+                                             "e2e_single_thread": e2e_val / st["value"]}
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def e2e_run(ctx, ks, w, rng, K, M, N, gather, mm_args, args):
+    """End to end through the C ABI with host buffers: every step uploads its
+    F32 activations from pinned host memory (H2D), converts them (to_lns), runs
+    mul_mat -- at N > 1 with the fused all-gather and its barrier, then the
+    gathered codes' decode (to_f32) -- and reads the F32 result back into
+    pinned host memory (D2H); the weights stay resident, as the reference's
+    weight cache keeps them.  Steps are double buffered the way a serving
+    loop runs them: step i+1's upload and step i's read-back go on their own
+    copy streams, so the copies overlap the kernels of the neighbouring
+    steps.  Returns (ms per step, max over ranks; H2D bytes; D2H bytes)."""
+    import numpy as np
+    torch = ctx.torch
+    import lnsb200
+    NB, world = 2, ctx.world
+    MO = M * world
     xh = torch.from_numpy(rng.normal(0, 1, (N, K)).astype(np.float32)).pin_memory()
-    yh = [torch.empty(N * M, dtype=torch.float32).pin_memory() for _ in range(NB)]
+    yh = [torch.empty(N * MO, dtype=torch.float32).pin_memory() for _ in range(NB)]
     xd = [torch.empty(N * K, dtype=torch.float32, device="cuda") for _ in range(NB)]
     xc = [torch.empty(N * K, dtype=torch.int16, device="cuda") for _ in range(NB)]
-    yd = [torch.empty(N * M, dtype=torch.float32, device="cuda") for _ in range(NB)]
+    yd = [torch.empty(N * MO, dtype=torch.float32, device="cuda") for _ in range(NB)]
+    args_b = [lnsb200.MulMatArgs(w.data_ptr(), xc[b].data_ptr(), yd[b].data_ptr(), K, M, N, 1, 1, 1, 1, 7)
+              for b in range(NB)]
+    stream = ctx.stream
     up, down = torch.cuda.Stream(), torch.cuda.Stream()
     ev_up = [torch.cuda.Event() for _ in range(NB)]        # input b uploaded
     ev_cv = [torch.cuda.Event() for _ in range(NB)]        # input b converted: xd[b] free
     ev_mm = [torch.cuda.Event() for _ in range(NB)]        # result b computed
     ev_dn = [torch.cuda.Event() for _ in range(NB)]        # result b read back: yd[b] free
+    status = [0]
 
     def upload(i):
         b = i % NB
@@ -386,7 +530,11 @@ def run_ours(args, wl):
         stream.wait_event(ev_dn[b])
         ks.to_lns(xd[b], xc[b], stream=stream)
         ev_cv[b].record(stream)
-        ks.mul_mat(w, xc[b], yd[b], K, M, N, monte_seed=7, stream=stream)
+        if gather is None:
+            ks.lib.lnsb_mul_mat(16, ctypes.byref(args_b[b]), ctx.sp)
+        else:
+            g = gather.step(ctypes.byref(args_b[b]), status)
+            ks.to_f32(g, yd[b], stream=stream)             # the read of this step's gather, on this stream
         ev_mm[b].record(stream)
 
     def download(i):
@@ -396,7 +544,7 @@ def run_ours(args, wl):
             yh[b].copy_(yd[b], non_blocking=True)
         ev_dn[b].record(down)
 
-    def e2e_run(n):
+    def run(n):
         up.wait_stream(stream)
         upload(0)
         for i in range(n):
@@ -406,123 +554,147 @@ def run_ours(args, wl):
             download(i)
         stream.wait_event(ev_dn[(n - 1) % NB])
 
-    e2e_run(max(3, args.warmup))
+    run(max(3, args.warmup))
     torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
+    if ctx.dist:
+        ctx.dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    e2e_run(args.steps)
+    run(args.steps)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = t.item()
-        dist.barrier()
-
-    adds = adds_of(K, M, N)
-    wkey = "configs4:%d:%d" % (K, N) if strong else args.workload
-    pkey = (wkey, args.mode) if world == 1 or not strong else None   # the captured launch is this rank's launch
-    value = adds * world * args.steps / (step_ms / 1000) / 1e9
-    e2e_val = adds * world * args.steps / (e2e_ms / 1000) / 1e9
-    scaling = "strong" if strong else "weak"
-    kern_s = kern_ms / 1000 / args.steps
-    hbm, smmax, src = peaks()
-    f_mhz = clocks.get("sm_mhz") or smmax
-    c = C_MODE.get(args.mode, 18)
-    int_peak = SMS * LANES_PER_SM * f_mhz * 1e6 / c / 1e9
-    achieved = adds / kern_s / 1e9
-    bytes_alg = algorithmic_bytes(K, M, N)
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step_ms / args.steps, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
-        "dtype": "u16 (xlns16 codes; integer LNS arithmetic)", "data": "synthetic",
-        "config": {"workload": wl["desc"] + ((" per rank" if not strong else "") + ", output rows sharded + all-gather (config.gather)" if world > 1 else ""),
-                   "K": K, "M": M, "N": N, "mode": args.mode, "parallelism": "rowshard%d" % world, "gather": gather if world > 1 else None,
-                   "l2": "flushed (256 MB write) before every timed step"},
-        "roofline": {"bound": "int", "achieved": achieved, "peak": int_peak, "unit": UNIT, "frac": achieved / int_peak,
-                     "traffic": traffic_of(pkey), "traffic_source": PROFILE.get(pkey),
-                     "c_mode": c, "sm_mhz_used": f_mhz,
-                     "note": "integer-issue bound: %d SMs x %d lanes x f_sm / c_mode (%s SM clock)" % (SMS, LANES_PER_SM, "sampled" if clocks.get("sm_mhz") else src),
-                     "hbm": {"achieved_gbs": bytes_alg / kern_s / 1e9, "peak_gbs": hbm, "frac": bytes_alg / kern_s / 1e9 / hbm,
-                             "algorithmic_bytes": bytes_alg}},
-        "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": N * K * 4, "d2h_bytes_per_step": N * M * 4,
-                "path": "per step: H2D of F32 activations (pinned), lnsb_to_lns, lnsb_mul_mat (F32 out), D2H of the F32 "
-                        "result (pinned); double buffered, copies on their own streams overlapping neighbouring steps"},
-        "gpu_launches": args.steps * (2 if peer is not None else 1),   # mul_mat (+ the peer barrier)
-        "clocks": clocks,
-    }
-    if world == 1 and args.workload == "configs1":
-        # BASELINE's metric is quoted at K=1536: configs[0], timed the same way, beside the main line
-        line["k1536"] = time_secondary(lib, lnsb200, torch, np, WORKLOADS["configs0"], args, flush, stream)
-        # the rows beside the path: MUL_MAT_ID and the typed weight decode
-        line["mul_mat_id"] = time_mul_mat_id(lnsb200, torch, np, args, flush, stream, int_peak)
-        line["weights"] = time_weights(lnsb200, torch, np, args, flush, stream, hbm)
-        line["normalisers"] = time_norms(lnsb200, torch, np, args, flush, stream)
-    if args.workload == "configs1" and not args.no_decode:
-        # the metric's second half: model decode tok/s (BASELINE configs[2]), one sequence per GPU
-        line["decode"] = run_decode(torch, dist, rank, world, args, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
-        if world == 1:
-            # BASELINE configs[3]: the same model and prompt in LNS32, on 1 GPU
-            line["decode_lns32"] = run_decode(torch, dist, rank, world, args,
-                                              cpu=(rank == 0 and not args.no_cpu_baseline), fmt=32)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not strong:
-        line["cpu_baseline"] = cpu_leg(wl, args.mode, 10.0, os.cpu_count() or 1)
-        # the reference's CPU backend runs one thread (its ops are sequential loops): the
-        # same port on one core, beside the all-cores figure
-        line["cpu_baseline"]["single_thread"] = cpu_leg(wl, args.mode, 5.0, 1)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if dist:
-        dist.destroy_process_group()
-    return 0
+    if status[0] != 0:
+        raise lnsb200.LnsbError(ks.lib, "lnsb_mul_mat_lns_peers", status[0])
+    ctx.check_barrier()
+    ms, = ctx.max_over_ranks(e0.elapsed_time(e1))
+    if ctx.dist:
+        ctx.dist.barrier()
+    return ms / args.steps, N * K * 4, N * MO * 4
 
 
-def time_secondary(lib, lnsb200, torch, np, wl, args, flush, stream):
-    """Device-timed steps of another workload through the same C ABI call (inputs
-    resident, L2 flushed before every step), for a sub-object of the JSON line."""
+# ------------------------------------------------------------------ side objects
+
+def time_side_mul_mat(ctx, lnsb200, torch, np, wl, args, int_peak, f_mhz):
+    """Another BASELINE mul_mat workload through the same C ABI call (inputs
+    resident, L2 flushed before every step; N > 1: this rank's rows with the
+    fused all-gather), with its roofline."""
     K, M, N = wl["K"], wl["M"], wl["N"]
     ks = lnsb200.KernelSet(16, args.mode)
-    rng = np.random.default_rng(wl["seed"])
-    w_f32 = torch.from_numpy(rng.normal(0, 0.02, (M, K)).astype(np.float32)).cuda()
-    x_f32 = torch.from_numpy(rng.normal(0, 1, (N, K)).astype(np.float32)).cuda()
-    w = torch.empty(K * M, dtype=torch.int16, device="cuda")
-    x = torch.empty(N * K, dtype=torch.int16, device="cuda")
-    ks.to_lns_transposed(w_f32, w, M, K, M)
-    ks.to_lns(x_f32, x)
+    lib = ks.lib
+    w, x, _ = lns_operands(torch, np, ks, K, M, N, wl["seed"], ctx.rank)
     out = torch.empty(N * M, dtype=torch.int16, device="cuda")
     a = lnsb200.MulMatArgs(w.data_ptr(), x.data_ptr(), None, K, M, N, 1, 1, 1, 1, 7)
-    ap, op, sp = ctypes.byref(a), ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream.cuda_stream)
-    for _ in range(args.warmup):
-        flush.zero_()
-        if lib.lnsb_mul_mat_lns(16, ap, op, sp) != 0:
-            raise RuntimeError("lnsb_mul_mat_lns failed on the K=1536 workload")
-    torch.cuda.synchronize()
-    steps = max(args.steps, 20)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    for i in range(steps):
-        flush.zero_()
-        ev[i][0].record(stream)
-        lib.lnsb_mul_mat_lns(16, ap, op, sp)
-        ev[i][1].record(stream)
-    torch.cuda.synchronize()
-    ms = sum(b.elapsed_time(e) for b, e in ev) / steps
-    adds = adds_of(K, M, N)
-    return {"workload": wl["desc"], "mode": args.mode, "steps": steps, "ms_per_step": ms,
-            "value": adds / (ms / 1000) / 1e9, "unit": UNIT,
-            "bound": "chain latency: %d dependent additions per output" % (K - 1),
+    ap, op = ctypes.byref(a), ctypes.c_void_p(out.data_ptr())
+    status = [0]
+    gather = FusedGather(ctx, lib, 16, N, M) if ctx.world > 1 else None
+
+    def call():
+        if gather is not None:
+            gather.step(ap, status)
+        elif lib.lnsb_mul_mat_lns(16, ap, op, ctx.sp) != 0:
+            status[0] = -1
+    ms = timed(ctx, call, max(args.steps, 20), args.warmup)
+    if status[0] != 0:
+        raise RuntimeError("lnsb_mul_mat_lns failed on %s" % wl["desc"])
+    ctx.check_barrier()
+    adds = adds_of(K, M, N) * ctx.world
+    val = adds / (ms / 1000) / 1e9
+    c = C_MODE.get(args.mode, 18)
+    out_d = {"workload": wl["desc"] + (" per rank, fused all-gather" if ctx.world > 1 else ""), "mode": args.mode,
+             "ms_per_step": ms, "value": val, "unit": UNIT,
+             "roofline": {"bound": "int", "achieved": val / ctx.world, "peak": int_peak, "frac": val / ctx.world / int_peak,
+                          "unit": UNIT, "c_mode": c, "traffic": traffic_of((wl_key(wl), args.mode)),
+                          "traffic_source": PROFILE.get((wl_key(wl), args.mode))},
+             "l2": "flushed (256 MB write) before every timed step"}
+    if args.mode == "base" and wl_key(wl) == "configs0":
+        l_add = ks.add_latency(0, 16, 4096)
+        t_chain = (K - 1) * l_add / (f_mhz * 1e6)
+        out_d["roofline"]["chain"] = {"l_add_cycles": l_add, "t_chain_us": t_chain * 1e6, "frac": t_chain / (ms / 1000)}
+    return out_d
+
+
+def wl_key(wl):
+    for k, v in WORKLOADS.items():
+        if v is wl:
+            return k
+    return None
+
+
+def time_configs4(ctx, lnsb200, torch, np, args, f_mhz):
+    """BASELINE configs[4] sweep points (sum32): W 8192 x 14336 N(0,0.02), X
+    14336 x N N(0,1), N in {1, 16, 128}; the 8192 output rows split into
+    ctx.world contiguous blocks (strong scaling), each rank's block gathered
+    on every GPU by the fused peer-store all-gather.  Weights are generated on
+    the device per 1024-row block (torch generator seeded 3000 + block), so
+    every GPU count runs the same matrix; activations numpy default_rng(3)."""
+    K, MT = 14336, 8192
+    world, rank = ctx.world, ctx.rank
+    Mr = MT // world
+    ks = lnsb200.KernelSet(16, "sum32")
+    ks.upload_tables()
+    lib = ks.lib
+    w = torch.empty(K * Mr, dtype=torch.int16, device="cuda")
+    blk = 1024
+    wf = torch.empty((blk, K), dtype=torch.float32, device="cuda")
+    for b in range(Mr // blk):
+        g = torch.Generator(device="cuda")
+        g.manual_seed(3000 + rank * (Mr // blk) + b)
+        wf.normal_(0.0, 0.02, generator=g)
+        ks.to_lns_transposed(wf, w[b * blk:], blk, K, Mr)
+    del wf
+    res = {}
+    for N in (1, 16, 128):
+        xf = torch.from_numpy(np.random.default_rng(3).normal(0, 1, (N, K)).astype(np.float32)).cuda()
+        x = torch.empty(N * K, dtype=torch.int16, device="cuda")
+        ks.to_lns(xf, x)
+        out = torch.empty(N * Mr, dtype=torch.int16, device="cuda")
+        a = lnsb200.MulMatArgs(w.data_ptr(), x.data_ptr(), None, K, Mr, N, 1, 1, 1, 1, 7)
+        ap, op = ctypes.byref(a), ctypes.c_void_p(out.data_ptr())
+        status = [0]
+        gather = FusedGather(ctx, lib, 16, N, Mr) if world > 1 else None
+        if gather is not None:
+            from lnsb200 import shard
+            g = gather.step(ap, status)
+            lib.lnsb_mul_mat_lns(16, ap, op, ctx.sp)
+            want = shard.all_gather_rows(out.view(N, Mr), world).contiguous().view(-1)
+            torch.cuda.synchronize()
+            ctx.check_barrier()
+            if not torch.equal(g, want):
+                raise SystemExit("configs4: fused peer all-gather differs from the NCCL all-gather")
+
+        def call():
+            if gather is not None:
+                gather.step(ap, status)
+            elif lib.lnsb_mul_mat_lns(16, ap, op, ctx.sp) != 0:
+                status[0] = -1
+        steps = 3 if N == 128 else 6
+        ms = timed(ctx, call, steps, 2)
+        if status[0] != 0:
+            raise RuntimeError("configs4 mul_mat failed")
+        ctx.check_barrier()
+        adds = adds_of(K, MT, N)
+        int_peak = SMS * LANES_PER_SM * f_mhz * 1e6 / C_MODE["sum32"] / 1e9
+        val = adds / (ms / 1000) / 1e9
+        res["N%d" % N] = {"ms_per_step": ms, "value": val, "unit": UNIT, "adds": adds,
+                          "frac_int": val / world / int_peak,
+                          "bound": "chain latency (K dependent sum32 additions)" if N == 1 else "integer issue"}
+        del gather
+    return {"workload": "BASELINE configs[4] LNS16 sum32 mul_mat: W 8192x14336 x X 14336xN, rows split %d ways" % world,
+            "mode": "sum32", "K": K, "rows_per_gpu": Mr, "scaling": "strong", "n_gpus": world, "points": res,
+            "gather": "fused peer-store all-gather + barrier" if world > 1 else None,
             "l2": "flushed (256 MB write) before every timed step"}
 
 
-def time_norms(lnsb200, torch, np, args, flush, stream):
+def time_norms(ctx, lnsb200, torch, np, args, f_mhz):
     """BASELINE configs[1]'s normalisers on xlns16 codes, device-timed, L2
     flushed before every step: soft_max over logits N(0, 3) shaped [9 heads]
     [512 queries][512 keys] with a causal mask (keys after the query are
     -inf) and scale 1.0 (4,608 rows x 511 additions, masked zeros included),
     and rms_norm over 512 rows of 576 N(0, 1) values, eps 1e-5 (576 additions
-    per row); inputs numpy default_rng(1), converted to codes on the device."""
+    per row); inputs numpy default_rng(1), converted to codes on the device.
+    Bound: one row's chain of dependent additions, every row in parallel:
+    T_chain = additions per row x L_add / f_sm, L_add measured on this GPU
+    (lnsb_add_latency: the non-negative addition the mode's normalisers run)."""
     ks = lnsb200.KernelSet(16, args.mode)
     lib = ks.lib
     rng = np.random.default_rng(1)
@@ -542,39 +714,32 @@ def time_norms(lnsb200, torch, np, args, flush, stream):
     rn_dst = torch.empty_like(rn_src)
     ne = (ctypes.c_int64 * 4)(n, q, h, 1)
     mne = (ctypes.c_int64 * 4)(n, q, 1, 1)
-    sp = ctypes.c_void_p(stream.cuda_stream)
+    sp = ctx.sp
     P = lambda t: ctypes.c_void_p(t.data_ptr())                        # noqa: E731
+    kind = {"base": 1, "sum32": 2}.get(args.mode)
+    l_add = ks.add_latency(kind, 32, 4096) if kind is not None else None
     calls = {
         "soft_max": (lambda: lib.lnsb_soft_max_lns(16, P(sm_src), ne, P(mask), mne, 0x4000, P(sm_dst), P(sm_work), 7, sp),
-                     h * q * (n - 1), "chain latency: %d dependent additions per row, %d rows" % (n - 1, h * q),
-                     "[9][512][512] xlns16 logits N(0,3), causal mask, scale 1.0"),
+                     h * q * (n - 1), n - 1, h * q, "[9][512][512] xlns16 logits N(0,3), causal mask, scale 1.0"),
         "rms_norm": (lambda: lib.lnsb_rms_norm_lns(16, P(rn_src), P(rn_dst), cols, rows, ctypes.c_float(1e-5), 7, sp),
-                     rows * cols, "chain latency: %d dependent additions per row, %d rows" % (cols, rows),
-                     "512 x 576 xlns16 values N(0,1), eps 1e-5"),
+                     rows * cols, cols, rows, "512 x 576 xlns16 values N(0,1), eps 1e-5"),
     }
     out = {}
-    steps = max(args.steps, 20)
-    for name, (call, adds, bound, what) in calls.items():
-        for _ in range(args.warmup):
-            flush.zero_()
-            if call() != 0:
-                raise RuntimeError("lnsb_%s_lns failed" % name)
-        torch.cuda.synchronize()
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-        for i in range(steps):
-            flush.zero_()
-            ev[i][0].record(stream)
-            call()
-            ev[i][1].record(stream)
-        torch.cuda.synchronize()
-        ms = sum(b.elapsed_time(e) for b, e in ev) / steps
-        out[name] = {"workload": "BASELINE configs[1] %s: %s" % (name, what), "mode": args.mode, "steps": steps,
-                     "ms_per_step": ms, "value": adds / (ms / 1000) / 1e9, "unit": UNIT, "adds": adds, "bound": bound,
-                     "l2": "flushed (256 MB write) before every timed step"}
+    for name, (call, adds, per_row, nrows, what) in calls.items():
+        ms = timed(ctx, call, max(args.steps, 20), args.warmup)
+        d = {"workload": "BASELINE configs[1] %s: %s" % (name, what), "mode": args.mode, "ms_per_step": ms,
+             "value": adds / (ms / 1000) / 1e9, "unit": UNIT, "adds": adds,
+             "bound": "chain latency: %d dependent additions per row, %d rows" % (per_row, nrows),
+             "l2": "flushed (256 MB write) before every timed step"}
+        if l_add is not None:
+            t_chain = per_row * l_add / (f_mhz * 1e6)
+            d["chain"] = {"l_add_cycles": l_add, "t_chain_us": t_chain * 1e6, "frac": t_chain / (ms / 1000),
+                          "adder": "non-negative xlns16 (padd16)" if kind == 1 else "non-negative xlns32 (padd32f)"}
+        out[name] = d
     return out
 
 
-def time_mul_mat_id(lnsb200, torch, np, args, flush, stream, int_peak):
+def time_mul_mat_id(ctx, lnsb200, torch, np, args, int_peak):
     """MUL_MAT_ID on a mixture-of-experts FFN shape (8 experts of 1536 x 576,
     128 tokens, 2 experts per token; synthetic N(0,0.02) / N(0,1) codes, seed
     4), device-timed, L2 flushed before every step; roofline as the main
@@ -591,27 +756,17 @@ def time_mul_mat_id(lnsb200, torch, np, args, flush, stream, int_peak):
     ks.to_lns(xf, x)
     ids = torch.from_numpy(rng.integers(0, n_exp, (n_tok, n_used)).astype(np.int32)).cuda()
     out = torch.empty(n_tok * n_used * M, dtype=torch.int16, device="cuda")
-    for _ in range(max(3, args.warmup)):
-        ks.mul_mat_id_lns(w, x, ids, out, K, M, n_exp, 1, n_used, n_tok, stream=stream)
-    torch.cuda.synchronize()
-    steps = max(args.steps, 10)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    for i in range(steps):
-        flush.zero_()
-        ev[i][0].record(stream)
-        ks.mul_mat_id_lns(w, x, ids, out, K, M, n_exp, 1, n_used, n_tok, stream=stream)
-        ev[i][1].record(stream)
-    torch.cuda.synchronize()
-    ms = sum(b.elapsed_time(e) for b, e in ev) / steps
+    ms = timed(ctx, lambda: ks.mul_mat_id_lns(w, x, ids, out, K, M, n_exp, 1, n_used, n_tok, stream=ctx.stream),
+               max(args.steps, 10), max(3, args.warmup))
     adds = n_tok * n_used * M * (K - 1)
     val = adds / (ms / 1000) / 1e9
     return {"workload": "MUL_MAT_ID: 8 experts of 1536x576, 128 tokens x 2 experts (synthetic, seed 4)",
-            "mode": args.mode, "steps": steps, "ms_per_step": ms, "value": val, "unit": UNIT,
+            "mode": args.mode, "ms_per_step": ms, "value": val, "unit": UNIT,
             "roofline": {"bound": "int", "achieved": val, "peak": int_peak, "frac": val / int_peak, "unit": UNIT},
             "l2": "flushed (256 MB write) before every timed step"}
 
 
-def time_weights(lnsb200, torch, np, args, flush, stream, hbm):
+def time_weights(ctx, lnsb200, torch, np, args, hbm):
     """Weights in ggml storage types decoded on the device into the k-major LNS
     image (lnsb_to_lns_transposed_typed), 8192 x 4096 per type; algorithmic
     bytes = the packed rows read + the codes written; bound HBM."""
@@ -632,21 +787,9 @@ def time_weights(lnsb200, torch, np, args, flush, stream, hbm):
                 d = rng.uniform(1e-3, 1e-1, (rows, cols // qk)).astype(np.float16)
                 blocks[:, :, off:off + 2] = d.view(np.uint8).reshape(rows, cols // qk, 2)
             raw = torch.from_numpy(blocks.reshape(rows, rb)).cuda()
-        for _ in range(3):
-            ks.to_lns_transposed_typed(t, raw, dst, rows, cols, rows, stream=stream)
-        torch.cuda.synchronize()
-        n = 10
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-        for i in range(n):
-            flush.zero_()
-            ev[i][0].record(stream)
-            ks.to_lns_transposed_typed(t, raw, dst, rows, cols, rows, stream=stream)
-            ev[i][1].record(stream)
-        torch.cuda.synchronize()
-        ms = sum(b.elapsed_time(e) for b, e in ev) / n
+        ms = timed(ctx, lambda: ks.to_lns_transposed_typed(t, raw, dst, rows, cols, rows, stream=ctx.stream), 10, 3)
         by = rows * rb + rows * cols * 2
-        out[t] = {"ms": ms, "gbs": by / (ms / 1000) / 1e9, "frac_hbm": by / (ms / 1000) / 1e9 / hbm,
-                  "bytes": by}
+        out[t] = {"ms": ms, "gbs": by / (ms / 1000) / 1e9, "frac_hbm": by / (ms / 1000) / 1e9 / hbm, "bytes": by}
     return {"workload": "8192 x 4096 weight -> xlns16 k-major image, per storage type", "bound": "hbm",
             "peak_gbs": hbm, "types": out,
             "l2": "flushed (256 MB write) before every timed launch", "launches_per_type": 10}
@@ -694,9 +837,9 @@ def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16):
     if cpu:
         # the CPU oracle (the reference's algorithm, host cores) on a bounded sample:
         # prefill of 8 tokens, then 16 decode steps (a few seconds)
-        import time
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        o = model.OracleOps(cfg, w, mode=args.decode_mode, n_ctx=32, nthreads=os.cpu_count() or 1, fmt=fmt)
+        from oracle_model import OracleOps
+        o = OracleOps(cfg, w, mode=args.decode_mode, n_ctx=32, nthreads=os.cpu_count() or 1, fmt=fmt)
         lo = model.forward(o, cfg, prompt[:8], 0)
         t0 = time.perf_counter()
         tk = o.argmax(lo)
@@ -710,16 +853,7 @@ def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16):
 
 def main():
     args = parse()
-    if args.workload == "configs4":
-        # 8192 x K weights, K x N activations, seed 3; output rows
-        # sharded across the ranks (strong scaling), gathered with NCCL
-        wl = dict(desc="BASELINE configs[4] LNS16 mul_mat sweep: W 8192x%d x X %dx%d, rows sharded"
-                       % (args.sweep_k, args.sweep_k, args.sweep_n),
-                  K=args.sweep_k, M=8192, N=args.sweep_n, seed=3, strong=True)
-    else:
-        wl = WORKLOADS[args.workload]
-    if args.mode is None:
-        args.mode = "sum32" if args.workload == "configs4" else "base"
+    wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, wl)
     return run_ours(args, wl)

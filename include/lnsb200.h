@@ -165,9 +165,17 @@ int lnsb_mul_mat_lns(int fmt, const lnsb_mul_mat_args * args, void * dst_lns, ln
  * of a [slices][N][ld] codes result that lives on every GPU of the group; the
  * kernel stores each code into all `n` peer buffers (device pointers valid in
  * this process, e.g. a symmetric-memory allocation's buffer_ptrs_dev, own
- * buffer included) over NVLink, plain stores.  The caller synchronises the
- * group (a barrier) before reading.  xlns16 base / monte builds (the tiled
- * kernel, whatever the size); otherwise LNSB_E_UNSUPPORTED. */
+ * buffer included) over NVLink, plain stores; codes of the format's width
+ * (16 or 32 bits).  Every summation mode and both formats.
+ * Ordering, both ways:
+ *  - read after write: run lnsb_group_barrier after the call and before any
+ *    read of the gathered result;
+ *  - write after read: a peer may still be reading step e's result when this
+ *    rank's step e+1 stores arrive.  Either alternate between two result
+ *    buffers by step parity, with every read of step e issued on this rank's
+ *    stream before its step e+1 call (passing barrier e+1 then means every
+ *    peer has finished its step e reads), or run a second lnsb_group_barrier
+ *    after the last read of step e, before the next call. */
 typedef struct {
     void * const * ptrs;       /* device array of n buffer pointers */
     int            n;
@@ -177,9 +185,23 @@ int lnsb_mul_mat_lns_peers(int fmt, const lnsb_mul_mat_args * args, const lnsb_p
 /* the barrier to follow it: flags is a device array of `world` pointers to
  * each GPU's int32[world] flag array (zeroed once; peer memory), epoch counts
  * the calls from 1.  Each GPU signals every peer and waits for every peer's
- * signal of this epoch; a wait that runs past about two seconds sets *err
- * (device memory) to 1 and returns instead of hanging. */
+ * signal of this epoch.  The wait is bounded: after 2^21 polls, each followed
+ * by a sleep of about 100 ns (in total about 0.2 s or more, depending on the
+ * scheduler), it sets *err (device memory) to 1 and returns instead of
+ * hanging. */
 int lnsb_group_barrier(int32_t * const * flags, int world, int rank, int32_t epoch, int32_t * err, lnsb_stream_t stream);
+
+/* Diagnostic, no counterpart in the reference: the dependent latency of one
+ * LNS addition on the current device, for the chain bound T_chain = (n - 1)
+ * L_add / f_sm of a latency-bound reduction.  One warp runs `steps` dependent
+ * additions per lane (2 <= steps; lanes 1..32 distinct chains, the other lanes
+ * repeating them) over operands of a dot product's spread, with the adder's
+ * table in shared memory as the kernels hold it.  kind 0: the key-form xlns16
+ * addition of the latency mul_mat kernels; 1: the non-negative xlns16
+ * addition of the normalisers (base); 2: the non-negative xlns32 addition of
+ * the normalisers (sum32, xlns32).  out: device memory, two int64 -- out[0] =
+ * SM cycles over steps - 1 additions, out[1] = the final accumulator. */
+int lnsb_add_latency(int kind, int lanes, int steps, int64_t * out, lnsb_stream_t stream);
 
 /* kernel_set::soft_max (lns-cuda-kernels.h:136) */
 int lnsb_soft_max(int fmt, const lnsb_soft_max_args * args, lnsb_stream_t stream);

@@ -24,6 +24,7 @@ def caches(rng, n_ctx, kvd):
 @pytest.mark.parametrize("nkv", [1, 37, 300])
 def test_attn_decode_matches_unfused_and_oracle(fmt, mode, nkv):
     from lnsb200 import model
+    from oracle_model import OracleOps
     rng = np.random.default_rng(nkv + fmt)
     H, HKV, D = CFG["n_head"], CFG["n_head_kv"], CFG["head_dim"]
     w = model.init_weights(CFG, seed=1)
@@ -36,7 +37,7 @@ def test_attn_decode_matches_unfused_and_oracle(fmt, mode, nkv):
     g.fuse_attn = False
     plain = g.attention(0, q, 1, H, HKV, D, nkv - 1).cpu().numpy()
     assert np.array_equal(fused.view(np.uint32), plain.view(np.uint32))
-    o = model.OracleOps(CFG, w, mode=mode, n_ctx=320, fmt=fmt)
+    o = OracleOps(CFG, w, mode=mode, n_ctx=320, fmt=fmt)
     o.kc[0][:] = k
     o.vc[0][:] = v
     want = o.attention(0, q.cpu().numpy(), 1, H, HKV, D, nkv - 1)

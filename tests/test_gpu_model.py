@@ -15,10 +15,11 @@ SMALL = dict(n_layer=2, n_embd=128, n_head=4, n_head_kv=2, head_dim=32, n_ff=256
 
 def run_both(cfg, mode, n_prompt, n_steps, n_ctx=64, fmt=16):
     from lnsb200 import model
+    from oracle_model import OracleOps
     w = model.init_weights(cfg, seed=2)
     prompt = model.prompt_ids(cfg, n_prompt, seed=2)
     g = model.GpuOps(cfg, w, mode=mode, n_ctx=n_ctx, fmt=fmt)
-    o = model.OracleOps(cfg, w, mode=mode, n_ctx=n_ctx, fmt=fmt)
+    o = OracleOps(cfg, w, mode=mode, n_ctx=n_ctx, fmt=fmt)
     lg = model.forward(g, cfg, prompt, 0)
     lo = model.forward(o, cfg, prompt, 0)
     steps = [(lg.cpu().numpy().ravel(), lo.ravel())]
@@ -43,6 +44,7 @@ def test_smollm2_shape_decode_bit_exact():
     """the full configs[2] shape (30 layers, d 576, 9/3 heads, ffn 1536, vocab
     49152), a short prompt and three decode steps"""
     from lnsb200 import model
+    from oracle_model import OracleOps
     for i, (a, b) in enumerate(run_both(model.SMOLLM2_135M, "sum32", 6, 3, n_ctx=16)):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), "logits differ at step %d" % i
 
@@ -55,23 +57,26 @@ def test_small_model_decode_bit_exact_xlns32():
 def test_smollm2_shape_decode_bit_exact_xlns32():
     """the LNS32 model (every op in xlns32) at the full SmolLM2-135M shape"""
     from lnsb200 import model
+    from oracle_model import OracleOps
     for i, (a, b) in enumerate(run_both(model.SMOLLM2_135M, "sum32", 6, 3, n_ctx=16, fmt=32)):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), "logits differ at step %d" % i
 
 
 def test_generate_matches_forward_loop():
     from lnsb200 import model
+    from oracle_model import OracleOps
     w = model.init_weights(SMALL, seed=2)
     prompt = model.prompt_ids(SMALL, 5, seed=2)
     g = model.GpuOps(SMALL, w, mode="sum32", n_ctx=32)
     toks = model.generate(g, SMALL, prompt, 6)
-    o = model.OracleOps(SMALL, w, mode="sum32", n_ctx=32)
+    o = OracleOps(SMALL, w, mode="sum32", n_ctx=32)
     assert toks == model.generate(o, SMALL, prompt, 6)
 
 
 def test_graph_decode_matches_eager():
     """CUDA-graph decode (one graph per position) gives the eager path's tokens"""
     from lnsb200 import model
+    from oracle_model import OracleOps
     w = model.init_weights(SMALL, seed=2)
     prompt = model.prompt_ids(SMALL, 5, seed=2)
     g = model.GpuOps(SMALL, w, mode="sum32", n_ctx=32)
@@ -87,6 +92,7 @@ def test_graph_decode_matches_eager():
 
 def test_graph_decode_matches_eager_xlns32():
     from lnsb200 import model
+    from oracle_model import OracleOps
     w = model.init_weights(SMALL, seed=2)
     prompt = model.prompt_ids(SMALL, 5, seed=2)
     eager = model.generate(model.GpuOps(SMALL, w, mode="sum32", n_ctx=32, fmt=32), SMALL, prompt, 5)
@@ -103,10 +109,11 @@ def test_small_model_mixed_policy_bit_exact(policy):
     """LNS16_SUM_POLICY-style mixed modes (one library per mode): the second
     policy splits the fused q/k/v product and picks wo by its input's name"""
     from lnsb200 import model
+    from oracle_model import OracleOps
     w = model.init_weights(SMALL, seed=2)
     prompt = model.prompt_ids(SMALL, 6, seed=2)
     g = model.GpuOps(SMALL, w, mode="base", n_ctx=32, policy=policy)
-    o = model.OracleOps(SMALL, w, mode="base", n_ctx=32, policy=policy)
+    o = OracleOps(SMALL, w, mode="base", n_ctx=32, policy=policy)
     lg, lo = model.forward(g, SMALL, prompt, 0), model.forward(o, SMALL, prompt, 0)
     assert np.array_equal(lg.cpu().numpy().ravel().view(np.uint32), lo.ravel().view(np.uint32))
     tg = g.argmax(lg)
@@ -122,6 +129,7 @@ def test_fused_step_matches_op_by_op(fmt, mode):
     glu + to_lns) against the op-by-op graph on the same GPU, prefill and two
     decode steps, in every summation mode and xlns32"""
     from lnsb200 import model
+    from oracle_model import OracleOps
     w = model.init_weights(SMALL, seed=2)
     prompt = model.prompt_ids(SMALL, 5, seed=3)
     a = model.GpuOps(SMALL, w, mode=mode, n_ctx=16, fmt=fmt)

@@ -60,8 +60,9 @@ TINY = dict(n_layer=2, n_embd=64, n_head=4, n_head_kv=2, head_dim=16, n_ff=128, 
 
 def _logits(policy, mode="base"):
     from lnsb200 import model
+    from oracle_model import OracleOps
     w = model.init_weights(TINY, seed=2)
-    o = model.OracleOps(TINY, w, mode=mode, n_ctx=16, policy=policy)
+    o = OracleOps(TINY, w, mode=mode, n_ctx=16, policy=policy)
     return model.forward(o, TINY, model.prompt_ids(TINY, 5, seed=2), 0)
 
 

@@ -73,3 +73,12 @@ def test_row_range_partitions():
             assert ranges[0][0] == 0 and ranges[-1][1] == M
             assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
             assert max(b - a for a, b in ranges) - min(b - a for a, b in ranges) <= 1
+
+
+def test_monte_seed_for_shard_refuses_slices():
+    """a sharded Monte mul_mat with several slices has no single start state"""
+    import oracle
+    from lnsb200 import shard
+    assert shard.monte_seed_for_shard(7, oracle.lfsr_jump, 64, 4, 16, 1, 2) == oracle.lfsr_jump(7, 32 * 4 * 15)
+    with pytest.raises(ValueError):
+        shard.monte_seed_for_shard(7, oracle.lfsr_jump, 64, 4, 16, 1, 2, slices=3)

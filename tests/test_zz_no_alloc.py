@@ -9,7 +9,9 @@ of a caller-provided work buffer.  The test calls it through the C ABI twice
 in a row (different inputs, so the second call reuses the array the first
 one wrote) and checks each result against the existing entry point
 (lnsb_soft_max_lns with its own work buffer), bit for bit -- the tolerance
-every parity test here uses.  It also checks the size limit is refused.
+every parity test here uses.  It also checks that the size limit is refused,
+including shapes whose element count would wrap a 64-bit integer, and that a
+call after the first one leaves the device's free memory unchanged.
 
 This file is collected last on purpose, and works both on its own in a fresh
 process and after the rest of the suite.
@@ -88,3 +90,29 @@ def test_noalloc_refuses_beyond_its_scratch():
                                        ctypes.c_void_p(dummy.data_ptr()), 7, stream)
     assert st == -4                                                          # LNSB_E_TOO_LARGE
     assert b"limit" in lib.lnsb_error_string(st)
+    # element counts that wrap int64 (2^64 -> 0, 2^63 + small) are refused, not run
+    for shape in ((1 << 32, 1 << 32, 1, 1), (1 << 31, 1 << 31, 4, 1), (3, 1 << 62, 2, 1)):
+        st = lib.lnsb_soft_max_lns_noalloc(16, ctypes.c_void_p(dummy.data_ptr()), _ne(shape), None, None, 0x4000,
+                                           ctypes.c_void_p(dummy.data_ptr()), 7, stream)
+        assert st == -4, shape
+
+
+def test_noalloc_allocates_nothing():
+    """after the first call on a device (the one-time symbol lookup), a call
+    leaves cudaMemGetInfo's free bytes exactly as they were"""
+    from lnsb200 import _lib
+    lib = _lib.load("base")
+    assert lib.lnsb_upload_tables(16) == 0
+    rng = np.random.default_rng(11)
+    src = torch.from_numpy((rng.integers(0x3800, 0x4800, 64 * 700)).astype(np.uint16).view(np.int16)).cuda()
+    out = torch.empty_like(src)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    call = lambda: lib.lnsb_soft_max_lns_noalloc(16, ctypes.c_void_p(src.data_ptr()), _ne((700, 64, 1, 1)), None,
+                                                 None, 0x4000, ctypes.c_void_p(out.data_ptr()), 7, stream)
+    assert call() == 0
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        assert call() == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0

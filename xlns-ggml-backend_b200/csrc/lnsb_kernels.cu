@@ -1160,135 +1160,241 @@ k_mul_mat16_lat(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * 
     }
 }
 
-// ======= MUL_MAT (xlns16, base mode, few outputs, weights resident) ==========
-//
-// For K up to a few thousand the whole weight slice of a CTA -- 32 rows x K
-// codes -- fits in shared memory and is staged once, so the chain loop has no
-// block-wide barrier and no chunk staging (which cost k_mul_mat16_lat about a
-// third of its time).  A CTA is 32 rows x TNC tokens: warp w runs the 32
-// chains of token n0 + w, one per lane, in blocks of 8 steps whose products are
-// formed first.  The key form's range check is made per segment of LR_SEG
-// steps from ranges the prologue records (weights per CTA, tokens per warp),
-// each warp deciding for itself: a segment that fails (a zero weight, say)
-// runs on packed codes, and the chain returns to the key form at the next
-// segment that passes -- the bits are the same either way.
-constexpr int LR_OFF_W  = LT_OFF_TAB2 + MM_TABPAD;                // [K][32] codes, then x keys, x codes
+// Segments of the key form's range check in the weight-resident latency
+// kernels (k_mul_mat16_res2): the check is made per LR_SEG steps.
 constexpr int LR_SEG    = 256;
 constexpr int LR_MAXSEG = 16;                                     // K <= LR_SEG * LR_MAXSEG
-inline int lr_smem(int64_t K, int tnc) {
-    const int64_t kp = (K + 3) & ~3;
-    return (int) (LR_OFF_W + kp * 64 + kp * 6 * tnc + 16);
-}
-constexpr int LR_SMEM_MAX = 226 * 1024;                          // leaves room for the static shared memory
 
-template <bool OUT_F32>
-__global__ void __launch_bounds__(128)
-k_mul_mat16_res(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
-                void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
-                int64_t r2, int64_t r3, int vec) {
+// ======= MUL_MAT (xlns16, base mode, few outputs, weight keys resident) =====
+//
+// The latency form of the chain with less work on each step.  The
+// CTA's weight slice is held as 32-bit keys in [row][k] order (a row's pitch
+// r2_pitch(K) words, 4 mod 32, so the 16-byte loads of different rows start
+// in different banks), the tokens' rows as keys beside it, so a lane reads
+// four steps of weights and four of activations with two 16-byte loads and
+// converts nothing inside the loop.  A warp runs R rows x 32/R tokens (lane =
+// row + R * token slot): R = 32 for a single token where it fits, else 16
+// rows against two tokens.  The table index is clamped with one unsigned
+// add-min: the signed table holds the adjustment of a key difference D at
+// byte KM + D and both ends (|D| >= KM) hold zero, so a difference below -KM,
+// which wraps to a huge unsigned value, may be clamped to the upper end.  The
+// dependent path of a step is therefore
+//     idx = min(a + (KM - p), 2 KM) (unsigned)  ->  table load
+//       ->  a = max(max(a, p) + adj, 0)
+// with p and KM - p formed off the path (one-warp measurement on B200: 47
+// cycles a step with 32 lanes, 41 with one; the load alone is most of it).
+// The range check is per segment of LR_SEG steps and per warp (both token
+// slots) from the ranges staging records; a segment that fails runs on packed codes
+// rebuilt from the keys.
+//
+// Warps [0, cw) run the chains; the other 4 - cw warps produce: the whole CTA
+// stages the tables, the token rows and the first segment of weights, then
+// each producer warp stages later segments (16-byte loads, keys, the
+// segment's log range) and signals segment s on hardware named barrier s
+// (bar.arrive), which the chain warps wait on (bar.sync) just before they
+// reach it -- so the staging of segments 1.. runs under the chain.  With
+// cw = 4 there are no producers and everything is staged first.  Output:
+// codes, F32, or codes into every peer's buffer (the fused all-gather of
+// output-row shards, peers.n > 0).
+constexpr int R2_THREADS = 128;
+constexpr int R2_OFF_W   = LT_OFF_TAB2 + MM_TABPAD;              // [R][pitch] weight keys, then [tokens][pitch] x keys
+__host__ __device__ constexpr int r2_pitch(int64_t K) {     // >= K rounded to 4, and 4 mod 32
+    return (int) ((K + 3) & ~3) + (36 - (int) (((K + 3) & ~3) % 32)) % 32;
+}
+inline int r2_smem(int64_t K, int R, int ntok) { return R2_OFF_W + (R + ntok) * r2_pitch(K) * 4; }
+constexpr int R2_SMEM_MAX = 225 * 1024;                          // with the kernel's 1.1 KB of static shared memory
+
+// weight keys of k-rows [k0, k1) of the CTA's R rows, staged by threads t of
+// nt: 16-byte loads of 8 codes (vec: M a multiple of 8, W 16-byte aligned),
+// eight in flight per thread, otherwise one code per load; rows past M hold
+// 1.0.  lo / hi: this thread's smallest / largest log field staged.
+template <int R>
+__device__ __forceinline__ void r2_stage_w(int * wk, int PW, const uint16_t * __restrict__ Wz, int64_t M, int64_t m0,
+                                           int k0, int k1, int t, int nt, int vec, int & lo, int & hi) {
+    if (vec) {
+        constexpr int QR = R / 8;                        // 16-byte pieces of a k-row
+        const int nld = (k1 - k0) * QR;
+        for (int base = t; base < nld; base += nt * 8) {
+            uint4 q[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = base + u * nt, k = k0 + i / QR, c8 = (i % QR) * 8;
+                q[u] = (i < nld && m0 + c8 < M) ? __ldg(reinterpret_cast<const uint4 *>(Wz + (int64_t) k * M + m0 + c8))
+                                                : make_uint4(0x40004000u, 0x40004000u, 0x40004000u, 0x40004000u);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = base + u * nt, k = k0 + i / QR, c8 = (i % QR) * 8;
+                if (i >= nld) break;
+                const uint32_t wd[4] = { q[u].x, q[u].y, q[u].z, q[u].w };
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const uint32_t c = (wd[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+                    wk[(c8 + e) * PW + k] = key_of_code_w(c);
+                    lo = min(lo, (int) (c & 0x7FFFu));
+                    hi = max(hi, (int) (c & 0x7FFFu));
+                }
+            }
+        }
+    } else {
+        for (int i = t; i < (k1 - k0) * R; i += nt) {
+            const int k = k0 + i / R, r = i % R;
+            const int64_t m = m0 + r;
+            const uint32_t c = m < M ? (uint32_t) Wz[(int64_t) k * M + m] : 0x4000u;
+            wk[r * PW + k] = key_of_code_w(c);
+            lo = min(lo, (int) (c & 0x7FFFu));
+            hi = max(hi, (int) (c & 0x7FFFu));
+        }
+    }
+}
+
+template <bool OUT_F32, int R, int TPW>
+__global__ void __launch_bounds__(R2_THREADS)
+k_mul_mat16_res2(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
+                 void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
+                 int64_t r2, int64_t r3, int cw, int vec, peer_out_dev peers) {
+    // TPW token slots per warp: 32 / R, or 1 with R = 16, where lanes 16..31
+    // repeat lanes 0..15 (same addresses: the table lookup sees 16 distinct
+    // addresses, fewer bank conflicts, a shorter step) and only lanes 0..15 store
+    static_assert(R * TPW == 32 || (R == 16 && TPW == 1), "lane layout");
     pdl_entry();
     extern __shared__ __align__(16) unsigned char smem[];
-    const int  Ki    = (int) K;
-    const int  KP    = (Ki + 3) & ~3;
-    const int  tnc   = blockDim.x >> 5;
-    const int  nseg  = (Ki + LR_SEG - 1) / LR_SEG;
-    int16_t *  tab2  = reinterpret_cast<int16_t *>(smem + LT_OFF_TAB2);
-    uint16_t * ws    = reinterpret_cast<uint16_t *>(smem + LR_OFF_W);                        // [K][32]
-    int *      xkeys = reinterpret_cast<int *>(smem + LR_OFF_W + KP * 64);                   // [tnc][KP]
-    uint16_t * xcod  = reinterpret_cast<uint16_t *>(smem + LR_OFF_W + KP * 64 + tnc * KP * 4);
-    __shared__ int wseg[LR_MAXSEG][2];                  // weight log range per segment
-    __shared__ int xseg[4][LR_MAXSEG][2];               // token log range per warp and segment
+    const int Ki = (int) K, PW = r2_pitch(K);
+    const int ntok  = cw * TPW;                          // token rows staged by this CTA
+    const int nseg  = (Ki + LR_SEG - 1) / LR_SEG;
+    const int nprod = R2_THREADS / 32 - cw;              // producer warps
+    const int kpre  = nprod > 0 ? min(Ki, LR_SEG) : Ki;  // weight rows staged before the chains start
+    const int16_t * tab2 = reinterpret_cast<const int16_t *>(smem + LT_OFF_TAB2);
+    int * wk = reinterpret_cast<int *>(smem + R2_OFF_W);                  // [R][PW]
+    int * xk = wk + R * PW;                                                // [ntok][PW]
+    __shared__ int wseg[LR_MAXSEG][2];                   // weight log range per segment
+    __shared__ int xseg[8][LR_MAXSEG][2];                // token log range per token row and segment
+    __shared__ int wred[R2_THREADS / 32][2];             // per-warp weight range of the first staging
 
     const int64_t z = blockIdx.z, i12 = z % ne12, i13 = z / ne12;
-    const int64_t m0 = (int64_t) blockIdx.x * 32, n0 = (int64_t) blockIdx.y * tnc;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t m0 = (int64_t) blockIdx.x * R, n0 = (int64_t) blockIdx.y * ntok;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint16_t * Wz = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
-    // weight slice: row k of the k-major matrix gives 32 consecutive codes (64 bytes)
-    for (int i = threadIdx.x; i < Ki * 4; i += blockDim.x) {
-        const int r = i >> 2, q = i & 3;
-        const int64_t mm = m0 + q * 8;
-        if (vec && mm < M) {
-            cp_async16(ws + r * 32 + q * 8, Wz + (int64_t) r * M + mm);
-        } else {
+
+    lt_tables_async(T, smem);                            // signed key table, packed table
+    cp_async_commit();
+    {
+        int lo = 0x7FFF, hi = 0;
+        r2_stage_w<R>(wk, PW, Wz, M, m0, 0, kpre, tid, R2_THREADS, vec, lo, hi);
+        lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+        hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+        if (lane == 0) { wred[warp][0] = lo; wred[warp][1] = hi; }
+    }
+    // token keys: token row t is token n0 + t (the last token stands in past
+    // N); 16-byte loads where K is a multiple of 8 and X 16-byte aligned
+    if (Ki % 8 == 0 && ((uintptr_t) X % 16) == 0) {
+        const int k8n = Ki / 8, nld = ntok * k8n;
+        for (int base = tid; base < nld; base += R2_THREADS * 4) {
+            uint4 q[4];
 #pragma unroll
-            for (int e = 0; e < 8; e++) ws[r * 32 + q * 8 + e] = mm + e < M ? Wz[(int64_t) r * M + mm + e] : (uint16_t) 0x4000;
+            for (int u = 0; u < 4; u++) {
+                const int i = base + u * R2_THREADS, t = i / k8n;
+                const int64_t n = min(n0 + t, N - 1);
+                if (i < nld) q[u] = __ldg(reinterpret_cast<const uint4 *>(X + (z * N + n) * K + (int64_t) (i - t * k8n) * 8));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = base + u * R2_THREADS, t = i / k8n, k = (i - t * k8n) * 8;
+                if (i >= nld) break;
+                const uint32_t wd[4] = { q[u].x, q[u].y, q[u].z, q[u].w };
+                int key[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) key[e] = key_of_code_x((wd[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
+                *reinterpret_cast<int4 *>(xk + t * PW + k)     = make_int4(key[0], key[1], key[2], key[3]);
+                *reinterpret_cast<int4 *>(xk + t * PW + k + 4) = make_int4(key[4], key[5], key[6], key[7]);
+            }
+        }
+    } else {
+        for (int i = tid; i < ntok * Ki; i += R2_THREADS) {
+            const int t = i / Ki, k = i - t * Ki;
+            const int64_t n = min(n0 + t, N - 1);
+            xk[t * PW + k] = key_of_code_x(X[(z * N + n) * K + k]);
         }
     }
-    cp_async_commit();
-    lt_tables_async(T, smem);                           // signed key table, packed table
-    cp_async_commit();
-    for (int i = threadIdx.x; i < nseg; i += blockDim.x) { wseg[i][0] = 0x7FFF; wseg[i][1] = 0; }
-    // this warp's token (8 codes per 16-byte load where the row allows), with
-    // its log range per segment
-    const int64_t n = n0 + warp;
-    const bool    tok = n < N;
-    {
-        const uint16_t * xr = X + (z * N + (tok ? n : N - 1)) * K;
-        const bool xv = ((uintptr_t) xr % 16) == 0;
-        for (int sg = 0; sg < nseg; sg++) {
-            int xmin = 0x7FFF, xmax = 0;
-            auto put = [&](int k, uint32_t c) {
-                xcod[warp * KP + k]  = (uint16_t) c;
-                xkeys[warp * KP + k] = key_of_code_x(c);
-                xmin = min(xmin, (int) (c & 0x7FFFu));
-                xmax = max(xmax, (int) (c & 0x7FFFu));
-            };
-            const int k0 = sg * LR_SEG + lane * 8;      // each lane: 8 consecutive codes of the segment
-            if (xv && k0 + 8 <= Ki) {
-                const uint4 q = __ldg(reinterpret_cast<const uint4 *>(xr + k0));
-                const uint32_t wd[4] = { q.x, q.y, q.z, q.w };
-#pragma unroll
-                for (int e = 0; e < 4; e++) { put(k0 + 2 * e, wd[e] & 0xFFFFu); put(k0 + 2 * e + 1, wd[e] >> 16); }
-            } else {
-                for (int k = k0; k < k0 + 8 && k < Ki; k++) put(k, xr[k]);
+    __syncthreads();
+    // log ranges: the tokens' per token row and segment; the weights' of the
+    // first staging (segment 0, or every segment without producers)
+    const int wsegs = nprod > 0 ? min(nseg, 1) : nseg;
+    for (int j = warp; j < nseg * ntok + (nprod > 0 ? 0 : nseg); j += R2_THREADS / 32) {
+        const bool wj = j >= nseg * ntok;
+        const int sg = j % nseg, t = j / nseg;
+        const int k0 = sg * LR_SEG, k1 = min(Ki, k0 + LR_SEG);
+        int lo = 0x7FFF, hi = 0;
+        if (wj) {
+            for (int i = lane; i < (k1 - k0) * R; i += 32) {
+                const int l = (wk[(i % R) * PW + k0 + i / R] >> 4) & 0x7FFF;
+                lo = min(lo, l); hi = max(hi, l);
             }
-            xmin = __reduce_min_sync(0xFFFFFFFFu, xmin);
-            xmax = __reduce_max_sync(0xFFFFFFFFu, xmax);
-            if (lane == 0) { xseg[warp][sg][0] = xmin; xseg[warp][sg][1] = xmax; }
+        } else {
+            for (int k = k0 + lane; k < k1; k += 32) {
+                const int l = ((xk[t * PW + k] + 16 * 0x4000) >> 4) & 0x7FFF;
+                lo = min(lo, l); hi = max(hi, l);
+            }
         }
+        lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+        hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+        if (lane == 0) {
+            if (wj) { wseg[sg][0] = lo; wseg[sg][1] = hi; }
+            else    { xseg[t][sg][0] = lo; xseg[t][sg][1] = hi; }
+        }
+    }
+    if (nprod > 0 && tid == 0 && wsegs > 0) {
+        int lo = 0x7FFF, hi = 0;
+        for (int w = 0; w < R2_THREADS / 32; w++) { lo = min(lo, wred[w][0]); hi = max(hi, wred[w][1]); }
+        wseg[0][0] = lo; wseg[0][1] = hi;
     }
     cp_async_wait<0>();
-    __syncthreads();
-    // weight log range per segment (SIMD over pairs of codes; padding rows hold 1.0)
-    for (int sg = 0; sg < nseg; sg++) {
-        unsigned vmin = 0x7FFF7FFFu, vmax = 0u;
-        const int v1 = min(Ki, (sg + 1) * LR_SEG) * 4;
-#pragma unroll 4
-        for (int v = sg * LR_SEG * 4 + threadIdx.x; v < v1; v += blockDim.x) {
-            const uint4 q = *reinterpret_cast<const uint4 *>(ws + v * 8);
-            const unsigned w0 = q.x & 0x7FFF7FFFu, w1 = q.y & 0x7FFF7FFFu, w2 = q.z & 0x7FFF7FFFu, w3 = q.w & 0x7FFF7FFFu;
-            vmin = __vminu2(vmin, __vminu2(__vminu2(w0, w1), __vminu2(w2, w3)));
-            vmax = __vmaxu2(vmax, __vmaxu2(__vmaxu2(w0, w1), __vmaxu2(w2, w3)));
+    __syncthreads();                                     // the last block-wide barrier
+
+    if (warp >= cw) {
+        // producer: segments s = 1 + (warp - cw), then every nprod-th, each
+        // signalled on named barrier s (ids 1..15: K <= 16 segments)
+        for (int sg = 1 + (warp - cw); sg < nseg; sg += nprod) {
+            const int k0 = sg * LR_SEG, k1 = min(Ki, k0 + LR_SEG);
+            int lo = 0x7FFF, hi = 0;
+            r2_stage_w<R>(wk, PW, Wz, M, m0, k0, k1, lane, 32, vec, lo, hi);
+            lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+            hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+            if (lane == 0) { wseg[sg][0] = lo; wseg[sg][1] = hi; }
+            __threadfence_block();
+            asm volatile("bar.arrive %0, %1;\n" ::"r"(sg), "r"(32 * (cw + 1)) : "memory");
         }
-        int wmin = (int) min(vmin & 0xFFFFu, vmin >> 16), wmax = (int) max(vmax & 0xFFFFu, vmax >> 16);
-        wmin = __reduce_min_sync(0xFFFFFFFFu, wmin);
-        wmax = __reduce_max_sync(0xFFFFFFFFu, wmax);
-        if (lane == 0) { atomicMin(&wseg[sg][0], wmin); atomicMax(&wseg[sg][1], wmax); }
+        return;
     }
-    __syncthreads();                                    // the last block-wide barrier
-    if (!tok) return;
+
+    const int row = lane % R, slot = (lane / R) % TPW, t = warp * TPW + slot;
+    const int64_t n = n0 + t;
+    const bool store_lane = lane < R * TPW;
+    const int * wr = wk + row * PW;
+    const int * xr = xk + t * PW;
     uint32_t v = 0;
     if (Ki > 0) {
-        const int *      xk = xkeys + warp * KP;
-        const uint16_t * xc = xcod + warp * KP;
-        int      a  = 0;                                // key (fast)
-        uint32_t ac = 0;                                // code (slow)
-        bool     fast = true;                           // uniform across the warp
+        constexpr int KM = LT_KM;
+        int      a  = 0;                                 // key (fast)
+        uint32_t ac = 0;                                 // code (slow)
+        bool     fast = true;                            // uniform across the warp
         auto step = [&](int p) {
-            const int d   = max(__viaddmin_s32(a, -p, LT_KM), -LT_KM);
-            const int adj = *reinterpret_cast<const int *>(smem + LT_KM + d);
+            const uint32_t idx = __viaddmin_u32((uint32_t) a, (uint32_t) (KM - p), 2u * KM);
+            const int adj = *reinterpret_cast<const int *>(smem + idx);
             a = __viaddmax_s32(max(a, p), adj, 0);
         };
         for (int sg = 0; sg < nseg; sg++) {
             const int s0 = sg * LR_SEG, s1 = min(Ki, s0 + LR_SEG);
+            if (sg > 0 && nprod > 0)                     // segment sg staged by its producer
+                asm volatile("bar.sync %0, %1;\n" ::"r"(sg), "r"(32 * (cw + 1)) : "memory");
             {
-                // exact in key form over this segment: every product >= 2^-120 (so
-                // no sum, whatever the accumulator, falls below 2^-128), and no sum
-                // can reach 2^127 within it (growth_bound).  The switch goes both
-                // ways, so only the segments that fail run on packed codes.
+                // exact in key form over this segment: every product >= 2^-120 and
+                // no sum able to reach 2^127 within it (growth_bound); decided for
+                // the warp (both token slots), both ways
                 const int am = __reduce_max_sync(0xFFFFFFFFu, sg == 0 ? 0 : fast ? (a >> 4) : (int) (ac & 0x7FFFu));
-                const bool ok = wseg[sg][0] + xseg[warp][sg][0] - 0x4000 >= 964 &&
-                                max(am, wseg[sg][1] + xseg[warp][sg][1] - 0x4000) + growth_bound(LR_SEG) <= 0x7FFF;
+                const bool mine = wseg[sg][0] + xseg[t][sg][0] - 0x4000 >= 964 &&
+                                  max(am, wseg[sg][1] + xseg[t][sg][1] - 0x4000) + growth_bound(LR_SEG) <= 0x7FFF;
+                const bool ok = __all_sync(0xFFFFFFFFu, mine);
                 if (sg > 0 && ok != fast) {
                     if (ok) a = key_of_code(ac);
                     else    ac = code_of_key(a);
@@ -1298,31 +1404,46 @@ k_mul_mat16_res(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * 
             int k = s0;
             if (fast) {
                 if (sg == 0) {
-                    a = key_of_product(key_of_code_w(ws[lane]), xk[0]);
-                    for (k = 1; k < 8 && k < s1; k++) step(key_of_product(key_of_code_w(ws[k * 32 + lane]), xk[k]));
+                    a = key_of_product(wr[0], xr[0]);
+                    for (k = 1; k < 4 && k < s1; k++) step(key_of_product(wr[k], xr[k]));
                 }
-                for (; k + 8 <= s1; k += 8) {
-                    const int4 x0 = *reinterpret_cast<const int4 *>(xk + k);
-                    const int4 x1 = *reinterpret_cast<const int4 *>(xk + k + 4);
-                    const int xk8[8] = { x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w };
-                    int p8[8];
-#pragma unroll
-                    for (int u = 0; u < 8; u++) p8[u] = key_of_product(key_of_code_w(ws[(k + u) * 32 + lane]), xk8[u]);
-#pragma unroll
-                    for (int u = 0; u < 8; u++) step(p8[u]);
+                if (k + 4 <= s1) {
+                    // four steps per pair of 16-byte loads, the next four loaded first
+                    int4 w4 = *reinterpret_cast<const int4 *>(wr + k), x4 = *reinterpret_cast<const int4 *>(xr + k);
+                    for (; k + 8 <= s1; k += 4) {
+                        const int4 wn = *reinterpret_cast<const int4 *>(wr + k + 4), xn = *reinterpret_cast<const int4 *>(xr + k + 4);
+                        step(key_of_product(w4.x, x4.x));
+                        step(key_of_product(w4.y, x4.y));
+                        step(key_of_product(w4.z, x4.z));
+                        step(key_of_product(w4.w, x4.w));
+                        w4 = wn; x4 = xn;
+                    }
+                    step(key_of_product(w4.x, x4.x));
+                    step(key_of_product(w4.y, x4.y));
+                    step(key_of_product(w4.z, x4.z));
+                    step(key_of_product(w4.w, x4.w));
+                    k += 4;
                 }
-                for (; k < s1; k++) step(key_of_product(key_of_code_w(ws[k * 32 + lane]), xk[k]));
+                for (; k < s1; k++) step(key_of_product(wr[k], xr[k]));
             } else {
-                if (sg == 0) { ac = mul16(ws[lane], xc[0]); k = 1; }
-                for (; k < s1; k++) ac = add16(ac, mul16(ws[k * 32 + lane], xc[k]), tab2);
+                auto wc = [&](int kk) { return code_of_key(wr[kk]); };
+                auto xc = [&](int kk) { return code_of_key(xr[kk] + 16 * 0x4000); };
+                if (sg == 0) { ac = mul16(wc(0), xc(0)); k = 1; }
+                for (; k < s1; k++) ac = add16(ac, mul16(wc(k), xc(k)), tab2);
             }
         }
         v = fast ? code_of_key(a) : ac;
     }
-    if (m0 + lane < M) {
-        const int64_t o = (z * N + n) * M + m0 + lane;
-        if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
-        else                   static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
+    const int64_t m = m0 + row;
+    if (store_lane && n < N && m < M) {
+        if (peers.n > 0) {
+            const int64_t o = (z * N + n) * peers.ld + peers.off + m;
+            for (int p = 0; p < peers.n; p++) peers.ptrs[p][o] = (uint16_t) v;
+        } else {
+            const int64_t o = (z * N + n) * M + m;
+            if constexpr (OUT_F32) static_cast<float *>(dst)[o] = to_f32_16(T, v);
+            else                   static_cast<uint16_t *>(dst)[o] = (uint16_t) v;
+        }
     }
 }
 
@@ -1576,7 +1697,7 @@ __global__ void __launch_bounds__(a32_threads(FMT, RING), 1)
 k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
               const typename a32_fmt<FMT>::elem * __restrict__ X, void * __restrict__ dst, int64_t K, int64_t M,
               int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3, int64_t nz, uint32_t monte_seed,
-              int vecx, int lat_sel) {
+              int vecx, int lat_sel, peer_out_dev peers) {
     using E  = typename a32_fmt<FMT>::elem;
     using OP = a32_fmt<FMT>;
     using RG = a32_ring<FMT, TN>;
@@ -1684,7 +1805,14 @@ k_mul_mat_a32(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
 #pragma unroll
             for (int t = 0; t < TN; t++) {
                 const int64_t n = tg * TN + t;
-                if (n < N) OP::store(T, dst, (z * N + n) * M + m, K == 0 ? 0u : OP::finish(acc[t]), OUT_F32);
+                if (n >= N) continue;
+                const uint32_t v = K == 0 ? 0u : OP::finish(acc[t]);
+                if (!OUT_F32 && peers.n > 0) {             // the fused all-gather: codes into every peer's buffer
+                    const int64_t o = (z * N + n) * peers.ld + peers.off + m;
+                    for (int p = 0; p < peers.n; p++) reinterpret_cast<E *>(peers.ptrs[p])[o] = (E) v;
+                } else {
+                    OP::store(T, dst, (z * N + n) * M + m, v, OUT_F32);
+                }
             }
         }
     }
@@ -2522,7 +2650,7 @@ int sm_count(int dev) {
 
 template <int FMT, int TN, bool OUT_F32, bool RING>
 int launch_a32(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, int64_t r2, int64_t r3, int64_t units,
-               int dev, bool vecx, cudaStream_t stream) {
+               int dev, bool vecx, cudaStream_t stream, const peer_out_dev & peers) {
     static bool attr[k_max_devices] = {};
     auto kern = k_mul_mat_a32<FMT, TN, OUT_F32, RING>;
     constexpr int smem = RING ? a32_ring<FMT, TN>::smem : a32_ring<FMT, TN>::table;
@@ -2536,22 +2664,22 @@ int launch_a32(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, in
     launch_k(kern, (unsigned) grid, a32_threads(FMT, RING), smem, stream, T, static_cast<const E *>(a->w), static_cast<const E *>(a->x),
                                                        dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3,
                                                        a->ne12 * a->ne13, a->monte_seed, vecx ? 1 : 0,
-                                                       units <= (int64_t) sm_count(dev) * LNSB_A32_SEL_WARPS ? 1 : 0);
+                                                       units <= (int64_t) sm_count(dev) * LNSB_A32_SEL_WARPS ? 1 : 0, peers);
     return launch_status();
 }
 
 template <int FMT, int TN>
 int launch_a32_by(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, bool out_f32, bool ring, int64_t r2,
-                  int64_t r3, int64_t units, int dev, bool vecx, cudaStream_t stream) {
-    if (ring) return out_f32 ? launch_a32<FMT, TN, true, true>(T, a, dst, r2, r3, units, dev, vecx, stream)
-                             : launch_a32<FMT, TN, false, true>(T, a, dst, r2, r3, units, dev, vecx, stream);
-    return out_f32 ? launch_a32<FMT, TN, true, false>(T, a, dst, r2, r3, units, dev, vecx, stream)
-                   : launch_a32<FMT, TN, false, false>(T, a, dst, r2, r3, units, dev, vecx, stream);
+                  int64_t r3, int64_t units, int dev, bool vecx, cudaStream_t stream, const peer_out_dev & peers) {
+    if (ring) return out_f32 ? launch_a32<FMT, TN, true, true>(T, a, dst, r2, r3, units, dev, vecx, stream, peers)
+                             : launch_a32<FMT, TN, false, true>(T, a, dst, r2, r3, units, dev, vecx, stream, peers);
+    return out_f32 ? launch_a32<FMT, TN, true, false>(T, a, dst, r2, r3, units, dev, vecx, stream, peers)
+                   : launch_a32<FMT, TN, false, false>(T, a, dst, r2, r3, units, dev, vecx, stream, peers);
 }
 
 // sum32-mode xlns16 and xlns32 mul_mat: one or two tokens per lane
 int mul_mat_a32(int fmt, const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, bool out_f32, int64_t r2,
-                int64_t r3, cudaStream_t stream) {
+                int64_t r3, cudaStream_t stream, const peer_out_dev & peers) {
     int dev = 0;
     const int ds = current_device(&dev);
     if (ds != 0) return ds;
@@ -2566,11 +2694,11 @@ int mul_mat_a32(int fmt, const dev_tables & T, const lnsb_mul_mat_args * a, void
     const bool vecx = (a->K * es) % 16 == 0 && ((uintptr_t) a->x % 16) == 0;
     const bool ring = vecx && (a->M * es) % 16 == 0 && ((uintptr_t) a->w % 16) == 0;
     if (fmt == LNSB_XLNS16) {
-        if (tn2) return launch_a32_by<16, 2>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream);
-        return launch_a32_by<16, 1>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream);
+        if (tn2) return launch_a32_by<16, 2>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream, peers);
+        return launch_a32_by<16, 1>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream, peers);
     }
-    if (tn2) return launch_a32_by<32, 2>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream);
-    return launch_a32_by<32, 1>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream);
+    if (tn2) return launch_a32_by<32, 2>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream, peers);
+    return launch_a32_by<32, 1>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream, peers);
 }
 
 int mul_mat_id_impl(int fmt, const lnsb_mul_mat_id_args * a, void * dst, bool out_f32, cudaStream_t stream) {
@@ -2625,28 +2753,55 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
     const int64_t r2 = a->ne12 / a->ne02, r3 = a->ne13 / a->ne03;
     const int64_t tiles = ((a->M + FB_BM - 1) / FB_BM) * ((a->N + FB_BN - 1) / FB_BN) * a->ne12 * a->ne13;
     const peer_out_dev no_peers{ nullptr, 0, 0, 0 };
-    if (peers != nullptr && !(fmt == LNSB_XLNS16 && (k_mode == M_BASE || k_mode == M_MONTE)))
-        return LNSB_E_UNSUPPORTED;                       // the gather is fused into the tiled kernel (any size) only
-    int lr_tnc = (int) (a->N < 4 ? a->N : 4);
-    while (lr_tnc > 1 && lr_smem(a->K, lr_tnc) > LR_SMEM_MAX) lr_tnc--;
-    if (peers == nullptr && fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && lr_smem(a->K, lr_tnc) <= LR_SMEM_MAX &&
-        a->K <= (int64_t) LR_SEG * LR_MAXSEG && (a->N + lr_tnc - 1) / lr_tnc <= 65535) {
-        // few outputs, weight slices resident in shared memory
-        const dim3 grid((unsigned) ((a->M + 31) / 32), (unsigned) ((a->N + lr_tnc - 1) / lr_tnc), (unsigned) (a->ne12 * a->ne13));
-        const bool vec = a->M % 8 == 0 && ((uintptr_t) a->w % 16) == 0;
-        const int smem = lr_smem(a->K, lr_tnc);
-        auto kern = out_f32 ? k_mul_mat16_res<true> : k_mul_mat16_res<false>;
-        static int rattr[k_max_devices][2] = {};
+    if (peers != nullptr && out_f32) return LNSB_E_INVALID;   // the fused gather stores codes
+    // few outputs, weight keys resident: the first lane layout (rows x token
+    // slots per warp: 32 x 1, 16 x 1 with lanes repeated, 16 x 2) and the
+    // fewest chain warps per CTA (1, 2, 3, then 4) that keep the grid within
+    // one CTA per SM and the slice within shared memory
+    int r2_R = 0, r2_tpw = 0, r2_cw = 0;
+    if (fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && a->K <= (int64_t) LR_SEG * LR_MAXSEG &&
+        (peers == nullptr || !out_f32)) {
         int dev = 0;
         const int ds = current_device(&dev);
         if (ds != 0) return ds;
-        if (rattr[dev][out_f32] < smem) {
-            const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LR_SMEM_MAX);
-            if (e != cudaSuccess) return (int) e;
-            rattr[dev][out_f32] = LR_SMEM_MAX;
+        const int64_t sms = sm_count(dev);
+        const int layouts[3][2] = { { 32, 1 }, { 16, 1 }, { 16, 2 } };
+        for (const auto & L : layouts) {               // with at least one producer warp
+            const int R = L[0], tpw = L[1];
+            for (const int cw : { 1, 2, 3 }) {
+                const int64_t tpc = (int64_t) cw * tpw;
+                const int64_t ctas = ((a->M + R - 1) / R) * ((a->N + tpc - 1) / tpc) * a->ne12 * a->ne13;
+                if (r2_smem(a->K, R, (int) tpc) > R2_SMEM_MAX || (a->N + tpc - 1) / tpc > 65535) break;
+                if (ctas <= sms) { r2_R = R; r2_tpw = tpw; r2_cw = cw; break; }
+            }
+            if (r2_R != 0) break;
         }
-        launch_k(kern, grid, 32 * lr_tnc, smem, stream, *T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
-                                                  dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, vec ? 1 : 0);
+        // more CTAs than SMs: 16 rows x 2 tokens, as many chain warps as fit
+        for (const int cw : { 3, 2, 1 })
+            if (r2_R == 0 && r2_smem(a->K, 16, 2 * cw) <= R2_SMEM_MAX && (a->N + 2 * cw - 1) / (2 * cw) <= 65535) {
+                r2_R = 16; r2_tpw = 2; r2_cw = cw;
+            }
+    }
+    if (r2_R != 0) {
+        const int tpc = r2_cw * r2_tpw;
+        const dim3 grid((unsigned) ((a->M + r2_R - 1) / r2_R), (unsigned) ((a->N + tpc - 1) / tpc), (unsigned) (a->ne12 * a->ne13));
+        const int smem = r2_smem(a->K, r2_R, tpc);
+        const int li = r2_R == 32 ? 0 : r2_tpw == 1 ? 1 : 2;
+        auto kern = li == 0 ? (out_f32 ? k_mul_mat16_res2<true, 32, 1> : k_mul_mat16_res2<false, 32, 1>)
+                  : li == 1 ? (out_f32 ? k_mul_mat16_res2<true, 16, 1> : k_mul_mat16_res2<false, 16, 1>)
+                            : (out_f32 ? k_mul_mat16_res2<true, 16, 2> : k_mul_mat16_res2<false, 16, 2>);
+        static bool r2attr[k_max_devices][2][3] = {};
+        int dev = 0;
+        const int ds = current_device(&dev);
+        if (ds != 0) return ds;
+        if (!r2attr[dev][out_f32][li]) {
+            const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, R2_SMEM_MAX);
+            if (e != cudaSuccess) return (int) e;
+            r2attr[dev][out_f32][li] = true;
+        }
+        launch_k(kern, grid, R2_THREADS, smem, stream, *T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
+                 dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, r2_cw,
+                 a->M % 8 == 0 && ((uintptr_t) a->w % 16) == 0 ? 1 : 0, peers != nullptr ? *peers : no_peers);
     } else if (peers == nullptr && fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && a->K <= LT_MAX_K && a->N <= 65535) {
         // few outputs: latency form, two tokens per thread where they fit
 #ifndef LNSB_LT_TN2
@@ -2722,7 +2877,7 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
                                                     a->ne12, r2, r3, a->monte_seed, vec ? 1 : 0, peers ? *peers : no_peers,
                                                     gx, nfull);
     } else if (fmt == LNSB_XLNS32 || k_mode == M_SUM32 || k_mode == M_LPVIP || k_mode == M_MONTE_BYLPVIP) {
-        return mul_mat_a32(fmt, *T, a, dst, out_f32, r2, r3, stream);
+        return mul_mat_a32(fmt, *T, a, dst, out_f32, r2, r3, stream, peers ? *peers : no_peers);
     } else {
         return LNSB_E_UNSUPPORTED;
     }
@@ -2925,6 +3080,58 @@ struct lnsb_weight_cache {
     size_t                 staging_bytes = 0;
     std::mutex             mu;
 };
+
+// Dependent latency of one addition, for the chain bounds of latency-bound
+// ops: one warp runs `steps` dependent additions per lane over operands of a
+// dot product's spread (logs -6 +- 2 octaves, mixed signs for the general
+// addition, non-negative terms for the normalisers'), with the adder's table
+// in shared memory as the kernels hold it; lanes past `lanes` repeat the
+// first `lanes` (same addresses).  kind 0: the key-form general xlns16
+// addition of the latency mul_mat kernels; 1: the non-negative xlns16
+// addition (padd16); 2: the non-negative xlns32 addition (padd32f).  out[0]:
+// SM cycles over the timed steps, out[1]: the final accumulator (keeps the
+// chain live).
+constexpr int AL_OPS = 256;                                      // operands per lane, cycled
+__global__ void __launch_bounds__(32) k_add_latency(dev_tables T, int kind, int lanes, int steps, int64_t * out) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    constexpr int TAB = (k16s_bytes > k32f_sb_bytes16 ? k16s_bytes : k32f_sb_bytes16);
+    const int lane = threadIdx.x, me = lane % lanes;
+    int32_t * ops = reinterpret_cast<int32_t *>(smem + TAB);     // [AL_OPS][32]
+    if (kind == 0) stage_async(smem, T.key16s, k16s_bytes);
+    else if (kind == 1) stage_async(smem, T.sbdb16, k16_tab_bytes16);
+    else stage_async(smem, T.flat32, k32f_sb_bytes16);
+    cp_async_commit();
+    for (int i = 0; i < AL_OPS; i++) {
+        uint32_t h = (uint32_t) (me * 7919 + i) * 2654435761u;
+        h ^= h >> 15;
+        h *= 2246822519u;
+        h ^= h >> 13;
+        const int lg = 0x4000 - 768 + (int) (h % 512u) - 256;    // -6 +- 2 octaves
+        const uint32_t code = (uint32_t) lg | (kind == 0 ? ((h >> 20) & 1u) << 15 : 0u);
+        ops[i * 32 + lane] = kind == 0 ? key_of_product(key_of_code_w(code), key_of_code_x(0x4000u))
+                           : kind == 1 ? (int32_t) code : (int32_t) (code << 16);
+    }
+    cp_async_wait<0>();
+    __syncwarp();
+    constexpr int KM = LT_KM;
+    uint32_t a = (uint32_t) ops[lane];
+    const long long t0 = clock64();
+    if (kind == 0) {
+        int ak = (int) a;
+        for (int k = 1; k < steps; k++) {
+            const int p = ops[(k & (AL_OPS - 1)) * 32 + lane];
+            const uint32_t idx = __viaddmin_u32((uint32_t) ak, (uint32_t) (KM - p), 2u * KM);
+            ak = __viaddmax_s32(max(ak, p), *reinterpret_cast<const int *>(smem + idx), 0);
+        }
+        a = (uint32_t) ak;
+    } else if (kind == 1) {
+        for (int k = 1; k < steps; k++) a = padd16(a, (uint32_t) ops[(k & (AL_OPS - 1)) * 32 + lane], reinterpret_cast<const int16_t *>(smem));
+    } else {
+        for (int k = 1; k < steps; k++) a = padd32f(reinterpret_cast<const int32_t *>(smem), a, (uint32_t) ops[(k & (AL_OPS - 1)) * 32 + lane]);
+    }
+    const long long t1 = clock64();
+    if (lane == 0) { out[0] = t1 - t0; out[1] = (int64_t) a; }
+}
 
 // the glu kernels by format, output form and activation
 template <int FMT, bool OUT_LNS>
@@ -3186,6 +3393,26 @@ int lnsb_group_barrier(int32_t * const * flags, int world, int rank, int32_t epo
     return launch_status();
 }
 
+int lnsb_add_latency(int kind, int lanes, int steps, int64_t * out, lnsb_stream_t stream) {
+    if (kind < 0 || kind > 2 || lanes < 1 || lanes > 32 || steps < 2 || out == nullptr) return LNSB_E_INVALID;
+    const dev_tables * T = nullptr;
+    const int st = tables_for(kind == 2 ? LNSB_XLNS32 : LNSB_XLNS16, &T);
+    if (st != 0) return st;
+    constexpr int TAB = (k16s_bytes > k32f_sb_bytes16 ? k16s_bytes : k32f_sb_bytes16);
+    constexpr int smem = TAB + AL_OPS * 32 * 4;
+    static bool attr[k_max_devices] = {};
+    int dev = 0;
+    const int ds = current_device(&dev);
+    if (ds != 0) return ds;
+    if (!attr[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(k_add_latency, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return (int) e;
+        attr[dev] = true;
+    }
+    k_add_latency<<<1, 32, smem, static_cast<cudaStream_t>(stream)>>>(*T, kind, lanes, steps, out);
+    return launch_status();
+}
+
 int lnsb_mul_mat_id(int fmt, const lnsb_mul_mat_id_args * args, lnsb_stream_t stream) {
     return mul_mat_id_impl(fmt, args, args ? args->dst : nullptr, true, static_cast<cudaStream_t>(stream));
 }
@@ -3238,9 +3465,15 @@ int lnsb_soft_max_lns_noalloc(int fmt, const void * src, const int64_t ne[4], co
     static std::mutex scratch_mu;
     if (!valid_fmt(fmt) || ne == nullptr || (mask != nullptr && mne == nullptr)) return LNSB_E_INVALID;
     for (int i = 0; i < 4; i++) if (ne[i] < 0) return LNSB_E_INVALID;
-    const int64_t nel = ne[0] * ne[1] * ne[2] * ne[3];
-    if (nel == 0) return 0;
-    if ((uint64_t) nel > LNSB_NOALLOC_SCRATCH_BYTES / lnsb_value_size(fmt)) return LNSB_E_TOO_LARGE;
+    for (int i = 0; i < 4; i++) if (ne[i] == 0) return 0;
+    // the element count as a running product, refused as soon as it passes the
+    // scratch's capacity, so that no product of huge dimensions can wrap
+    const int64_t cap = (int64_t) (LNSB_NOALLOC_SCRATCH_BYTES / lnsb_value_size(fmt));
+    int64_t nel = 1;
+    for (int i = 0; i < 4; i++) {
+        if (ne[i] > cap / nel) return LNSB_E_TOO_LARGE;
+        nel *= ne[i];
+    }
     int dev = 0;
     const int st = current_device(&dev);
     if (st != 0) return st;

@@ -76,6 +76,16 @@ class KernelSet:
     def upload_tables(self):
         _lib.check(self.lib, "lnsb_upload_tables", self.lib.lnsb_upload_tables(self.fmt))
 
+    def add_latency(self, kind, lanes=32, steps=4096):
+        """SM cycles of one dependent LNS addition (lnsb_add_latency): kind 0 the
+        key-form xlns16 addition of the latency mul_mat kernels, 1 / 2 the
+        non-negative xlns16 / xlns32 additions of the normalisers"""
+        import torch
+        out = torch.zeros(2, dtype=torch.int64, device="cuda")
+        _lib.check(self.lib, "lnsb_add_latency", self.lib.lnsb_add_latency(kind, lanes, steps, _ptr(out), None))
+        torch.cuda.synchronize()
+        return out[0].item() / (steps - 1)
+
     def to_lns(self, src, dst, stream=None):
         _lib.check(self.lib, "lnsb_to_lns", self.lib.lnsb_to_lns(self.fmt, _ptr(src), _ptr(dst), src.numel(), _stream(stream)))
 

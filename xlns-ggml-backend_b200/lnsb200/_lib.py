@@ -99,6 +99,7 @@ SIGNATURES = [
     ("lnsb_mul_mat_lns", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), _VP, _VP]),
     ("lnsb_mul_mat_lns_peers", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), ctypes.POINTER(PeerOut), _VP]),
     ("lnsb_group_barrier", ctypes.c_int, [_VP, ctypes.c_int, ctypes.c_int, ctypes.c_int32, _VP, _VP]),
+    ("lnsb_add_latency", ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP, _VP]),
     ("lnsb_mul_mat_id", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatIdArgs), _VP]),
     ("lnsb_mul_mat_id_lns", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatIdArgs), _VP, _VP]),
     ("lnsb_mul_mat_id_draws", ctypes.c_uint64, [ctypes.c_int, ctypes.POINTER(MulMatIdArgs)]),

@@ -55,10 +55,16 @@ def all_gather_rows(dst_shard, world, group=None):
     return gather_layout(out.view(dst_shard.dtype), world, N, Mr)
 
 
-def monte_seed_for_shard(seed, jump, M, N, K, rank, world):
+def monte_seed_for_shard(seed, jump, M, N, K, rank, world, slices=1):
     """LFSR state where rank's first chain starts, given the op's seed, for a
     single-slice mul_mat: the chain of global output o = m * N + n starts
     o * (K-1) draws after the op's seed, so the rank's outputs are the global
-    ones shifted by m0 * N.  jump(s, n) is the LFSR jump-ahead."""
+    ones shifted by m0 * N.  jump(s, n) is the LFSR jump-ahead.
+
+    With several slices (z > 0) the kernels number chain (z, m, n) as
+    (z * M_local + m) * N + n, so a shard's chains are not one contiguous run
+    of the global order and no single start state reproduces it: refused."""
+    if slices != 1:
+        raise ValueError("monte_seed_for_shard: a sharded Monte mul_mat must have a single slice (got %d)" % slices)
     m0, _ = row_range(M, world, rank)
     return jump(seed, m0 * N * max(K - 1, 0))
