@@ -141,3 +141,39 @@ def test_fused_step_matches_op_by_op(fmt, mode):
         t = a.argmax(la)
         la, lb = model.forward(a, SMALL, [t], pos), model.forward(b, SMALL, [t], pos)
     assert np.array_equal(la.cpu().numpy().view(np.uint32), lb.cpu().numpy().view(np.uint32))
+
+
+@pytest.mark.parametrize("fmt", [16, 32])
+def test_full_length_graph_decode_bit_exact(fmt):
+    """BASELINE configs[2] (LNS16 sum32) and configs[3] (LNS32) at their stated
+    length through the benched path: the SmolLM2-135M shape, the 128-token
+    prompt (seed 2), prefill, then 127 greedy steps replayed from the CUDA
+    graphs of GraphDecoder -- the logits bit for bit against the CPU oracle's
+    graph after the prefill and after every step, and the two greedy streams
+    equal"""
+    import os
+    from lnsb200 import model
+    from oracle_model import OracleOps
+    cfg = model.SMOLLM2_135M
+    w = model.init_weights(cfg, seed=2)
+    prompt = model.prompt_ids(cfg, 128, seed=2)
+    g = model.GpuOps(cfg, w, mode="sum32", n_ctx=256, fmt=fmt)
+    o = OracleOps(cfg, w, mode="sum32", n_ctx=256, nthreads=os.cpu_count() or 1, fmt=fmt)
+    dec = model.GraphDecoder(g, cfg)
+    dec.prepare(128, 128 + 127)
+    lg = model.forward(g, cfg, prompt, 0)
+    lo = model.forward(o, cfg, prompt, 0)
+    assert np.array_equal(lg.cpu().numpy().ravel().view(np.uint32), lo.ravel().view(np.uint32)), "prefill logits differ"
+    tok = g.argmax(lg)
+    assert tok == o.argmax(lo)
+    toks = [tok]
+    for pos in range(128, 128 + 127):
+        lgp = dec.step(pos, tok)
+        lo = model.forward(o, cfg, [tok], pos)
+        torch.cuda.synchronize()
+        assert np.array_equal(lgp.cpu().numpy().ravel().view(np.uint32), lo.ravel().view(np.uint32)), \
+            "logits differ at decode position %d" % pos
+        tok = int(dec.tok.item())
+        assert tok == o.argmax(lo)
+        toks.append(tok)
+    assert len(toks) == 128

@@ -386,6 +386,7 @@ class GraphDecoder:
         self.tok = torch.zeros(1, dtype=torch.int64, device=ops.dev)
         self.host = torch.zeros(ops.n_ctx, dtype=torch.int64).pin_memory()
         self.graphs = {}
+        self.logits = {}                 # each position's logits: the graph's own output buffer
 
     def capture(self, pos):
         torch = self.torch
@@ -395,6 +396,7 @@ class GraphDecoder:
             self.tok.copy_(torch.argmax(logits.view(-1)).view(1))
             self.host[pos:pos + 1].copy_(self.tok, non_blocking=True)
         self.graphs[pos] = g
+        self.logits[pos] = logits
 
     def prepare(self, pos_from, pos_to):
         """capture the steps at positions pos_from .. pos_to - 1 (after one eager
@@ -407,6 +409,14 @@ class GraphDecoder:
         for p in range(pos_from, pos_to):
             if p not in self.graphs:
                 self.capture(p)
+
+    def step(self, pos, token=None):
+        """replays position pos (after setting the current token, if given) and
+        returns that step's logits (device tensor, valid until pos replays again)"""
+        if token is not None:
+            self.tok.fill_(token)
+        self.graphs[pos].replay()
+        return self.logits[pos]
 
     def decode(self, first_token, pos_from, n):
         """n tokens: first_token is the one the prefill produced (at pos_from)"""
