@@ -19,8 +19,9 @@ LIB = os.path.join(HERE, "lib")
 # mode name -> LNSB_SUM_MODE value (csrc/lnsb_arith.cuh)
 MODES = {"base": 0, "monte": 1, "monte_bylpvip": 2, "lpvip": 3, "sum32": 4}
 
-SOURCES = ["lnsb_kernels.cu", "lnsb_tables.cpp"]
-HEADERS = ["lnsb_arith.cuh", "lnsb_tables.h", os.path.join(ROOT, "include", "lnsb200.h")]
+SOURCES = ["lnsb_kernels.cu", "lnsb_tables.cpp", "lnsb_graph.cpp"]
+HEADERS = ["lnsb_arith.cuh", "lnsb_tables.h", os.path.join(ROOT, "include", "lnsb200.h"),
+           os.path.join(ROOT, "include", "lnsb200_graph.h")]
 
 
 def nvcc():

@@ -20,6 +20,7 @@
 #include <utility>
 
 #include "lnsb200.h"
+#include "lnsb200_graph.h"
 #include "lnsb_arith.cuh"
 #include "lnsb_tables.h"
 
@@ -3133,6 +3134,20 @@ __global__ void __launch_bounds__(32) k_add_latency(dev_tables T, int kind, int 
     if (lane == 0) { out[0] = t1 - t0; out[1] = (int64_t) a; }
 }
 
+// dst (packed [ne3][ne2][ne1][ne0]) = the strided view src (byte strides nb)
+// of E elements: the gather of permuted views (KV-cache views and the like)
+template <typename E>
+__global__ void k_copy_strided(const unsigned char * __restrict__ src, lnsb_shape4 ne, lnsb_shape4 nb,
+                               E * __restrict__ dst, int64_t n) {
+    pdl_entry();
+    LNSB_GRID_STRIDE(i, n) {
+        const int64_t i0 = i % ne.ne[0], r = i / ne.ne[0];
+        const int64_t i1 = r % ne.ne[1], r2 = r / ne.ne[1];
+        const int64_t i2 = r2 % ne.ne[2], i3 = r2 / ne.ne[2];
+        dst[i] = *reinterpret_cast<const E *>(src + i0 * nb.ne[0] + i1 * nb.ne[1] + i2 * nb.ne[2] + i3 * nb.ne[3]);
+    }
+}
+
 // the glu kernels by format, output form and activation
 template <int FMT, bool OUT_LNS>
 void launch_glu(int op, unsigned g, cudaStream_t s, const dev_tables & T, const float * gate, const float * up,
@@ -3390,6 +3405,21 @@ int lnsb_group_barrier(int32_t * const * flags, int world, int rank, int32_t epo
         return LNSB_E_INVALID;
     launch_k(k_group_barrier, dim3(1), dim3((unsigned) ((world + 31) / 32 * 32)), 0, static_cast<cudaStream_t>(stream),
              flags, world, rank, epoch, err, (long long) 1 << 21);
+    return launch_status();
+}
+
+int lnsb_copy_strided(int elem_size, const void * src, const int64_t ne[4], const int64_t nb[4], void * dst,
+                      lnsb_stream_t stream) {
+    if ((elem_size != 2 && elem_size != 4) || ne == nullptr || nb == nullptr) return LNSB_E_INVALID;
+    for (int i = 0; i < 4; i++) if (ne[i] < 0) return LNSB_E_INVALID;
+    const int64_t n = ne[0] * ne[1] * ne[2] * ne[3];
+    if (n == 0) return 0;
+    if (src == nullptr || dst == nullptr) return LNSB_E_INVALID;
+    const lnsb_shape4 e{ { ne[0], ne[1], ne[2], ne[3] } }, b{ { nb[0], nb[1], nb[2], nb[3] } };
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const auto * in = static_cast<const unsigned char *>(src);
+    if (elem_size == 2) launch_k(k_copy_strided<uint16_t>, grid_for(n, 256), 256, 0, s, in, e, b, static_cast<uint16_t *>(dst), n);
+    else                launch_k(k_copy_strided<uint32_t>, grid_for(n, 256), 256, 0, s, in, e, b, static_cast<uint32_t *>(dst), n);
     return launch_status();
 }
 
