@@ -12,11 +12,13 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(ROOT, "include", "lnsb200.h")
+HEADERS = [HEADER, os.path.join(ROOT, "include", "lnsb200_graph.h")]
 MODES = ("base", "monte", "monte_bylpvip", "lpvip", "sum32")
 
 
 def declared():
-    text = open(HEADER).read()
+    """every function the C headers declare (lnsb200.h, the host layer's lnsb200_graph.h)"""
+    text = "".join(open(h).read() for h in HEADERS)
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(lnsb_[a-z0-9_]+)\s*\(", text)))
 
@@ -40,8 +42,8 @@ def test_header_declares_the_kernel_set_surface():
 
 def test_every_declared_symbol_is_exported(libs):
     names = declared()
-    from lnsb200 import _lib
-    bound = {n for n, _, _ in _lib.SIGNATURES}
+    from lnsb200 import _lib, graph
+    bound = {n for n, _, _ in _lib.SIGNATURES} | {n for n, _, _ in graph._SIGS}
     for mode, lib in libs.items():
         for n in names:
             assert hasattr(lib, n), "%s missing from liblnsb200_%s.so" % (n, mode)
