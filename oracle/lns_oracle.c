@@ -231,22 +231,30 @@ uint16_t orc16_mask_from_f32(float m) { return m <= -3.0e38f ? X16_NEG_INF : orc
 /*
  * Addition tables for xlns32 (the reference's LNS32 configuration,
  * "xlns32_alt": table sb with linear interpolation, cotransformed db;
- * docs/CUDA.md:141-143, lns-backend/src/lns16-sum32.h:22-24).  This is a
+ * docs/CUDA.md:141-143, lns-backend/src/lns16-sum32.h:22-24; the library
+ * itself, xlnscpp's xlns32.cpp, is an un-vendored submodule).  This is a
  * restatement of that scheme, not the library's table layout:
- *   sb: knots every 2^-10 octave on [0,8), every 2^-7 on [8,26)
- *   db: knots every 2^-11 / 2^-10 / 2^-9 / 2^-7 octave on [1,2) / [2,4) /
- *       [4,8) / [8,26); on (0,1) the cotransformation
+ *   sb: knots every 2^-9 octave on [0,26), truncated toward zero,
+ *       interpolation rounded to nearest.  Every sum32 "positive" record of
+ *       experiments/dot-product-scaling/results/synth.jsonl (sb only, K = 16
+ *       .. 16384) is reproduced to the printed digit by exactly this choice
+ *       among spacings 2^-7 .. 2^-13 and the truncate / round / floor knot and
+ *       interpolation rules.
+ *   db: on (0,1) the cotransformation
  *       db(z) = log2(A + B),  A = 1 - 2^z2,  B = 2^z2 (1 - 2^z1)
- *       with z1 = z rounded to 2^-11 octave and z2 = z - z1 (exact tables).
- * Knot values are rounded to nearest; interpolation floors.
+ *       with z1 = z rounded to 2^-11 octave and z2 = z - z1 (exact tables);
+ *       on [1,26) knots every 2^-9 octave, truncated, interpolation floored.
+ *       This reproduces the sum32 "signed" record at K = 16 to the printed
+ *       digit; at larger K the reference's error is a little higher (rms
+ *       3.865e-5 against 3.837e-5 at K = 4096), so db beyond one octave is
+ *       not pinned digit for digit.
  */
-typedef struct { uint32_t lo, hi; int shift; int base; } seg_t;
-static const seg_t k_sb_seg[2] = { {0u, 8u << 23, 13, 0}, {8u << 23, 26u << 23, 16, 0} };
-static const seg_t k_db_seg[4] = { {1u << 23, 2u << 23, 12, 0}, {2u << 23, 4u << 23, 13, 0},
-                                   {4u << 23, 8u << 23, 14, 0}, {8u << 23, 26u << 23, 16, 0} };
+typedef struct { uint32_t lo, hi; int shift; int round; } seg_t;
+static const seg_t k_sb_seg[1] = { {0u, 26u << 23, 14, 1} };
+static const seg_t k_db_seg[1] = { {1u << 23, 26u << 23, 14, 0} };
 static int32_t * g_sb32;   /* concatenated knots of both sb segments */
 static int32_t * g_db32;   /* concatenated knots of the 4 db segments */
-static int       g_sb_base[2], g_db_base[4];
+static int       g_sb_base[1], g_db_base[1];
 static int32_t   g_db32_hi[2048];    /* db at z1 = -j * 2^-11 octave, j = 1..2047 */
 static int32_t   g_db32_lo[4096];    /* db at z2 = -k * 2^-23 octave, k = 1..4095 */
 static uint32_t * g_logm32;          /* floor(log2(1 + j/2^23) * 2^23), j < 2^23 */
@@ -273,16 +281,16 @@ void orc_set_knot_mode(int m) { KNOT_MODE = m; }
 
 static int build32(void) {
     int tot = 0;
-    for (int s = 0; s < 2; s++) { g_sb_base[s] = tot; tot += (int)((k_sb_seg[s].hi - k_sb_seg[s].lo) >> k_sb_seg[s].shift) + 1; }
+    for (int s = 0; s < 1; s++) { g_sb_base[s] = tot; tot += (int)((k_sb_seg[s].hi - k_sb_seg[s].lo) >> k_sb_seg[s].shift) + 1; }
     g_sb32 = (int32_t *)malloc(sizeof(int32_t) * (size_t)tot);
-    for (int s = 0; s < 2; s++) {
+    for (int s = 0; s < 1; s++) {
         int n = (int)((k_sb_seg[s].hi - k_sb_seg[s].lo) >> k_sb_seg[s].shift);
         for (int i = 0; i <= n; i++) g_sb32[g_sb_base[s] + i] = knot_sb(k_sb_seg[s].lo + ((uint32_t)i << k_sb_seg[s].shift));
     }
     tot = 0;
-    for (int s = 0; s < 4; s++) { g_db_base[s] = tot; tot += (int)((k_db_seg[s].hi - k_db_seg[s].lo) >> k_db_seg[s].shift) + 1; }
+    for (int s = 0; s < 1; s++) { g_db_base[s] = tot; tot += (int)((k_db_seg[s].hi - k_db_seg[s].lo) >> k_db_seg[s].shift) + 1; }
     g_db32 = (int32_t *)malloc(sizeof(int32_t) * (size_t)tot);
-    for (int s = 0; s < 4; s++) {
+    for (int s = 0; s < 1; s++) {
         int n = (int)((k_db_seg[s].hi - k_db_seg[s].lo) >> k_db_seg[s].shift);
         for (int i = 0; i <= n; i++) g_db32[g_db_base[s] + i] = knot_db(k_db_seg[s].lo + ((uint32_t)i << k_db_seg[s].shift));
     }
@@ -296,7 +304,9 @@ static int build32(void) {
     g_expm32 = (float *)malloc(sizeof(float) << 23);
     g_lpvip_db = (int32_t *)malloc(sizeof(int32_t) << 23);
     if (!g_logm32 || !g_expm32 || !g_lpvip_db) return -1;
-    for (uint32_t j = 0; j < (1u << 23); j++) {
+    #pragma omp parallel for schedule(static)
+    for (int32_t jj = 0; jj < (1 << 23); jj++) {
+        const uint32_t j = (uint32_t)jj;
         long double m = 1.0L + (long double)j / (long double)X32_ONE_OCT;
         long double v = log2l(m) * (long double)X32_ONE_OCT;
         g_logm32[j] = (uint32_t)floorl(v);
@@ -324,20 +334,18 @@ static inline int32_t interp(const int32_t * t, const seg_t * sg, int base, uint
     uint32_t i = off >> sg->shift;
     uint32_t f = off & ((1u << sg->shift) - 1u);
     int32_t a = t[base + (int)i], b = t[base + (int)i + 1];
-    return a + (int32_t)(((int64_t)(b - a) * (int64_t)f) >> sg->shift);
+    return a + (int32_t)((((int64_t)(b - a) * (int64_t)f) + (sg->round ? (1LL << (sg->shift - 1)) : 0)) >> sg->shift);
 }
 
 static inline int32_t sb32(uint32_t d) {
     if (d >= X32_ESS) return 0;
-    int s = d >= k_sb_seg[1].lo;
-    return interp(g_sb32, &k_sb_seg[s], g_sb_base[s], d);
+    return interp(g_sb32, &k_sb_seg[0], g_sb_base[0], d);
 }
 
 static inline int32_t db32(uint32_t d) {   /* d > 0 */
     if (d >= X32_ESS) return 0;
     if (d >= X32_ONE_OCT) {
-        int s = d >= (8u << 23) ? 3 : d >= (4u << 23) ? 2 : d >= (2u << 23) ? 1 : 0;
-        return interp(g_db32, &k_db_seg[s], g_db_base[s], d);
+        return interp(g_db32, &k_db_seg[0], g_db_base[0], d);
     }
     uint32_t d1 = d >> 12, d2 = d & 4095u;
     if (d1 == 0) return g_db32_lo[d2];

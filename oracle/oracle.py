@@ -285,6 +285,19 @@ def lfsr_jump(s, n):
     return lib().orc_lfsr_jump(s, n)
 
 
+def synthstat(config, dist, K, seed=1):
+    """the reference's synthetic dot-product error statistics (dot-bench.cpp
+    synth(), run.py defaults) replayed through this oracle's mul_mat
+    (oracle/synthstat.cpp): {"acc", "acc_l2scale", "total"} each with bias,
+    sd, rms, mean_abs, rel_l2"""
+    import json
+    exe = os.path.join(os.path.dirname(PINCHECK), "synthstat")
+    if not os.path.exists(exe):
+        build()
+    out = subprocess.run([exe, config, dist, str(K), str(seed)], capture_output=True, text=True, check=True).stdout
+    return json.loads(out)
+
+
 def convstat(fmt, n=4194304, order=1):
     """the reference's conversion statistics (dot-bench.cpp convert()) replayed
     through this oracle's conversions (oracle/convstat.cpp); order 1 draws the

@@ -101,7 +101,20 @@ def main(ref):
                 convert[rec.pop("format")] = rec
     convert["source"] = ("experiments/dot-product-scaling/results/convert.jsonl "
                          "(protocol: experiments/dot-product-scaling/dot-bench.cpp convert())")
+    # the synthetic dot-product records of the reference's CUDA backend
+    # (dot-bench synth on LNSCUDA16 / LNSCUDA32), K <= 4096
+    synth = []
+    with open(os.path.join(ref, "experiments", "dot-product-scaling", "results", "synth.jsonl")) as f:
+        for line in f:
+            if line.strip():
+                rec = json.loads(line)
+                if rec["K"] <= 4096:
+                    synth.append({k: rec[k] for k in ("config", "dist", "K", "acc", "acc_l2scale", "total")})
     pins = {
+        "synth": {"records": synth,
+                  "source": "experiments/dot-product-scaling/results/synth.jsonl (protocol: "
+                            "experiments/dot-product-scaling/dot-bench.cpp synth(), run.py:62-75; "
+                            "run on the reference's CUDA devices, run.py:46)"},
         "swiglu": swiglu,
         "source": "xlnsresearch/xlns-ggml-backend results/sum32-evidence/*.txt (outputs of "
                   "lns-backend/tests/test-lns16-sum32.cpp and test-lns-backend.cpp)",

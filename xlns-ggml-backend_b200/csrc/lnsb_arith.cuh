@@ -42,8 +42,6 @@ struct dev_tables {
     const int32_t *  lpvip_db;   // 2^23 or null
     const uint16_t * lfsr_log;   // 65536
     const uint16_t * lfsr_alog;  // 65535
-    int              sb_base1;   // first knot of the second sb segment
-    int              db_base[4];
 };
 
 // ============================== xlns16 ====================================
@@ -113,28 +111,25 @@ __device__ __forceinline__ uint32_t div32(uint32_t a, uint32_t b) {
     return ((a ^ b) & 0x80000000u) | (uint32_t) p;
 }
 
-__device__ __forceinline__ int32_t interp32(const int32_t * __restrict__ t, uint32_t lo, int shift, int base,
-                                            uint32_t d) {
-    const uint32_t off = d - lo;
-    const uint32_t i   = off >> shift;
-    const uint32_t f   = off & ((1u << shift) - 1u);
-    const int32_t  a = __ldg(t + base + (int) i), b = __ldg(t + base + (int) i + 1);
-    return a + (int32_t) (((long long) (b - a) * (long long) f) >> shift);
+// sb(z) and db(z) between knots every 2^-9 octave (k32_sh): sb rounded to
+// nearest, db floored (z: sb [0, ess], db [1, ess]; z = ess reads the last
+// knot, 0, with fraction 0)
+__host__ __device__ __forceinline__ int32_t lerp32(int32_t v0, int32_t v1, uint32_t z, int32_t half) {
+    const int32_t f = (int32_t) (z & ((1u << k32_sh) - 1u));
+    return v0 + (((v1 - v0) * f + half) >> k32_sh);
 }
 
 __device__ __forceinline__ int32_t sb32(const dev_tables & T, uint32_t d) {
     if (d >= k32_ess) return 0;
-    if (d >= (8u << 23)) return interp32(T.sb32, 8u << 23, 16, T.sb_base1, d);
-    return interp32(T.sb32, 0u, 13, 0, d);
+    const int32_t i = (int32_t) (d >> k32_sh);
+    return lerp32(__ldg(T.sb32 + i), __ldg(T.sb32 + i + 1), d, 1 << (k32_sh - 1));
 }
 
 __device__ __forceinline__ int32_t db32(const dev_tables & T, uint32_t d) {   // d > 0
     if (d >= k32_ess) return 0;
     if (d >= k32_one) {
-        if (d >= (8u << 23)) return interp32(T.db32, 8u << 23, 16, T.db_base[3], d);
-        if (d >= (4u << 23)) return interp32(T.db32, 4u << 23, 14, T.db_base[2], d);
-        if (d >= (2u << 23)) return interp32(T.db32, 2u << 23, 13, T.db_base[1], d);
-        return interp32(T.db32, 1u << 23, 12, T.db_base[0], d);
+        const int32_t i = (int32_t) ((d - k32_one) >> k32_sh);
+        return lerp32(__ldg(T.db32 + i), __ldg(T.db32 + i + 1), d, 0);
     }
     // cotransformation: 1 - 2^z = (1 - 2^z2) + 2^z2 (1 - 2^z1)
     const uint32_t d1 = d >> 12, d2 = d & 4095u;
@@ -183,12 +178,9 @@ __host__ __device__ __forceinline__ uint32_t add32f(const int32_t * F, uint32_t 
     const uint32_t gap = (uint32_t) (la > lb ? la - lb : lb - la);
     uint32_t z = cot ? gap : d;
     z = z < k32_ess ? z : k32_ess;
-    const int32_t  desc = F[k32f_desc + (int32_t) (z >> 23) + (usedb && !cot ? k32f_desc_db : 0)];
-    const int      sh   = desc & 31;
-    const int32_t  i    = (int32_t) (z >> sh) + (desc >> 5);
-    const int32_t  f    = (int32_t) (z & ((1u << sh) - 1u));
-    const int32_t  v0 = F[i], v1 = F[i + 1];
-    const int32_t  adj = v0 + (((v1 - v0) * f) >> sh) + (cot ? hi : 0);
+    const bool     isdb = usedb && !cot;
+    const int32_t  i    = (int32_t) (z >> k32_sh) + (isdb ? k32f_db0 : k32f_sb);
+    const int32_t  adj  = lerp32(F[i], F[i + 1], z, isdb ? 0 : 1 << (k32_sh - 1)) + (cot ? hi : 0);
     const uint32_t u = (mx & 0x7FFFFFFFu) + (uint32_t) adj;      // adj > -2^28: wrap means negative
     uint32_t p = u < 0x7FFFFFFFu ? u : 0x7FFFFFFFu;
     if (u >= 0xC0000000u) p = 0;
@@ -196,16 +188,10 @@ __host__ __device__ __forceinline__ uint32_t add32f(const int32_t * F, uint32_t 
     return (usedb && d == 0) ? 0u : r;
 }
 
-// sb(z) or db(z) (db: z >= 1) by interpolation in multiply form: entry e of
-// k32f_dsc2 / k32f_dms gives the left knot's word and 2^(32 - shift), so the
-// shifts run as multiplications on the multiply-add pipe, not the integer ALU.
-__device__ __forceinline__ int32_t interp32f(const int32_t * F, uint32_t z, int e) {
-    const int2     ds = reinterpret_cast<const int2 *>(F + k32f_dsc2)[e];
-    const uint32_t ir = __umulhi(z, (uint32_t) ds.y);                    // z >> shift
-    const int32_t  f  = (int32_t) ir * F[k32f_dms + e] + (int32_t) z;     // z mod 2^shift
-    const int32_t * kp = F + ds.x + (int32_t) ir;
-    const int32_t  v0 = kp[0], v1 = kp[1];
-    return v0 + __mulhi((v1 - v0) * f, ds.y);                           // floor(.. / 2^shift)
+// sb(z) (db = false) or db(z) (db = true, z >= 1) over the flat image
+__device__ __forceinline__ int32_t interp32f(const int32_t * F, uint32_t z, bool db) {
+    const int32_t i = (int32_t) (z >> k32_sh) + (db ? k32f_db0 : k32f_sb);
+    return lerp32(F[i], F[i + 1], z, db ? 0 : 1 << (k32_sh - 1));
 }
 
 // the cotransformed db of add32f_lean's rare branch: opposite signs, d < 1
@@ -216,7 +202,7 @@ __device__ __forceinline__ uint32_t add32f_cot(const int32_t * F, uint32_t mx, u
     const int32_t  hi = la > lb ? la : lb;
     uint32_t       z  = (uint32_t) (la > lb ? la - lb : lb - la);
     z = z < k32_ess ? z : k32_ess;
-    const int32_t  p = (int32_t) (mx & 0x7FFFFFFFu) + hi + interp32f(F, z, (int) (z >> 23));   // hi + sb < 0
+    const int32_t  p = (int32_t) (mx & 0x7FFFFFFFu) + hi + interp32f(F, z, false);   // hi + sb < 0
     const uint32_t r = (mx & 0x80000000u) | (uint32_t) (p > 0 ? p : 0);
     return d == 0 ? 0u : r;
 }
@@ -242,7 +228,7 @@ __device__ __forceinline__ add32f_part add32f_main(const int32_t * F, uint32_t a
     o.mx = agt ? a : b;
     const bool     usedb = (int32_t) (a ^ b) < 0;
     const uint32_t z     = o.d < k32_ess ? o.d : k32_ess;
-    const uint32_t r     = o.mx + (uint32_t) interp32f(F, z, (int) (z >> 23) + (usedb ? k32f_dsc2_db : 0));
+    const uint32_t r     = o.mx + (uint32_t) interp32f(F, z, usedb);
     o.r   = (int32_t) (r ^ o.mx) < 0 ? (o.mx | 0x7FFFFFFFu) : r;
     o.cot = usedb && o.d < k32_one;
     return o;
@@ -253,16 +239,9 @@ __device__ __forceinline__ uint32_t add32f_lean(const int32_t * F, uint32_t a, u
 }
 
 // add32 over the flat image for a chain's latency: the main result (sb(d),
-// or db(d) for d >= 1, by the loaded descriptor of d's octave) and the
-// cotransformed one (sb of the gap, its segment by compare) are computed
+// or db(d) for d >= 1) and the cotransformed one (sb of the gap) are computed
 // independently and selected, so the dependent path is two table levels
 // deep instead of three.  Same bits as add32.
-__device__ __forceinline__ int32_t interp32_sh(const int32_t * F, uint32_t z, int sh, int32_t base) {
-    const int32_t i  = (int32_t) (z >> sh) + base;
-    const int32_t f  = (int32_t) (z & ((1u << sh) - 1u));
-    const int32_t v0 = F[i], v1 = F[i + 1];
-    return v0 + (((v1 - v0) * f) >> sh);
-}
 __device__ __forceinline__ uint32_t add32f_sel(const int32_t * F, uint32_t a, uint32_t b) {
     const uint32_t al = a & 0x7FFFFFFFu, bl = b & 0x7FFFFFFFu;
     const bool     agt   = al > bl;
@@ -272,8 +251,7 @@ __device__ __forceinline__ uint32_t add32f_sel(const int32_t * F, uint32_t a, ui
     const bool     cot   = usedb && d < k32_one;
     // main: |mx| + sb(d) or db(d); above 0x7FFFFFFF the carry reaches the sign bit
     const uint32_t z    = d < k32_ess ? d : k32_ess;
-    const int32_t  desc = F[k32f_desc + (int32_t) (z >> 23) + (usedb ? k32f_desc_db : 0)];
-    const uint32_t r0   = mx + (uint32_t) interp32_sh(F, z, desc & 31, desc >> 5);
+    const uint32_t r0   = mx + (uint32_t) interp32f(F, z, usedb);
     const uint32_t rm   = (int32_t) (r0 ^ mx) < 0 ? (mx | 0x7FFFFFFFu) : r0;
     // cot: max(la, lb) + sb(|la - lb|), clamped at zero
     const int32_t  d2 = (int32_t) (d & 4095u);
@@ -282,9 +260,7 @@ __device__ __forceinline__ uint32_t add32f_sel(const int32_t * F, uint32_t a, ui
     const int32_t  hi = la > lb ? la : lb;
     uint32_t       zc = (uint32_t) (la > lb ? la - lb : lb - la);
     zc = zc < k32_ess ? zc : k32_ess;
-    const bool     big = zc >= ((uint32_t) k32f_sb_split << 23);
-    const int32_t  p   = (int32_t) (mx & 0x7FFFFFFFu) + hi +
-                         interp32_sh(F, zc, big ? k32f_sb_sh1 : k32f_sb_sh0, big ? k32f_sb_base1 : k32f_sb);
+    const int32_t  p   = (int32_t) (mx & 0x7FFFFFFFu) + hi + interp32f(F, zc, false);
     const uint32_t rc  = (mx & 0x80000000u) | (uint32_t) (p > 0 ? p : 0);
     return cot ? (d == 0 ? 0u : rc) : rm;
 }
@@ -486,19 +462,12 @@ __device__ __forceinline__ uint32_t padd16(uint32_t a, uint32_t b, const int16_t
     const int adj = tab[min(d, k16_ess + 1)] >> 1;
     return (uint32_t) min(max((int) a, (int) b) + adj, 0x7FFF);
 }
-// padd32f: sb by interpolation with the segment chosen by a compare (no
-// descriptor load on the chain's dependent path), shifts in place of the
-// multiply form
+// padd32f: sb by interpolation, one table level on the chain's dependent path
 __device__ __forceinline__ uint32_t padd32f(const int32_t * F, uint32_t a, uint32_t b) {
     const uint32_t d  = a > b ? a - b : b - a;
     const uint32_t mx = a > b ? a : b;
     const uint32_t z  = d < k32_ess ? d : k32_ess;
-    const bool     hi = z >= ((uint32_t) k32f_sb_split << 23);
-    const int      sh = hi ? k32f_sb_sh1 : k32f_sb_sh0;
-    const int32_t  i  = (int32_t) (z >> sh) + (hi ? k32f_sb_base1 : k32f_sb);
-    const int32_t  f  = (int32_t) (z & ((1u << sh) - 1u));
-    const int32_t  v0 = F[i], v1 = F[i + 1];
-    const uint32_t r  = mx + (uint32_t) (v0 + (((v1 - v0) * f) >> sh));
+    const uint32_t r  = mx + (uint32_t) interp32f(F, z, false);
     return (int32_t) r < 0 ? 0x7FFFFFFFu : r;                      // saturation: the carry into bit 31
 }
 

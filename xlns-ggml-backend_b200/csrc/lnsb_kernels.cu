@@ -1453,7 +1453,7 @@ k_mul_mat16_res2(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 // xlns16 in sum32 mode (acc32 = add32(acc32, t << 16), narrowed once at the
 // end; lns-backend/cuda/lns-cuda-xlns16.cu:75-130, lns16-sum32.h:59-107) and
 // the xlns32 format (lns-backend/cuda/lns-cuda-xlns32.cu:30-67) share this
-// kernel.  The flat addition image (k32f_words, ~100 KB) is resident in shared
+// kernel.  The flat addition image (k32f_words, ~126 KB) is resident in shared
 // memory, one CTA per SM (32 warps for xlns16, 16 for xlns32).  A warp runs
 // 32 x TN chains side by side: 32 consecutive weight rows (one per lane)
 // against TN tokens (two once there are enough units of work, so a lane has
@@ -3237,8 +3237,6 @@ int lnsb_upload_tables(int fmt) {
         if (e == cudaSuccess) e = upload(H.flat32, &t.flat32);
         if (e == cudaSuccess) e = upload(H.lfsr_log, &t.lfsr_log);
         if (e == cudaSuccess) e = upload(H.lfsr_alog, &t.lfsr_alog);
-        t.sb_base1 = H.sb_seg[1].base;
-        for (int i = 0; i < 4; i++) t.db_base[i] = H.db_seg[i].base;
     }
     if (e == cudaSuccess && need_lpvip && t.lpvip_db == nullptr) e = upload(H.lpvip_db, &t.lpvip_db);
     if (e == cudaSuccess && need32 && t.logm32 == nullptr) {

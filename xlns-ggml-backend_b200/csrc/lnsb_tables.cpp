@@ -187,14 +187,15 @@ int32_t knot(long double v) { return (int32_t) (v * (long double) k32_one); }
 int32_t knot_sb(uint32_t d) { return knot(log1pl(exp2l(-(long double) d / (long double) k32_one)) / k_ln2); }
 int32_t knot_db(uint32_t d) { return knot(log1pl(-exp2l(-(long double) d / (long double) k32_one)) / k_ln2); }
 
-// The flat image of k32f_sb.  Checks that its layout matches the segment
-// geometry and that every interpolation product (right - left) * f fits in 32
-// bits, so the kernels' 32-bit multiply equals the 64-bit definition; on a
+// The flat image of k32f_sb.  Checks that every interpolation product
+// (right - left) * f plus the rounding half fits in 32 bits, so the kernels'
+// 32-bit multiply equals the 64-bit definition, and that z + db(z) >= 0 at
+// every db knot (the main path's result needs no clamp from below); on a
 // failed check the image stays empty and lnsb_upload_tables reports it.
 void build_flat32(host_tables & t) {
     auto & f = t.flat32;
     f.clear();
-    if ((int) t.sb32.size() != k32f_db - k32f_sb || (int) t.db32.size() != k32f_lo - k32f_db) return;
+    if ((int) t.sb32.size() != k32_sb_knots + 1 || (int) t.db32.size() != k32_db_knots + 1) return;
     f.assign(k32f_words, 0);
     std::copy(t.sb32.begin(), t.sb32.end(), f.begin() + k32f_sb);
     std::copy(t.db32.begin(), t.db32.end(), f.begin() + k32f_db);
@@ -202,63 +203,23 @@ void build_flat32(host_tables & t) {
     std::copy(t.db32_hi.begin(), t.db32_hi.end(), f.begin() + k32f_hi);
     f[k32f_lo] = k32f_none;
     f[k32f_hi] = k32f_none;
-    auto desc = [&](const seg32 & sg, int table) {
-        return ((table + sg.base - (int) (sg.lo >> sg.shift)) << 5) | sg.shift;
-    };
-    for (int s = 0; s <= 26; s++) {
-        const uint32_t z = (uint32_t) s << 23;
-        const seg32 & sb = z >= t.sb_seg[1].lo ? t.sb_seg[1] : t.sb_seg[0];
-        int j = 0;
-        while (j < 3 && z >= t.db_seg[j + 1].lo) j++;
-        f[k32f_desc + s] = desc(sb, k32f_sb);
-        f[k32f_desc + k32f_desc_db + s] = desc(t.db_seg[j], k32f_db);   // s = 0 (unused) as s = 1
-        const seg32 * ms[2] = { &sb, &t.db_seg[j] };
-        for (int h = 0; h < 2; h++) {
-            const int e = s + (h ? k32f_dsc2_db : 0);
-            f[k32f_dsc2 + 2 * e]     = (h ? k32f_db : k32f_sb) + ms[h]->base - (int) (ms[h]->lo >> ms[h]->shift);
-            f[k32f_dsc2 + 2 * e + 1] = (int32_t) (1u << (32 - ms[h]->shift));
-            f[k32f_dms + e]          = -(int32_t) (1u << ms[h]->shift);
-        }
-    }
-    auto fits = [&](const seg32 & sg, int table) {
-        const int n = (int) ((sg.hi - sg.lo) >> sg.shift);
-        for (int i = 0; i < n; i++) {
-            const long long dv = (long long) f[table + sg.base + i + 1] - f[table + sg.base + i];
-            if ((dv < 0 ? -dv : dv) * (((long long) 1 << sg.shift) - 1) >= ((long long) 1 << 31)) return false;
+    auto fits = [&](const std::vector<int32_t> & v) {
+        for (size_t i = 0; i + 1 < v.size(); i++) {
+            const long long dv = (long long) v[i + 1] - v[i];
+            if ((dv < 0 ? -dv : dv) * ((1ll << k32_sh) - 1) + (1ll << (k32_sh - 1)) >= (1ll << 31)) return false;
         }
         return true;
     };
-    bool ok = true;
-    for (int s = 0; s <= 26; s++) {
-        const bool hi = s >= k32f_sb_split;
-        ok = ok && f[k32f_desc + s] == (((hi ? k32f_sb_base1 : k32f_sb) << 5) | (hi ? k32f_sb_sh1 : k32f_sb_sh0));
-    }
-    for (const auto & sg : t.sb_seg) ok = ok && fits(sg, k32f_sb);
-    for (const auto & sg : t.db_seg) ok = ok && fits(sg, k32f_db);
+    bool ok = fits(t.sb32) && fits(t.db32);
+    for (int n = 0; n < k32_db_knots; n++) ok = ok && (long long) k32_one + ((long long) n << k32_sh) + t.db32[n] >= 0;
     if (!ok) f.clear();
 }
 
 void build32(host_tables & t, bool need32, bool need_lpvip) {
-    t.sb_seg[0] = { 0u, 8u << 23, 13, 0 };
-    t.sb_seg[1] = { 8u << 23, 26u << 23, 16, 0 };
-    t.db_seg[0] = { 1u << 23, 2u << 23, 12, 0 };
-    t.db_seg[1] = { 2u << 23, 4u << 23, 13, 0 };
-    t.db_seg[2] = { 4u << 23, 8u << 23, 14, 0 };
-    t.db_seg[3] = { 8u << 23, 26u << 23, 16, 0 };
-    int tot = 0;
-    for (auto & sg : t.sb_seg) { sg.base = tot; tot += (int) ((sg.hi - sg.lo) >> sg.shift) + 1; }
-    t.sb32.resize(tot);
-    for (const auto & sg : t.sb_seg) {
-        const int n = (int) ((sg.hi - sg.lo) >> sg.shift);
-        for (int i = 0; i <= n; i++) t.sb32[sg.base + i] = knot_sb(sg.lo + ((uint32_t) i << sg.shift));
-    }
-    tot = 0;
-    for (auto & sg : t.db_seg) { sg.base = tot; tot += (int) ((sg.hi - sg.lo) >> sg.shift) + 1; }
-    t.db32.resize(tot);
-    for (const auto & sg : t.db_seg) {
-        const int n = (int) ((sg.hi - sg.lo) >> sg.shift);
-        for (int i = 0; i <= n; i++) t.db32[sg.base + i] = knot_db(sg.lo + ((uint32_t) i << sg.shift));
-    }
+    t.sb32.assign(k32_sb_knots + 1, 0);
+    for (int n = 0; n < k32_sb_knots; n++) t.sb32[n] = knot_sb((uint32_t) n << k32_sh);
+    t.db32.assign(k32_db_knots + 1, 0);
+    for (int n = 0; n < k32_db_knots; n++) t.db32[n] = knot_db(k32_one + ((uint32_t) n << k32_sh));
     t.db32_hi.assign(2048, 0);
     for (int j = 1; j < 2048; j++) t.db32_hi[j] = knot_db((uint32_t) j << 12);
     t.db32_lo.assign(4096, 0);

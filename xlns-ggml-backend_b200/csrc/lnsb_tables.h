@@ -58,46 +58,34 @@ constexpr int k16s_bytes = (2 * k16_key_max + 4 + 15) / 16 * 16;   // 41008
 constexpr int k16m_key_max   = 16 * k16_monte_n + 4;
 constexpr int k16m_key_bytes = (k16m_key_max + 4 + 15) / 16 * 16;   // 36880
 
-// xlns32 interpolation geometry (units: 2^-23 octave)
-struct seg32 { uint32_t lo, hi; int shift; int base; };
+// xlns32 interpolation geometry (units: 2^-23 octave): sb knots every 2^-9
+// octave on [0, 26], db knots every 2^-9 octave on [1, 26]; sb interpolates
+// rounded to nearest, db floored.
 constexpr uint32_t k32_one = 1u << 23;
 constexpr uint32_t k32_ess = 26u << 23;
+constexpr int      k32_sh  = 14;                    // knot spacing 2^14 units
+constexpr int      k32_sb_knots = (26 << 9) + 1;   // z = n << 14, n = 0..13312
+constexpr int      k32_db_knots = (25 << 9) + 1;   // z = (1 << 23) + (n << 14), n = 0..12800
 
 // Flat xlns32 addition image (int32 words): everything one xlns32 addition
 // reads, in one block that a kernel keeps in shared memory.
-//   [k32f_sb,   +10498)  sb knots: [0,8) step 2^13, [8,26] step 2^16
-//   [k32f_db,   +8452)   db knots: [1,2) step 2^12, [2,4) 2^13, [4,8) 2^14, [8,26] 2^16
-//   [k32f_lo,   +4096)   db(d) for d = 0..4095 (cotransformation, low part)
-//   [k32f_hi,   +2048)   db(j << 12) for j = 0..2047 (cotransformation, high part)
-//                        index 0 of both holds k32f_none, which makes the
-//                        cotransformation's special cases (d < 4096 or d a
-//                        multiple of 4096) fall out of the general formula
-//   [k32f_desc, +96)     interpolation descriptor per octave s = min(z, ess) >> 23:
-//                        sb at +s, db at +k32f_desc_db + s, (base << 5) | shift,
-//                        the left knot of z being word (z >> shift) + base
-//   [k32f_dsc2, +134)    the same descriptors in multiply form, entry e = s (sb) or
-//                        k32f_dsc2_db + s (db): int2 {base, 2^(32 - shift)}, so
-//                        z >> shift = umulhi(z, 2^(32 - shift)) and t >> shift =
-//                        mulhi(t, 2^(32 - shift))
-//   [k32f_dms,  +67)     -2^shift per entry e: z mod 2^shift = (z >> shift) * -2^shift + z
+//   [k32f_sb, +13314)  sb knots, then a 0 (the right knot of z = ess)
+//   [k32f_db, +12802)  db knots, then a 0; the knot of z sits at word
+//                      k32f_db0 + (z >> 14) for z >= 1 octave
+//   [k32f_lo, +4096)   db(d) for d = 0..4095 (cotransformation, low part)
+//   [k32f_hi, +2048)   db(j << 12) for j = 0..2047 (cotransformation, high part)
+//                      index 0 of both holds k32f_none, which makes the
+//                      cotransformation's special cases (d < 4096 or d a
+//                      multiple of 4096) fall out of the general formula
+// Every interpolation product (right - left) * f, plus the rounding half,
+// fits in 32 bits (checked when the image is built).
 constexpr int     k32f_sb      = 0;
-constexpr int     k32f_db      = 10498;
-constexpr int     k32f_lo      = 18950;
-constexpr int     k32f_hi      = 23046;
-constexpr int     k32f_desc    = 25094;
-constexpr int     k32f_desc_db = 48;
-constexpr int     k32f_dsc2    = 25190;         // 8-byte aligned
-constexpr int     k32f_dsc2_db = 40;            // db entries on other banks than sb's
-constexpr int     k32f_dms     = 25324;
-constexpr int     k32f_words   = 25392;         // multiple of 4 (16-byte copies)
-// the sb descriptors as constants (the non-negative chains compute them
-// instead of loading them): s < k32f_sb_split: (k32f_sb, k32f_sb_sh0), else
-// (k32f_sb_base1, k32f_sb_sh1); build_flat32 checks them against the image
-constexpr int     k32f_sb_split = 8;
-constexpr int     k32f_sb_sh0   = 13;
-constexpr int     k32f_sb_sh1   = 16;
-constexpr int     k32f_sb_base1 = 7169;        // 8193 knots of the first segment - (8 << 23 >> 16)
-constexpr int     k32f_sb_bytes16 = (k32f_db * 4 + 15) / 16 * 16;   // the sb knots, in 16-byte pieces
+constexpr int     k32f_db      = 13316;
+constexpr int     k32f_db0     = k32f_db - 512;
+constexpr int     k32f_lo      = 26120;
+constexpr int     k32f_hi      = 30216;
+constexpr int     k32f_words   = 32264;          // multiple of 4 (16-byte copies)
+constexpr int     k32f_sb_bytes16 = k32f_db * 4;  // the sb knots, in 16-byte pieces
 constexpr int32_t k32f_none    = -(1 << 30);
 
 struct host_tables {
@@ -112,8 +100,8 @@ struct host_tables {
     std::vector<int32_t>  mkey16;      // k16m_key_bytes / 4 entries, see k16m_key_max
     std::vector<int32_t>  key16s;      // k16s_bytes / 4 entries, see k16s_bytes
     // xlns32
-    seg32 sb_seg[2], db_seg[4];
-    std::vector<int32_t>  sb32, db32;  // concatenated knots
+    std::vector<int32_t>  sb32;        // k32_sb_knots + 1 (a trailing 0)
+    std::vector<int32_t>  db32;        // k32_db_knots + 1 (a trailing 0)
     std::vector<int32_t>  db32_hi;     // 2048
     std::vector<int32_t>  db32_lo;     // 4096
     std::vector<int32_t>  flat32;      // k32f_words, see k32f_sb
