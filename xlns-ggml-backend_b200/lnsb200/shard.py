@@ -68,3 +68,79 @@ def monte_seed_for_shard(seed, jump, M, N, K, rank, world, slices=1):
         raise ValueError("monte_seed_for_shard: a sharded Monte mul_mat must have a single slice (got %d)" % slices)
     m0, _ = row_range(M, world, rank)
     return jump(seed, m0 * N * max(K - 1, 0))
+
+
+# ---------------------------------------------------------------------------
+# Failure detection on the host.  A rank that never joins, or leaves between
+# steps, is noticed by the others on the host -- through the rendezvous store,
+# with a deadline -- before their next launch, so no kernel or collective is
+# left waiting on it.  (The device-side waits have their own bounds: the peer
+# barrier of the fused gather gives up after a fixed number of polls and
+# reports a status.)
+# ---------------------------------------------------------------------------
+
+class ShardError(RuntimeError):
+    """A rank did not join, or is gone; .ranks names the missing ones."""
+
+    def __init__(self, msg, ranks=()):
+        super().__init__(msg)
+        self.ranks = tuple(ranks)
+
+
+def init_group(backend, rank, world, port, addr="127.0.0.1", timeout_s=30.0):
+    """init_process_group over a TCPStore that rank 0 hosts, with a deadline:
+    if any rank does not join within timeout_s, every rank that did raises
+    ShardError (rank 0 after waiting for the workers, the others after failing
+    to reach rank 0's store).  Returns the store (for StepGuard).  The process
+    group's own timeout is timeout_s as well, so a collective that a vanished
+    peer never joins ends with an error instead of hanging."""
+    import datetime
+    import torch.distributed as dist
+    td = datetime.timedelta(seconds=timeout_s)
+    try:
+        store = dist.TCPStore(addr, port, world, rank == 0, timeout=td, wait_for_workers=True)
+        store.set("lnsb/joined/%d" % rank, "1")
+        store.wait(["lnsb/joined/%d" % r for r in range(world)], td)
+    except Exception as e:                                   # torch raises DistStoreError / RuntimeError
+        raise ShardError("rank %d: the group of %d did not assemble within %.1f s (%s)"
+                         % (rank, world, timeout_s, type(e).__name__)) from e
+    dist.init_process_group(backend, store=store, rank=rank, world_size=world, timeout=td)
+    return store
+
+
+class StepGuard:
+    """Per-step heartbeat through the store.  enter(step) is called before a
+    step's first launch: it records this rank's arrival and waits, at most
+    timeout_s, for every other rank's; a rank that announced leave() (or never
+    arrives) makes enter raise ShardError naming it, on every rank still
+    present, before any of them launches the step's kernels or collectives."""
+
+    def __init__(self, store, rank, world, timeout_s=10.0, poll_s=0.01):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.poll_s = timeout_s, poll_s
+
+    def _key(self, step, r):
+        return "lnsb/step/%d/%d" % (step, r)
+
+    def _left(self):
+        return [r for r in range(self.world) if r != self.rank and self.store.check(["lnsb/left/%d" % r])]
+
+    def enter(self, step):
+        import time
+        self.store.set(self._key(step, self.rank), "1")
+        deadline = time.monotonic() + self.timeout_s
+        while True:
+            left = self._left()
+            if left:
+                raise ShardError("step %d: rank(s) %s left the group" % (step, left), left)
+            missing = [r for r in range(self.world) if not self.store.check([self._key(step, r)])]
+            if not missing:
+                return
+            if time.monotonic() >= deadline:
+                raise ShardError("step %d: rank(s) %s did not arrive within %.1f s" % (step, missing, self.timeout_s),
+                                 missing)
+            time.sleep(self.poll_s)
+
+    def leave(self):
+        """This rank leaves between steps (none of its work in flight)."""
+        self.store.set("lnsb/left/%d" % self.rank, "1")
