@@ -134,7 +134,10 @@ int lnsb_dequantize(int type, const void * src, float * dst, int64_t rows, int64
  * every use, as in the reference.  src may be host or device memory (host
  * rows are staged to the device in bounded chunks).  budget_bytes < 0 takes
  * the reference's rule: GGML_LNS_CUDA_CACHE_MB if set, else the device's free
- * memory less a 1 GiB reserve at creation. ---- */
+ * memory less a 1 GiB reserve at creation.  A device allocation that fails
+ * (out of memory) is not an error: the image goes to scratch as over budget.
+ * LNSB_WEIGHT_CACHE_FAIL_ALLOCS=n, read at creation, makes the cache's next n
+ * allocations fail that way (host-side fault injection for tests). ---- */
 typedef struct lnsb_weight_cache lnsb_weight_cache;
 lnsb_weight_cache * lnsb_weight_cache_create(int fmt, int64_t budget_bytes);
 void lnsb_weight_cache_destroy(lnsb_weight_cache * cache);

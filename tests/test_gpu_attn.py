@@ -51,7 +51,7 @@ def test_attn_decode_too_long_and_invalid():
     z16 = torch.zeros(64, dtype=torch.int16, device="cuda")
     zf = torch.zeros(64, dtype=torch.float32, device="cuda")
     mk = ks.attn_decode_max_keys(64)
-    assert 4000 < mk < 8000
+    assert 2000 < mk < 8000
     with pytest.raises(lnsb200.LnsbError):
         ks.attn_decode(zf, z16, z16, 64, mk + 1, 1, 1, 64, 0.125, zf)     # too many keys for shared memory
     with pytest.raises(lnsb200.LnsbError):

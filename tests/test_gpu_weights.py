@@ -185,3 +185,39 @@ def test_typed_errors(kss):
     with pytest.raises(lnsb200.LnsbError):
         ks.to_lns_transposed_typed("q4_k", z, d, 4, 128, 4)  # half a Q4_K block
     assert ks.type_row_bytes("q6_k", 512) == 420 and ks.type_row_bytes("q4_k", 100) == 0
+
+
+def test_weight_cache_allocation_failure(orc, kss, monkeypatch):
+    """An out-of-memory allocation in the cache (injected on the host,
+    LNSB_WEIGHT_CACHE_FAIL_ALLOCS) leaves no sticky error: the image goes to
+    scratch, or the call reports LNSB_E_TOO_LARGE without scratch, nothing is
+    cached, and the next allocation and a mul_mat afterwards succeed."""
+    import lnsb200
+    ks = kss[16]
+    rng = np.random.default_rng(5)
+    rows, cols = 64, 256
+    raw = random_rows(orc, "q4_k", rows, cols, rng)
+    want = orc.to_f32_16(orc.from_f32_16(orc.dequant("q4_k", raw, rows, cols)).T.reshape(-1))
+    dsrc = torch.from_numpy(raw).cuda()
+    monkeypatch.setenv("LNSB_WEIGHT_CACHE_FAIL_ALLOCS", "2")
+    c = lnsb200.WeightCache(ks, budget=1 << 30)
+    scratch = torch.empty(rows * cols, dtype=torch.int16, device="cuda")
+    assert c.get(dsrc, "q4_k", rows, cols, scratch=scratch) == scratch.data_ptr()     # failure 1: to scratch
+    assert c.stats()["entries"] == 0
+    assert np.array_equal(image_f32(ks, scratch.data_ptr(), rows * cols).view(np.uint32), want.view(np.uint32))
+    with pytest.raises(lnsb200.LnsbError):                                              # failure 2: no scratch
+        c.get(dsrc, "q4_k", rows, cols)
+    a = c.get(dsrc, "q4_k", rows, cols)                                                 # allocations work again
+    assert c.stats()["entries"] == 1 and a != scratch.data_ptr()
+    assert np.array_equal(image_f32(ks, a, rows * cols).view(np.uint32), want.view(np.uint32))
+    c.close()
+    # the context is clean: an ordinary mul_mat runs bit-exact afterwards
+    K, M, N = 64, 16, 3
+    w = orc.from_f32_16(rng.normal(0, 0.1, (M, K)).astype(np.float32))
+    x = orc.from_f32_16(rng.normal(0, 1, (N, K)).astype(np.float32))
+    wd = torch.from_numpy(np.ascontiguousarray(w.T).view(np.int16)).cuda()
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    out = torch.empty(N * M, dtype=torch.int16, device="cuda")
+    ks.mul_mat_lns(wd, xd, out, K, M, N)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint16).reshape(N, M), orc.mul_mat16(ks.mode, w, x, seed=7))

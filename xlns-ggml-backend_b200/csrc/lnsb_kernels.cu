@@ -3076,6 +3076,7 @@ struct lnsb_weight_cache {
     };
     int                    fmt = 0, dev = 0;
     int64_t                budget = 0, used = 0;
+    int64_t                fail_allocs = 0;      // host-side fault injection: allocations to refuse
     std::map<key, void *>  entries;
     void *                 staging = nullptr;
     size_t                 staging_bytes = 0;
@@ -3808,6 +3809,10 @@ lnsb_weight_cache * lnsb_weight_cache_create(int fmt, int64_t budget_bytes) {
     c->fmt = fmt;
     c->dev = dev;
     c->budget = budget_bytes;
+    // LNSB_WEIGHT_CACHE_FAIL_ALLOCS=n: the cache's next n device allocations
+    // report out-of-memory (failure handling is tested without exhausting
+    // the device)
+    if (const char * env = std::getenv("LNSB_WEIGHT_CACHE_FAIL_ALLOCS")) c->fail_allocs = std::atoll(env);
     return c;
 }
 
@@ -3841,9 +3846,13 @@ int lnsb_weight_cache_get(lnsb_weight_cache * c, const void * src, int type, int
     }
     const int64_t bytes = rows * cols * (int64_t) lnsb_value_size(c->fmt);
     void * dst = nullptr;
-    if (c->used + bytes <= c->budget && cudaMalloc(&dst, (size_t) bytes) != cudaSuccess) {
-        cudaGetLastError();                                          // out of memory: not sticky, fall back
-        dst = nullptr;
+    if (c->used + bytes <= c->budget) {
+        if (c->fail_allocs > 0) {
+            c->fail_allocs--;                                        // injected out-of-memory
+        } else if (cudaMalloc(&dst, (size_t) bytes) != cudaSuccess) {
+            cudaGetLastError();                                      // out of memory: not sticky, fall back
+            dst = nullptr;
+        }
     }
     const bool cached = dst != nullptr;
     if (!cached) {
