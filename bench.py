@@ -68,6 +68,10 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-decode", action="store_true", help="skip the model decode measurements")
     p.add_argument("--no-sides", action="store_true", help="the headline only (no side objects)")
+    p.add_argument("--sides", default="all",
+                   help="comma-separated side objects to run (configs, configs4, mul_mat_id, weights, normalisers; "
+                        "default all) -- for profiling one of them")
+    p.add_argument("--c4-points", default="1,16,128", help="configs[4] token counts N to time (default 1,16,128)")
     p.add_argument("--decode-mode", default="sum32", help="sum mode of the decode (BASELINE configs[2]: sum32)")
     return p.parse_args()
 
@@ -453,20 +457,28 @@ def run_ours(args, wl):
         "clocks": clocks,
     }
     if not args.no_sides:
+        sides = set(args.sides.split(",")) if args.sides != "all" else \
+            {"configs", "configs4", "mul_mat_id", "weights", "normalisers"}
         other = "configs1" if args.workload == "configs0" else "configs0"
-        line[other] = time_side_mul_mat(ctx, lnsb200, torch, np, WORKLOADS[other], args, int_peak, f_mhz)
-        line["configs4"] = time_configs4(ctx, lnsb200, torch, np, args, f_mhz)
+        if "configs" in sides:
+            line[other] = time_side_mul_mat(ctx, lnsb200, torch, np, WORKLOADS[other], args, int_peak, f_mhz)
+        if "configs4" in sides:
+            line["configs4"] = time_configs4(ctx, lnsb200, torch, np, args, f_mhz)
         if world == 1:
-            line["mul_mat_id"] = time_mul_mat_id(ctx, lnsb200, torch, np, args, int_peak)
-            line["weights"] = time_weights(ctx, lnsb200, torch, np, args, hbm)
-            line["normalisers"] = time_norms(ctx, lnsb200, torch, np, args, f_mhz)
+            if "mul_mat_id" in sides:
+                line["mul_mat_id"] = time_mul_mat_id(ctx, lnsb200, torch, np, args, int_peak)
+            if "weights" in sides:
+                line["weights"] = time_weights(ctx, lnsb200, torch, np, args, hbm)
+            if "normalisers" in sides:
+                line["normalisers"] = time_norms(ctx, lnsb200, torch, np, args, f_mhz)
     if not args.no_decode:
         # the metric's second half: model decode tok/s, one sequence per GPU
-        line["decode"] = run_decode(torch, dist, rank, world, args, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
+        line["decode"] = run_decode(torch, dist, rank, world, args, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline),
+                                    f_mhz=f_mhz)
         if world == 1:
             # the same model and prompt in LNS32, on 1 GPU
             line["decode_lns32"] = run_decode(torch, dist, rank, world, args,
-                                              cpu=(rank == 0 and not args.no_cpu_baseline), fmt=32)
+                                              cpu=(rank == 0 and not args.no_cpu_baseline), fmt=32, f_mhz=f_mhz)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_leg(wl, args.mode, 10.0, os.cpu_count() or 1)
         # the reference's CPU backend runs one thread (its ops are sequential loops): the
@@ -643,7 +655,7 @@ def time_configs4(ctx, lnsb200, torch, np, args, f_mhz):
         ks.to_lns_transposed(wf, w[b * blk:], blk, K, Mr)
     del wf
     res = {}
-    for N in (1, 16, 128):
+    for N in (int(n) for n in args.c4_points.split(",")):
         xf = torch.from_numpy(np.random.default_rng(3).normal(0, 1, (N, K)).astype(np.float32)).cuda()
         x = torch.empty(N * K, dtype=torch.int16, device="cuda")
         ks.to_lns(xf, x)
@@ -795,7 +807,7 @@ def time_weights(ctx, lnsb200, torch, np, args, hbm):
             "l2": "flushed (256 MB write) before every timed launch", "launches_per_type": 10}
 
 
-def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16):
+def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16, f_mhz=1965.0):
     """BASELINE configs[2] (fmt 16) and configs[3] (fmt 32): SmolLM2-135M-shaped
     random-init Llama, LNS16 in the decode sum mode or LNS32, 128-token prompt
     prefill then 128-token greedy decode, one independent sequence per GPU
@@ -834,6 +846,25 @@ def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16):
            "ms_per_token": dec_ms / 127, "prefill_ms": pre_ms,
            "timing": "device events; prefill eager, decode as one CUDA graph per position (captured before the timed region); each step's greedy token is copied to pinned host memory",
            "first_tokens": toks[:8]}
+    # the chain bound of one decode step: its dependent additions, the general
+    # xlns32 addition (mat-vecs, q.K and p.V chains) and the non-negative one
+    # (rms_norm and softmax normalisers), at their measured latencies (sum32 and
+    # xlns32 run both on the flat xlns32 adder)
+    import lnsb200
+    if fmt == 32 or args.decode_mode == "sum32":
+        ks = lnsb200.KernelSet(fmt, args.decode_mode if fmt == 16 else "base")
+        ks.upload_tables()
+        l3, l2 = ks.add_latency(3, 32), ks.add_latency(2, 32)
+        L, d, ffn, hd = cfg["n_layer"], cfg["n_embd"], cfg["n_ff"], cfg["head_dim"]
+        nkv = (129 + 255) / 2                             # keys per step, averaged over the 127 steps
+        s3 = L * (d + hd + nkv + d + d + ffn) + d          # qkv, q.K, p.V, wo, up/gate, down; output
+        s2 = L * (d + d + nkv - 1) + d                     # two norm blocks and the softmax per layer; final norm
+        f = f_mhz * 1e6
+        t_chain = (s3 * l3 + s2 * l2) / f * 1e3
+        out["chain"] = {"general_steps": s3, "nonneg_steps": s2, "l_add_general_cycles": l3, "l_add_nonneg_cycles": l2,
+                        "sm_mhz_used": f / 1e6, "t_chain_ms_per_token": t_chain, "frac": t_chain / (dec_ms / 127),
+                        "bound": "one token's dependent additions (mat-vec, attention and normaliser chains) at "
+                                 "the measured latency of each adder"}
     if cpu:
         # the CPU oracle (the reference's algorithm, host cores) on a bounded sample:
         # prefill of 8 tokens, then 16 decode steps (a few seconds)

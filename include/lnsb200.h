@@ -202,7 +202,9 @@ int lnsb_group_barrier(int32_t * const * flags, int world, int rank, int32_t epo
  * table in shared memory as the kernels hold it.  kind 0: the key-form xlns16
  * addition of the latency mul_mat kernels; 1: the non-negative xlns16
  * addition of the normalisers (base); 2: the non-negative xlns32 addition of
- * the normalisers (sum32, xlns32).  out: device memory, two int64 -- out[0] =
+ * the normalisers (sum32, xlns32); 3: the general xlns32 addition of the
+ * latency-bound mat-vecs (sum32, xlns32; both signs, the cotransformed db
+ * beside the main result).  out: device memory, two int64 -- out[0] =
  * SM cycles over steps - 1 additions, out[1] = the final accumulator. */
 int lnsb_add_latency(int kind, int lanes, int steps, int64_t * out, lnsb_stream_t stream);
 

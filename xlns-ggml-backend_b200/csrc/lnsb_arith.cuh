@@ -111,25 +111,24 @@ __device__ __forceinline__ uint32_t div32(uint32_t a, uint32_t b) {
     return ((a ^ b) & 0x80000000u) | (uint32_t) p;
 }
 
-// sb(z) and db(z) between knots every 2^-9 octave (k32_sh): sb rounded to
-// nearest, db floored (z: sb [0, ess], db [1, ess]; z = ess reads the last
-// knot, 0, with fraction 0)
-__host__ __device__ __forceinline__ int32_t lerp32(int32_t v0, int32_t v1, uint32_t z, int32_t half) {
+// sb(z) and db(z) between knots every 2^-9 octave (k32_sh), floored (z: sb
+// [0, ess], db [1, ess]; z = ess reads the last knot, 0, with fraction 0)
+__host__ __device__ __forceinline__ int32_t lerp32(int32_t v0, int32_t v1, uint32_t z) {
     const int32_t f = (int32_t) (z & ((1u << k32_sh) - 1u));
-    return v0 + (((v1 - v0) * f + half) >> k32_sh);
+    return v0 + (((v1 - v0) * f) >> k32_sh);
 }
 
 __device__ __forceinline__ int32_t sb32(const dev_tables & T, uint32_t d) {
     if (d >= k32_ess) return 0;
     const int32_t i = (int32_t) (d >> k32_sh);
-    return lerp32(__ldg(T.sb32 + i), __ldg(T.sb32 + i + 1), d, 1 << (k32_sh - 1));
+    return lerp32(__ldg(T.sb32 + i), __ldg(T.sb32 + i + 1), d);
 }
 
 __device__ __forceinline__ int32_t db32(const dev_tables & T, uint32_t d) {   // d > 0
     if (d >= k32_ess) return 0;
     if (d >= k32_one) {
         const int32_t i = (int32_t) ((d - k32_one) >> k32_sh);
-        return lerp32(__ldg(T.db32 + i), __ldg(T.db32 + i + 1), d, 0);
+        return lerp32(__ldg(T.db32 + i), __ldg(T.db32 + i + 1), d);
     }
     // cotransformation: 1 - 2^z = (1 - 2^z2) + 2^z2 (1 - 2^z1)
     const uint32_t d1 = d >> 12, d2 = d & 4095u;
@@ -180,7 +179,7 @@ __host__ __device__ __forceinline__ uint32_t add32f(const int32_t * F, uint32_t 
     z = z < k32_ess ? z : k32_ess;
     const bool     isdb = usedb && !cot;
     const int32_t  i    = (int32_t) (z >> k32_sh) + (isdb ? k32f_db0 : k32f_sb);
-    const int32_t  adj  = lerp32(F[i], F[i + 1], z, isdb ? 0 : 1 << (k32_sh - 1)) + (cot ? hi : 0);
+    const int32_t  adj  = lerp32(F[i], F[i + 1], z) + (cot ? hi : 0);
     const uint32_t u = (mx & 0x7FFFFFFFu) + (uint32_t) adj;      // adj > -2^28: wrap means negative
     uint32_t p = u < 0x7FFFFFFFu ? u : 0x7FFFFFFFu;
     if (u >= 0xC0000000u) p = 0;
@@ -191,7 +190,7 @@ __host__ __device__ __forceinline__ uint32_t add32f(const int32_t * F, uint32_t 
 // sb(z) (db = false) or db(z) (db = true, z >= 1) over the flat image
 __device__ __forceinline__ int32_t interp32f(const int32_t * F, uint32_t z, bool db) {
     const int32_t i = (int32_t) (z >> k32_sh) + (db ? k32f_db0 : k32f_sb);
-    return lerp32(F[i], F[i + 1], z, db ? 0 : 1 << (k32_sh - 1));
+    return lerp32(F[i], F[i + 1], z);
 }
 
 // the cotransformed db of add32f_lean's rare branch: opposite signs, d < 1

@@ -1991,19 +1991,31 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
     }
     const int64_t P = nn_pitch(ncols, nn_term_bytes<FMT>());   // row pitch of the squares
     if (NN) {
-        for (int64_t e = threadIdx.x; e < nr * ncols; e += blockDim.x) {
-            uint32_t v;
-            if (FUSE && x_out != nullptr) {              // x once: the scaling pass reads it back
-                const float xf = xval(row0 * ncols + e);
-                x_out[row0 * ncols + e] = xf;
-                v = f2c(xf);
-            } else {
-                v = load(row0 * ncols + e);
-            }
+        auto square = [&](int64_t e, uint32_t v) {
             const int r = (int) e / (int) ncols;         // nr * ncols fits the block's shared memory
             const int64_t o = r * P + ((int) e - r * (int) ncols);
             if constexpr (FMT == 16) sq[o] = (uint16_t) mul16(v, v);
             else                     sq32[o] = mul32(v, v);
+        };
+        const int64_t tot = nr * ncols;
+        if (FUSE && x_out != nullptr) {
+            for (int64_t e = threadIdx.x; e < tot; e += blockDim.x) {
+                const float xf = xval(row0 * ncols + e);     // x once: the scaling pass reads it back
+                x_out[row0 * ncols + e] = xf;
+                square(e, f2c(xf));
+            }
+        } else {
+            constexpr int U = 8;                         // loads in flight per thread
+            const int64_t step = (int64_t) blockDim.x * U;
+            int64_t e0 = 0;
+            for (; e0 + step <= tot; e0 += step) {
+                uint32_t v[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) v[u] = load(row0 * ncols + e0 + u * blockDim.x + threadIdx.x);
+#pragma unroll
+                for (int u = 0; u < U; u++) square(e0 + u * blockDim.x + threadIdx.x, v[u]);
+            }
+            for (int64_t e = e0 + threadIdx.x; e < tot; e += blockDim.x) square(e, load(row0 * ncols + e));
         }
     }
     cp_async_commit();
@@ -2082,9 +2094,12 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
 
 // ============================ SOFT_MAX =====================================
 // Block = up to 32 rows, SM_THREADS threads.  Pass 1 (whole block): scale, mask, row max;
-// pass 2 (whole block): c = exp(v - max) into the work buffer; pass 3 (one
-// lane per row): the normaliser chain over c in element order; pass 4 (whole
-// block): dst = c / total.
+// pass 2 (whole block): c = exp(v - max); pass 3 (one lane per row): the
+// normaliser chain over c in element order; pass 4 (whole block): dst = c /
+// total.  When the block's rows fit in shared memory (ST, every mode) pass 1
+// loads each logit once, eight loads in flight per lane, and keeps the scaled,
+// masked value there; pass 2 rewrites it in place with c, and passes 3 and 4
+// read c there.  Otherwise c goes through the work buffer in global memory.
 constexpr int SM_THREADS = 512;
 template <int FMT, bool IO_F32>
 __global__ void __launch_bounds__(SM_THREADS)
@@ -2092,15 +2107,16 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
            lnsb_shape4 ms, uint32_t scale_l, void * __restrict__ dst, void * __restrict__ work,
            uint32_t monte_seed, int rpb, int nn_ok) {
     pdl_entry();
-    extern __shared__ __align__(16) int32_t dyn[];          // NNCHAIN: [sb knots (sum32)][exp terms: rpb x n]
+    extern __shared__ __align__(16) int32_t dyn[];          // [sb knots (xlns32, sum32)][terms: rpb x pitch]
     __shared__ __align__(16) int16_t tab[k16_tab_bytes16 / 2];
     __shared__ __align__(16) int16_t fine[k_mode == M_MONTE ? 2 * k16_monte_n : 8];
     __shared__ uint32_t s_max[32][4];
     __shared__ uint32_t s_tot[32];
     constexpr uint32_t NEG_INF = FMT == 16 ? 0xFFFFu : 0xFFFFFFFFu;
-    const bool NN = (FMT == 32 || NNCHAIN) && nn_ok != 0;
+    const bool ST = nn_ok != 0;                             // the rows' terms stay in shared memory
+    const bool NN = (FMT == 32 || NNCHAIN) && ST;
     if constexpr (FMT == 16) norm_tables(T, tab, fine);
-    if (NN) nn_tables<FMT>(T, dyn);
+    if (ST) nn_tables<FMT>(T, dyn);
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
@@ -2142,13 +2158,42 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         return v;
     };
 
-    // pass 1: row max (each warp takes rows warp, warp + nw, ...)
+    uint16_t * cs   = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
+    uint32_t * cs32 = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
+    const int64_t P = nn_pitch(n, nn_term_bytes<FMT>());       // row pitch of the shared terms
+    auto put = [&](int r, int64_t i, uint32_t v) {
+        if constexpr (FMT == 16) cs[r * P + i] = (uint16_t) v;
+        else                     cs32[r * P + i] = v;
+    };
+    auto get = [&](int r, int64_t i) -> uint32_t { return FMT == 16 ? (uint32_t) cs[r * P + i] : cs32[r * P + i]; };
+    constexpr int U = 8;                                     // loads in flight per lane
+
+    // pass 1: row max (each warp takes rows warp, warp + nw, ...); ST: the values into shared memory
     for (int r = warp; r < nr; r += nw) {
         const int64_t row = row0 + r, mrow = mask != nullptr ? mask_row(row) : 0;
         uint32_t mx = NEG_INF;
-        for (int64_t i = lane; i < n; i += 32) {
-            const uint32_t v = value(row, mrow, i);
-            if (FMT == 16 ? gt16(v, mx) : gt32(v, mx)) mx = v;
+        if (ST) {
+            int64_t i0 = 0;
+            for (; i0 + 32 * U <= n; i0 += 32 * U) {
+                uint32_t v[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) v[u] = value(row, mrow, i0 + u * 32 + lane);
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    put(r, i0 + u * 32 + lane, v[u]);
+                    if (FMT == 16 ? gt16(v[u], mx) : gt32(v[u], mx)) mx = v[u];
+                }
+            }
+            for (int64_t i = i0 + lane; i < n; i += 32) {
+                const uint32_t v = value(row, mrow, i);
+                put(r, i, v);
+                if (FMT == 16 ? gt16(v, mx) : gt32(v, mx)) mx = v;
+            }
+        } else {
+            for (int64_t i = lane; i < n; i += 32) {
+                const uint32_t v = value(row, mrow, i);
+                if (FMT == 16 ? gt16(v, mx) : gt32(v, mx)) mx = v;
+            }
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) {
@@ -2158,52 +2203,60 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         if (lane == 0) s_max[r][0] = mx;
     }
     __syncthreads();
-    // pass 2: c = exp(v - max) into work (and, for the non-negative chain, shared memory)
-    uint16_t * cs   = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
-    uint32_t * cs32 = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
-    const int64_t P = nn_pitch(n, nn_term_bytes<FMT>());       // row pitch of the shared terms
+    // pass 2: c = exp(v - max), in place (ST) or into work
+    auto expo = [&](uint32_t v, uint32_t mx) -> uint32_t {
+        if constexpr (FMT == 16) return __ldg(T.exp16 + sub16(v, mx, tab));
+        else                     return exp32(T, sub32(T, v, mx));
+    };
     for (int r = warp; r < nr; r += nw) {
-        const int64_t row = row0 + r, mrow = mask != nullptr ? mask_row(row) : 0;
+        const int64_t row = row0 + r;
         const uint32_t mx = s_max[r][0];
-        for (int64_t i = lane; i < n; i += 32) {
-            const uint32_t v = value(row, mrow, i);
-            if constexpr (FMT == 16) {
-                const uint16_t e = __ldg(T.exp16 + sub16(v, mx, tab));
-                static_cast<uint16_t *>(work)[row * n + i] = e;
-                if (NN) cs[r * P + i] = e;
-            } else {
-                const uint32_t e = exp32(T, sub32(T, v, mx));
-                static_cast<uint32_t *>(work)[row * n + i] = e;
-                if (NN) cs32[r * P + i] = e;
+        if (ST) {
+            int64_t i0 = 0;
+            for (; i0 + 32 * U <= n; i0 += 32 * U) {
+                uint32_t e[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) e[u] = expo(get(r, i0 + u * 32 + lane), mx);
+#pragma unroll
+                for (int u = 0; u < U; u++) put(r, i0 + u * 32 + lane, e[u]);
+            }
+            for (int64_t i = i0 + lane; i < n; i += 32) put(r, i, expo(get(r, i), mx));
+        } else {
+            const int64_t mrow = mask != nullptr ? mask_row(row) : 0;
+            for (int64_t i = lane; i < n; i += 32) {
+                const uint32_t e = expo(value(row, mrow, i), mx);
+                if constexpr (FMT == 16) static_cast<uint16_t *>(work)[row * n + i] = (uint16_t) e;
+                else                     static_cast<uint32_t *>(work)[row * n + i] = e;
             }
         }
     }
     __syncthreads();
     // pass 3: the normaliser, one sequential chain per row (xlns16_sum order)
     if (threadIdx.x < nr) {
-        const int64_t row = row0 + threadIdx.x;
-        const void * c = work;
+        const int r = threadIdx.x;
+        const int64_t row = row0 + r;
         if (NN && FMT == 32) {
-            const uint32_t * q = cs32 + threadIdx.x * P;
+            const uint32_t * q = cs32 + r * P;
             uint32_t acc = q[0];
             for (int64_t i = 1; i < n; i++) acc = padd32f(dyn, acc, q[i]);
-            s_tot[threadIdx.x] = acc;
+            s_tot[r] = acc;
         } else if (NN) {
-            const uint16_t * q = cs + threadIdx.x * P;
+            const uint16_t * q = cs + r * P;
             red16 R{ &T, tab, fine };
             uint32_t acc = R.from(q[0]);
             for (int64_t i = 1; i < n; i++) acc = nn_add(dyn, tab, acc, q[i]);
-            s_tot[threadIdx.x] = R.finish(acc);
+            s_tot[r] = R.finish(acc);
         } else if constexpr (FMT == 16) {
             red16 R{ &T, tab, fine };
             uint32_t st = k_stochastic ? lfsr_jump(T, monte_seed, (unsigned long long) row * (unsigned long long) (n - 1)) : 0u;
-            uint32_t acc = R.from(ld(c, row * n));
-            for (int64_t i = 1; i < n; i++) acc = R.add(acc, ld(c, row * n + i), st);
-            s_tot[threadIdx.x] = R.finish(acc);
+            auto term = [&](int64_t i) -> uint32_t { return ST ? get(r, i) : ld(work, row * n + i); };
+            uint32_t acc = R.from(term(0));
+            for (int64_t i = 1; i < n; i++) acc = R.add(acc, term(i), st);
+            s_tot[r] = R.finish(acc);
         } else {
-            uint32_t acc = ld(c, row * n);
-            for (int64_t i = 1; i < n; i++) acc = add32(T, acc, ld(c, row * n + i));
-            s_tot[threadIdx.x] = acc;
+            uint32_t acc = ld(work, row * n);
+            for (int64_t i = 1; i < n; i++) acc = add32(T, acc, ld(work, row * n + i));
+            s_tot[r] = acc;
         }
     }
     __syncthreads();
@@ -2212,7 +2265,7 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         const int64_t row = row0 + r;
         const uint32_t tot = s_tot[r];
         for (int64_t i = lane; i < n; i += 32) {
-            const uint32_t cv = ld(work, row * n + i);
+            const uint32_t cv = ST ? get(r, i) : ld(work, row * n + i);
             if constexpr (FMT == 16) {
                 const uint32_t y = div16(cv, tot);
                 if constexpr (IO_F32) static_cast<float *>(dst)[row * n + i] = to_f32_16(T, y);
@@ -2998,7 +3051,7 @@ int soft_max_impl(int fmt, const void * src, lnsb_shape4 s, const void * mask, l
     const int ds = current_device(&dev);
     if (ds != 0) return ds;
     int rpb = (int) imin64(32, (nrows + 2 * sm_count(dev) - 1) / (2 * sm_count(dev))), nn_ok = 0, dsmem = 0;
-    if (fmt == LNSB_XLNS32 || NNCHAIN) {
+    {   // the rows' terms in shared memory when they fit (every mode); the table the chain reads before them
         const int tabb = fmt == LNSB_XLNS32 ? nn_tab<32>() : nn_tab<16>();
         const int tb   = fmt == LNSB_XLNS32 ? 4 : 2;
         const int64_t fit = (NN_SMEM_MAX - tabb) / (nn_pitch(s.ne[0], tb) * tb);
@@ -3090,18 +3143,21 @@ struct lnsb_weight_cache {
 // in shared memory as the kernels hold it; lanes past `lanes` repeat the
 // first `lanes` (same addresses).  kind 0: the key-form general xlns16
 // addition of the latency mul_mat kernels; 1: the non-negative xlns16
-// addition (padd16); 2: the non-negative xlns32 addition (padd32f).  out[0]:
+// addition (padd16); 2: the non-negative xlns32 addition (padd32f); 3: the
+// general xlns32 addition of the latency mat-vecs (add32f_sel).  out[0]:
 // SM cycles over the timed steps, out[1]: the final accumulator (keeps the
 // chain live).
 constexpr int AL_OPS = 256;                                      // operands per lane, cycled
+constexpr int AL_TAB = k32f_words * 4 > k16s_bytes ? k32f_words * 4 : k16s_bytes;   // the largest table staged
 __global__ void __launch_bounds__(32) k_add_latency(dev_tables T, int kind, int lanes, int steps, int64_t * out) {
     extern __shared__ __align__(16) unsigned char smem[];
-    constexpr int TAB = (k16s_bytes > k32f_sb_bytes16 ? k16s_bytes : k32f_sb_bytes16);
+    constexpr int TAB = AL_TAB;
     const int lane = threadIdx.x, me = lane % lanes;
     int32_t * ops = reinterpret_cast<int32_t *>(smem + TAB);     // [AL_OPS][32]
     if (kind == 0) stage_async(smem, T.key16s, k16s_bytes);
     else if (kind == 1) stage_async(smem, T.sbdb16, k16_tab_bytes16);
-    else stage_async(smem, T.flat32, k32f_sb_bytes16);
+    else if (kind == 2) stage_async(smem, T.flat32, k32f_sb_bytes16);
+    else stage_async(smem, T.flat32, k32f_words * 4);
     cp_async_commit();
     for (int i = 0; i < AL_OPS; i++) {
         uint32_t h = (uint32_t) (me * 7919 + i) * 2654435761u;
@@ -3109,7 +3165,7 @@ __global__ void __launch_bounds__(32) k_add_latency(dev_tables T, int kind, int 
         h *= 2246822519u;
         h ^= h >> 13;
         const int lg = 0x4000 - 768 + (int) (h % 512u) - 256;    // -6 +- 2 octaves
-        const uint32_t code = (uint32_t) lg | (kind == 0 ? ((h >> 20) & 1u) << 15 : 0u);
+        const uint32_t code = (uint32_t) lg | (kind == 0 || kind == 3 ? ((h >> 20) & 1u) << 15 : 0u);
         ops[i * 32 + lane] = kind == 0 ? key_of_product(key_of_code_w(code), key_of_code_x(0x4000u))
                            : kind == 1 ? (int32_t) code : (int32_t) (code << 16);
     }
@@ -3128,8 +3184,10 @@ __global__ void __launch_bounds__(32) k_add_latency(dev_tables T, int kind, int 
         a = (uint32_t) ak;
     } else if (kind == 1) {
         for (int k = 1; k < steps; k++) a = padd16(a, (uint32_t) ops[(k & (AL_OPS - 1)) * 32 + lane], reinterpret_cast<const int16_t *>(smem));
-    } else {
+    } else if (kind == 2) {
         for (int k = 1; k < steps; k++) a = padd32f(reinterpret_cast<const int32_t *>(smem), a, (uint32_t) ops[(k & (AL_OPS - 1)) * 32 + lane]);
+    } else {
+        for (int k = 1; k < steps; k++) a = add32f_sel(reinterpret_cast<const int32_t *>(smem), a, (uint32_t) ops[(k & (AL_OPS - 1)) * 32 + lane]);
     }
     const long long t1 = clock64();
     if (lane == 0) { out[0] = t1 - t0; out[1] = (int64_t) a; }
@@ -3423,12 +3481,11 @@ int lnsb_copy_strided(int elem_size, const void * src, const int64_t ne[4], cons
 }
 
 int lnsb_add_latency(int kind, int lanes, int steps, int64_t * out, lnsb_stream_t stream) {
-    if (kind < 0 || kind > 2 || lanes < 1 || lanes > 32 || steps < 2 || out == nullptr) return LNSB_E_INVALID;
+    if (kind < 0 || kind > 3 || lanes < 1 || lanes > 32 || steps < 2 || out == nullptr) return LNSB_E_INVALID;
     const dev_tables * T = nullptr;
-    const int st = tables_for(kind == 2 ? LNSB_XLNS32 : LNSB_XLNS16, &T);
+    const int st = tables_for(kind >= 2 ? LNSB_XLNS32 : LNSB_XLNS16, &T);
     if (st != 0) return st;
-    constexpr int TAB = (k16s_bytes > k32f_sb_bytes16 ? k16s_bytes : k32f_sb_bytes16);
-    constexpr int smem = TAB + AL_OPS * 32 * 4;
+    constexpr int smem = AL_TAB + AL_OPS * 32 * 4;
     static bool attr[k_max_devices] = {};
     int dev = 0;
     const int ds = current_device(&dev);

@@ -188,8 +188,8 @@ int32_t knot_sb(uint32_t d) { return knot(log1pl(exp2l(-(long double) d / (long 
 int32_t knot_db(uint32_t d) { return knot(log1pl(-exp2l(-(long double) d / (long double) k32_one)) / k_ln2); }
 
 // The flat image of k32f_sb.  Checks that every interpolation product
-// (right - left) * f plus the rounding half fits in 32 bits, so the kernels'
-// 32-bit multiply equals the 64-bit definition, and that z + db(z) >= 0 at
+// (right - left) * f fits in 32 bits, so the kernels' 32-bit multiply equals
+// the 64-bit definition, and that z + db(z) >= 0 at
 // every db knot (the main path's result needs no clamp from below); on a
 // failed check the image stays empty and lnsb_upload_tables reports it.
 void build_flat32(host_tables & t) {
@@ -206,7 +206,7 @@ void build_flat32(host_tables & t) {
     auto fits = [&](const std::vector<int32_t> & v) {
         for (size_t i = 0; i + 1 < v.size(); i++) {
             const long long dv = (long long) v[i + 1] - v[i];
-            if ((dv < 0 ? -dv : dv) * ((1ll << k32_sh) - 1) + (1ll << (k32_sh - 1)) >= (1ll << 31)) return false;
+            if ((dv < 0 ? -dv : dv) * ((1ll << k32_sh) - 1) >= (1ll << 31)) return false;
         }
         return true;
     };

@@ -59,8 +59,8 @@ constexpr int k16m_key_max   = 16 * k16_monte_n + 4;
 constexpr int k16m_key_bytes = (k16m_key_max + 4 + 15) / 16 * 16;   // 36880
 
 // xlns32 interpolation geometry (units: 2^-23 octave): sb knots every 2^-9
-// octave on [0, 26], db knots every 2^-9 octave on [1, 26]; sb interpolates
-// rounded to nearest, db floored.
+// octave on [0, 26], db knots every 2^-9 octave on [1, 26], knots truncated
+// toward zero, interpolation floored.
 constexpr uint32_t k32_one = 1u << 23;
 constexpr uint32_t k32_ess = 26u << 23;
 constexpr int      k32_sh  = 14;                    // knot spacing 2^14 units
@@ -77,8 +77,8 @@ constexpr int      k32_db_knots = (25 << 9) + 1;   // z = (1 << 23) + (n << 14),
 //                      index 0 of both holds k32f_none, which makes the
 //                      cotransformation's special cases (d < 4096 or d a
 //                      multiple of 4096) fall out of the general formula
-// Every interpolation product (right - left) * f, plus the rounding half,
-// fits in 32 bits (checked when the image is built).
+// Every interpolation product (right - left) * f fits in 32 bits (checked
+// when the image is built).
 constexpr int     k32f_sb      = 0;
 constexpr int     k32f_db      = 13316;
 constexpr int     k32f_db0     = k32f_db - 512;

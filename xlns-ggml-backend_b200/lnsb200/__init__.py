@@ -79,7 +79,8 @@ class KernelSet:
     def add_latency(self, kind, lanes=32, steps=4096):
         """SM cycles of one dependent LNS addition (lnsb_add_latency): kind 0 the
         key-form xlns16 addition of the latency mul_mat kernels, 1 / 2 the
-        non-negative xlns16 / xlns32 additions of the normalisers"""
+        non-negative xlns16 / xlns32 additions of the normalisers, 3 the
+        general xlns32 addition of the latency mat-vecs (sum32, xlns32)"""
         import torch
         out = torch.zeros(2, dtype=torch.int64, device="cuda")
         _lib.check(self.lib, "lnsb_add_latency", self.lib.lnsb_add_latency(kind, lanes, steps, _ptr(out), None))
