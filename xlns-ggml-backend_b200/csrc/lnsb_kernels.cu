@@ -1477,6 +1477,12 @@ __host__ __device__ constexpr int a32_threads(int fmt, bool ring) { return fmt =
 // cotransformed case
 #define LNSB_A32_SEL_WARPS 16
 #endif
+#ifndef LNSB_A32_LAT_ADDER
+// the adder of the latency regime: 0 the selected one (add32f_sel: main and
+// cotransformed results side by side), 1 the single-path one (add32f: the
+// cotransformation lookups, then one interpolation, fewer instructions)
+#define LNSB_A32_LAT_ADDER 0
+#endif
 #ifndef LNSB_A32_TN2_MIN_UNITS
 #define LNSB_A32_TN2_MIN_UNITS 2     // two tokens per lane once each warp gets this many units
 #endif
@@ -1582,7 +1588,8 @@ __device__ __forceinline__ void a32_step_x(const int32_t * F, const int32_t * LP
         // latency regime: the selected adder (main and cotransformed results
         // side by side, two table levels deep), no divergence on the dependent path
 #pragma unroll
-        for (int t = 0; t < TN; t++) acc[t] = add32f_sel(F, acc[t], OP::term(w, x[t]));
+        for (int t = 0; t < TN; t++)
+            acc[t] = LNSB_A32_LAT_ADDER ? add32f(F, acc[t], OP::term(w, x[t])) : add32f_sel(F, acc[t], OP::term(w, x[t]));
     } else if constexpr (a32_kind<FMT>() == A32_FLAT) {
         uint32_t    b[TN];
         add32f_part o[TN];
@@ -1625,6 +1632,30 @@ template <int FMT, int TN, bool BF = false>
 __device__ __forceinline__ void a32_steps(const int32_t * F, const int32_t * LP, const a32_chunk<FMT, TN> & c,
                                           uint32_t (&acc)[TN], uint32_t (&st)[TN], bool first, int64_t kv) {
     using OP = a32_fmt<FMT>;
+    if constexpr (BF && a32_kind<FMT>() == A32_FLAT) {
+        // latency regime: the chunk's products first (independent of the
+        // chains), so each step's dependent path is the addition alone
+        uint32_t tm[8][TN];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+#pragma unroll
+            for (int t = 0; t < TN; t++) tm[j][t] = OP::term(c.w[j], c.xv(t, j));
+        }
+        const int j0 = first ? 1 : 0;
+        if (first) {
+#pragma unroll
+            for (int t = 0; t < TN; t++) acc[t] = tm[0][t];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (j >= j0 && j < kv) {
+#pragma unroll
+                for (int t = 0; t < TN; t++)
+                    acc[t] = LNSB_A32_LAT_ADDER ? add32f(F, acc[t], tm[j][t]) : add32f_sel(F, acc[t], tm[j][t]);
+            }
+        }
+        return;
+    }
     if (first) {
 #pragma unroll
         for (int t = 0; t < TN; t++) acc[t] = OP::term(c.w[0], c.xv(t, 0));
@@ -2942,6 +2973,25 @@ constexpr int NN_SMEM_MAX = 200 * 1024;      // dynamic shared memory of a norma
 
 // raises a kernel's dynamic shared memory limit once per device and kernel
 // (whenever it takes any: the default 48 KB covers static and dynamic together)
+// resident blocks per SM of a kernel at a block size and dynamic shared
+// memory (the occupancy query, cached per device; 0 if it fails)
+int blocks_per_sm(const void * kern, int threads, int smem) {
+    int dev = 0;
+    if (current_device(&dev) != 0) return 0;
+    struct entry { const void * k; int t, s, occ; };
+    static std::mutex mu;
+    static std::array<std::vector<entry>, k_max_devices> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto & e : cache[dev]) if (e.k == kern && e.t == threads && e.s == smem) return e.occ;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, (size_t) smem) != cudaSuccess) {
+        cudaGetLastError();
+        occ = 0;
+    }
+    cache[dev].push_back({ kern, threads, smem, occ });
+    return occ;
+}
+
 int nn_smem_attr(const void * kern, int bytes) {
     if (bytes <= 0) return 0;
     int dev = 0;
@@ -3044,28 +3094,36 @@ int soft_max_impl(int fmt, const void * src, lnsb_shape4 s, const void * mask, l
     const dev_tables * T = nullptr;
     const int st = tables_for(fmt, &T);
     if (st != 0) return st;
-    // rows over about two blocks per SM: a block's element passes are latency
-    // bound, so more blocks with fewer rows each finish sooner (each row's
-    // chain is one lane whatever the split)
     int dev = 0;
     const int ds = current_device(&dev);
     if (ds != 0) return ds;
-    int rpb = (int) imin64(32, (nrows + 2 * sm_count(dev) - 1) / (2 * sm_count(dev))), nn_ok = 0, dsmem = 0;
-    {   // the rows' terms in shared memory when they fit (every mode); the table the chain reads before them
-        const int tabb = fmt == LNSB_XLNS32 ? nn_tab<32>() : nn_tab<16>();
-        const int tb   = fmt == LNSB_XLNS32 ? 4 : 2;
-        const int64_t fit = (NN_SMEM_MAX - tabb) / (nn_pitch(s.ne[0], tb) * tb);
-        if (fit >= 1) {
-            rpb = (int) imin64(rpb, fit);
-            nn_ok = 1;
-            dsmem = tabb + (int) (((int64_t) rpb * nn_pitch(s.ne[0], tb) * tb + 15) / 16 * 16);
-        }
-    }
-    const unsigned blocks = (unsigned) ((nrows + rpb - 1) / rpb);
     auto kern = fmt == LNSB_XLNS16 ? (io_f32 ? k_soft_max<16, true> : k_soft_max<16, false>)
                                    : (io_f32 ? k_soft_max<32, true> : k_soft_max<32, false>);
-    const int st2 = nn_smem_attr((const void *) kern, dsmem);
+    const int tabb = fmt == LNSB_XLNS32 ? nn_tab<32>() : nn_tab<16>();
+    const int tb   = fmt == LNSB_XLNS32 ? 4 : 2;
+    const int64_t pitch_b = nn_pitch(s.ne[0], tb) * tb;
+    const int64_t fit = (NN_SMEM_MAX - tabb) / pitch_b;          // rows whose terms fit in shared memory
+    const int nn_ok = fit >= 1 ? 1 : 0;
+    auto smem_for = [&](int r) { return nn_ok ? tabb + (int) (((int64_t) r * pitch_b + 15) / 16 * 16) : 0; };
+    // rows over about two blocks per SM, then as many more rows per block as it
+    // takes for every block to be resident at once: a second wave would repeat
+    // the whole chain time
+    int rpb = (int) imin64(32, (nrows + 2 * sm_count(dev) - 1) / (2 * sm_count(dev)));
+    if (nn_ok) rpb = (int) imin64(rpb, fit);
+    const int st2 = nn_smem_attr((const void *) kern, smem_for(rpb));
     if (st2 != 0) return st2;
+    for (int it = 0; it < 4; it++) {
+        const int occ = blocks_per_sm((const void *) kern, SM_THREADS, smem_for(rpb));
+        if (occ < 1) break;
+        const int64_t resident = (int64_t) occ * sm_count(dev);
+        if ((nrows + rpb - 1) / rpb <= resident) break;
+        int want = (int) imin64(32, (nrows + resident - 1) / resident);
+        if (nn_ok) want = (int) imin64(want, fit);
+        if (want <= rpb) break;
+        rpb = want;
+    }
+    const int dsmem = smem_for(rpb);
+    const unsigned blocks = (unsigned) ((nrows + rpb - 1) / rpb);
     launch_k(kern, blocks, SM_THREADS, dsmem, stream, *T, src, s, mask, ms, scale_l, dst, work, seed, rpb, nn_ok);
     return launch_status();
 }
@@ -3482,8 +3540,10 @@ int lnsb_copy_strided(int elem_size, const void * src, const int64_t ne[4], cons
 
 int lnsb_add_latency(int kind, int lanes, int steps, int64_t * out, lnsb_stream_t stream) {
     if (kind < 0 || kind > 3 || lanes < 1 || lanes > 32 || steps < 2 || out == nullptr) return LNSB_E_INVALID;
+    // every adder table here (key16s, sbdb16, the flat xlns32 image) is uploaded with either format's tables
     const dev_tables * T = nullptr;
-    const int st = tables_for(kind >= 2 ? LNSB_XLNS32 : LNSB_XLNS16, &T);
+    int st = tables_for(LNSB_XLNS16, &T);
+    if (st == LNSB_E_NO_TABLES) st = tables_for(LNSB_XLNS32, &T);
     if (st != 0) return st;
     constexpr int smem = AL_TAB + AL_OPS * 32 * 4;
     static bool attr[k_max_devices] = {};
