@@ -1632,30 +1632,6 @@ template <int FMT, int TN, bool BF = false>
 __device__ __forceinline__ void a32_steps(const int32_t * F, const int32_t * LP, const a32_chunk<FMT, TN> & c,
                                           uint32_t (&acc)[TN], uint32_t (&st)[TN], bool first, int64_t kv) {
     using OP = a32_fmt<FMT>;
-    if constexpr (BF && a32_kind<FMT>() == A32_FLAT) {
-        // latency regime: the chunk's products first (independent of the
-        // chains), so each step's dependent path is the addition alone
-        uint32_t tm[8][TN];
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-#pragma unroll
-            for (int t = 0; t < TN; t++) tm[j][t] = OP::term(c.w[j], c.xv(t, j));
-        }
-        const int j0 = first ? 1 : 0;
-        if (first) {
-#pragma unroll
-            for (int t = 0; t < TN; t++) acc[t] = tm[0][t];
-        }
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            if (j >= j0 && j < kv) {
-#pragma unroll
-                for (int t = 0; t < TN; t++)
-                    acc[t] = LNSB_A32_LAT_ADDER ? add32f(F, acc[t], tm[j][t]) : add32f_sel(F, acc[t], tm[j][t]);
-            }
-        }
-        return;
-    }
     if (first) {
 #pragma unroll
         for (int t = 0; t < TN; t++) acc[t] = OP::term(c.w[0], c.xv(t, 0));
@@ -1972,6 +1948,32 @@ __device__ __forceinline__ void norm_tables(const dev_tables & T, int16_t * tab,
     stage_async(tab, T.sbdb16, k16_tab_bytes16);
     if constexpr (k_mode == M_MONTE) stage_async(fine, T.monte16, 2 * k16_monte_n * 2);
 }
+// A chain acc = add(acc, q[i]), i in [i0, n), over terms in shared memory: the
+// terms are loaded a batch ahead of the additions (they do not depend on the
+// chain), so a step's dependent path is the addition alone.
+template <typename E, typename ADD>
+__device__ __forceinline__ uint32_t chain_smem(const E * q, int i0, int n, uint32_t acc, ADD add) {
+    constexpr int U = 8;
+    uint32_t cur[U];
+    int i = i0;
+#pragma unroll
+    for (int u = 0; u < U; u++) cur[u] = i + u < n ? (uint32_t) q[i + u] : 0u;
+    for (; i + U <= n; i += U) {
+        uint32_t nxt[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) nxt[u] = i + U + u < n ? (uint32_t) q[i + U + u] : 0u;
+#pragma unroll
+        for (int u = 0; u < U; u++) acc = add(acc, cur[u]);
+#pragma unroll
+        for (int u = 0; u < U; u++) cur[u] = nxt[u];
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        if (i + u < n) acc = add(acc, cur[u]);
+    }
+    return acc;
+}
+
 // one non-negative addition of the mode: accumulator form (sum32: acc32) and term code
 __device__ __forceinline__ uint32_t nn_add(const int32_t * F, const int16_t * tab, uint32_t acc, uint32_t t) {
     if constexpr (k_mode == M_SUM32) return padd32f(F, acc, t << 16);
@@ -2057,13 +2059,13 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
         if (NN && FMT == 32) {
             const uint32_t * q = sq32 + threadIdx.x * P;
             uint32_t acc = 0u;
-            for (int64_t i = 0; i < ncols; i++) acc = padd32f(dyn, acc, q[i]);
+            acc = chain_smem(q, 0, (int) ncols, acc, [&](uint32_t a, uint32_t t) { return padd32f(dyn, a, t); });
             const uint32_t mean = mul32(acc, inv_n);
             s_inv[threadIdx.x] = recip32(sqrt32(add32(T, mean, eps_l)));
         } else if (NN) {
             const uint16_t * q = sq + threadIdx.x * P;
             uint32_t acc = 0u;                              // the zero code (acc32 0 in sum32)
-            for (int64_t i = 0; i < ncols; i++) acc = nn_add(dyn, tab, acc, q[i]);
+            acc = chain_smem(q, 0, (int) ncols, acc, [&](uint32_t a, uint32_t t) { return nn_add(dyn, tab, a, t); });
             red16 R{ &T, tab, fine };
             const uint32_t mean = mul16(R.finish(acc), inv_n);
             s_inv[threadIdx.x] = recip16(sqrt16(add16(mean, eps_l, tab)));
@@ -2164,23 +2166,35 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         const int64_t i1 = row % s.ne[1], i2 = (row / s.ne[1]) % s.ne[2], i3 = row / (s.ne[1] * s.ne[2]);
         return ((i3 % ms.ne[3]) * ms.ne[2] + i2 % ms.ne[2]) * ms.ne[1] + i1;
     };
-    auto value = [&](int64_t row, int64_t mrow, int64_t i) -> uint32_t {   // scaled, masked logit
+    // a logit in two parts, so a batch's loads are all in flight before any is used:
+    // the raw words (the source value, the mask value; IO_F32: float bits), then
+    // the scaled, masked code
+    auto rawv = [&](int64_t row, int64_t i) -> uint32_t {
+        if constexpr (IO_F32) return __float_as_uint(static_cast<const float *>(src)[row * n + i]);
+        else                  return ld(src, row * n + i);
+    };
+    auto rawm = [&](int64_t mrow, int64_t i) -> uint32_t {
+        if (mask == nullptr) return 0u;
+        if constexpr (IO_F32) return __float_as_uint(static_cast<const float *>(mask)[mrow * n + i]);
+        else                  return ld(mask, mrow * n + i);
+    };
+    auto cook = [&](uint32_t rv, uint32_t rm) -> uint32_t {
         uint32_t v;
         if constexpr (IO_F32) {
-            const float f = static_cast<const float *>(src)[row * n + i];
+            const float f = __uint_as_float(rv);
             v = FMT == 16 ? from_f32_16(T, f) : from_f32_32(T, f);
         } else {
-            v = ld(src, row * n + i);
+            v = rv;
         }
         if (v != NEG_INF) {
             v = FMT == 16 ? mul16(v, scale_l) : mul32(v, scale_l);
             if (mask != nullptr) {
                 uint32_t mk;
                 if constexpr (IO_F32) {
-                    const float mf = static_cast<const float *>(mask)[mrow * n + i];
+                    const float mf = __uint_as_float(rm);
                     mk = mf <= -3.0e38f ? NEG_INF : (FMT == 16 ? from_f32_16(T, mf) : from_f32_32(T, mf));
                 } else {
-                    mk = ld(mask, mrow * n + i);
+                    mk = rm;
                 }
                 if (mk == NEG_INF) v = NEG_INF;
                 else if (FMT == 16 ? !is_zero16(mk) : !is_zero32(mk)) v = FMT == 16 ? add16(v, mk, tab) : add32(T, v, mk);
@@ -2188,6 +2202,7 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         }
         return v;
     };
+    auto value = [&](int64_t row, int64_t mrow, int64_t i) -> uint32_t { return cook(rawv(row, i), rawm(mrow, i)); };
 
     uint16_t * cs   = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
     uint32_t * cs32 = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
@@ -2206,9 +2221,14 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         if (ST) {
             int64_t i0 = 0;
             for (; i0 + 32 * U <= n; i0 += 32 * U) {
-                uint32_t v[U];
+                uint32_t v[U], m[U];
 #pragma unroll
-                for (int u = 0; u < U; u++) v[u] = value(row, mrow, i0 + u * 32 + lane);
+                for (int u = 0; u < U; u++) {
+                    v[u] = rawv(row, i0 + u * 32 + lane);
+                    m[u] = rawm(mrow, i0 + u * 32 + lane);
+                }
+#pragma unroll
+                for (int u = 0; u < U; u++) v[u] = cook(v[u], m[u]);
 #pragma unroll
                 for (int u = 0; u < U; u++) {
                     put(r, i0 + u * 32 + lane, v[u]);
@@ -2269,13 +2289,13 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
         if (NN && FMT == 32) {
             const uint32_t * q = cs32 + r * P;
             uint32_t acc = q[0];
-            for (int64_t i = 1; i < n; i++) acc = padd32f(dyn, acc, q[i]);
+            acc = chain_smem(q, 1, (int) n, acc, [&](uint32_t a, uint32_t t) { return padd32f(dyn, a, t); });
             s_tot[r] = acc;
         } else if (NN) {
             const uint16_t * q = cs + r * P;
             red16 R{ &T, tab, fine };
             uint32_t acc = R.from(q[0]);
-            for (int64_t i = 1; i < n; i++) acc = nn_add(dyn, tab, acc, q[i]);
+            acc = chain_smem(q, 1, (int) n, acc, [&](uint32_t a, uint32_t t) { return nn_add(dyn, tab, a, t); });
             s_tot[r] = R.finish(acc);
         } else if constexpr (FMT == 16) {
             red16 R{ &T, tab, fine };
@@ -2438,11 +2458,11 @@ k_attn_decode(dev_tables T, const float * __restrict__ q, const __half * __restr
         uint32_t acc;
         if constexpr (FMT == 32) {
             acc = sv[0];
-            for (int64_t k = 1; k < nkv; k++) acc = padd32f(F, acc, sv[k]);
+            acc = chain_smem(sv, 1, (int) nkv, acc, [&](uint32_t a, uint32_t t) { return padd32f(F, a, t); });
         } else if constexpr (NNCHAIN) {
             red16 R{ &T, tab, fine };
             acc = R.from(sv[0]);
-            for (int64_t k = 1; k < nkv; k++) acc = nn_add(F, tab, acc, sv[k]);
+            acc = chain_smem(sv, 1, (int) nkv, acc, [&](uint32_t a, uint32_t t) { return nn_add(F, tab, a, t); });
             acc = R.finish(acc);
         } else {
             red16 R{ &T, tab, fine };
