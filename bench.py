@@ -69,7 +69,7 @@ def parse():
     p.add_argument("--no-decode", action="store_true", help="skip the model decode measurements")
     p.add_argument("--no-sides", action="store_true", help="the headline only (no side objects)")
     p.add_argument("--sides", default="all",
-                   help="comma-separated side objects to run (configs, configs4, mul_mat_id, weights, normalisers; "
+                   help="comma-separated side objects to run (configs, configs4, mul_mat_id, weights, normalisers, matvec; "
                         "default all) -- for profiling one of them")
     p.add_argument("--c4-points", default="1,16,128", help="configs[4] token counts N to time (default 1,16,128)")
     p.add_argument("--decode-mode", default="sum32", help="sum mode of the decode (BASELINE configs[2]: sum32)")
@@ -458,7 +458,7 @@ def run_ours(args, wl):
     }
     if not args.no_sides:
         sides = set(args.sides.split(",")) if args.sides != "all" else \
-            {"configs", "configs4", "mul_mat_id", "weights", "normalisers"}
+            {"configs", "configs4", "mul_mat_id", "weights", "normalisers", "matvec"}
         other = "configs1" if args.workload == "configs0" else "configs0"
         if "configs" in sides:
             line[other] = time_side_mul_mat(ctx, lnsb200, torch, np, WORKLOADS[other], args, int_peak, f_mhz)
@@ -471,6 +471,8 @@ def run_ours(args, wl):
                 line["weights"] = time_weights(ctx, lnsb200, torch, np, args, hbm)
             if "normalisers" in sides:
                 line["normalisers"] = time_norms(ctx, lnsb200, torch, np, args, f_mhz)
+            if "matvec" in sides:
+                line["matvec"] = time_matvec(ctx, lnsb200, torch, np, args, f_mhz)
     if not args.no_decode:
         # the metric's second half: model decode tok/s, one sequence per GPU
         line["decode"] = run_decode(torch, dist, rank, world, args, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline),
@@ -748,6 +750,42 @@ def time_norms(ctx, lnsb200, torch, np, args, f_mhz):
             d["chain"] = {"l_add_cycles": l_add, "t_chain_us": t_chain * 1e6, "frac": t_chain / (ms / 1000),
                           "adder": "non-negative xlns16 (padd16)" if kind == 1 else "non-negative xlns32 (padd32f)"}
         out[name] = d
+    return out
+
+
+def time_matvec(ctx, lnsb200, torch, np, args, f_mhz):
+    """The decode's mat-vecs (BASELINE configs[2] / [3] shapes, one token):
+    q/k/v (576 -> 960), up/gate (576 -> 3072) and down (1536 -> 576) in LNS16
+    sum32 and LNS32, weights N(0, 0.02), the token N(0, 1) (numpy
+    default_rng(5)), codes in and out, device-timed, L2 flushed before every
+    step.  Bound: the chain, K - 1 dependent additions per output through the
+    general xlns32 adder, L_add measured on this GPU (lnsb_add_latency kind 3):
+    T_chain = (K - 1) L_add / f_sm."""
+    rng = np.random.default_rng(5)
+    out = {}
+    shapes = (("qkv", 576, 960), ("up_gate", 576, 3072), ("down", 1536, 576))
+    for fmt, mode in ((16, "sum32"), (32, "base")):
+        ks = lnsb200.KernelSet(fmt, mode)
+        ks.upload_tables()
+        l_add = ks.add_latency(3, 32, 4096)
+        dt = torch.int16 if fmt == 16 else torch.int32
+        for name, K, M in shapes:
+            wf = torch.from_numpy(rng.normal(0, 0.02, (M, K)).astype(np.float32)).cuda()
+            xf = torch.from_numpy(rng.normal(0, 1, (1, K)).astype(np.float32)).cuda()
+            w = torch.empty(K * M, dtype=dt, device="cuda")
+            ks.to_lns_transposed(wf, w, M, K, M)
+            x = torch.empty(K, dtype=dt, device="cuda")
+            ks.to_lns(xf, x)
+            y = torch.empty(M, dtype=dt, device="cuda")
+            ms = timed(ctx, lambda: ks.mul_mat_lns(w, x, y, K, M, 1, stream=ctx.stream), max(args.steps, 20), args.warmup)
+            t_chain = (K - 1) * l_add / (f_mhz * 1e6)
+            out["%s_%s" % ("lns16_sum32" if fmt == 16 else "lns32", name)] = {
+                "K": K, "M": M, "ms_per_step": ms, "value": M * (K - 1) / (ms / 1000) / 1e9, "unit": UNIT,
+                "cycles_per_step": ms / 1000 * f_mhz * 1e6 / (K - 1),
+                "chain": {"l_add_cycles": l_add, "t_chain_us": t_chain * 1e6, "frac": t_chain / (ms / 1000),
+                          "adder": "general xlns32 (add32f_sel)"}}
+    out["kernel"] = "k_mat_vec_lat: a producer warp writes the products into a shared ring, the chain warp adds"
+    out["l2"] = "flushed (256 MB write) before every timed step"
     return out
 
 

@@ -193,7 +193,7 @@ __device__ __forceinline__ int32_t interp32f(const int32_t * F, uint32_t z, bool
     return lerp32(F[i], F[i + 1], z);
 }
 
-// the cotransformed db of add32f_lean's rare branch: opposite signs, d < 1
+// the cotransformed db of the throughput adder's rare branch: opposite signs, d < 1
 __device__ __forceinline__ uint32_t add32f_cot(const int32_t * F, uint32_t mx, uint32_t d) {
     const int32_t  d2 = (int32_t) (d & 4095u);
     const int32_t  la = F[k32f_lo + d2];
@@ -231,10 +231,6 @@ __device__ __forceinline__ add32f_part add32f_main(const int32_t * F, uint32_t a
     o.r   = (int32_t) (r ^ o.mx) < 0 ? (o.mx | 0x7FFFFFFFu) : r;
     o.cot = usedb && o.d < k32_one;
     return o;
-}
-__device__ __forceinline__ uint32_t add32f_lean(const int32_t * F, uint32_t a, uint32_t b) {
-    const add32f_part o = add32f_main(F, a, b);
-    return o.cot ? add32f_cot(F, o.mx, o.d) : o.r;
 }
 
 // add32 over the flat image for a chain's latency: the main result (sb(d),
