@@ -385,3 +385,35 @@ def test_errors_are_reported(ks16):
     with pytest.raises(LnsbError):
         ks16.mul_mat_lns(torch.zeros(4, dtype=torch.int16, device="cuda"), torch.zeros(4, dtype=torch.int16, device="cuda"),
                          torch.zeros(4, dtype=torch.int16, device="cuda"), 2, 2, 2, slices=(3, 1, 4, 1))
+
+
+# ----------------------------------------------------- the latency mat-vec (k_mat_vec_lat)
+
+@pytest.mark.parametrize("fmt", [16, 32])
+@pytest.mark.parametrize("K,M,N", [(100, 2000, 3), (1537, 4700, 1), (577, 9000, 4), (33, 1000, 1), (2, 70, 2)])
+def test_mat_vec_lat(orc, fmt, K, M, N):
+    """sum32 / xlns32 products with few 32-row x 1-token units per SM run the
+    producer/chain kernel with 1 .. 8 units per block (a partial last block,
+    K not a multiple of the 16-step stage, M not a multiple of 32): bit-exact
+    against the oracle"""
+    import lnsb200
+    rng = np.random.default_rng(K * 7 + M + N)
+    if fmt == 16:
+        ks = lnsb200.KernelSet(16, "sum32")
+        ks.upload_tables()
+        w = codes16(orc, rng, (M, K), 0.02)
+        x = codes16(orc, rng, (N, K), 1.0)
+        want = orc.mul_mat16("sum32", w, x, nthreads=NT).ravel()
+        out = torch.empty(N * M, dtype=torch.int16, device="cuda")
+        ks.mul_mat_lns(dev16(np.ascontiguousarray(w.T)), dev16(x), out, K, M, N)
+        got = host16(out)
+    else:
+        ks = lnsb200.KernelSet(32, "base")
+        ks.upload_tables()
+        w = codes32(orc, rng, (M, K), 0.02)
+        x = codes32(orc, rng, (N, K), 1.0)
+        want = orc.mul_mat32(w, x, nthreads=NT).ravel()
+        out = torch.empty(N * M, dtype=torch.int32, device="cuda")
+        ks.mul_mat_lns(dev32(np.ascontiguousarray(w.T)), dev32(x), out, K, M, N)
+        got = host32(out)
+    assert np.array_equal(got, want)

@@ -1484,8 +1484,12 @@ __host__ __device__ constexpr int a32_threads(int fmt, bool ring) { return fmt =
 #define LNSB_A32_LAT_ADDER 0
 #endif
 #ifndef LNSB_A32_LV
-// 1: mat-vecs with at most one unit per SM (sum32, xlns32) run k_mat_vec_lat
+// 1: products with few units per SM (sum32, xlns32) run k_mat_vec_lat
 #define LNSB_A32_LV 1
+#endif
+#ifndef LNSB_A32_LV_PAIRS
+// ... up to this many units per SM (at most LV_MAX_PAIRS)
+#define LNSB_A32_LV_PAIRS 6
 #endif
 #ifndef LNSB_A32_TN2_MIN_UNITS
 #define LNSB_A32_TN2_MIN_UNITS 2     // two tokens per lane once each warp gets this many units
@@ -1857,45 +1861,54 @@ __device__ __forceinline__ uint32_t chain_smem_strided(const uint32_t * q, int i
 }
 
 // ============== latency mat-vec over the flat xlns32 addition ===============
-// At most one unit (32 weight rows x 1 token) per SM -- the decode's mat-vecs
-// in sum32 and xlns32 -- the time is the chain: K dependent additions per
-// lane.  Two warps per unit.  The producer warp streams the unit's weights and
-// the token's values and writes the products into a shared ring of LV_STAGES
-// stages of LV_STEPS steps ([step][lane], one word each); the chain warp reads
-// a product and adds it (add32f_sel), so its instruction stream is the
-// addition alone.  Stage s is handed over with named barriers counting both
-// warps: id 1 + s (products written) and 1 + LV_STAGES + s (stage free again,
-// arrived only for stages the producer refills).  Same bits as k_mul_mat_a32.
-constexpr int LV_STEPS = 32, LV_STAGES = 4;
-constexpr int LV_RING_BYTES = LV_STAGES * LV_STEPS * 32 * 4;
+// Up to LV_MAX_PAIRS units (32 weight rows x 1 token each) per SM -- the
+// decode's mat-vecs in sum32 and xlns32, the one- and few-token products of
+// large ones -- the time is the chain: K dependent additions per lane.  Two
+// warps per unit, np units per block sharing the 129 KB addition image.  A
+// unit's producer warp streams its 32 rows' weights and the token's values and
+// writes the products into its own ring of LV_STAGES stages of LV_STEPS steps
+// ([step][lane], one word each); its chain warp reads a product (a batch
+// ahead) and adds it (add32f_sel), so the chain warp's instruction stream is
+// the addition alone.  Stage s is handed over with named barriers counted over
+// the whole block, so the block's units move in step: id 1 + s (every
+// producer wrote stage s) and 1 + LV_STAGES + s (every chain warp is done with
+// it; arrived only for stages the producers refill, so each wait has its
+// arrivals).  Units past the end run on the last unit's operands and store
+// nothing.  Same bits as k_mul_mat_a32.
+constexpr int LV_STEPS = 32, LV_STAGES = 4, LV_MAX_PAIRS = 6;
+constexpr int LV_RING_BYTES = LV_STAGES * LV_STEPS * 32 * 4;     // per unit
 template <int FMT, bool OUT_F32>
-__global__ void __launch_bounds__(64, 1)
+__global__ void __launch_bounds__(64 * LV_MAX_PAIRS, 1)
 k_mat_vec_lat(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
               const typename a32_fmt<FMT>::elem * __restrict__ X, void * __restrict__ dst, int64_t K, int64_t M,
-              int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3) {
+              int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3, int64_t units) {
     using E  = typename a32_fmt<FMT>::elem;
     using OP = a32_fmt<FMT>;
     extern __shared__ __align__(16) int32_t F[];
-    uint32_t * ring = reinterpret_cast<uint32_t *>(F + k32f_words);
     stage_async(F, T.flat32, k32f_words * 4);              // read-only tables: before the wait
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
     pdl_entry();
-    const int     lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int     lane = threadIdx.x & 31, warp = threadIdx.x >> 5, pair = warp >> 1;
+    const int     np = (int) (blockDim.x >> 6), nthr = (int) blockDim.x;
+    uint32_t * ring = reinterpret_cast<uint32_t *>(F + k32f_words) + pair * (LV_RING_BYTES / 4);
     const int64_t RB = (M + 31) / 32;
-    const int64_t u = blockIdx.x, n = u % N, rest = u / N, rb = rest % RB, z = rest / RB;
+    const int64_t u0 = (int64_t) blockIdx.x * np + pair;
+    const bool    valid = u0 < units;
+    const int64_t u = valid ? u0 : units - 1;
+    const int64_t n = u % N, rest = u / N, rb = rest % RB, z = rest / RB;
     const int64_t i12 = z % ne12, i13 = z / ne12;
     const int64_t m = rb * 32 + lane;
     const E * wb = W + ((i13 / r3) * ne02 + i12 / r2) * K * M;
     const E * xt = X + (z * N + n) * K;
     const int64_t nch = (K + LV_STEPS - 1) / LV_STEPS;
-    if (warp == 1) {
+    if (warp & 1) {
         // producer: the products of chunk c into stage c % LV_STAGES
         const E * wl = wb + (m < M ? m : M - 1);
         for (int64_t c = 0; c < nch; c++) {
             const int sidx = (int) (c % LV_STAGES);
-            if (c >= LV_STAGES) asm volatile("bar.sync %0, 64;\n" ::"r"(1 + LV_STAGES + sidx) : "memory");
+            if (c >= LV_STAGES) asm volatile("bar.sync %0, %1;\n" ::"r"(1 + LV_STAGES + sidx), "r"(nthr) : "memory");
             const int64_t k0 = c * LV_STEPS;
             uint32_t * st = ring + sidx * LV_STEPS * 32 + lane;
             uint32_t w[LV_STEPS];
@@ -1906,7 +1919,7 @@ k_mat_vec_lat(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
                 const uint32_t x = k0 + j < K ? (uint32_t) __ldg(xt + k0 + j) : 0u;
                 st[j * 32] = OP::term(w[j], x);
             }
-            asm volatile("bar.arrive %0, 64;\n" ::"r"(1 + sidx) : "memory");
+            asm volatile("bar.arrive %0, %1;\n" ::"r"(1 + sidx), "r"(nthr) : "memory");
         }
         return;
     }
@@ -1914,14 +1927,14 @@ k_mat_vec_lat(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
     uint32_t acc = 0;
     for (int64_t c = 0; c < nch; c++) {
         const int sidx = (int) (c % LV_STAGES);
-        asm volatile("bar.sync %0, 64;\n" ::"r"(1 + sidx) : "memory");
+        asm volatile("bar.sync %0, %1;\n" ::"r"(1 + sidx), "r"(nthr) : "memory");
         const uint32_t * q = ring + sidx * LV_STEPS * 32 + lane;
         const int kv = (int) imin64(LV_STEPS, K - c * LV_STEPS);
         if (c == 0) acc = q[0];
         acc = chain_smem_strided(q, c == 0 ? 1 : 0, kv, acc, [&](uint32_t a, uint32_t t) { return add32f_sel(F, a, t); });
-        if (c + LV_STAGES < nch) asm volatile("bar.arrive %0, 64;\n" ::"r"(1 + LV_STAGES + sidx) : "memory");
+        if (c + LV_STAGES < nch) asm volatile("bar.arrive %0, %1;\n" ::"r"(1 + LV_STAGES + sidx), "r"(nthr) : "memory");
     }
-    if (m < M) OP::store(T, dst, (z * N + n) * M + m, K == 0 ? 0u : OP::finish(acc), OUT_F32);
+    if (valid && m < M) OP::store(T, dst, (z * N + n) * M + m, K == 0 ? 0u : OP::finish(acc), OUT_F32);
 }
 
 // ============================ MUL_MAT_ID ===================================
@@ -2880,21 +2893,26 @@ int launch_a32_by(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst,
                    : launch_a32<FMT, TN, false, false>(T, a, dst, r2, r3, units, dev, vecx, stream, peers);
 }
 
-// the latency mat-vec (k_mat_vec_lat): one block of two warps per unit
+// the latency mat-vec (k_mat_vec_lat): np = ceil(units / SMs) units per block
+// of 2 np warps, one wave
 template <int FMT, bool OUT_F32>
 int launch_lv(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, int64_t r2, int64_t r3, int64_t units,
               int dev, cudaStream_t stream) {
     static bool attr[k_max_devices] = {};
     auto kern = k_mat_vec_lat<FMT, OUT_F32>;
-    constexpr int smem = k32f_words * 4 + LV_RING_BYTES;
+    constexpr int smem_max = k32f_words * 4 + LV_MAX_PAIRS * LV_RING_BYTES;
     if (!attr[dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
         if (e != cudaSuccess) return (int) e;
         attr[dev] = true;
     }
+    const int64_t sms = sm_count(dev);
+    const int np = (int) ((units + sms - 1) / sms);                    // 1 .. LV_MAX_PAIRS (checked by the caller)
+    const int64_t grid = (units + np - 1) / np;
+    const int smem = k32f_words * 4 + np * LV_RING_BYTES;
     using E = typename a32_fmt<FMT>::elem;
-    launch_k(kern, (unsigned) units, 64, smem, stream, T, static_cast<const E *>(a->w), static_cast<const E *>(a->x), dst,
-             a->K, a->M, a->N, a->ne02, a->ne12, r2, r3);
+    launch_k(kern, (unsigned) grid, 64 * np, smem, stream, T, static_cast<const E *>(a->w), static_cast<const E *>(a->x),
+             dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, units);
     return launch_status();
 }
 
@@ -2914,9 +2932,9 @@ int mul_mat_a32(int fmt, const dev_tables & T, const lnsb_mul_mat_args * a, void
     const int64_t es = fmt == LNSB_XLNS16 ? 2 : 4;
     const bool vecx = (a->K * es) % 16 == 0 && ((uintptr_t) a->x % 16) == 0;
     const bool ring = vecx && (a->M * es) % 16 == 0 && ((uintptr_t) a->w % 16) == 0;
-    // at most one unit of 32 rows x 1 token per SM, the flat adder, no peer stores: the latency mat-vec
+    // at most LNSB_A32_LV_PAIRS units of 32 rows x 1 token per SM, the flat adder, no peer stores: the latency mat-vec
     if (LNSB_A32_LV && (fmt == LNSB_XLNS32 || k_mode == M_SUM32) && peers.n == 0 && a->K > 0 &&
-        nz * RB * a->N <= (int64_t) sm_count(dev)) {
+        nz * RB * a->N <= (int64_t) sm_count(dev) * LNSB_A32_LV_PAIRS) {
         const int64_t lv_units = nz * RB * a->N;
         if (fmt == LNSB_XLNS16) return out_f32 ? launch_lv<16, true>(T, a, dst, r2, r3, lv_units, dev, stream)
                                                : launch_lv<16, false>(T, a, dst, r2, r3, lv_units, dev, stream);
