@@ -73,6 +73,8 @@ def parse():
                         "default all) -- for profiling one of them")
     p.add_argument("--c4-points", default="1,16,128", help="configs[4] token counts N to time (default 1,16,128)")
     p.add_argument("--decode-mode", default="sum32", help="sum mode of the decode (BASELINE configs[2]: sum32)")
+    p.add_argument("--decode-tokens", type=int, default=128,
+                   help="tokens generated per sequence (BASELINE configs[2]: 128); fewer only for profiling")
     return p.parse_args()
 
 
@@ -862,7 +864,8 @@ def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16, f_mhz=1965.0):
     e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     model.forward(g, cfg, prompt[:8], 0)                 # warm-up (also fills the allocator)
     dec = model.GraphDecoder(g, cfg)                     # one CUDA graph per decode position,
-    dec.prepare(len(prompt), len(prompt) + 127)          # captured once before the timed region
+    G = args.decode_tokens - 1                          # steps after the prefill's token
+    dec.prepare(len(prompt), len(prompt) + G)            # captured once before the timed region
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -870,7 +873,7 @@ def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16, f_mhz=1965.0):
     logits = model.forward(g, cfg, prompt, 0)
     toks = [g.argmax(logits)]
     e[1].record(stream)
-    toks += dec.decode(toks[0], len(prompt), 127)       # each step's token copied to pinned host memory
+    toks += dec.decode(toks[0], len(prompt), G)         # each step's token copied to pinned host memory
     e[2].record(stream)
     torch.cuda.synchronize()
     pre_ms, dec_ms = e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])
@@ -879,9 +882,9 @@ def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16, f_mhz=1965.0):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         pre_ms, dec_ms = t.tolist()
     out = {"model": "SmolLM2-135M shape (30 layers, d 576, 9/3 heads, ffn 1536, vocab 49152), random N(0,0.02) weights seed 2",
-           "format": "xlns%d" % fmt, "mode": args.decode_mode if fmt == 16 else None, "prompt": 128, "generated": 128, "sequences": world,
-           "prefill_tok_per_s": world * 128 / (pre_ms / 1000), "decode_tok_per_s": world * 127 / (dec_ms / 1000),
-           "ms_per_token": dec_ms / 127, "prefill_ms": pre_ms,
+           "format": "xlns%d" % fmt, "mode": args.decode_mode if fmt == 16 else None, "prompt": 128, "generated": G + 1, "sequences": world,
+           "prefill_tok_per_s": world * 128 / (pre_ms / 1000), "decode_tok_per_s": world * G / (dec_ms / 1000),
+           "ms_per_token": dec_ms / G, "prefill_ms": pre_ms,
            "timing": "device events; prefill eager, decode as one CUDA graph per position (captured before the timed region); each step's greedy token is copied to pinned host memory",
            "first_tokens": toks[:8]}
     # the chain bound of one decode step: its dependent additions, the general
@@ -894,13 +897,13 @@ def run_decode(torch, dist, rank, world, args, cpu=False, fmt=16, f_mhz=1965.0):
         ks.upload_tables()
         l3, l2 = ks.add_latency(3, 32), ks.add_latency(2, 32)
         L, d, ffn, hd = cfg["n_layer"], cfg["n_embd"], cfg["n_ff"], cfg["head_dim"]
-        nkv = (129 + 255) / 2                             # keys per step, averaged over the 127 steps
+        nkv = (129 + 128 + G) / 2                         # keys per step, averaged over the G steps
         s3 = L * (d + hd + nkv + d + d + ffn) + d          # qkv, q.K, p.V, wo, up/gate, down; output
         s2 = L * (d + d + nkv - 1) + d                     # two norm blocks and the softmax per layer; final norm
         f = f_mhz * 1e6
         t_chain = (s3 * l3 + s2 * l2) / f * 1e3
         out["chain"] = {"general_steps": s3, "nonneg_steps": s2, "l_add_general_cycles": l3, "l_add_nonneg_cycles": l2,
-                        "sm_mhz_used": f / 1e6, "t_chain_ms_per_token": t_chain, "frac": t_chain / (dec_ms / 127),
+                        "sm_mhz_used": f / 1e6, "t_chain_ms_per_token": t_chain, "frac": t_chain / (dec_ms / G),
                         "bound": "one token's dependent additions (mat-vec, attention and normaliser chains) at "
                                  "the measured latency of each adder"}
     if cpu:

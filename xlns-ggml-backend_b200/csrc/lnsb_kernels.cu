@@ -2143,10 +2143,27 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
         };
         const int64_t tot = nr * ncols;
         if (FUSE && x_out != nullptr) {
-            for (int64_t e = threadIdx.x; e < tot; e += blockDim.x) {
-                const float xf = xval(row0 * ncols + e);     // x once: the scaling pass reads it back
-                x_out[row0 * ncols + e] = xf;
-                square(e, f2c(xf));
+            // x once (the scaling pass reads it back); a thread's values in
+            // batches, so their chains of table lookups interleave
+            constexpr int U = 4;
+            for (int64_t e0 = threadIdx.x; e0 < tot; e0 += (int64_t) blockDim.x * U) {
+                float xf[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int64_t e = e0 + (int64_t) u * blockDim.x;
+                    xf[u] = e < tot ? xval(row0 * ncols + e) : 0.0f;
+                }
+                uint32_t c[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) c[u] = f2c(xf[u]);
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int64_t e = e0 + (int64_t) u * blockDim.x;
+                    if (e < tot) {
+                        x_out[row0 * ncols + e] = xf[u];
+                        square(e, c[u]);
+                    }
+                }
             }
         } else {
             constexpr int U = 8;                         // loads in flight per thread
@@ -2201,6 +2218,42 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
         }
     }
     __syncthreads();
+    if constexpr (FUSE) {
+        if (x_out != nullptr && NN) {
+            // the fused block's scaling pass in batches (the x values were
+            // written by the squares pass of this block)
+            constexpr int U = 4;
+            const int64_t tot = nr * ncols;
+            for (int64_t e0 = threadIdx.x; e0 < tot; e0 += (int64_t) blockDim.x * U) {
+                float yf[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int64_t e = e0 + (int64_t) u * blockDim.x;
+                    const int64_t ee = e < tot ? e : tot - 1;
+                    const int64_t r = ee / ncols;
+                    const int64_t idx = (row0 + r) * ncols + (ee - r * ncols);
+                    const uint32_t inv = s_inv[r];
+                    const uint32_t v = f2c(x_out[idx]);
+                    yf[u] = c2f(FMT == 16 ? mul16(v, inv) : mul32(v, inv));
+                    if (nw != nullptr) {
+                        const uint32_t yc = f2c(yf[u]), wc = f2c(nw[ee - r * ncols]);
+                        yf[u] = c2f(FMT == 16 ? mul16(yc, wc) : mul32(yc, wc));
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int64_t e = e0 + (int64_t) u * blockDim.x;
+                    if (e < tot) {
+                        const int64_t r = e / ncols;
+                        const int64_t idx = (row0 + r) * ncols + (e - r * ncols);
+                        if constexpr (FMT == 16) static_cast<uint16_t *>(dst)[idx] = (uint16_t) f2c(yf[u]);
+                        else                     static_cast<uint32_t *>(dst)[idx] = f2c(yf[u]);
+                    }
+                }
+            }
+            return;
+        }
+    }
     for (int64_t e = threadIdx.x; e < nr * ncols; e += blockDim.x) {
         const int64_t r = e / ncols;
         const int64_t idx = (row0 + r) * ncols + (e - r * ncols);
@@ -2523,14 +2576,38 @@ k_attn_decode(dev_tables T, const float * __restrict__ q, const __half * __restr
     const __half * kh = kc + (int64_t) kvh * D;
     const __half * vh = vc + (int64_t) kvh * D;
     for (int d = tid; d < D; d += nt) qc[d] = O.from(q[(int64_t) h * D + d]);
+    // a tile of nk keys of the F16 cache into codes (F16 -> F32 -> codes), K as
+    // [d][k] (kt) or V as [k][d]: each thread's values in batches of eight, the
+    // cache loads and then the conversions' table loads all in flight
+    auto stage_kv = [&](const __half * src, int64_t t0, int nk, bool kt) {
+        constexpr int U = 8;
+        const int n = nk * D;
+        for (int i0 = tid; i0 < n; i0 += nt * U) {
+            float f[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int i = i0 + u * nt;
+                const int kk = i / D, d = i - kk * D;
+                f[u] = i < n ? __half2float(src[(t0 + kk) * kv_ld + d]) : 0.0f;
+            }
+            uint32_t c[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) c[u] = O.from(f[u]);
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int i = i0 + u * nt;
+                if (i < n) {
+                    const int kk = i / D, d = i - kk * D;
+                    tile[kt ? d * KTP + kk : kk * D + d] = c[u];
+                }
+            }
+        }
+    };
     // kq: one chain over d per key, a tile of keys at a time
     for (int64_t t0 = 0; t0 < nkv; t0 += ATTN_KT) {
         const int64_t nk = nkv - t0 < ATTN_KT ? nkv - t0 : ATTN_KT;
         __syncthreads();                                             // the previous tile's chains are done
-        for (int64_t i = tid; i < nk * D; i += nt) {
-            const int64_t kk = i / D, d = i - kk * D;
-            tile[d * KTP + kk] = O.from(__half2float(kh[(t0 + kk) * kv_ld + d]));
-        }
+        stage_kv(kh, t0, (int) nk, true);
         __syncthreads();
         for (int64_t kk = tid; kk < nk; kk += nt) {
             const int64_t k = t0 + kk;
@@ -2595,10 +2672,7 @@ k_attn_decode(dev_tables T, const float * __restrict__ q, const __half * __restr
     for (int64_t t0 = 0; t0 < nkv; t0 += ATTN_KT) {
         const int64_t nk = nkv - t0 < ATTN_KT ? nkv - t0 : ATTN_KT;
         __syncthreads();
-        for (int64_t i = tid; i < nk * D; i += nt) {
-            const int64_t kk = i / D, d = i - kk * D;
-            tile[kk * D + d] = O.from(__half2float(vh[(t0 + kk) * kv_ld + d]));
-        }
+        stage_kv(vh, t0, (int) nk, false);
         __syncthreads();
         if (tid < D) {
             for (int64_t kk = 0; kk < nk; kk++) {
