@@ -417,3 +417,25 @@ def test_mat_vec_lat(orc, fmt, K, M, N):
         ks.mul_mat_lns(dev32(np.ascontiguousarray(w.T)), dev32(x), out, K, M, N)
         got = host32(out)
     assert np.array_equal(got, want)
+
+
+def test_xlns32_conversions_exhaustive(orc, ks32):
+    """The xlns32 conversions compute the 2^23-entry mantissa tables' entries in
+    double precision (a table read only near the rounding edges): every
+    mantissa at an exponent of each sign (float -> xlns32, the +1 of negative
+    exponents included) and every fraction field (xlns32 -> float) equal the
+    oracle's exact tables"""
+    man = np.arange(1 << 23, dtype=np.uint32)
+    for ex in (127, 126, 1):                         # 1.m, 0.5 * 1.m (negative log), near the subnormals
+        f = ((ex << 23) | man).view(np.float32)
+        want = orc.from_f32_32(f)
+        out = torch.empty(f.size, dtype=torch.int32, device="cuda")
+        ks32.to_lns(torch.from_numpy(f).cuda(), out)
+        assert np.array_equal(host32(out), want), ex
+    for lg in (0x40000000, 0x3F800000, 0x42000000):  # fraction fields at three log magnitudes
+        codes = (np.uint32(lg) + man).astype(np.uint32)
+        want = orc.to_f32_32(codes)
+        out = torch.empty(codes.size, dtype=torch.float32, device="cuda")
+        ks32.to_f32(dev32(codes), out)
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32)), hex(lg)

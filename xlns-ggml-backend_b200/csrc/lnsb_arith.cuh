@@ -97,6 +97,10 @@ __device__ __forceinline__ uint32_t from_f32_16(const dev_tables & T, float x) {
 }
 __device__ __forceinline__ float to_f32_16(const dev_tables & T, uint32_t v) { return __ldg(T.dec16 + (v & 0xFFFFu)); }
 
+#ifndef LNSB_X32_CONV_FAST
+#define LNSB_X32_CONV_FAST 1
+#endif
+
 // ============================== xlns32 ====================================
 
 __device__ __forceinline__ uint32_t mul32(uint32_t a, uint32_t b) {
@@ -277,6 +281,33 @@ __device__ __forceinline__ bool gt32(uint32_t a, uint32_t b) { return canon32(a)
 __device__ __forceinline__ bool is_zero32(uint32_t v) { return (v & 0x7FFFFFFFu) == 0; }
 
 // float -> xlns32, truncation toward zero of log2|x| * 2^23 (exact: mantissa table)
+// floor(log2(1 + man / 2^23) * 2^23), the entry man of the 2^23-entry table
+// T.logm32.  Computed in double precision (log2, at most an ulp or two off:
+// far below the 2^-20 margin kept from the integers); the rare values within
+// the margin of an integer, where the floor could go either way, read the
+// table.  Same value as the table for every man (checked exhaustively on the
+// GPU); the table is 32 MB, so the computation saves a memory round trip.
+__device__ __forceinline__ uint32_t logm32_of(const dev_tables & T, uint32_t man) {
+#if LNSB_X32_CONV_FAST
+    const double v = log2(1.0 + (double) man * 0x1p-23) * 0x1p23;
+    const double fl = floor(v);
+    const double fr = v - fl;
+    if (fr > 0x1p-20 && fr < 1.0 - 0x1p-20) return (uint32_t) fl;
+#endif
+    return __ldg(T.logm32 + man);
+}
+// the float nearest 2^(f / 2^23), f < 2^23: the entry f of T.expm32, computed
+// in double precision (exp2) and rounded to float, except within a 2^-21 float
+// ulp of a rounding midpoint, where the table is read
+__device__ __forceinline__ float expm32_of(const dev_tables & T, uint32_t f) {
+#if LNSB_X32_CONV_FAST
+    const double d = exp2((double) f * 0x1p-23);
+    const double t = d * 0x1p24;                         // floats of [1, 2) at even t, midpoints at odd t
+    if (fabs(t - rint(t)) > 0x1p-21) return __double2float_rn(d);
+#endif
+    return __ldg(T.expm32 + f);
+}
+
 __device__ __forceinline__ uint32_t from_f32_32(const dev_tables & T, float x) {
     const uint32_t b = __float_as_uint(x);
     const uint32_t sign = b & 0x80000000u;
@@ -291,7 +322,7 @@ __device__ __forceinline__ uint32_t from_f32_32(const dev_tables & T, float x) {
     } else {
         e = (int) ex - 127;
     }
-    long long l = (long long) e * (long long) k32_one + (long long) __ldg(T.logm32 + man);
+    long long l = (long long) e * (long long) k32_one + (long long) logm32_of(T, man);
     if (e < 0 && man != 0) l += 1;
     return sign | (uint32_t) ((l + 0x40000000LL) & 0x7FFFFFFFLL);
 }
@@ -322,7 +353,7 @@ __device__ __forceinline__ float to_f32_32(const dev_tables & T, uint32_t v) {
     if ((v & 0x7FFFFFFFu) == 0) return 0.0f;
     const int32_t l = (int32_t) (v & 0x7FFFFFFFu) - 0x40000000;
     const int e = l >> 23;
-    const float r = scale_pow2(__ldg(T.expm32 + ((uint32_t) l & 0x7FFFFFu)), e);
+    const float r = scale_pow2(expm32_of(T, (uint32_t) l & 0x7FFFFFu), e);
     return (v & 0x80000000u) ? -r : r;
 }
 
