@@ -439,3 +439,21 @@ def test_xlns32_conversions_exhaustive(orc, ks32):
         ks32.to_f32(dev32(codes), out)
         torch.cuda.synchronize()
         assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32)), hex(lg)
+
+
+def test_xlns16_conversion_every_bucket(orc):
+    """float -> xlns16: every one of the 131,072 sign / exponent /
+    top-mantissa buckets, with its low 15 bits zero, all ones and random,
+    gives the oracle's code (zeros, subnormals, infinities and NaNs
+    included)"""
+    import lnsb200
+    ks = lnsb200.KernelSet(16, "base")
+    ks.upload_tables()
+    rng = np.random.default_rng(21)
+    idx = np.arange(1 << 17, dtype=np.uint32)
+    for low in (np.zeros_like(idx), np.full_like(idx, 0x7FFF), rng.integers(0, 1 << 15, idx.size).astype(np.uint32)):
+        f = ((idx << 15) | low).astype(np.uint32).view(np.float32)
+        want = orc.from_f32_16(f)
+        out = torch.empty(f.size, dtype=torch.int16, device="cuda")
+        ks.to_lns(torch.from_numpy(f).cuda(), out)
+        assert np.array_equal(host16(out), want)
