@@ -1279,6 +1279,39 @@ k_mul_mat16_res2(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
 
     lt_tables_async(T, smem);                            // signed key table, packed table
     cp_async_commit();
+    // token keys: token row t is token n0 + t (the last token stands in past
+    // N); 16-byte loads where K is a multiple of 8 and X 16-byte aligned.  The
+    // first batch of token loads is issued before the weights are staged, so
+    // the two trips to memory overlap.
+    const bool xvec = Ki % 8 == 0 && ((uintptr_t) X % 16) == 0;
+    const int  k8n = Ki / 8, nld = xvec ? ntok * k8n : 0;
+    auto xload = [&](int base, uint4 (&q)[4]) {
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = base + u * R2_THREADS;
+            if (i < nld) {
+                const int t = i / k8n;
+                const int64_t n = min(n0 + t, N - 1);
+                q[u] = __ldg(reinterpret_cast<const uint4 *>(X + (z * N + n) * K + (int64_t) (i - t * k8n) * 8));
+            }
+        }
+    };
+    auto xstore = [&](int base, const uint4 (&q)[4]) {
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = base + u * R2_THREADS;
+            if (i >= nld) break;
+            const int t = i / k8n, k = (i - t * k8n) * 8;
+            const uint32_t wd[4] = { q[u].x, q[u].y, q[u].z, q[u].w };
+            int key[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) key[e] = key_of_code_x((wd[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
+            *reinterpret_cast<int4 *>(xk + t * PW + k)     = make_int4(key[0], key[1], key[2], key[3]);
+            *reinterpret_cast<int4 *>(xk + t * PW + k + 4) = make_int4(key[4], key[5], key[6], key[7]);
+        }
+    };
+    uint4 xq0[4];
+    if (xvec) xload(tid, xq0);
     {
         int lo = 0x7FFF, hi = 0;
         r2_stage_w<R>(wk, PW, Wz, M, m0, 0, kpre, tid, R2_THREADS, vec, lo, hi);
@@ -1286,29 +1319,12 @@ k_mul_mat16_res2(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
         hi = __reduce_max_sync(0xFFFFFFFFu, hi);
         if (lane == 0) { wred[warp][0] = lo; wred[warp][1] = hi; }
     }
-    // token keys: token row t is token n0 + t (the last token stands in past
-    // N); 16-byte loads where K is a multiple of 8 and X 16-byte aligned
-    if (Ki % 8 == 0 && ((uintptr_t) X % 16) == 0) {
-        const int k8n = Ki / 8, nld = ntok * k8n;
-        for (int base = tid; base < nld; base += R2_THREADS * 4) {
+    if (xvec) {
+        xstore(tid, xq0);
+        for (int base = tid + R2_THREADS * 4; base < nld; base += R2_THREADS * 4) {
             uint4 q[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int i = base + u * R2_THREADS, t = i / k8n;
-                const int64_t n = min(n0 + t, N - 1);
-                if (i < nld) q[u] = __ldg(reinterpret_cast<const uint4 *>(X + (z * N + n) * K + (int64_t) (i - t * k8n) * 8));
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int i = base + u * R2_THREADS, t = i / k8n, k = (i - t * k8n) * 8;
-                if (i >= nld) break;
-                const uint32_t wd[4] = { q[u].x, q[u].y, q[u].z, q[u].w };
-                int key[8];
-#pragma unroll
-                for (int e = 0; e < 8; e++) key[e] = key_of_code_x((wd[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
-                *reinterpret_cast<int4 *>(xk + t * PW + k)     = make_int4(key[0], key[1], key[2], key[3]);
-                *reinterpret_cast<int4 *>(xk + t * PW + k + 4) = make_int4(key[4], key[5], key[6], key[7]);
-            }
+            xload(base, q);
+            xstore(base, q);
         }
     } else {
         for (int i = tid; i < ntok * Ki; i += R2_THREADS) {
