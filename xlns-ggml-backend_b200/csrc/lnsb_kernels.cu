@@ -2116,7 +2116,6 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
            uint32_t eps_l, uint32_t inv_n, uint32_t monte_seed, int rpb, int nn_ok,
            const float * __restrict__ res = nullptr, float * __restrict__ x_out = nullptr,
            const float * __restrict__ nw = nullptr) {
-    pdl_entry();
     __shared__ __align__(16) int16_t tab[k16_tab_bytes16 / 2];
     __shared__ __align__(16) int16_t fine[k_mode == M_MONTE ? 2 * k16_monte_n : 8];
     __shared__ uint32_t s_inv[32];
@@ -2144,6 +2143,7 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
     uint16_t * sq   = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
     uint32_t * sq32 = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(dyn) + nn_tab<FMT>());
     if (NN) nn_tables<FMT>(T, dyn);
+    pdl_entry();                                         // read-only tables above: before the wait
     if constexpr (FUSE) {                                // the residual add reads the packed table
         cp_async_commit();
         cp_async_wait<0>();
@@ -2319,7 +2319,6 @@ __global__ void __launch_bounds__(SM_THREADS)
 k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const void * __restrict__ mask,
            lnsb_shape4 ms, uint32_t scale_l, void * __restrict__ dst, void * __restrict__ work,
            uint32_t monte_seed, int rpb, int nn_ok) {
-    pdl_entry();
     extern __shared__ __align__(16) int32_t dyn[];          // [sb knots (xlns32, sum32)][terms: rpb x pitch]
     __shared__ __align__(16) int16_t tab[k16_tab_bytes16 / 2];
     __shared__ __align__(16) int16_t fine[k_mode == M_MONTE ? 2 * k16_monte_n : 8];
@@ -2331,6 +2330,7 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
     if constexpr (FMT == 16) norm_tables(T, tab, fine);
     if (ST) nn_tables<FMT>(T, dyn);
     cp_async_commit();
+    pdl_entry();                                            // read-only tables above: before the wait
     cp_async_wait<0>();
     __syncthreads();
     const int64_t n = s.ne[0];
