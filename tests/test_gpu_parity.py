@@ -390,11 +390,11 @@ def test_errors_are_reported(ks16):
 # ----------------------------------------------------- the latency mat-vec (k_mat_vec_lat)
 
 @pytest.mark.parametrize("fmt", [16, 32])
-@pytest.mark.parametrize("K,M,N", [(100, 2000, 3), (1537, 4700, 1), (577, 9000, 4), (33, 1000, 1), (2, 70, 2)])
+@pytest.mark.parametrize("K,M,N", [(100, 2000, 3), (1537, 4700, 1), (577, 4000, 4), (33, 1000, 1), (2, 70, 2)])
 def test_mat_vec_lat(orc, fmt, K, M, N):
     """sum32 / xlns32 products with few 32-row x 1-token units per SM run the
-    producer/chain kernel with 1 .. 8 units per block (a partial last block,
-    K not a multiple of the 16-step stage, M not a multiple of 32): bit-exact
+    producer/chain kernel with 1 .. 4 units per block (a partial last block,
+    K not a multiple of the 32-step stage, M not a multiple of 32): bit-exact
     against the oracle"""
     import lnsb200
     rng = np.random.default_rng(K * 7 + M + N)

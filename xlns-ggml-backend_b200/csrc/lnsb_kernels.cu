@@ -1504,8 +1504,10 @@ __host__ __device__ constexpr int a32_threads(int fmt, bool ring) { return fmt =
 #define LNSB_A32_LV 1
 #endif
 #ifndef LNSB_A32_LV_PAIRS
-// ... up to this many units per SM (at most LV_MAX_PAIRS)
-#define LNSB_A32_LV_PAIRS 6
+// ... up to this many units per SM (at most LV_MAX_PAIRS).  Measured per step
+// at N = 16 against k_mul_mat_a32: 189 / 223 / 227 / 227 cycles at 1 / 2 / 3 / 4
+// units per SM against 232-234; 287 / 358 at 5 / 6 against 276
+#define LNSB_A32_LV_PAIRS 4
 #endif
 #ifndef LNSB_A32_TN2_MIN_UNITS
 #define LNSB_A32_TN2_MIN_UNITS 2     // two tokens per lane once each warp gets this many units
@@ -1897,7 +1899,7 @@ template <int FMT, bool OUT_F32>
 __global__ void __launch_bounds__(64 * LV_MAX_PAIRS, 1)
 k_mat_vec_lat(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
               const typename a32_fmt<FMT>::elem * __restrict__ X, void * __restrict__ dst, int64_t K, int64_t M,
-              int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3, int64_t units) {
+              int64_t N, int64_t ne02, int64_t ne12, int64_t r2, int64_t r3, int64_t units, peer_out_dev peers) {
     using E  = typename a32_fmt<FMT>::elem;
     using OP = a32_fmt<FMT>;
     extern __shared__ __align__(16) int32_t F[];
@@ -1950,7 +1952,15 @@ k_mat_vec_lat(dev_tables T, const typename a32_fmt<FMT>::elem * __restrict__ W,
         acc = chain_smem_strided(q, c == 0 ? 1 : 0, kv, acc, [&](uint32_t a, uint32_t t) { return add32f_sel(F, a, t); });
         if (c + LV_STAGES < nch) asm volatile("bar.arrive %0, %1;\n" ::"r"(1 + LV_STAGES + sidx), "r"(nthr) : "memory");
     }
-    if (valid && m < M) OP::store(T, dst, (z * N + n) * M + m, K == 0 ? 0u : OP::finish(acc), OUT_F32);
+    if (valid && m < M) {
+        const uint32_t v = K == 0 ? 0u : OP::finish(acc);
+        if (!OUT_F32 && peers.n > 0) {                     // the fused all-gather: codes into every peer's buffer
+            const int64_t o = (z * N + n) * peers.ld + peers.off + m;
+            for (int p = 0; p < peers.n; p++) reinterpret_cast<E *>(peers.ptrs[p])[o] = (E) v;
+        } else {
+            OP::store(T, dst, (z * N + n) * M + m, v, OUT_F32);
+        }
+    }
 }
 
 // ============================ MUL_MAT_ID ===================================
@@ -2987,7 +2997,7 @@ int launch_a32_by(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst,
 // of 2 np warps, one wave
 template <int FMT, bool OUT_F32>
 int launch_lv(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, int64_t r2, int64_t r3, int64_t units,
-              int dev, cudaStream_t stream) {
+              int dev, cudaStream_t stream, const peer_out_dev & peers) {
     static bool attr[k_max_devices] = {};
     auto kern = k_mat_vec_lat<FMT, OUT_F32>;
     constexpr int smem_max = k32f_words * 4 + LV_MAX_PAIRS * LV_RING_BYTES;
@@ -3002,7 +3012,7 @@ int launch_lv(const dev_tables & T, const lnsb_mul_mat_args * a, void * dst, int
     const int smem = k32f_words * 4 + np * LV_RING_BYTES;
     using E = typename a32_fmt<FMT>::elem;
     launch_k(kern, (unsigned) grid, 64 * np, smem, stream, T, static_cast<const E *>(a->w), static_cast<const E *>(a->x),
-             dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, units);
+             dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, units, peers);
     return launch_status();
 }
 
@@ -3022,14 +3032,14 @@ int mul_mat_a32(int fmt, const dev_tables & T, const lnsb_mul_mat_args * a, void
     const int64_t es = fmt == LNSB_XLNS16 ? 2 : 4;
     const bool vecx = (a->K * es) % 16 == 0 && ((uintptr_t) a->x % 16) == 0;
     const bool ring = vecx && (a->M * es) % 16 == 0 && ((uintptr_t) a->w % 16) == 0;
-    // at most LNSB_A32_LV_PAIRS units of 32 rows x 1 token per SM, the flat adder, no peer stores: the latency mat-vec
-    if (LNSB_A32_LV && (fmt == LNSB_XLNS32 || k_mode == M_SUM32) && peers.n == 0 && a->K > 0 &&
+    // at most LNSB_A32_LV_PAIRS units of 32 rows x 1 token per SM, the flat adder: the latency mat-vec
+    if (LNSB_A32_LV && (fmt == LNSB_XLNS32 || k_mode == M_SUM32) && a->K > 0 &&
         nz * RB * a->N <= (int64_t) sm_count(dev) * LNSB_A32_LV_PAIRS) {
         const int64_t lv_units = nz * RB * a->N;
-        if (fmt == LNSB_XLNS16) return out_f32 ? launch_lv<16, true>(T, a, dst, r2, r3, lv_units, dev, stream)
-                                               : launch_lv<16, false>(T, a, dst, r2, r3, lv_units, dev, stream);
-        return out_f32 ? launch_lv<32, true>(T, a, dst, r2, r3, lv_units, dev, stream)
-                       : launch_lv<32, false>(T, a, dst, r2, r3, lv_units, dev, stream);
+        if (fmt == LNSB_XLNS16) return out_f32 ? launch_lv<16, true>(T, a, dst, r2, r3, lv_units, dev, stream, peers)
+                                               : launch_lv<16, false>(T, a, dst, r2, r3, lv_units, dev, stream, peers);
+        return out_f32 ? launch_lv<32, true>(T, a, dst, r2, r3, lv_units, dev, stream, peers)
+                       : launch_lv<32, false>(T, a, dst, r2, r3, lv_units, dev, stream, peers);
     }
     if (fmt == LNSB_XLNS16) {
         if (tn2) return launch_a32_by<16, 2>(T, a, dst, out_f32, ring, r2, r3, units, dev, vecx, stream, peers);
