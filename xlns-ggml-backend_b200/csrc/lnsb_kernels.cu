@@ -1509,8 +1509,11 @@ __host__ __device__ constexpr int a32_threads(int fmt, bool ring) { return fmt =
 // units per SM against 232-234; 287 / 358 at 5 / 6 against 276
 #define LNSB_A32_LV_PAIRS 4
 #endif
-#ifndef LNSB_A32_TN2_MIN_UNITS
-#define LNSB_A32_TN2_MIN_UNITS 2     // two tokens per lane once each warp gets this many units
+#ifndef LNSB_A32_TN2_MIN_QUARTERS
+// two tokens per lane once the two-token units fill this many quarters of the
+// warps (W 8192 x 4096, sum32: N = 32 runs 443 -> 549 G-LNSadd/s with two
+// tokens, 0.86 of the warps busy; N = 16 falls 465 -> 331, 0.43 busy)
+#define LNSB_A32_TN2_MIN_QUARTERS 3
 #endif
 
 // Accumulation policy of the kernel: the flat xlns32 addition (xlns32, and
@@ -3027,7 +3030,7 @@ int mul_mat_a32(int fmt, const dev_tables & T, const lnsb_mul_mat_args * a, void
     const bool ring0 = (a->K * es0) % 16 == 0 && ((uintptr_t) a->x % 16) == 0 && (a->M * es0) % 16 == 0 &&
                        ((uintptr_t) a->w % 16) == 0;
     const int64_t warps = (int64_t) sm_count(dev) * (a32_threads(fmt == LNSB_XLNS16 ? 16 : 32, ring0) / 32);
-    const bool tn2 = a->N >= 2 && nz * RB * ((a->N + 1) / 2) >= LNSB_A32_TN2_MIN_UNITS * warps;
+    const bool tn2 = a->N >= 2 && 4 * nz * RB * ((a->N + 1) / 2) >= LNSB_A32_TN2_MIN_QUARTERS * warps;
     const int64_t units = nz * RB * (tn2 ? (a->N + 1) / 2 : a->N);
     const int64_t es = fmt == LNSB_XLNS16 ? 2 : 4;
     const bool vecx = (a->K * es) % 16 == 0 && ((uintptr_t) a->x % 16) == 0;
