@@ -451,10 +451,13 @@ def run_ours(args, wl):
                    "l2": "flushed (256 MB write) before every timed step"},
         "roofline": roof,
         "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "per step: H2D of F32 activations (pinned), lnsb_to_lns, " +
-                        ("lnsb_mul_mat (F32 out)" if world == 1 else
-                         "lnsb_mul_mat_lns_peers + lnsb_group_barrier (the fused all-gather), lnsb_to_f32 of the gathered codes") +
-                        ", D2H of the F32 result (pinned); double buffered, copies on their own streams"},
+                "path": "per step: H2D of F32 activations (pinned), " +
+                        ("lnsb_mul_mat_xf32 (the activations' conversion and mul_mat in one call, F32 out)"
+                         if world == 1 else
+                         "lnsb_to_lns, lnsb_mul_mat_lns_peers + lnsb_group_barrier (the fused all-gather), "
+                         "lnsb_to_f32 of the gathered codes") +
+                        ", D2H of the F32 result (pinned); double buffered, copies on their own streams",
+                "l2": "not flushed between steps: a serving loop's steady state, weights resident (value flushes)"},
         "gpu_launches": launches,
         "clocks": clocks,
     }
@@ -505,9 +508,10 @@ def run_ours(args, wl):
 
 def e2e_run(ctx, ks, w, rng, K, M, N, gather, mm_args, args):
     """End to end through the C ABI with host buffers: every step uploads its
-    F32 activations from pinned host memory (H2D), converts them (to_lns), runs
-    mul_mat -- at N > 1 with the fused all-gather and its barrier, then the
-    gathered codes' decode (to_f32) -- and reads the F32 result back into
+    F32 activations from pinned host memory (H2D), converts them and runs
+    mul_mat -- on one GPU in one call (lnsb_mul_mat_xf32), at N > 1 to_lns and
+    mul_mat with the fused all-gather and its barrier, then the gathered
+    codes' decode (to_f32) -- and reads the F32 result back into
     pinned host memory (D2H); the weights stay resident, as the reference's
     weight cache keeps them.  Steps are double buffered the way a serving
     loop runs them: step i+1's upload and step i's read-back go on their own
@@ -523,8 +527,10 @@ def e2e_run(ctx, ks, w, rng, K, M, N, gather, mm_args, args):
     xd = [torch.empty(N * K, dtype=torch.float32, device="cuda") for _ in range(NB)]
     xc = [torch.empty(N * K, dtype=torch.int16, device="cuda") for _ in range(NB)]
     yd = [torch.empty(N * MO, dtype=torch.float32, device="cuda") for _ in range(NB)]
-    args_b = [lnsb200.MulMatArgs(w.data_ptr(), xc[b].data_ptr(), yd[b].data_ptr(), K, M, N, 1, 1, 1, 1, 7)
-              for b in range(NB)]
+    # one GPU: the F32 activations go straight to lnsb_mul_mat_xf32 (xc[b] its
+    # x_work); with the gather, to_lns into xc[b] and the peer-store mul_mat
+    args_b = [lnsb200.MulMatArgs(w.data_ptr(), (xd[b] if gather is None else xc[b]).data_ptr(), yd[b].data_ptr(),
+                                 K, M, N, 1, 1, 1, 1, 7) for b in range(NB)]
     stream = ctx.stream
     up, down = torch.cuda.Stream(), torch.cuda.Stream()
     ev_up = [torch.cuda.Event() for _ in range(NB)]        # input b uploaded
@@ -544,11 +550,14 @@ def e2e_run(ctx, ks, w, rng, K, M, N, gather, mm_args, args):
         b = i % NB
         stream.wait_event(ev_up[b])
         stream.wait_event(ev_dn[b])
-        ks.to_lns(xd[b], xc[b], stream=stream)
-        ev_cv[b].record(stream)
         if gather is None:
-            ks.lib.lnsb_mul_mat(16, ctypes.byref(args_b[b]), ctx.sp)
+            st = ks.lib.lnsb_mul_mat_xf32(16, ctypes.byref(args_b[b]), ctypes.c_void_p(xc[b].data_ptr()), ctx.sp)
+            if st != 0:
+                raise lnsb200.LnsbError(ks.lib, "lnsb_mul_mat_xf32", st)
+            ev_cv[b].record(stream)
         else:
+            ks.to_lns(xd[b], xc[b], stream=stream)
+            ev_cv[b].record(stream)
             g = gather.step(ctypes.byref(args_b[b]), status)
             ks.to_f32(g, yd[b], stream=stream)             # the read of this step's gather, on this stream
         ev_mm[b].record(stream)

@@ -162,6 +162,15 @@ int lnsb_mul_mat(int fmt, const lnsb_mul_mat_args * args, lnsb_stream_t stream);
  * (args->dst is ignored).  The reference's LNS16-typed dst path,
  * lns-ops.cpp:374-379. */
 int lnsb_mul_mat_lns(int fmt, const lnsb_mul_mat_args * args, void * dst_lns, lnsb_stream_t stream);
+/* the MUL_MAT op over F32 activations: args->x holds F32 values (N x K per
+ * activation slice) instead of codes.  Same result as lnsb_to_lns of x into
+ * x_work followed by lnsb_mul_mat over x_work, which is the reference's
+ * compute_mul_mat (lns-cuda-ops.cpp:57-75: to_lns of src1, then
+ * kernel_set::mul_mat).  The weight-resident latency kernel (xlns16 base mode,
+ * few outputs) converts the activations as it stages them, with no separate
+ * launch and x_work untouched; every other case converts into x_work first.
+ * x_work (N * K * ne12 * ne13 LNS values) is required whenever K > 0. */
+int lnsb_mul_mat_xf32(int fmt, const lnsb_mul_mat_args * args, void * x_work, lnsb_stream_t stream);
 
 /* mul_mat with the all-gather of output-row shards fused into the store (no
  * counterpart in the reference): the caller owns rows [offset, offset + M)

@@ -110,6 +110,12 @@ public:
         return ret(lnsb_soft_max(fmt_, &b, stream));
     }
 
+    // the MUL_MAT op over F32 activations (to_lns of src1 and mul_mat in one call,
+    // lns-cuda-ops.cpp:57-75); a.x holds F32 values, x_work N*K codes
+    cudaError_t mul_mat_xf32(const mul_mat_args & a, void * x_work, cudaStream_t stream) const {
+        return ret(lnsb_mul_mat_xf32(fmt_, c_args(a), x_work, stream));
+    }
+
     // LNS-resident forms (codes in and out; not in the reference's interface)
     cudaError_t mul_mat_lns(const mul_mat_args & a, void * dst, cudaStream_t stream) const {
         return ret(lnsb_mul_mat_lns(fmt_, c_args(a), dst, stream));

@@ -567,13 +567,18 @@ int compute_mul_mat(lnsb_graph_ctx & c, lnsb_tensor * n) {
     const lnsb_tensor * s1 = n->src[1];
     const void * w = lns_matrix(c, s0, &st);
     if (w == nullptr) return st;
-    const void * x = lns_operand(c, s1, R_SRC1, R_LNS1, &st);
-    if (x == nullptr) return st;
+    // the F32 activations go to lnsb_mul_mat_xf32, which converts them while
+    // staging where its kernel can (else into x_work first): the reference's
+    // to_lns + mul_mat pair in one call
+    const float * xf = static_cast<const float *>(packed(c, s1, R_SRC1, &st));
+    if (xf == nullptr) return st;
+    void * x_work = c.dev(R_LNS1, (size_t) nelements(s1) * lnsb_value_size(c.fmt));
+    if (x_work == nullptr) return LNSB_E_TOO_LARGE;
     float * out = result(c, n, &st);
     if (out == nullptr) return st;
-    lnsb_mul_mat_args a{ w, x, out, s0->ne[0], s0->ne[1], s1->ne[1], s0->ne[2], s0->ne[3], s1->ne[2], s1->ne[3], 0 };
+    lnsb_mul_mat_args a{ w, xf, out, s0->ne[0], s0->ne[1], s1->ne[1], s0->ne[2], s0->ne[3], s1->ne[2], s1->ne[3], 0 };
     a.monte_seed = reserve_monte(lnsb_mul_mat_draws(c.fmt, &a));
-    st = lnsb_mul_mat(c.fmt, &a, c.stream);
+    st = lnsb_mul_mat_xf32(c.fmt, &a, x_work, c.stream);
     return st != 0 ? st : finish(c, n, out);
 }
 

@@ -1249,14 +1249,16 @@ __device__ __forceinline__ void r2_stage_w(int * wk, int PW, const uint16_t * __
     }
 }
 
-template <bool OUT_F32, int R, int TPW>
+template <bool OUT_F32, int R, int TPW, bool XF32>
 __global__ void __launch_bounds__(R2_THREADS)
-k_mul_mat16_res2(dev_tables T, const uint16_t * __restrict__ W, const uint16_t * __restrict__ X,
+k_mul_mat16_res2(dev_tables T, const uint16_t * __restrict__ W, const void * __restrict__ X,
                  void * __restrict__ dst, int64_t K, int64_t M, int64_t N, int64_t ne02, int64_t ne12,
                  int64_t r2, int64_t r3, int cw, int vec, peer_out_dev peers) {
     // TPW token slots per warp: 32 / R, or 1 with R = 16, where lanes 16..31
     // repeat lanes 0..15 (same addresses: the table lookup sees 16 distinct
-    // addresses, fewer bank conflicts, a shorter step) and only lanes 0..15 store
+    // addresses, fewer bank conflicts, a shorter step) and only lanes 0..15 store.
+    // XF32: the activations arrive as F32 and are converted (from_f32_16, the
+    // conversion of k_to_lns) as they are staged.
     static_assert(R * TPW == 32 || (R == 16 && TPW == 1), "lane layout");
     pdl_entry();
     extern __shared__ __align__(16) unsigned char smem[];
@@ -1285,32 +1287,62 @@ k_mul_mat16_res2(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
     // the two trips to memory overlap.
     const bool xvec = Ki % 8 == 0 && ((uintptr_t) X % 16) == 0;
     const int  k8n = Ki / 8, nld = xvec ? ntok * k8n : 0;
-    auto xload = [&](int base, uint4 (&q)[4]) {
+    constexpr int XQ = XF32 ? 2 : 1;                     // 16-byte words per piece of 8 values
+    auto xload = [&](int base, uint4 (&q)[4 * XQ]) {
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             const int i = base + u * R2_THREADS;
             if (i < nld) {
                 const int t = i / k8n;
-                const int64_t n = min(n0 + t, N - 1);
-                q[u] = __ldg(reinterpret_cast<const uint4 *>(X + (z * N + n) * K + (int64_t) (i - t * k8n) * 8));
+                const int64_t n = min(n0 + t, N - 1), o = (z * N + n) * K + (int64_t) (i - t * k8n) * 8;
+                if constexpr (XF32) {
+                    const uint4 * p = reinterpret_cast<const uint4 *>(static_cast<const float *>(X) + o);
+                    q[2 * u] = __ldg(p);
+                    q[2 * u + 1] = __ldg(p + 1);
+                } else {
+                    q[u] = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(X) + o));
+                }
             }
         }
     };
-    auto xstore = [&](int base, const uint4 (&q)[4]) {
+    auto xstore = [&](int base, const uint4 (&q)[4 * XQ]) {
+        if constexpr (XF32) {
+            uint32_t c[4][8];                            // the pieces' codes, every lookup issued first
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int i = base + u * R2_THREADS;
-            if (i >= nld) break;
-            const int t = i / k8n, k = (i - t * k8n) * 8;
-            const uint32_t wd[4] = { q[u].x, q[u].y, q[u].z, q[u].w };
-            int key[8];
+            for (int u = 0; u < 4; u++) {
+                if (base + u * R2_THREADS >= nld) continue;
+                const uint32_t wd[8] = { q[2 * u].x, q[2 * u].y, q[2 * u].z, q[2 * u].w,
+                                         q[2 * u + 1].x, q[2 * u + 1].y, q[2 * u + 1].z, q[2 * u + 1].w };
 #pragma unroll
-            for (int e = 0; e < 8; e++) key[e] = key_of_code_x((wd[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
-            *reinterpret_cast<int4 *>(xk + t * PW + k)     = make_int4(key[0], key[1], key[2], key[3]);
-            *reinterpret_cast<int4 *>(xk + t * PW + k + 4) = make_int4(key[4], key[5], key[6], key[7]);
+                for (int e = 0; e < 8; e++) c[u][e] = from_f32_16(T, __uint_as_float(wd[e]));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = base + u * R2_THREADS;
+                if (i >= nld) break;
+                const int t = i / k8n, k = (i - t * k8n) * 8;
+                int key[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) key[e] = key_of_code_x(c[u][e]);
+                *reinterpret_cast<int4 *>(xk + t * PW + k)     = make_int4(key[0], key[1], key[2], key[3]);
+                *reinterpret_cast<int4 *>(xk + t * PW + k + 4) = make_int4(key[4], key[5], key[6], key[7]);
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = base + u * R2_THREADS;
+                if (i >= nld) break;
+                const int t = i / k8n, k = (i - t * k8n) * 8;
+                const uint32_t wd[4] = { q[u].x, q[u].y, q[u].z, q[u].w };
+                int key[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) key[e] = key_of_code_x((wd[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
+                *reinterpret_cast<int4 *>(xk + t * PW + k)     = make_int4(key[0], key[1], key[2], key[3]);
+                *reinterpret_cast<int4 *>(xk + t * PW + k + 4) = make_int4(key[4], key[5], key[6], key[7]);
+            }
         }
     };
-    uint4 xq0[4];
+    uint4 xq0[4 * XQ];
     if (xvec) xload(tid, xq0);
     {
         int lo = 0x7FFF, hi = 0;
@@ -1322,15 +1354,16 @@ k_mul_mat16_res2(dev_tables T, const uint16_t * __restrict__ W, const uint16_t *
     if (xvec) {
         xstore(tid, xq0);
         for (int base = tid + R2_THREADS * 4; base < nld; base += R2_THREADS * 4) {
-            uint4 q[4];
+            uint4 q[4 * XQ];
             xload(base, q);
             xstore(base, q);
         }
     } else {
         for (int i = tid; i < ntok * Ki; i += R2_THREADS) {
             const int t = i / Ki, k = i - t * Ki;
-            const int64_t n = min(n0 + t, N - 1);
-            xk[t * PW + k] = key_of_code_x(X[(z * N + n) * K + k]);
+            const int64_t o = (z * N + min(n0 + t, N - 1)) * K + k;
+            xk[t * PW + k] = key_of_code_x(XF32 ? from_f32_16(T, static_cast<const float *>(X)[o])
+                                                : (uint32_t) static_cast<const uint16_t *>(X)[o]);
         }
     }
     __syncthreads();
@@ -3090,13 +3123,17 @@ int mul_mat_id_impl(int fmt, const lnsb_mul_mat_id_args * a, void * dst, bool ou
     return out_f32 ? go(k_mul_mat_id<32, true>, mmid_smem<32>(), w, x) : go(k_mul_mat_id<32, false>, mmid_smem<32>(), w, x);
 }
 
+// xf32: a->x holds F32 activations; the weight-resident latency kernel
+// converts them as it stages its token rows, every other kernel reads codes
+// converted into x_work (N x K per activation slice) first
 int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32, cudaStream_t stream,
-                 const peer_out_dev * peers = nullptr) {
+                 const peer_out_dev * peers = nullptr, bool xf32 = false, void * x_work = nullptr) {
     if (!valid_fmt(fmt) || a == nullptr) return LNSB_E_INVALID;
     if (a->K < 0 || a->M < 0 || a->N < 0 || a->ne02 <= 0 || a->ne03 <= 0 || a->ne12 <= 0 || a->ne13 <= 0) return LNSB_E_INVALID;
     if (a->ne12 % a->ne02 != 0 || a->ne13 % a->ne03 != 0) return LNSB_E_INVALID;
     if (a->M == 0 || a->N == 0) return 0;
     if ((dst == nullptr && peers == nullptr) || (a->K > 0 && (a->w == nullptr || a->x == nullptr))) return LNSB_E_INVALID;
+    if (xf32 && a->K > 0 && x_work == nullptr) return LNSB_E_INVALID;
     if (a->ne12 * a->ne13 > 65535) return LNSB_E_TOO_LARGE;
     const dev_tables * T = nullptr;
     const int st = tables_for(fmt, &T);
@@ -3133,24 +3170,38 @@ int mul_mat_impl(int fmt, const lnsb_mul_mat_args * a, void * dst, bool out_f32,
                 r2_R = 16; r2_tpw = 2; r2_cw = cw;
             }
     }
+    lnsb_mul_mat_args xa;                                // the arguments over x_work's codes
+    if (xf32 && r2_R == 0 && a->K > 0) {
+        const int64_t n = a->N * a->K * a->ne12 * a->ne13;
+        if (fmt == LNSB_XLNS16) launch_k(k_to_lns<16>, grid_for(n, 256), 256, 0, stream, *T, static_cast<const float *>(a->x), x_work, n);
+        else                    launch_k(k_to_lns<32>, grid_for(n, 256), 256, 0, stream, *T, static_cast<const float *>(a->x), x_work, n);
+        xa = *a;
+        xa.x = x_work;
+        a = &xa;
+    }
     if (r2_R != 0) {
         const int tpc = r2_cw * r2_tpw;
         const dim3 grid((unsigned) ((a->M + r2_R - 1) / r2_R), (unsigned) ((a->N + tpc - 1) / tpc), (unsigned) (a->ne12 * a->ne13));
         const int smem = r2_smem(a->K, r2_R, tpc);
         const int li = r2_R == 32 ? 0 : r2_tpw == 1 ? 1 : 2;
-        auto kern = li == 0 ? (out_f32 ? k_mul_mat16_res2<true, 32, 1> : k_mul_mat16_res2<false, 32, 1>)
-                  : li == 1 ? (out_f32 ? k_mul_mat16_res2<true, 16, 1> : k_mul_mat16_res2<false, 16, 1>)
-                            : (out_f32 ? k_mul_mat16_res2<true, 16, 2> : k_mul_mat16_res2<false, 16, 2>);
-        static bool r2attr[k_max_devices][2][3] = {};
+        using r2_kern = void (*)(dev_tables, const uint16_t *, const void *, void *, int64_t, int64_t, int64_t, int64_t,
+                                 int64_t, int64_t, int64_t, int, int, peer_out_dev);
+        static const r2_kern kerns[2][2][3] = {          // [x F32][out F32][layout]
+            { { k_mul_mat16_res2<false, 32, 1, false>, k_mul_mat16_res2<false, 16, 1, false>, k_mul_mat16_res2<false, 16, 2, false> },
+              { k_mul_mat16_res2<true, 32, 1, false>,  k_mul_mat16_res2<true, 16, 1, false>,  k_mul_mat16_res2<true, 16, 2, false> } },
+            { { k_mul_mat16_res2<false, 32, 1, true>,  k_mul_mat16_res2<false, 16, 1, true>,  k_mul_mat16_res2<false, 16, 2, true> },
+              { k_mul_mat16_res2<true, 32, 1, true>,   k_mul_mat16_res2<true, 16, 1, true>,   k_mul_mat16_res2<true, 16, 2, true> } } };
+        const r2_kern kern = kerns[xf32][out_f32][li];
+        static bool r2attr[k_max_devices][2][2][3] = {};
         int dev = 0;
         const int ds = current_device(&dev);
         if (ds != 0) return ds;
-        if (!r2attr[dev][out_f32][li]) {
+        if (!r2attr[dev][xf32][out_f32][li]) {
             const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, R2_SMEM_MAX);
             if (e != cudaSuccess) return (int) e;
-            r2attr[dev][out_f32][li] = true;
+            r2attr[dev][xf32][out_f32][li] = true;
         }
-        launch_k(kern, grid, R2_THREADS, smem, stream, *T, static_cast<const uint16_t *>(a->w), static_cast<const uint16_t *>(a->x),
+        launch_k(kern, grid, R2_THREADS, smem, stream, *T, static_cast<const uint16_t *>(a->w), a->x,
                  dst, a->K, a->M, a->N, a->ne02, a->ne12, r2, r3, r2_cw,
                  a->M % 8 == 0 && ((uintptr_t) a->w % 16) == 0 ? 1 : 0, peers != nullptr ? *peers : no_peers);
     } else if (peers == nullptr && fmt == LNSB_XLNS16 && k_mode == M_BASE && tiles < 2 * 148 && a->K <= LT_MAX_K && a->N <= 65535) {
@@ -3771,6 +3822,10 @@ int lnsb_mul_mat(int fmt, const lnsb_mul_mat_args * args, lnsb_stream_t stream) 
 
 int lnsb_mul_mat_lns(int fmt, const lnsb_mul_mat_args * args, void * dst_lns, lnsb_stream_t stream) {
     return mul_mat_impl(fmt, args, dst_lns, false, static_cast<cudaStream_t>(stream));
+}
+
+int lnsb_mul_mat_xf32(int fmt, const lnsb_mul_mat_args * args, void * x_work, lnsb_stream_t stream) {
+    return mul_mat_impl(fmt, args, args ? args->dst : nullptr, true, static_cast<cudaStream_t>(stream), nullptr, true, x_work);
 }
 
 int lnsb_mul_mat_lns_peers(int fmt, const lnsb_mul_mat_args * args, const lnsb_peer_out * peers, lnsb_stream_t stream) {

@@ -108,6 +108,13 @@ class KernelSet:
         a = self._mm_args(w, x, dst, K, M, N, slices, monte_seed)
         _lib.check(self.lib, "lnsb_mul_mat", self.lib.lnsb_mul_mat(self.fmt, ctypes.byref(a), _stream(stream)))
 
+    def mul_mat_xf32(self, w, x_f32, x_work, dst, K, M, N, slices=(1, 1, 1, 1), monte_seed=7, stream=None):
+        """the MUL_MAT op over F32 activations (lnsb_mul_mat_xf32): x_f32 [N][K] floats, converted as
+        the kernel stages them or into x_work (N*K codes) first; dst F32 as mul_mat"""
+        a = self._mm_args(w, x_f32, dst, K, M, N, slices, monte_seed)
+        _lib.check(self.lib, "lnsb_mul_mat_xf32",
+                   self.lib.lnsb_mul_mat_xf32(self.fmt, ctypes.byref(a), _ptr(x_work), _stream(stream)))
+
     def mul_mat_lns(self, w, x, dst, K, M, N, slices=(1, 1, 1, 1), monte_seed=7, stream=None):
         """as mul_mat with LNS codes out"""
         a = self._mm_args(w, x, None, K, M, N, slices, monte_seed)

@@ -97,6 +97,7 @@ SIGNATURES = [
     ("lnsb_weight_cache_stats", ctypes.c_int, [_VP, ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
     ("lnsb_mul_mat", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), _VP]),
     ("lnsb_mul_mat_lns", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), _VP, _VP]),
+    ("lnsb_mul_mat_xf32", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), _VP, _VP]),
     ("lnsb_mul_mat_lns_peers", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(MulMatArgs), ctypes.POINTER(PeerOut), _VP]),
     ("lnsb_group_barrier", ctypes.c_int, [_VP, ctypes.c_int, ctypes.c_int, ctypes.c_int32, _VP, _VP]),
     ("lnsb_add_latency", ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP, _VP]),
