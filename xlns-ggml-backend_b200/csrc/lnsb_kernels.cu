@@ -2177,7 +2177,7 @@ k_rms_norm(dev_tables T, const void * __restrict__ src, void * __restrict__ dst,
         const float f = static_cast<const float *>(src)[idx];
         if (!FUSE || res == nullptr) return f;
         const uint32_t a = f2c(f), b = f2c(res[idx]);
-        return c2f(FMT == 16 ? add16(a, b, tab) : add32(T, a, b));
+        return c2f(FMT == 16 ? add16(a, b, tab) : add32f(T.flat32, a, b));
     };
     auto load = [&](int64_t idx) -> uint32_t {
         if constexpr (IO_F32) {
@@ -2423,7 +2423,7 @@ k_soft_max(dev_tables T, const void * __restrict__ src, lnsb_shape4 s, const voi
                     mk = rm;
                 }
                 if (mk == NEG_INF) v = NEG_INF;
-                else if (FMT == 16 ? !is_zero16(mk) : !is_zero32(mk)) v = FMT == 16 ? add16(v, mk, tab) : add32(T, v, mk);
+                else if (FMT == 16 ? !is_zero16(mk) : !is_zero32(mk)) v = FMT == 16 ? add16(v, mk, tab) : add32f(T.flat32, v, mk);
             }
         }
         return v;
@@ -2795,8 +2795,10 @@ template <> struct ew<16> {
 template <> struct ew<32> {
     __device__ static __forceinline__ uint32_t from(const dev_tables & T, float x) { return from_f32_32(T, x); }
     __device__ static __forceinline__ float    to(const dev_tables & T, uint32_t v) { return to_f32_32(T, v); }
-    __device__ static __forceinline__ uint32_t add(const dev_tables & T, uint32_t a, uint32_t b) { return add32(T, a, b); }
-    __device__ static __forceinline__ uint32_t sub(const dev_tables & T, uint32_t a, uint32_t b) { return add32(T, a, b ^ 0x80000000u); }
+    // the flat image's branch-free addition (same bits as add32): a warp's
+    // lanes take no separate sb / db / cotransformation paths
+    __device__ static __forceinline__ uint32_t add(const dev_tables & T, uint32_t a, uint32_t b) { return add32f(T.flat32, a, b); }
+    __device__ static __forceinline__ uint32_t sub(const dev_tables & T, uint32_t a, uint32_t b) { return add32f(T.flat32, a, b ^ 0x80000000u); }
     __device__ static __forceinline__ uint32_t mul(uint32_t a, uint32_t b) { return mul32(a, b); }
     __device__ static __forceinline__ uint32_t div(uint32_t a, uint32_t b) { return div32(a, b); }
 };
@@ -2824,7 +2826,7 @@ __device__ __forceinline__ uint32_t gelu16(const dev_tables & T, uint32_t x) {
 // softmax; tanh and gelu through double precision (lnsb_tanh_d), as xlns32's
 // activations go through floating point in the reference
 __device__ __forceinline__ uint32_t silu32(const dev_tables & T, uint32_t x) {
-    return div32(x, add32(T, 0x40000000u, exp32(T, x ^ 0x80000000u)));
+    return div32(x, add32f(T.flat32, 0x40000000u, exp32(T, x ^ 0x80000000u)));
 }
 __device__ __forceinline__ uint32_t relu32(uint32_t x) { return ((x & 0x80000000u) || (x & 0x7FFFFFFFu) == 0) ? 0u : x; }
 __device__ __forceinline__ uint32_t tanh32(const dev_tables & T, uint32_t x) {
